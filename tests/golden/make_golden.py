@@ -1,0 +1,219 @@
+"""Generate the golden fixtures under tests/golden/ (run once, here, on CPU).
+
+    python tests/golden/make_golden.py
+
+Expected outputs come from HuggingFace ``transformers`` (``BertModel`` and
+``CLIPVisionModelWithProjection``, eager attention, float64), an independent
+implementation of the same encoder math that the reference's own parity test
+(``crates/jammi-encoders/tests/parity.rs``) checks its encoder against through
+candle-transformers.  Pooling and L2 are applied with torch ops following
+``crates/jammi-encoders/src/pooling.rs`` -- written here independently of
+``oracle/``, so the oracle can be pinned against these files.
+
+Fixtures (``.npz``, weights included so the GPU tests need nothing else):
+
+* ``tiny_bert_seeded.npz``    H 32, 1 layer, 2 heads, FFN 128, vocab 256, pos 128
+  (the shape of the reference's ``cookbook/fixtures/tiny_bert``), seeded weights,
+  ragged rows including a one-token row and an all-padding row.
+* ``small_bert_prefixed.npz`` H 64, 2 layers, 4 heads, FFN 256, keys under the
+  ``bert.`` prefix (the ``BertForX`` layout probed at ``bert.rs:508-517``).
+* ``tiny_clip_gap.npz`` / ``tiny_clip_cls.npz``  OpenCLIP ViT W 32, 1 layer,
+  4 heads, patch 4, image 8, embed 16 (the shape of the reference's
+  ``tests/fixtures/tiny_open_clip``), global-average and CLS pooling.
+* ``reference_tiny_bert.npz`` outputs of the reference's own committed
+  ``tiny_bert`` fixture (weights are NOT copied: its sha256 is stored and the
+  CPU test re-reads the fixture when the reference checkout is present).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.abspath(os.path.join(HERE, "..", "..")))
+
+from oracle.bert import BertConfig, random_bert_weights  # noqa: E402  (weight recipe only)
+from oracle.clip import ClipVisionConfig, random_clip_weights  # noqa: E402
+
+REF_TINY_BERT = "/root/reference/cookbook/fixtures/tiny_bert"
+
+
+def torch_pool_all(hidden: torch.Tensor, mask: torch.Tensor) -> dict:
+    """pooling.rs:31-148 restated with torch ops (float64)."""
+    m = mask.to(torch.float64).unsqueeze(-1)
+    S = hidden.shape[1]
+    out = {}
+    out["mean"] = (hidden * m).sum(1) / m.sum(1).clamp(min=1.0)
+    out["cls"] = hidden[:, 0, :]
+    out["max"] = torch.where(m > 0, hidden, torch.full_like(hidden, -1e30)).amax(1)
+    w = torch.arange(1, S + 1, dtype=torch.float64).view(1, S, 1) * m
+    out["weighted_mean"] = (hidden * w).sum(1) / w.sum(1).clamp(min=1.0)
+    res = {}
+    for k, v in out.items():
+        # the reference forms the norm in the compute dtype (f32 on CPU) and
+        # clamps at f32::MAX; in float64 the clamp is a no-op except for the
+        # max-pool all-padding row, handled identically by taking the f32 norm.
+        n32 = torch.sqrt((v.to(torch.float32) ** 2).sum(-1, keepdim=True)).to(torch.float64)
+        n = torch.sqrt((v ** 2).sum(-1, keepdim=True))
+        n = torch.where(torch.isinf(n32), torch.full_like(n, float(np.finfo(np.float32).max)), n)
+        res[k] = v / n.clamp(min=1e-12)
+    return res
+
+
+def hf_bert_hidden(weights: dict, cfg: BertConfig, ids, mask) -> np.ndarray:
+    from transformers import BertConfig as HFBertConfig, BertModel
+    hcfg = HFBertConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                        num_hidden_layers=cfg.num_hidden_layers,
+                        num_attention_heads=cfg.num_attention_heads,
+                        intermediate_size=cfg.intermediate_size, hidden_act="gelu",
+                        hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0,
+                        max_position_embeddings=cfg.max_position_embeddings,
+                        type_vocab_size=cfg.type_vocab_size,
+                        layer_norm_eps=cfg.layer_norm_eps)
+    hcfg._attn_implementation = "eager"
+    model = BertModel(hcfg, add_pooling_layer=False).eval().to(torch.float64)
+    sd = {k[5:] if k.startswith("bert.") else k: torch.from_numpy(np.asarray(v, dtype=np.float64))
+          for k, v in weights.items()}
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [k for k in missing if not k.endswith("position_ids") and "token_type_ids" not in k]
+    assert not missing and not unexpected, (missing, unexpected)
+    with torch.no_grad():
+        out = model(input_ids=torch.from_numpy(ids.astype(np.int64)),
+                    attention_mask=torch.from_numpy(mask.astype(np.int64)),
+                    token_type_ids=torch.zeros(ids.shape, dtype=torch.int64))
+    return out.last_hidden_state.numpy()
+
+
+def bert_fixture(name, cfg: BertConfig, seed, lens, S, prefix=""):
+    w = random_bert_weights(cfg, seed)
+    if prefix:
+        w = {prefix + k: v for k, v in w.items()}
+    rng = np.random.default_rng(seed + 1)
+    B = len(lens)
+    ids = np.zeros((B, S), dtype=np.uint32)
+    mask = np.zeros((B, S), dtype=np.uint32)
+    for b, n in enumerate(lens):
+        ids[b, :n] = rng.integers(1, cfg.vocab_size, size=n)
+        mask[b, :n] = 1
+    hidden = hf_bert_hidden(w, cfg, ids, mask)
+    pooled = torch_pool_all(torch.from_numpy(hidden), torch.from_numpy(mask.astype(np.int64)))
+    arrs = {"w::" + k: v for k, v in w.items()}
+    arrs.update({"ids": ids, "mask": mask, "hidden": hidden,
+                 "config_json": np.frombuffer(json.dumps(cfg.to_dict()).encode(), dtype=np.uint8)})
+    arrs.update({"pooled_" + k: v.numpy() for k, v in pooled.items()})
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, {k: v.shape for k, v in arrs.items() if not k.startswith("w::")})
+
+
+def hf_clip_embed(w: dict, cfg: ClipVisionConfig, pixels) -> np.ndarray:
+    from transformers import CLIPVisionConfig, CLIPVisionModelWithProjection
+    hcfg = CLIPVisionConfig(hidden_size=cfg.width, intermediate_size=cfg.mlp,
+                            num_hidden_layers=cfg.layers, num_attention_heads=cfg.heads,
+                            image_size=cfg.image_size, patch_size=cfg.patch_size,
+                            projection_dim=cfg.embed_dim, hidden_act="quick_gelu",
+                            layer_norm_eps=1e-5, num_channels=3)
+    hcfg._attn_implementation = "eager"
+    model = CLIPVisionModelWithProjection(hcfg).eval().to(torch.float64)
+    t = lambda k: torch.from_numpy(np.asarray(w["visual." + k], dtype=np.float64))
+    W = cfg.width
+    sd = {
+        "vision_model.embeddings.class_embedding": t("class_embedding"),
+        "vision_model.embeddings.patch_embedding.weight": t("conv1.weight"),
+        "vision_model.embeddings.position_embedding.weight": t("positional_embedding"),
+        "vision_model.pre_layrnorm.weight": t("ln_pre.weight"),
+        "vision_model.pre_layrnorm.bias": t("ln_pre.bias"),
+        "vision_model.post_layernorm.weight": t("ln_post.weight"),
+        "vision_model.post_layernorm.bias": t("ln_post.bias"),
+        "visual_projection.weight": t("proj").T.contiguous(),
+    }
+    for i in range(cfg.layers):
+        p = f"transformer.resblocks.{i}."
+        q = f"vision_model.encoder.layers.{i}."
+        ipw, ipb = t(p + "attn.in_proj_weight"), t(p + "attn.in_proj_bias")
+        for j, nm in enumerate(("q_proj", "k_proj", "v_proj")):
+            sd[q + f"self_attn.{nm}.weight"] = ipw[j * W:(j + 1) * W]
+            sd[q + f"self_attn.{nm}.bias"] = ipb[j * W:(j + 1) * W]
+        sd[q + "self_attn.out_proj.weight"] = t(p + "attn.out_proj.weight")
+        sd[q + "self_attn.out_proj.bias"] = t(p + "attn.out_proj.bias")
+        sd[q + "layer_norm1.weight"] = t(p + "ln_1.weight")
+        sd[q + "layer_norm1.bias"] = t(p + "ln_1.bias")
+        sd[q + "layer_norm2.weight"] = t(p + "ln_2.weight")
+        sd[q + "layer_norm2.bias"] = t(p + "ln_2.bias")
+        sd[q + "mlp.fc1.weight"] = t(p + "mlp.c_fc.weight")
+        sd[q + "mlp.fc1.bias"] = t(p + "mlp.c_fc.bias")
+        sd[q + "mlp.fc2.weight"] = t(p + "mlp.c_proj.weight")
+        sd[q + "mlp.fc2.bias"] = t(p + "mlp.c_proj.bias")
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [k for k in missing if "position_ids" not in k]
+    assert not missing and not unexpected, (missing, unexpected)
+    px = torch.from_numpy(np.asarray(pixels, dtype=np.float64))
+    with torch.no_grad():
+        if not cfg.global_average_pool:
+            e = model(pixel_values=px).image_embeds
+        else:
+            vm = model.vision_model
+            hs = vm.encoder(inputs_embeds=vm.pre_layrnorm(vm.embeddings(px))).last_hidden_state
+            e = model.visual_projection(vm.post_layernorm(hs[:, 1:, :].mean(1)))
+    e = e.numpy()
+    return e, e / np.maximum(np.linalg.norm(e, axis=-1, keepdims=True), 1e-12)
+
+
+def clip_fixture(name, cfg: ClipVisionConfig, seed, batch):
+    w = random_clip_weights(cfg, seed)
+    pixels = np.random.default_rng(seed + 1).standard_normal(
+        (batch, 3, cfg.image_size, cfg.image_size)).astype(np.float32)
+    raw, normed = hf_clip_embed(w, cfg, pixels)
+    arrs = {"w::" + k: v for k, v in w.items()}
+    arrs.update({"pixels": pixels, "embed_raw": raw, "embed": normed,
+                 "config_json": np.frombuffer(json.dumps(cfg.to_open_clip_config()).encode(), dtype=np.uint8)})
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, raw.shape)
+
+
+def reference_fixture():
+    st = os.path.join(REF_TINY_BERT, "model.safetensors")
+    if not os.path.exists(st):
+        print("reference checkout absent: reference_tiny_bert.npz not regenerated")
+        return
+    from safetensors.numpy import load_file
+    w = load_file(st)
+    cfg = BertConfig.from_dict(json.load(open(os.path.join(REF_TINY_BERT, "config.json"))))
+    # the all-padding-row case of crates/jammi-encoders/tests/it/bert.rs:260-315
+    # plus ragged rows (ids < vocab 256)
+    ids = np.array([[1, 2, 3, 4, 5, 0, 0, 0], [0] * 8, [7, 9, 11, 0, 0, 0, 0, 0],
+                    [101, 50, 60, 70, 80, 90, 100, 102]], dtype=np.uint32)
+    mask = (np.arange(8)[None, :] < np.array([5, 0, 3, 8])[:, None]).astype(np.uint32)
+    hidden = hf_bert_hidden(w, cfg, ids, mask)
+    pooled = torch_pool_all(torch.from_numpy(hidden), torch.from_numpy(mask.astype(np.int64)))
+    sha = hashlib.sha256(open(st, "rb").read()).hexdigest()
+    arrs = {"ids": ids, "mask": mask, "hidden": hidden,
+            "sha256": np.frombuffer(sha.encode(), dtype=np.uint8)}
+    arrs.update({"pooled_" + k: v.numpy() for k, v in pooled.items()})
+    np.savez_compressed(os.path.join(HERE, "reference_tiny_bert.npz"), **arrs)
+    print("wrote reference_tiny_bert.npz sha256", sha)
+
+
+def main():
+    tiny = BertConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=2,
+                      intermediate_size=128, vocab_size=256, max_position_embeddings=128)
+    bert_fixture("tiny_bert_seeded.npz", tiny, seed=1234, lens=[16, 9, 1, 0, 13, 5], S=16)
+    small = BertConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                       intermediate_size=256, vocab_size=512, max_position_embeddings=64)
+    bert_fixture("small_bert_prefixed.npz", small, seed=99, lens=[40, 33, 64, 2, 17], S=64,
+                 prefix="bert.")
+    c = ClipVisionConfig(width=32, layers=1, heads=4, mlp_ratio=4.0, image_size=8,
+                         patch_size=4, embed_dim=16, global_average_pool=True)
+    clip_fixture("tiny_clip_gap.npz", c, seed=7, batch=3)
+    c2 = ClipVisionConfig(width=32, layers=2, heads=4, mlp_ratio=4.0, image_size=8,
+                          patch_size=4, embed_dim=16, global_average_pool=False)
+    clip_fixture("tiny_clip_cls.npz", c2, seed=8, batch=3)
+    reference_fixture()
+
+
+if __name__ == "__main__":
+    main()

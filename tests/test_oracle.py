@@ -1,0 +1,164 @@
+"""Pin the CPU oracle: the reference's known answers and the golden vectors."""
+import hashlib
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from conftest import load_golden
+from oracle import bert as ob
+from oracle import clip as oc
+from oracle import quant as oq
+
+REF_FIXTURE = "/root/reference/cookbook/fixtures/tiny_bert"
+
+
+# ── crates/jammi-encoders/tests/it/pooling.rs:15-83 (known answers) ─────────
+
+def _hidden_fixture():
+    return np.array([[[1.0, 0.0], [0.0, 1.0], [2.0, 2.0]]], dtype=np.float32)
+
+
+def test_pooling_mean_ignores_padding():
+    out = ob.pool_and_normalize(_hidden_fixture(), np.array([[1, 1, 0]]), ob.POOL_MEAN)[0]
+    assert abs(out[0] - 1 / math.sqrt(2)) < 1e-6 and abs(out[1] - 1 / math.sqrt(2)) < 1e-6
+
+
+def test_pooling_mean_all_real():
+    out = ob.pool_and_normalize(_hidden_fixture(), np.array([[1, 1, 1]]), ob.POOL_MEAN)[0]
+    assert abs(np.linalg.norm(out) - 1) < 1e-6 and abs(out[0] - out[1]) < 1e-6
+
+
+def test_pooling_cls():
+    out = ob.pool_and_normalize(_hidden_fixture(), np.array([[1, 1, 1]]), ob.POOL_CLS)[0]
+    assert abs(out[0] - 1) < 1e-6 and abs(out[1]) < 1e-6
+
+
+def test_pooling_max_excludes_padding():
+    out = ob.pool_and_normalize(_hidden_fixture(), np.array([[1, 1, 0]]), ob.POOL_MAX)[0]
+    assert abs(out[0] - 1 / math.sqrt(2)) < 1e-6 and abs(out[1] - 1 / math.sqrt(2)) < 1e-6
+
+
+def test_pooling_weighted_mean():
+    out = ob.pool_and_normalize(_hidden_fixture(), np.array([[1, 1, 1]]), ob.POOL_WEIGHTED_MEAN)[0]
+    d = math.sqrt(113.0)
+    assert abs(out[0] - 7 / d) < 1e-5 and abs(out[1] - 8 / d) < 1e-5
+
+
+def test_pooling_all_padding_row_is_zero_or_finite():
+    # tests/it/bert.rs:260-315: all-padding row -> exact zero for mean and
+    # weighted-mean; finite for max.
+    h = np.random.default_rng(0).standard_normal((2, 5, 8)).astype(np.float32)
+    m = np.array([[1] * 5, [0] * 5])
+    for s in (ob.POOL_MEAN, ob.POOL_WEIGHTED_MEAN, ob.POOL_MAX):
+        out = ob.pool_and_normalize(h, m, s)
+        assert np.all(np.isfinite(out))
+        if s != ob.POOL_MAX:
+            assert np.all(np.abs(out[1]) < 1e-6)
+    # max: -1e30 sentinel, squared norm overflows f32, clamp at f32::MAX
+    out = ob.pool_and_normalize(h, m, ob.POOL_MAX)[1]
+    np.testing.assert_allclose(out, np.float32(-1e30) / np.finfo(np.float32).max, rtol=1e-6)
+
+
+def test_extended_mask_values():
+    ext = ob.extended_attention_mask(np.array([[1, 0, 1]], dtype=np.uint32))
+    assert ext.shape == (1, 1, 1, 3)
+    assert list(ext[0, 0, 0]) == [0.0, -10000.0, 0.0]
+
+
+def test_sequence_too_long():
+    cfg = ob.BertConfig(32, 1, 2, 128, 256, 8)
+    w = ob.random_bert_weights(cfg, 0)
+    with pytest.raises(ob.SequenceTooLong):
+        ob.bert_forward_hidden(w, cfg, np.zeros((1, 9), np.uint32), np.ones((1, 9), np.uint32))
+
+
+# ── golden vectors (HF transformers, float64) ───────────────────────────────
+
+@pytest.mark.parametrize("name", ["tiny_bert_seeded.npz", "small_bert_prefixed.npz"])
+def test_bert_oracle_matches_golden(name):
+    w, g = load_golden(name)
+    cfg = ob.BertConfig.from_dict(json.loads(bytes(g["config_json"]).decode()))
+    valid = g["mask"].astype(bool)
+    h64 = ob.bert_forward_hidden(w, cfg, g["ids"], g["mask"], dtype=np.float64)
+    np.testing.assert_allclose(h64[valid], g["hidden"][valid], atol=1e-9, rtol=0)
+    h32 = ob.bert_forward_hidden(w, cfg, g["ids"], g["mask"], dtype=np.float32)
+    np.testing.assert_allclose(h32[valid], g["hidden"][valid], atol=2e-5, rtol=0)
+    nonempty = g["mask"].sum(1) > 0
+    for pname, pid in ob.POOLING_NAMES.items():
+        out = ob.pool_and_normalize(h64, g["mask"], pid)
+        # CLS of an all-padding row reads a padded position, whose hidden
+        # state depends on the mask constant (-10000 in mask.rs:14-20, the
+        # dtype minimum in transformers); every other strategy masks it out.
+        rows = nonempty if pid == ob.POOL_CLS else slice(None)
+        np.testing.assert_allclose(out[rows], g["pooled_" + pname][rows], atol=1e-9, rtol=0)
+
+
+def test_bert_oracle_on_reference_fixture():
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert.npz"))
+    st = os.path.join(REF_FIXTURE, "model.safetensors")
+    if not os.path.exists(st):
+        pytest.skip("reference checkout not present")
+    assert hashlib.sha256(open(st, "rb").read()).hexdigest() == bytes(z["sha256"]).decode()
+    from safetensors.numpy import load_file
+    w = load_file(st)
+    cfg = ob.BertConfig.from_dict(json.load(open(os.path.join(REF_FIXTURE, "config.json"))))
+    h = ob.bert_forward_hidden(w, cfg, z["ids"], z["mask"])
+    valid = z["mask"].astype(bool)
+    np.testing.assert_allclose(h[valid], z["hidden"][valid], atol=1e-9, rtol=0)
+    nonempty = z["mask"].sum(1) > 0
+    for pname, pid in ob.POOLING_NAMES.items():
+        rows = nonempty if pid == ob.POOL_CLS else slice(None)
+        np.testing.assert_allclose(ob.pool_and_normalize(h, z["mask"], pid)[rows],
+                                   z["pooled_" + pname][rows], atol=1e-9)
+    # all-padding row (row 1) -> exact zero vector for mean pooling
+    assert np.all(ob.pool_and_normalize(h, z["mask"], ob.POOL_MEAN)[1] == 0)
+
+
+@pytest.mark.parametrize("name", ["tiny_clip_gap.npz", "tiny_clip_cls.npz"])
+def test_clip_oracle_matches_golden(name):
+    w, g = load_golden(name)
+    cfg = oc.ClipVisionConfig.from_open_clip_config(json.loads(bytes(g["config_json"]).decode()))
+    raw = oc.clip_vision_forward(w, cfg, g["pixels"])
+    np.testing.assert_allclose(raw, g["embed_raw"], atol=1e-9, rtol=0)
+    np.testing.assert_allclose(oc.l2_normalize_image(raw), g["embed"], atol=1e-9, rtol=0)
+
+
+# ── int8 format: integer-exact properties ───────────────────────────────────
+
+def test_quantize_rows_properties():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((64, 96)).astype(np.float32) * rng.uniform(0.01, 10, size=(64, 1)).astype(np.float32)
+    x[5] = 0.0
+    q, s = oq.quantize_rows(x)
+    assert q.dtype == np.int8 and np.abs(q.astype(int)).max() <= 127
+    # the element of largest magnitude maps to +-127 in every non-zero row
+    nz = np.abs(x).max(1) > 0
+    assert np.all(np.abs(q[nz]).max(1) == 127)
+    assert np.all(q[5] == 0) and s[5] == 0
+    # dequantised error is at most half a step
+    err = np.abs(q.astype(np.float64) * s[:, None] - x)
+    assert np.all(err <= 0.5 * s[:, None] * (1 + 1e-6) + 1e-30)
+
+
+def test_gemm_s8_s32_exact():
+    rng = np.random.default_rng(4)
+    a = rng.integers(-127, 128, size=(33, 4096), dtype=np.int64).astype(np.int8)
+    b = rng.integers(-127, 128, size=(17, 4096), dtype=np.int64).astype(np.int8)
+    a[0, :] = 127; b[0, :] = 127  # the largest possible accumulator at K=4096
+    acc = oq.gemm_s8_s32(a, b)
+    assert acc[0, 0] == 4096 * 127 * 127
+    ref = np.array([[int(np.dot(a[i].astype(object), b[j].astype(object))) for j in range(3)] for i in range(3)])
+    assert np.array_equal(acc[:3, :3], ref)
+
+
+def test_int8_bert_close_to_float():
+    cfg = ob.BertConfig(64, 2, 4, 256, 512, 64)
+    w = ob.random_bert_weights(cfg, 11)
+    ids, mask = ob.random_token_batch(4, 32, [32, 20, 7, 1], seed=5, id_lo=1, id_hi=511, cls_id=1, sep_id=2)
+    ref = ob.pool_and_normalize(ob.bert_forward_hidden(w, cfg, ids, mask), mask)
+    q = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    cos = (ref * q).sum(1)
+    assert np.all(cos > 0.999), cos
