@@ -1,0 +1,356 @@
+// The C ABI (include/jammi_b200.h): argument checks, exception -> status
+// mapping, the thread-local error message and the per-handle lock.
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "jb_model.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+jb_status set_error(jb_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+template <typename F>
+jb_status guarded(F&& f) {
+  try {
+    f();
+    g_last_error.clear();
+    return JB_OK;
+  } catch (const jb::Error& e) {
+    return set_error(e.status, e.msg);
+  } catch (const std::bad_alloc&) {
+    return set_error(JB_ERR_OOM, "host out of memory");
+  } catch (const std::exception& e) {
+    return set_error(JB_ERR_INVALID, e.what());
+  }
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// One error flag per device for the single-op entry points.
+int* op_flag(int device) {
+  static std::mutex mu;
+  static int* flags[64] = {nullptr};
+  if (device < 0 || device >= 64) jb::fail(JB_ERR_INVALID, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!flags[device]) {
+    jb::check_cuda(cudaMalloc(&flags[device], sizeof(int)), "op error flag");
+    jb::check_cuda(cudaMemset(flags[device], 0, sizeof(int)), "op error flag");
+  }
+  return flags[device];
+}
+int current_device() {
+  int d = 0;
+  jb::check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+  return d;
+}
+
+void check_text_args(const jb_model* m, int batch, int max_seq, int pooling) {
+  if (!m) jb::fail(JB_ERR_INVALID, "null model");
+  if (m->family != JB_FAMILY_BERT) jb::fail(JB_ERR_INVALID, "model is not a text encoder");
+  if (batch < 0 || max_seq < 0) jb::fail(JB_ERR_INVALID, "batch and max_seq must be >= 0");
+  if (pooling < JB_POOL_MEAN || pooling > JB_POOL_WEIGHTED_MEAN) jb::fail(JB_ERR_INVALID, "unknown pooling");
+  // Bert::forward_hidden's SequenceTooLong check (bert.rs:263-268)
+  if (max_seq > m->max_pos)
+    jb::fail(JB_ERR_SEQ_TOO_LONG, "sequence length " + std::to_string(max_seq) +
+                                      " exceeds max_position_embeddings " + std::to_string(m->max_pos));
+  if (static_cast<int64_t>(batch) * max_seq > (int64_t(1) << 30))
+    jb::fail(JB_ERR_INVALID, "batch * max_seq too large");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* jb_last_error(void) { return g_last_error.c_str(); }
+
+jb_status jb_model_load(const char* safetensors_path, const char* config_json, int device,
+                        int format, jb_model** out) {
+  return guarded([&] {
+    if (!out) jb::fail(JB_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    *out = jb::model_load(safetensors_path, config_json, device, format);
+  });
+}
+
+void jb_model_free(jb_model* model) {
+  try {
+    jb::model_free(model);
+  } catch (...) {
+  }
+}
+
+jb_status jb_model_get_info(const jb_model* m, jb_model_info* out) {
+  return guarded([&] {
+    if (!m || !out) jb::fail(JB_ERR_INVALID, "null argument");
+    std::memset(out, 0, sizeof(*out));
+    out->family = m->family;
+    out->format = m->format;
+    out->device = m->device;
+    out->hidden = m->hidden;
+    out->output_dim = m->family == JB_FAMILY_BERT ? m->hidden : m->embed_dim;
+    out->layers = m->layers;
+    out->heads = m->heads;
+    out->ffn = m->ffn;
+    out->max_seq = m->max_pos;
+    out->image_size = m->image_size;
+    out->weight_bytes = m->weight_bytes;
+  });
+}
+
+size_t jb_estimate_batch_bytes(const jb_model* m, int batch, int seq) {
+  if (!m || batch < 0 || seq < 0) return 0;
+  return jb::estimate_batch_bytes(m, batch, seq);
+}
+
+jb_status jb_model_sync(jb_model* m, void* stream) {
+  return guarded([&] {
+    if (!m) jb::fail(JB_ERR_INVALID, "null model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::check_device_flag(m, as_stream(stream));
+  });
+}
+
+jb_status jb_model_profile_enable(jb_model* m, int enable) {
+  return guarded([&] {
+    if (!m) jb::fail(JB_ERR_INVALID, "null model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::profile_enable(m, enable != 0);
+  });
+}
+
+jb_status jb_model_profile_read(jb_model* m, double ms[3], int32_t launches[3]) {
+  return guarded([&] {
+    if (!m || !ms || !launches) jb::fail(JB_ERR_INVALID, "null argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    int l[jb::kProfKinds];
+    jb::profile_read(m, ms, l);
+    for (int k = 0; k < jb::kProfKinds; ++k) launches[k] = l[k];
+  });
+}
+
+jb_status jb_encode_text(jb_model* m, const uint32_t* ids, const uint32_t* lens, int batch,
+                         int max_seq, int pooling, float* out, void* stream) {
+  return guarded([&] {
+    check_text_args(m, batch, max_seq, pooling);
+    if (batch == 0) return;
+    if (!ids || !lens || !out) jb::fail(JB_ERR_INVALID, "null buffer");
+    for (int b = 0; b < batch; ++b)
+      if (lens[b] > static_cast<uint32_t>(max_seq)) jb::fail(JB_ERR_INVALID, "a row length exceeds max_seq");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    cudaStream_t s = as_stream(stream);
+    jb::ensure_workspace(m, batch, std::max(max_seq, 1));
+    jb::Workspace& ws = m->ws;
+    jb::check_cuda(cudaMemcpyAsync(ws.ids, ids, size_t(batch) * max_seq * 4, cudaMemcpyHostToDevice, s), "H2D ids");
+    jb::check_cuda(cudaMemcpyAsync(ws.lens, lens, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D lens");
+    jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, s);
+    jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->hidden * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    jb::check_device_flag(m, s);
+  });
+}
+
+jb_status jb_encode_text_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens,
+                                int batch, int max_seq, int pooling, float* d_out, void* stream) {
+  return guarded([&] {
+    check_text_args(m, batch, max_seq, pooling);
+    if (batch == 0) return;
+    if (!d_ids || !d_lens || !d_out) jb::fail(JB_ERR_INVALID, "null buffer");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::ensure_workspace(m, batch, std::max(max_seq, 1));
+    jb::bert_forward_device(m, d_ids, d_lens, batch, max_seq, pooling, d_out, nullptr, as_stream(stream));
+  });
+}
+
+jb_status jb_forward_hidden_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens,
+                                   int batch, int max_seq, float* d_hidden, void* stream) {
+  return guarded([&] {
+    check_text_args(m, batch, max_seq, JB_POOL_MEAN);
+    if (batch == 0) return;
+    if (!d_ids || !d_lens || !d_hidden) jb::fail(JB_ERR_INVALID, "null buffer");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::ensure_workspace(m, batch, std::max(max_seq, 1));
+    jb::bert_forward_device(m, d_ids, d_lens, batch, max_seq, JB_POOL_MEAN, nullptr, d_hidden,
+                            as_stream(stream));
+  });
+}
+
+jb_status jb_encode_image(jb_model* m, const float* pixels, int batch, float* out, void* stream) {
+  return guarded([&] {
+    if (!m || m->family != JB_FAMILY_CLIP_VISION) jb::fail(JB_ERR_INVALID, "model is not a vision encoder");
+    if (batch < 0) jb::fail(JB_ERR_INVALID, "batch must be >= 0");
+    if (batch == 0) return;
+    if (!pixels || !out) jb::fail(JB_ERR_INVALID, "null buffer");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    cudaStream_t s = as_stream(stream);
+    jb::ensure_workspace(m, batch, m->tokens);
+    jb::Workspace& ws = m->ws;
+    const size_t px = size_t(batch) * 3 * m->image_size * m->image_size;
+    jb::check_cuda(cudaMemcpyAsync(ws.pixels, pixels, px * 4, cudaMemcpyHostToDevice, s), "H2D pixels");
+    jb::clip_forward_device(m, ws.pixels, batch, ws.out, s);
+    jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->embed_dim * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    jb::check_device_flag(m, s);
+  });
+}
+
+jb_status jb_encode_image_device(jb_model* m, const float* d_pixels, int batch, float* d_out,
+                                 void* stream) {
+  return guarded([&] {
+    if (!m || m->family != JB_FAMILY_CLIP_VISION) jb::fail(JB_ERR_INVALID, "model is not a vision encoder");
+    if (batch < 0) jb::fail(JB_ERR_INVALID, "batch must be >= 0");
+    if (batch == 0) return;
+    if (!d_pixels || !d_out) jb::fail(JB_ERR_INVALID, "null buffer");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::ensure_workspace(m, batch, m->tokens);
+    jb::clip_forward_device(m, d_pixels, batch, d_out, as_stream(stream));
+  });
+}
+
+// ── single ops ──────────────────────────────────────────────────────────────
+
+jb_status jb_op_sync(void* stream) {
+  return guarded([&] {
+    int* flag = op_flag(current_device());
+    jb::check_cuda(cudaStreamSynchronize(as_stream(stream)), "op");
+    int v = 0;
+    jb::check_cuda(cudaMemcpy(&v, flag, sizeof(int), cudaMemcpyDeviceToHost), "op flag");
+    if (v) {
+      cudaMemset(flag, 0, sizeof(int));
+      jb::fail(v & jb::kErrTimeout ? JB_ERR_TIMEOUT : JB_ERR_CUDA, "device-side wait exceeded its limit");
+    }
+  });
+}
+
+jb_status jb_op_linear(const void* A, int a_dtype, const void* W, int w_dtype, const float* bias,
+                       const void* residual, void* C, int c_dtype, int M, int N, int K,
+                       int epilogue, void* stream) {
+  return guarded([&] {
+    if (a_dtype != w_dtype || (a_dtype != JB_DT_F32 && a_dtype != JB_DT_BF16))
+      jb::fail(JB_ERR_INVALID, "jb_op_linear: A and W must both be f32 or both bf16");
+    if (c_dtype != JB_DT_F32 && c_dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "jb_op_linear: C must be f32 or bf16");
+    if (epilogue < JB_EPI_NONE || epilogue > JB_EPI_RESIDUAL) jb::fail(JB_ERR_INVALID, "unknown epilogue");
+    if (!A || !W || !C || M < 0) jb::fail(JB_ERR_INVALID, "jb_op_linear: null buffer or negative M");
+    jb::GemmArgs g;
+    g.A = A;
+    g.W = W;
+    g.ab_dtype = a_dtype;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.resid = residual;
+    g.C = C;
+    g.c_dtype = c_dtype;
+    g.epi = epilogue;
+    g.err = op_flag(current_device());
+    std::string why;
+    cudaError_t e = jb::launch_gemm(g, as_stream(stream), &why);
+    if (e != cudaSuccess) {
+      if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
+      jb::check_cuda(e, "jb_op_linear");
+    }
+  });
+}
+
+jb_status jb_op_linear_s8(const int8_t* Aq, const float* a_scale, const int8_t* Wq,
+                          const float* w_scale, const float* bias, const void* residual, void* C,
+                          int c_dtype, int M, int N, int K, int epilogue, void* stream) {
+  return guarded([&] {
+    if (c_dtype != JB_DT_F32 && c_dtype != JB_DT_BF16 && c_dtype != JB_DT_S32)
+      jb::fail(JB_ERR_INVALID, "jb_op_linear_s8: C must be s32, f32 or bf16");
+    if (epilogue < JB_EPI_NONE || epilogue > JB_EPI_RESIDUAL) jb::fail(JB_ERR_INVALID, "unknown epilogue");
+    if (!Aq || !Wq || !C || M < 0) jb::fail(JB_ERR_INVALID, "jb_op_linear_s8: null buffer or negative M");
+    jb::GemmArgs g;
+    g.A = Aq;
+    g.W = Wq;
+    g.ab_dtype = JB_DT_S8;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.resid = residual;
+    g.a_scale = a_scale;
+    g.w_scale = w_scale;
+    g.C = C;
+    g.c_dtype = c_dtype;
+    g.epi = epilogue;
+    g.err = op_flag(current_device());
+    std::string why;
+    cudaError_t e = jb::launch_gemm(g, as_stream(stream), &why);
+    if (e != cudaSuccess) {
+      if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
+      jb::check_cuda(e, "jb_op_linear_s8");
+    }
+  });
+}
+
+jb_status jb_op_quantize_rows(const void* x, int x_dtype, int8_t* q, float* scale, int rows,
+                              int cols, void* stream) {
+  return guarded([&] {
+    if (!x || !q || !scale || rows < 0 || cols <= 0) jb::fail(JB_ERR_INVALID, "jb_op_quantize_rows: bad argument");
+    if (x_dtype != JB_DT_F32 && x_dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "x must be f32 or bf16");
+    jb::check_cuda(jb::launch_quantize_rows(x, x_dtype, q, scale, rows, nullptr, cols, as_stream(stream)),
+                   "jb_op_quantize_rows");
+  });
+}
+
+jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamma,
+                          const float* beta, void* y, int dtype, int rows, int cols, float eps,
+                          void* stream) {
+  return guarded([&] {
+    if (!x || !gamma || !beta || !y || rows < 0 || cols <= 0) jb::fail(JB_ERR_INVALID, "jb_op_layernorm: bad argument");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    jb::LnArgs a;
+    a.x = x;
+    a.resid = residual;
+    a.gamma = gamma;
+    a.beta = beta;
+    a.y = y;
+    a.dtype = dtype;
+    a.rows = rows;
+    a.cols = cols;
+    a.eps = eps;
+    jb::check_cuda(jb::launch_layernorm(a, as_stream(stream)), "jb_op_layernorm");
+  });
+}
+
+jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype, int batch,
+                          int heads, int head_dim, int max_len, void* stream) {
+  return guarded([&] {
+    if (!qkv || !cu_seqlens || !ctx || batch < 0 || heads <= 0 || head_dim <= 0 || max_len < 0)
+      jb::fail(JB_ERR_INVALID, "jb_op_attention: bad argument");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    std::string why;
+    cudaError_t e = jb::launch_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len,
+                                         as_stream(stream), &why);
+    if (e != cudaSuccess) {
+      if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
+      jb::check_cuda(e, "jb_op_attention");
+    }
+  });
+}
+
+jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens, float* out,
+                               int batch, int H, int pooling, void* stream) {
+  return guarded([&] {
+    if (!hidden || !cu_seqlens || !out || batch < 0 || H <= 0) jb::fail(JB_ERR_INVALID, "jb_op_pool_normalize: bad argument");
+    if (pooling < JB_POOL_MEAN || pooling > JB_POOL_WEIGHTED_MEAN) jb::fail(JB_ERR_INVALID, "unknown pooling");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    jb::check_cuda(jb::launch_pool_normalize(hidden, dtype, cu_seqlens, out, batch, H, pooling, as_stream(stream)),
+                   "jb_op_pool_normalize");
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// Variable-length self-attention over packed rows.
+//
+// BertSelfAttention::forward (crates/jammi-encoders/src/bert.rs:135-155)
+// computes softmax(Q K^T / sqrt(d) + mask) V on the padded [B, h, S, S]
+// score tensor with an additive -10000 mask (mask.rs:14-20).  exp(s - 10000
+// - max) underflows to exactly 0 in f32 for |s| << 10^4, so excluding padded
+// keys reproduces it; padded query rows are never read by the pooling.  Here
+// every (row, head, 64-query block) is one CTA that streams the row's valid
+// keys only, with an online softmax in f32 registers.
+//
+//   flash_attn_bf16_d64: head_dim 64, bf16; QK^T and PV on mma.sync
+//                        m16n8k16 tensor-core tiles, K/V double-buffered
+//                        through cp.async into 128-byte-swizzled smem.
+//   attn_simt:           any head_dim in {8,16,32,64}, f32 or bf16 (the f32
+//                        compute precision and the tiny fixtures).
+#include <cmath>
+
+#include "jb_common.cuh"
+#include "jb_internal.h"
+
+namespace jb {
+namespace {
+
+constexpr int kFaRows = 64;     // queries per CTA (16 per warp)
+constexpr int kFaKeys = 64;     // keys per pipeline stage
+constexpr int kFaThreads = 128;
+constexpr int kTileBytes = 64 * 128;  // 64 rows x 64 bf16
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  const int sz = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// 64 rows x 8 chunks of 16 B; chunk index XOR (row & 7) avoids bank conflicts.
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int row, int chunk) {
+  return tile + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+// Rows >= rows_valid are zero-filled (cp.async with source size 0).
+__device__ __forceinline__ void load_tile(uint32_t tile, const bf16* g, int ld, int rows_valid,
+                                          int tid) {
+#pragma unroll
+  for (int i = tid; i < 64 * 8; i += kFaThreads) {
+    const int r = i >> 3, c = i & 7;
+    const bool ok = r < rows_valid;
+    cp_async16(swz(tile, r, c), ok ? g + static_cast<size_t>(r) * ld + c * 8 : g, ok);
+  }
+}
+
+__global__ void __launch_bounds__(kFaThreads) flash_attn_bf16_d64(const bf16* __restrict__ qkv,
+                                                                  const int* __restrict__ cu,
+                                                                  bf16* __restrict__ ctx, int heads,
+                                                                  float scale_log2) {
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int start = cu[b], n = cu[b + 1] - start;
+  const int q0 = qb * kFaRows;
+  if (q0 >= n) return;
+  const int H = heads * 64, ld = 3 * H;
+  __shared__ __align__(1024) uint8_t sm[5 * kTileBytes];
+  const uint32_t sQ = smem_u32(sm);
+  const uint32_t sK0 = sQ + kTileBytes, sV0 = sQ + 2 * kTileBytes;
+  const uint32_t sK1 = sQ + 3 * kTileBytes, sV1 = sQ + 4 * kTileBytes;
+  const bf16* gQ = qkv + static_cast<size_t>(start + q0) * ld + h * 64;
+  const bf16* gK = qkv + static_cast<size_t>(start) * ld + H + h * 64;
+  const bf16* gV = gK + H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  load_tile(sQ, gQ, ld, n - q0, tid);
+  load_tile(sK0, gK, ld, n, tid);
+  load_tile(sV0, gV, ld, n, tid);
+  cp_async_commit();
+
+  const int nkb = (n + kFaKeys - 1) / kFaKeys;
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  uint32_t qf[4][4];
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const uint32_t sK = (kb & 1) ? sK1 : sK0, sV = (kb & 1) ? sV1 : sV0;
+    if (kb + 1 < nkb) {
+      const size_t off = static_cast<size_t>(kb + 1) * kFaKeys * ld;
+      load_tile((kb & 1) ? sK0 : sK1, gK + off, ld, n - (kb + 1) * kFaKeys, tid);
+      load_tile((kb & 1) ? sV0 : sV1, gV + off, ld, n - (kb + 1) * kFaKeys, tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const int r = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int c = 2 * ks + (lane >> 4);
+        ldsm_x4(swz(sQ, r, c), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+      }
+    }
+    // S = Q K^T for this warp's 16 queries x 64 keys
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int r = np * 16 + (lane & 7) + 8 * (lane >> 4);
+        const int c = 2 * ks + ((lane >> 3) & 1);
+        ldsm_x4(swz(sK, r, c), b0, b1, b2, b3);
+        mma16816(s[2 * np], qf[ks], b0, b1);
+        mma16816(s[2 * np + 1], qf[ks], b2, b3);
+      }
+    }
+    // mask keys beyond the row's length, then the online softmax update
+    const int kbase = kb * kFaKeys;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kbase + nt * 8 + 2 * (lane & 3) + (e & 1);
+        float v = s[nt][e] * scale_log2;
+        if (key >= n) v = -INFINITY;
+        s[nt][e] = v;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - mn0);
+      s[nt][1] = exp2f(s[nt][1] - mn0);
+      s[nt][2] = exp2f(s[nt][2] - mn1);
+      s[nt][3] = exp2f(s[nt][3] - mn1);
+      rs0 += s[nt][0] + s[nt][1];
+      rs1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * a0 + rs0;
+    l1 = l1 * a1 + rs1;
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      o[dt][0] *= a0;
+      o[dt][1] *= a0;
+      o[dt][2] *= a1;
+      o[dt][3] *= a1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 4; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int c = 2 * dp + (lane >> 4);
+        ldsm_x4_t(swz(sV, r, c), b0, b1, b2, b3);
+        mma16816(o[2 * dp], a, b0, b1);
+        mma16816(o[2 * dp + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.f / l0, i1 = 1.f / l1;
+  const int r0 = q0 + warp * 16 + (lane >> 2), r1 = r0 + 8;
+#pragma unroll
+  for (int dt = 0; dt < 8; ++dt) {
+    const int col = h * 64 + dt * 8 + 2 * (lane & 3);
+    if (r0 < n)
+      *reinterpret_cast<__nv_bfloat162*>(ctx + static_cast<size_t>(start + r0) * H + col) =
+          __floats2bfloat162_rn(o[dt][0] * i0, o[dt][1] * i0);
+    if (r1 < n)
+      *reinterpret_cast<__nv_bfloat162*>(ctx + static_cast<size_t>(start + r1) * H + col) =
+          __floats2bfloat162_rn(o[dt][2] * i1, o[dt][3] * i1);
+  }
+}
+
+constexpr int kSimtRows = 64;
+constexpr int kSimtKeys = 64;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kSimtRows) attn_simt(const T* __restrict__ qkv,
+                                                      const int* __restrict__ cu,
+                                                      T* __restrict__ ctx, int heads, float scale) {
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int start = cu[b], n = cu[b + 1] - start;
+  if (blockIdx.x * kSimtRows >= n) return;
+  const int q = blockIdx.x * kSimtRows + threadIdx.x;
+  const int H = heads * D, ld = 3 * H;
+  __shared__ float Ks[kSimtKeys][D + 1];
+  __shared__ float Vs[kSimtKeys][D + 1];
+  const bool active = q < n;
+  float qv[D], o[D];
+  float m = -INFINITY, l = 0.f;
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+    qv[d] = active ? to_f(qkv[static_cast<size_t>(start + q) * ld + h * D + d]) : 0.f;
+    o[d] = 0.f;
+  }
+  for (int k0 = 0; k0 < n; k0 += kSimtKeys) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kSimtKeys * D; i += kSimtRows) {
+      const int r = i / D, d = i % D;
+      const bool ok = k0 + r < n;
+      const size_t base = static_cast<size_t>(start + k0 + r) * ld + h * D + d;
+      Ks[r][d] = ok ? to_f(qkv[base + H]) : 0.f;
+      Vs[r][d] = ok ? to_f(qkv[base + 2 * H]) : 0.f;
+    }
+    __syncthreads();
+    if (active) {
+      const int kn = min(kSimtKeys, n - k0);
+      for (int j = 0; j < kn; ++j) {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) s = fmaf(qv[d], Ks[j][d], s);
+        s *= scale;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn);
+        const float p = expf(s - mn);
+        l = l * corr + p;
+#pragma unroll
+        for (int d = 0; d < D; ++d) o[d] = fmaf(p, Vs[j][d], o[d] * corr);
+        m = mn;
+      }
+    }
+  }
+  if (active) {
+    const float inv = 1.f / l;
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      ctx[static_cast<size_t>(start + q) * H + h * D + d] = from_f<T>(o[d] * inv);
+  }
+}
+
+template <typename T>
+cudaError_t launch_simt(const void* qkv, const int* cu, void* ctx, int batch, int heads, int d,
+                        int max_len, cudaStream_t s, std::string* why) {
+  dim3 grid((max_len + kSimtRows - 1) / kSimtRows, heads, batch);
+  const float scale = 1.0f / sqrtf(static_cast<float>(d));
+  const T* q = static_cast<const T*>(qkv);
+  T* c = static_cast<T*>(ctx);
+  switch (d) {
+    case 8: attn_simt<T, 8><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
+    case 16: attn_simt<T, 16><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
+    case 32: attn_simt<T, 32><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
+    case 64: attn_simt<T, 64><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
+    default:
+      if (why) *why = "attention: head_dim must be 8, 16, 32 or 64";
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
+                             int heads, int head_dim, int max_len, cudaStream_t s,
+                             std::string* why) {
+  if (batch == 0 || max_len == 0) return cudaSuccess;
+  if (batch > 65535 || heads > 65535) {
+    if (why) *why = "attention: batch and heads must be <= 65535";
+    return cudaErrorInvalidValue;
+  }
+  if (dtype == JB_DT_BF16 && head_dim == 64) {
+    dim3 grid((max_len + kFaRows - 1) / kFaRows, heads, batch);
+    const float scale_log2 = 1.4426950408889634f / sqrtf(64.f);
+    flash_attn_bf16_d64<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu,
+                                                    static_cast<bf16*>(ctx), heads, scale_log2);
+    return cudaGetLastError();
+  }
+  if (dtype == JB_DT_BF16) return launch_simt<bf16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why);
+  return launch_simt<float>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why);
+}
+
+}  // namespace jb

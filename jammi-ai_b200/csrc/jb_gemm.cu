@@ -1,0 +1,500 @@
+// Linear layers: C = epi(A . W^T + bias).
+//
+// bf16 and int8 operands run on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in TMEM, operands staged by TMA with 128-byte
+// swizzle); f32 operands run on a SIMT kernel (the f32 compute precision,
+// whose parity bar is 1e-4 and which tf32 tensor cores would not meet).
+//
+// tcgen05 kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile [128 x 128 B] + W tile [BN x 128 B] per stage
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, dequant / bias /
+//               activation / residual, vectorised global stores
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "jb_common.cuh"
+#include "jb_internal.h"
+
+namespace jb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kRowBytes = 128;  // one 128-byte swizzle row of K per stage
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct TcCfg {
+  static constexpr int A_BYTES = kBM * kRowBytes;
+  static constexpr int B_BYTES = BN * kRowBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_FIT = (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+};
+
+struct EpiParams {
+  void* C;
+  int ldc;
+  int c_dtype;
+  int epi;
+  const float* bias;
+  const void* resid;
+  int ldr;
+  const float* a_scale;
+  const float* w_scale;
+  int M;
+  const int* dM;
+  int N;
+  int K;
+  int* err;
+};
+
+__device__ __forceinline__ float apply_epi(float v, int epi) {
+  if (epi == JB_EPI_GELU) return gelu_erf(v);
+  if (epi == JB_EPI_QUICK_GELU) return quick_gelu(v);
+  return v;
+}
+
+// Stores 32 consecutive accumulator columns of one row.
+template <bool S8>
+__device__ __forceinline__ void store_chunk(const EpiParams& p, int row, int col0,
+                                            const uint32_t (&r)[32]) {
+  const int ncols = min(32, p.N - col0);
+  const size_t off = static_cast<size_t>(row) * p.ldc + col0;
+  if (p.c_dtype == JB_DT_S32) {
+    int* c = static_cast<int*>(p.C) + off;
+    if (ncols == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<int4*>(c + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) c[j] = static_cast<int>(r[j]);
+    }
+    return;
+  }
+  float v[32];
+  if constexpr (S8) {
+    const float as = p.a_scale[row];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float ws = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.f;
+      v[j] = static_cast<float>(static_cast<int>(r[j])) * (as * ws);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  }
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += (j < ncols) ? __ldg(p.bias + col0 + j) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = apply_epi(v[j], p.epi);
+  const size_t roff = static_cast<size_t>(row) * p.ldr + col0;
+  if (p.c_dtype == JB_DT_BF16) {
+    bf16* c = static_cast<bf16*>(p.C) + off;
+    if (ncols == 32) {
+      if (p.epi == JB_EPI_RESIDUAL) {
+        const bf16* rs = static_cast<const bf16*>(p.resid) + roff;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 raw = *reinterpret_cast<const uint4*>(rs + j);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 f = __bfloat1622float2(h[e]);
+            v[j + 2 * e] += f.x;
+            v[j + 2 * e + 1] += f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 out;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(c + j) = out;
+      }
+    } else {
+      const bf16* rs = static_cast<const bf16*>(p.resid) + roff;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < ncols) {
+          float x = v[j];
+          if (p.epi == JB_EPI_RESIDUAL) x += __bfloat162float(rs[j]);
+          c[j] = __float2bfloat16_rn(x);
+        }
+      }
+    }
+  } else {  // f32 output
+    float* c = static_cast<float*>(p.C) + off;
+    const float* rs = static_cast<const float*>(p.resid) + roff;
+    if (ncols == 32) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        if (p.epi == JB_EPI_RESIDUAL) {
+          float4 q = *reinterpret_cast<const float4*>(rs + j);
+          o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
+        }
+        *reinterpret_cast<float4*>(c + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) c[j] = v[j] + (p.epi == JB_EPI_RESIDUAL ? rs[j] : 0.f);
+    }
+  }
+}
+
+template <bool S8, int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const EpiParams p) {
+  using Cfg = TcCfg<BN>;
+  constexpr int kElemsPerRow = S8 ? 128 : 64;  // K elements per 128-byte row
+  constexpr int kSteps = 4;                    // 32-byte MMA K steps per row
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (Cfg::STAGES + s); };
+  auto tfull_bar = [&](int i) { return bars + 8u * (2 * Cfg::STAGES + i); };
+  auto tempty_bar = [&](int i) { return bars + 8u * (2 * Cfg::STAGES + 2 + i); };
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(gbase + Cfg::STAGES * Cfg::STAGE_BYTES + 8 * (2 * Cfg::STAGES + 4));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = p.dM ? min(*p.dM, p.M) : p.M;
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int total = m_tiles * n_tiles;
+  const int kb_count = (p.K + kElemsPerRow - 1) / kElemsPerRow;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull_bar(i), 1);
+      mbar_init(tempty_bar(i), 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && kb_count > 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int mb = t / n_tiles, nb = t % n_tiles;
+        bool ok = true;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(empty_bar(stage), ph ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t sa = base + stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, kb * kElemsPerRow, mb * kBM, full_bar(stage));
+          tma_load_2d(sa + Cfg::A_BYTES, &tmB, kb * kElemsPerRow, nb * BN, full_bar(stage));
+          if (++stage == Cfg::STAGES) { stage = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && kb_count > 0) {
+      constexpr uint32_t idesc = S8 ? idesc_s8_s32(kBM, BN) : idesc_bf16_f32(kBM, BN);
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(full_bar(stage), ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = base + stage * Cfg::STAGE_BYTES;
+#pragma unroll
+          for (int k = 0; k < kSteps; ++k) {
+            const uint64_t ad = umma_desc_sw128(sa + 32u * k);
+            const uint64_t bd = umma_desc_sw128(sa + Cfg::A_BYTES + 32u * k);
+            if constexpr (S8)
+              mma_s8(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else
+              mma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit(empty_bar(stage));
+          if (++stage == Cfg::STAGES) { stage = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+    }
+  } else {
+    // Epilogue: warp w may read TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int t = blockIdx.x; t < total && kb_count > 0; t += gridDim.x) {
+      const int mb = t / n_tiles, nb = t % n_tiles;
+      bool ok = mbar_wait(tfull_bar(acc), acc_ph, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int col0 = nb * BN + c;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_wait_ld();
+        if (row < M) store_chunk<S8>(p, row, col0, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag && p.err) atomicOr(p.err, kErrTimeout);
+}
+
+// ── f32 SIMT kernel ─────────────────────────────────────────────────────────
+constexpr int kSimtTile = 64;
+constexpr int kSimtK = 16;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__ A,
+                                                       const float* __restrict__ W, EpiParams p) {
+  __shared__ float As[kSimtK][kSimtTile + 4];
+  __shared__ float Ws[kSimtK][kSimtTile + 4];
+  const int M = p.dM ? min(*p.dM, p.M) : p.M;
+  const int m0 = blockIdx.y * kSimtTile, n0 = blockIdx.x * kSimtTile;
+  if (m0 >= M) return;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < p.K; k0 += kSimtK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = threadIdx.x + i * 256;
+      const int r = idx / kSimtK, kk = idx % kSimtK;
+      const int gk = k0 + kk;
+      As[kk][r] = (m0 + r < M && gk < p.K) ? A[static_cast<size_t>(m0 + r) * p.K + gk] : 0.f;
+      Ws[kk][r] = (n0 + r < p.N && gk < p.K) ? W[static_cast<size_t>(n0 + r) * p.K + gk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kSimtK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Ws[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = m0 + ty * 4 + i;
+    if (row >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = n0 + tx * 4 + j;
+      if (col >= p.N) continue;
+      float v = acc[i][j] + (p.bias ? p.bias[col] : 0.f);
+      v = apply_epi(v, p.epi);
+      if (p.epi == JB_EPI_RESIDUAL) {
+        const size_t ro = static_cast<size_t>(row) * p.ldr + col;
+        v += (p.c_dtype == JB_DT_BF16) ? __bfloat162float(static_cast<const bf16*>(p.resid)[ro])
+                                       : static_cast<const float*>(p.resid)[ro];
+      }
+      const size_t o = static_cast<size_t>(row) * p.ldc + col;
+      if (p.c_dtype == JB_DT_BF16)
+        static_cast<bf16*>(p.C)[o] = __float2bfloat16_rn(v);
+      else
+        static_cast<float*>(p.C)[o] = v;
+    }
+  }
+}
+
+// ── host side ───────────────────────────────────────────────────────────────
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D K-major map over [rows, k_elems] with a (128-byte x box_rows) box.
+bool make_map(CUtensorMap* map, const void* ptr, bool s8, int rows, int k_elems, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int esz = s8 ? 1 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_elems), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k_elems) * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytes / esz), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool S8, int BN>
+cudaError_t launch_tc(const GemmArgs& g, const EpiParams& p, cudaStream_t s, std::string* why) {
+  using Cfg = TcCfg<BN>;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, g.A, S8, g.M, g.K, kBM) || !make_map(&mb, g.W, S8, g.N, g.K, BN)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed (pointer alignment or shape)";
+    return cudaErrorInvalidValue;
+  }
+  auto kern = gemm_tc_kernel<S8, BN>;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  (void)configured_dev;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+  if (e != cudaSuccess) return e;
+  const int m_tiles = (g.M + kBM - 1) / kBM;
+  const int n_tiles = (g.N + BN - 1) / BN;
+  const int grid = std::min(num_sms(dev), m_tiles * n_tiles);
+  kern<<<grid, kGemmThreads, Cfg::SMEM, s>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int num_sms(int device) {
+  static int cached[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (!cached[device]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    cached[device] = n > 0 ? n : 148;
+  }
+  return cached[device];
+}
+
+cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why) {
+  if (g.M < 0 || g.N <= 0 || g.K <= 0) {
+    if (why) *why = "linear: M, N, K must be positive";
+    return cudaErrorInvalidValue;
+  }
+  if (g.M == 0) return cudaSuccess;
+  EpiParams p;
+  p.C = g.C;
+  p.ldc = g.ldc ? g.ldc : g.N;
+  p.c_dtype = g.c_dtype;
+  p.epi = g.epi;
+  p.bias = g.bias;
+  p.resid = g.resid;
+  p.ldr = g.ldr ? g.ldr : g.N;
+  p.a_scale = g.a_scale;
+  p.w_scale = g.w_scale;
+  p.M = g.M;
+  p.dM = g.dM;
+  p.N = g.N;
+  p.K = g.K;
+  p.err = g.err;
+  if (g.epi == JB_EPI_RESIDUAL && !g.resid) {
+    if (why) *why = "linear: residual epilogue without a residual tensor";
+    return cudaErrorInvalidValue;
+  }
+  if (g.ab_dtype == JB_DT_F32) {
+    if (g.c_dtype != JB_DT_F32 && g.c_dtype != JB_DT_BF16) {
+      if (why) *why = "linear(f32): output must be f32 or bf16";
+      return cudaErrorInvalidValue;
+    }
+    dim3 grid((g.N + kSimtTile - 1) / kSimtTile, (g.M + kSimtTile - 1) / kSimtTile);
+    gemm_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(g.A),
+                                         static_cast<const float*>(g.W), p);
+    return cudaGetLastError();
+  }
+  const bool s8 = g.ab_dtype == JB_DT_S8;
+  if (!s8 && g.ab_dtype != JB_DT_BF16) {
+    if (why) *why = "linear: unsupported operand dtype";
+    return cudaErrorInvalidValue;
+  }
+  // TMA: row strides must be multiples of 16 bytes, bases 16-byte aligned.
+  const int esz = s8 ? 1 : 2;
+  if ((g.K * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(g.A) & 15) ||
+      (reinterpret_cast<uintptr_t>(g.W) & 15)) {
+    if (why) *why = "linear: K*elem_size must be a multiple of 16 and A/W 16-byte aligned";
+    return cudaErrorInvalidValue;
+  }
+  if (s8 && g.c_dtype != JB_DT_S32 && (!g.a_scale || !g.w_scale)) {
+    if (why) *why = "linear(int8): dequantised output needs a_scale and w_scale";
+    return cudaErrorInvalidValue;
+  }
+  if (!s8 && g.c_dtype == JB_DT_S32) {
+    if (why) *why = "linear(bf16): s32 output is only defined for int8 operands";
+    return cudaErrorInvalidValue;
+  }
+  if ((p.ldc % 8) || (reinterpret_cast<uintptr_t>(g.C) & 15) ||
+      (g.resid && ((p.ldr % 8) || (reinterpret_cast<uintptr_t>(g.resid) & 15)))) {
+    if (why) *why = "linear: C/residual must be 16-byte aligned with row strides multiple of 8";
+    return cudaErrorInvalidValue;
+  }
+  if (g.N >= 512 || g.N % 256 == 0)
+    return s8 ? launch_tc<true, 256>(g, p, s, why) : launch_tc<false, 256>(g, p, s, why);
+  if (g.N >= 128)
+    return s8 ? launch_tc<true, 128>(g, p, s, why) : launch_tc<false, 128>(g, p, s, why);
+  return s8 ? launch_tc<true, 64>(g, p, s, why) : launch_tc<false, 64>(g, p, s, why);
+}
+
+}  // namespace jb

@@ -1,0 +1,114 @@
+// Internal launcher interface shared by the kernels and the host runtime.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/jammi_b200.h"
+
+namespace jb {
+
+// Device error flag bits (atomicOr into a caller-owned int): 1 = a bounded
+// wait gave up, 2 = token id out of range, 4 = row length above max_seq.
+constexpr int kErrTimeout = 1;
+
+// y = epi(A[M,K] . W[N,K]^T (+ bias)) with an optional residual; see
+// jb_op_linear / jb_op_linear_s8 for the meaning of every field.
+struct GemmArgs {
+  const void* A = nullptr;
+  const void* W = nullptr;
+  int ab_dtype = JB_DT_BF16;  // JB_DT_F32 | JB_DT_BF16 | JB_DT_S8 (A and W alike)
+  int M = 0;                  // rows the buffers hold (upper bound of the live count)
+  const int* dM = nullptr;    // optional live row count in device memory (<= M)
+  int N = 0, K = 0;
+  const float* bias = nullptr;
+  const void* resid = nullptr;
+  int ldr = 0;
+  const float* a_scale = nullptr;  // int8: per-row activation scale
+  const float* w_scale = nullptr;  // int8: per-column weight scale
+  void* C = nullptr;
+  int ldc = 0;
+  int c_dtype = JB_DT_BF16;
+  int epi = JB_EPI_NONE;
+  int* err = nullptr;  // device flag set when a bounded wait gives up
+};
+
+// Returns cudaSuccess or an error; *why receives a message for invalid shapes.
+cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why);
+
+struct LnArgs {
+  const void* x = nullptr;
+  const void* resid = nullptr;
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  void* y = nullptr;
+  int8_t* yq = nullptr;   // optional fused per-row int8 quantisation of y
+  float* yscale = nullptr;
+  int dtype = JB_DT_BF16;
+  int rows = 0;
+  const int* drows = nullptr;
+  int cols = 0;
+  float eps = 1e-12f;
+};
+cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s);
+
+cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
+                                 const int* drows, int cols, cudaStream_t s);
+
+// BERT embeddings: word[ids] + type[0] + pos[p] -> LayerNorm, written packed
+// at row cu[b] + p for p < len[b].
+struct EmbedArgs {
+  const uint32_t* ids = nullptr;  // [batch, max_seq]
+  const int* cu = nullptr;        // [batch + 1]
+  const void* word = nullptr;     // [vocab, H]
+  const void* pos = nullptr;      // [max_pos, H]
+  const void* type0 = nullptr;    // [H]
+  const float* gamma = nullptr;
+  const float* beta = nullptr;
+  void* y = nullptr;
+  int8_t* yq = nullptr;
+  float* yscale = nullptr;
+  int dtype = JB_DT_BF16;
+  int batch = 0, max_seq = 0, H = 0, vocab = 0;
+  float eps = 1e-12f;
+  int* err = nullptr;  // set (bit 2) on an out-of-range token id
+};
+cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
+
+cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
+                             int heads, int head_dim, int max_len, cudaStream_t s,
+                             std::string* why);
+
+cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
+                                  int batch, int H, int pooling, cudaStream_t s);
+
+// cu[0] = 0, cu[b+1] = cu[b] + min(len[b], max_seq); total also to *d_total.
+// Lengths above max_seq set bit 4 of *err.
+cudaError_t launch_lens_to_cu(const uint32_t* lens, int batch, int max_seq, int* cu, int* d_total,
+                              int* err, cudaStream_t s);
+
+// Scatter packed f32-converted hidden rows back to a zero-filled [B, S, H].
+cudaError_t launch_unpack_hidden(const void* packed, int dtype, const int* cu, float* out,
+                                 int batch, int max_seq, int H, cudaStream_t s);
+
+// ViT: pixels [B,3,I,I] f32 -> patches [B*g*g, 3*p*p] (dtype), (c, ky, kx) order.
+cudaError_t launch_patchify(const float* px, void* patches, int dtype, int batch, int image,
+                            int patch, cudaStream_t s);
+// ViT: x[b, 0] = cls + pos[0]; x[b, i] = patch_out[b, i-1] + pos[i]; then LN.
+cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const void* pos,
+                                const float* gamma, const float* beta, void* y, int dtype,
+                                int batch, int tokens, int W, float eps, cudaStream_t s);
+// ViT pooling before ln_post: CLS token (gap = 0) or mean of tokens 1.. (gap = 1), then LN.
+cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* beta, void* y,
+                               int dtype, int batch, int tokens, int W, int gap, float eps,
+                               cudaStream_t s);
+// cu[b] = b * tokens for b in [0, batch] (fixed-length rows, e.g. ViT tokens).
+cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s);
+// Row-wise x / clamp(||x||, 1e-12) over f32 [rows, cols], in place.
+cudaError_t launch_l2_rows(float* x, int rows, int cols, cudaStream_t s);
+
+int num_sms(int device);
+
+}  // namespace jb

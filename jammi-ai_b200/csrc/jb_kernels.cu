@@ -1,0 +1,589 @@
+// Memory-bound kernels of the encoder forward: embeddings + LayerNorm,
+// (residual +) LayerNorm with optional fused per-token int8 quantisation,
+// per-row int8 quantisation, pooling + L2 normalisation, and the ViT
+// patch / CLS / pooling helpers.  One warp per row with 16-byte vector
+// loads; all statistics in f32.
+#include <cfloat>
+
+#include "jb_common.cuh"
+#include "jb_internal.h"
+
+namespace jb {
+namespace {
+
+constexpr int kRowsPerBlock = 8;  // warps per 256-thread block
+
+// 16-byte vector of T: 8 bf16 or 4 f32.
+template <typename T> struct Vec;
+template <> struct Vec<bf16> {
+  static constexpr int N = 8;
+  __device__ static void load(const bf16* p, float* v) {
+    uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+  __device__ static void store(bf16* p, const float* v) {
+    uint4 raw;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    *reinterpret_cast<uint4*>(p) = raw;
+  }
+  // value as it will be read back after the store (bf16 rounding)
+  __device__ static float rounded(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+};
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float* v) {
+    float4 f = *reinterpret_cast<const float4*>(p);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  }
+  __device__ static void store(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+  __device__ static float rounded(float x) { return x; }
+};
+
+// Per-token symmetric int8 quantisation of values already rounded to the
+// stored dtype: scale = amax/127, q = clamp(rint(x * (127/amax))).
+__device__ __forceinline__ int8_t quant1(float x, float inv) {
+  int q = __float2int_rn(x * inv);
+  q = max(-127, min(127, q));
+  return static_cast<int8_t>(q);
+}
+
+// Normalises the row held in v[] (nvec vectors of Vec<T>::N per lane slot),
+// writes y (and optionally int8 + scale).  Called by one full warp.
+template <typename T, int MAXV>
+__device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec, int cols, int lane,
+                                          const float* __restrict__ gamma,
+                                          const float* __restrict__ beta, float eps, T* yrow,
+                                          int8_t* qrow, float* scale_out) {
+  constexpr int VN = Vec<T>::N;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i)
+    if (lane + i * 32 < nvec)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) s += v[i * VN + e];
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i)
+    if (lane + i * 32 < nvec)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) {
+        const float d = v[i * VN + e] - mean;
+        ss += d * d;
+      }
+  const float var = warp_sum(ss) / static_cast<float>(cols);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + i * 32;
+    if (vi < nvec) {
+      float o[VN];
+#pragma unroll
+      for (int e = 0; e < VN; ++e) {
+        const int c = vi * VN + e;
+        o[e] = (v[i * VN + e] - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
+        v[i * VN + e] = Vec<T>::rounded(o[e]);
+        amax = fmaxf(amax, fabsf(v[i * VN + e]));
+      }
+      Vec<T>::store(yrow + vi * VN, o);
+    }
+  }
+  if (qrow) {
+    amax = warp_max(amax);
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        char4 q[VN / 4];
+#pragma unroll
+        for (int e = 0; e < VN / 4; ++e)
+          q[e] = make_char4(quant1(v[i * VN + 4 * e], inv), quant1(v[i * VN + 4 * e + 1], inv),
+                            quant1(v[i * VN + 4 * e + 2], inv), quant1(v[i * VN + 4 * e + 3], inv));
+#pragma unroll
+        for (int e = 0; e < VN / 4; ++e) reinterpret_cast<char4*>(qrow + vi * VN)[e] = q[e];
+      }
+    }
+    if (lane == 0) *scale_out = amax / 127.0f;
+  }
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) layernorm_kernel(LnArgs a) {
+  constexpr int VN = Vec<T>::N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  const int R = a.drows ? min(*a.drows, a.rows) : a.rows;
+  if (row >= R) return;
+  const int nvec = a.cols / VN;
+  const T* x = static_cast<const T*>(a.x) + static_cast<size_t>(row) * a.cols;
+  const T* r = a.resid ? static_cast<const T*>(a.resid) + static_cast<size_t>(row) * a.cols : nullptr;
+  float v[MAXV * VN];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + i * 32;
+    if (vi < nvec) {
+      Vec<T>::load(x + vi * VN, v + i * VN);
+      if (r) {
+        float t[VN];
+        Vec<T>::load(r + vi * VN, t);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) v[i * VN + e] += t[e];
+      }
+    }
+  }
+  ln_finish<T, MAXV>(v, nvec, a.cols, lane, a.gamma, a.beta, a.eps,
+                     static_cast<T*>(a.y) + static_cast<size_t>(row) * a.cols,
+                     a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
+                     a.yscale ? a.yscale + row : nullptr);
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
+  constexpr int VN = Vec<T>::N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos_idx = blockIdx.x * kRowsPerBlock + warp;
+  if (pos_idx >= a.batch * a.max_seq) return;
+  const int b = pos_idx / a.max_seq, p = pos_idx % a.max_seq;
+  const int start = a.cu[b], len = a.cu[b + 1] - start;
+  if (p >= len) return;
+  uint32_t id = a.ids[static_cast<size_t>(b) * a.max_seq + p];
+  if (id >= static_cast<uint32_t>(a.vocab)) {
+    if (lane == 0 && a.err) atomicOr(a.err, 2);
+    id = 0;
+  }
+  const int nvec = a.H / VN;
+  const T* w = static_cast<const T*>(a.word) + static_cast<size_t>(id) * a.H;
+  const T* pe = static_cast<const T*>(a.pos) + static_cast<size_t>(p) * a.H;
+  const T* te = static_cast<const T*>(a.type0);
+  float v[MAXV * VN];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + i * 32;
+    if (vi < nvec) {
+      float t1[VN], t2[VN];
+      Vec<T>::load(w + vi * VN, v + i * VN);
+      Vec<T>::load(te + vi * VN, t1);
+      Vec<T>::load(pe + vi * VN, t2);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) v[i * VN + e] += t1[e] + t2[e];
+    }
+  }
+  const size_t row = static_cast<size_t>(start + p);
+  ln_finish<T, MAXV>(v, nvec, a.H, lane, a.gamma, a.beta, a.eps, static_cast<T*>(a.y) + row * a.H,
+                     a.yq ? a.yq + row * a.H : nullptr, a.yscale ? a.yscale + row : nullptr);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int8_t* q,
+                                                            float* scale, int rows,
+                                                            const int* drows, int cols) {
+  constexpr int VN = Vec<T>::N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  const int R = drows ? min(*drows, rows) : rows;
+  if (row >= R) return;
+  const T* xr = x + static_cast<size_t>(row) * cols;
+  const int nvec = cols / VN;
+  float amax = 0.f;
+  for (int vi = lane; vi < nvec; vi += 32) {
+    float v[VN];
+    Vec<T>::load(xr + vi * VN, v);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  }
+  amax = warp_max(amax);
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  int8_t* qr = q + static_cast<size_t>(row) * cols;
+  for (int vi = lane; vi < nvec; vi += 32) {
+    float v[VN];
+    Vec<T>::load(xr + vi * VN, v);
+#pragma unroll
+    for (int e = 0; e < VN / 4; ++e)
+      reinterpret_cast<char4*>(qr + vi * VN)[e] =
+          make_char4(quant1(v[4 * e], inv), quant1(v[4 * e + 1], inv), quant1(v[4 * e + 2], inv),
+                     quant1(v[4 * e + 3], inv));
+  }
+  if (lane == 0) scale[row] = amax / 127.0f;
+}
+
+// ── pooling + L2 (pooling.rs:31-148) ──────────────────────────────────────
+constexpr int kPoolThreads = 128;
+constexpr int kPoolMaxCols = 8;  // columns per thread -> H <= 1024
+
+__device__ __forceinline__ float block_sum_128(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPoolThreads / 32; ++i) t += red[i];
+  return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPoolThreads) pool_normalize_kernel(const T* __restrict__ hidden,
+                                                                      const int* __restrict__ cu,
+                                                                      float* __restrict__ out, int H,
+                                                                      int pooling) {
+  __shared__ float red[kPoolThreads / 32];
+  const int b = blockIdx.x;
+  const int start = cu[b], n = cu[b + 1] - start;
+  float acc[kPoolMaxCols];
+  const float init = (pooling == JB_POOL_MAX) ? -1e30f : 0.f;
+#pragma unroll
+  for (int k = 0; k < kPoolMaxCols; ++k) acc[k] = init;
+  if (pooling == JB_POOL_CLS) {
+    if (n > 0) {
+#pragma unroll
+      for (int k = 0; k < kPoolMaxCols; ++k) {
+        const int c = threadIdx.x + k * kPoolThreads;
+        if (c < H) acc[k] = to_f(hidden[static_cast<size_t>(start) * H + c]);
+      }
+    }
+  } else {
+    for (int t = 0; t < n; ++t) {
+      const T* hr = hidden + static_cast<size_t>(start + t) * H;
+      const float w = static_cast<float>(t + 1);
+#pragma unroll
+      for (int k = 0; k < kPoolMaxCols; ++k) {
+        const int c = threadIdx.x + k * kPoolThreads;
+        if (c < H) {
+          const float x = to_f(hr[c]);
+          if (pooling == JB_POOL_MAX)
+            acc[k] = fmaxf(acc[k], x);
+          else if (pooling == JB_POOL_WEIGHTED_MEAN)
+            acc[k] += x * w;
+          else
+            acc[k] += x;
+        }
+      }
+    }
+    float den = 1.f;
+    if (pooling == JB_POOL_MEAN) den = fmaxf(static_cast<float>(n), 1.f);
+    if (pooling == JB_POOL_WEIGHTED_MEAN)
+      den = fmaxf(0.5f * static_cast<float>(n) * static_cast<float>(n + 1), 1.f);
+    if (pooling != JB_POOL_MAX) {
+#pragma unroll
+      for (int k = 0; k < kPoolMaxCols; ++k) acc[k] = acc[k] / den;
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kPoolMaxCols; ++k)
+    if (threadIdx.x + k * kPoolThreads < H) ss += acc[k] * acc[k];
+  ss = block_sum_128(ss, red);
+  // clamp(||x||, 1e-12, f32::MAX): an overflowing square sum (the -1e30
+  // max-pool sentinel of an all-padding row) clamps to f32::MAX.
+  const float norm = fminf(fmaxf(sqrtf(ss), 1e-12f), FLT_MAX);
+#pragma unroll
+  for (int k = 0; k < kPoolMaxCols; ++k) {
+    const int c = threadIdx.x + k * kPoolThreads;
+    if (c < H) out[static_cast<size_t>(b) * H + c] = acc[k] / norm;
+  }
+}
+
+__global__ void l2_rows_kernel(float* x, int cols) {
+  __shared__ float red[kPoolThreads / 32];
+  float* r = x + static_cast<size_t>(blockIdx.x) * cols;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kPoolThreads) ss += r[c] * r[c];
+  ss = block_sum_128(ss, red);
+  const float norm = fmaxf(sqrtf(ss), 1e-12f);
+  for (int c = threadIdx.x; c < cols; c += kPoolThreads) r[c] = r[c] / norm;
+}
+
+// Exclusive scan of clamped lengths into cu[0..batch]; one 1024-thread block.
+__global__ void __launch_bounds__(1024) lens_to_cu_kernel(const uint32_t* lens, int batch,
+                                                          int max_seq, int* cu, int* total,
+                                                          int* err) {
+  __shared__ int part[1024];
+  const int per = (batch + 1023) / 1024;
+  const int b0 = threadIdx.x * per;
+  int s = 0;
+  for (int i = 0; i < per; ++i) {
+    const int b = b0 + i;
+    if (b < batch) {
+      uint32_t l = lens[b];
+      if (l > static_cast<uint32_t>(max_seq)) {
+        if (err) atomicOr(err, 4);
+        l = max_seq;
+      }
+      s += static_cast<int>(l);
+    }
+  }
+  part[threadIdx.x] = s;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int v = threadIdx.x >= off ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int run = part[threadIdx.x] - s;  // exclusive prefix of this thread's chunk
+  for (int i = 0; i < per; ++i) {
+    const int b = b0 + i;
+    if (b < batch) {
+      cu[b] = run;
+      run += static_cast<int>(min(lens[b], static_cast<uint32_t>(max_seq)));
+    }
+  }
+  if (threadIdx.x == 1023) {
+    cu[batch] = part[1023];
+    if (total) *total = part[1023];
+  }
+}
+
+template <typename T>
+__global__ void unpack_hidden_kernel(const T* packed, const int* cu, float* out, int batch,
+                                     int max_seq, int H) {
+  const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t total = static_cast<size_t>(batch) * max_seq * H;
+  if (idx >= total) return;
+  const int c = idx % H;
+  const int p = (idx / H) % max_seq;
+  const int b = idx / (static_cast<size_t>(H) * max_seq);
+  const int start = cu[b], n = cu[b + 1] - start;
+  out[idx] = p < n ? to_f(packed[static_cast<size_t>(start + p) * H + c]) : 0.f;
+}
+
+template <typename T>
+__global__ void patchify_kernel(const float* px, T* out, int batch, int image, int patch) {
+  const int g = image / patch;
+  const int K = 3 * patch * patch;
+  const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t total = static_cast<size_t>(batch) * g * g * K;
+  if (idx >= total) return;
+  const int k = idx % K;
+  const size_t prow = idx / K;
+  const int b = prow / (g * g);
+  const int pidx = prow % (g * g);
+  const int gy = pidx / g, gx = pidx % g;
+  const int c = k / (patch * patch), ky = (k / patch) % patch, kx = k % patch;
+  const float v = px[((static_cast<size_t>(b) * 3 + c) * image + gy * patch + ky) * image +
+                     gx * patch + kx];
+  out[idx] = from_f<T>(v);
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) vit_embed_ln_kernel(const T* patch_out, const T* cls,
+                                                           const T* pos, const float* gamma,
+                                                           const float* beta, T* y, int batch,
+                                                           int tokens, int W, float eps) {
+  constexpr int VN = Vec<T>::N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  if (row >= batch * tokens) return;
+  const int b = row / tokens, i = row % tokens;
+  const T* src = i == 0 ? cls : patch_out + (static_cast<size_t>(b) * (tokens - 1) + i - 1) * W;
+  const T* pe = pos + static_cast<size_t>(i) * W;
+  const int nvec = W / VN;
+  float v[MAXV * VN];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int vi = lane + k * 32;
+    if (vi < nvec) {
+      float t[VN];
+      Vec<T>::load(src + vi * VN, v + k * VN);
+      Vec<T>::load(pe + vi * VN, t);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) v[k * VN + e] += t[e];
+    }
+  }
+  ln_finish<T, MAXV>(v, nvec, W, lane, gamma, beta, eps, y + static_cast<size_t>(row) * W, nullptr,
+                     nullptr);
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(32) vit_pool_ln_kernel(const T* x, const float* gamma,
+                                                         const float* beta, T* y, int tokens,
+                                                         int W, int gap, float eps) {
+  constexpr int VN = Vec<T>::N;
+  const int lane = threadIdx.x;
+  const int b = blockIdx.x;
+  const int nvec = W / VN;
+  float v[MAXV * VN];
+#pragma unroll
+  for (int k = 0; k < MAXV * VN; ++k) v[k] = 0.f;
+  const int t0 = gap ? 1 : 0, t1 = gap ? tokens : 1;
+  for (int t = t0; t < t1; ++t) {
+    const T* xr = x + (static_cast<size_t>(b) * tokens + t) * W;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      const int vi = lane + k * 32;
+      if (vi < nvec) {
+        float tmp[VN];
+        Vec<T>::load(xr + vi * VN, tmp);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) v[k * VN + e] += tmp[e];
+      }
+    }
+  }
+  if (gap) {
+    const float inv_n = 1.0f / static_cast<float>(tokens - 1);
+#pragma unroll
+    for (int k = 0; k < MAXV * VN; ++k) v[k] *= inv_n;
+  }
+  ln_finish<T, MAXV>(v, nvec, W, lane, gamma, beta, eps, y + static_cast<size_t>(b) * W, nullptr,
+                     nullptr);
+}
+
+__global__ void fill_cu_uniform_kernel(int* cu, int batch, int tokens) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b <= batch) cu[b] = b * tokens;
+}
+
+inline unsigned blocks_for(size_t n, unsigned per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+}  // namespace
+
+cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
+  if (a.rows == 0) return cudaSuccess;
+  const unsigned grid = blocks_for(a.rows, kRowsPerBlock);
+  if (a.dtype == JB_DT_BF16) {
+    if (a.cols % 8 || a.cols > 1024) return cudaErrorInvalidValue;
+    layernorm_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (a.cols % 4 || a.cols > 1024) return cudaErrorInvalidValue;
+    layernorm_kernel<float, 8><<<grid, 256, 0, s>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(a.batch) * a.max_seq;
+  if (n == 0) return cudaSuccess;
+  const unsigned grid = blocks_for(n, kRowsPerBlock);
+  if (a.dtype == JB_DT_BF16) {
+    if (a.H % 8 || a.H > 1024) return cudaErrorInvalidValue;
+    embed_ln_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (a.H % 4 || a.H > 1024) return cudaErrorInvalidValue;
+    embed_ln_kernel<float, 8><<<grid, 256, 0, s>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
+                                 const int* drows, int cols, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const unsigned grid = blocks_for(rows, kRowsPerBlock);
+  if (dtype == JB_DT_BF16) {
+    if (cols % 8) return cudaErrorInvalidValue;
+    quantize_rows_kernel<bf16><<<grid, 256, 0, s>>>(static_cast<const bf16*>(x), q, scale, rows,
+                                                    drows, cols);
+  } else {
+    if (cols % 4) return cudaErrorInvalidValue;
+    quantize_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q, scale, rows,
+                                                     drows, cols);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
+                                  int batch, int H, int pooling, cudaStream_t s) {
+  if (batch == 0) return cudaSuccess;
+  if (H > kPoolThreads * kPoolMaxCols || pooling < 0 || pooling > 3) return cudaErrorInvalidValue;
+  if (dtype == JB_DT_BF16)
+    pool_normalize_kernel<bf16><<<batch, kPoolThreads, 0, s>>>(static_cast<const bf16*>(hidden), cu,
+                                                               out, H, pooling);
+  else
+    pool_normalize_kernel<float><<<batch, kPoolThreads, 0, s>>>(static_cast<const float*>(hidden),
+                                                                cu, out, H, pooling);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lens_to_cu(const uint32_t* lens, int batch, int max_seq, int* cu, int* d_total,
+                              int* err, cudaStream_t s) {
+  lens_to_cu_kernel<<<1, 1024, 0, s>>>(lens, batch, max_seq, cu, d_total, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpack_hidden(const void* packed, int dtype, const int* cu, float* out,
+                                 int batch, int max_seq, int H, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(batch) * max_seq * H;
+  if (n == 0) return cudaSuccess;
+  if (dtype == JB_DT_BF16)
+    unpack_hidden_kernel<bf16><<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(packed),
+                                                                  cu, out, batch, max_seq, H);
+  else
+    unpack_hidden_kernel<float><<<blocks_for(n, 256), 256, 0, s>>>(
+        static_cast<const float*>(packed), cu, out, batch, max_seq, H);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_patchify(const float* px, void* patches, int dtype, int batch, int image,
+                            int patch, cudaStream_t s) {
+  const int g = image / patch;
+  const size_t n = static_cast<size_t>(batch) * g * g * 3 * patch * patch;
+  if (n == 0) return cudaSuccess;
+  if (dtype == JB_DT_BF16)
+    patchify_kernel<bf16><<<blocks_for(n, 256), 256, 0, s>>>(px, static_cast<bf16*>(patches), batch,
+                                                             image, patch);
+  else
+    patchify_kernel<float><<<blocks_for(n, 256), 256, 0, s>>>(px, static_cast<float*>(patches),
+                                                              batch, image, patch);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const void* pos,
+                                const float* gamma, const float* beta, void* y, int dtype,
+                                int batch, int tokens, int W, float eps, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(batch) * tokens;
+  if (n == 0) return cudaSuccess;
+  const unsigned grid = blocks_for(n, kRowsPerBlock);
+  if (dtype == JB_DT_BF16) {
+    if (W % 8 || W > 1024) return cudaErrorInvalidValue;
+    vit_embed_ln_kernel<bf16, 4><<<grid, 256, 0, s>>>(
+        static_cast<const bf16*>(patch_out), static_cast<const bf16*>(cls),
+        static_cast<const bf16*>(pos), gamma, beta, static_cast<bf16*>(y), batch, tokens, W, eps);
+  } else {
+    if (W % 4 || W > 1024) return cudaErrorInvalidValue;
+    vit_embed_ln_kernel<float, 8><<<grid, 256, 0, s>>>(
+        static_cast<const float*>(patch_out), static_cast<const float*>(cls),
+        static_cast<const float*>(pos), gamma, beta, static_cast<float*>(y), batch, tokens, W, eps);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* beta, void* y,
+                               int dtype, int batch, int tokens, int W, int gap, float eps,
+                               cudaStream_t s) {
+  if (batch == 0) return cudaSuccess;
+  if (dtype == JB_DT_BF16) {
+    if (W % 8 || W > 1024) return cudaErrorInvalidValue;
+    vit_pool_ln_kernel<bf16, 4><<<batch, 32, 0, s>>>(static_cast<const bf16*>(x), gamma, beta,
+                                                     static_cast<bf16*>(y), tokens, W, gap, eps);
+  } else {
+    if (W % 4 || W > 1024) return cudaErrorInvalidValue;
+    vit_pool_ln_kernel<float, 8><<<batch, 32, 0, s>>>(static_cast<const float*>(x), gamma, beta,
+                                                      static_cast<float*>(y), tokens, W, gap, eps);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s) {
+  fill_cu_uniform_kernel<<<blocks_for(static_cast<size_t>(batch) + 1, 256), 256, 0, s>>>(cu, batch, tokens);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_l2_rows(float* x, int rows, int cols, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  l2_rows_kernel<<<rows, kPoolThreads, 0, s>>>(x, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace jb

@@ -1,0 +1,754 @@
+// Model loading (safetensors + HF / OpenCLIP config), weight packing and the
+// encoder forward passes.
+//
+// BERT: CandleBackend::load BERT arm (crates/jammi-ai/src/model/backend/candle.rs:1585-1604)
+//       -> Bert::builder().build (crates/jammi-encoders/src/bert.rs:489-587).
+// ViT:  OpenCLIP arm (candle.rs:1474-1501) -> OpenClipVisionTransformer::load
+//       (crates/jammi-ai/src/model/backend/open_clip_vit.rs:258-303).
+#include "jb_model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <sstream>
+
+#include "jb_json.h"
+
+namespace jb {
+
+[[noreturn]] void fail(jb_status st, const std::string& msg) { throw Error{st, msg}; }
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return;
+  cudaGetLastError();  // clear a sticky-free launch error
+  if (e == cudaErrorMemoryAllocation)
+    fail(JB_ERR_OOM, std::string(what) + ": CUDA out of memory");
+  fail(JB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+  cudaGetDevice(&prev);
+  if (prev != dev) check_cuda(cudaSetDevice(dev), "cudaSetDevice");
+}
+DeviceGuard::~DeviceGuard() {
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+}
+
+namespace {
+
+// ── safetensors ────────────────────────────────────────────────────────────
+struct StTensor {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  size_t begin = 0, end = 0;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto d : shape) n *= d;
+    return n;
+  }
+};
+
+float half_to_float(uint16_t h) {
+  const uint32_t sign = (h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1F, man = h & 0x3FF;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // subnormal: renormalise
+      int e = -1;
+      do { ++e; man <<= 1; } while (!(man & 0x400));
+      bits = sign | ((127 - 15 - e) << 23) | ((man & 0x3FF) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+uint16_t float_to_bf16(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;  // NaN
+  u += 0x7FFFu + ((u >> 16) & 1u);                      // round to nearest even
+  return static_cast<uint16_t>(u >> 16);
+}
+
+struct SafeTensors {
+  std::vector<char> file;
+  size_t data_start = 0;
+  std::map<std::string, StTensor> t;
+
+  explicit SafeTensors(const std::string& path) {
+    std::ifstream in(path, std::ios::binary | std::ios::ate);
+    if (!in) fail(JB_ERR_IO, "cannot open weights file " + path);
+    const std::streamsize size = in.tellg();
+    in.seekg(0);
+    file.resize(static_cast<size_t>(size));
+    if (!in.read(file.data(), size)) fail(JB_ERR_IO, "cannot read weights file " + path);
+    if (file.size() < 8) fail(JB_ERR_IO, "safetensors file too short");
+    uint64_t hlen = 0;
+    std::memcpy(&hlen, file.data(), 8);
+    if (8 + hlen > file.size()) fail(JB_ERR_IO, "safetensors header length out of range");
+    data_start = 8 + hlen;
+    Json h;
+    try {
+      h = Json::parse(std::string(file.data() + 8, hlen));
+    } catch (const std::exception& e) {
+      fail(JB_ERR_IO, std::string("safetensors header: ") + e.what());
+    }
+    for (auto& kv : h.obj) {
+      if (kv.first == "__metadata__") continue;
+      StTensor st;
+      st.dtype = kv.second.str_or("dtype", "");
+      if (const Json* sh = kv.second.get("shape"))
+        for (auto& d : sh->arr) st.shape.push_back(static_cast<int64_t>(d.num));
+      const Json* off = kv.second.get("data_offsets");
+      if (!off || off->arr.size() != 2) fail(JB_ERR_IO, "safetensors: bad offsets for " + kv.first);
+      st.begin = static_cast<size_t>(off->arr[0].num);
+      st.end = static_cast<size_t>(off->arr[1].num);
+      if (data_start + st.end > file.size() || st.begin > st.end)
+        fail(JB_ERR_IO, "safetensors: tensor out of range: " + kv.first);
+      t[kv.first] = st;
+    }
+  }
+  bool has(const std::string& k) const { return t.count(k) != 0; }
+  const StTensor& get(const std::string& k) const {
+    auto it = t.find(k);
+    if (it == t.end()) fail(JB_ERR_IO, "missing tensor " + k);
+    return it->second;
+  }
+  const char* ptr(const StTensor& s) const { return file.data() + data_start + s.begin; }
+
+  std::vector<float> f32(const std::string& k, int64_t expect) const {
+    const StTensor& s = get(k);
+    if (s.numel() != expect)
+      fail(JB_ERR_IO, "tensor " + k + " has " + std::to_string(s.numel()) + " elements, expected " +
+                          std::to_string(expect));
+    std::vector<float> out(static_cast<size_t>(expect));
+    const char* p = ptr(s);
+    if (s.dtype == "F32") {
+      std::memcpy(out.data(), p, expect * 4);
+    } else if (s.dtype == "BF16") {
+      for (int64_t i = 0; i < expect; ++i) {
+        uint16_t v;
+        std::memcpy(&v, p + 2 * i, 2);
+        const uint32_t u = static_cast<uint32_t>(v) << 16;
+        std::memcpy(&out[i], &u, 4);
+      }
+    } else if (s.dtype == "F16") {
+      for (int64_t i = 0; i < expect; ++i) {
+        uint16_t v;
+        std::memcpy(&v, p + 2 * i, 2);
+        out[i] = half_to_float(v);
+      }
+    } else if (s.dtype == "F64") {
+      for (int64_t i = 0; i < expect; ++i) {
+        double v;
+        std::memcpy(&v, p + 8 * i, 8);
+        out[i] = static_cast<float>(v);
+      }
+    } else {
+      fail(JB_ERR_IO, "tensor " + k + ": unsupported dtype " + s.dtype);
+    }
+    return out;
+  }
+  std::vector<float> f32_or(const std::string& k, int64_t n, float fill) const {
+    return has(k) ? f32(k, n) : std::vector<float>(static_cast<size_t>(n), fill);
+  }
+  std::vector<int8_t> i8(const std::string& k, int64_t expect) const {
+    const StTensor& s = get(k);
+    if (s.numel() != expect || (s.dtype != "I8" && s.dtype != "U8"))
+      fail(JB_ERR_IO, "tensor " + k + " must be I8 with " + std::to_string(expect) + " elements");
+    std::vector<int8_t> out(static_cast<size_t>(expect));
+    std::memcpy(out.data(), ptr(s), expect);
+    return out;
+  }
+};
+
+// ── device uploads ─────────────────────────────────────────────────────────
+void* dev_alloc(jb_model* m, size_t bytes) {
+  void* p = nullptr;
+  check_cuda(cudaMalloc(&p, std::max<size_t>(bytes, 16)), "weight allocation");
+  m->weight_allocs.push_back(p);
+  m->weight_bytes += static_cast<int64_t>(bytes);
+  return p;
+}
+void* upload_bytes(jb_model* m, const void* src, size_t bytes) {
+  void* p = dev_alloc(m, bytes);
+  check_cuda(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice), "weight upload");
+  return p;
+}
+float* upload_f32(jb_model* m, const std::vector<float>& v) {
+  return static_cast<float*>(upload_bytes(m, v.data(), v.size() * 4));
+}
+// Upload in the model's activation dtype (f32 or bf16).
+void* upload_act(jb_model* m, const std::vector<float>& v) {
+  if (m->act == JB_DT_F32) return upload_f32(m, v);
+  std::vector<uint16_t> h(v.size());
+  for (size_t i = 0; i < v.size(); ++i) h[i] = float_to_bf16(v[i]);
+  return upload_bytes(m, h.data(), h.size() * 2);
+}
+
+// Symmetric per-row int8: amax/127 scale, rint(w * 127/amax), f32 arithmetic.
+void quantize_rows_host(const float* w, int rows, int cols, int8_t* q, float* scale) {
+  for (int r = 0; r < rows; ++r) {
+    const float* x = w + static_cast<size_t>(r) * cols;
+    float amax = 0.f;
+    for (int c = 0; c < cols; ++c) amax = std::max(amax, std::fabs(x[c]));
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    for (int c = 0; c < cols; ++c) {
+      const float v = std::nearbyint(x[c] * inv);
+      q[static_cast<size_t>(r) * cols + c] = static_cast<int8_t>(std::max(-127.f, std::min(127.f, v)));
+    }
+    scale[r] = amax / 127.0f;
+  }
+}
+
+// A linear whose output rows are the concatenation of `names` (each
+// "<prefix>.weight" [n_i, K] + "<prefix>.bias" [n_i]).
+Linear load_linear(jb_model* m, const SafeTensors& st, const std::vector<std::string>& names,
+                   const std::vector<int>& rows, int K, bool has_bias, int fmt_dtype,
+                   bool transpose_src = false) {
+  Linear L;
+  L.K = K;
+  L.dtype = fmt_dtype;
+  for (int r : rows) L.N += r;
+  std::vector<float> bias;
+  if (fmt_dtype == JB_DT_S8) {
+    std::vector<int8_t> q(static_cast<size_t>(L.N) * K);
+    std::vector<float> sc(L.N);
+    int r0 = 0;
+    for (size_t i = 0; i < names.size(); ++i) {
+      const std::string& nm = names[i];
+      const size_t n = static_cast<size_t>(rows[i]) * K;
+      if (st.has(nm + ".weight_q")) {
+        auto qi = st.i8(nm + ".weight_q", static_cast<int64_t>(n));
+        auto si = st.f32(nm + ".weight_scale", rows[i]);
+        std::memcpy(q.data() + static_cast<size_t>(r0) * K, qi.data(), n);
+        std::memcpy(sc.data() + r0, si.data(), rows[i] * 4);
+      } else {
+        auto w = st.f32(nm + ".weight", static_cast<int64_t>(n));
+        quantize_rows_host(w.data(), rows[i], K, q.data() + static_cast<size_t>(r0) * K,
+                           sc.data() + r0);
+      }
+      r0 += rows[i];
+    }
+    L.w = upload_bytes(m, q.data(), q.size());
+    L.w_scale = upload_f32(m, sc);
+  } else {
+    std::vector<float> w;
+    w.reserve(static_cast<size_t>(L.N) * K);
+    for (size_t i = 0; i < names.size(); ++i) {
+      auto wi = st.f32(names[i] + (transpose_src ? "" : ".weight"),
+                       static_cast<int64_t>(rows[i]) * K);
+      if (transpose_src) {  // stored [K, N] (OpenCLIP proj) -> [N, K]
+        std::vector<float> t(wi.size());
+        for (int k = 0; k < K; ++k)
+          for (int n = 0; n < rows[i]; ++n) t[static_cast<size_t>(n) * K + k] = wi[static_cast<size_t>(k) * rows[i] + n];
+        wi.swap(t);
+      }
+      w.insert(w.end(), wi.begin(), wi.end());
+    }
+    if (fmt_dtype == JB_DT_F32) {
+      L.w = upload_f32(m, w);
+    } else {
+      std::vector<uint16_t> h(w.size());
+      for (size_t i = 0; i < w.size(); ++i) h[i] = float_to_bf16(w[i]);
+      L.w = upload_bytes(m, h.data(), h.size() * 2);
+    }
+  }
+  if (has_bias) {
+    for (size_t i = 0; i < names.size(); ++i) {
+      auto b = st.f32_or(names[i] + ".bias", rows[i], 0.f);
+      bias.insert(bias.end(), b.begin(), b.end());
+    }
+    L.bias = upload_f32(m, bias);
+  }
+  return L;
+}
+
+int linear_dtype(int format) {
+  return format == JB_FMT_F32 ? JB_DT_F32 : (format == JB_FMT_INT8 ? JB_DT_S8 : JB_DT_BF16);
+}
+
+void load_bert(jb_model* m, const SafeTensors& st, const Json& cfg) {
+  m->family = JB_FAMILY_BERT;
+  m->hidden = static_cast<int>(cfg.num_or("hidden_size", 0));
+  m->layers = static_cast<int>(cfg.num_or("num_hidden_layers", 0));
+  m->heads = static_cast<int>(cfg.num_or("num_attention_heads", 0));
+  m->ffn = static_cast<int>(cfg.num_or("intermediate_size", 0));
+  m->vocab = static_cast<int>(cfg.num_or("vocab_size", 0));
+  m->max_pos = static_cast<int>(cfg.num_or("max_position_embeddings", 0));
+  m->type_vocab = static_cast<int>(cfg.num_or("type_vocab_size", 2));
+  m->eps = static_cast<float>(cfg.num_or("layer_norm_eps", 1e-12));
+  const int H = m->hidden, F = m->ffn;
+  if (H <= 0 || m->layers <= 0 || m->heads <= 0 || F <= 0 || m->vocab <= 0 || m->max_pos <= 0 ||
+      H % m->heads)
+    fail(JB_ERR_INVALID, "config.json: incomplete or inconsistent BERT dimensions");
+  if (H > 1024 || H % 8) fail(JB_ERR_INVALID, "hidden_size must be a multiple of 8 and <= 1024");
+  // the "bert." prefix probe of BertBuilder::build (bert.rs:508-517)
+  const std::string p = st.has("bert.embeddings.word_embeddings.weight") ? "bert." : "";
+  m->word = upload_act(m, st.f32(p + "embeddings.word_embeddings.weight", int64_t(m->vocab) * H));
+  m->pos = upload_act(m, st.f32(p + "embeddings.position_embeddings.weight", int64_t(m->max_pos) * H));
+  auto tt = st.f32(p + "embeddings.token_type_embeddings.weight", int64_t(m->type_vocab) * H);
+  tt.resize(H);  // token_type_ids are all zero (bert.rs:269)
+  m->type0 = upload_act(m, tt);
+  m->emb_ln_g = upload_f32(m, st.f32_or(p + "embeddings.LayerNorm.weight", H, 1.f));
+  m->emb_ln_b = upload_f32(m, st.f32_or(p + "embeddings.LayerNorm.bias", H, 0.f));
+  const int ld = linear_dtype(m->format);
+  for (int l = 0; l < m->layers; ++l) {
+    const std::string q = p + "encoder.layer." + std::to_string(l) + ".";
+    BertLayerW w;
+    w.qkv = load_linear(m, st,
+                        {q + "attention.self.query", q + "attention.self.key", q + "attention.self.value"},
+                        {H, H, H}, H, true, ld);
+    w.o = load_linear(m, st, {q + "attention.output.dense"}, {H}, H, true, ld);
+    w.ffn1 = load_linear(m, st, {q + "intermediate.dense"}, {F}, H, true, ld);
+    w.ffn2 = load_linear(m, st, {q + "output.dense"}, {H}, F, true, ld);
+    w.ln1_g = upload_f32(m, st.f32_or(q + "attention.output.LayerNorm.weight", H, 1.f));
+    w.ln1_b = upload_f32(m, st.f32_or(q + "attention.output.LayerNorm.bias", H, 0.f));
+    w.ln2_g = upload_f32(m, st.f32_or(q + "output.LayerNorm.weight", H, 1.f));
+    w.ln2_b = upload_f32(m, st.f32_or(q + "output.LayerNorm.bias", H, 0.f));
+    m->bert_layers.push_back(w);
+  }
+}
+
+void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
+  m->family = JB_FAMILY_CLIP_VISION;
+  const Json* mc = cfg.get("model_cfg");
+  const Json* vc = mc ? mc->get("vision_cfg") : nullptr;
+  if (!mc || !vc) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.vision_cfg'");
+  if (!mc->get("embed_dim")) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.embed_dim'");
+  // defaults of OpenClipVisionConfig::from_open_clip_config (open_clip_vit.rs:45-101)
+  m->hidden = static_cast<int>(vc->num_or("width", 768));
+  m->layers = static_cast<int>(vc->num_or("layers", 12));
+  m->heads = static_cast<int>(vc->num_or("heads", m->hidden / 64));
+  m->ffn = static_cast<int>(m->hidden * vc->num_or("mlp_ratio", 4.0));
+  m->image_size = static_cast<int>(vc->num_or("image_size", 224));
+  m->patch = static_cast<int>(vc->num_or("patch_size", 32));
+  m->embed_dim = static_cast<int>(mc->num_or("embed_dim", 0));
+  m->gap = vc->bool_or("global_average_pool", false);
+  m->eps = 1e-5f;
+  const int W = m->hidden, F = m->ffn, P = m->patch, g = m->image_size / m->patch;
+  m->tokens = g * g + 1;
+  m->max_pos = m->tokens;
+  if (W <= 0 || W % m->heads || W % 8 || W > 1024 || m->embed_dim <= 0 || g <= 0)
+    fail(JB_ERR_INVALID, "OpenCLIP config: unsupported vision dimensions");
+  if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are only defined for BERT encoders");
+  const std::string p = st.has("visual.conv1.weight") ? "visual." : "";
+  const int ld = linear_dtype(m->format);
+  m->conv = load_linear(m, st, {p + "conv1"}, {W}, 3 * P * P, false, ld);
+  m->cls = upload_act(m, st.f32(p + "class_embedding", W));
+  m->vpos = upload_act(m, st.f32(p + "positional_embedding", int64_t(m->tokens) * W));
+  m->ln_pre_g = upload_f32(m, st.f32(p + "ln_pre.weight", W));
+  m->ln_pre_b = upload_f32(m, st.f32(p + "ln_pre.bias", W));
+  for (int l = 0; l < m->layers; ++l) {
+    const std::string q = p + "transformer.resblocks." + std::to_string(l) + ".";
+    ClipBlockW w;
+    // in_proj_weight / in_proj_bias use underscores (open_clip_vit.rs:139-141)
+    {
+      Linear L;
+      L.N = 3 * W;
+      L.K = W;
+      L.dtype = ld;
+      auto wv = st.f32(q + "attn.in_proj_weight", int64_t(3) * W * W);
+      if (ld == JB_DT_F32) {
+        L.w = upload_f32(m, wv);
+      } else {
+        std::vector<uint16_t> h(wv.size());
+        for (size_t i = 0; i < wv.size(); ++i) h[i] = float_to_bf16(wv[i]);
+        L.w = upload_bytes(m, h.data(), h.size() * 2);
+      }
+      L.bias = upload_f32(m, st.f32(q + "attn.in_proj_bias", 3 * W));
+      w.qkv = L;
+    }
+    w.o = load_linear(m, st, {q + "attn.out_proj"}, {W}, W, true, ld);
+    w.fc = load_linear(m, st, {q + "mlp.c_fc"}, {F}, W, true, ld);
+    w.proj = load_linear(m, st, {q + "mlp.c_proj"}, {W}, F, true, ld);
+    w.ln1_g = upload_f32(m, st.f32(q + "ln_1.weight", W));
+    w.ln1_b = upload_f32(m, st.f32(q + "ln_1.bias", W));
+    w.ln2_g = upload_f32(m, st.f32(q + "ln_2.weight", W));
+    w.ln2_b = upload_f32(m, st.f32(q + "ln_2.bias", W));
+    m->clip_blocks.push_back(w);
+  }
+  m->ln_post_g = upload_f32(m, st.f32(p + "ln_post.weight", W));
+  m->ln_post_b = upload_f32(m, st.f32(p + "ln_post.bias", W));
+  m->proj = load_linear(m, st, {p + "proj"}, {m->embed_dim}, W, false, ld, /*transpose_src=*/true);
+}
+
+void free_workspace(Workspace& ws) {
+  for (void* p : ws.bufs) cudaFree(p);
+  ws = Workspace();
+}
+
+size_t esz(int dt) { return dt == JB_DT_F32 ? 4 : 2; }
+
+// Sizes of every workspace buffer for (batch, seq); shared by the allocator
+// and jb_estimate_batch_bytes.
+struct WsPlan {
+  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, pixels, patches, patch_out, pooled;
+  size_t sum() const {
+    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + pixels + patches + patch_out +
+           pooled;
+  }
+};
+size_t round_up(size_t v) { return (v + 255) & ~size_t(255); }
+WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
+  WsPlan p{};
+  const size_t B = batch, S = seq, T = B * S, e = esz(m->act);
+  const size_t H = m->hidden, F = m->ffn;
+  p.ids = round_up(B * S * 4);
+  p.lens = round_up(B * 4);
+  p.cu = round_up((B + 1) * 4);
+  p.total = 256;
+  p.out = round_up(B * std::max<size_t>(H, m->embed_dim) * 4);
+  p.x = round_up(T * H * e);
+  p.qkv = round_up(T * 3 * H * e);
+  p.hf = round_up(T * F * e);
+  if (m->format == JB_FMT_INT8) {
+    p.aq = round_up(T * std::max(H, F));
+    p.as = round_up(T * 4);
+  }
+  if (m->family == JB_FAMILY_CLIP_VISION) {
+    const size_t g = m->image_size / m->patch;
+    p.pixels = round_up(B * 3 * m->image_size * m->image_size * 4);
+    p.patches = round_up(B * g * g * 3 * m->patch * m->patch * e);
+    p.patch_out = round_up(B * g * g * H * e);
+    p.pooled = round_up(B * H * e);
+  }
+  return p;
+}
+
+}  // namespace
+
+size_t estimate_batch_bytes(const jb_model* m, int batch, int seq) {
+  if (m->family == JB_FAMILY_CLIP_VISION) seq = m->tokens;
+  return plan_workspace(m, batch, seq).sum();
+}
+
+void ensure_workspace(jb_model* m, int batch, int seq) {
+  Workspace& ws = m->ws;
+  if (batch <= ws.batch_cap && seq <= ws.seq_cap) return;
+  const int nb = std::max(batch, ws.batch_cap), ns = std::max(seq, ws.seq_cap);
+  free_workspace(ws);
+  const WsPlan p = plan_workspace(m, nb, ns);
+  char* base = nullptr;
+  const size_t total = p.sum();
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&base), total);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(JB_ERR_OOM, "CUDA out of memory: workspace of " + std::to_string(total) + " bytes for batch " +
+                         std::to_string(nb) + " x seq " + std::to_string(ns));
+  }
+  ws.bufs.push_back(base);
+  ws.bytes = total;
+  ws.batch_cap = nb;
+  ws.seq_cap = ns;
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    if (!bytes) return nullptr;
+    void* r = base + off;
+    off += bytes;
+    return r;
+  };
+  ws.ids = static_cast<uint32_t*>(take(p.ids));
+  ws.lens = static_cast<uint32_t*>(take(p.lens));
+  ws.cu = static_cast<int*>(take(p.cu));
+  ws.total = static_cast<int*>(take(p.total));
+  ws.out = static_cast<float*>(take(p.out));
+  ws.x = take(p.x);
+  ws.x1 = take(p.x);
+  ws.y = take(p.x);
+  ws.ctx = take(p.x);
+  ws.qkv = take(p.qkv);
+  ws.hf = take(p.hf);
+  ws.aq = static_cast<int8_t*>(take(p.aq));
+  ws.as = static_cast<float*>(take(p.as));
+  ws.pixels = static_cast<float*>(take(p.pixels));
+  ws.patches = take(p.patches);
+  ws.patch_out = take(p.patch_out);
+  ws.pooled = take(p.pooled);
+}
+
+jb_model* model_load(const char* path, const char* config_json, int device, int format) {
+  if (!path || !config_json) fail(JB_ERR_INVALID, "weights path and config must be non-null");
+  if (format < JB_FMT_F32 || format > JB_FMT_INT8) fail(JB_ERR_INVALID, "unknown weight format");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    fail(JB_ERR_NO_DEVICE, "no CUDA device available (require_gpu)");
+  }
+  if (device < 0 || device >= ndev) fail(JB_ERR_NO_DEVICE, "device ordinal out of range");
+  cudaDeviceProp prop;
+  check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    fail(JB_ERR_NO_DEVICE, "this library is built for sm_100a (B200); device is sm_" +
+                               std::to_string(prop.major * 10 + prop.minor));
+  Json cfg;
+  try {
+    cfg = Json::parse(config_json);
+  } catch (const std::exception& e) {
+    fail(JB_ERR_INVALID, std::string("config json: ") + e.what());
+  }
+  DeviceGuard guard(device);
+  std::unique_ptr<jb_model> m(new jb_model());
+  m->device = device;
+  m->format = format;
+  m->act = format == JB_FMT_F32 ? JB_DT_F32 : JB_DT_BF16;
+  try {
+    SafeTensors st(path);
+    if (cfg.get("model_cfg"))
+      load_clip(m.get(), st, cfg);
+    else
+      load_bert(m.get(), st, cfg);
+    check_cuda(cudaMalloc(&m->d_err, sizeof(int)), "error flag");
+    check_cuda(cudaMemset(m->d_err, 0, sizeof(int)), "error flag");
+  } catch (...) {
+    for (void* p : m->weight_allocs) cudaFree(p);
+    if (m->d_err) cudaFree(m->d_err);
+    throw;
+  }
+  return m.release();
+}
+
+void model_free(jb_model* m) {
+  if (!m) return;
+  {
+    DeviceGuard guard(m->device);
+    cudaDeviceSynchronize();
+    free_workspace(m->ws);
+    for (void* p : m->weight_allocs) cudaFree(p);
+    if (m->d_err) cudaFree(m->d_err);
+    profile_enable(m, false);
+    for (cudaEvent_t e : m->prof_free) cudaEventDestroy(e);
+  }
+  delete m;
+}
+
+namespace {
+cudaEvent_t take_event(jb_model* m) {
+  if (!m->prof_free.empty()) {
+    cudaEvent_t e = m->prof_free.back();
+    m->prof_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e;
+  check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+  return e;
+}
+}  // namespace
+
+ProfScope::ProfScope(jb_model* m_, int kind, cudaStream_t s_) : m(m_), s(s_), on(m_->prof_on) {
+  if (!on) return;
+  rec.kind = kind;
+  rec.a = take_event(m);
+  rec.b = take_event(m);
+  cudaEventRecord(rec.a, s);
+}
+ProfScope::~ProfScope() {
+  if (!on) return;
+  cudaEventRecord(rec.b, s);
+  m->prof_recs.push_back(rec);
+}
+
+void profile_enable(jb_model* m, bool on) {
+  for (auto& r : m->prof_recs) {
+    m->prof_free.push_back(r.a);
+    m->prof_free.push_back(r.b);
+  }
+  m->prof_recs.clear();
+  m->prof_on = on;
+}
+
+void profile_read(jb_model* m, double* ms, int* launches) {
+  for (int k = 0; k < kProfKinds; ++k) {
+    ms[k] = 0;
+    launches[k] = 0;
+  }
+  for (auto& r : m->prof_recs) {
+    check_cuda(cudaEventSynchronize(r.b), "profile");
+    float t = 0;
+    check_cuda(cudaEventElapsedTime(&t, r.a, r.b), "profile");
+    ms[r.kind] += t;
+    launches[r.kind] += 1;
+  }
+}
+
+void check_device_flag(jb_model* m, cudaStream_t s) {
+  check_cuda(cudaStreamSynchronize(s), "forward");
+  int flag = 0;
+  check_cuda(cudaMemcpy(&flag, m->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error flag read");
+  if (!flag) return;
+  cudaMemset(m->d_err, 0, sizeof(int));
+  if (flag & kErrTimeout) fail(JB_ERR_TIMEOUT, "a device-side wait exceeded its limit");
+  if (flag & 2) fail(JB_ERR_INVALID, "token id out of range for the vocabulary");
+  if (flag & 4) fail(JB_ERR_INVALID, "a row length exceeds max_seq");
+  fail(JB_ERR_CUDA, "device error flag " + std::to_string(flag));
+}
+
+#define PROF_MEM_CALL(expr, name)        \
+  do {                                   \
+    ProfScope ps_(m, kProfMemory, s);    \
+    check_cuda((expr), name);            \
+  } while (0)
+
+namespace {
+void run_linear(jb_model* m, const Linear& L, const void* A, const float* a_scale, int Mcap,
+                const int* dM, void* C, int c_dtype, int epi, const void* resid, cudaStream_t s) {
+  GemmArgs g;
+  g.A = A;
+  g.W = L.w;
+  g.ab_dtype = L.dtype;
+  g.M = Mcap;
+  g.dM = dM;
+  g.N = L.N;
+  g.K = L.K;
+  g.bias = L.bias;
+  g.resid = resid;
+  g.a_scale = a_scale;
+  g.w_scale = L.w_scale;
+  g.C = C;
+  g.c_dtype = c_dtype;
+  g.epi = epi;
+  g.err = m->d_err;
+  std::string why;
+  ProfScope ps(m, kProfLinear, s);
+  cudaError_t e = launch_gemm(g, s, &why);
+  if (e != cudaSuccess) {
+    if (!why.empty()) fail(JB_ERR_INVALID, why);
+    check_cuda(e, "linear");
+  }
+}
+void run_ln(jb_model* m, const void* x, const void* resid, const float* g, const float* b, void* y, int8_t* yq,
+            float* ys, int dtype, int rows, const int* drows, int cols, float eps, cudaStream_t s) {
+  LnArgs a;
+  a.x = x;
+  a.resid = resid;
+  a.gamma = g;
+  a.beta = b;
+  a.y = y;
+  a.yq = yq;
+  a.yscale = ys;
+  a.dtype = dtype;
+  a.rows = rows;
+  a.drows = drows;
+  a.cols = cols;
+  a.eps = eps;
+  ProfScope ps(m, kProfMemory, s);
+  check_cuda(launch_layernorm(a, s), "layernorm");
+}
+}  // namespace
+
+void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens, int batch,
+                         int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s) {
+  Workspace& ws = m->ws;
+  const int H = m->hidden, Mcap = batch * max_seq;
+  const bool q8 = m->format == JB_FMT_INT8;
+  const int act = m->act;
+  PROF_MEM_CALL(launch_lens_to_cu(d_lens, batch, max_seq, ws.cu, ws.total, m->d_err, s), "lengths");
+  EmbedArgs ea;
+  ea.ids = d_ids;
+  ea.cu = ws.cu;
+  ea.word = m->word;
+  ea.pos = m->pos;
+  ea.type0 = m->type0;
+  ea.gamma = m->emb_ln_g;
+  ea.beta = m->emb_ln_b;
+  ea.y = ws.x;
+  ea.yq = q8 ? ws.aq : nullptr;
+  ea.yscale = q8 ? ws.as : nullptr;
+  ea.dtype = act;
+  ea.batch = batch;
+  ea.max_seq = max_seq;
+  ea.H = H;
+  ea.vocab = m->vocab;
+  ea.eps = m->eps;
+  ea.err = m->d_err;
+  PROF_MEM_CALL(launch_embed_ln(ea, s), "embeddings");
+  for (const BertLayerW& w : m->bert_layers) {
+    // BertSelfAttention (bert.rs:135-155): fused QKV projection
+    run_linear(m, w.qkv, q8 ? ws.aq : ws.x, ws.as, Mcap, ws.total, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+    std::string why;
+    cudaError_t e;
+    {
+      ProfScope ps(m, kProfAttention, s);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads,
+                                     max_seq, s, &why);
+    }
+    if (e != cudaSuccess) {
+      if (!why.empty()) fail(JB_ERR_INVALID, why);
+      check_cuda(e, "attention");
+    }
+    if (q8) PROF_MEM_CALL(launch_quantize_rows(ws.ctx, act, ws.aq, ws.as, Mcap, ws.total, H, s), "quantize");
+    // BertSelfOutput (bert.rs:164-167): LN(dense(ctx) + x)
+    run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
+    run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
+           Mcap, ws.total, H, m->eps, s);
+    // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1))
+    run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act, JB_EPI_GELU, nullptr, s);
+    if (q8)
+      PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s), "quantize");
+    // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
+    run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);
+    run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
+           Mcap, ws.total, H, m->eps, s);
+  }
+  if (d_hidden)
+    PROF_MEM_CALL(launch_unpack_hidden(ws.x, act, ws.cu, d_hidden, batch, max_seq, H, s), "unpack");
+  if (d_out)
+    PROF_MEM_CALL(launch_pool_normalize(ws.x, act, ws.cu, d_out, batch, H, pooling, s), "pooling");
+}
+
+void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s) {
+  Workspace& ws = m->ws;
+  const int W = m->hidden, T = m->tokens, g = m->image_size / m->patch, act = m->act;
+  const int Mrows = batch * T, Prows = batch * g * g;
+  PROF_MEM_CALL(launch_patchify(d_px, ws.patches, act, batch, m->image_size, m->patch, s), "patchify");
+  // conv1: kernel = stride = patch, no bias (open_clip_vit.rs:259-269, 313)
+  run_linear(m, m->conv, ws.patches, nullptr, Prows, nullptr, ws.patch_out, act, JB_EPI_NONE, nullptr, s);
+  // CLS cat + positional add + ln_pre (open_clip_vit.rs:319-330)
+  PROF_MEM_CALL(launch_vit_embed_ln(ws.patch_out, m->cls, m->vpos, m->ln_pre_g, m->ln_pre_b, ws.x, act,
+                                 batch, T, W, m->eps, s),
+             "vit embed");
+  PROF_MEM_CALL(launch_fill_cu_uniform(ws.cu, batch, T, s), "cu");
+  void* x = ws.x;
+  void* y = ws.y;
+  for (const ClipBlockW& w : m->clip_blocks) {
+    // ResidualAttentionBlock::forward (open_clip_vit.rs:226-236)
+    run_ln(m, x, nullptr, w.ln1_g, w.ln1_b, ws.x1, nullptr, nullptr, act, Mrows, nullptr, W, m->eps, s);
+    run_linear(m, w.qkv, ws.x1, nullptr, Mrows, nullptr, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+    std::string why;
+    cudaError_t e;
+    {
+      ProfScope ps(m, kProfAttention, s);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, T, s, &why);
+    }
+    if (e != cudaSuccess) {
+      if (!why.empty()) fail(JB_ERR_INVALID, why);
+      check_cuda(e, "attention");
+    }
+    run_linear(m, w.o, ws.ctx, nullptr, Mrows, nullptr, y, act, JB_EPI_RESIDUAL, x, s);
+    std::swap(x, y);
+    run_ln(m, x, nullptr, w.ln2_g, w.ln2_b, ws.x1, nullptr, nullptr, act, Mrows, nullptr, W, m->eps, s);
+    run_linear(m, w.fc, ws.x1, nullptr, Mrows, nullptr, ws.hf, act, JB_EPI_QUICK_GELU, nullptr, s);
+    run_linear(m, w.proj, ws.hf, nullptr, Mrows, nullptr, y, act, JB_EPI_RESIDUAL, x, s);
+    std::swap(x, y);
+  }
+  // CLS (or GAP) pool -> ln_post -> proj (open_clip_vit.rs:339-352), then l2_normalize (candle.rs:425-438)
+  PROF_MEM_CALL(launch_vit_pool_ln(x, m->ln_post_g, m->ln_post_b, ws.pooled, act, batch, T, W,
+                                m->gap ? 1 : 0, m->eps, s),
+             "vit pool");
+  run_linear(m, m->proj, ws.pooled, nullptr, batch, nullptr, d_out, JB_DT_F32, JB_EPI_NONE, nullptr, s);
+  PROF_MEM_CALL(launch_l2_rows(d_out, batch, m->embed_dim, s), "l2");
+}
+
+}  // namespace jb

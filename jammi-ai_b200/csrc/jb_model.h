@@ -1,0 +1,129 @@
+// Host-side model handle: device weights, workspace and the encoder forward.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "jb_internal.h"
+
+namespace jb {
+
+// Thrown inside the library and turned into a jb_status at the C boundary.
+struct Error {
+  jb_status status;
+  std::string msg;
+};
+[[noreturn]] void fail(jb_status st, const std::string& msg);
+void check_cuda(cudaError_t e, const char* what);
+
+// Sets the calling thread's current device for a scope, restoring it after.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev);
+  ~DeviceGuard();
+};
+
+struct Linear {
+  void* w = nullptr;         // [N, K] in the operand dtype
+  int dtype = JB_DT_BF16;    // JB_DT_F32 | JB_DT_BF16 | JB_DT_S8
+  float* w_scale = nullptr;  // int8: [N]
+  float* bias = nullptr;     // [N] or null
+  int N = 0, K = 0;
+};
+
+struct BertLayerW {
+  Linear qkv, o, ffn1, ffn2;
+  float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+};
+
+struct ClipBlockW {
+  Linear qkv, o, fc, proj;
+  float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+};
+
+// Kernel classes timed by the profiler.
+enum ProfKind { kProfLinear = 0, kProfAttention = 1, kProfMemory = 2, kProfKinds = 3 };
+struct ProfRec {
+  int kind;
+  cudaEvent_t a, b;
+};
+
+struct Workspace {
+  int batch_cap = 0, seq_cap = 0;
+  size_t bytes = 0;
+  std::vector<void*> bufs;
+  // shared
+  uint32_t* ids = nullptr;
+  uint32_t* lens = nullptr;
+  int* cu = nullptr;
+  int* total = nullptr;
+  float* out = nullptr;
+  void *x = nullptr, *x1 = nullptr, *y = nullptr, *qkv = nullptr, *ctx = nullptr, *hf = nullptr;
+  int8_t* aq = nullptr;
+  float* as = nullptr;
+  // vision
+  float* pixels = nullptr;
+  void *patches = nullptr, *patch_out = nullptr, *pooled = nullptr;
+};
+
+}  // namespace jb
+
+struct jb_model {
+  int family = JB_FAMILY_BERT;
+  int format = JB_FMT_BF16;
+  int device = 0;
+  int act = JB_DT_BF16;  // activation storage dtype
+  // architecture
+  int hidden = 0, layers = 0, heads = 0, ffn = 0, vocab = 0, max_pos = 0, type_vocab = 2;
+  float eps = 1e-12f;
+  int image_size = 0, patch = 0, embed_dim = 0, tokens = 0;
+  bool gap = false;
+  // BERT weights
+  void *word = nullptr, *pos = nullptr, *type0 = nullptr;
+  float *emb_ln_g = nullptr, *emb_ln_b = nullptr;
+  std::vector<jb::BertLayerW> bert_layers;
+  // ViT weights
+  jb::Linear conv, proj;
+  void *cls = nullptr, *vpos = nullptr;
+  float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
+  std::vector<jb::ClipBlockW> clip_blocks;
+  // bookkeeping
+  std::vector<void*> weight_allocs;
+  int64_t weight_bytes = 0;
+  int* d_err = nullptr;
+  jb::Workspace ws;
+  std::mutex mu;
+  // CUDA-event timing of every launch (off unless enabled)
+  bool prof_on = false;
+  std::vector<jb::ProfRec> prof_recs;
+  std::vector<cudaEvent_t> prof_free;
+};
+
+namespace jb {
+
+jb_model* model_load(const char* path, const char* config_json, int device, int format);
+void model_free(jb_model* m);
+size_t estimate_batch_bytes(const jb_model* m, int batch, int seq);
+// Forward passes on device buffers (the workspace must already hold them).
+void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens, int batch,
+                         int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s);
+void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s);
+void ensure_workspace(jb_model* m, int batch, int seq);
+// Records CUDA events around one launch when profiling is on.
+struct ProfScope {
+  jb_model* m;
+  cudaStream_t s;
+  ProfRec rec;
+  bool on;
+  ProfScope(jb_model* m, int kind, cudaStream_t s);
+  ~ProfScope();
+};
+void profile_enable(jb_model* m, bool on);
+void profile_read(jb_model* m, double* ms, int* launches);
+// Synchronises `s` and turns the device error flag into an Error.
+void check_device_flag(jb_model* m, cudaStream_t s);
+
+}  // namespace jb

@@ -1,0 +1,234 @@
+"""Python mirror of the reference's encoder surface over the C ABI.
+
+* ``Bert``                       -- ``jammi_encoders::Bert``
+  (crates/jammi-encoders/src/bert.rs): ``forward`` (pooled, L2-normalised),
+  ``forward_hidden``, ``hidden_size``, ``max_seq_length``, ``SequenceTooLong``.
+* ``OpenClipVisionTransformer``  -- crates/jammi-ai/src/model/backend/open_clip_vit.rs
+  with the caller's ``l2_normalize`` (candle.rs:425-438).
+* ``load_model``                 -- ``CandleBackend::load`` for these two families.
+
+All compute runs in libjammi_b200.so on the GPU; numpy/torch only carry
+buffers across the boundary.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import tempfile
+
+import numpy as np
+
+from . import _lib as L
+from ._lib import JbError, check, lib
+
+POOLING = {"mean": L.POOL_MEAN, "cls": L.POOL_CLS, "max": L.POOL_MAX,
+           "weighted_mean": L.POOL_WEIGHTED_MEAN}
+
+
+class SequenceTooLong(JbError):
+    """``EncoderError::SequenceTooLong`` (bert.rs:263-268)."""
+
+
+def _ptr(a) -> int:
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        return 0
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+class Model:
+    """An owned jb_model handle bound to one device."""
+
+    def __init__(self, weights_path: str, config: dict | str, device: int = 0,
+                 fmt: str = "bf16"):
+        cfg = config if isinstance(config, str) else json.dumps(config)
+        h = ctypes.c_void_p()
+        check(lib().jb_model_load(weights_path.encode(), cfg.encode(), int(device),
+                                  L.FORMATS[fmt], ctypes.byref(h)))
+        self._h = h
+        info = L.ModelInfo()
+        check(lib().jb_model_get_info(self._h, ctypes.byref(info)))
+        self.info = info
+        self.device = device
+        self.fmt = fmt
+
+    @classmethod
+    def from_weights(cls, weights: dict, config: dict, device: int = 0, fmt: str = "bf16"):
+        """Write ``weights`` (name -> numpy array) to a temporary safetensors
+        file and load it (the file is removed once the weights are on device)."""
+        from safetensors.numpy import save_file
+        fd, path = tempfile.mkstemp(suffix=".safetensors")
+        os.close(fd)
+        try:
+            save_file({k: np.ascontiguousarray(v) for k, v in weights.items()}, path)
+            return cls(path, config, device, fmt)
+        finally:
+            os.unlink(path)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().jb_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def estimate_batch_bytes(self, batch: int, seq: int) -> int:
+        return int(lib().jb_estimate_batch_bytes(self._h, batch, seq))
+
+    def sync(self, stream=None):
+        check(lib().jb_model_sync(self._h, _stream_ptr(stream)))
+
+    def profile_enable(self, on: bool = True):
+        check(lib().jb_model_profile_enable(self._h, 1 if on else 0))
+
+    def profile_read(self) -> dict:
+        """Summed device ms and launch counts per kernel class since enable."""
+        ms = (ctypes.c_double * 3)()
+        n = (ctypes.c_int32 * 3)()
+        check(lib().jb_model_profile_read(self._h, ms, n))
+        names = ("linear", "attention", "memory")
+        return {k: {"ms": ms[i], "launches": n[i]} for i, k in enumerate(names)}
+
+
+def _raise_seq(e: JbError):
+    if e.status == L.ERR_SEQ_TOO_LONG:
+        raise SequenceTooLong(e.status, str(e)) from None
+    raise e
+
+
+def mask_to_lengths(mask) -> np.ndarray:
+    """The attention mask of ``BatchEncoding`` is a prefix of ones per row
+    (right padding, crates/jammi-ai/src/model/tokenizer.rs:82-93); lengths
+    are its row sums.  Masks with holes are rejected."""
+    m = np.asarray(mask).astype(np.uint32)
+    lens = m.sum(axis=1).astype(np.uint32)
+    S = m.shape[1]
+    prefix = (np.arange(S)[None, :] < lens[:, None]).astype(np.uint32)
+    if not np.array_equal(prefix, m):
+        raise ValueError("attention mask must be a prefix of ones per row (right padding)")
+    return lens
+
+
+class Bert(Model):
+    """``jammi_encoders::Bert`` on the B200 library."""
+
+    def __init__(self, *a, pooling: str = "mean", **kw):
+        super().__init__(*a, **kw)
+        if self.info.family != L.FAMILY_BERT:
+            raise JbError(L.ERR_INVALID, "not a BERT checkpoint")
+        self.pooling = pooling
+
+    @classmethod
+    def from_weights(cls, weights, config, device=0, fmt="bf16", pooling="mean"):
+        m = super().from_weights(weights, config, device, fmt)
+        m.pooling = pooling
+        return m
+
+    def hidden_size(self) -> int:
+        return self.info.hidden
+
+    def max_seq_length(self) -> int:
+        return self.info.max_seq
+
+    def encode(self, ids, lens, pooling: str | None = None, stream=None) -> np.ndarray:
+        """Host buffers in, host f32 [B, H] out (``jb_encode_text``)."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        lens = np.ascontiguousarray(lens, dtype=np.uint32)
+        B, S = ids.shape
+        out = np.zeros((B, self.info.hidden), dtype=np.float32)
+        try:
+            check(lib().jb_encode_text(self._h, _ptr(ids), _ptr(lens), B, S,
+                                       POOLING[pooling or self.pooling], _ptr(out),
+                                       _stream_ptr(stream)))
+        except JbError as e:
+            _raise_seq(e)
+        return out
+
+    def forward(self, input_ids, mask) -> np.ndarray:
+        """``Bert::forward`` (bert.rs:279-282): pooled and L2-normalised."""
+        return self.encode(input_ids, mask_to_lengths(mask))
+
+    def encode_device(self, ids, lens, out, pooling: str | None = None, stream=None):
+        """Device tensors (torch, uint32/int32 ids and lens, f32 out); async."""
+        B, S = ids.shape
+        try:
+            check(lib().jb_encode_text_device(self._h, _ptr(ids), _ptr(lens), B, S,
+                                              POOLING[pooling or self.pooling], _ptr(out),
+                                              _stream_ptr(stream)))
+        except JbError as e:
+            _raise_seq(e)
+        return out
+
+    def forward_hidden(self, input_ids, mask):
+        """``Bert::forward_hidden`` (bert.rs:257-276) -> torch f32 [B, S, H] on
+        the model's device, zeros at padded positions."""
+        import torch
+        lens = mask_to_lengths(mask)
+        dev = torch.device("cuda", self.device)
+        ids_t = torch.from_numpy(np.ascontiguousarray(input_ids, dtype=np.int32)).to(dev)
+        lens_t = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        B, S = ids_t.shape
+        out = torch.empty((B, S, self.info.hidden), dtype=torch.float32, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        try:
+            check(lib().jb_forward_hidden_device(self._h, _ptr(ids_t), _ptr(lens_t), B, S,
+                                                 _ptr(out), _stream_ptr(stream)))
+        except JbError as e:
+            _raise_seq(e)
+        self.sync(stream)
+        return out
+
+
+class OpenClipVisionTransformer(Model):
+    """OpenCLIP vision tower + ``l2_normalize`` on the B200 library."""
+
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        if self.info.family != L.FAMILY_CLIP_VISION:
+            raise JbError(L.ERR_INVALID, "not an OpenCLIP vision checkpoint")
+
+    def embed_dim(self) -> int:
+        return self.info.output_dim
+
+    def image_size(self) -> int:
+        return self.info.image_size
+
+    def forward_image(self, pixels, stream=None) -> np.ndarray:
+        px = np.ascontiguousarray(pixels, dtype=np.float32)
+        B = px.shape[0]
+        out = np.zeros((B, self.info.output_dim), dtype=np.float32)
+        check(lib().jb_encode_image(self._h, _ptr(px), B, _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def forward_image_device(self, pixels, out, stream=None):
+        check(lib().jb_encode_image_device(self._h, _ptr(pixels), pixels.shape[0], _ptr(out),
+                                           _stream_ptr(stream)))
+        return out
+
+
+def load_model(weights_path: str, config_path_or_dict, device: int = 0, fmt: str = "bf16",
+               pooling: str = "mean"):
+    """``CandleBackend::load`` for the BERT and OpenCLIP-vision arms: the
+    family is detected from the config (``model_cfg`` -> OpenCLIP)."""
+    cfg = config_path_or_dict
+    if isinstance(cfg, str) and os.path.exists(cfg):
+        cfg = json.load(open(cfg))
+    if isinstance(cfg, str):
+        cfg = json.loads(cfg)
+    if "model_cfg" in cfg:
+        return OpenClipVisionTransformer(weights_path, cfg, device, fmt)
+    return Bert(weights_path, cfg, device, fmt, pooling=pooling)

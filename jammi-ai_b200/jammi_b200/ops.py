@@ -1,0 +1,98 @@
+"""Single-op entry points over torch CUDA tensors (device pointers only).
+
+Each function calls one C-ABI op of libjammi_b200.so on the current torch
+stream.  They exist for op-level parity tests and for callers that compose
+their own forward; the encoder forward itself runs entirely inside the
+library (``jb_encode_text`` / ``jb_encode_image``).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+
+_DT = {torch.float32: L.DT_F32, torch.bfloat16: L.DT_BF16, torch.int8: L.DT_S8, torch.int32: L.DT_S32}
+
+
+def _s(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t):
+    return 0 if t is None else t.data_ptr()
+
+
+def _contig(*ts):
+    for t in ts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError("tensors must be contiguous")
+
+
+def sync(device=None):
+    """``jb_op_sync``: synchronise the current stream and raise on a device-side timeout."""
+    check(lib().jb_op_sync(torch.cuda.current_stream(device).cuda_stream))
+
+
+def linear(a: torch.Tensor, w: torch.Tensor, bias=None, residual=None, epilogue: int = L.EPI_NONE,
+           out_dtype=None) -> torch.Tensor:
+    """``epi(a @ w.T + bias)``; a [M, K], w [N, K] both f32 or both bf16."""
+    _contig(a, w, bias, residual)
+    M, K = a.shape
+    N = w.shape[0]
+    out_dtype = out_dtype or a.dtype
+    c = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    check(lib().jb_op_linear(_p(a), _DT[a.dtype], _p(w), _DT[w.dtype], _p(bias), _p(residual),
+                             _p(c), _DT[out_dtype], M, N, K, epilogue, _s(a)))
+    return c
+
+
+def linear_s8(aq: torch.Tensor, a_scale, wq: torch.Tensor, w_scale, bias=None, residual=None,
+              epilogue: int = L.EPI_NONE, out_dtype=torch.int32) -> torch.Tensor:
+    """int8 linear: s32 accumulators (out_dtype int32) or dequantised output."""
+    _contig(aq, a_scale, wq, w_scale, bias, residual)
+    M, K = aq.shape
+    N = wq.shape[0]
+    c = torch.empty((M, N), dtype=out_dtype, device=aq.device)
+    check(lib().jb_op_linear_s8(_p(aq), _p(a_scale), _p(wq), _p(w_scale), _p(bias), _p(residual),
+                                _p(c), _DT[out_dtype], M, N, K, epilogue, _s(aq)))
+    return c
+
+
+def quantize_rows(x: torch.Tensor):
+    _contig(x)
+    R, C = x.shape
+    q = torch.empty((R, C), dtype=torch.int8, device=x.device)
+    s = torch.empty((R,), dtype=torch.float32, device=x.device)
+    check(lib().jb_op_quantize_rows(_p(x), _DT[x.dtype], _p(q), _p(s), R, C, _s(x)))
+    return q, s
+
+
+def layernorm(x: torch.Tensor, gamma, beta, eps: float, residual=None) -> torch.Tensor:
+    _contig(x, gamma, beta, residual)
+    R, C = x.shape
+    y = torch.empty_like(x)
+    check(lib().jb_op_layernorm(_p(x), _p(residual), _p(gamma), _p(beta), _p(y), _DT[x.dtype], R, C,
+                                float(eps), _s(x)))
+    return y
+
+
+def attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, heads: int, max_len: int) -> torch.Tensor:
+    """qkv [T, 3*heads*d] packed rows, cu_seqlens int32 [B+1] -> ctx [T, heads*d]."""
+    _contig(qkv, cu_seqlens)
+    T, three_h = qkv.shape
+    H = three_h // 3
+    ctx = torch.empty((T, H), dtype=qkv.dtype, device=qkv.device)
+    check(lib().jb_op_attention(_p(qkv), _p(cu_seqlens), _p(ctx), _DT[qkv.dtype],
+                                cu_seqlens.numel() - 1, heads, H // heads, max_len, _s(qkv)))
+    return ctx
+
+
+def pool_normalize(hidden: torch.Tensor, cu_seqlens: torch.Tensor, pooling: int = L.POOL_MEAN):
+    _contig(hidden, cu_seqlens)
+    T, H = hidden.shape
+    B = cu_seqlens.numel() - 1
+    out = torch.empty((B, H), dtype=torch.float32, device=hidden.device)
+    check(lib().jb_op_pool_normalize(_p(hidden), _DT[hidden.dtype], _p(cu_seqlens), _p(out), B, H,
+                                     pooling, _s(hidden)))
+    return out

@@ -1,0 +1,62 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the
+header declares, and fails loudly (no CPU fallback) without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "jammi_b200.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(jb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    for s in ("jb_model_load", "jb_encode_text", "jb_encode_image", "jb_op_linear", "jb_op_linear_s8"):
+        assert s in syms
+
+
+def test_library_exports_every_header_symbol():
+    from jammi_b200 import _lib
+    lib = _lib.lib()
+    missing = [s for s in header_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+    # the ctypes table covers every declared entry point
+    assert set(header_symbols()) <= set(_lib.exported_symbols())
+
+
+def test_load_without_gpu_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from jammi_b200 import _lib
+    h = ctypes.c_void_p()
+    st = _lib.lib().jb_model_load(b"/nonexistent.safetensors", b"{}", 0, _lib.FMT_BF16, ctypes.byref(h))
+    assert st == _lib.ERR_NO_DEVICE
+    assert b"device" in _lib.lib().jb_last_error().lower()
+    assert not h.value
+
+
+def test_missing_library_raises(monkeypatch, tmp_path):
+    import importlib
+    import jammi_b200._lib as L
+    monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "absent.so"))
+    monkeypatch.setattr(L, "_lib", None)
+    with pytest.raises(ImportError):
+        L.lib()
+    importlib.reload(L)
+
+
+def test_mask_to_lengths_rejects_holes():
+    import numpy as np
+    from jammi_b200.encoders import mask_to_lengths
+    assert list(mask_to_lengths(np.array([[1, 1, 0], [0, 0, 0], [1, 1, 1]]))) == [2, 0, 3]
+    with pytest.raises(ValueError):
+        mask_to_lengths(np.array([[1, 0, 1]]))

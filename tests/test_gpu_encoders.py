@@ -1,0 +1,215 @@
+"""End-to-end GPU parity of the encoder forward (through the C ABI) against
+the golden vectors and the CPU oracle.
+
+Acceptance (per row, on the L2-normalised embedding):
+* f32 format:  max |gpu - ref| <= 1e-4 and cosine >= 0.9999
+* bf16 format: max |gpu - ref| <= 2e-3 and cosine >= 0.9999
+* int8 format: the same bf16 bar, against the int8 oracle (same quantisation
+  points, integer-exact accumulation); the s32 accumulators themselves are
+  checked bit-exact in test_gpu_ops.py.
+"""
+import json
+
+import numpy as np
+import pytest
+
+from conftest import load_golden
+from oracle import bert as ob
+from oracle import clip as oc
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL = {"f32": 1e-4, "bf16": 2e-3, "int8": 2e-3}
+COS = 0.9999
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def assert_close_rows(got, ref, fmt, rows=None):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if rows is not None:
+        got, ref = got[rows], ref[rows]
+    err = np.abs(got - ref).max(axis=1)
+    nz = (np.linalg.norm(ref, axis=1) > 0.5)
+    cos = (got * ref).sum(1)[nz] / (np.linalg.norm(got, axis=1)[nz] * np.linalg.norm(ref, axis=1)[nz])
+    assert err.max() <= TOL[fmt], f"max-abs {err.max():.3e} > {TOL[fmt]} ({fmt})"
+    assert cos.size == 0 or cos.min() >= COS, f"cosine {cos.min():.6f} < {COS} ({fmt})"
+    return err.max(), (cos.min() if cos.size else 1.0)
+
+
+def _bert(weights, cfg, fmt, pooling="mean"):
+    from jammi_b200 import Bert
+    return Bert.from_weights(weights, cfg, device=0, fmt=fmt, pooling=pooling)
+
+
+# ── golden fixtures (HF transformers) ───────────────────────────────────────
+
+@pytest.mark.parametrize("name", ["tiny_bert_seeded.npz", "small_bert_prefixed.npz"])
+@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+def test_bert_golden_all_poolings(name, fmt):
+    w, g = load_golden(name)
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _bert(w, cfg, fmt)
+    lens = g["mask"].sum(1)
+    for pname in ("mean", "cls", "max", "weighted_mean"):
+        out = model.encode(g["ids"], lens, pooling=pname)
+        rows = lens > 0 if pname == "cls" else None
+        assert_close_rows(out, g["pooled_" + pname], fmt, rows)
+    # all-padding row -> exact zero vector for mean pooling (tests/it/bert.rs:260-315)
+    out = model.encode(g["ids"], lens, pooling="mean")
+    assert np.all(out[lens == 0] == 0)
+
+
+def test_bert_forward_hidden_golden():
+    w, g = load_golden("tiny_bert_seeded.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _bert(w, cfg, "f32")
+    h = model.forward_hidden(g["ids"], g["mask"]).cpu().numpy()
+    valid = g["mask"].astype(bool)
+    assert np.abs(h[valid] - g["hidden"][valid]).max() <= 1e-4
+    assert np.all(h[~valid] == 0)
+
+
+def test_bert_forward_mask_api_matches_lengths():
+    w, g = load_golden("tiny_bert_seeded.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _bert(w, cfg, "bf16")
+    a = model.forward(g["ids"], g["mask"])
+    b = model.encode(g["ids"], g["mask"].sum(1))
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["tiny_clip_gap.npz", "tiny_clip_cls.npz"])
+@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+def test_clip_golden(name, fmt):
+    from jammi_b200 import OpenClipVisionTransformer
+    w, g = load_golden(name)
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = OpenClipVisionTransformer.from_weights(w, cfg, device=0, fmt=fmt)
+    out = model.forward_image(g["pixels"])
+    assert_close_rows(out, g["embed"], fmt)
+
+
+# ── benchmark-config shapes against the oracle ──────────────────────────────
+
+def test_minilm_l6_f32_config():
+    """MiniLM-L6 architecture, f32, batch 32 x seq 128, lengths U[16,128]."""
+    cfg = ob.BertConfig(384, 6, 12, 1536, 30522, 512)
+    w = ob.random_bert_weights(cfg, seed=101)
+    rng = np.random.default_rng(102)
+    lens = rng.integers(16, 129, size=32)
+    ids, mask = ob.random_token_batch(32, 128, lens, seed=103)
+    ref = ob.bert_forward(w, cfg, ids, mask)
+    out = _bert(w, cfg.to_dict(), "f32").encode(ids, lens)
+    assert_close_rows(out, ref, "f32")
+
+
+def _bert_base(seed):
+    cfg = ob.BertConfig(768, 12, 12, 3072, 30522, 512)
+    return cfg, ob.random_bert_weights(cfg, seed=seed)
+
+
+def test_bert_base_bf16_config():
+    """BERT-base, bf16, seq 256, lengths U[32,256] (batch reduced for the oracle)."""
+    cfg, w = _bert_base(201)
+    rng = np.random.default_rng(202)
+    lens = rng.integers(32, 257, size=12)
+    lens[0] = 256
+    ids, mask = ob.random_token_batch(12, 256, lens, seed=203)
+    ref = ob.bert_forward(w, cfg, ids, mask)
+    out = _bert(w, cfg.to_dict(), "bf16").encode(ids, lens)
+    assert_close_rows(out, ref, "bf16")
+
+
+def test_bert_base_int8_config():
+    """BERT-base with int8 weights (per-channel) and per-token int8 activations."""
+    cfg, w = _bert_base(301)
+    rng = np.random.default_rng(302)
+    lens = rng.integers(32, 257, size=8)
+    ids, mask = ob.random_token_batch(8, 256, lens, seed=303)
+    ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
+    assert_close_rows(out, ref, "int8")
+    # and the quantisation error itself stays small against the float model
+    fref = ob.bert_forward(w, cfg, ids, mask)
+    assert (out * fref).sum(1).min() > 0.995
+
+
+def test_bert_large_prequantised_int8():
+    """BERT-large layout in the int8 checkpoint format: int8 weights with
+    per-output-channel scales log-uniform in [1e-3, 1e-1]; lengths lognormal."""
+    cfg = ob.BertConfig(1024, 2, 16, 4096, 30522, 512)  # 2 of 24 layers keep the oracle fast
+    w = ob.random_bert_weights(cfg, seed=401)
+    rng = np.random.default_rng(402)
+    for n in range(cfg.num_hidden_layers):
+        for lin, (o, i) in zip(oq.LINEARS, [(1024, 1024)] * 4 + [(4096, 1024), (1024, 4096)]):
+            q, s = oq.random_int8_linear(o, i, rng)
+            k = f"encoder.layer.{n}.{lin}"
+            del w[k + ".weight"]
+            w[k + ".weight_q"] = q
+            w[k + ".weight_scale"] = s
+    lens = np.clip(np.round(rng.lognormal(5.0, 0.6, size=6)), 8, 512).astype(int)
+    ids, mask = ob.random_token_batch(6, int(lens.max()), lens, seed=403)
+    ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
+    assert_close_rows(out, ref, "int8")
+
+
+def test_clip_vit_b32_bf16_config():
+    """CLIP ViT-B/32 vision tower, bf16, pixels N(0,1) (batch reduced for the oracle)."""
+    from jammi_b200 import OpenClipVisionTransformer
+    cfg = oc.ClipVisionConfig()
+    w = oc.random_clip_weights(cfg, seed=501)
+    px = np.random.default_rng(502).standard_normal((6, 3, 224, 224)).astype(np.float32)
+    ref = oc.l2_normalize_image(oc.clip_vision_forward(w, cfg, px))
+    model = OpenClipVisionTransformer.from_weights(w, cfg.to_open_clip_config(), device=0, fmt="bf16")
+    assert_close_rows(model.forward_image(px), ref, "bf16")
+
+
+# ── API behaviour ───────────────────────────────────────────────────────────
+
+def test_host_and_device_entry_points_agree():
+    cfg, w = _bert_base(601)
+    rng = np.random.default_rng(602)
+    lens = rng.integers(1, 129, size=40)
+    ids, _ = ob.random_token_batch(40, 128, lens, seed=603)
+    model = _bert(w, cfg.to_dict(), "bf16")
+    host = model.encode(ids, lens)
+    d_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
+    d_lens = torch.from_numpy(lens.astype(np.int32)).cuda()
+    out = torch.empty((40, 768), device="cuda")
+    model.encode_device(d_ids, d_lens, out, stream=torch.cuda.current_stream())
+    model.sync(torch.cuda.current_stream())
+    assert np.array_equal(out.cpu().numpy(), host)
+    assert np.array_equal(model.encode(ids, lens), host)  # deterministic
+
+
+def test_sequence_too_long():
+    from jammi_b200 import SequenceTooLong
+    w, g = load_golden("tiny_bert_seeded.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _bert(w, cfg, "bf16")
+    ids = np.ones((1, 129), np.uint32)
+    with pytest.raises(SequenceTooLong):
+        model.encode(ids, np.array([129], np.uint32))
+
+
+def test_invalid_token_id_is_an_error():
+    from jammi_b200 import JbError
+    w, g = load_golden("tiny_bert_seeded.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _bert(w, cfg, "bf16")
+    ids = np.full((2, 4), 7, np.uint32)
+    ids[1, 2] = 256  # vocab is 256
+    with pytest.raises(JbError):
+        model.encode(ids, np.array([4, 4], np.uint32))
+    # the handle stays usable afterwards
+    ids[1, 2] = 5
+    assert np.all(np.isfinite(model.encode(ids, np.array([4, 4], np.uint32))))

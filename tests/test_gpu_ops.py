@@ -1,0 +1,261 @@
+"""GPU parity of every single op against the CPU oracle (or exact integer
+arithmetic), called through the C ABI on seeded inputs.
+
+Tolerances (written next to each check):
+* int8 accumulators and int8 quantisation: bit-exact.
+* bf16 outputs: error within a few bf16 ulps of the f32/f64 reference.
+* f32 outputs: 1e-4 absolute or tighter.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import bert as ob
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _ops():
+    from jammi_b200 import ops
+    return ops
+
+
+def _bf16(x, dev):
+    return torch.from_numpy(np.asarray(x, dtype=np.float32)).to(dev).to(torch.bfloat16)
+
+
+# ── linear (tcgen05 bf16) ────────────────────────────────────────────────────
+
+LIN_SHAPES = [  # (M, N, K)
+    (1, 768, 768), (37, 96, 32), (128, 256, 64), (300, 2304, 768), (1000, 768, 3072),
+    (777, 3072, 768), (64, 512, 768), (5, 16, 48), (256, 128, 1024), (4096, 768, 768),
+]
+
+
+@pytest.mark.parametrize("M,N,K", LIN_SHAPES)
+def test_linear_bf16_matches_fp32(dev, M, N, K):
+    ops = _ops()
+    rng = np.random.default_rng(M * 7 + N + K)
+    a = _bf16(rng.standard_normal((M, K)), dev)
+    w = _bf16(rng.standard_normal((N, K)) * 0.05, dev)
+    bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+    c = ops.linear(a, w, bias=bias)
+    ops.sync()
+    ref = a.float() @ w.float().T + bias
+    err = (c.float() - ref).abs().max().item()
+    # bf16 output rounding: <= 2^-8 relative to the largest |ref| (+ f32 accumulation)
+    assert err <= 8e-3 * ref.abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("epi", ["gelu", "quick_gelu", "residual"])
+def test_linear_bf16_epilogues(dev, epi):
+    import jammi_b200 as jb
+    ops = _ops()
+    M, N, K = 333, 768, 768
+    rng = np.random.default_rng(5)
+    a = _bf16(rng.standard_normal((M, K)), dev)
+    w = _bf16(rng.standard_normal((N, K)) * 0.05, dev)
+    bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+    res = _bf16(rng.standard_normal((M, N)), dev)
+    z = a.float() @ w.float().T + bias
+    if epi == "gelu":
+        c = ops.linear(a, w, bias=bias, epilogue=jb.EPI_GELU)
+        ref = 0.5 * z * (1 + torch.erf(z / math.sqrt(2)))
+    elif epi == "quick_gelu":
+        c = ops.linear(a, w, bias=bias, epilogue=jb.EPI_QUICK_GELU)
+        ref = z * torch.sigmoid(1.702 * z)
+    else:
+        c = ops.linear(a, w, bias=bias, residual=res, epilogue=jb.EPI_RESIDUAL)
+        ref = z + res.float()
+    ops.sync()
+    err = (c.float() - ref).abs().max().item()
+    assert err <= 8e-3 * ref.abs().max().item() + 1e-3, err
+
+
+def test_linear_bf16_f32_output(dev):
+    ops = _ops()
+    rng = np.random.default_rng(9)
+    a = _bf16(rng.standard_normal((200, 768)), dev)
+    w = _bf16(rng.standard_normal((512, 768)) * 0.05, dev)
+    c = ops.linear(a, w, out_dtype=torch.float32)
+    ops.sync()
+    ref = a.double() @ w.double().T
+    assert (c.double() - ref).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(70, 96, 32), (300, 768, 768), (129, 3072, 384)])
+def test_linear_f32_simt(dev, M, N, K):
+    ops = _ops()
+    rng = np.random.default_rng(M)
+    a = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
+    w = torch.from_numpy((rng.standard_normal((N, K)) * 0.05).astype(np.float32)).to(dev)
+    b = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+    c = ops.linear(a, w, bias=b)
+    ops.sync()
+    ref = a.double() @ w.double().T + b.double()
+    assert (c.double() - ref).abs().max().item() < 1e-4
+
+
+# ── int8 (tcgen05 kind::i8): bit-exact accumulators ─────────────────────────
+
+@pytest.mark.parametrize("M,N,K", [(1, 768, 768), (300, 2304, 768), (513, 768, 3072), (129, 4096, 1024),
+                                   (77, 96, 32)])
+def test_linear_s8_accumulators_bit_exact(dev, M, N, K):
+    ops = _ops()
+    rng = np.random.default_rng(M + N)
+    aq = rng.integers(-127, 128, size=(M, K), dtype=np.int64).astype(np.int8)
+    wq = rng.integers(-127, 128, size=(N, K), dtype=np.int64).astype(np.int8)
+    aq[0, :] = 127
+    wq[0, :] = 127
+    wq[1, :] = -127
+    a_t = torch.from_numpy(aq).to(dev)
+    w_t = torch.from_numpy(wq).to(dev)
+    ones_m = torch.ones(M, device=dev)
+    ones_n = torch.ones(N, device=dev)
+    acc = ops.linear_s8(a_t, ones_m, w_t, ones_n, out_dtype=torch.int32)
+    ops.sync()
+    ref = oq.gemm_s8_s32(aq, wq)
+    got = acc.cpu().numpy()
+    assert np.array_equal(got, ref), np.argwhere(got != ref)[:5]
+    assert got[0, 0] == K * 127 * 127 and got[0, 1] == -K * 127 * 127
+
+
+def test_linear_s8_dequant_epilogue(dev):
+    import jammi_b200 as jb
+    ops = _ops()
+    M, N, K = 260, 768, 768
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    xq, xs = oq.quantize_rows(x)
+    wq, ws = oq.quantize_rows(w)
+    t = lambda v: torch.from_numpy(v).to(dev)
+    out = ops.linear_s8(t(xq), t(xs), t(wq), t(ws), bias=t(b), epilogue=jb.EPI_GELU,
+                        out_dtype=torch.float32)
+    ops.sync()
+    z = oq.dequant(oq.gemm_s8_s32(xq, wq), xs, ws, b)
+    ref = 0.5 * z * (1 + np.vectorize(math.erf)(z / math.sqrt(2)))
+    assert np.abs(out.cpu().numpy() - ref).max() < 1e-4 * np.abs(ref).max() + 1e-5
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_quantize_rows_bit_exact(dev, dtype):
+    ops = _ops()
+    rng = np.random.default_rng(23)
+    x = (rng.standard_normal((513, 3072)) * rng.uniform(0.01, 20, size=(513, 1))).astype(np.float32)
+    x[3] = 0
+    xt = _bf16(x, dev) if dtype == "bf16" else torch.from_numpy(x).to(dev)
+    q, s = ops.quantize_rows(xt)
+    ops.sync()
+    q_ref, s_ref = oq.quantize_rows(xt.float().cpu().numpy())
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+
+
+# ── LayerNorm ───────────────────────────────────────────────────────────────
+
+@pytest.mark.parametrize("dtype,cols", [("f32", 384), ("f32", 32), ("bf16", 768), ("bf16", 1024), ("bf16", 64)])
+def test_layernorm(dev, dtype, cols):
+    ops = _ops()
+    rng = np.random.default_rng(cols)
+    R = 1000
+    x = (rng.standard_normal((R, cols)) * 3 + 1).astype(np.float32)
+    r = rng.standard_normal((R, cols)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+    b = rng.standard_normal(cols).astype(np.float32)
+    mk = (lambda v: _bf16(v, dev)) if dtype == "bf16" else (lambda v: torch.from_numpy(v).to(dev))
+    xt, rt = mk(x), mk(r)
+    y = ops.layernorm(xt, torch.from_numpy(g).to(dev), torch.from_numpy(b).to(dev), 1e-12, residual=rt)
+    ops.sync()
+    ref = ob.layer_norm(xt.double().cpu().numpy() + rt.double().cpu().numpy(), g, b, 1e-12)
+    err = np.abs(y.double().cpu().numpy() - ref).max()
+    tol = 3e-2 if dtype == "bf16" else 1e-5  # bf16: |y| <~ 6, ulp 2^-5 at 4-8
+    assert err < tol, err
+
+
+# ── attention (varlen) ──────────────────────────────────────────────────────
+
+def _attn_ref(qkv, cu, heads):
+    T, three_h = qkv.shape
+    H = three_h // 3
+    d = H // heads
+    out = np.zeros((T, H))
+    for b in range(len(cu) - 1):
+        s, e = cu[b], cu[b + 1]
+        if e == s:
+            continue
+        for h in range(heads):
+            q = qkv[s:e, h * d:(h + 1) * d]
+            k = qkv[s:e, H + h * d:H + (h + 1) * d]
+            v = qkv[s:e, 2 * H + h * d:2 * H + (h + 1) * d]
+            out[s:e, h * d:(h + 1) * d] = ob.softmax_last(q @ k.T / math.sqrt(d)) @ v
+    return out
+
+
+@pytest.mark.parametrize("dtype,heads,d,lens", [
+    ("bf16", 12, 64, [1, 2, 63, 64, 65, 127, 128, 129, 200, 256]),
+    ("bf16", 16, 64, [512, 333, 8, 0, 511]),
+    ("bf16", 12, 64, [50] * 7),
+    ("f32", 12, 32, [128, 16, 77, 1, 0, 100]),
+    ("f32", 2, 16, [16, 9, 1]),
+    ("bf16", 4, 8, [5, 5, 5]),
+])
+def test_attention_varlen(dev, dtype, heads, d, lens):
+    ops = _ops()
+    rng = np.random.default_rng(sum(lens) + heads)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = (rng.standard_normal((max(T, 1), 3 * heads * d)) * 1.5).astype(np.float32)[:T]
+    qt = _bf16(qkv, dev) if dtype == "bf16" else torch.from_numpy(qkv).to(dev)
+    if T == 0:
+        return
+    ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens))
+    ops.sync()
+    ref = _attn_ref(qt.double().cpu().numpy(), cu, heads)
+    err = np.abs(ctx.double().cpu().numpy() - ref).max()
+    tol = 2e-2 if dtype == "bf16" else 1e-5  # bf16: P and V in bf16, outputs |.| < ~3
+    assert err < tol, err
+
+
+# ── pooling + L2 ────────────────────────────────────────────────────────────
+
+@pytest.mark.parametrize("pooling", ["mean", "cls", "max", "weighted_mean"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_pool_normalize(dev, pooling, dtype):
+    ops = _ops()
+    rng = np.random.default_rng(3)
+    lens = [5, 1, 0, 128, 77]
+    H = 768
+    S = max(lens)
+    hidden = rng.standard_normal((len(lens), S, H)).astype(np.float32)
+    mask = (np.arange(S)[None, :] < np.array(lens)[:, None]).astype(np.uint32)
+    packed = np.concatenate([hidden[b, :n] for b, n in enumerate(lens)], axis=0)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    pt = _bf16(packed, dev) if dtype == "bf16" else torch.from_numpy(packed).to(dev)
+    out = ops.pool_normalize(pt, torch.from_numpy(cu).to(dev), ob.POOLING_NAMES[pooling])
+    ops.sync()
+    h_used = np.zeros_like(hidden)
+    pk = pt.float().cpu().numpy()
+    for b, n in enumerate(lens):
+        h_used[b, :n] = pk[cu[b]:cu[b + 1]]
+    ref = ob.pool_and_normalize(h_used.astype(np.float32), mask, ob.POOLING_NAMES[pooling])
+    got = out.cpu().numpy()
+    if pooling == "cls":
+        # an all-padding row has no token: the library returns the zero vector
+        ref[2] = 0.0
+    assert np.all(np.isfinite(got))
+    assert np.abs(got - ref).max() < 1e-5
+    if pooling in ("mean", "weighted_mean"):
+        assert np.all(got[2] == 0)
