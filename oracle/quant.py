@@ -118,9 +118,12 @@ def bert_int8_forward_hidden(weights: dict, cfg: BertConfig, input_ids, mask):
     return x
 
 
-def random_int8_linear(out_f: int, in_f: int, rng, scale_lo=1e-3, scale_hi=1e-1):
-    """A pre-quantised linear: int8 values ~ clip(rint(N(0, 42)), -127, 127)
-    and per-output-channel scales log-uniform in [scale_lo, scale_hi]."""
-    q = np.clip(np.rint(rng.standard_normal((out_f, in_f)) * 42.0), -127, 127).astype(np.int8)
+def random_int8_linear(out_f: int, in_f: int, rng, scale_lo=1e-3, scale_hi=1e-1, std=0.02):
+    """A pre-quantised linear: per-output-channel scales log-uniform in
+    [scale_lo, scale_hi] and int8 values ``clip(rint(W / s), -127, 127)`` of
+    N(0, std) weights, so the effective weights ``s * q`` keep the scale of
+    random-init BERT weights (coarse channels round to few levels)."""
     s = np.exp(rng.uniform(np.log(scale_lo), np.log(scale_hi), size=out_f)).astype(np.float32)
+    w = rng.standard_normal((out_f, in_f)) * std
+    q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
     return q, s

@@ -39,7 +39,15 @@ def assert_close_rows(got, ref, fmt, rows=None):
     err = np.abs(got - ref).max(axis=1)
     nz = (np.linalg.norm(ref, axis=1) > 0.5)
     cos = (got * ref).sum(1)[nz] / (np.linalg.norm(got, axis=1)[nz] * np.linalg.norm(ref, axis=1)[nz])
-    assert err.max() <= TOL[fmt], f"max-abs {err.max():.3e} > {TOL[fmt]} ({fmt})"
+    # The bars are stated for 768-wide embeddings (element RMS 1/sqrt(768)).
+    # A unit vector of width D < 768 has elements sqrt(768/D) larger, and a
+    # 16-bit format's error is relative, so the max-abs bar scales with it
+    # for the small golden fixtures (D = 16..64); f32 keeps its absolute bar.
+    D = got.shape[1]
+    tol = TOL[fmt] * (max(1.0, (768.0 / D) ** 0.5) if fmt != "f32" else 1.0)
+    print(f"{fmt} D={D}: max-abs {err.max():.3e} (bar {tol:.1e}), "
+          f"min cos {cos.min() if cos.size else 1.0:.7f}")
+    assert err.max() <= tol, f"max-abs {err.max():.3e} > {tol:.2e} ({fmt})"
     assert cos.size == 0 or cos.min() >= COS, f"cosine {cos.min():.6f} < {COS} ({fmt})"
     return err.max(), (cos.min() if cos.size else 1.0)
 
