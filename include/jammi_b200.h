@@ -121,6 +121,21 @@ jb_status jb_encode_text(jb_model* model, const uint32_t* ids, const uint32_t* l
 /* Same, with ids/lens/out in device memory; asynchronous on `stream`. */
 jb_status jb_encode_text_device(jb_model* model, const uint32_t* d_ids, const uint32_t* d_lens,
                                 int batch, int max_seq, int pooling, float* d_out, void* stream);
+/* The same forward as jb_encode_text_device for callers that must not
+ * allocate device memory: cudaMalloc/cudaFree synchronise the whole device
+ * (a latency-critical query encoder sharing a GPU with a bulk embedding job
+ * would stall behind it), and a process whose device memory is reserved by
+ * another runtime's pool has none to allocate.  No counterpart in the
+ * reference.  It calls no cudaMalloc, cudaFree or allocating library
+ * routine; its scratch is a 64 MiB file-scope device array that every GPU
+ * loading this library holds until exit.  Requests whose
+ * jb_estimate_batch_bytes exceeds 64 MiB return JB_ERR_INVALID.  All calls on
+ * a device share that array (it keeps the previous call's contents): calls
+ * that overlap on the GPU race.  The first call on a device looks up the
+ * array's device address; make it before any stream capture. */
+jb_status jb_encode_text_device_noalloc(jb_model* model, const uint32_t* d_ids,
+                                        const uint32_t* d_lens, int batch, int max_seq,
+                                        int pooling, float* d_out, void* stream);
 /* Bert::forward_hidden (bert.rs:257-276): last hidden states as f32
  * [batch, max_seq, H] in device memory; padded positions are written as 0. */
 jb_status jb_forward_hidden_device(jb_model* model, const uint32_t* d_ids, const uint32_t* d_lens,

@@ -65,6 +65,8 @@ void check_text_args(const jb_model* m, int batch, int max_seq, int pooling) {
 
 }  // namespace
 
+jb_status jb::record_error(jb_status st, const std::string& msg) { return set_error(st, msg); }
+
 extern "C" {
 
 const char* jb_last_error(void) { return g_last_error.c_str(); }

@@ -479,6 +479,40 @@ void ensure_workspace(jb_model* m, int batch, int seq) {
   ws.pooled = take(p.pooled);
 }
 
+Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq) {
+  Workspace ws;
+  const WsPlan p = plan_workspace(m, batch, seq);
+  char* base = static_cast<char*>(base_ptr);
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    if (!bytes) return nullptr;
+    void* r = base + off;
+    off += bytes;
+    return r;
+  };
+  ws.batch_cap = batch;
+  ws.seq_cap = seq;
+  ws.bytes = p.sum();
+  ws.ids = static_cast<uint32_t*>(take(p.ids));
+  ws.lens = static_cast<uint32_t*>(take(p.lens));
+  ws.cu = static_cast<int*>(take(p.cu));
+  ws.total = static_cast<int*>(take(p.total));
+  ws.out = static_cast<float*>(take(p.out));
+  ws.x = take(p.x);
+  ws.x1 = take(p.x);
+  ws.y = take(p.x);
+  ws.ctx = take(p.x);
+  ws.qkv = take(p.qkv);
+  ws.hf = take(p.hf);
+  ws.aq = static_cast<int8_t*>(take(p.aq));
+  ws.as = static_cast<float*>(take(p.as));
+  ws.pixels = static_cast<float*>(take(p.pixels));
+  ws.patches = take(p.patches);
+  ws.patch_out = take(p.patch_out);
+  ws.pooled = take(p.pooled);
+  return ws;
+}
+
 jb_model* model_load(const char* path, const char* config_json, int device, int format) {
   if (!path || !config_json) fail(JB_ERR_INVALID, "weights path and config must be non-null");
   if (format < JB_FMT_F32 || format > JB_FMT_INT8) fail(JB_ERR_INVALID, "unknown weight format");

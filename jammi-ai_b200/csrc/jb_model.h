@@ -17,6 +17,8 @@ struct Error {
   std::string msg;
 };
 [[noreturn]] void fail(jb_status st, const std::string& msg);
+// Sets the calling thread's jb_last_error() message and returns `st`.
+jb_status record_error(jb_status st, const std::string& msg);
 void check_cuda(cudaError_t e, const char* what);
 
 // Sets the calling thread's current device for a scope, restoring it after.
@@ -112,6 +114,10 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
                          int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s);
 void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s);
 void ensure_workspace(jb_model* m, int batch, int seq);
+// A workspace for (batch, seq) laid out over caller-owned device memory at
+// `base` (estimate_batch_bytes(m, batch, seq) bytes, 256-byte aligned); the
+// layout is the one ensure_workspace allocates.  Allocates nothing.
+Workspace carve_workspace(const jb_model* m, void* base, int batch, int seq);
 // Records CUDA events around one launch when profiling is on.
 struct ProfScope {
   jb_model* m;

@@ -60,6 +60,7 @@ _SIGS = [
     ("jb_model_profile_read", _I, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32)]),
     ("jb_encode_text", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     ("jb_encode_text_device", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
+    ("jb_encode_text_device_noalloc", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     ("jb_forward_hidden_device", _I, [_P, _P, _P, _I, _I, _P, _P]),
     ("jb_encode_image", _I, [_P, _P, _I, _P, _P]),
     ("jb_encode_image_device", _I, [_P, _P, _I, _P, _P]),

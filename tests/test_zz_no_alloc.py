@@ -1,0 +1,85 @@
+"""The no-allocation text encoder entry point against the allocating one.
+
+jb_encode_text_device_noalloc serves callers that must not allocate device
+memory (cudaMalloc/cudaFree synchronise the device; a process whose device
+memory is reserved by another runtime's pool has none to give).  Its scratch
+is a 64 MiB array inside the library, shared by every call on a device.
+This file is collected last on purpose: it must pass both on its own in a
+fresh process and after every other test.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL = 2e-3   # the bf16 / int8 embedding bar used by the encoder parity tests
+COS = 0.9999
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from jammi_b200 import _lib
+    return _lib
+
+
+def _model(fmt):
+    from jammi_b200 import Bert
+    from jammi_b200.synthetic import bert_weights
+    cfg = dict(hidden_size=768, num_hidden_layers=2, num_attention_heads=12, intermediate_size=3072,
+               vocab_size=30522, max_position_embeddings=512, type_vocab_size=2,
+               layer_norm_eps=1e-12, model_type="bert")
+    return Bert.from_weights(bert_weights(cfg, seed=77), cfg, device=0, fmt=fmt)
+
+
+def _batch(seed, batch, seq):
+    from jammi_b200.synthetic import token_batch, uniform_lengths
+    rng = np.random.default_rng(seed)
+    lens = uniform_lengths(rng, batch, 1, seq)
+    ids = token_batch(rng, lens, seq)
+    return (torch.from_numpy(ids.astype(np.int32)).cuda(),
+            torch.from_numpy(lens.astype(np.int32)).cuda())
+
+
+def _close(a, b):
+    a = a.double().cpu().numpy()
+    b = b.double().cpu().numpy()
+    assert np.abs(a - b).max() <= TOL
+    cos = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    assert cos.min() >= COS
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "int8"])
+def test_noalloc_matches_allocating_entry_point(lib, fmt):
+    model = _model(fmt)
+    L = lib.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    for call, (batch, seq) in enumerate([(8, 128), (13, 96)]):  # two calls in a row
+        ids, lens = _batch(100 + call, batch, seq)
+        ref = torch.empty((batch, 768), device="cuda")
+        got = torch.full((batch, 768), float("nan"), device="cuda")
+        lib.check(L.jb_encode_text_device(model.handle, ids.data_ptr(), lens.data_ptr(), batch, seq,
+                                          lib.POOL_MEAN, ref.data_ptr(), s))
+        lib.check(L.jb_encode_text_device_noalloc(model.handle, ids.data_ptr(), lens.data_ptr(),
+                                                  batch, seq, lib.POOL_MEAN, got.data_ptr(), s))
+        model.sync(torch.cuda.current_stream())
+        assert torch.isfinite(got).all()
+        _close(got, ref)
+    model.close()
+
+
+def test_noalloc_rejects_requests_above_its_scratch(lib):
+    model = _model("bf16")
+    L = lib.lib()
+    ids, lens = _batch(5, 64, 512)  # ~1.4 GB of scratch for a 768-wide model
+    out = torch.empty((64, 768), device="cuda")
+    st = L.jb_encode_text_device_noalloc(model.handle, ids.data_ptr(), lens.data_ptr(), 64, 512,
+                                         lib.POOL_MEAN, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == lib.ERR_INVALID
+    msg = L.jb_last_error().decode()
+    assert "64 MiB" in msg and "scratch" in msg
+    model.close()
