@@ -24,8 +24,11 @@ namespace jb {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kRowBytes = 128;  // one 128-byte swizzle row of K per stage
-constexpr int kGemmThreads = 192;
+constexpr int kRowBytes = 128;   // one 128-byte swizzle row of K per stage
+constexpr int kEpiWarps = 8;     // two per TMEM lane quarter, each on half the columns
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kGemmThreads = 64 + kEpiThreads;  // TMA warp + MMA warp + epilogue
+constexpr int kEpiBarrier = 1;   // named barrier among the epilogue warps
 
 template <int BN>
 struct TcCfg {
@@ -35,8 +38,12 @@ struct TcCfg {
   static constexpr int STAGES_FIT = (192 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
+  // per accumulator buffer: bias[BN] and weight scale[BN] of the tile, f32
+  static constexpr int PARAM_BYTES = 2 * 2 * BN * 4;
+  // one 32 x 32 bf16 output chunk per epilogue warp
+  static constexpr int CHUNK_BYTES = kEpiWarps * 32 * 64;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + PARAM_BYTES + CHUNK_BYTES + BAR_BYTES + 1024;
 };
 
 struct EpiParams {
@@ -56,16 +63,151 @@ struct EpiParams {
   int* err;
 };
 
+// SIMT path: CUDA's erff / expf.
 __device__ __forceinline__ float apply_epi(float v, int epi) {
   if (epi == JB_EPI_GELU) return gelu_erf(v);
   if (epi == JB_EPI_QUICK_GELU) return quick_gelu(v);
   return v;
 }
 
-// Stores 32 consecutive accumulator columns of one row.
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions (1964),
+// eq. 7.1.26: erf(x) = 1 - (a1 t + ... + a5 t^5) exp(-x^2), t = 1/(1 + p|x|),
+// |error| <= 1.5e-7 -- far below the bf16 rounding of the stored result.
+// The approximate reciprocal and exponential intrinsics keep the GELU
+// epilogue off the critical path of the int8 main loop.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  poly *= t;
+  const float r = fmaf(-poly, __expf(-ax * ax), 1.0f);
+  return copysignf(r, x);
+}
+__device__ __forceinline__ float gelu_tc(float x) {
+  return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float quick_gelu_tc(float x) {
+  return __fdividef(x, 1.0f + __expf(-1.702f * x));
+}
+
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kEpiBarrier), "n"(kEpiThreads) : "memory");
+}
+
+// ── coalesced bf16 epilogue ─────────────────────────────────────────────────
+// Each epilogue warp owns a 2 KB shared buffer holding one 32 x 32 bf16 chunk
+// (32 rows of 64 B).  16-byte slot q of row r lives at r*64 + ((q ^ ((r>>1)&3))*16):
+// both the row-per-thread pattern (thread r touches row r) and the
+// coalesced pattern (lane l touches row 8i + l/4, slot l%4) are free of
+// bank conflicts.
+constexpr int kChunkBytes = 32 * 64;
+__device__ __forceinline__ uint32_t chunk_slot(uint32_t buf, int row, int q) {
+  return buf + row * 64 + ((q ^ ((row >> 1) & 3)) << 4);
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+
+// 32 rows (row0 .. row0+31, thread `lane` owns row0+lane) x 32 columns of a
+// bf16 output with full columns.  Residual reads and output writes move
+// through `buf` so that global accesses are row-contiguous.
 template <bool S8>
-__device__ __forceinline__ void store_chunk(const EpiParams& p, int row, int col0,
-                                            const uint32_t (&r)[32]) {
+__device__ __forceinline__ void epi_chunk_bf16(const EpiParams& p, int row0, int lane, int M,
+                                               int col0, const uint32_t (&r)[32], const float* sb,
+                                               const float* ss, float as, uint32_t buf) {
+  const bool resid = p.epi == JB_EPI_RESIDUAL;
+  uint4 rres[4];
+  if (resid) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = row0 + i * 8 + (lane >> 2);
+      rres[i] = make_uint4(0, 0, 0, 0);
+      if (rr < M)
+        rres[i] = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) +
+                                                        static_cast<size_t>(rr) * p.ldr + col0 +
+                                                        (lane & 3) * 8));
+    }
+  }
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 b = *reinterpret_cast<const float4*>(sb + j);
+    if constexpr (S8) {
+      const float4 s = *reinterpret_cast<const float4*>(ss + j);
+      v[j + 0] = fmaf(__int2float_rn(static_cast<int>(r[j + 0])), as * s.x, b.x);
+      v[j + 1] = fmaf(__int2float_rn(static_cast<int>(r[j + 1])), as * s.y, b.y);
+      v[j + 2] = fmaf(__int2float_rn(static_cast<int>(r[j + 2])), as * s.z, b.z);
+      v[j + 3] = fmaf(__int2float_rn(static_cast<int>(r[j + 3])), as * s.w, b.w);
+    } else {
+      v[j + 0] = __uint_as_float(r[j + 0]) + b.x;
+      v[j + 1] = __uint_as_float(r[j + 1]) + b.y;
+      v[j + 2] = __uint_as_float(r[j + 2]) + b.z;
+      v[j + 3] = __uint_as_float(r[j + 3]) + b.w;
+    }
+  }
+  if (p.epi == JB_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
+  } else if (p.epi == JB_EPI_QUICK_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = quick_gelu_tc(v[j]);
+  }
+  if (resid) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sts128(chunk_slot(buf, i * 8 + (lane >> 2), lane & 3), rres[i]);
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 raw = lds128(chunk_slot(buf, lane, q));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        v[8 * q + 2 * e] += f.x;
+        v[8 * q + 2 * e + 1] += f.y;
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 out;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+    sts128(chunk_slot(buf, lane, q), out);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = row0 + i * 8 + (lane >> 2);
+    const uint4 o = lds128(chunk_slot(buf, i * 8 + (lane >> 2), lane & 3));
+    if (rr < M)
+      *reinterpret_cast<uint4*>(static_cast<bf16*>(p.C) + static_cast<size_t>(rr) * p.ldc + col0 +
+                                (lane & 3) * 8) = o;
+  }
+  __syncwarp();
+}
+
+// 32 accumulator columns of one row -> stored outputs.  sb / ss are the
+// tile's staged bias and weight scales for these columns (zero past N).
+template <bool S8>
+__device__ __forceinline__ void epi_chunk(const EpiParams& p, int row, int col0,
+                                          const uint32_t (&r)[32], const float* sb,
+                                          const float* ss, float as) {
   const int ncols = min(32, p.N - col0);
   const size_t off = static_cast<size_t>(row) * p.ldc + col0;
   if (p.c_dtype == JB_DT_S32) {
@@ -81,39 +223,51 @@ __device__ __forceinline__ void store_chunk(const EpiParams& p, int row, int col
     }
     return;
   }
-  float v[32];
-  if constexpr (S8) {
-    const float as = p.a_scale[row];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float ws = (j < ncols) ? __ldg(p.w_scale + col0 + j) : 0.f;
-      v[j] = static_cast<float>(static_cast<int>(r[j])) * (as * ws);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  }
-  if (p.bias) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += (j < ncols) ? __ldg(p.bias + col0 + j) : 0.f;
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = apply_epi(v[j], p.epi);
+  const bool full = ncols == 32;
   const size_t roff = static_cast<size_t>(row) * p.ldr + col0;
+  const bool res_bf16 = p.epi == JB_EPI_RESIDUAL && p.c_dtype == JB_DT_BF16 && full;
+  uint4 res[4];
+  if (res_bf16) {  // issue the residual loads before the arithmetic
+    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) + roff);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) res[e] = __ldg(rp + e);
+  }
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 b = *reinterpret_cast<const float4*>(sb + j);
+    if constexpr (S8) {
+      const float4 s = *reinterpret_cast<const float4*>(ss + j);
+      v[j + 0] = fmaf(__int2float_rn(static_cast<int>(r[j + 0])), as * s.x, b.x);
+      v[j + 1] = fmaf(__int2float_rn(static_cast<int>(r[j + 1])), as * s.y, b.y);
+      v[j + 2] = fmaf(__int2float_rn(static_cast<int>(r[j + 2])), as * s.z, b.z);
+      v[j + 3] = fmaf(__int2float_rn(static_cast<int>(r[j + 3])), as * s.w, b.w);
+    } else {
+      v[j + 0] = __uint_as_float(r[j + 0]) + b.x;
+      v[j + 1] = __uint_as_float(r[j + 1]) + b.y;
+      v[j + 2] = __uint_as_float(r[j + 2]) + b.z;
+      v[j + 3] = __uint_as_float(r[j + 3]) + b.w;
+    }
+  }
+  if (p.epi == JB_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
+  } else if (p.epi == JB_EPI_QUICK_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = quick_gelu_tc(v[j]);
+  }
   if (p.c_dtype == JB_DT_BF16) {
     bf16* c = static_cast<bf16*>(p.C) + off;
-    if (ncols == 32) {
-      if (p.epi == JB_EPI_RESIDUAL) {
-        const bf16* rs = static_cast<const bf16*>(p.resid) + roff;
+    if (full) {
+      if (res_bf16) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 raw = *reinterpret_cast<const uint4*>(rs + j);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&res[e]);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 f = __bfloat1622float2(h[e]);
-            v[j + 2 * e] += f.x;
-            v[j + 2 * e + 1] += f.y;
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h[q]);
+            v[8 * e + 2 * q] += f.x;
+            v[8 * e + 2 * q + 1] += f.y;
           }
         }
       }
@@ -122,7 +276,7 @@ __device__ __forceinline__ void store_chunk(const EpiParams& p, int row, int col
         uint4 out;
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+        for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
         *reinterpret_cast<uint4*>(c + j) = out;
       }
     } else {
@@ -139,12 +293,12 @@ __device__ __forceinline__ void store_chunk(const EpiParams& p, int row, int col
   } else {  // f32 output
     float* c = static_cast<float*>(p.C) + off;
     const float* rs = static_cast<const float*>(p.resid) + roff;
-    if (ncols == 32) {
+    if (full) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
         float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         if (p.epi == JB_EPI_RESIDUAL) {
-          float4 q = *reinterpret_cast<const float4*>(rs + j);
+          const float4 q = *reinterpret_cast<const float4*>(rs + j);
           o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
         }
         *reinterpret_cast<float4*>(c + j) = o;
@@ -168,13 +322,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+  // layout: [stages][A | B] | params [2][bias BN | scale BN] | epilogue chunks |
+  //         barriers | tmem slot | abort flag
+  float* params = reinterpret_cast<float*>(gbase + Cfg::STAGES * Cfg::STAGE_BYTES);
+  const uint32_t chunks = base + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::PARAM_BYTES;
+  const uint32_t bars = chunks + Cfg::CHUNK_BYTES;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (Cfg::STAGES + s); };
   auto tfull_bar = [&](int i) { return bars + 8u * (2 * Cfg::STAGES + i); };
   auto tempty_bar = [&](int i) { return bars + 8u * (2 * Cfg::STAGES + 2 + i); };
-  uint32_t* tmem_slot =
-      reinterpret_cast<uint32_t*>(gbase + Cfg::STAGES * Cfg::STAGE_BYTES + 8 * (2 * Cfg::STAGES + 4));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + Cfg::STAGES * Cfg::STAGE_BYTES +
+                                                    Cfg::PARAM_BYTES + Cfg::CHUNK_BYTES +
+                                                    8 * (2 * Cfg::STAGES + 4));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -192,7 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(tfull_bar(i), 1);
-      mbar_init(tempty_bar(i), 4);
+      mbar_init(tempty_bar(i), kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -260,26 +419,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue: warp w may read TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    // Epilogue warps 2..9.  Warp w may read TMEM lanes 32*(w%4)..+31; the two
+    // warps of a lane quarter split the tile's columns in halves.
     const int quarter = warp & 3;
+    const int etid = threadIdx.x - 64;
+    const int half = (warp - 2) >> 2;
+    constexpr int kHalfCols = BN / 2;
+    const uint32_t my_chunk = chunks + static_cast<uint32_t>(etid >> 5) * kChunkBytes;
     int acc = 0;
     uint32_t acc_ph = 0;
     for (int t = blockIdx.x; t < total && kb_count > 0; t += gridDim.x) {
       const int mb = t / n_tiles, nb = t % n_tiles;
-      bool ok = mbar_wait(tfull_bar(acc), acc_ph, abort_flag);
+      // Stage this tile's per-column parameters (buffer `acc`; its previous
+      // readers finished before the last staging barrier).
+      float* pb = params + acc * 2 * BN;
+      float* ps = pb + BN;
+      for (int i = etid; i < BN; i += kEpiThreads) {
+        const int col = nb * BN + i;
+        const bool in = col < p.N;
+        pb[i] = (in && p.bias) ? __ldg(p.bias + col) : 0.f;
+        ps[i] = (S8 && in && p.w_scale) ? __ldg(p.w_scale + col) : 0.f;
+      }
+      epi_bar();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const float as = (S8 && p.a_scale && row < M) ? __ldg(p.a_scale + row) : 0.f;
+      const bool ok = mbar_wait(tfull_bar(acc), acc_ph, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int row = mb * kBM + quarter * 32 + lane;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; c += 32) {
         const int col0 = nb * BN + c;
         if (col0 >= p.N) break;  // warp-uniform
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + c, r);
         tmem_wait_ld();
-        if (row < M) store_chunk<S8>(p, row, col0, r);
+        if (p.c_dtype == JB_DT_BF16 && col0 + 32 <= p.N)  // warp-uniform
+          epi_chunk_bf16<S8>(p, row - lane, lane, M, col0, r, pb + c, ps + c, as, my_chunk);
+        else if (row < M)
+          epi_chunk<S8>(p, row, col0, r, pb + c, ps + c, as);
       }
       tc_fence_before();
       __syncwarp();

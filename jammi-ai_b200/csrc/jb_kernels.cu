@@ -58,11 +58,11 @@ __device__ __forceinline__ int8_t quant1(float x, float inv) {
 }
 
 // Normalises the row held in v[] (nvec vectors of Vec<T>::N per lane slot),
-// writes y (and optionally int8 + scale).  Called by one full warp.
+// writes y (and optionally int8 + scale).  Called by one full warp; gamma
+// and beta are read as float4 (16-byte aligned, shared or global memory).
 template <typename T, int MAXV>
 __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec, int cols, int lane,
-                                          const float* __restrict__ gamma,
-                                          const float* __restrict__ beta, float eps, T* yrow,
+                                          const float* gamma, const float* beta, float eps, T* yrow,
                                           int8_t* qrow, float* scale_out) {
   constexpr int VN = Vec<T>::N;
   float s = 0.f;
@@ -89,10 +89,18 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
     const int vi = lane + i * 32;
     if (vi < nvec) {
       float o[VN];
+      const float4* g4 = reinterpret_cast<const float4*>(gamma + vi * VN);
+      const float4* b4 = reinterpret_cast<const float4*>(beta + vi * VN);
+#pragma unroll
+      for (int q = 0; q < VN / 4; ++q) {
+        const float4 g = g4[q], b = b4[q];
+        o[4 * q + 0] = (v[i * VN + 4 * q + 0] - mean) * rstd * g.x + b.x;
+        o[4 * q + 1] = (v[i * VN + 4 * q + 1] - mean) * rstd * g.y + b.y;
+        o[4 * q + 2] = (v[i * VN + 4 * q + 2] - mean) * rstd * g.z + b.z;
+        o[4 * q + 3] = (v[i * VN + 4 * q + 3] - mean) * rstd * g.w + b.w;
+      }
 #pragma unroll
       for (int e = 0; e < VN; ++e) {
-        const int c = vi * VN + e;
-        o[e] = (v[i * VN + e] - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
         v[i * VN + e] = Vec<T>::rounded(o[e]);
         amax = fmaxf(amax, fabsf(v[i * VN + e]));
       }
@@ -119,70 +127,92 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
   }
 }
 
+constexpr int kLnMaxCols = 1024;
+
+// Stages gamma / beta (cols <= 1024 floats each) in shared memory.
+__device__ __forceinline__ void stage_params(float* sg, float* sb, const float* gamma,
+                                             const float* beta, int cols) {
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    sg[c] = gamma[c];
+    sb[c] = beta[c];
+  }
+  __syncthreads();
+}
+
+// Persistent over rows: warp w of block b handles rows b*8+w, +gridDim*8, ...
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) layernorm_kernel(LnArgs a) {
   constexpr int VN = Vec<T>::N;
+  __shared__ __align__(16) float sg[kLnMaxCols];
+  __shared__ __align__(16) float sb[kLnMaxCols];
+  stage_params(sg, sb, a.gamma, a.beta, a.cols);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRowsPerBlock + warp;
   const int R = a.drows ? min(*a.drows, a.rows) : a.rows;
-  if (row >= R) return;
   const int nvec = a.cols / VN;
-  const T* x = static_cast<const T*>(a.x) + static_cast<size_t>(row) * a.cols;
-  const T* r = a.resid ? static_cast<const T*>(a.resid) + static_cast<size_t>(row) * a.cols : nullptr;
-  float v[MAXV * VN];
+  for (int row = blockIdx.x * kRowsPerBlock + warp; row < R; row += gridDim.x * kRowsPerBlock) {
+    const T* x = static_cast<const T*>(a.x) + static_cast<size_t>(row) * a.cols;
+    const T* r = a.resid ? static_cast<const T*>(a.resid) + static_cast<size_t>(row) * a.cols : nullptr;
+    float v[MAXV * VN];
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int vi = lane + i * 32;
-    if (vi < nvec) {
-      Vec<T>::load(x + vi * VN, v + i * VN);
-      if (r) {
-        float t[VN];
-        Vec<T>::load(r + vi * VN, t);
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        Vec<T>::load(x + vi * VN, v + i * VN);
+        if (r) {
+          float t[VN];
+          Vec<T>::load(r + vi * VN, t);
 #pragma unroll
-        for (int e = 0; e < VN; ++e) v[i * VN + e] += t[e];
+          for (int e = 0; e < VN; ++e) v[i * VN + e] += t[e];
+        }
       }
     }
+    ln_finish<T, MAXV>(v, nvec, a.cols, lane, sg, sb, a.eps,
+                       static_cast<T*>(a.y) + static_cast<size_t>(row) * a.cols,
+                       a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
+                       a.yscale ? a.yscale + row : nullptr);
   }
-  ln_finish<T, MAXV>(v, nvec, a.cols, lane, a.gamma, a.beta, a.eps,
-                     static_cast<T*>(a.y) + static_cast<size_t>(row) * a.cols,
-                     a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
-                     a.yscale ? a.yscale + row : nullptr);
 }
 
+// Persistent over (row b, position p) slots; padding slots are skipped.
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
   constexpr int VN = Vec<T>::N;
+  __shared__ __align__(16) float sg[kLnMaxCols];
+  __shared__ __align__(16) float sb[kLnMaxCols];
+  stage_params(sg, sb, a.gamma, a.beta, a.H);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos_idx = blockIdx.x * kRowsPerBlock + warp;
-  if (pos_idx >= a.batch * a.max_seq) return;
-  const int b = pos_idx / a.max_seq, p = pos_idx % a.max_seq;
-  const int start = a.cu[b], len = a.cu[b + 1] - start;
-  if (p >= len) return;
-  uint32_t id = a.ids[static_cast<size_t>(b) * a.max_seq + p];
-  if (id >= static_cast<uint32_t>(a.vocab)) {
-    if (lane == 0 && a.err) atomicOr(a.err, 2);
-    id = 0;
-  }
   const int nvec = a.H / VN;
-  const T* w = static_cast<const T*>(a.word) + static_cast<size_t>(id) * a.H;
-  const T* pe = static_cast<const T*>(a.pos) + static_cast<size_t>(p) * a.H;
-  const T* te = static_cast<const T*>(a.type0);
-  float v[MAXV * VN];
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int vi = lane + i * 32;
-    if (vi < nvec) {
-      float t1[VN], t2[VN];
-      Vec<T>::load(w + vi * VN, v + i * VN);
-      Vec<T>::load(te + vi * VN, t1);
-      Vec<T>::load(pe + vi * VN, t2);
-#pragma unroll
-      for (int e = 0; e < VN; ++e) v[i * VN + e] += t1[e] + t2[e];
+  const int slots = a.batch * a.max_seq;
+  for (int pos_idx = blockIdx.x * kRowsPerBlock + warp; pos_idx < slots;
+       pos_idx += gridDim.x * kRowsPerBlock) {
+    const int b = pos_idx / a.max_seq, p = pos_idx % a.max_seq;
+    const int start = a.cu[b], len = a.cu[b + 1] - start;
+    if (p >= len) continue;  // warp-uniform
+    uint32_t id = a.ids[static_cast<size_t>(b) * a.max_seq + p];
+    if (id >= static_cast<uint32_t>(a.vocab)) {
+      if (lane == 0 && a.err) atomicOr(a.err, 2);
+      id = 0;
     }
+    const T* w = static_cast<const T*>(a.word) + static_cast<size_t>(id) * a.H;
+    const T* pe = static_cast<const T*>(a.pos) + static_cast<size_t>(p) * a.H;
+    const T* te = static_cast<const T*>(a.type0);
+    float v[MAXV * VN];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        float t1[VN], t2[VN];
+        Vec<T>::load(w + vi * VN, v + i * VN);
+        Vec<T>::load(te + vi * VN, t1);
+        Vec<T>::load(pe + vi * VN, t2);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) v[i * VN + e] = (v[i * VN + e] + t1[e]) + t2[e];
+      }
+    }
+    const size_t row = static_cast<size_t>(start + p);
+    ln_finish<T, MAXV>(v, nvec, a.H, lane, sg, sb, a.eps, static_cast<T*>(a.y) + row * a.H,
+                       a.yq ? a.yq + row * a.H : nullptr, a.yscale ? a.yscale + row : nullptr);
   }
-  const size_t row = static_cast<size_t>(start + p);
-  ln_finish<T, MAXV>(v, nvec, a.H, lane, a.gamma, a.beta, a.eps, static_cast<T*>(a.y) + row * a.H,
-                     a.yq ? a.yq + row * a.H : nullptr, a.yscale ? a.yscale + row : nullptr);
 }
 
 template <typename T>
@@ -220,7 +250,6 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
 
 // ── pooling + L2 (pooling.rs:31-148) ──────────────────────────────────────
 constexpr int kPoolThreads = 128;
-constexpr int kPoolMaxCols = 8;  // columns per thread -> H <= 1024
 
 __device__ __forceinline__ float block_sum_128(float v, float* red) {
   v = warp_sum(v);
@@ -234,65 +263,87 @@ __device__ __forceinline__ float block_sum_128(float v, float* red) {
   return t;
 }
 
+// One block per row: warp w accumulates tokens w, w+8, ... over all columns
+// (each lane owns 16-byte column vectors lane, lane+32, ...); the eight
+// partial vectors meet in shared memory, then the block forms the L2 norm.
+constexpr int kPoolWarps = 8;
+constexpr int kPoolMaxH = 1024;
+
 template <typename T>
-__global__ void __launch_bounds__(kPoolThreads) pool_normalize_kernel(const T* __restrict__ hidden,
-                                                                      const int* __restrict__ cu,
-                                                                      float* __restrict__ out, int H,
-                                                                      int pooling) {
-  __shared__ float red[kPoolThreads / 32];
+__global__ void __launch_bounds__(kPoolWarps * 32) pool_normalize_kernel(const T* __restrict__ hidden,
+                                                                         const int* __restrict__ cu,
+                                                                         float* __restrict__ out, int H,
+                                                                         int pooling) {
+  constexpr int VN = Vec<T>::N;
+  constexpr int MAXV = kPoolMaxH / (32 * VN);
+  __shared__ float part[kPoolWarps][kPoolMaxH];
+  __shared__ float red[kPoolWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x;
   const int start = cu[b], n = cu[b + 1] - start;
-  float acc[kPoolMaxCols];
-  const float init = (pooling == JB_POOL_MAX) ? -1e30f : 0.f;
+  const int nvec = H / VN;
+  const bool is_max = pooling == JB_POOL_MAX;
+  float acc[MAXV * VN];
 #pragma unroll
-  for (int k = 0; k < kPoolMaxCols; ++k) acc[k] = init;
-  if (pooling == JB_POOL_CLS) {
-    if (n > 0) {
+  for (int k = 0; k < MAXV * VN; ++k) acc[k] = is_max ? -1e30f : 0.f;
+  // CLS reads token 0 only; an all-padding row has none and stays zero.
+  const int t_end = pooling == JB_POOL_CLS ? min(n, 1) : n;
+  for (int t = warp; t < t_end; t += kPoolWarps) {
+    const T* hr = hidden + static_cast<size_t>(start + t) * H;
+    const float w = pooling == JB_POOL_WEIGHTED_MEAN ? static_cast<float>(t + 1) : 1.f;
 #pragma unroll
-      for (int k = 0; k < kPoolMaxCols; ++k) {
-        const int c = threadIdx.x + k * kPoolThreads;
-        if (c < H) acc[k] = to_f(hidden[static_cast<size_t>(start) * H + c]);
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        float x[VN];
+        Vec<T>::load(hr + vi * VN, x);
+#pragma unroll
+        for (int e = 0; e < VN; ++e)
+          acc[i * VN + e] = is_max ? fmaxf(acc[i * VN + e], x[e]) : fmaf(x[e], w, acc[i * VN + e]);
       }
-    }
-  } else {
-    for (int t = 0; t < n; ++t) {
-      const T* hr = hidden + static_cast<size_t>(start + t) * H;
-      const float w = static_cast<float>(t + 1);
-#pragma unroll
-      for (int k = 0; k < kPoolMaxCols; ++k) {
-        const int c = threadIdx.x + k * kPoolThreads;
-        if (c < H) {
-          const float x = to_f(hr[c]);
-          if (pooling == JB_POOL_MAX)
-            acc[k] = fmaxf(acc[k], x);
-          else if (pooling == JB_POOL_WEIGHTED_MEAN)
-            acc[k] += x * w;
-          else
-            acc[k] += x;
-        }
-      }
-    }
-    float den = 1.f;
-    if (pooling == JB_POOL_MEAN) den = fmaxf(static_cast<float>(n), 1.f);
-    if (pooling == JB_POOL_WEIGHTED_MEAN)
-      den = fmaxf(0.5f * static_cast<float>(n) * static_cast<float>(n + 1), 1.f);
-    if (pooling != JB_POOL_MAX) {
-#pragma unroll
-      for (int k = 0; k < kPoolMaxCols; ++k) acc[k] = acc[k] / den;
     }
   }
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) part[warp][vi * VN + e] = acc[i * VN + e];
+  }
+  __syncthreads();
+  float den = 1.f;
+  if (pooling == JB_POOL_MEAN) den = fmaxf(static_cast<float>(n), 1.f);
+  if (pooling == JB_POOL_WEIGHTED_MEAN)
+    den = fmaxf(0.5f * static_cast<float>(n) * static_cast<float>(n + 1), 1.f);
+  constexpr int kPer = kPoolMaxH / (kPoolWarps * 32);
+  float vals[kPer];
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kPoolMaxCols; ++k)
-    if (threadIdx.x + k * kPoolThreads < H) ss += acc[k] * acc[k];
-  ss = block_sum_128(ss, red);
+  for (int k = 0; k < kPer; ++k) {
+    const int c = threadIdx.x + k * kPoolWarps * 32;
+    float v = 0.f;
+    if (c < H) {
+      v = part[0][c];
+#pragma unroll
+      for (int w = 1; w < kPoolWarps; ++w) v = is_max ? fmaxf(v, part[w][c]) : v + part[w][c];
+      if (!is_max) v = v / den;
+      ss += v * v;
+    }
+    vals[k] = v;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int w = 0; w < kPoolWarps; ++w) ss += red[w];
   // clamp(||x||, 1e-12, f32::MAX): an overflowing square sum (the -1e30
   // max-pool sentinel of an all-padding row) clamps to f32::MAX.
   const float norm = fminf(fmaxf(sqrtf(ss), 1e-12f), FLT_MAX);
 #pragma unroll
-  for (int k = 0; k < kPoolMaxCols; ++k) {
-    const int c = threadIdx.x + k * kPoolThreads;
-    if (c < H) out[static_cast<size_t>(b) * H + c] = acc[k] / norm;
+  for (int k = 0; k < kPer; ++k) {
+    const int c = threadIdx.x + k * kPoolWarps * 32;
+    if (c < H) out[static_cast<size_t>(b) * H + c] = vals[k] / norm;
   }
 }
 
@@ -450,9 +501,19 @@ inline unsigned blocks_for(size_t n, unsigned per) { return static_cast<unsigned
 
 }  // namespace
 
+// Persistent row kernels: at most 4 resident 256-thread blocks per SM.
+unsigned persistent_grid(size_t rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned cap = static_cast<unsigned>(num_sms(dev)) * 4u;
+  const unsigned need = blocks_for(rows, kRowsPerBlock);
+  return need < cap ? need : cap;
+}
+
 cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
   if (a.rows == 0) return cudaSuccess;
-  const unsigned grid = blocks_for(a.rows, kRowsPerBlock);
+  if (a.cols > kLnMaxCols) return cudaErrorInvalidValue;
+  const unsigned grid = persistent_grid(a.rows);
   if (a.dtype == JB_DT_BF16) {
     if (a.cols % 8 || a.cols > 1024) return cudaErrorInvalidValue;
     layernorm_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
@@ -466,7 +527,7 @@ cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s) {
   const size_t n = static_cast<size_t>(a.batch) * a.max_seq;
   if (n == 0) return cudaSuccess;
-  const unsigned grid = blocks_for(n, kRowsPerBlock);
+  const unsigned grid = persistent_grid(n);
   if (a.dtype == JB_DT_BF16) {
     if (a.H % 8 || a.H > 1024) return cudaErrorInvalidValue;
     embed_ln_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
@@ -496,13 +557,16 @@ cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* sca
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s) {
   if (batch == 0) return cudaSuccess;
-  if (H > kPoolThreads * kPoolMaxCols || pooling < 0 || pooling > 3) return cudaErrorInvalidValue;
-  if (dtype == JB_DT_BF16)
-    pool_normalize_kernel<bf16><<<batch, kPoolThreads, 0, s>>>(static_cast<const bf16*>(hidden), cu,
-                                                               out, H, pooling);
-  else
-    pool_normalize_kernel<float><<<batch, kPoolThreads, 0, s>>>(static_cast<const float*>(hidden),
-                                                                cu, out, H, pooling);
+  if (H > kPoolMaxH || pooling < 0 || pooling > 3) return cudaErrorInvalidValue;
+  if (dtype == JB_DT_BF16) {
+    if (H % 8) return cudaErrorInvalidValue;
+    pool_normalize_kernel<bf16><<<batch, kPoolWarps * 32, 0, s>>>(static_cast<const bf16*>(hidden),
+                                                                  cu, out, H, pooling);
+  } else {
+    if (H % 4) return cudaErrorInvalidValue;
+    pool_normalize_kernel<float><<<batch, kPoolWarps * 32, 0, s>>>(
+        static_cast<const float*>(hidden), cu, out, H, pooling);
+  }
   return cudaGetLastError();
 }
 

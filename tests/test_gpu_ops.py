@@ -83,6 +83,31 @@ def test_linear_bf16_epilogues(dev, epi):
     assert err <= 8e-3 * ref.abs().max().item() + 1e-3, err
 
 
+@pytest.mark.parametrize("epi", ["gelu", "quick_gelu"])
+def test_tensor_core_activation_accuracy(dev, epi):
+    """The tensor-core epilogue's activations against float64: C[m, n] = x_m
+    exactly (one non-zero product), so C - act(x) is the activation's own
+    error.  GELU uses erf from Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7);
+    the bar allows that plus the approximate reciprocal / exponential."""
+    import jammi_b200 as jb
+    ops = _ops()
+    x = torch.linspace(-12, 12, 8192).to(torch.bfloat16).float().numpy()
+    a = np.zeros((x.size, 64), np.float32)
+    a[:, 0] = x
+    w = np.zeros((32, 64), np.float32)
+    w[:, 0] = 1.0
+    e = jb.EPI_GELU if epi == "gelu" else jb.EPI_QUICK_GELU
+    c = ops.linear(_bf16(a, dev), _bf16(w, dev), epilogue=e, out_dtype=torch.float32)
+    ops.sync()
+    xd = x.astype(np.float64)
+    if epi == "gelu":
+        ref = 0.5 * xd * (1 + np.vectorize(math.erf)(xd / math.sqrt(2)))
+    else:
+        ref = xd / (1 + np.exp(-1.702 * xd))
+    err = np.abs(c.double().cpu().numpy() - ref[:, None])
+    assert np.all(err <= 1e-6 * np.maximum(1.0, np.abs(xd))[:, None]), err.max()
+
+
 def test_linear_bf16_f32_output(dev):
     ops = _ops()
     rng = np.random.default_rng(9)
