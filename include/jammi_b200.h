@@ -204,6 +204,72 @@ jb_status jb_op_sync(void* stream);
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens,
                                float* out, int batch, int H, int pooling, void* stream);
 
+/* ── memory-budget admission ──────────────────────────────────────────────
+ * GpuScheduler (crates/jammi-ai/src/concurrency/gpu_scheduler.rs:11-218):
+ * budget = total * (1 - headroom_fraction); reservations by compare-and-swap;
+ * a release wakes blocked acquirers; priority is accepted and ignored. */
+typedef struct jb_scheduler jb_scheduler;
+/* GpuScheduler::new; NULL (and jb_last_error) when headroom is outside [0, 1]. */
+jb_scheduler* jb_scheduler_new(uint64_t total_bytes, double headroom_fraction);
+/* GpuScheduler::new_unlimited (CPU, or a failed memory probe). */
+jb_scheduler* jb_scheduler_new_unlimited(void);
+/* GpuScheduler::for_device (gpu_scheduler.rs:114-145): cudaMemGetInfo on
+ * `device`, headroom = 1 - memory_fraction clamped to [0, 1]; device < 0 or a
+ * failed probe gives an unlimited scheduler. */
+jb_scheduler* jb_scheduler_for_device(int device, double memory_fraction);
+void jb_scheduler_free(jb_scheduler* s);
+int jb_scheduler_is_unlimited(const jb_scheduler* s);
+uint64_t jb_scheduler_available(const jb_scheduler* s);
+/* GpuScheduler::try_acquire: 1 when reserved, 0 when it would exceed the budget. */
+int jb_scheduler_try_acquire(jb_scheduler* s, uint64_t bytes);
+/* GpuScheduler::acquire: blocks until the bytes fit (woken by releases).
+ * Requests larger than the whole budget fail at once with JB_ERR_OOM;
+ * timeout_ms < 0 waits indefinitely, otherwise JB_ERR_TIMEOUT. */
+jb_status jb_scheduler_acquire(jb_scheduler* s, uint64_t bytes, int priority, int64_t timeout_ms);
+/* Drop of GpuPermit: returns the bytes and wakes waiters. */
+void jb_scheduler_release(jb_scheduler* s, uint64_t bytes);
+
+/* ── chunked runner ───────────────────────────────────────────────────────
+ * InferenceRunner::run_chunks (crates/jammi-ai/src/inference/runner.rs:176-241):
+ * forward(user, start, count, msg, msg_len) runs rows [start, start+count)
+ * and returns a jb_status, writing a message on failure.  When the message is
+ * an OOM (is_oom_error, runner.rs:243-256: "out of memory", "out_of_memory",
+ * "outofmemory" or "oom", case-insensitive) and *batch_size > 1, the batch
+ * size halves and the same slice is retried; any other failure, or an OOM at
+ * batch size 1, is returned.  *batch_size keeps the final size. */
+typedef int (*jb_forward_cb)(void* user, int64_t start, int64_t count, char* msg, size_t msg_len);
+jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, void* user);
+int jb_is_oom_message(const char* msg);
+
+/* ── multi-device embedding generation ────────────────────────────────────
+ * The generate_embeddings driver (crates/jammi-ai/src/pipeline/embedding.rs:47-282
+ * -> runner.rs:176-241 -> candle.rs:764-856) over one model handle per device:
+ * rows are given as ragged token ids (values + row offsets, the layout of an
+ * Arrow list array); empty rows are excluded and come out as zero vectors
+ * with a null validity bit (candle.rs:785-797); the rest are length-bucketed
+ * (longest first), cut into batches of batch_rows, and pulled by one worker
+ * thread per device (one stream each, pinned double-buffered staging,
+ * OOM batch-halving).  Embeddings land in row order in out[rows, H] -- the
+ * values buffer of an Arrow FixedSizeList<Float32>[H]
+ * (crates/jammi-ai/src/inference/adapter/embedding.rs:32-55) -- and
+ * validity[(rows+7)/8] is the Arrow bitmap (may be NULL).
+ * memory_fraction > 0 enables per-device admission (jb_scheduler_for_device). */
+typedef struct {
+  int32_t batch_rows;      /* rows per batch, e.g. 256 */
+  int32_t pooling;         /* jb_pooling */
+  int32_t sort_by_length;  /* length bucketing, longest first */
+  int32_t pad_multiple;    /* pad each batch's width up to a multiple (>= 1) */
+  double memory_fraction;  /* GpuConfig::memory_fraction; <= 0 disables admission */
+} jb_generate_opts;
+typedef struct {
+  int64_t rows, valid_rows, batches, tokens, oom_retries;
+  double seconds;
+} jb_generate_stats;
+jb_status jb_generate_embeddings(jb_model** models, int n_models, const uint32_t* ids,
+                                 const uint64_t* offsets, int64_t rows,
+                                 const jb_generate_opts* opts, float* out, uint8_t* validity,
+                                 jb_generate_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

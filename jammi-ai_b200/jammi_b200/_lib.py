@@ -71,6 +71,18 @@ _SIGS = [
     ("jb_op_layernorm", _I, [_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
     ("jb_op_attention", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_pool_normalize", _I, [_P, _I, _P, _P, _I, _I, _I, _P]),
+    ("jb_scheduler_new", _P, [ctypes.c_uint64, ctypes.c_double]),
+    ("jb_scheduler_new_unlimited", _P, []),
+    ("jb_scheduler_for_device", _P, [_I, ctypes.c_double]),
+    ("jb_scheduler_free", None, [_P]),
+    ("jb_scheduler_is_unlimited", _I, [_P]),
+    ("jb_scheduler_available", ctypes.c_uint64, [_P]),
+    ("jb_scheduler_try_acquire", _I, [_P, ctypes.c_uint64]),
+    ("jb_scheduler_acquire", _I, [_P, ctypes.c_uint64, _I, ctypes.c_int64]),
+    ("jb_scheduler_release", None, [_P, ctypes.c_uint64]),
+    ("jb_is_oom_message", _I, [ctypes.c_char_p]),
+    ("jb_run_chunks", _I, [ctypes.c_int64, ctypes.POINTER(ctypes.c_int), _P, _P]),
+    ("jb_generate_embeddings", _I, [_P, _I, _P, _P, ctypes.c_int64, _P, _P, _P, _P]),
 ]
 
 

@@ -1,0 +1,136 @@
+"""Host runtime bindings: memory-budget admission, the chunked runner and the
+multi-device embedding driver (all implemented in C++ inside the library).
+
+* ``Scheduler``            -- ``GpuScheduler`` (crates/jammi-ai/src/concurrency/gpu_scheduler.rs)
+* ``run_chunks``           -- ``InferenceRunner::run_chunks`` with OOM halving
+  (crates/jammi-ai/src/inference/runner.rs:176-256)
+* ``generate_embeddings``  -- the ``generate_embeddings`` driver over one model
+  handle per device, row-order output in Arrow FixedSizeList layout.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib as L
+from ._lib import JbError, check, lib
+from .encoders import POOLING
+
+
+class GenerateOpts(ctypes.Structure):
+    _fields_ = [("batch_rows", ctypes.c_int32), ("pooling", ctypes.c_int32),
+                ("sort_by_length", ctypes.c_int32), ("pad_multiple", ctypes.c_int32),
+                ("memory_fraction", ctypes.c_double)]
+
+
+class GenerateStats(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int64), ("valid_rows", ctypes.c_int64), ("batches", ctypes.c_int64),
+                ("tokens", ctypes.c_int64), ("oom_retries", ctypes.c_int64), ("seconds", ctypes.c_double)]
+
+
+FORWARD_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                              ctypes.c_void_p, ctypes.c_size_t)
+
+
+class Scheduler:
+    """GPU memory-budget admission (one per device)."""
+
+    def __init__(self, handle):
+        if not handle:
+            msg = lib().jb_last_error()
+            raise JbError(L.ERR_INVALID, msg.decode() if msg else "scheduler creation failed")
+        self._h = ctypes.c_void_p(handle)
+
+    @classmethod
+    def new(cls, total_bytes: int, headroom_fraction: float):
+        return cls(lib().jb_scheduler_new(int(total_bytes), float(headroom_fraction)))
+
+    @classmethod
+    def unlimited(cls):
+        return cls(lib().jb_scheduler_new_unlimited())
+
+    @classmethod
+    def for_device(cls, device: int, memory_fraction: float):
+        return cls(lib().jb_scheduler_for_device(int(device), float(memory_fraction)))
+
+    @property
+    def is_unlimited(self) -> bool:
+        return bool(lib().jb_scheduler_is_unlimited(self._h))
+
+    def available(self) -> int:
+        return int(lib().jb_scheduler_available(self._h))
+
+    def try_acquire(self, nbytes: int) -> bool:
+        return bool(lib().jb_scheduler_try_acquire(self._h, int(nbytes)))
+
+    def acquire(self, nbytes: int, priority: int = 0, timeout_ms: int = -1):
+        check(lib().jb_scheduler_acquire(self._h, int(nbytes), int(priority), int(timeout_ms)))
+
+    def release(self, nbytes: int):
+        lib().jb_scheduler_release(self._h, int(nbytes))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().jb_scheduler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def is_oom_message(msg: str) -> bool:
+    return bool(lib().jb_is_oom_message(msg.encode()))
+
+
+def run_chunks(rows: int, batch_size: int, forward) -> int:
+    """Run ``forward(start, count)`` over ``rows`` in chunks; an exception whose
+    text is an OOM halves the batch and retries the same slice.  Returns the
+    final batch size; raises JbError for a propagated failure."""
+    def cb(_user, start, count, msg, msg_len):
+        try:
+            forward(int(start), int(count))
+            return L.OK
+        except Exception as e:  # noqa: BLE001 -- the message crosses the ABI
+            text = str(e).encode()[: max(0, int(msg_len) - 1)]
+            ctypes.memmove(msg, text + b"\0", len(text) + 1)
+            return int(getattr(e, "status", L.ERR_INVALID))
+    c_cb = FORWARD_CB(cb)
+    bs = ctypes.c_int(int(batch_size))
+    check(lib().jb_run_chunks(int(rows), ctypes.byref(bs), ctypes.cast(c_cb, ctypes.c_void_p), None))
+    return bs.value
+
+
+def pack_rows(rows) -> tuple[np.ndarray, np.ndarray]:
+    """List of token-id sequences -> (values u32, offsets u64[len+1])."""
+    lens = np.array([len(r) for r in rows], dtype=np.uint64)
+    offsets = np.zeros(len(rows) + 1, dtype=np.uint64)
+    np.cumsum(lens, out=offsets[1:])
+    values = np.concatenate([np.asarray(r, dtype=np.uint32) for r in rows]) if len(rows) else np.zeros(0, np.uint32)
+    return np.ascontiguousarray(values, dtype=np.uint32), offsets
+
+
+def generate_embeddings(models, values, offsets, batch_rows: int = 256, pooling: str = "mean",
+                        sort_by_length: bool = True, pad_multiple: int = 8,
+                        memory_fraction: float = 0.0):
+    """Embeddings for every row, in row order.  ``models``: one Bert per device.
+    Returns (out f32 [rows, H], validity bitmap u8 [(rows+7)//8], stats dict)."""
+    values = np.ascontiguousarray(values, dtype=np.uint32)
+    offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+    rows = offsets.size - 1
+    H = models[0].info.hidden
+    out = np.empty((rows, H), dtype=np.float32)
+    validity = np.zeros((rows + 7) // 8, dtype=np.uint8)
+    handles = (ctypes.c_void_p * len(models))(*[m.handle.value for m in models])
+    opts = GenerateOpts(int(batch_rows), POOLING[pooling], 1 if sort_by_length else 0,
+                        int(pad_multiple), float(memory_fraction))
+    stats = GenerateStats()
+    vp = values.ctypes.data if values.size else None
+    check(lib().jb_generate_embeddings(handles, len(models), vp, offsets.ctypes.data, rows,
+                                       ctypes.byref(opts), out.ctypes.data, validity.ctypes.data,
+                                       ctypes.byref(stats)))
+    st = {k: getattr(stats, k) for k, _ in GenerateStats._fields_}
+    return out, validity, st

@@ -1,0 +1,165 @@
+"""Host runtime on CPU: the memory-budget scheduler and the chunked runner,
+restating the reference's own tests with fakes (no GPU needed):
+crates/jammi-ai/tests/it/scheduling.rs, crates/jammi-ai/src/concurrency/gpu_scheduler.rs:221-266,
+crates/jammi-ai/src/inference/runner.rs:297-502."""
+import threading
+import time
+
+import pytest
+
+from jammi_b200 import _lib as L
+from jammi_b200.driver import Scheduler, is_oom_message, run_chunks
+from jammi_b200._lib import JbError
+
+GB = 1_000_000_000
+
+
+# ── scheduler ───────────────────────────────────────────────────────────────
+
+def test_permit_lifecycle_and_release():
+    s = Scheduler.new(GB, 0.2)
+    initial = s.available()
+    assert initial == 800_000_000
+    assert s.try_acquire(300_000_000)
+    assert s.available() == initial - 300_000_000
+    s.release(300_000_000)
+    assert s.available() == initial
+
+
+def test_headroom_fraction_enforced():
+    s = Scheduler.new(GB, 0.2)
+    assert s.try_acquire(800_000_000), "exact usable limit must succeed"
+    assert s.available() == 0
+    assert not s.try_acquire(1)
+    s.release(800_000_000)
+    assert s.available() == 800_000_000
+    half = Scheduler.new(GB, 0.5)
+    assert half.available() == 500_000_000
+    assert not half.try_acquire(600_000_000)
+    assert half.try_acquire(500_000_000)
+
+
+def test_headroom_out_of_range_rejected():
+    with pytest.raises(JbError):
+        Scheduler.new(GB, 1.5)
+
+
+def test_unlimited_and_cpu_device():
+    u = Scheduler.unlimited()
+    assert u.is_unlimited and u.available() == 2**64 - 1
+    assert u.try_acquire(10**18)
+    assert Scheduler.for_device(-1, 0.9).is_unlimited
+
+
+def test_for_device_probe_failure_is_unlimited():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the probe succeeds")
+    assert Scheduler.for_device(0, 0.9).is_unlimited
+
+
+def test_blocking_acquire_wakes_on_release():
+    s = Scheduler.new(GB, 0.0)
+    assert s.try_acquire(900_000_000)
+    got = threading.Event()
+
+    def waiter():
+        s.acquire(500_000_000, timeout_ms=10_000)
+        got.set()
+
+    t = threading.Thread(target=waiter)
+    t.start()
+    time.sleep(0.05)
+    assert not got.is_set(), "must block while the budget is exhausted"
+    s.release(900_000_000)
+    t.join(5)
+    assert got.is_set()
+    assert s.available() == 500_000_000
+
+
+def test_acquire_timeout_and_oversize():
+    s = Scheduler.new(GB, 0.0)
+    assert s.try_acquire(GB)
+    with pytest.raises(JbError) as e:
+        s.acquire(1, timeout_ms=50)
+    assert e.value.status == L.ERR_TIMEOUT
+    with pytest.raises(JbError) as e:
+        s.acquire(2 * GB, timeout_ms=50)
+    assert e.value.status == L.ERR_OOM and "out of memory" in str(e.value)
+
+
+def test_concurrent_acquire_stress_and_liveness():
+    s = Scheduler.new(GB, 0.1)
+    usable = s.available()
+    permit = 100_000_000
+    violations = []
+
+    def task():
+        for _ in range(50):
+            s.acquire(permit, timeout_ms=10_000)
+            if s.available() > usable - permit:
+                violations.append(s.available())
+            s.release(permit)
+
+    ts = [threading.Thread(target=task) for _ in range(16)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(30)
+    assert not violations
+    assert s.available() == usable
+
+
+# ── runner ──────────────────────────────────────────────────────────────────
+
+class FakeOom(Exception):
+    status = L.ERR_OOM
+
+
+def test_oom_classifier():
+    for msg in ("CUDA out of memory", "CUDA_ERROR_OUT_OF_MEMORY", "OutOfMemory", "oom killer"):
+        assert is_oom_message(msg)
+    for msg in ("CUDA_ERROR_INVALID_PTX", "cuda launch failed", "shape mismatch"):
+        assert not is_oom_message(msg)
+
+
+def test_row_conservation_across_oom_halving():
+    seen = []
+
+    def forward(start, count):
+        if count > 37:
+            raise FakeOom("CUDA out of memory: tried to allocate")
+        seen.extend(range(start, start + count))
+
+    bs = run_chunks(300, 256, forward)
+    assert seen == list(range(300)), "no row skipped or duplicated"
+    assert bs == 32
+
+
+def test_persistent_oom_at_batch_one_propagates():
+    calls = []
+
+    def forward(start, count):
+        calls.append(count)
+        raise FakeOom("out of memory")
+
+    with pytest.raises(JbError) as e:
+        run_chunks(10, 8, forward)
+    assert calls == [8, 4, 2, 1]
+    assert "out of memory" in str(e.value)
+
+
+def test_non_oom_error_propagates_immediately():
+    calls = []
+
+    class Broken(Exception):
+        status = L.ERR_CUDA
+
+    def forward(start, count):
+        calls.append(count)
+        raise Broken("CUDA_ERROR_INVALID_PTX")
+
+    with pytest.raises(JbError) as e:
+        run_chunks(100, 16, forward)
+    assert calls == [16], "a systemic error is never retried"
+    assert e.value.status == L.ERR_CUDA
