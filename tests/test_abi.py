@@ -45,13 +45,12 @@ def test_load_without_gpu_fails_loudly():
 
 
 def test_missing_library_raises(monkeypatch, tmp_path):
-    import importlib
     import jammi_b200._lib as L
     monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "absent.so"))
     monkeypatch.setattr(L, "_lib", None)
     with pytest.raises(ImportError):
         L.lib()
-    importlib.reload(L)
+    # monkeypatch restores LIB_PATH and the loaded handle afterwards
 
 
 def test_mask_to_lengths_rejects_holes():
