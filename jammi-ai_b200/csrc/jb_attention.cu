@@ -75,7 +75,9 @@ __device__ __forceinline__ void load_tile(uint32_t tile, const bf16* g, int ld, 
   }
 }
 
-__global__ void __launch_bounds__(kFaThreads) flash_attn_bf16_d64(const bf16* __restrict__ qkv,
+// Four CTAs per SM (128 registers, 40 KB shared memory each): the rows are
+// short, so the kernel is latency-bound and occupancy is what hides it.
+__global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16* __restrict__ qkv,
                                                                   const int* __restrict__ cu,
                                                                   bf16* __restrict__ ctx, int heads,
                                                                   float scale_log2) {
@@ -314,6 +316,8 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
   if (dtype == JB_DT_BF16 && head_dim == 64) {
     dim3 grid((max_len + kFaRows - 1) / kFaRows, heads, batch);
     const float scale_log2 = 1.4426950408889634f / sqrtf(64.f);
+    cudaFuncSetAttribute(flash_attn_bf16_d64, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
     flash_attn_bf16_d64<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu,
                                                     static_cast<bf16*>(ctx), heads, scale_log2);
     return cudaGetLastError();
