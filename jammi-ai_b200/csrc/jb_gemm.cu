@@ -106,8 +106,18 @@ __device__ __forceinline__ float quick_gelu_tc(float x) {
   return x * rcp_approx(1.0f + ex2_approx(-2.45546696f * x));
 }
 
-__device__ __forceinline__ void epi_bar() {
-  asm volatile("bar.sync %0, %1;" ::"n"(kEpiBarrier), "n"(kEpiThreads) : "memory");
+// Named barrier over the epilogue warps that also ANDs a predicate across them.
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kEpiBarrier), "n"(kEpiThreads)
+      : "memory");
+  return r != 0;
 }
 
 // ── coalesced bf16 epilogue ─────────────────────────────────────────────────
@@ -453,11 +463,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pb[i] = (in && p.bias) ? __ldg(p.bias + col) : 0.f;
         ps[i] = (S8 && in && p.w_scale) ? __ldg(p.w_scale + col) : 0.f;
       }
-      epi_bar();
       const int row = mb * kBM + quarter * 32 + lane;
       const float as = (S8 && p.a_scale && row < M) ? __ldg(p.a_scale + row) : 0.f;
-      const bool ok = mbar_wait(tfull_bar(acc), acc_ph, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      // One barrier orders the staging above and makes the accumulator-ready
+      // decision the same for every epilogue warp (so none can be left
+      // waiting at a later barrier after an abort).
+      const bool ok = epi_bar_and(mbar_wait(tfull_bar(acc), acc_ph, abort_flag));
+      if (!ok) break;
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
@@ -596,10 +608,8 @@ cudaError_t launch_tc(const GemmArgs& g, const EpiParams& p, cudaStream_t s, std
     return cudaErrorInvalidValue;
   }
   auto kern = gemm_tc_kernel<S8, BN>;
-  static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
-  (void)configured_dev;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
   if (e != cudaSuccess) return e;
   const int m_tiles = (g.M + kBM - 1) / kBM;
