@@ -8,10 +8,15 @@
 // tcgen05 kernel structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A tile [128 x 128 B] + W tile [BN x 128 B] per stage
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, dequant / bias /
-//               activation / residual, vectorised global stores
+//   warps 2..   epilogue (kEpiWarps, an equal number per TMEM lane quarter,
+//               each on a share of the tile's columns): tcgen05.ld of the
+//               accumulator, dequant / bias / activation / residual,
+//               coalesced global stores through a per-warp shared buffer
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the
-// epilogue of tile i overlaps the main loop of tile i+1.
+// epilogue of tile i overlaps the main loop of tile i+1.  The epilogue is
+// latency-bound, so it loads what it can one step ahead: the next tile's
+// bias / weight scales / token scales during the current tile, and each
+// unit's residual rows during the previous unit.
 #include <cudaTypedefs.h>
 
 #include <cstdio>
@@ -25,7 +30,13 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kRowBytes = 128;   // one 128-byte swizzle row of K per stage
-constexpr int kEpiWarps = 8;     // two per TMEM lane quarter, each on half the columns
+#ifndef JB_EPI_WARPS
+#define JB_EPI_WARPS 8
+#endif
+#ifndef JB_EPI_UNIT_COLS
+#define JB_EPI_UNIT_COLS 32
+#endif
+constexpr int kEpiWarps = JB_EPI_WARPS;  // kEpiWarps / 4 per TMEM lane quarter
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kGemmThreads = 64 + kEpiThreads;  // TMA warp + MMA warp + epilogue
 constexpr int kEpiBarrier = 1;   // named barrier among the epilogue warps
@@ -35,13 +46,15 @@ struct TcCfg {
   static constexpr int A_BYTES = kBM * kRowBytes;
   static constexpr int B_BYTES = BN * kRowBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES_FIT = (192 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN;
   // per accumulator buffer: bias[BN] and weight scale[BN] of the tile, f32
   static constexpr int PARAM_BYTES = 2 * 2 * BN * 4;
-  // one 32 x 32 bf16 output chunk per epilogue warp
-  static constexpr int CHUNK_BYTES = kEpiWarps * 32 * 64;
+  // one 32-row bf16 output unit per epilogue warp
+  static constexpr int CHUNK_BYTES = kEpiWarps * 32 * JB_EPI_UNIT_COLS * 2;
+  // as many operand stages (at most 8) as fit in 227 KB beside the rest
+  static constexpr int STAGES_FIT =
+      (232448 - PARAM_BYTES - CHUNK_BYTES - (8 * (2 * 8 + 4) + 16) - 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
   static constexpr int SMEM = STAGES * STAGE_BYTES + PARAM_BYTES + CHUNK_BYTES + BAR_BYTES + 1024;
 };
@@ -121,14 +134,27 @@ __device__ __forceinline__ bool epi_bar_and(bool v) {
 }
 
 // ── coalesced bf16 epilogue ─────────────────────────────────────────────────
-// Each epilogue warp owns a 2 KB shared buffer holding one 32 x 32 bf16 chunk
-// (32 rows of 64 B).  16-byte slot q of row r lives at r*64 + ((q ^ ((r>>1)&3))*16):
-// both the row-per-thread pattern (thread r touches row r) and the
-// coalesced pattern (lane l touches row 8i + l/4, slot l%4) are free of
-// bank conflicts.
-constexpr int kChunkBytes = 32 * 64;
-__device__ __forceinline__ uint32_t chunk_slot(uint32_t buf, int row, int q) {
-  return buf + row * 64 + ((q ^ ((row >> 1) & 3)) << 4);
+// The epilogue works in units of 32 rows x kUnitCols columns (one tcgen05.ld
+// 32x32b).  Each epilogue warp owns a shared buffer holding one unit in bf16
+// (32 rows of kSlots 16-byte slots).  Slot q of row r lives at
+// r*kUnitCols*2 + ((q ^ ((r >> kSwzShift) & (kSlots-1)))*16): both the
+// row-per-thread pattern (thread r touches row r) and the coalesced pattern
+// (lane l touches row kRowsPerIns*i + l/kSlots, slot l%kSlots, so each row's
+// segment is whole sectors) are free of bank conflicts.
+constexpr int kUnitCols = JB_EPI_UNIT_COLS;
+static_assert(kUnitCols == 16 || kUnitCols == 32, "unit of 16 or 32 columns");
+constexpr int kSlots = kUnitCols / 8;
+constexpr int kRowsPerIns = 32 / kSlots;
+constexpr int kSwzShift = kSlots == 4 ? 1 : 2;
+constexpr int kUnitBytes = 32 * kUnitCols * 2;
+__device__ __forceinline__ uint32_t unit_slot(uint32_t buf, int row, int q) {
+  return buf + row * (kUnitCols * 2) + ((q ^ ((row >> kSwzShift) & (kSlots - 1))) << 4);
+}
+__device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[16]) {
+  tmem_ld_32x32b_x16(taddr, r);
+}
+__device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld_32x32b_x32(taddr, r);
 }
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
@@ -144,29 +170,29 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
   return v;
 }
 
-// 32 rows (row0 .. row0+31, thread `lane` owns row0+lane) x 32 columns of a
-// bf16 output with full columns.  Residual reads and output writes move
-// through `buf` so that global accesses are row-contiguous.
-template <bool S8>
-__device__ __forceinline__ void epi_chunk_bf16(const EpiParams& p, int row0, int lane, int M,
-                                               int col0, const uint32_t (&r)[32], const float* sb,
-                                               const float* ss, float as, uint32_t buf) {
-  const bool resid = p.epi == JB_EPI_RESIDUAL;
-  uint4 rres[4];
-  if (resid) {
+// Residual rows of one unit in the coalesced pattern (lane l holds row
+// row0 + kRowsPerIns*i + l/kSlots, 16-byte slot l%kSlots); rows >= M read
+// as zero.
+__device__ __forceinline__ void load_resid_unit(const EpiParams& p, int row0, int lane, int M,
+                                                int col0, uint4 (&rres)[kSlots]) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = row0 + i * 8 + (lane >> 2);
-      rres[i] = make_uint4(0, 0, 0, 0);
-      if (rr < M)
-        rres[i] = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) +
-                                                        static_cast<size_t>(rr) * p.ldr + col0 +
-                                                        (lane & 3) * 8));
-    }
+  for (int i = 0; i < kSlots; ++i) {
+    const int rr = row0 + i * kRowsPerIns + lane / kSlots;
+    rres[i] = make_uint4(0, 0, 0, 0);
+    if (rr < M)
+      rres[i] = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) +
+                                                      static_cast<size_t>(rr) * p.ldr + col0 +
+                                                      (lane % kSlots) * 8));
   }
-  float v[32];
+}
+
+// Accumulator -> f32 value before the activation: int8 dequantisation
+// (per-token x per-channel scale) or the f32 accumulator, plus bias.
+template <bool S8, int W>
+__device__ __forceinline__ void dequant_bias(const uint32_t (&r)[W], const float* sb,
+                                             const float* ss, float as, float (&v)[W]) {
 #pragma unroll
-  for (int j = 0; j < 32; j += 4) {
+  for (int j = 0; j < W; j += 4) {
     const float4 b = *reinterpret_cast<const float4*>(sb + j);
     if constexpr (S8) {
       const float4 s = *reinterpret_cast<const float4*>(ss + j);
@@ -181,20 +207,39 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiParams& p, int row0, int
       v[j + 3] = __uint_as_float(r[j + 3]) + b.w;
     }
   }
-  if (p.epi == JB_EPI_GELU) {
+}
+template <int W>
+__device__ __forceinline__ void activation(int epi, float (&v)[W]) {
+  if (epi == JB_EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
-  } else if (p.epi == JB_EPI_QUICK_GELU) {
+    for (int j = 0; j < W; ++j) v[j] = gelu_tc(v[j]);
+  } else if (epi == JB_EPI_QUICK_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = quick_gelu_tc(v[j]);
+    for (int j = 0; j < W; ++j) v[j] = quick_gelu_tc(v[j]);
   }
-  if (resid) {
+}
+
+// One unit of a bf16 output whose columns all lie inside N: rows row0 ..
+// row0+31 (thread `lane` owns row0+lane).  The residual (loaded ahead by the
+// caller with load_resid_unit) and the output move through `buf` so that
+// every global access is a whole row segment.
+template <bool S8>
+__device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, int row0, int lane, int M,
+                                              int col0, const uint32_t (&r)[kUnitCols],
+                                              const float* sb, const float* ss, float as,
+                                              uint32_t buf, const uint4 (&rres)[kSlots]) {
+  float v[kUnitCols];
+  dequant_bias<S8, kUnitCols>(r, sb, ss, as, v);
+  activation<kUnitCols>(p.epi, v);
+  if (p.epi == JB_EPI_RESIDUAL) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sts128(chunk_slot(buf, i * 8 + (lane >> 2), lane & 3), rres[i]);
+    for (int i = 0; i < kSlots; ++i)
+      sts128(unit_slot(buf, i * kRowsPerIns + lane / kSlots, lane % kSlots), rres[i]);
     __syncwarp();
+    // Thread `lane` reads, then overwrites below, only row `lane`'s slots.
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 raw = lds128(chunk_slot(buf, lane, q));
+    for (int q = 0; q < kSlots; ++q) {
+      const uint4 raw = lds128(unit_slot(buf, lane, q));
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -203,114 +248,65 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiParams& p, int row0, int
         v[8 * q + 2 * e + 1] += f.y;
       }
     }
-    __syncwarp();
   }
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < kSlots; ++q) {
     uint4 out;
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
     for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
-    sts128(chunk_slot(buf, lane, q), out);
+    sts128(unit_slot(buf, lane, q), out);
   }
   __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int rr = row0 + i * 8 + (lane >> 2);
-    const uint4 o = lds128(chunk_slot(buf, i * 8 + (lane >> 2), lane & 3));
+  for (int i = 0; i < kSlots; ++i) {
+    const int rr = row0 + i * kRowsPerIns + lane / kSlots;
+    const uint4 o = lds128(unit_slot(buf, i * kRowsPerIns + lane / kSlots, lane % kSlots));
     if (rr < M)
       *reinterpret_cast<uint4*>(static_cast<bf16*>(p.C) + static_cast<size_t>(rr) * p.ldc + col0 +
-                                (lane & 3) * 8) = o;
+                                (lane % kSlots) * 8) = o;
   }
-  __syncwarp();
+  __syncwarp();  // the buffer is rewritten by the next unit
 }
 
-// 32 accumulator columns of one row -> stored outputs.  sb / ss are the
-// tile's staged bias and weight scales for these columns (zero past N).
+// One row's kUnitCols accumulator columns -> stored outputs, for every case
+// the coalesced bf16 unit does not take: s32 (raw accumulator) and f32
+// outputs, and bf16 units that cross N.  sb / ss are the tile's staged bias
+// and weight scales for these columns (zero past N).
 template <bool S8>
-__device__ __forceinline__ void epi_chunk(const EpiParams& p, int row, int col0,
-                                          const uint32_t (&r)[32], const float* sb,
-                                          const float* ss, float as) {
-  const int ncols = min(32, p.N - col0);
+__device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
+                                         const uint32_t (&r)[kUnitCols], const float* sb,
+                                         const float* ss, float as) {
+  constexpr int W = kUnitCols;
+  const int ncols = min(W, p.N - col0);
+  const bool full = ncols == W;
   const size_t off = static_cast<size_t>(row) * p.ldc + col0;
   if (p.c_dtype == JB_DT_S32) {
     int* c = static_cast<int*>(p.C) + off;
-    if (ncols == 32) {
+    if (full) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4)
+      for (int j = 0; j < W; j += 4)
         *reinterpret_cast<int4*>(c + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < W; ++j)
         if (j < ncols) c[j] = static_cast<int>(r[j]);
     }
     return;
   }
-  const bool full = ncols == 32;
+  float v[W];
+  dequant_bias<S8, W>(r, sb, ss, as, v);
+  activation<W>(p.epi, v);
   const size_t roff = static_cast<size_t>(row) * p.ldr + col0;
-  const bool res_bf16 = p.epi == JB_EPI_RESIDUAL && p.c_dtype == JB_DT_BF16 && full;
-  uint4 res[4];
-  if (res_bf16) {  // issue the residual loads before the arithmetic
-    const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const bf16*>(p.resid) + roff);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) res[e] = __ldg(rp + e);
-  }
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) {
-    const float4 b = *reinterpret_cast<const float4*>(sb + j);
-    if constexpr (S8) {
-      const float4 s = *reinterpret_cast<const float4*>(ss + j);
-      v[j + 0] = fmaf(__int2float_rn(static_cast<int>(r[j + 0])), as * s.x, b.x);
-      v[j + 1] = fmaf(__int2float_rn(static_cast<int>(r[j + 1])), as * s.y, b.y);
-      v[j + 2] = fmaf(__int2float_rn(static_cast<int>(r[j + 2])), as * s.z, b.z);
-      v[j + 3] = fmaf(__int2float_rn(static_cast<int>(r[j + 3])), as * s.w, b.w);
-    } else {
-      v[j + 0] = __uint_as_float(r[j + 0]) + b.x;
-      v[j + 1] = __uint_as_float(r[j + 1]) + b.y;
-      v[j + 2] = __uint_as_float(r[j + 2]) + b.z;
-      v[j + 3] = __uint_as_float(r[j + 3]) + b.w;
-    }
-  }
-  if (p.epi == JB_EPI_GELU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tc(v[j]);
-  } else if (p.epi == JB_EPI_QUICK_GELU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = quick_gelu_tc(v[j]);
-  }
   if (p.c_dtype == JB_DT_BF16) {
     bf16* c = static_cast<bf16*>(p.C) + off;
-    if (full) {
-      if (res_bf16) {
+    const bf16* rs = static_cast<const bf16*>(p.resid) + roff;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&res[e]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(h[q]);
-            v[8 * e + 2 * q] += f.x;
-            v[8 * e + 2 * q + 1] += f.y;
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 out;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
-        *reinterpret_cast<uint4*>(c + j) = out;
-      }
-    } else {
-      const bf16* rs = static_cast<const bf16*>(p.resid) + roff;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (j < ncols) {
-          float x = v[j];
-          if (p.epi == JB_EPI_RESIDUAL) x += __bfloat162float(rs[j]);
-          c[j] = __float2bfloat16_rn(x);
-        }
+    for (int j = 0; j < W; ++j) {
+      if (j < ncols) {
+        float x = v[j];
+        if (p.epi == JB_EPI_RESIDUAL) x += __bfloat162float(rs[j]);
+        c[j] = __float2bfloat16_rn(x);
       }
     }
   } else {  // f32 output
@@ -318,7 +314,7 @@ __device__ __forceinline__ void epi_chunk(const EpiParams& p, int row, int col0,
     const float* rs = static_cast<const float*>(p.resid) + roff;
     if (full) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
+      for (int j = 0; j < W; j += 4) {
         float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         if (p.epi == JB_EPI_RESIDUAL) {
           const float4 q = *reinterpret_cast<const float4*>(rs + j);
@@ -328,7 +324,7 @@ __device__ __forceinline__ void epi_chunk(const EpiParams& p, int row, int col0,
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < W; ++j)
         if (j < ncols) c[j] = v[j] + (p.epi == JB_EPI_RESIDUAL ? rs[j] : 0.f);
     }
   }
@@ -442,52 +438,90 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..9.  Warp w may read TMEM lanes 32*(w%4)..+31; the two
-    // warps of a lane quarter split the tile's columns in halves.
+    // Epilogue warps 2..(1 + kEpiWarps).  Warp w may read TMEM lanes
+    // 32*(w%4)..+31; the kEpiWarps/4 warps of a lane quarter take an equal
+    // share of the tile's columns each.
     const int quarter = warp & 3;
     const int etid = threadIdx.x - 64;
-    const int half = (warp - 2) >> 2;
-    constexpr int kHalfCols = BN / 2;
-    const uint32_t my_chunk = chunks + static_cast<uint32_t>(etid >> 5) * kChunkBytes;
+    const int part = (warp - 2) >> 2;
+    constexpr int kPartCols = BN / (kEpiWarps / 4);
+    const uint32_t my_buf = chunks + static_cast<uint32_t>(etid >> 5) * kUnitBytes;
+    const bool fast_out = p.c_dtype == JB_DT_BF16;
+    const bool res_ahead = fast_out && p.epi == JB_EPI_RESIDUAL;
+    // Per-column parameters of a tile: thread etid < BN owns column etid.
+    auto load_params = [&](int t, float& b, float& sc) {
+      const int col = (t % n_tiles) * BN + etid;
+      const bool in = etid < BN && col < p.N;
+      b = (in && p.bias) ? __ldg(p.bias + col) : 0.f;
+      sc = (S8 && in && p.w_scale) ? __ldg(p.w_scale + col) : 0.f;
+    };
+    auto load_ascale = [&](int t) {
+      const int row = (t / n_tiles) * kBM + quarter * 32 + lane;
+      return (S8 && p.a_scale && row < M) ? __ldg(p.a_scale + row) : 0.f;
+    };
+    auto stage_params = [&](int buf, float b, float sc) {
+      if (etid < BN) {
+        params[buf * 2 * BN + etid] = b;
+        params[buf * 2 * BN + BN + etid] = sc;
+      }
+    };
     int acc = 0;
     uint32_t acc_ph = 0;
+    float as = 0.f;
+    if (blockIdx.x < total && kb_count > 0) {
+      float b, sc;
+      load_params(blockIdx.x, b, sc);
+      stage_params(0, b, sc);  // ordered by the first tile's barrier
+      as = load_ascale(blockIdx.x);
+    }
     for (int t = blockIdx.x; t < total && kb_count > 0; t += gridDim.x) {
       const int mb = t / n_tiles, nb = t % n_tiles;
-      // Stage this tile's per-column parameters (buffer `acc`; its previous
-      // readers finished before the last staging barrier).
-      float* pb = params + acc * 2 * BN;
-      float* ps = pb + BN;
-      for (int i = etid; i < BN; i += kEpiThreads) {
-        const int col = nb * BN + i;
-        const bool in = col < p.N;
-        pb[i] = (in && p.bias) ? __ldg(p.bias + col) : 0.f;
-        ps[i] = (S8 && in && p.w_scale) ? __ldg(p.w_scale + col) : 0.f;
+      const int t_next = t + gridDim.x;
+      // The next tile's parameters are loaded now and staged into the other
+      // buffer after this tile, ordered by the next tile's barrier.
+      float nb_b = 0.f, nb_s = 0.f, as_next = 0.f;
+      if (t_next < total) {
+        load_params(t_next, nb_b, nb_s);
+        as_next = load_ascale(t_next);
       }
-      const int row = mb * kBM + quarter * 32 + lane;
-      const float as = (S8 && p.a_scale && row < M) ? __ldg(p.a_scale + row) : 0.f;
-      // One barrier orders the staging above and makes the accumulator-ready
-      // decision the same for every epilogue warp (so none can be left
-      // waiting at a later barrier after an abort).
+      const float* pb = params + acc * 2 * BN;
+      const float* ps = pb + BN;
+      const int row0 = mb * kBM + quarter * 32;
+      const int c_begin = part * kPartCols, c_end = c_begin + kPartCols;
+      auto fast = [&](int c) { return fast_out && nb * BN + c + kUnitCols <= p.N; };  // warp-uniform
+      uint4 rres[kSlots] = {};
+      if (res_ahead && fast(c_begin)) load_resid_unit(p, row0, lane, M, nb * BN + c_begin, rres);
+      // One barrier orders the staged parameters and makes the
+      // accumulator-ready decision the same for every epilogue warp (so none
+      // can be left waiting at a later barrier after an abort).
       const bool ok = epi_bar_and(mbar_wait(tfull_bar(acc), acc_ph, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = half * kHalfCols; c < (half + 1) * kHalfCols; c += 32) {
+      for (int c = c_begin; c < c_end; c += kUnitCols) {
         const int col0 = nb * BN + c;
         if (col0 >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c, r);
+        uint32_t r[kUnitCols];
+        tmem_ld_unit(tbase + c, r);
+        // the next unit's residual rows load while this unit computes
+        uint4 rnext[kSlots] = {};
+        if (res_ahead && c + kUnitCols < c_end && fast(c + kUnitCols))
+          load_resid_unit(p, row0, lane, M, col0 + kUnitCols, rnext);
         tmem_wait_ld();
-        if (p.c_dtype == JB_DT_BF16 && col0 + 32 <= p.N)  // warp-uniform
-          epi_chunk_bf16<S8>(p, row - lane, lane, M, col0, r, pb + c, ps + c, as, my_chunk);
-        else if (row < M)
-          epi_chunk<S8>(p, row, col0, r, pb + c, ps + c, as);
+        if (fast(c))
+          epi_unit_bf16<S8>(p, row0, lane, M, col0, r, pb + c, ps + c, as, my_buf, rres);
+        else if (row0 + lane < M)
+          epi_unit<S8>(p, row0 + lane, col0, r, pb + c, ps + c, as);
+#pragma unroll
+        for (int i = 0; i < kSlots; ++i) rres[i] = rnext[i];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
+      stage_params(acc ^ 1, nb_b, nb_s);
+      as = as_next;
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1u;
     }
