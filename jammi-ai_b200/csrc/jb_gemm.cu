@@ -20,6 +20,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "jb_common.cuh"
@@ -150,11 +151,10 @@ constexpr int kUnitBytes = 32 * kUnitCols * 2;
 __device__ __forceinline__ uint32_t unit_slot(uint32_t buf, int row, int q) {
   return buf + row * (kUnitCols * 2) + ((q ^ ((row >> kSwzShift) & (kSlots - 1))) << 4);
 }
-__device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[16]) {
-  tmem_ld_32x32b_x16(taddr, r);
-}
-__device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[32]) {
-  tmem_ld_32x32b_x32(taddr, r);
+template <int W>
+__device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 16) tmem_ld_32x32b_x16(taddr, r);
+  else tmem_ld_32x32b_x32(taddr, r);
 }
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
@@ -221,16 +221,21 @@ __device__ __forceinline__ void activation(int epi, float (&v)[W]) {
 
 // One unit of a bf16 output whose columns all lie inside N: rows row0 ..
 // row0+31 (thread `lane` owns row0+lane).  The residual (loaded ahead by the
-// caller with load_resid_unit) and the output move through `buf` so that
-// every global access is a whole row segment.
+// caller with load_resid_unit) moves through `buf` so that its global reads
+// are whole row segments; the output is laid out in `buf` in the tensor
+// map's swizzled box layout and written by one TMA store (rows past the
+// map's extent are not written).
 template <bool S8>
-__device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, int row0, int lane, int M,
-                                              int col0, const uint32_t (&r)[kUnitCols],
+__device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensorMap* tmC, int row0,
+                                              int lane, int col0, const uint32_t (&r)[kUnitCols],
                                               const float* sb, const float* ss, float as,
                                               uint32_t buf, const uint4 (&rres)[kSlots]) {
   float v[kUnitCols];
   dequant_bias<S8, kUnitCols>(r, sb, ss, as, v);
   activation<kUnitCols>(p.epi, v);
+  // the previous unit's store must have read the buffer before it is reused
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
   if (p.epi == JB_EPI_RESIDUAL) {
 #pragma unroll
     for (int i = 0; i < kSlots; ++i)
@@ -257,16 +262,12 @@ __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, int row0, int 
     for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
     sts128(unit_slot(buf, lane, q), out);
   }
+  fence_proxy_async_smem();
   __syncwarp();
-#pragma unroll
-  for (int i = 0; i < kSlots; ++i) {
-    const int rr = row0 + i * kRowsPerIns + lane / kSlots;
-    const uint4 o = lds128(unit_slot(buf, i * kRowsPerIns + lane / kSlots, lane % kSlots));
-    if (rr < M)
-      *reinterpret_cast<uint4*>(static_cast<bf16*>(p.C) + static_cast<size_t>(rr) * p.ldc + col0 +
-                                (lane % kSlots) * 8) = o;
+  if (lane == 0) {
+    tma_store_2d(tmC, buf, col0, row0);
+    bulk_commit();
   }
-  __syncwarp();  // the buffer is rewritten by the next unit
 }
 
 // One row's kUnitCols accumulator columns -> stored outputs, for every case
@@ -333,7 +334,7 @@ __device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
 template <bool S8, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const EpiParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const EpiParams p) {
   using Cfg = TcCfg<BN>;
   constexpr int kElemsPerRow = S8 ? 128 : 64;  // K elements per 128-byte row
   constexpr int kSteps = 4;                    // 32-byte MMA K steps per row
@@ -379,6 +380,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
+    if (p.c_dtype == JB_DT_BF16) prefetch_tensormap(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           load_resid_unit(p, row0, lane, M, col0 + kUnitCols, rnext);
         tmem_wait_ld();
         if (fast(c))
-          epi_unit_bf16<S8>(p, row0, lane, M, col0, r, pb + c, ps + c, as, my_buf, rres);
+          epi_unit_bf16<S8>(p, &tmC, row0, lane, col0, r, pb + c, ps + c, as, my_buf, rres);
         else if (row0 + lane < M)
           epi_unit<S8>(p, row0 + lane, col0, r, pb + c, ps + c, as);
 #pragma unroll
@@ -525,6 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete
   }
 
   tc_fence_before();
@@ -633,11 +636,30 @@ bool make_map(CUtensorMap* map, const void* ptr, bool s8, int rows, int k_elems,
   return r == CUDA_SUCCESS;
 }
 
+// Store map over a bf16 output [rows, cols] with row stride ld elements: one
+// epilogue unit (32 rows x kUnitCols columns) per box, swizzled to match
+// unit_slot (64-byte rows: SWIZZLE_64B; 32-byte rows: SWIZZLE_32B).
+bool make_store_map(CUtensorMap* map, void* ptr, int rows, int cols, int ld) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kUnitCols), 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   kUnitCols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <bool S8, int BN>
 cudaError_t launch_tc(const GemmArgs& g, const EpiParams& p, cudaStream_t s, std::string* why) {
   using Cfg = TcCfg<BN>;
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, g.A, S8, g.M, g.K, kBM) || !make_map(&mb, g.W, S8, g.N, g.K, BN)) {
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));  // unused unless the output is bf16
+  if (!make_map(&ma, g.A, S8, g.M, g.K, kBM) || !make_map(&mb, g.W, S8, g.N, g.K, BN) ||
+      (p.c_dtype == JB_DT_BF16 && !make_store_map(&mc, g.C, g.M, g.N, p.ldc))) {
     if (why) *why = "cuTensorMapEncodeTiled failed (pointer alignment or shape)";
     return cudaErrorInvalidValue;
   }
@@ -649,7 +671,7 @@ cudaError_t launch_tc(const GemmArgs& g, const EpiParams& p, cudaStream_t s, std
   const int m_tiles = (g.M + kBM - 1) / kBM;
   const int n_tiles = (g.N + BN - 1) / BN;
   const int grid = std::min(num_sms(dev), m_tiles * n_tiles);
-  kern<<<grid, kGemmThreads, Cfg::SMEM, s>>>(ma, mb, p);
+  kern<<<grid, kGemmThreads, Cfg::SMEM, s>>>(ma, mb, mc, p);
   return cudaGetLastError();
 }
 

@@ -18,7 +18,9 @@ template <typename T> struct Vec;
 template <> struct Vec<bf16> {
   static constexpr int N = 8;
   __device__ static void load(const bf16* p, float* v) {
-    uint4 raw = *reinterpret_cast<const uint4*>(p);
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ static void unpack(const uint4& raw, float* v) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -42,6 +44,10 @@ template <> struct Vec<float> {
   __device__ static void load(const float* p, float* v) {
     float4 f = *reinterpret_cast<const float4*>(p);
     v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  }
+  __device__ static void unpack(const uint4& raw, float* v) {
+    v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y);
+    v[2] = __uint_as_float(raw.z); v[3] = __uint_as_float(raw.w);
   }
   __device__ static void store(float* p, const float* v) {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
@@ -173,6 +179,59 @@ __global__ void __launch_bounds__(256) layernorm_kernel(LnArgs a) {
   }
 }
 
+// bf16 rows of up to MAXV x 256 columns, persistent over rows like
+// layernorm_kernel, but each warp loads its next row (and residual row) into
+// registers before it normalises the current one, so the memory latency of
+// one row overlaps the reductions and stores of the other.
+template <int MAXV, bool RES>
+__global__ void __launch_bounds__(256) layernorm_bf16_kernel(LnArgs a) {
+  __shared__ __align__(16) float sg[kLnMaxCols];
+  __shared__ __align__(16) float sb[kLnMaxCols];
+  stage_params(sg, sb, a.gamma, a.beta, a.cols);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = a.drows ? min(*a.drows, a.rows) : a.rows;
+  const int nvec = a.cols / 8;
+  const int stride = gridDim.x * kRowsPerBlock;
+  auto fetch = [&](int row, uint4 (&xr)[MAXV], uint4 (&rr)[MAXV]) {
+    const uint4* x = reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.x) +
+                                                    static_cast<size_t>(row) * a.cols);
+    const uint4* r = RES ? reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.resid) +
+                                                         static_cast<size_t>(row) * a.cols)
+                         : nullptr;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        xr[i] = x[vi];
+        if constexpr (RES) rr[i] = r[vi];
+      }
+    }
+  };
+  uint4 nx[MAXV], nr[MAXV];
+  int row = blockIdx.x * kRowsPerBlock + warp;
+  if (row < R) fetch(row, nx, nr);
+  for (; row < R; row += stride) {
+    float v[MAXV * 8];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + i * 32 < nvec) {
+        Vec<bf16>::unpack(nx[i], v + i * 8);
+        if constexpr (RES) {
+          float t[8];
+          Vec<bf16>::unpack(nr[i], t);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[i * 8 + e] += t[e];
+        }
+      }
+    }
+    if (row + stride < R) fetch(row + stride, nx, nr);
+    ln_finish<bf16, MAXV>(v, nvec, a.cols, lane, sg, sb, a.eps,
+                          static_cast<bf16*>(a.y) + static_cast<size_t>(row) * a.cols,
+                          a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
+                          a.yscale ? a.yscale + row : nullptr);
+  }
+}
+
 // Persistent over (row b, position p) slots; padding slots are skipped.
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
@@ -215,7 +274,10 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
   }
 }
 
-template <typename T>
+// One warp per row.  Rows of up to MAXV 16-byte vectors per lane are held
+// in registers, so each element is read from memory once; MAXV == 0 is the
+// general two-pass form for longer rows.
+template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int8_t* q,
                                                             float* scale, int rows,
                                                             const int* drows, int cols) {
@@ -226,6 +288,42 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   if (row >= R) return;
   const T* xr = x + static_cast<size_t>(row) * cols;
   const int nvec = cols / VN;
+  int8_t* qr = q + static_cast<size_t>(row) * cols;
+  if constexpr (MAXV > 0) {
+    uint4 raw[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) raw[i] = __ldg(reinterpret_cast<const uint4*>(xr + vi * VN));
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + i * 32 < nvec) {
+        float v[VN];
+        Vec<T>::unpack(raw[i], v);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+      }
+    }
+    amax = warp_max(amax);
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        float v[VN];
+        Vec<T>::unpack(raw[i], v);
+#pragma unroll
+        for (int e = 0; e < VN / 4; ++e)
+          reinterpret_cast<char4*>(qr + vi * VN)[e] =
+              make_char4(quant1(v[4 * e], inv), quant1(v[4 * e + 1], inv),
+                         quant1(v[4 * e + 2], inv), quant1(v[4 * e + 3], inv));
+      }
+    }
+    if (lane == 0) scale[row] = amax / 127.0f;
+    return;
+  }
   float amax = 0.f;
   for (int vi = lane; vi < nvec; vi += 32) {
     float v[VN];
@@ -235,7 +333,6 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   }
   amax = warp_max(amax);
   const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-  int8_t* qr = q + static_cast<size_t>(row) * cols;
   for (int vi = lane; vi < nvec; vi += 32) {
     float v[VN];
     Vec<T>::load(xr + vi * VN, v);
@@ -501,11 +598,20 @@ inline unsigned blocks_for(size_t n, unsigned per) { return static_cast<unsigned
 
 }  // namespace
 
-// Persistent row kernels: at most 4 resident 256-thread blocks per SM.
+// Persistent row kernels run one wave of 256-thread blocks: as many per SM
+// as the kernel's registers and shared memory let reside (asked of the
+// occupancy calculator once per kernel), so no block waits for a second wave.
+template <auto Kern>
 unsigned persistent_grid(size_t rows) {
+  static const int per_sm = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kern, 256, 0) != cudaSuccess || n < 1)
+      n = 1;
+    return n;
+  }();
   int dev = 0;
   cudaGetDevice(&dev);
-  const unsigned cap = static_cast<unsigned>(num_sms(dev)) * 4u;
+  const unsigned cap = static_cast<unsigned>(num_sms(dev)) * static_cast<unsigned>(per_sm);
   const unsigned need = blocks_for(rows, kRowsPerBlock);
   return need < cap ? need : cap;
 }
@@ -513,13 +619,26 @@ unsigned persistent_grid(size_t rows) {
 cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
   if (a.rows == 0) return cudaSuccess;
   if (a.cols > kLnMaxCols) return cudaErrorInvalidValue;
-  const unsigned grid = persistent_grid(a.rows);
   if (a.dtype == JB_DT_BF16) {
     if (a.cols % 8 || a.cols > 1024) return cudaErrorInvalidValue;
-    layernorm_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
+    if (a.cols <= 768) {
+      if (a.resid)
+        layernorm_bf16_kernel<3, true>
+            <<<persistent_grid<layernorm_bf16_kernel<3, true>>(a.rows), 256, 0, s>>>(a);
+      else
+        layernorm_bf16_kernel<3, false>
+            <<<persistent_grid<layernorm_bf16_kernel<3, false>>(a.rows), 256, 0, s>>>(a);
+    } else {
+      if (a.resid)
+        layernorm_bf16_kernel<4, true>
+            <<<persistent_grid<layernorm_bf16_kernel<4, true>>(a.rows), 256, 0, s>>>(a);
+      else
+        layernorm_bf16_kernel<4, false>
+            <<<persistent_grid<layernorm_bf16_kernel<4, false>>(a.rows), 256, 0, s>>>(a);
+    }
   } else {
     if (a.cols % 4 || a.cols > 1024) return cudaErrorInvalidValue;
-    layernorm_kernel<float, 8><<<grid, 256, 0, s>>>(a);
+    layernorm_kernel<float, 8><<<persistent_grid<layernorm_kernel<float, 8>>(a.rows), 256, 0, s>>>(a);
   }
   return cudaGetLastError();
 }
@@ -527,13 +646,12 @@ cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s) {
   const size_t n = static_cast<size_t>(a.batch) * a.max_seq;
   if (n == 0) return cudaSuccess;
-  const unsigned grid = persistent_grid(n);
   if (a.dtype == JB_DT_BF16) {
     if (a.H % 8 || a.H > 1024) return cudaErrorInvalidValue;
-    embed_ln_kernel<bf16, 4><<<grid, 256, 0, s>>>(a);
+    embed_ln_kernel<bf16, 4><<<persistent_grid<embed_ln_kernel<bf16, 4>>(n), 256, 0, s>>>(a);
   } else {
     if (a.H % 4 || a.H > 1024) return cudaErrorInvalidValue;
-    embed_ln_kernel<float, 8><<<grid, 256, 0, s>>>(a);
+    embed_ln_kernel<float, 8><<<persistent_grid<embed_ln_kernel<float, 8>>(n), 256, 0, s>>>(a);
   }
   return cudaGetLastError();
 }
@@ -544,12 +662,22 @@ cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* sca
   const unsigned grid = blocks_for(rows, kRowsPerBlock);
   if (dtype == JB_DT_BF16) {
     if (cols % 8) return cudaErrorInvalidValue;
-    quantize_rows_kernel<bf16><<<grid, 256, 0, s>>>(static_cast<const bf16*>(x), q, scale, rows,
-                                                    drows, cols);
+    const bf16* xb = static_cast<const bf16*>(x);
+    const int per_lane = (cols / 8 + 31) / 32;
+    if (per_lane <= 4)
+      quantize_rows_kernel<bf16, 4><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+    else if (per_lane <= 8)
+      quantize_rows_kernel<bf16, 8><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+    else if (per_lane <= 12)
+      quantize_rows_kernel<bf16, 12><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+    else if (per_lane <= 16)
+      quantize_rows_kernel<bf16, 16><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+    else
+      quantize_rows_kernel<bf16, 0><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
   } else {
     if (cols % 4) return cudaErrorInvalidValue;
-    quantize_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q, scale, rows,
-                                                     drows, cols);
+    quantize_rows_kernel<float, 0><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q, scale,
+                                                        rows, drows, cols);
   }
   return cudaGetLastError();
 }
