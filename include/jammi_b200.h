@@ -182,6 +182,12 @@ jb_status jb_op_linear_s8(const int8_t* Aq, const float* a_scale, const int8_t* 
  * scale = amax/127, q = clamp(rint(x * (127/amax)), -127, 127). */
 jb_status jb_op_quantize_rows(const void* x, int x_dtype, int8_t* q, float* scale,
                               int rows, int cols, void* stream);
+/* jb_op_quantize_rows of act(x): activation JB_EPI_GELU quantises
+ * gelu_erf(x) rounded to x's dtype (the int8 FFN input: BertIntermediate,
+ * bert.rs:187-190, followed by the per-token quantiser); JB_EPI_NONE is
+ * jb_op_quantize_rows.  No reference counterpart (int8 format). */
+jb_status jb_op_quantize_rows_act(const void* x, int x_dtype, int activation, int8_t* q,
+                                  float* scale, int rows, int cols, void* stream);
 /* y = LayerNorm(x (+ residual)) over the last dim, in place allowed
  * (crates/jammi-encoders/src/layer_norm.rs:55-84).  x/y dtype F32 or BF16. */
 jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamma,

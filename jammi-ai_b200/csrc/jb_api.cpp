@@ -308,6 +308,20 @@ jb_status jb_op_quantize_rows(const void* x, int x_dtype, int8_t* q, float* scal
   });
 }
 
+jb_status jb_op_quantize_rows_act(const void* x, int x_dtype, int activation, int8_t* q,
+                                  float* scale, int rows, int cols, void* stream) {
+  return guarded([&] {
+    if (!x || !q || !scale || rows < 0 || cols <= 0)
+      jb::fail(JB_ERR_INVALID, "jb_op_quantize_rows_act: bad argument");
+    if (x_dtype != JB_DT_F32 && x_dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "x must be f32 or bf16");
+    if (activation != JB_EPI_NONE && activation != JB_EPI_GELU)
+      jb::fail(JB_ERR_INVALID, "activation must be JB_EPI_NONE or JB_EPI_GELU");
+    jb::check_cuda(jb::launch_quantize_rows(x, x_dtype, q, scale, rows, nullptr, cols,
+                                            as_stream(stream), activation),
+                   "jb_op_quantize_rows_act");
+  });
+}
+
 jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamma,
                           const float* beta, void* y, int dtype, int rows, int cols, float eps,
                           void* stream) {

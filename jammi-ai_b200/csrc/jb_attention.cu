@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
         ldsm_x4(swz(sQ, r, c), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
       }
     }
+    if (q0 + warp * 16 < n) {  // warps past the row's end only load
     // S = Q K^T for this warp's 16 queries x 64 keys
     float s[8][4];
 #pragma unroll
@@ -147,18 +148,20 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
         mma16816(s[2 * np + 1], qf[ks], b2, b3);
       }
     }
-    // mask keys beyond the row's length, then the online softmax update
+    // Keys past the row's end (last block only) score -inf; then the online
+    // softmax in log2 units, p = 2^(s * scale_log2 - m), the scale folded
+    // into one fma per score.
     const int kbase = kb * kFaKeys;
+    if (kbase + kFaKeys > n) {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) >= n) s[nt][e] = -INFINITY;
+    }
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kbase + nt * 8 + 2 * (lane & 3) + (e & 1);
-        float v = s[nt][e] * scale_log2;
-        if (key >= n) v = -INFINITY;
-        s[nt][e] = v;
-      }
       mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
       mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
     }
@@ -166,17 +169,17 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);
+    const float mn0 = fmaxf(m0, mx0 * scale_log2), mn1 = fmaxf(m1, mx1 * scale_log2);
+    const float a0 = ex2_approx(m0 - mn0), a1 = ex2_approx(m1 - mn1);
     m0 = mn0;
     m1 = mn1;
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = exp2f(s[nt][0] - mn0);
-      s[nt][1] = exp2f(s[nt][1] - mn0);
-      s[nt][2] = exp2f(s[nt][2] - mn1);
-      s[nt][3] = exp2f(s[nt][3] - mn1);
+      s[nt][0] = ex2_approx(fmaf(s[nt][0], scale_log2, -mn0));
+      s[nt][1] = ex2_approx(fmaf(s[nt][1], scale_log2, -mn0));
+      s[nt][2] = ex2_approx(fmaf(s[nt][2], scale_log2, -mn1));
+      s[nt][3] = ex2_approx(fmaf(s[nt][3], scale_log2, -mn1));
       rs0 += s[nt][0] + s[nt][1];
       rs1 += s[nt][2] + s[nt][3];
     }
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
         mma16816(o[2 * dp], a, b0, b1);
         mma16816(o[2 * dp + 1], a, b2, b3);
       }
+    }
     }
     __syncthreads();
   }

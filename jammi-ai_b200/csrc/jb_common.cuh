@@ -44,6 +44,47 @@ __device__ __forceinline__ float quick_gelu(float x) {
   return x / (1.0f + expf(-1.702f * x));
 }
 
+// Fast activations for the GEMM epilogue and the activation-fused row
+// quantiser, on the hardware 2^x and 1/x approximations.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU(x) = x * Phi(x) with erf from Abramowitz & Stegun, Handbook of
+// Mathematical Functions (1964), eq. 7.1.28: for z >= 0
+//   erf(z) = 1 - (1 + a1 z + a2 z^2 + ... + a6 z^6)^-16,  |error| <= 3e-7,
+// so with z = |x|/sqrt2 and r = (1 + ...)^-16 = 1 - erf(z):
+//   Phi(x) = 1 - r/2 (x >= 0),  r/2 (x < 0).
+// The coefficients below are a_k / sqrt2^k (the polynomial is evaluated at
+// |x|); one reciprocal per value, and r -> 0 cleanly when the power
+// overflows to +inf for large |x|.  The error stays below 1e-6 * max(1, |x|)
+// -- far under the bf16 rounding of the stored result.
+__device__ __forceinline__ float gelu_tc(float x) {
+  const float ax = fabsf(x);
+  float p = fmaf(ax, 0.0000430638f * 0.125f, 0.0002765672f * 0.17677669529663688f);
+  p = fmaf(ax, p, 0.0001520143f * 0.25f);
+  p = fmaf(ax, p, 0.0092705272f * 0.35355339059327376f);
+  p = fmaf(ax, p, 0.0422820123f * 0.5f);
+  p = fmaf(ax, p, 0.0705230784f * 0.70710678118654752f);
+  p = fmaf(ax, p, 1.0f);
+  p *= p;  // ^2
+  p *= p;  // ^4
+  p *= p;  // ^8
+  p *= p;  // ^16
+  const float h = 0.5f * rcp_approx(p);  // (1 - erf(|x|/sqrt2)) / 2
+  return x * (x >= 0.f ? 1.0f - h : h);
+}
+// x * sigmoid(1.702 x) = x / (1 + 2^(-1.702 log2(e) x))
+__device__ __forceinline__ float quick_gelu_tc(float x) {
+  return x * rcp_approx(1.0f + ex2_approx(-2.45546696f * x));
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

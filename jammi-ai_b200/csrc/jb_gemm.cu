@@ -84,42 +84,6 @@ __device__ __forceinline__ float apply_epi(float v, int epi) {
   return v;
 }
 
-// Tensor-core epilogue activations.  erf follows Abramowitz & Stegun,
-// Handbook of Mathematical Functions (1964), eq. 7.1.26:
-// erf(x) = 1 - (a1 t + ... + a5 t^5) exp(-x^2), t = 1/(1 + p|x|),
-// |error| <= 1.5e-7 -- far below the bf16 rounding of the stored result --
-// evaluated with the hardware 2^x and 1/x approximations so the GELU
-// epilogue keeps pace with the int8 main loop.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-// GELU(x) = x * Phi(x), Phi(x) = 1 - erfc(|x|/sqrt2)/2 for x >= 0 (erfc/2 for
-// x < 0), with erfc(z) = (a1 t + ... + a5 t^5) exp(-z^2), t = 1/(1 + p z):
-// the coefficients are folded with the 1/sqrt2 and 1/2 factors, and
-// exp(-x^2/2) = 2^(-x^2 log2(e)/2).
-__device__ __forceinline__ float gelu_tc(float x) {
-  const float ax = fabsf(x);
-  const float t = rcp_approx(fmaf(0.3275911f * 0.70710678118654752f, ax, 1.0f));
-  float poly = fmaf(t, 0.5f * 1.061405429f, 0.5f * -1.453152027f);
-  poly = fmaf(t, poly, 0.5f * 1.421413741f);
-  poly = fmaf(t, poly, 0.5f * -0.284496736f);
-  poly = fmaf(t, poly, 0.5f * 0.254829592f);
-  poly *= t;
-  const float h = poly * ex2_approx(x * x * -0.72134752044448170f);  // erfc(|x|/sqrt2) / 2
-  return x * (x >= 0.f ? 1.0f - h : h);
-}
-// x * sigmoid(1.702 x) = x / (1 + 2^(-1.702 log2(e) x))
-__device__ __forceinline__ float quick_gelu_tc(float x) {
-  return x * rcp_approx(1.0f + ex2_approx(-2.45546696f * x));
-}
-
 // Named barrier over the epilogue warps that also ANDs a predicate across them.
 __device__ __forceinline__ bool epi_bar_and(bool v) {
   uint32_t r;

@@ -55,7 +55,8 @@ struct LnArgs {
 cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s);
 
 cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
-                                 const int* drows, int cols, cudaStream_t s);
+                                 const int* drows, int cols, cudaStream_t s,
+                                 int activation = JB_EPI_NONE);
 
 // BERT embeddings: word[ids] + type[0] + pos[p] -> LayerNorm, written packed
 // at row cu[b] + p for p < len[b].

@@ -29,13 +29,14 @@ template <> struct Vec<bf16> {
       v[2 * e + 1] = f.y;
     }
   }
-  __device__ static void store(bf16* p, const float* v) {
+  __device__ static uint4 pack(const float* v) {
     uint4 raw;
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
     for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
-    *reinterpret_cast<uint4*>(p) = raw;
+    return raw;
   }
+  __device__ static void store(bf16* p, const float* v) { *reinterpret_cast<uint4*>(p) = pack(v); }
   // value as it will be read back after the store (bf16 rounding)
   __device__ static float rounded(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
@@ -49,6 +50,10 @@ template <> struct Vec<float> {
     v[0] = __uint_as_float(raw.x); v[1] = __uint_as_float(raw.y);
     v[2] = __uint_as_float(raw.z); v[3] = __uint_as_float(raw.w);
   }
+  __device__ static uint4 pack(const float* v) {
+    return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                      __float_as_uint(v[3]));
+  }
   __device__ static void store(float* p, const float* v) {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   }
@@ -56,11 +61,20 @@ template <> struct Vec<float> {
 };
 
 // Per-token symmetric int8 quantisation of values already rounded to the
-// stored dtype: scale = amax/127, q = clamp(rint(x * (127/amax))).
-__device__ __forceinline__ int8_t quant1(float x, float inv) {
-  int q = __float2int_rn(x * inv);
-  q = max(-127, min(127, q));
-  return static_cast<int8_t>(q);
+// stored dtype: scale = amax/127, q = clamp(rint(x * (127/amax)), -127, 127).
+// With |x| <= amax the product is at most 127 (1 + 2^-24), so the clamp never
+// acts; rint of |y| < 2^22 is the low bits of y + 1.5 * 2^23 (the addition
+// rounds to the nearest integer, ties to even), whose low byte is the int8
+// code.  quant4 packs four codes with byte permutes: no conversion
+// instructions.
+__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float inv) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  // __fmul_rn / __fadd_rn: two roundings, never contracted into one fma
+  const uint32_t qa = __float_as_uint(__fadd_rn(__fmul_rn(a, inv), kMagic));
+  const uint32_t qb = __float_as_uint(__fadd_rn(__fmul_rn(b, inv), kMagic));
+  const uint32_t qc = __float_as_uint(__fadd_rn(__fmul_rn(c, inv), kMagic));
+  const uint32_t qd = __float_as_uint(__fadd_rn(__fmul_rn(d, inv), kMagic));
+  return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
 }
 
 // Normalises the row held in v[] (nvec vectors of Vec<T>::N per lane slot),
@@ -120,13 +134,11 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
     for (int i = 0; i < MAXV; ++i) {
       const int vi = lane + i * 32;
       if (vi < nvec) {
-        char4 q[VN / 4];
 #pragma unroll
         for (int e = 0; e < VN / 4; ++e)
-          q[e] = make_char4(quant1(v[i * VN + 4 * e], inv), quant1(v[i * VN + 4 * e + 1], inv),
-                            quant1(v[i * VN + 4 * e + 2], inv), quant1(v[i * VN + 4 * e + 3], inv));
-#pragma unroll
-        for (int e = 0; e < VN / 4; ++e) reinterpret_cast<char4*>(qrow + vi * VN)[e] = q[e];
+          reinterpret_cast<uint32_t*>(qrow + vi * VN)[e] =
+              quant4(v[i * VN + 4 * e], v[i * VN + 4 * e + 1], v[i * VN + 4 * e + 2],
+                     v[i * VN + 4 * e + 3], inv);
       }
     }
     if (lane == 0) *scale_out = amax / 127.0f;
@@ -274,10 +286,19 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
   }
 }
 
-// One warp per row.  Rows of up to MAXV 16-byte vectors per lane are held
-// in registers, so each element is read from memory once; MAXV == 0 is the
-// general two-pass form for longer rows.
-template <typename T, int MAXV>
+// The value quantised for input x: x itself, or (ACT == JB_EPI_GELU) the
+// GELU of x rounded to T -- what a stored activation tensor of type T holds.
+template <typename T, int ACT>
+__device__ __forceinline__ float pre_quant(float x) {
+  if constexpr (ACT == JB_EPI_GELU) return Vec<T>::rounded(gelu_tc(x));
+  else return x;
+}
+
+// One warp per row, optionally applying an activation first.  Rows of up to
+// MAXV 16-byte vectors per lane are held in registers (after the
+// activation), so each element is read from memory and activated once;
+// MAXV == 0 is the general two-pass form for longer rows.
+template <typename T, int MAXV, int ACT>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int8_t* q,
                                                             float* scale, int rows,
                                                             const int* drows, int cols) {
@@ -303,7 +324,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
         float v[VN];
         Vec<T>::unpack(raw[i], v);
 #pragma unroll
-        for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        for (int e = 0; e < VN; ++e) {
+          v[e] = pre_quant<T, ACT>(v[e]);
+          amax = fmaxf(amax, fabsf(v[e]));
+        }
+        if constexpr (ACT != JB_EPI_NONE) raw[i] = Vec<T>::pack(v);  // exact: v is T-rounded
       }
     }
     amax = warp_max(amax);
@@ -316,9 +341,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
         Vec<T>::unpack(raw[i], v);
 #pragma unroll
         for (int e = 0; e < VN / 4; ++e)
-          reinterpret_cast<char4*>(qr + vi * VN)[e] =
-              make_char4(quant1(v[4 * e], inv), quant1(v[4 * e + 1], inv),
-                         quant1(v[4 * e + 2], inv), quant1(v[4 * e + 3], inv));
+          reinterpret_cast<uint32_t*>(qr + vi * VN)[e] =
+              quant4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3], inv);
       }
     }
     if (lane == 0) scale[row] = amax / 127.0f;
@@ -329,7 +353,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
     float v[VN];
     Vec<T>::load(xr + vi * VN, v);
 #pragma unroll
-    for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(pre_quant<T, ACT>(v[e])));
   }
   amax = warp_max(amax);
   const float inv = amax > 0.f ? 127.0f / amax : 0.f;
@@ -337,10 +361,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
     float v[VN];
     Vec<T>::load(xr + vi * VN, v);
 #pragma unroll
+    for (int e = 0; e < VN; ++e) v[e] = pre_quant<T, ACT>(v[e]);
+#pragma unroll
     for (int e = 0; e < VN / 4; ++e)
-      reinterpret_cast<char4*>(qr + vi * VN)[e] =
-          make_char4(quant1(v[4 * e], inv), quant1(v[4 * e + 1], inv), quant1(v[4 * e + 2], inv),
-                     quant1(v[4 * e + 3], inv));
+      reinterpret_cast<uint32_t*>(qr + vi * VN)[e] =
+          quant4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3], inv);
   }
   if (lane == 0) scale[row] = amax / 127.0f;
 }
@@ -656,30 +681,41 @@ cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
-                                 const int* drows, int cols, cudaStream_t s) {
-  if (rows == 0) return cudaSuccess;
+namespace {
+template <int ACT>
+cudaError_t launch_quantize_act(const void* x, int dtype, int8_t* q, float* scale, int rows,
+                                const int* drows, int cols, cudaStream_t s) {
   const unsigned grid = blocks_for(rows, kRowsPerBlock);
   if (dtype == JB_DT_BF16) {
     if (cols % 8) return cudaErrorInvalidValue;
     const bf16* xb = static_cast<const bf16*>(x);
     const int per_lane = (cols / 8 + 31) / 32;
     if (per_lane <= 4)
-      quantize_rows_kernel<bf16, 4><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+      quantize_rows_kernel<bf16, 4, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
     else if (per_lane <= 8)
-      quantize_rows_kernel<bf16, 8><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+      quantize_rows_kernel<bf16, 8, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
     else if (per_lane <= 12)
-      quantize_rows_kernel<bf16, 12><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+      quantize_rows_kernel<bf16, 12, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
     else if (per_lane <= 16)
-      quantize_rows_kernel<bf16, 16><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+      quantize_rows_kernel<bf16, 16, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
     else
-      quantize_rows_kernel<bf16, 0><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+      quantize_rows_kernel<bf16, 0, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
   } else {
     if (cols % 4) return cudaErrorInvalidValue;
-    quantize_rows_kernel<float, 0><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q, scale,
-                                                        rows, drows, cols);
+    quantize_rows_kernel<float, 0, ACT><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q,
+                                                             scale, rows, drows, cols);
   }
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
+                                 const int* drows, int cols, cudaStream_t s, int activation) {
+  if (rows == 0) return cudaSuccess;
+  if (activation == JB_EPI_GELU)
+    return launch_quantize_act<JB_EPI_GELU>(x, dtype, q, scale, rows, drows, cols, s);
+  if (activation != JB_EPI_NONE) return cudaErrorInvalidValue;
+  return launch_quantize_act<JB_EPI_NONE>(x, dtype, q, scale, rows, drows, cols, s);
 }
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,

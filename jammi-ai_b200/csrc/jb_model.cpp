@@ -727,10 +727,15 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
     run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
     run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
            Mcap, ws.total, H, m->eps, s);
-    // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1))
-    run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act, JB_EPI_GELU, nullptr, s);
+    // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1)).  int8: the
+    // GELU runs in the quantiser that FFN2's input needs anyway, on the bf16
+    // dense output (the reference's bf16 order: Linear -> bf16 -> gelu).
+    run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act,
+               q8 ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
     if (q8)
-      PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s), "quantize");
+      PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s,
+                                         JB_EPI_GELU),
+                    "quantize");
     // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
     run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);
     run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,

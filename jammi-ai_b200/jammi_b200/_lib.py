@@ -68,6 +68,7 @@ _SIGS = [
     ("jb_op_linear", _I, [_P, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_linear_s8", _I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_quantize_rows", _I, [_P, _I, _P, _P, _I, _I, _P]),
+    ("jb_op_quantize_rows_act", _I, [_P, _I, _I, _P, _P, _I, _I, _P]),
     ("jb_op_layernorm", _I, [_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
     ("jb_op_attention", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_pool_normalize", _I, [_P, _I, _P, _P, _I, _I, _I, _P]),

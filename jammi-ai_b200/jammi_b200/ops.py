@@ -59,12 +59,18 @@ def linear_s8(aq: torch.Tensor, a_scale, wq: torch.Tensor, w_scale, bias=None, r
     return c
 
 
-def quantize_rows(x: torch.Tensor):
+def quantize_rows(x: torch.Tensor, activation: int = L.EPI_NONE):
+    """Per-row int8 of x, or of activation(x) rounded to x's dtype
+    (activation EPI_GELU): returns (q int8 [R, C], scale f32 [R])."""
     _contig(x)
     R, C = x.shape
     q = torch.empty((R, C), dtype=torch.int8, device=x.device)
     s = torch.empty((R,), dtype=torch.float32, device=x.device)
-    check(lib().jb_op_quantize_rows(_p(x), _DT[x.dtype], _p(q), _p(s), R, C, _s(x)))
+    if activation == L.EPI_NONE:
+        check(lib().jb_op_quantize_rows(_p(x), _DT[x.dtype], _p(q), _p(s), R, C, _s(x)))
+    else:
+        check(lib().jb_op_quantize_rows_act(_p(x), _DT[x.dtype], int(activation), _p(q), _p(s), R, C,
+                                            _s(x)))
     return q, s
 
 
