@@ -130,86 +130,86 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
       }
     }
     if (q0 + warp * 16 < n) {  // warps past the row's end only load
-    // S = Q K^T for this warp's 16 queries x 64 keys
-    float s[8][4];
+      // S = Q K^T for this warp's 16 queries x 64 keys
+      float s[8][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
+        for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+      for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t b0, b1, b2, b3;
-        const int r = np * 16 + (lane & 7) + 8 * (lane >> 4);
-        const int c = 2 * ks + ((lane >> 3) & 1);
-        ldsm_x4(swz(sK, r, c), b0, b1, b2, b3);
-        mma16816(s[2 * np], qf[ks], b0, b1);
-        mma16816(s[2 * np + 1], qf[ks], b2, b3);
+        for (int np = 0; np < 4; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int r = np * 16 + (lane & 7) + 8 * (lane >> 4);
+          const int c = 2 * ks + ((lane >> 3) & 1);
+          ldsm_x4(swz(sK, r, c), b0, b1, b2, b3);
+          mma16816(s[2 * np], qf[ks], b0, b1);
+          mma16816(s[2 * np + 1], qf[ks], b2, b3);
+        }
       }
-    }
-    // Keys past the row's end (last block only) score -inf; then the online
-    // softmax in log2 units, p = 2^(s * scale_log2 - m), the scale folded
-    // into one fma per score.
-    const int kbase = kb * kFaKeys;
-    if (kbase + kFaKeys > n) {
+      // Keys past the row's end (last block only) score -inf; then the online
+      // softmax in log2 units, p = 2^(s * scale_log2 - m), the scale folded
+      // into one fma per score.
+      const int kbase = kb * kFaKeys;
+      if (kbase + kFaKeys > n) {
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+        for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) >= n) s[nt][e] = -INFINITY;
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0 * scale_log2), mn1 = fmaxf(m1, mx1 * scale_log2);
-    const float a0 = ex2_approx(m0 - mn0), a1 = ex2_approx(m1 - mn1);
-    m0 = mn0;
-    m1 = mn1;
-    float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = ex2_approx(fmaf(s[nt][0], scale_log2, -mn0));
-      s[nt][1] = ex2_approx(fmaf(s[nt][1], scale_log2, -mn0));
-      s[nt][2] = ex2_approx(fmaf(s[nt][2], scale_log2, -mn1));
-      s[nt][3] = ex2_approx(fmaf(s[nt][3], scale_log2, -mn1));
-      rs0 += s[nt][0] + s[nt][1];
-      rs1 += s[nt][2] + s[nt][3];
-    }
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-#pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      o[dt][0] *= a0;
-      o[dt][1] *= a0;
-      o[dt][2] *= a1;
-      o[dt][3] *= a1;
-    }
-    // O += P V
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t a[4];
-      a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int dp = 0; dp < 4; ++dp) {
-        uint32_t b0, b1, b2, b3;
-        const int r = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-        const int c = 2 * dp + (lane >> 4);
-        ldsm_x4_t(swz(sV, r, c), b0, b1, b2, b3);
-        mma16816(o[2 * dp], a, b0, b1);
-        mma16816(o[2 * dp + 1], a, b2, b3);
+          for (int e = 0; e < 4; ++e)
+            if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) >= n) s[nt][e] = -INFINITY;
       }
-    }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0 * scale_log2), mn1 = fmaxf(m1, mx1 * scale_log2);
+      const float a0 = ex2_approx(m0 - mn0), a1 = ex2_approx(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] = ex2_approx(fmaf(s[nt][0], scale_log2, -mn0));
+        s[nt][1] = ex2_approx(fmaf(s[nt][1], scale_log2, -mn0));
+        s[nt][2] = ex2_approx(fmaf(s[nt][2], scale_log2, -mn1));
+        s[nt][3] = ex2_approx(fmaf(s[nt][3], scale_log2, -mn1));
+        rs0 += s[nt][0] + s[nt][1];
+        rs1 += s[nt][2] + s[nt][3];
+      }
+      l0 = l0 * a0 + rs0;
+      l1 = l1 * a1 + rs1;
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        o[dt][0] *= a0;
+        o[dt][1] *= a0;
+        o[dt][2] *= a1;
+        o[dt][3] *= a1;
+      }
+      // O += P V
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a[4];
+        a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+        for (int dp = 0; dp < 4; ++dp) {
+          uint32_t b0, b1, b2, b3;
+          const int r = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+          const int c = 2 * dp + (lane >> 4);
+          ldsm_x4_t(swz(sV, r, c), b0, b1, b2, b3);
+          mma16816(o[2 * dp], a, b0, b1);
+          mma16816(o[2 * dp + 1], a, b2, b3);
+        }
+      }
     }
     __syncthreads();
   }
