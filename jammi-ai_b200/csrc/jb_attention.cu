@@ -176,10 +176,12 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        s[nt][0] = ex2_approx(fmaf(s[nt][0], scale_log2, -mn0));
-        s[nt][1] = ex2_approx(fmaf(s[nt][1], scale_log2, -mn0));
-        s[nt][2] = ex2_approx(fmaf(s[nt][2], scale_log2, -mn1));
-        s[nt][3] = ex2_approx(fmaf(s[nt][3], scale_log2, -mn1));
+        const float2 e01 = __ffma2_rn(make_float2(s[nt][0], s[nt][1]), f2(scale_log2), f2(-mn0));
+        const float2 e23 = __ffma2_rn(make_float2(s[nt][2], s[nt][3]), f2(scale_log2), f2(-mn1));
+        s[nt][0] = ex2_approx(e01.x);
+        s[nt][1] = ex2_approx(e01.y);
+        s[nt][2] = ex2_approx(e23.x);
+        s[nt][3] = ex2_approx(e23.y);
         rs0 += s[nt][0] + s[nt][1];
         rs1 += s[nt][2] + s[nt][3];
       }
@@ -187,10 +189,9 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
       l1 = l1 * a1 + rs1;
 #pragma unroll
       for (int dt = 0; dt < 8; ++dt) {
-        o[dt][0] *= a0;
-        o[dt][1] *= a0;
-        o[dt][2] *= a1;
-        o[dt][3] *= a1;
+        const float2 o01 = __fmul2_rn(make_float2(o[dt][0], o[dt][1]), f2(a0));
+        const float2 o23 = __fmul2_rn(make_float2(o[dt][2], o[dt][3]), f2(a1));
+        o[dt][0] = o01.x; o[dt][1] = o01.y; o[dt][2] = o23.x; o[dt][3] = o23.y;
       }
       // O += P V
 #pragma unroll

@@ -80,6 +80,25 @@ __device__ __forceinline__ float gelu_tc(float x) {
   const float h = 0.5f * rcp_approx(p);  // (1 - erf(|x|/sqrt2)) / 2
   return x * (x >= 0.f ? 1.0f - h : h);
 }
+// gelu_tc on a pair, its polynomial and powers as packed f32x2 operations
+// (one instruction per two values; the same roundings as gelu_tc).
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 gelu_tc2(float2 x) {
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  float2 p = __ffma2_rn(ax, f2(0.0000430638f * 0.125f), f2(0.0002765672f * 0.17677669529663688f));
+  p = __ffma2_rn(ax, p, f2(0.0001520143f * 0.25f));
+  p = __ffma2_rn(ax, p, f2(0.0092705272f * 0.35355339059327376f));
+  p = __ffma2_rn(ax, p, f2(0.0422820123f * 0.5f));
+  p = __ffma2_rn(ax, p, f2(0.0705230784f * 0.70710678118654752f));
+  p = __ffma2_rn(ax, p, f2(1.0f));
+  p = __fmul2_rn(p, p);
+  p = __fmul2_rn(p, p);
+  p = __fmul2_rn(p, p);
+  p = __fmul2_rn(p, p);
+  const float2 h = __fmul2_rn(make_float2(rcp_approx(p.x), rcp_approx(p.y)), f2(0.5f));
+  const float2 t = make_float2(x.x >= 0.f ? 1.0f - h.x : h.x, x.y >= 0.f ? 1.0f - h.y : h.y);
+  return __fmul2_rn(x, t);
+}
 // x * sigmoid(1.702 x) = x / (1 + 2^(-1.702 log2(e) x))
 __device__ __forceinline__ float quick_gelu_tc(float x) {
   return x * rcp_approx(1.0f + ex2_approx(-2.45546696f * x));

@@ -158,17 +158,24 @@ __device__ __forceinline__ void dequant_bias(const uint32_t (&r)[W], const float
 #pragma unroll
   for (int j = 0; j < W; j += 4) {
     const float4 b = *reinterpret_cast<const float4*>(sb + j);
+    // packed f32x2 arithmetic: one instruction per two columns
     if constexpr (S8) {
       const float4 s = *reinterpret_cast<const float4*>(ss + j);
-      v[j + 0] = fmaf(__int2float_rn(static_cast<int>(r[j + 0])), as * s.x, b.x);
-      v[j + 1] = fmaf(__int2float_rn(static_cast<int>(r[j + 1])), as * s.y, b.y);
-      v[j + 2] = fmaf(__int2float_rn(static_cast<int>(r[j + 2])), as * s.z, b.z);
-      v[j + 3] = fmaf(__int2float_rn(static_cast<int>(r[j + 3])), as * s.w, b.w);
+      const float2 s01 = __fmul2_rn(f2(as), make_float2(s.x, s.y));
+      const float2 s23 = __fmul2_rn(f2(as), make_float2(s.z, s.w));
+      const float2 v01 = __ffma2_rn(make_float2(__int2float_rn(static_cast<int>(r[j + 0])),
+                                                __int2float_rn(static_cast<int>(r[j + 1]))),
+                                    s01, make_float2(b.x, b.y));
+      const float2 v23 = __ffma2_rn(make_float2(__int2float_rn(static_cast<int>(r[j + 2])),
+                                                __int2float_rn(static_cast<int>(r[j + 3]))),
+                                    s23, make_float2(b.z, b.w));
+      v[j + 0] = v01.x; v[j + 1] = v01.y; v[j + 2] = v23.x; v[j + 3] = v23.y;
     } else {
-      v[j + 0] = __uint_as_float(r[j + 0]) + b.x;
-      v[j + 1] = __uint_as_float(r[j + 1]) + b.y;
-      v[j + 2] = __uint_as_float(r[j + 2]) + b.z;
-      v[j + 3] = __uint_as_float(r[j + 3]) + b.w;
+      const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1])),
+                                    make_float2(b.x, b.y));
+      const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
+                                    make_float2(b.z, b.w));
+      v[j + 0] = v01.x; v[j + 1] = v01.y; v[j + 2] = v23.x; v[j + 3] = v23.y;
     }
   }
 }
@@ -176,7 +183,11 @@ template <int W>
 __device__ __forceinline__ void activation(int epi, float (&v)[W]) {
   if (epi == JB_EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < W; ++j) v[j] = gelu_tc(v[j]);
+    for (int j = 0; j < W; j += 2) {
+      const float2 g = gelu_tc2(make_float2(v[j], v[j + 1]));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
   } else if (epi == JB_EPI_QUICK_GELU) {
 #pragma unroll
     for (int j = 0; j < W; ++j) v[j] = quick_gelu_tc(v[j]);

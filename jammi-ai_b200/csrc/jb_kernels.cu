@@ -70,6 +70,7 @@ template <> struct Vec<float> {
 __device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float inv) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   // __fmul_rn / __fadd_rn: two roundings, never contracted into one fma
+  // (the packed f32x2 forms are not held to that and break bit-exactness)
   const uint32_t qa = __float_as_uint(__fadd_rn(__fmul_rn(a, inv), kMagic));
   const uint32_t qb = __float_as_uint(__fadd_rn(__fmul_rn(b, inv), kMagic));
   const uint32_t qc = __float_as_uint(__fadd_rn(__fmul_rn(c, inv), kMagic));
@@ -323,11 +324,16 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
       if (lane + i * 32 < nvec) {
         float v[VN];
         Vec<T>::unpack(raw[i], v);
+        if constexpr (ACT == JB_EPI_GELU) {
 #pragma unroll
-        for (int e = 0; e < VN; ++e) {
-          v[e] = pre_quant<T, ACT>(v[e]);
-          amax = fmaxf(amax, fabsf(v[e]));
+          for (int e = 0; e < VN; e += 2) {
+            const float2 g = gelu_tc2(make_float2(v[e], v[e + 1]));
+            v[e] = Vec<T>::rounded(g.x);
+            v[e + 1] = Vec<T>::rounded(g.y);
+          }
         }
+#pragma unroll
+        for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
         if constexpr (ACT != JB_EPI_NONE) raw[i] = Vec<T>::pack(v);  // exact: v is T-rounded
       }
     }
