@@ -210,6 +210,12 @@ def run_reference(args, wl):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch,
+# averaged over the four linears of one layer, from the ncu capture recorded
+# in profiles/bert_base_int8_b256_s256_launches.md (same workload).
+GEMM_TRAFFIC_PER_LAUNCH = {"bert-base-int8-s256": 159.1e6}
+
+
 def main():
     args = parse()
     wl = WORKLOADS[args.workload]
@@ -342,7 +348,11 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (all six linears)",
                          "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved_tflops / peak) if achieved_tflops else None,
-                         "traffic": None, "peak_source": peak_note,
+                         "traffic": GEMM_TRAFFIC_PER_LAUNCH.get(args.workload),
+                         "traffic_unit": "bytes per launch (mean of one layer's four linears)",
+                         "traffic_source": "ncu --set full capture, "
+                                           "profiles/bert_base_int8_b256_s256_launches.md",
+                         "peak_source": peak_note,
                          "flops_per_step": flops_per_step_avg},
             "kernel_ms_per_step": {k: v["ms"] / args.steps for k, v in prof.items()},
             "clocks": clk,
