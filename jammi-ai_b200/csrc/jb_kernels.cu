@@ -287,6 +287,12 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
   }
 }
 
+// The GELU quantiser is ALU-bound: it is compiled for this many resident
+// 256-thread blocks per SM, trading unrolled temporaries for warps.
+#ifndef JB_GELU_Q_BLOCKS
+#define JB_GELU_Q_BLOCKS 3
+#endif
+
 // The value quantised for input x: x itself, or (ACT == JB_EPI_GELU) the
 // GELU of x rounded to T -- what a stored activation tensor of type T holds.
 template <typename T, int ACT>
@@ -300,7 +306,7 @@ __device__ __forceinline__ float pre_quant(float x) {
 // activation), so each element is read from memory and activated once;
 // MAXV == 0 is the general two-pass form for longer rows.
 template <typename T, int MAXV, int ACT>
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int8_t* q,
+__global__ void __launch_bounds__(256, (ACT == JB_EPI_GELU ? JB_GELU_Q_BLOCKS : 1)) quantize_rows_kernel(const T* __restrict__ x, int8_t* q,
                                                             float* scale, int rows,
                                                             const int* drows, int cols) {
   constexpr int VN = Vec<T>::N;
