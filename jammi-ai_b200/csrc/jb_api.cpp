@@ -154,7 +154,9 @@ jb_status jb_encode_text(jb_model* m, const uint32_t* ids, const uint32_t* lens,
     jb::Workspace& ws = m->ws;
     jb::check_cuda(cudaMemcpyAsync(ws.ids, ids, size_t(batch) * max_seq * 4, cudaMemcpyHostToDevice, s), "H2D ids");
     jb::check_cuda(cudaMemcpyAsync(ws.lens, lens, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D lens");
-    jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, s);
+    jb::run_graphed(m, 0, batch, max_seq, pooling, s, [&](cudaStream_t gs) {
+      jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
+    });
     jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->hidden * 4, cudaMemcpyDeviceToHost, s), "D2H");
     jb::check_device_flag(m, s);
   });
@@ -169,7 +171,16 @@ jb_status jb_encode_text_device(jb_model* m, const uint32_t* d_ids, const uint32
     std::lock_guard<std::mutex> lk(m->mu);
     jb::DeviceGuard g(m->device);
     jb::ensure_workspace(m, batch, std::max(max_seq, 1));
-    jb::bert_forward_device(m, d_ids, d_lens, batch, max_seq, pooling, d_out, nullptr, as_stream(stream));
+    // The forward runs on workspace copies of the inputs, so that one CUDA
+    // graph per shape serves every caller buffer.
+    cudaStream_t s = as_stream(stream);
+    jb::Workspace& ws = m->ws;
+    jb::check_cuda(cudaMemcpyAsync(ws.ids, d_ids, size_t(batch) * max_seq * 4, cudaMemcpyDeviceToDevice, s), "ids");
+    jb::check_cuda(cudaMemcpyAsync(ws.lens, d_lens, size_t(batch) * 4, cudaMemcpyDeviceToDevice, s), "lens");
+    jb::run_graphed(m, 0, batch, max_seq, pooling, s, [&](cudaStream_t gs) {
+      jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
+    });
+    jb::check_cuda(cudaMemcpyAsync(d_out, ws.out, size_t(batch) * m->hidden * 4, cudaMemcpyDeviceToDevice, s), "out");
   });
 }
 
@@ -200,7 +211,9 @@ jb_status jb_encode_image(jb_model* m, const float* pixels, int batch, float* ou
     jb::Workspace& ws = m->ws;
     const size_t px = size_t(batch) * 3 * m->image_size * m->image_size;
     jb::check_cuda(cudaMemcpyAsync(ws.pixels, pixels, px * 4, cudaMemcpyHostToDevice, s), "H2D pixels");
-    jb::clip_forward_device(m, ws.pixels, batch, ws.out, s);
+    jb::run_graphed(m, 1, batch, m->tokens, 0, s, [&](cudaStream_t gs) {
+      jb::clip_forward_device(m, ws.pixels, batch, ws.out, gs);
+    });
     jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->embed_dim * 4, cudaMemcpyDeviceToHost, s), "D2H");
     jb::check_device_flag(m, s);
   });

@@ -439,6 +439,7 @@ void ensure_workspace(jb_model* m, int batch, int seq) {
   Workspace& ws = m->ws;
   if (batch <= ws.batch_cap && seq <= ws.seq_cap) return;
   const int nb = std::max(batch, ws.batch_cap), ns = std::max(seq, ws.seq_cap);
+  clear_graphs(m);
   free_workspace(ws);
   const WsPlan p = plan_workspace(m, nb, ns);
   char* base = nullptr;
@@ -559,6 +560,10 @@ void model_free(jb_model* m) {
   {
     DeviceGuard guard(m->device);
     cudaDeviceSynchronize();
+    clear_graphs(m);
+    if (m->graph_stream) cudaStreamDestroy(m->graph_stream);
+    if (m->graph_in) cudaEventDestroy(m->graph_in);
+    if (m->graph_out) cudaEventDestroy(m->graph_out);
     free_workspace(m->ws);
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);
@@ -615,6 +620,73 @@ void profile_read(jb_model* m, double* ms, int* launches) {
     ms[r.kind] += t;
     launches[r.kind] += 1;
   }
+}
+
+void clear_graphs(jb_model* m) {
+  for (GraphEntry& g : m->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  m->graphs.clear();
+}
+
+void run_graphed(jb_model* m, int kind, int batch, int seq, int pooling, cudaStream_t s,
+                 const std::function<void(cudaStream_t)>& forward) {
+  if (m->prof_on) {
+    forward(s);
+    return;
+  }
+  constexpr size_t kMaxShapes = 64;
+  GraphEntry* g = nullptr;
+  for (GraphEntry& e : m->graphs)
+    if (e.kind == kind && e.batch == batch && e.seq == seq && e.pooling == pooling) g = &e;
+  if (!g) {
+    if (m->graphs.size() >= kMaxShapes) {  // forget the least recently used shape
+      auto lru = std::min_element(m->graphs.begin(), m->graphs.end(),
+                                  [](const GraphEntry& a, const GraphEntry& b) {
+                                    return a.last_use < b.last_use;
+                                  });
+      if (lru->exec) cudaGraphExecDestroy(lru->exec);
+      m->graphs.erase(lru);
+    }
+    GraphEntry e;
+    e.kind = kind;
+    e.batch = batch;
+    e.seq = seq;
+    e.pooling = pooling;
+    m->graphs.push_back(e);
+    g = &m->graphs.back();
+  }
+  g->last_use = ++m->graph_clock;
+  if (++g->seen < 2) {  // a shape seen once may never come back: no capture yet
+    forward(s);
+    return;
+  }
+  if (!m->graph_stream) {
+    check_cuda(cudaStreamCreateWithFlags(&m->graph_stream, cudaStreamNonBlocking), "graph stream");
+    check_cuda(cudaEventCreateWithFlags(&m->graph_in, cudaEventDisableTiming), "graph event");
+    check_cuda(cudaEventCreateWithFlags(&m->graph_out, cudaEventDisableTiming), "graph event");
+  }
+  cudaStream_t gs = m->graph_stream;
+  if (!g->exec) {
+    check_cuda(cudaStreamBeginCapture(gs, cudaStreamCaptureModeRelaxed), "graph capture");
+    cudaGraph_t graph = nullptr;
+    try {
+      forward(gs);
+    } catch (...) {
+      cudaStreamEndCapture(gs, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      throw;
+    }
+    check_cuda(cudaStreamEndCapture(gs, &graph), "graph capture");
+    const cudaError_t e = cudaGraphInstantiate(&g->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(e, "graph instantiate");
+  }
+  check_cuda(cudaEventRecord(m->graph_in, s), "graph order");
+  check_cuda(cudaStreamWaitEvent(gs, m->graph_in, 0), "graph order");
+  check_cuda(cudaGraphLaunch(g->exec, gs), "graph launch");
+  check_cuda(cudaEventRecord(m->graph_out, gs), "graph order");
+  check_cuda(cudaStreamWaitEvent(s, m->graph_out, 0), "graph order");
 }
 
 void check_device_flag(jb_model* m, cudaStream_t s) {

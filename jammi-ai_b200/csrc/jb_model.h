@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -73,6 +74,17 @@ struct Workspace {
 
 }  // namespace jb
 
+namespace jb {
+// A whole forward captured as a CUDA graph on workspace buffers, replayed for
+// every later call of the same shape (kind: 0 pooled text, 1 image).
+struct GraphEntry {
+  int kind = 0, batch = 0, seq = 0, pooling = 0;
+  int seen = 0;                    // calls with this shape so far
+  cudaGraphExec_t exec = nullptr;  // captured on the second call
+  uint64_t last_use = 0;
+};
+}  // namespace jb
+
 struct jb_model {
   int family = JB_FAMILY_BERT;
   int format = JB_FMT_BF16;
@@ -102,6 +114,12 @@ struct jb_model {
   bool prof_on = false;
   std::vector<jb::ProfRec> prof_recs;
   std::vector<cudaEvent_t> prof_free;
+  // forward graphs (jb::run_graphed): private capture / replay stream and the
+  // events that order it after, and before, the caller's stream
+  std::vector<jb::GraphEntry> graphs;
+  uint64_t graph_clock = 0;
+  cudaStream_t graph_stream = nullptr;
+  cudaEvent_t graph_in = nullptr, graph_out = nullptr;
 };
 
 namespace jb {
@@ -131,5 +149,14 @@ void profile_enable(jb_model* m, bool on);
 void profile_read(jb_model* m, double* ms, int* launches);
 // Synchronises `s` and turns the device error flag into an Error.
 void check_device_flag(jb_model* m, cudaStream_t s);
+// Runs forward(stream), a whole forward over workspace buffers only, ordered
+// after the work already queued on `s` and before the work queued next.  The
+// first call of a shape (kind, batch, seq, pooling) launches it directly; the
+// second captures it as a CUDA graph on the model's private stream; later
+// calls replay the graph (one launch instead of ~110).  Profiling runs direct.
+void run_graphed(jb_model* m, int kind, int batch, int seq, int pooling, cudaStream_t s,
+                 const std::function<void(cudaStream_t)>& forward);
+// Drops every captured graph (their pointers die with the workspace).
+void clear_graphs(jb_model* m);
 
 }  // namespace jb
