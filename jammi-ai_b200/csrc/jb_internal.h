@@ -54,6 +54,10 @@ struct LnArgs {
 };
 cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s);
 
+// Tabulates the bf16 GELU on the current device (once; later calls return at
+// once).  The first int8 BERT forward or GELU quantisation on a device needs
+// it: model loading calls it so that no forward (or graph capture) does.
+cudaError_t init_gelu_table(cudaStream_t s);
 cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
                                  const int* drows, int cols, cudaStream_t s,
                                  int activation = JB_EPI_NONE);

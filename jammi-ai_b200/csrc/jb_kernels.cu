@@ -3,7 +3,9 @@
 // per-row int8 quantisation, pooling + L2 normalisation, and the ViT
 // patch / CLS / pooling helpers.  One warp per row with 16-byte vector
 // loads; all statistics in f32.
+#include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 #include "jb_common.cuh"
 #include "jb_internal.h"
@@ -382,6 +384,90 @@ __global__ void __launch_bounds__(256, (ACT == JB_EPI_GELU ? JB_GELU_Q_BLOCKS : 
   if (lane == 0) scale[row] = amax / 127.0f;
 }
 
+// ── GELU by table, fused into the per-token quantiser ───────────────────────
+// Every bf16 input has one correctly rounded bf16 GELU: bf16(x * Phi(x)) with
+// Phi from CUDA's double-precision erf, tabulated once per device (65536
+// entries, 128 KB).  The FFN2-input quantiser stages the table in shared
+// memory and replaces the activation's arithmetic by one lookup per value,
+// so it runs at the speed of the plain quantiser (memory-bound).
+__device__ __align__(16) uint16_t g_gelu_bf16[65536];
+
+__global__ void gelu_table_kernel() {
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= 65536) return;
+  __nv_bfloat16_raw r;
+  r.x = static_cast<unsigned short>(u);
+  const double x = static_cast<double>(__bfloat162float(__nv_bfloat16(r)));
+  const double g = 0.5 * x * (1.0 + erf(x * 0.70710678118654752440));
+  const __nv_bfloat16 b = __double2bfloat16(g);
+  g_gelu_bf16[u] = static_cast<__nv_bfloat16_raw>(b).x;
+}
+
+constexpr int kGeluQThreads = 512;
+constexpr int kGeluTableBytes = 65536 * 2;
+
+// GELU of the two bf16 halves of w by lookup (table in shared memory).
+__device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* tab, uint32_t w) {
+  const uint32_t lo = tab[w & 0xFFFFu], hi = tab[w >> 16];
+  return lo | (hi << 16);
+}
+
+// One warp per row (up to MAXV 16-byte vectors per lane, held in registers
+// after the lookup); persistent, one block per SM.
+template <int MAXV>
+__global__ void __launch_bounds__(kGeluQThreads, 1)
+    gelu_quantize_bf16_kernel(const bf16* __restrict__ x, int8_t* q, float* scale, int rows,
+                              const int* drows, int cols) {
+  extern __shared__ __align__(16) uint16_t tab[];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(g_gelu_bf16);
+    uint4* dst = reinterpret_cast<uint4*>(tab);
+    for (int i = threadIdx.x; i < kGeluTableBytes / 16; i += kGeluQThreads) dst[i] = src[i];
+  }
+  __syncthreads();
+  constexpr int kWarps = kGeluQThreads / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = drows ? min(*drows, rows) : rows;
+  const int nvec = cols / 8;
+  for (int row = blockIdx.x * kWarps + warp; row < R; row += gridDim.x * kWarps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
+    uint4 raw[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+      if (lane + i * 32 < nvec) raw[i] = __ldg(xr + lane + i * 32);
+    // lookup, and the largest |value| as bf16 magnitude bits (integer order
+    // of non-negative bf16 bit patterns is their numeric order)
+    uint32_t mx2 = 0;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + i * 32 < nvec) {
+        raw[i].x = gelu_lookup2(tab, raw[i].x);
+        raw[i].y = gelu_lookup2(tab, raw[i].y);
+        raw[i].z = gelu_lookup2(tab, raw[i].z);
+        raw[i].w = gelu_lookup2(tab, raw[i].w);
+        mx2 = __vmaxu2(mx2, raw[i].x & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, raw[i].y & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, raw[i].z & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, raw[i].w & 0x7FFF7FFFu);
+      }
+    }
+    const float amax = warp_max(fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u)));
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    int8_t* qr = q + static_cast<size_t>(row) * cols;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + i * 32;
+      if (vi < nvec) {
+        float v[8];
+        Vec<bf16>::unpack(raw[i], v);
+        *reinterpret_cast<uint2*>(qr + vi * 8) =
+            make_uint2(quant4(v[0], v[1], v[2], v[3], inv), quant4(v[4], v[5], v[6], v[7], inv));
+      }
+    }
+    if (lane == 0) scale[row] = amax / 127.0f;
+  }
+}
+
 // ── pooling + L2 (pooling.rs:31-148) ──────────────────────────────────────
 constexpr int kPoolThreads = 128;
 
@@ -721,9 +807,57 @@ cudaError_t launch_quantize_act(const void* x, int dtype, int8_t* q, float* scal
 }
 }  // namespace
 
+namespace {
+std::mutex g_gelu_mu;
+bool g_gelu_ready[64] = {};
+
+template <int MAXV>
+cudaError_t launch_gelu_lookup(const bf16* x, int8_t* q, float* scale, int rows, const int* drows,
+                               int cols, cudaStream_t s) {
+  auto kern = gelu_quantize_bf16_kernel<MAXV>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGeluTableBytes);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned need = blocks_for(rows, kGeluQThreads / 32);
+  const unsigned grid = std::min<unsigned>(need, static_cast<unsigned>(num_sms(dev)));
+  kern<<<grid, kGeluQThreads, kGeluTableBytes, s>>>(x, q, scale, rows, drows, cols);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t init_gelu_table(cudaStream_t s) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_gelu_mu);
+  if (dev >= 0 && dev < 64 && g_gelu_ready[dev]) return cudaSuccess;
+  // Built once, synchronously, so that work on any stream may use it after.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(s, &cap);
+  if (e != cudaSuccess) return e;
+  if (cap != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
+  gelu_table_kernel<<<65536 / 256, 256, 0, s>>>();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) g_gelu_ready[dev] = true;
+  return e;
+}
+
 cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
                                  const int* drows, int cols, cudaStream_t s, int activation) {
   if (rows == 0) return cudaSuccess;
+  if (activation == JB_EPI_GELU && dtype == JB_DT_BF16 && cols % 8 == 0 && cols <= 4096) {
+    cudaError_t e = init_gelu_table(s);  // no-op after the first call on this device
+    if (e != cudaSuccess) return e;
+    const bf16* xb = static_cast<const bf16*>(x);
+    const int per_lane = (cols / 8 + 31) / 32;
+    if (per_lane <= 4) return launch_gelu_lookup<4>(xb, q, scale, rows, drows, cols, s);
+    if (per_lane <= 8) return launch_gelu_lookup<8>(xb, q, scale, rows, drows, cols, s);
+    if (per_lane <= 12) return launch_gelu_lookup<12>(xb, q, scale, rows, drows, cols, s);
+    return launch_gelu_lookup<16>(xb, q, scale, rows, drows, cols, s);
+  }
   if (activation == JB_EPI_GELU)
     return launch_quantize_act<JB_EPI_GELU>(x, dtype, q, scale, rows, drows, cols, s);
   if (activation != JB_EPI_NONE) return cudaErrorInvalidValue;

@@ -547,6 +547,9 @@ jb_model* model_load(const char* path, const char* config_json, int device, int 
       load_bert(m.get(), st, cfg);
     check_cuda(cudaMalloc(&m->d_err, sizeof(int)), "error flag");
     check_cuda(cudaMemset(m->d_err, 0, sizeof(int)), "error flag");
+    // the int8 FFN2 input quantiser looks the GELU up in a per-device table
+    if (m->family == JB_FAMILY_BERT && m->format == JB_FMT_INT8)
+      check_cuda(init_gelu_table(nullptr), "GELU table");
   } catch (...) {
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);
