@@ -388,8 +388,9 @@ __global__ void __launch_bounds__(256, (ACT == JB_EPI_GELU ? JB_GELU_Q_BLOCKS : 
 // Every bf16 input has one correctly rounded bf16 GELU: bf16(x * Phi(x)) with
 // Phi from CUDA's double-precision erf, tabulated once per device (65536
 // entries, 128 KB).  The FFN2-input quantiser stages the table in shared
-// memory and replaces the activation's arithmetic by one lookup per value,
-// so it runs at the speed of the plain quantiser (memory-bound).
+// memory and replaces the activation's arithmetic by one lookup for half of
+// the values (the lookups' bank conflicts, not the arithmetic, would bound a
+// table-only kernel); the other half use gelu_tc2.
 __device__ __align__(16) uint16_t g_gelu_bf16[65536];
 
 __global__ void gelu_table_kernel() {
@@ -441,10 +442,20 @@ __global__ void __launch_bounds__(kGeluQThreads, 1)
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       if (lane + i * 32 < nvec) {
+        // half of the values by table (shared-memory pipe), half by the
+        // A&S 7.1.28 arithmetic (FMA pipe): the two pipes share the work
         raw[i].x = gelu_lookup2(tab, raw[i].x);
         raw[i].y = gelu_lookup2(tab, raw[i].y);
-        raw[i].z = gelu_lookup2(tab, raw[i].z);
-        raw[i].w = gelu_lookup2(tab, raw[i].w);
+        {
+          float v[4];
+          v[0] = __uint_as_float(raw[i].z << 16); v[1] = __uint_as_float(raw[i].z & 0xFFFF0000u);
+          v[2] = __uint_as_float(raw[i].w << 16); v[3] = __uint_as_float(raw[i].w & 0xFFFF0000u);
+          const float2 g0 = gelu_tc2(make_float2(v[0], v[1]));
+          const float2 g1 = gelu_tc2(make_float2(v[2], v[3]));
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(g0.x, g0.y), h1 = __floats2bfloat162_rn(g1.x, g1.y);
+          raw[i].z = *reinterpret_cast<uint32_t*>(&h0);
+          raw[i].w = *reinterpret_cast<uint32_t*>(&h1);
+        }
         mx2 = __vmaxu2(mx2, raw[i].x & 0x7FFF7FFFu);
         mx2 = __vmaxu2(mx2, raw[i].y & 0x7FFF7FFFu);
         mx2 = __vmaxu2(mx2, raw[i].z & 0x7FFF7FFFu);
