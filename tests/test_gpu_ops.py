@@ -190,11 +190,12 @@ def test_quantize_rows_bit_exact(dev, dtype):
 
 
 def test_gelu_quantize_rows(dev):
-    """GELU fused into the per-row quantiser (the int8 FFN input): the device
-    GELU (Abramowitz-Stegun 7.1.28 erf, |error| <= 3e-7) rounded to bf16 equals the
-    exact GELU rounded to bf16 except where the exact value sits within that
-    error of a rounding boundary, so the int8 codes may differ by one there
-    and nowhere else; the scales follow the same amax."""
+    """GELU fused into the per-row quantiser (the int8 FFN input).  The device
+    takes half of the values from a table of correctly rounded bf16 GELUs and
+    computes the other half with the Abramowitz-Stegun 7.1.28 erf (|error| <=
+    3e-7), which rounds to the same bf16 except where the exact value sits
+    within that error of a rounding boundary; so the int8 codes may differ by
+    one there and nowhere else, and the scales follow the same amax."""
     ops = _ops()
     from jammi_b200._lib import EPI_GELU
     rng = np.random.default_rng(29)
