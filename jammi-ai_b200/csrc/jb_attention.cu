@@ -14,6 +14,9 @@
 //   attn_simt:           any head_dim in {8,16,32,64}, f32 or bf16 (the f32
 //                        compute precision and the tiny fixtures).
 #include <cmath>
+#include <cstring>
+
+#include <cudaTypedefs.h>
 
 #include "jb_common.cuh"
 #include "jb_internal.h"
@@ -77,16 +80,23 @@ __device__ __forceinline__ void load_tile(uint32_t tile, const bf16* g, int ld, 
 
 // Four CTAs per SM (128 registers, 40 KB shared memory each): the rows are
 // short, so the kernel is latency-bound and occupancy is what hides it.
-__global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16* __restrict__ qkv,
-                                                                  const int* __restrict__ cu,
-                                                                  bf16* __restrict__ ctx, int heads,
-                                                                  float scale_log2) {
+// TMA = false: tiles by cp.async, rows past the row's end zero-filled.
+// TMA = true:  one thread loads each tile with one TMA copy (the tensor map
+// covers the buffer's row capacity; rows past the row's end hold other rows'
+// values and are masked: K by the -inf scores, V zeroed in shared memory in
+// the row's last key block so that 0 * V stays 0).
+template <bool TMA>
+__global__ void __launch_bounds__(kFaThreads, 4)
+    flash_attn_bf16_d64(const bf16* __restrict__ qkv, const int* __restrict__ cu,
+                        bf16* __restrict__ ctx, int heads, float scale_log2,
+                        const __grid_constant__ CUtensorMap tm, int* err) {
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = cu[b], n = cu[b + 1] - start;
   const int q0 = qb * kFaRows;
   if (q0 >= n) return;
   const int H = heads * 64, ld = 3 * H;
   __shared__ __align__(1024) uint8_t sm[5 * kTileBytes];
+  __shared__ __align__(8) uint64_t bars[2];
   const uint32_t sQ = smem_u32(sm);
   const uint32_t sK0 = sQ + kTileBytes, sV0 = sQ + 2 * kTileBytes;
   const uint32_t sK1 = sQ + 3 * kTileBytes, sV1 = sQ + 4 * kTileBytes;
@@ -94,11 +104,27 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
   const bf16* gK = qkv + static_cast<size_t>(start) * ld + H + h * 64;
   const bf16* gV = gK + H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t bar0 = smem_u32(&bars[0]), bar1 = smem_u32(&bars[1]);
 
-  load_tile(sQ, gQ, ld, n - q0, tid);
-  load_tile(sK0, gK, ld, n, tid);
-  load_tile(sV0, gV, ld, n, tid);
-  cp_async_commit();
+  if constexpr (TMA) {
+    if (tid == 0) {
+      mbar_init(bar0, 1);
+      mbar_init(bar1, 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar0, 3 * kTileBytes);
+      tma_load_2d(sQ, &tm, h * 64, start + q0, bar0);
+      tma_load_2d(sK0, &tm, H + h * 64, start, bar0);
+      tma_load_2d(sV0, &tm, 2 * H + h * 64, start, bar0);
+    }
+  } else {
+    load_tile(sQ, gQ, ld, n - q0, tid);
+    load_tile(sK0, gK, ld, n, tid);
+    load_tile(sV0, gV, ld, n, tid);
+    cp_async_commit();
+  }
 
   const int nkb = (n + kFaKeys - 1) / kFaKeys;
   float o[8][4];
@@ -111,16 +137,45 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
 
   for (int kb = 0; kb < nkb; ++kb) {
     const uint32_t sK = (kb & 1) ? sK1 : sK0, sV = (kb & 1) ? sV1 : sV0;
-    if (kb + 1 < nkb) {
-      const size_t off = static_cast<size_t>(kb + 1) * kFaKeys * ld;
-      load_tile((kb & 1) ? sK0 : sK1, gK + off, ld, n - (kb + 1) * kFaKeys, tid);
-      load_tile((kb & 1) ? sV0 : sV1, gV + off, ld, n - (kb + 1) * kFaKeys, tid);
-      cp_async_commit();
-      cp_async_wait<1>();
+    if constexpr (TMA) {
+      // the other buffer was last read in the previous iteration, which
+      // ended with a CTA barrier
+      if (kb + 1 < nkb && tid == 0) {
+        const uint32_t bar = (kb & 1) ? bar0 : bar1;
+        const int row = start + (kb + 1) * kFaKeys;
+        mbar_arrive_expect_tx(bar, 2 * kTileBytes);
+        tma_load_2d((kb & 1) ? sK0 : sK1, &tm, H + h * 64, row, bar);
+        tma_load_2d((kb & 1) ? sV0 : sV1, &tm, 2 * H + h * 64, row, bar);
+      }
+      // all threads wait for this stage (bounded); a CTA whose wait gave up
+      // reports it and leaves as a whole
+      volatile int no_abort = 0;
+      const bool ok = mbar_wait((kb & 1) ? bar1 : bar0, (kb >> 1) & 1, &no_abort);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0 && err) atomicOr(err, kErrTimeout);
+        return;
+      }
+      const int valid = n - kb * kFaKeys;  // V rows of this block inside the row
+      if (valid < kFaKeys) {
+        for (int i = tid; i < (kFaKeys - valid) * 8; i += kFaThreads) {
+          const int r = valid + (i >> 3), c = i & 7;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(swz(sV, r, c)), "r"(0)
+                       : "memory");
+        }
+        __syncthreads();
+      }
     } else {
-      cp_async_wait<0>();
+      if (kb + 1 < nkb) {
+        const size_t off = static_cast<size_t>(kb + 1) * kFaKeys * ld;
+        load_tile((kb & 1) ? sK0 : sK1, gK + off, ld, n - (kb + 1) * kFaKeys, tid);
+        load_tile((kb & 1) ? sV0 : sV1, gV + off, ld, n - (kb + 1) * kFaKeys, tid);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
     }
-    __syncthreads();
     if (kb == 0) {
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
@@ -187,11 +242,14 @@ __global__ void __launch_bounds__(kFaThreads, 4) flash_attn_bf16_d64(const bf16*
       }
       l0 = l0 * a0 + rs0;
       l1 = l1 * a1 + rs1;
+      // o is zero before the first block, and unchanged when no row max moved
+      if (kb > 0 && __any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
 #pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        const float2 o01 = __fmul2_rn(make_float2(o[dt][0], o[dt][1]), f2(a0));
-        const float2 o23 = __fmul2_rn(make_float2(o[dt][2], o[dt][3]), f2(a1));
-        o[dt][0] = o01.x; o[dt][1] = o01.y; o[dt][2] = o23.x; o[dt][3] = o23.y;
+        for (int dt = 0; dt < 8; ++dt) {
+          const float2 o01 = __fmul2_rn(make_float2(o[dt][0], o[dt][1]), f2(a0));
+          const float2 o23 = __fmul2_rn(make_float2(o[dt][2], o[dt][3]), f2(a1));
+          o[dt][0] = o01.x; o[dt][1] = o01.y; o[dt][2] = o23.x; o[dt][3] = o23.y;
+        }
       }
       // O += P V
 #pragma unroll
@@ -308,11 +366,33 @@ cudaError_t launch_simt(const void* qkv, const int* cu, void* ctx, int batch, in
   return cudaGetLastError();
 }
 
+// 2-D map over qkv [rows, 3 * H] bf16 with one 64 x 64 box (128-byte rows,
+// 128-byte swizzle: the layout swz() reads).
+bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  if (!enc || (reinterpret_cast<uintptr_t>(qkv) & 15)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(3) * H, static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(3) * H * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
-                             std::string* why) {
+                             std::string* why, int rows_cap, int* err) {
   if (batch == 0 || max_len == 0) return cudaSuccess;
   if (batch > 65535 || heads > 65535) {
     if (why) *why = "attention: batch and heads must be <= 65535";
@@ -321,10 +401,14 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
   if (dtype == JB_DT_BF16 && head_dim == 64) {
     dim3 grid((max_len + kFaRows - 1) / kFaRows, heads, batch);
     const float scale_log2 = 1.4426950408889634f / sqrtf(64.f);
-    cudaFuncSetAttribute(flash_attn_bf16_d64, cudaFuncAttributePreferredSharedMemoryCarveout,
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof(tm));
+    const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64);
+    auto kern = tma ? flash_attn_bf16_d64<true> : flash_attn_bf16_d64<false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
-    flash_attn_bf16_d64<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu,
-                                                    static_cast<bf16*>(ctx), heads, scale_log2);
+    kern<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu, static_cast<bf16*>(ctx),
+                                     heads, scale_log2, tm, err);
     return cudaGetLastError();
   }
   if (dtype == JB_DT_BF16) return launch_simt<bf16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why);

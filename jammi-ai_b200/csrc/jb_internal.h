@@ -84,7 +84,8 @@ cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
 
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
-                             std::string* why);
+                             std::string* why,
+                             int rows_cap = 0, int* err = nullptr);
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s);

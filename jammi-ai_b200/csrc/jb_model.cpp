@@ -790,8 +790,8 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
     cudaError_t e;
     {
       ProfScope ps(m, kProfAttention, s);
-      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads,
-                                     max_seq, s, &why);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s,
+                           &why, Mcap, m->d_err);
     }
     if (e != cudaSuccess) {
       if (!why.empty()) fail(JB_ERR_INVALID, why);
@@ -844,7 +844,8 @@ void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out
     cudaError_t e;
     {
       ProfScope ps(m, kProfAttention, s);
-      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, T, s, &why);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, T, s, &why,
+                           batch * T, m->d_err);
     }
     if (e != cudaSuccess) {
       if (!why.empty()) fail(JB_ERR_INVALID, why);
