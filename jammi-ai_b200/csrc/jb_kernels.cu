@@ -519,20 +519,40 @@ __global__ void __launch_bounds__(kPoolWarps * 32) pool_normalize_kernel(const T
   for (int k = 0; k < MAXV * VN; ++k) acc[k] = is_max ? -1e30f : 0.f;
   // CLS reads token 0 only; an all-padding row has none and stays zero.
   const int t_end = pooling == JB_POOL_CLS ? min(n, 1) : n;
-  for (int t = warp; t < t_end; t += kPoolWarps) {
-    const T* hr = hidden + static_cast<size_t>(start + t) * H;
+  auto add_token = [&](int t, const uint4 (&raw)[MAXV]) {
     const float w = pooling == JB_POOL_WEIGHTED_MEAN ? static_cast<float>(t + 1) : 1.f;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
+      if (lane + 32 * i < nvec) {
         float x[VN];
-        Vec<T>::load(hr + vi * VN, x);
+        Vec<T>::unpack(raw[i], x);
 #pragma unroll
         for (int e = 0; e < VN; ++e)
           acc[i * VN + e] = is_max ? fmaxf(acc[i * VN + e], x[e]) : fmaf(x[e], w, acc[i * VN + e]);
       }
     }
+  };
+  auto load_token = [&](int t, uint4 (&raw)[MAXV]) {
+    const uint4* hr = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(start + t) * H);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+      if (lane + 32 * i < nvec) raw[i] = __ldg(hr + lane + 32 * i);
+  };
+  // Warp w takes tokens w, w+8, ... in order; bf16 rows load four tokens at
+  // a time (the accumulation order, hence the result, is unchanged).
+  constexpr int kUnroll = sizeof(T) == 2 ? 4 : 1;
+  int t = warp;
+  for (; t + (kUnroll - 1) * kPoolWarps < t_end; t += kUnroll * kPoolWarps) {
+    uint4 raw[kUnroll][MAXV];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) load_token(t + u * kPoolWarps, raw[u]);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) add_token(t + u * kPoolWarps, raw[u]);
+  }
+  for (; t < t_end; t += kPoolWarps) {
+    uint4 raw[MAXV];
+    load_token(t, raw);
+    add_token(t, raw);
   }
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
