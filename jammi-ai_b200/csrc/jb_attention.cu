@@ -214,12 +214,21 @@ __global__ void __launch_bounds__(kFaThreads, 4)
           for (int e = 0; e < 4; ++e)
             if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) >= n) s[nt][e] = -INFINITY;
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      // row maxima and sums as trees (depth 4, not 8): short dependency chains
+      float t0[8], t1[8];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
-        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+        t0[nt] = fmaxf(s[nt][0], s[nt][1]);
+        t1[nt] = fmaxf(s[nt][2], s[nt][3]);
       }
+#pragma unroll
+      for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+        for (int nt = 0; nt < w; ++nt) {
+          t0[nt] = fmaxf(t0[nt], t0[nt + w]);
+          t1[nt] = fmaxf(t1[nt], t1[nt + w]);
+        }
+      float mx0 = t0[0], mx1 = t1[0];
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
@@ -228,7 +237,7 @@ __global__ void __launch_bounds__(kFaThreads, 4)
       const float a0 = ex2_approx(m0 - mn0), a1 = ex2_approx(m1 - mn1);
       m0 = mn0;
       m1 = mn1;
-      float rs0 = 0.f, rs1 = 0.f;
+      float2 rs[8];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const float2 e01 = __ffma2_rn(make_float2(s[nt][0], s[nt][1]), f2(scale_log2), f2(-mn0));
@@ -237,9 +246,13 @@ __global__ void __launch_bounds__(kFaThreads, 4)
         s[nt][1] = ex2_approx(e01.y);
         s[nt][2] = ex2_approx(e23.x);
         s[nt][3] = ex2_approx(e23.y);
-        rs0 += s[nt][0] + s[nt][1];
-        rs1 += s[nt][2] + s[nt][3];
+        rs[nt] = __fadd2_rn(make_float2(s[nt][0], s[nt][2]), make_float2(s[nt][1], s[nt][3]));
       }
+#pragma unroll
+      for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+        for (int nt = 0; nt < w; ++nt) rs[nt] = __fadd2_rn(rs[nt], rs[nt + w]);
+      const float rs0 = rs[0].x, rs1 = rs[0].y;
       l0 = l0 * a0 + rs0;
       l1 = l1 * a1 + rs1;
       // o is zero before the first block, and unchanged when no row max moved
