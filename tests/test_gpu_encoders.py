@@ -247,3 +247,23 @@ def test_graph_replay_matches_direct_launches():
                                 torch.from_numpy(lens.astype(np.int32)).cuda(), d_out, stream=None)
             model.sync(None)
             assert np.array_equal(d_out.cpu().numpy(), ref), fmt
+
+
+def test_graphs_follow_workspace_growth():
+    """Captured graphs hold workspace pointers: a larger batch regrows the
+    workspace, which must drop them; the original shape then re-runs (and
+    re-captures) against the new buffers with unchanged results."""
+    cfg, w = _bert_base(621)
+    rng = np.random.default_rng(622)
+    lens_s, lens_b = rng.integers(1, 65, size=8), rng.integers(1, 129, size=48)
+    ids_s, _ = ob.random_token_batch(8, 64, lens_s, seed=623)
+    ids_b, _ = ob.random_token_batch(48, 128, lens_b, seed=624)
+    ref_small = _bert(w, cfg.to_dict(), "int8").encode(ids_s, lens_s)
+    ref_big = _bert(w, cfg.to_dict(), "int8").encode(ids_b, lens_b)
+    model = _bert(w, cfg.to_dict(), "int8")
+    for _ in range(3):  # direct, capture, replay
+        assert np.array_equal(model.encode(ids_s, lens_s), ref_small)
+    assert np.array_equal(model.encode(ids_b, lens_b), ref_big)  # workspace grows
+    for _ in range(3):
+        assert np.array_equal(model.encode(ids_s, lens_s), ref_small)
+        assert np.array_equal(model.encode(ids_b, lens_b), ref_big)
