@@ -213,7 +213,7 @@ def run_reference(args, wl):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch,
 # averaged over the four linears of one layer, from the ncu capture recorded
 # in profiles/bert_base_int8_b256_s256_launches.md (same workload).
-GEMM_TRAFFIC_PER_LAUNCH = {"bert-base-int8-s256": 159.1e6}
+GEMM_TRAFFIC_PER_LAUNCH = {"bert-base-int8-s256": 158.9e6}
 
 
 def main():
