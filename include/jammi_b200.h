@@ -71,6 +71,8 @@ typedef struct {
   int32_t max_seq;         /* max_position_embeddings, or tokens per image */
   int32_t image_size;      /* ViT only */
   int64_t weight_bytes;    /* device bytes held by the weights */
+  int32_t projection_rank; /* rank of the installed projection head, 0 if none */
+  int32_t reserved;
 } jb_model_info;
 
 /* ── lifecycle ─────────────────────────────────────────────────────────── */
@@ -209,6 +211,23 @@ jb_status jb_op_sync(void* stream);
  * cu_seqlens [batch+1]: out f32 [batch, H] (pooling.rs:31-148). */
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens,
                                float* out, int batch, int H, int pooling, void* stream);
+
+/* ── post-pool projection head ───────────────────────────────────────────
+ * The projection head of a fine-tuned embedding adapter (CandleModel's
+ * projection_head, crates/jammi-ai/src/model/backend/candle.rs:823-829, built by
+ * load_projection_head, candle.rs:1857-1892): a LoraLinear over an identity
+ * base applied to the pooled, L2-normalised text embedding,
+ *   y = x + (lora_alpha / rank) * (x A^T) B^T   (lora_linear.rs:206-305),
+ * not re-normalised afterwards.  lora_a [rank, H] and lora_b [H, rank] are f32
+ * host arrays; rank 0 removes the head.  Text (BERT) models only; every text
+ * entry point that returns pooled embeddings applies it. */
+jb_status jb_model_set_projection_head(jb_model* model, const float* lora_a, const float* lora_b,
+                                       int rank, double lora_alpha);
+/* The same from an adapter safetensors file holding "projection.lora_a" and
+ * "projection.lora_b" (any float dtype).  A file without them installs no
+ * head and returns JB_OK, like the reference's Ok(None). */
+jb_status jb_model_load_projection_head(jb_model* model, const char* adapter_path,
+                                        double lora_alpha);
 
 /* ── memory-budget admission ──────────────────────────────────────────────
  * GpuScheduler (crates/jammi-ai/src/concurrency/gpu_scheduler.rs:11-218):

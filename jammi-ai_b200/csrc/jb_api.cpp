@@ -102,6 +102,26 @@ jb_status jb_model_get_info(const jb_model* m, jb_model_info* out) {
     out->max_seq = m->max_pos;
     out->image_size = m->image_size;
     out->weight_bytes = m->weight_bytes;
+    out->projection_rank = m->head_rank;
+  });
+}
+
+jb_status jb_model_set_projection_head(jb_model* m, const float* lora_a, const float* lora_b,
+                                       int rank, double lora_alpha) {
+  return guarded([&] {
+    if (!m) jb::fail(JB_ERR_INVALID, "null model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::set_projection_head(m, lora_a, lora_b, rank, lora_alpha);
+  });
+}
+
+jb_status jb_model_load_projection_head(jb_model* m, const char* adapter_path, double lora_alpha) {
+  return guarded([&] {
+    if (!m || !adapter_path) jb::fail(JB_ERR_INVALID, "null argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::load_projection_head(m, adapter_path, lora_alpha);
   });
 }
 

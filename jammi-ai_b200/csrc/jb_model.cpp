@@ -395,9 +395,10 @@ size_t esz(int dt) { return dt == JB_DT_F32 ? 4 : 2; }
 // Sizes of every workspace buffer for (batch, seq); shared by the allocator
 // and jb_estimate_batch_bytes.
 struct WsPlan {
-  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, pixels, patches, patch_out, pooled;
+  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, head_t, pixels, patches, patch_out, pooled;
   size_t sum() const {
-    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + pixels + patches + patch_out +
+    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + head_t + pixels + patches +
+           patch_out +
            pooled;
   }
 };
@@ -414,6 +415,7 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
   p.x = round_up(T * H * e);
   p.qkv = round_up(T * 3 * H * e);
   p.hf = round_up(T * F * e);
+  p.head_t = m->head_rank > 0 ? round_up(B * m->head_rank * 4) : 0;
   if (m->format == JB_FMT_INT8) {
     p.aq = round_up(T * std::max(H, F));
     p.as = round_up(T * 4);
@@ -474,6 +476,7 @@ void ensure_workspace(jb_model* m, int batch, int seq) {
   ws.hf = take(p.hf);
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
+  ws.head_t = static_cast<float*>(take(p.head_t));
   ws.pixels = static_cast<float*>(take(p.pixels));
   ws.patches = take(p.patches);
   ws.patch_out = take(p.patch_out);
@@ -507,6 +510,7 @@ Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq)
   ws.hf = take(p.hf);
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
+  ws.head_t = static_cast<float*>(take(p.head_t));
   ws.pixels = static_cast<float*>(take(p.pixels));
   ws.patches = take(p.patches);
   ws.patch_out = take(p.patch_out);
@@ -692,6 +696,46 @@ void run_graphed(jb_model* m, int kind, int batch, int seq, int pooling, cudaStr
   check_cuda(cudaStreamWaitEvent(s, m->graph_out, 0), "graph order");
 }
 
+void set_projection_head(jb_model* m, const float* a, const float* b, int rank, double alpha) {
+  if (m->family != JB_FAMILY_BERT) fail(JB_ERR_INVALID, "projection heads apply to text models");
+  if (rank < 0 || (rank > 0 && (!a || !b))) fail(JB_ERR_INVALID, "projection head: bad arguments");
+  cudaDeviceSynchronize();  // no forward may still read the old head or workspace
+  clear_graphs(m);
+  free_workspace(m->ws);
+  m->weight_bytes -= 2ll * m->head_rank * m->hidden * 4;
+  auto drop = [&](float*& p) {
+    if (!p) return;
+    cudaFree(p);
+    m->weight_allocs.erase(std::remove(m->weight_allocs.begin(), m->weight_allocs.end(),
+                                       static_cast<void*>(p)),
+                           m->weight_allocs.end());
+    p = nullptr;
+  };
+  drop(m->head_a);
+  drop(m->head_b);
+  m->head_rank = 0;
+  if (rank == 0) return;
+  const size_t n = static_cast<size_t>(rank) * m->hidden;
+  const float scale = static_cast<float>(alpha / rank);  // LoraLinear::from_loaded
+  std::vector<float> bs(b, b + n);
+  for (float& v : bs) v *= scale;
+  m->head_a = static_cast<float*>(upload_bytes(m, a, n * 4));
+  m->head_b = static_cast<float*>(upload_bytes(m, bs.data(), n * 4));
+  m->head_rank = rank;
+}
+
+void load_projection_head(jb_model* m, const char* path, double alpha) {
+  SafeTensors st(path);
+  if (!st.has("projection.lora_a") || !st.has("projection.lora_b")) return;  // Ok(None)
+  const StTensor& ta = st.get("projection.lora_a");
+  if (ta.shape.size() != 2 || ta.shape[1] != m->hidden)
+    fail(JB_ERR_IO, "projection.lora_a must be [rank, hidden]");
+  const int rank = static_cast<int>(ta.shape[0]);
+  const std::vector<float> a = st.f32("projection.lora_a", static_cast<int64_t>(rank) * m->hidden);
+  const std::vector<float> b = st.f32("projection.lora_b", static_cast<int64_t>(rank) * m->hidden);
+  set_projection_head(m, a.data(), b.data(), rank, alpha);
+}
+
 void check_device_flag(jb_model* m, cudaStream_t s) {
   check_cuda(cudaStreamSynchronize(s), "forward");
   int flag = 0;
@@ -818,8 +862,22 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
   }
   if (d_hidden)
     PROF_MEM_CALL(launch_unpack_hidden(ws.x, act, ws.cu, d_hidden, batch, max_seq, H, s), "unpack");
-  if (d_out)
+  if (d_out) {
     PROF_MEM_CALL(launch_pool_normalize(ws.x, act, ws.cu, d_out, batch, H, pooling, s), "pooling");
+    if (m->head_rank > 0) {  // projection head: d_out += (d_out A^T) (s B)^T, f32
+      Linear la, lb;
+      la.w = m->head_a;
+      la.dtype = JB_DT_F32;
+      la.N = m->head_rank;
+      la.K = H;
+      lb.w = m->head_b;
+      lb.dtype = JB_DT_F32;
+      lb.N = H;
+      lb.K = m->head_rank;
+      run_linear(m, la, d_out, nullptr, batch, nullptr, ws.head_t, JB_DT_F32, JB_EPI_NONE, nullptr, s);
+      run_linear(m, lb, ws.head_t, nullptr, batch, nullptr, d_out, JB_DT_F32, JB_EPI_RESIDUAL, d_out, s);
+    }
+  }
 }
 
 void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s) {

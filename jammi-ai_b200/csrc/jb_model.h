@@ -68,6 +68,7 @@ struct Workspace {
   int8_t* aq = nullptr;
   float* as = nullptr;
   // vision
+  float* head_t = nullptr;  // projection head: x A^T, [batch, rank] f32
   float* pixels = nullptr;
   void *patches = nullptr, *patch_out = nullptr, *pooled = nullptr;
 };
@@ -104,6 +105,9 @@ struct jb_model {
   void *cls = nullptr, *vpos = nullptr;
   float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
   std::vector<jb::ClipBlockW> clip_blocks;
+  // post-pool projection head: A [rank, H], B [H, rank] pre-scaled by alpha / rank
+  float *head_a = nullptr, *head_b = nullptr;
+  int head_rank = 0;
   // bookkeeping
   std::vector<void*> weight_allocs;
   int64_t weight_bytes = 0;
@@ -158,5 +162,9 @@ void run_graphed(jb_model* m, int kind, int batch, int seq, int pooling, cudaStr
                  const std::function<void(cudaStream_t)>& forward);
 // Drops every captured graph (their pointers die with the workspace).
 void clear_graphs(jb_model* m);
+// Installs (rank > 0) or removes the projection head; drops the workspace
+// (its layout depends on the rank) and the graphs.
+void set_projection_head(jb_model* m, const float* a, const float* b, int rank, double alpha);
+void load_projection_head(jb_model* m, const char* path, double alpha);
 
 }  // namespace jb

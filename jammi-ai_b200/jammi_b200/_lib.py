@@ -41,7 +41,8 @@ class ModelInfo(ctypes.Structure):
     _fields_ = [("family", ctypes.c_int32), ("format", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("hidden", ctypes.c_int32), ("output_dim", ctypes.c_int32), ("layers", ctypes.c_int32),
                 ("heads", ctypes.c_int32), ("ffn", ctypes.c_int32), ("max_seq", ctypes.c_int32),
-                ("image_size", ctypes.c_int32), ("weight_bytes", ctypes.c_int64)]
+                ("image_size", ctypes.c_int32), ("weight_bytes", ctypes.c_int64),
+                ("projection_rank", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 _lib = None
@@ -57,6 +58,8 @@ _SIGS = [
     ("jb_estimate_batch_bytes", ctypes.c_size_t, [_P, _I, _I]),
     ("jb_model_sync", _I, [_P, _P]),
     ("jb_model_profile_enable", _I, [_P, _I]),
+    ("jb_model_set_projection_head", _I, [_P, _P, _P, _I, ctypes.c_double]),
+    ("jb_model_load_projection_head", _I, [_P, ctypes.c_char_p, ctypes.c_double]),
     ("jb_model_profile_read", _I, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32)]),
     ("jb_encode_text", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     ("jb_encode_text_device", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),

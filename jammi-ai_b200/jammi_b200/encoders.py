@@ -52,11 +52,14 @@ class Model:
         check(lib().jb_model_load(weights_path.encode(), cfg.encode(), int(device),
                                   L.FORMATS[fmt], ctypes.byref(h)))
         self._h = h
-        info = L.ModelInfo()
-        check(lib().jb_model_get_info(self._h, ctypes.byref(info)))
-        self.info = info
+        self.info = self._info()
         self.device = device
         self.fmt = fmt
+
+    def _info(self):
+        info = L.ModelInfo()
+        check(lib().jb_model_get_info(self._h, ctypes.byref(info)))
+        return info
 
     @classmethod
     def from_weights(cls, weights: dict, config: dict, device: int = 0, fmt: str = "bf16"):
@@ -91,6 +94,24 @@ class Model:
 
     def sync(self, stream=None):
         check(lib().jb_model_sync(self._h, _stream_ptr(stream)))
+
+    def set_projection_head(self, lora_a, lora_b, lora_alpha: float):
+        """Install the post-pool projection head y = x + (alpha/rank) (x A^T) B^T
+        (``jb_model_set_projection_head``); ``lora_a`` [rank, H], ``lora_b`` [H, rank].
+        ``lora_a=None`` removes it."""
+        if lora_a is None:
+            check(lib().jb_model_set_projection_head(self._h, None, None, 0, float(lora_alpha)))
+        else:
+            a = np.ascontiguousarray(lora_a, dtype=np.float32)
+            b = np.ascontiguousarray(lora_b, dtype=np.float32)
+            check(lib().jb_model_set_projection_head(self._h, a.ctypes.data, b.ctypes.data,
+                                                     int(a.shape[0]), float(lora_alpha)))
+        self.info = self._info()
+
+    def load_projection_head(self, adapter_path: str, lora_alpha: float):
+        """``jb_model_load_projection_head``: from an adapter safetensors file."""
+        check(lib().jb_model_load_projection_head(self._h, str(adapter_path).encode(), float(lora_alpha)))
+        self.info = self._info()
 
     def profile_enable(self, on: bool = True):
         check(lib().jb_model_profile_enable(self._h, 1 if on else 0))

@@ -270,3 +270,16 @@ def random_token_batch(batch: int, seq: int, lengths, seed: int,
         ids[b, :n] = row
         mask[b, :n] = 1
     return ids, mask
+
+
+def projection_head(x, lora_a, lora_b, lora_alpha):
+    """Post-pool projection head of a fine-tuned embedding adapter: CandleModel
+    applies it to the pooled, L2-normalised embedding without re-normalising
+    (crates/jammi-ai/src/model/backend/candle.rs:823-829); load_projection_head
+    (candle.rs:1857-1892) builds a LoraLinear over an identity base with
+    scaling alpha / rank (crates/jammi-lora/src/lora_linear.rs:206-218), whose
+    inference forward is base(x) + scaling * (x @ A^T) @ B^T (lora_linear.rs:226-305)."""
+    x = np.asarray(x, dtype=np.float64)
+    a = np.asarray(lora_a, dtype=np.float64)
+    b = np.asarray(lora_b, dtype=np.float64)
+    return x + (lora_alpha / a.shape[0]) * ((x @ a.T) @ b.T)

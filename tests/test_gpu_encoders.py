@@ -267,3 +267,41 @@ def test_graphs_follow_workspace_growth():
     for _ in range(3):
         assert np.array_equal(model.encode(ids_s, lens_s), ref_small)
         assert np.array_equal(model.encode(ids_b, lens_b), ref_big)
+
+
+# ── post-pool projection head (row (f): fine-tuned embedding adapters) ─────────
+
+@pytest.mark.parametrize("fmt", ["f32", "bf16", "int8"])
+def test_projection_head_matches_oracle(fmt, tmp_path):
+    """LoraLinear over an identity base on the pooled embedding
+    (candle.rs:823-829, 1857-1892): set from arrays, loaded from an adapter
+    file, and removed again."""
+    from safetensors.numpy import save_file
+    cfg, w = _bert_base(631)
+    rng = np.random.default_rng(632)
+    lens = rng.integers(32, 97, size=12)  # the int8 workload's row lengths (U[32, ...])
+    ids, mask = ob.random_token_batch(12, 96, lens, seed=633)
+    fwd = oq.bert_int8_forward_hidden if fmt == "int8" else ob.bert_forward_hidden
+    pooled = ob.pool_and_normalize(fwd(w, cfg, ids, mask), mask)
+    rank, alpha = 8, 16.0
+    a = (rng.standard_normal((rank, 768)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal((768, rank)) * 0.05).astype(np.float32)
+    ref = ob.projection_head(pooled, a, b, alpha)
+    model = _bert(w, cfg.to_dict(), fmt)
+    plain = model.encode(ids, lens)
+    model.set_projection_head(a, b, alpha)
+    assert model.info.projection_rank == rank
+    assert_close_rows(model.encode(ids, lens), ref, fmt)
+    assert_close_rows(model.encode(ids, lens), ref, fmt)  # graph capture keeps the head
+    path = tmp_path / "adapter.safetensors"
+    save_file({"projection.lora_a": a, "projection.lora_b": b}, str(path))
+    model.set_projection_head(None, None, 0.0)
+    assert model.info.projection_rank == 0
+    assert np.array_equal(model.encode(ids, lens), plain)
+    model.load_projection_head(str(path), alpha)
+    assert_close_rows(model.encode(ids, lens), ref, fmt)
+    empty = tmp_path / "no_head.safetensors"
+    save_file({"other": np.zeros(4, np.float32)}, str(empty))
+    model.set_projection_head(None, None, 0.0)
+    model.load_projection_head(str(empty), alpha)  # the reference's Ok(None)
+    assert model.info.projection_rank == 0

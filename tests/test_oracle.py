@@ -162,3 +162,15 @@ def test_int8_bert_close_to_float():
     q = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
     cos = (ref * q).sum(1)
     assert np.all(cos > 0.999), cos
+
+
+def test_projection_head_oracle():
+    """LoraLinear over an identity base: x + (alpha/rank) (x A^T) B^T; a zero B
+    leaves the embedding unchanged (LoRA's standard init, lora_linear.rs)."""
+    x = np.array([[0.6, 0.8, 0.0], [1.0, 0.0, 0.0]])
+    a = np.array([[1.0, 0.0, 0.0], [0.0, 1.0, 0.0]])   # rank 2
+    b = np.array([[0.0, 1.0], [1.0, 0.0], [0.5, 0.5]])
+    y = ob.projection_head(x, a, b, lora_alpha=4.0)       # scaling 2
+    # x A^T = [[0.6, 0.8], [1, 0]]; (x A^T) B^T = [[0.8, 0.6, 0.7], [0, 1, 0.5]]
+    assert np.allclose(y, [[0.6 + 1.6, 0.8 + 1.2, 1.4], [1.0, 2.0, 1.0]])
+    assert np.array_equal(ob.projection_head(x, a, np.zeros_like(b), 8.0), x)
