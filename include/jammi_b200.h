@@ -56,6 +56,10 @@ typedef enum {
 } jb_pooling;
 
 typedef enum { JB_FAMILY_BERT = 0, JB_FAMILY_CLIP_VISION = 1 } jb_family;
+/* BERT-family text encoders sharing one forward: BERT (crates/jammi-encoders/src/bert.rs)
+ * and DistilBERT (crates/jammi-encoders/src/distilbert.rs: no token-type table,
+ * config keys dim / n_layers / n_heads / hidden_dim, weights under "distilbert."). */
+typedef enum { JB_TEXT_BERT = 0, JB_TEXT_DISTILBERT = 1 } jb_text_variant;
 
 typedef struct jb_model jb_model;
 
@@ -72,7 +76,7 @@ typedef struct {
   int32_t image_size;      /* ViT only */
   int64_t weight_bytes;    /* device bytes held by the weights */
   int32_t projection_rank; /* rank of the installed projection head, 0 if none */
-  int32_t reserved;
+  int32_t variant;         /* text family: jb_text_variant */
 } jb_model_info;
 
 /* ── lifecycle ─────────────────────────────────────────────────────────── */

@@ -103,6 +103,7 @@ jb_status jb_model_get_info(const jb_model* m, jb_model_info* out) {
     out->image_size = m->image_size;
     out->weight_bytes = m->weight_bytes;
     out->projection_rank = m->head_rank;
+    out->variant = m->variant;
   });
 }
 

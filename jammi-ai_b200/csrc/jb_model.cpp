@@ -280,44 +280,71 @@ int linear_dtype(int format) {
   return format == JB_FMT_F32 ? JB_DT_F32 : (format == JB_FMT_INT8 ? JB_DT_S8 : JB_DT_BF16);
 }
 
+// BERT and DistilBERT share the forward (post-LN encoder, exact-erf GELU,
+// additive mask); DistilBERT (crates/jammi-encoders/src/distilbert.rs:1-13)
+// has no token-type table and its own config and weight names.
+struct TextNames {
+  std::string prefix, type_table, layer, q, k, v, o, ln1, ffn1, ffn2, ln2;
+};
+
 void load_bert(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->family = JB_FAMILY_BERT;
-  m->hidden = static_cast<int>(cfg.num_or("hidden_size", 0));
-  m->layers = static_cast<int>(cfg.num_or("num_hidden_layers", 0));
-  m->heads = static_cast<int>(cfg.num_or("num_attention_heads", 0));
-  m->ffn = static_cast<int>(cfg.num_or("intermediate_size", 0));
+  const bool distil = cfg.str_or("model_type", "") == "distilbert" ||
+                      (cfg.get("dim") && cfg.get("n_layers"));
+  m->variant = distil ? JB_TEXT_DISTILBERT : JB_TEXT_BERT;
+  TextNames nm;
+  if (distil) {  // DistilBertConfig (distilbert.rs:32-57), weights under "distilbert."
+    m->hidden = static_cast<int>(cfg.num_or("dim", 0));
+    m->layers = static_cast<int>(cfg.num_or("n_layers", 0));
+    m->heads = static_cast<int>(cfg.num_or("n_heads", 0));
+    m->ffn = static_cast<int>(cfg.num_or("hidden_dim", 0));
+    m->type_vocab = 0;
+    nm = {"distilbert.", "", "transformer.layer.", "attention.q_lin", "attention.k_lin",
+          "attention.v_lin", "attention.out_lin", "sa_layer_norm", "ffn.lin1", "ffn.lin2",
+          "output_layer_norm"};
+  } else {
+    m->hidden = static_cast<int>(cfg.num_or("hidden_size", 0));
+    m->layers = static_cast<int>(cfg.num_or("num_hidden_layers", 0));
+    m->heads = static_cast<int>(cfg.num_or("num_attention_heads", 0));
+    m->ffn = static_cast<int>(cfg.num_or("intermediate_size", 0));
+    m->type_vocab = static_cast<int>(cfg.num_or("type_vocab_size", 2));
+    // the "bert." prefix probe of BertBuilder::build (bert.rs:508-517)
+    nm = {st.has("bert.embeddings.word_embeddings.weight") ? "bert." : "",
+          "embeddings.token_type_embeddings.weight", "encoder.layer.", "attention.self.query",
+          "attention.self.key", "attention.self.value", "attention.output.dense",
+          "attention.output.LayerNorm", "intermediate.dense", "output.dense", "output.LayerNorm"};
+  }
   m->vocab = static_cast<int>(cfg.num_or("vocab_size", 0));
   m->max_pos = static_cast<int>(cfg.num_or("max_position_embeddings", 0));
-  m->type_vocab = static_cast<int>(cfg.num_or("type_vocab_size", 2));
   m->eps = static_cast<float>(cfg.num_or("layer_norm_eps", 1e-12));
   const int H = m->hidden, F = m->ffn;
   if (H <= 0 || m->layers <= 0 || m->heads <= 0 || F <= 0 || m->vocab <= 0 || m->max_pos <= 0 ||
       H % m->heads)
-    fail(JB_ERR_INVALID, "config.json: incomplete or inconsistent BERT dimensions");
+    fail(JB_ERR_INVALID, "config.json: incomplete or inconsistent encoder dimensions");
   if (H > 1024 || H % 8) fail(JB_ERR_INVALID, "hidden_size must be a multiple of 8 and <= 1024");
-  // the "bert." prefix probe of BertBuilder::build (bert.rs:508-517)
-  const std::string p = st.has("bert.embeddings.word_embeddings.weight") ? "bert." : "";
+  const std::string& p = nm.prefix;
   m->word = upload_act(m, st.f32(p + "embeddings.word_embeddings.weight", int64_t(m->vocab) * H));
   m->pos = upload_act(m, st.f32(p + "embeddings.position_embeddings.weight", int64_t(m->max_pos) * H));
-  auto tt = st.f32(p + "embeddings.token_type_embeddings.weight", int64_t(m->type_vocab) * H);
-  tt.resize(H);  // token_type_ids are all zero (bert.rs:269)
+  std::vector<float> tt(H, 0.f);  // token_type_ids are all zero (bert.rs:269); none in DistilBERT
+  if (!nm.type_table.empty()) {
+    tt = st.f32(p + nm.type_table, int64_t(m->type_vocab) * H);
+    tt.resize(H);
+  }
   m->type0 = upload_act(m, tt);
   m->emb_ln_g = upload_f32(m, st.f32_or(p + "embeddings.LayerNorm.weight", H, 1.f));
   m->emb_ln_b = upload_f32(m, st.f32_or(p + "embeddings.LayerNorm.bias", H, 0.f));
   const int ld = linear_dtype(m->format);
   for (int l = 0; l < m->layers; ++l) {
-    const std::string q = p + "encoder.layer." + std::to_string(l) + ".";
+    const std::string q = p + nm.layer + std::to_string(l) + ".";
     BertLayerW w;
-    w.qkv = load_linear(m, st,
-                        {q + "attention.self.query", q + "attention.self.key", q + "attention.self.value"},
-                        {H, H, H}, H, true, ld);
-    w.o = load_linear(m, st, {q + "attention.output.dense"}, {H}, H, true, ld);
-    w.ffn1 = load_linear(m, st, {q + "intermediate.dense"}, {F}, H, true, ld);
-    w.ffn2 = load_linear(m, st, {q + "output.dense"}, {H}, F, true, ld);
-    w.ln1_g = upload_f32(m, st.f32_or(q + "attention.output.LayerNorm.weight", H, 1.f));
-    w.ln1_b = upload_f32(m, st.f32_or(q + "attention.output.LayerNorm.bias", H, 0.f));
-    w.ln2_g = upload_f32(m, st.f32_or(q + "output.LayerNorm.weight", H, 1.f));
-    w.ln2_b = upload_f32(m, st.f32_or(q + "output.LayerNorm.bias", H, 0.f));
+    w.qkv = load_linear(m, st, {q + nm.q, q + nm.k, q + nm.v}, {H, H, H}, H, true, ld);
+    w.o = load_linear(m, st, {q + nm.o}, {H}, H, true, ld);
+    w.ffn1 = load_linear(m, st, {q + nm.ffn1}, {F}, H, true, ld);
+    w.ffn2 = load_linear(m, st, {q + nm.ffn2}, {H}, F, true, ld);
+    w.ln1_g = upload_f32(m, st.f32_or(q + nm.ln1 + ".weight", H, 1.f));
+    w.ln1_b = upload_f32(m, st.f32_or(q + nm.ln1 + ".bias", H, 0.f));
+    w.ln2_g = upload_f32(m, st.f32_or(q + nm.ln2 + ".weight", H, 1.f));
+    w.ln2_b = upload_f32(m, st.f32_or(q + nm.ln2 + ".bias", H, 0.f));
     m->bert_layers.push_back(w);
   }
 }

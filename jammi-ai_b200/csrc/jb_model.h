@@ -88,6 +88,7 @@ struct GraphEntry {
 
 struct jb_model {
   int family = JB_FAMILY_BERT;
+  int variant = JB_TEXT_BERT;  // text family: BERT or DistilBERT weights / config
   int format = JB_FMT_BF16;
   int device = 0;
   int act = JB_DT_BF16;  // activation storage dtype

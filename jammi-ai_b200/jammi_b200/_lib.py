@@ -25,6 +25,7 @@ DT_F32, DT_BF16, DT_S8, DT_S32 = 0, 1, 2, 3
 EPI_NONE, EPI_GELU, EPI_QUICK_GELU, EPI_RESIDUAL = 0, 1, 2, 3
 # jb_family
 FAMILY_BERT, FAMILY_CLIP_VISION = 0, 1
+TEXT_BERT, TEXT_DISTILBERT = 0, 1
 
 
 class JbError(RuntimeError):
@@ -42,7 +43,7 @@ class ModelInfo(ctypes.Structure):
                 ("hidden", ctypes.c_int32), ("output_dim", ctypes.c_int32), ("layers", ctypes.c_int32),
                 ("heads", ctypes.c_int32), ("ffn", ctypes.c_int32), ("max_seq", ctypes.c_int32),
                 ("image_size", ctypes.c_int32), ("weight_bytes", ctypes.c_int64),
-                ("projection_rank", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("projection_rank", ctypes.c_int32), ("variant", ctypes.c_int32)]
 
 
 _lib = None

@@ -283,3 +283,53 @@ def projection_head(x, lora_a, lora_b, lora_alpha):
     a = np.asarray(lora_a, dtype=np.float64)
     b = np.asarray(lora_b, dtype=np.float64)
     return x + (lora_alpha / a.shape[0]) * ((x @ a.T) @ b.T)
+
+
+# ── DistilBERT ───────────────────────────────────────────────────────────────
+# crates/jammi-encoders/src/distilbert.rs: the same post-LN encoder as BERT
+# (embeddings :69-77 word + position then LayerNorm, no token-type table;
+# attention :104-128 with the same additive mask; FFN :137-141 lin1 ->
+# gelu_erf -> lin2; layer :152-162 residual then LayerNorm; forward_hidden
+# :203-222), under its own config keys and weight names.
+DISTILBERT_LAYER_NAMES = {  # DistilBERT module -> the BERT module computing the same op
+    "attention.q_lin": "attention.self.query", "attention.k_lin": "attention.self.key",
+    "attention.v_lin": "attention.self.value", "attention.out_lin": "attention.output.dense",
+    "sa_layer_norm": "attention.output.LayerNorm", "ffn.lin1": "intermediate.dense",
+    "ffn.lin2": "output.dense", "output_layer_norm": "output.LayerNorm",
+}
+
+
+def distilbert_config(d: dict) -> BertConfig:
+    """``DistilBertConfig`` (distilbert.rs:32-57): dim / n_layers / n_heads /
+    hidden_dim, layer_norm_eps default 1e-12, no token types."""
+    return BertConfig(hidden_size=int(d["dim"]), num_hidden_layers=int(d["n_layers"]),
+                      num_attention_heads=int(d["n_heads"]), intermediate_size=int(d["hidden_dim"]),
+                      vocab_size=int(d["vocab_size"]),
+                      max_position_embeddings=int(d["max_position_embeddings"]),
+                      type_vocab_size=1, layer_norm_eps=float(d.get("layer_norm_eps", 1e-12)))
+
+
+def distilbert_as_bert(weights: dict, d_cfg: dict):
+    """DistilBERT weights (``distilbert.`` prefix, distilbert.rs:440) renamed onto
+    the BERT modules that compute the same ops, with an all-zero token-type row
+    (DistilBERT adds none): ``(bert_weights, BertConfig)``."""
+    cfg = distilbert_config(d_cfg)
+    w = {}
+    for k, v in weights.items():
+        k = k[len("distilbert."):] if k.startswith("distilbert.") else k
+        if k.startswith("transformer.layer."):
+            n, rest = k[len("transformer.layer."):].split(".", 1)
+            for a, b in DISTILBERT_LAYER_NAMES.items():
+                if rest.startswith(a + "."):
+                    rest = b + rest[len(a):]
+                    break
+            k = f"encoder.layer.{n}.{rest}"
+        w[k] = v
+    w["embeddings.token_type_embeddings.weight"] = np.zeros((1, cfg.hidden_size))
+    return w, cfg
+
+
+def distilbert_forward_hidden(weights: dict, d_cfg: dict, input_ids, mask, dtype=np.float64):
+    """``DistilBert::forward_hidden`` (distilbert.rs:203-222) -> ``[B, S, H]``."""
+    w, cfg = distilbert_as_bert(weights, d_cfg)
+    return bert_forward_hidden(w, cfg, input_ids, mask, dtype=dtype)

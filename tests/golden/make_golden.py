@@ -20,6 +20,10 @@ Fixtures (``.npz``, weights included so the GPU tests need nothing else):
 * ``tiny_clip_gap.npz`` / ``tiny_clip_cls.npz``  OpenCLIP ViT W 32, 1 layer,
   4 heads, patch 4, image 8, embed 16 (the shape of the reference's
   ``tests/fixtures/tiny_open_clip``), global-average and CLS pooling.
+* ``small_distilbert.npz``  DistilBERT (HF ``DistilBertModel``) H 64, 2 layers, 4 heads,
+  FFN 256: the BERT weight recipe under DistilBERT names (``distilbert.`` prefix,
+  ``transformer.layer.N.{attention.q_lin, ..., ffn.lin1, output_layer_norm}``) and no
+  token-type table (``crates/jammi-encoders/src/distilbert.rs``).
 * ``reference_tiny_bert.npz`` outputs of the reference's own committed
   ``tiny_bert`` fixture (weights are NOT copied: its sha256 is stored and the
   CPU test re-reads the fixture when the reference checkout is present).
@@ -105,6 +109,75 @@ def bert_fixture(name, cfg: BertConfig, seed, lens, S, prefix=""):
     arrs = {"w::" + k: v for k, v in w.items()}
     arrs.update({"ids": ids, "mask": mask, "hidden": hidden,
                  "config_json": np.frombuffer(json.dumps(cfg.to_dict()).encode(), dtype=np.uint8)})
+    arrs.update({"pooled_" + k: v.numpy() for k, v in pooled.items()})
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, {k: v.shape for k, v in arrs.items() if not k.startswith("w::")})
+
+
+DISTIL_NAMES = {  # BERT recipe name -> DistilBERT name (distilbert.rs:440-545)
+    "attention.self.query": "attention.q_lin", "attention.self.key": "attention.k_lin",
+    "attention.self.value": "attention.v_lin", "attention.output.dense": "attention.out_lin",
+    "attention.output.LayerNorm": "sa_layer_norm", "intermediate.dense": "ffn.lin1",
+    "output.dense": "ffn.lin2", "output.LayerNorm": "output_layer_norm",
+}
+
+
+def distil_weights(cfg: BertConfig, seed) -> dict:
+    """The BERT weight recipe under DistilBERT names (prefix ``distilbert.``,
+    ``transformer.layer.N``), without the token-type table."""
+    out = {}
+    for k, v in random_bert_weights(cfg, seed).items():
+        if "token_type_embeddings" in k:
+            continue
+        if k.startswith("encoder.layer."):
+            n, rest = k[len("encoder.layer."):].split(".", 1)
+            for a, b in DISTIL_NAMES.items():
+                if rest.startswith(a + "."):
+                    rest = b + rest[len(a):]
+                    break
+            k = f"transformer.layer.{n}.{rest}"
+        out["distilbert." + k] = v
+    return out
+
+
+def hf_distilbert_hidden(weights: dict, cfg: BertConfig, ids, mask) -> np.ndarray:
+    from transformers import DistilBertConfig, DistilBertModel
+    hcfg = DistilBertConfig(vocab_size=cfg.vocab_size, dim=cfg.hidden_size,
+                            n_layers=cfg.num_hidden_layers, n_heads=cfg.num_attention_heads,
+                            hidden_dim=cfg.intermediate_size, activation="gelu", dropout=0.0,
+                            attention_dropout=0.0,
+                            max_position_embeddings=cfg.max_position_embeddings,
+                            sinusoidal_pos_embds=False)
+    hcfg._attn_implementation = "eager"
+    model = DistilBertModel(hcfg).eval().to(torch.float64)
+    sd = {k[len("distilbert."):]: torch.from_numpy(np.asarray(v, dtype=np.float64))
+          for k, v in weights.items()}
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [k for k in missing if not k.endswith("position_ids")]
+    assert not missing and not unexpected, (missing, unexpected)
+    with torch.no_grad():
+        out = model(input_ids=torch.from_numpy(ids.astype(np.int64)),
+                    attention_mask=torch.from_numpy(mask.astype(np.int64)))
+    return out.last_hidden_state.numpy()
+
+
+def distilbert_fixture(name, cfg: BertConfig, seed, lens, S):
+    w = distil_weights(cfg, seed)
+    rng = np.random.default_rng(seed + 1)
+    B = len(lens)
+    ids = np.zeros((B, S), dtype=np.uint32)
+    mask = np.zeros((B, S), dtype=np.uint32)
+    for b, n in enumerate(lens):
+        ids[b, :n] = rng.integers(1, cfg.vocab_size, size=n)
+        mask[b, :n] = 1
+    hidden = hf_distilbert_hidden(w, cfg, ids, mask)
+    pooled = torch_pool_all(torch.from_numpy(hidden), torch.from_numpy(mask.astype(np.int64)))
+    dcfg = {"model_type": "distilbert", "dim": cfg.hidden_size, "n_layers": cfg.num_hidden_layers,
+            "n_heads": cfg.num_attention_heads, "hidden_dim": cfg.intermediate_size,
+            "vocab_size": cfg.vocab_size, "max_position_embeddings": cfg.max_position_embeddings}
+    arrs = {"w::" + k: v for k, v in w.items()}
+    arrs.update({"ids": ids, "mask": mask, "hidden": hidden,
+                 "config_json": np.frombuffer(json.dumps(dcfg).encode(), dtype=np.uint8)})
     arrs.update({"pooled_" + k: v.numpy() for k, v in pooled.items()})
     np.savez_compressed(os.path.join(HERE, name), **arrs)
     print("wrote", name, {k: v.shape for k, v in arrs.items() if not k.startswith("w::")})
@@ -212,6 +285,9 @@ def main():
     c2 = ClipVisionConfig(width=32, layers=2, heads=4, mlp_ratio=4.0, image_size=8,
                           patch_size=4, embed_dim=16, global_average_pool=False)
     clip_fixture("tiny_clip_cls.npz", c2, seed=8, batch=3)
+    distil = BertConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                        intermediate_size=256, vocab_size=512, max_position_embeddings=64)
+    distilbert_fixture("small_distilbert.npz", distil, seed=321, lens=[64, 17, 1, 0, 40], S=64)
     reference_fixture()
 
 

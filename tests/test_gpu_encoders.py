@@ -75,6 +75,27 @@ def test_bert_golden_all_poolings(name, fmt):
     assert np.all(out[lens == 0] == 0)
 
 
+@pytest.mark.parametrize("fmt", ["f32", "bf16", "int8"])
+def test_distilbert_golden(fmt):
+    """DistilBERT weights and config (distilbert.rs) through the same forward,
+    against HF DistilBertModel (f32 / bf16) or the int8 oracle."""
+    from jammi_b200 import Bert
+    from jammi_b200._lib import TEXT_DISTILBERT
+    w, g = load_golden("small_distilbert.npz")
+    d_cfg = json.loads(bytes(g["config_json"]).decode())
+    ids, mask = g["ids"], g["mask"]
+    lens = mask.sum(1)
+    model = Bert.from_weights(w, d_cfg, device=0, fmt=fmt, pooling="mean")
+    assert model.info.variant == TEXT_DISTILBERT
+    out = model.encode(ids, lens)
+    if fmt == "int8":  # the int8 oracle over the same weights, renamed onto BERT
+        bw, cfg = ob.distilbert_as_bert(w, d_cfg)
+        ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(bw, cfg, ids, mask), mask)
+    else:
+        ref = g["pooled_mean"]
+    assert_close_rows(out, ref, fmt)
+
+
 def test_bert_forward_hidden_golden():
     w, g = load_golden("tiny_bert_seeded.npz")
     cfg = json.loads(bytes(g["config_json"]).decode())

@@ -96,6 +96,19 @@ def test_bert_oracle_matches_golden(name):
         np.testing.assert_allclose(out[rows], g["pooled_" + pname][rows], atol=1e-9, rtol=0)
 
 
+def test_distilbert_oracle_matches_golden():
+    w, g = load_golden("small_distilbert.npz")
+    d_cfg = json.loads(bytes(g["config_json"]).decode())
+    valid = g["mask"].astype(bool)
+    h64 = ob.distilbert_forward_hidden(w, d_cfg, g["ids"], g["mask"])
+    np.testing.assert_allclose(h64[valid], g["hidden"][valid], atol=1e-9, rtol=0)
+    nonempty = g["mask"].sum(1) > 0
+    for pname, pid in ob.POOLING_NAMES.items():
+        out = ob.pool_and_normalize(h64, g["mask"], pid)
+        rows = nonempty if pid == ob.POOL_CLS else slice(None)
+        np.testing.assert_allclose(out[rows], g["pooled_" + pname][rows], atol=1e-9, rtol=0)
+
+
 def test_bert_oracle_on_reference_fixture():
     z = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert.npz"))
     st = os.path.join(REF_FIXTURE, "model.safetensors")
