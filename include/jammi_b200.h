@@ -233,6 +233,36 @@ jb_status jb_model_set_projection_head(jb_model* model, const float* lora_a, con
 jb_status jb_model_load_projection_head(jb_model* model, const char* adapter_path,
                                         double lora_alpha);
 
+/* ── LoRA adapters inside the encoder linears ────────────────────────────
+ * An encoder adapter (SavedAdapter::EncoderAdapters, crates/jammi-ai/src/
+ * fine_tune/target.rs:221-230) wraps a layer's linears in LoraLinear
+ * (crates/jammi-lora/src/lora_linear.rs:226-305, sites built by LoraSite::build,
+ * crates/jammi-encoders/src/bert.rs:590-640 and distilbert.rs):
+ *   y = base(x) + scaling * (x A^T) B^T,
+ * scaling = lora_alpha / rank, or lora_alpha / sqrt(rank) with use_rslora.
+ * The FFN-in site adds before the GELU.  f32 and bf16 formats only (an int8
+ * model answers JB_ERR_INVALID); text (BERT / DistilBERT) models only. */
+typedef enum {
+  JB_LORA_QUERY = 0,     /* query    | q_lin   */
+  JB_LORA_KEY = 1,       /* key      | k_lin   */
+  JB_LORA_VALUE = 2,     /* value    | v_lin   */
+  JB_LORA_ATTN_OUT = 3,  /* dense    | out_lin */
+  JB_LORA_FFN_IN = 4,    /* intermediate_dense | lin1 */
+  JB_LORA_FFN_OUT = 5    /* output_dense       | lin2 */
+} jb_lora_site;
+/* Install (rank > 0) or remove (rank 0) the adapter of one site of one layer.
+ * lora_a [rank, in_features], lora_b [out_features, rank], f32 host arrays;
+ * `scaling` multiplies (x A^T) B^T as given. */
+jb_status jb_model_set_lora(jb_model* model, int layer, int site, const float* lora_a,
+                            const float* lora_b, int rank, double scaling);
+/* Every adapter of an adapter.safetensors file: keys
+ * "layer.{n}.{module}.lora_a" / ".lora_b" (bert.rs:299-346, distilbert.rs:
+ * 245-296; module names per the site enum above), rank from lora_a's rows.
+ * *n_sites (may be NULL) receives the number of sites installed; a file with
+ * none installs nothing and returns JB_OK. */
+jb_status jb_model_load_lora(jb_model* model, const char* adapter_path, double lora_alpha,
+                             int use_rslora, int* n_sites);
+
 /* ── memory-budget admission ──────────────────────────────────────────────
  * GpuScheduler (crates/jammi-ai/src/concurrency/gpu_scheduler.rs:11-218):
  * budget = total * (1 - headroom_fraction); reservations by compare-and-swap;

@@ -126,6 +126,27 @@ jb_status jb_model_load_projection_head(jb_model* m, const char* adapter_path, d
   });
 }
 
+jb_status jb_model_set_lora(jb_model* m, int layer, int site, const float* lora_a,
+                            const float* lora_b, int rank, double scaling) {
+  return guarded([&] {
+    if (!m) jb::fail(JB_ERR_INVALID, "null model");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    jb::set_lora(m, layer, site, lora_a, lora_b, rank, scaling);
+  });
+}
+
+jb_status jb_model_load_lora(jb_model* m, const char* adapter_path, double lora_alpha,
+                             int use_rslora, int* n_sites) {
+  return guarded([&] {
+    if (!m || !adapter_path) jb::fail(JB_ERR_INVALID, "null argument");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    const int n = jb::load_lora(m, adapter_path, lora_alpha, use_rslora != 0);
+    if (n_sites) *n_sites = n;
+  });
+}
+
 size_t jb_estimate_batch_bytes(const jb_model* m, int batch, int seq) {
   if (!m || batch < 0 || seq < 0) return 0;
   return jb::estimate_batch_bytes(m, batch, seq);

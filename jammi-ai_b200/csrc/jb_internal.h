@@ -114,6 +114,9 @@ cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* b
 cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s);
 // Row-wise x / clamp(||x||, 1e-12) over f32 [rows, cols], in place.
 cudaError_t launch_l2_rows(float* x, int rows, int cols, cudaStream_t s);
+// x = gelu_erf(x) in place over rows < *drows (drows may be null).
+cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int cols,
+                             cudaStream_t s);
 
 int num_sms(int device);
 

@@ -479,6 +479,23 @@ __global__ void __launch_bounds__(kGeluQThreads, 1)
   }
 }
 
+// ── elementwise exact-erf GELU, in place ──────────────────────────────────
+// Rows < *drows of x [rows, cols] (cols a multiple of the 16-byte vector).
+template <typename T>
+__global__ void __launch_bounds__(256) gelu_rows_kernel(T* x, int rows, const int* drows, int cols) {
+  constexpr int VN = Vec<T>::N;
+  const int R = drows ? min(*drows, rows) : rows;
+  const size_t nv = static_cast<size_t>(R) * (cols / VN);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float v[VN];
+    Vec<T>::load(x + i * VN, v);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) v[e] = gelu_erf(v[e]);
+    Vec<T>::store(x + i * VN, v);
+  }
+}
+
 // ── pooling + L2 (pooling.rs:31-148) ──────────────────────────────────────
 constexpr int kPoolThreads = 128;
 
@@ -893,6 +910,22 @@ cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* sca
     return launch_quantize_act<JB_EPI_GELU>(x, dtype, q, scale, rows, drows, cols, s);
   if (activation != JB_EPI_NONE) return cudaErrorInvalidValue;
   return launch_quantize_act<JB_EPI_NONE>(x, dtype, q, scale, rows, drows, cols, s);
+}
+
+cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int cols,
+                             cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned grid = static_cast<unsigned>(num_sms(dev)) * 8u;
+  if (dtype == JB_DT_BF16) {
+    if (cols % 8) return cudaErrorInvalidValue;
+    gelu_rows_kernel<bf16><<<grid, 256, 0, s>>>(static_cast<bf16*>(x), rows, drows, cols);
+  } else {
+    if (cols % 4) return cudaErrorInvalidValue;
+    gelu_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(x), rows, drows, cols);
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,

@@ -422,10 +422,11 @@ size_t esz(int dt) { return dt == JB_DT_F32 ? 4 : 2; }
 // Sizes of every workspace buffer for (batch, seq); shared by the allocator
 // and jb_estimate_batch_bytes.
 struct WsPlan {
-  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, head_t, pixels, patches, patch_out, pooled;
+  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, head_t, lora_t, pixels, patches, patch_out,
+      pooled;
   size_t sum() const {
-    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + head_t + pixels + patches +
-           patch_out +
+    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + head_t + lora_t + pixels +
+           patches + patch_out +
            pooled;
   }
 };
@@ -443,6 +444,7 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
   p.qkv = round_up(T * 3 * H * e);
   p.hf = round_up(T * F * e);
   p.head_t = m->head_rank > 0 ? round_up(B * m->head_rank * 4) : 0;
+  p.lora_t = m->lora_width > 0 ? round_up(T * m->lora_width * e) : 0;
   if (m->format == JB_FMT_INT8) {
     p.aq = round_up(T * std::max(H, F));
     p.as = round_up(T * 4);
@@ -504,6 +506,7 @@ void ensure_workspace(jb_model* m, int batch, int seq) {
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
   ws.head_t = static_cast<float*>(take(p.head_t));
+  ws.lora_t = take(p.lora_t);
   ws.pixels = static_cast<float*>(take(p.pixels));
   ws.patches = take(p.patches);
   ws.patch_out = take(p.patch_out);
@@ -538,6 +541,7 @@ Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq)
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
   ws.head_t = static_cast<float*>(take(p.head_t));
+  ws.lora_t = take(p.lora_t);
   ws.pixels = static_cast<float*>(take(p.pixels));
   ws.patches = take(p.patches);
   ws.patch_out = take(p.patch_out);
@@ -751,6 +755,128 @@ void set_projection_head(jb_model* m, const float* a, const float* b, int rank, 
   m->head_rank = rank;
 }
 
+namespace {
+// Frees a device matrix that upload_* allocated for this model.
+void drop_dev(jb_model* m, void*& p, size_t bytes) {
+  if (!p) return;
+  cudaFree(p);
+  m->weight_allocs.erase(std::remove(m->weight_allocs.begin(), m->weight_allocs.end(), p),
+                         m->weight_allocs.end());
+  m->weight_bytes -= static_cast<int64_t>(bytes);
+  p = nullptr;
+}
+size_t linear_bytes(const jb_model* m, const Linear& L) {
+  return static_cast<size_t>(L.N) * L.K * (m->act == JB_DT_F32 ? 4 : 2);
+}
+int pad8(int r) { return (r + 7) / 8 * 8; }
+
+// A [Rp, in] stacking the sites' A rows (zeros after), B [sum(out), Rp]
+// block-diagonal with each site's scaling folded in; Linear in the activation
+// dtype (w == nullptr when every site has rank 0).
+void build_fused(jb_model* m, const LoraSiteHost* const* sites, const int* outs, int n, int in,
+                 Linear& A, Linear& B) {
+  drop_dev(m, A.w, linear_bytes(m, A));
+  drop_dev(m, B.w, linear_bytes(m, B));
+  A = Linear();
+  B = Linear();
+  int R = 0, O = 0;
+  for (int i = 0; i < n; ++i) {
+    R += sites[i]->rank;
+    O += outs[i];
+  }
+  if (R == 0) return;
+  const int Rp = pad8(R);
+  std::vector<float> a(static_cast<size_t>(Rp) * in, 0.f), b(static_cast<size_t>(O) * Rp, 0.f);
+  int r0 = 0, o0 = 0;
+  for (int i = 0; i < n; ++i) {
+    const LoraSiteHost& st = *sites[i];
+    for (int r = 0; r < st.rank; ++r)
+      std::copy(st.a.begin() + static_cast<size_t>(r) * in, st.a.begin() + static_cast<size_t>(r + 1) * in,
+                a.begin() + static_cast<size_t>(r0 + r) * in);
+    for (int o = 0; o < outs[i] && st.rank; ++o)
+      for (int r = 0; r < st.rank; ++r)
+        b[static_cast<size_t>(o0 + o) * Rp + r0 + r] =
+            static_cast<float>(st.b[static_cast<size_t>(o) * st.rank + r] * st.scaling);
+    r0 += st.rank;
+    o0 += outs[i];
+  }
+  A.w = upload_act(m, a);
+  A.dtype = m->act;
+  A.N = Rp;
+  A.K = in;
+  B.w = upload_act(m, b);
+  B.dtype = m->act;
+  B.N = O;
+  B.K = Rp;
+}
+}  // namespace
+
+void set_lora(jb_model* m, int layer, int site, const float* a, const float* b, int rank,
+              double scaling) {
+  if (m->family != JB_FAMILY_BERT) fail(JB_ERR_INVALID, "LoRA adapters apply to text encoders");
+  if (m->format == JB_FMT_INT8)
+    fail(JB_ERR_INVALID, "LoRA adapters run in the f32 and bf16 formats");
+  if (layer < 0 || layer >= m->layers || site < 0 || site >= kLoraSites || rank < 0 ||
+      (rank > 0 && (!a || !b)))
+    fail(JB_ERR_INVALID, "LoRA: bad layer, site or rank");
+  const int H = m->hidden, F = m->ffn;
+  const int in[kLoraSites] = {H, H, H, H, H, F};
+  const int out[kLoraSites] = {H, H, H, H, F, H};
+  cudaDeviceSynchronize();  // no forward may still read the old matrices or workspace
+  clear_graphs(m);
+  free_workspace(m->ws);
+  if (m->lora.empty()) m->lora.resize(m->layers);
+  LoraLayerW& L = m->lora[layer];
+  LoraSiteHost& st = L.site[site];
+  st.rank = rank;
+  st.scaling = scaling;
+  st.a.assign(a ? a : nullptr, a ? a + static_cast<size_t>(rank) * in[site] : nullptr);
+  st.b.assign(b ? b : nullptr, b ? b + static_cast<size_t>(out[site]) * rank : nullptr);
+  if (site < 3) {
+    const LoraSiteHost* qkv[3] = {&L.site[0], &L.site[1], &L.site[2]};
+    const int outs[3] = {H, H, H};
+    build_fused(m, qkv, outs, 3, H, L.a_qkv, L.b_qkv);
+  } else {
+    const LoraSiteHost* one[1] = {&st};
+    const int outs[1] = {out[site]};
+    Linear& A = site == 3 ? L.a_o : site == 4 ? L.a_1 : L.a_2;
+    Linear& B = site == 3 ? L.b_o : site == 4 ? L.b_1 : L.b_2;
+    build_fused(m, one, outs, 1, in[site], A, B);
+  }
+  m->lora_width = 0;
+  for (const LoraLayerW& l : m->lora)
+    for (const Linear* A : {&l.a_qkv, &l.a_o, &l.a_1, &l.a_2}) m->lora_width = std::max(m->lora_width, A->N);
+}
+
+int load_lora(jb_model* m, const char* path, double alpha, bool rslora) {
+  // Adapter keys: layer.{n}.{module}.lora_a / .lora_b (bert.rs:299-346,
+  // distilbert.rs:245-296), sites in the order query, key, value, attention
+  // output, FFN in, FFN out.
+  static const char* kBertSites[kLoraSites] = {"query", "key", "value", "dense",
+                                                "intermediate_dense", "output_dense"};
+  static const char* kDistilSites[kLoraSites] = {"q_lin", "k_lin", "v_lin", "out_lin", "lin1", "lin2"};
+  const char* const* kSites = m->variant == JB_TEXT_DISTILBERT ? kDistilSites : kBertSites;
+  SafeTensors st(path);
+  int n = 0;
+  for (int l = 0; l < m->layers; ++l)
+    for (int s = 0; s < kLoraSites; ++s) {
+      const std::string k = "layer." + std::to_string(l) + "." + kSites[s];
+      if (!st.has(k + ".lora_a") || !st.has(k + ".lora_b")) continue;
+      const StTensor& ta = st.get(k + ".lora_a");
+      if (ta.shape.size() != 2) fail(JB_ERR_IO, k + ".lora_a must be [rank, in]");
+      const int rank = static_cast<int>(ta.shape[0]);
+      const int64_t in = ta.shape[1];
+      const int64_t outd = (s == 4 ? m->ffn : m->hidden);
+      if (in != (s == 5 ? m->ffn : m->hidden)) fail(JB_ERR_IO, k + ".lora_a has the wrong width");
+      const std::vector<float> a = st.f32(k + ".lora_a", rank * in);
+      const std::vector<float> b = st.f32(k + ".lora_b", rank * outd);
+      const double scaling = rslora ? alpha / std::sqrt(static_cast<double>(rank)) : alpha / rank;
+      set_lora(m, l, s, a.data(), b.data(), rank, scaling);
+      ++n;
+    }
+  return n;
+}
+
 void load_projection_head(jb_model* m, const char* path, double alpha) {
   SafeTensors st(path);
   if (!st.has("projection.lora_a") || !st.has("projection.lora_b")) return;  // Ok(None)
@@ -854,9 +980,19 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
   ea.eps = m->eps;
   ea.err = m->d_err;
   PROF_MEM_CALL(launch_embed_ln(ea, s), "embeddings");
+  int layer_idx = 0;
   for (const BertLayerW& w : m->bert_layers) {
+    const LoraLayerW* lw = m->lora.empty() ? nullptr : &m->lora[layer_idx];
+    ++layer_idx;
+    // base(x) + scaling (x A^T) B^T: T = x A^T, then C += T B^T in place
+    auto lora = [&](const Linear& A, const Linear& B, const void* x, void* C) {
+      if (!A.w) return;
+      run_linear(m, A, x, nullptr, Mcap, ws.total, ws.lora_t, act, JB_EPI_NONE, nullptr, s);
+      run_linear(m, B, ws.lora_t, nullptr, Mcap, ws.total, C, act, JB_EPI_RESIDUAL, C, s);
+    };
     // BertSelfAttention (bert.rs:135-155): fused QKV projection
     run_linear(m, w.qkv, q8 ? ws.aq : ws.x, ws.as, Mcap, ws.total, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+    if (lw) lora(lw->a_qkv, lw->b_qkv, ws.x, ws.qkv);
     std::string why;
     cudaError_t e;
     {
@@ -871,19 +1007,26 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
     if (q8) PROF_MEM_CALL(launch_quantize_rows(ws.ctx, act, ws.aq, ws.as, Mcap, ws.total, H, s), "quantize");
     // BertSelfOutput (bert.rs:164-167): LN(dense(ctx) + x)
     run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
+    if (lw) lora(lw->a_o, lw->b_o, ws.ctx, ws.y);
     run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
            Mcap, ws.total, H, m->eps, s);
     // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1)).  int8: the
     // GELU runs in the quantiser that FFN2's input needs anyway, on the bf16
     // dense output (the reference's bf16 order: Linear -> bf16 -> gelu).
+    const bool lora1 = lw && lw->a_1.w;  // the adapter adds before the activation
     run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act,
-               q8 ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
+               (q8 || lora1) ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
+    if (lora1) {
+      lora(lw->a_1, lw->b_1, ws.x1, ws.hf);
+      PROF_MEM_CALL(launch_gelu_rows(ws.hf, act, Mcap, ws.total, m->ffn, s), "gelu");
+    }
     if (q8)
       PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s,
                                          JB_EPI_GELU),
                     "quantize");
     // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
     run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);
+    if (lw) lora(lw->a_2, lw->b_2, ws.hf, ws.y);
     run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
            Mcap, ws.total, H, m->eps, s);
   }

@@ -42,6 +42,22 @@ struct BertLayerW {
   float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
 };
 
+// LoRA adapters of one encoder layer (the six sites of bert.rs:437-446:
+// query, key, value, attention-output dense, intermediate dense, output
+// dense).  Host copies per site rebuild the device matrices the forward uses:
+// the q/k/v adapters fused into one [R, H] A and one block-diagonal [3H, R] B,
+// each B pre-scaled, rank dimensions padded to a multiple of 8 with zeros.
+struct LoraSiteHost {
+  std::vector<float> a, b;  // A [rank, in], B [out, rank]
+  int rank = 0;
+  double scaling = 0;
+};
+struct LoraLayerW {
+  LoraSiteHost site[6];
+  Linear a_qkv, b_qkv, a_o, b_o, a_1, b_1, a_2, b_2;  // w == nullptr: no adapter
+};
+constexpr int kLoraSites = 6;
+
 struct ClipBlockW {
   Linear qkv, o, fc, proj;
   float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
@@ -69,6 +85,7 @@ struct Workspace {
   float* as = nullptr;
   // vision
   float* head_t = nullptr;  // projection head: x A^T, [batch, rank] f32
+  void* lora_t = nullptr;   // LoRA: x A^T, [rows, lora_width] in the activation dtype
   float* pixels = nullptr;
   void *patches = nullptr, *patch_out = nullptr, *pooled = nullptr;
 };
@@ -106,6 +123,9 @@ struct jb_model {
   void *cls = nullptr, *vpos = nullptr;
   float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
   std::vector<jb::ClipBlockW> clip_blocks;
+  // LoRA adapters (empty: none) and the widest padded rank of a fused site
+  std::vector<jb::LoraLayerW> lora;
+  int lora_width = 0;
   // post-pool projection head: A [rank, H], B [H, rank] pre-scaled by alpha / rank
   float *head_a = nullptr, *head_b = nullptr;
   int head_rank = 0;
@@ -167,5 +187,12 @@ void clear_graphs(jb_model* m);
 // (its layout depends on the rank) and the graphs.
 void set_projection_head(jb_model* m, const float* a, const float* b, int rank, double alpha);
 void load_projection_head(jb_model* m, const char* path, double alpha);
+// Installs (rank > 0) or removes the LoRA adapter of one site; drops the
+// workspace and the graphs.  f32 / bf16 formats.
+void set_lora(jb_model* m, int layer, int site, const float* a, const float* b, int rank,
+              double scaling);
+// Every layer.{n}.{site}.lora_a / lora_b pair of an adapter file, scaling
+// lora_alpha / rank (use_rslora: lora_alpha / sqrt(rank)).  Returns the count.
+int load_lora(jb_model* m, const char* path, double alpha, bool rslora);
 
 }  // namespace jb

@@ -61,6 +61,8 @@ _SIGS = [
     ("jb_model_profile_enable", _I, [_P, _I]),
     ("jb_model_set_projection_head", _I, [_P, _P, _P, _I, ctypes.c_double]),
     ("jb_model_load_projection_head", _I, [_P, ctypes.c_char_p, ctypes.c_double]),
+    ("jb_model_set_lora", _I, [_P, _I, _I, _P, _P, _I, ctypes.c_double]),
+    ("jb_model_load_lora", _I, [_P, ctypes.c_char_p, ctypes.c_double, _I, _P]),
     ("jb_model_profile_read", _I, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int32)]),
     ("jb_encode_text", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     ("jb_encode_text_device", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),

@@ -113,6 +113,29 @@ class Model:
         check(lib().jb_model_load_projection_head(self._h, str(adapter_path).encode(), float(lora_alpha)))
         self.info = self._info()
 
+    LORA_SITES = ("query", "key", "value", "dense", "intermediate_dense", "output_dense")
+
+    def set_lora(self, layer: int, site, lora_a, lora_b, scaling: float):
+        """``jb_model_set_lora``: base(x) + scaling (x A^T) B^T at one linear.
+        ``site`` is an index or a name of ``LORA_SITES``; ``lora_a=None``
+        removes the adapter."""
+        s = self.LORA_SITES.index(site) if isinstance(site, str) else int(site)
+        if lora_a is None:
+            check(lib().jb_model_set_lora(self._h, int(layer), s, None, None, 0, float(scaling)))
+            return
+        a = np.ascontiguousarray(lora_a, dtype=np.float32)
+        b = np.ascontiguousarray(lora_b, dtype=np.float32)
+        check(lib().jb_model_set_lora(self._h, int(layer), s, a.ctypes.data, b.ctypes.data,
+                                      int(a.shape[0]), float(scaling)))
+
+    def load_lora(self, adapter_path: str, lora_alpha: float, use_rslora: bool = False) -> int:
+        """``jb_model_load_lora``: every ``layer.{n}.{module}.lora_a/b`` of an
+        adapter file; returns the number of sites installed."""
+        n = ctypes.c_int32(0)
+        check(lib().jb_model_load_lora(self._h, str(adapter_path).encode(), float(lora_alpha),
+                                       1 if use_rslora else 0, ctypes.byref(n)))
+        return n.value
+
     def profile_enable(self, on: bool = True):
         check(lib().jb_model_profile_enable(self._h, 1 if on else 0))
 

@@ -121,9 +121,18 @@ def _w(weights, key, dtype):
     return np.asarray(weights[key], dtype=dtype)
 
 
+LORA_SITES = ("query", "key", "value", "dense", "intermediate_dense", "output_dense")
+
+
 def bert_forward_hidden(weights: dict, cfg: BertConfig, input_ids, mask,
-                        dtype=np.float64):
-    """``Bert::forward_hidden`` (bert.rs:257-276) -> ``[B, S, H]``."""
+                        dtype=np.float64, lora=None):
+    """``Bert::forward_hidden`` (bert.rs:257-276) -> ``[B, S, H]``.
+
+    ``lora``: optional ``{(layer, site): (A [rank, in], B [out, rank], scaling)}``
+    over the six sites of ``lora_sites`` (bert.rs:437-446): each adapted linear
+    is ``MaybeLoraLinear::Lora`` (crates/jammi-lora/src/wrapper.rs:15-42), whose
+    inference forward is ``base(x) + scaling * (x @ A^T) @ B^T``
+    (crates/jammi-lora/src/lora_linear.rs:226-305, no dropout)."""
     ids = np.asarray(input_ids, dtype=np.int64)
     mask = np.asarray(mask)
     B, S = ids.shape
@@ -142,11 +151,20 @@ def bert_forward_hidden(weights: dict, cfg: BertConfig, input_ids, mask,
     x = layer_norm(x, g("embeddings.LayerNorm.weight"), g("embeddings.LayerNorm.bias"), eps)
 
     ext = extended_attention_mask(mask).astype(dtype)
+    lora = lora or {}
+
+    def lin(n, site, inp, name):
+        y = linear(inp, g(pre + name + ".weight"), g(pre + name + ".bias"))
+        if (n, site) in lora:
+            a, b, scaling = lora[(n, site)]
+            y = y + scaling * ((inp @ np.asarray(a, dtype).T) @ np.asarray(b, dtype).T)
+        return y
+
     for n in range(cfg.num_hidden_layers):
         pre = f"encoder.layer.{n}."
-        q = linear(x, g(pre + "attention.self.query.weight"), g(pre + "attention.self.query.bias"))
-        k = linear(x, g(pre + "attention.self.key.weight"), g(pre + "attention.self.key.bias"))
-        v = linear(x, g(pre + "attention.self.value.weight"), g(pre + "attention.self.value.bias"))
+        q = lin(n, "query", x, "attention.self.query")
+        k = lin(n, "key", x, "attention.self.key")
+        v = lin(n, "value", x, "attention.self.value")
         # transpose_for_scores (bert.rs:126-133): [B,S,H] -> [B,h,S,d]
         q = q.reshape(B, S, nh, d).transpose(0, 2, 1, 3)
         k = k.reshape(B, S, nh, d).transpose(0, 2, 1, 3)
@@ -154,11 +172,11 @@ def bert_forward_hidden(weights: dict, cfg: BertConfig, input_ids, mask,
         scores = (q @ k.transpose(0, 1, 3, 2)) / math.sqrt(d)
         probs = softmax_last(scores + ext)
         ctx = (probs @ v).transpose(0, 2, 1, 3).reshape(B, S, H)
-        a = linear(ctx, g(pre + "attention.output.dense.weight"), g(pre + "attention.output.dense.bias"))
+        a = lin(n, "dense", ctx, "attention.output.dense")
         x1 = layer_norm(a + x, g(pre + "attention.output.LayerNorm.weight"),
                         g(pre + "attention.output.LayerNorm.bias"), eps)
-        f = gelu_erf(linear(x1, g(pre + "intermediate.dense.weight"), g(pre + "intermediate.dense.bias")))
-        o = linear(f, g(pre + "output.dense.weight"), g(pre + "output.dense.bias"))
+        f = gelu_erf(lin(n, "intermediate_dense", x1, "intermediate.dense"))
+        o = lin(n, "output_dense", f, "output.dense")
         x = layer_norm(o + x1, g(pre + "output.LayerNorm.weight"), g(pre + "output.LayerNorm.bias"), eps)
     return x
 
@@ -329,7 +347,16 @@ def distilbert_as_bert(weights: dict, d_cfg: dict):
     return w, cfg
 
 
-def distilbert_forward_hidden(weights: dict, d_cfg: dict, input_ids, mask, dtype=np.float64):
-    """``DistilBert::forward_hidden`` (distilbert.rs:203-222) -> ``[B, S, H]``."""
+DISTILBERT_LORA_SITES = ("q_lin", "k_lin", "v_lin", "out_lin", "lin1", "lin2")
+
+
+def distilbert_forward_hidden(weights: dict, d_cfg: dict, input_ids, mask, dtype=np.float64,
+                              lora=None):
+    """``DistilBert::forward_hidden`` (distilbert.rs:203-222) -> ``[B, S, H]``.
+    ``lora`` keys name DistilBERT's modules (``DISTILBERT_LORA_SITES``,
+    distilbert.rs:245-296), mapped onto the same six sites."""
     w, cfg = distilbert_as_bert(weights, d_cfg)
-    return bert_forward_hidden(w, cfg, input_ids, mask, dtype=dtype)
+    if lora:
+        ren = dict(zip(DISTILBERT_LORA_SITES, LORA_SITES))
+        lora = {(n, ren.get(s, s)): v for (n, s), v in lora.items()}
+    return bert_forward_hidden(w, cfg, input_ids, mask, dtype=dtype, lora=lora)

@@ -326,3 +326,98 @@ def test_projection_head_matches_oracle(fmt, tmp_path):
     model.set_projection_head(None, None, 0.0)
     model.load_projection_head(str(empty), alpha)  # the reference's Ok(None)
     assert model.info.projection_rank == 0
+
+
+# ── LoRA adapters inside the encoder linears (row (f): encoder adapters) ──────
+
+def _lora_set(cfg, seed, ranks, layers, sites=ob.LORA_SITES):
+    """{(layer, site): (A [rank, in], B [out, rank], scaling)} at every site of
+    `layers`, ranks cycling through `ranks` (odd ones exercise the padding)."""
+    rng = np.random.default_rng(seed)
+    H, F = cfg.hidden_size, cfg.intermediate_size
+    dims = {"query": (H, H), "key": (H, H), "value": (H, H), "dense": (H, H),
+            "intermediate_dense": (H, F), "output_dense": (F, H)}
+    out, i = {}, 0
+    for n in layers:
+        for s_name, s_bert in zip(sites, ob.LORA_SITES):
+            r = ranks[i % len(ranks)]
+            i += 1
+            fin, fout = dims[s_bert]
+            a = (rng.standard_normal((r, fin)) * (1.0 / np.sqrt(fin))).astype(np.float32)
+            b = (rng.standard_normal((fout, r)) * 0.05).astype(np.float32)
+            out[(n, s_name)] = (a, b, 16.0 / r)
+    return out
+
+
+@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+def test_lora_adapters_match_oracle(fmt, tmp_path):
+    """base(x) + scaling (x A^T) B^T at all six linears (LoraLinear,
+    lora_linear.rs:226-305; sites of bert.rs:590-640): set from arrays, kept by
+    graph replay, removed back to the plain model, loaded from an adapter file
+    with alpha / rank and alpha / sqrt(rank) scaling."""
+    from safetensors.numpy import save_file
+    cfg = ob.BertConfig(256, 4, 4, 1024, 1000, 128)
+    w = ob.random_bert_weights(cfg, seed=651)
+    rng = np.random.default_rng(652)
+    lens = rng.integers(1, 97, size=10)
+    lens[0] = 96
+    ids, mask = ob.random_token_batch(10, 96, lens, seed=653, id_lo=1, id_hi=999)
+    lora = _lora_set(cfg, 654, ranks=[8, 4, 3, 16, 5, 8], layers=[0, 2, 3])
+    ref = ob.pool_and_normalize(ob.bert_forward_hidden(w, cfg, ids, mask, lora=lora), mask)
+    plain_ref = ob.pool_and_normalize(ob.bert_forward_hidden(w, cfg, ids, mask), mask)
+    assert np.abs(ref - plain_ref).max() > 20 * TOL[fmt]  # the adapters matter
+    model = _bert(w, cfg.to_dict(), fmt)
+    plain = model.encode(ids, lens)
+    for (n, site), (a, b, sc) in lora.items():
+        model.set_lora(n, site, a, b, sc)
+    for _ in range(3):  # direct, capture, replay
+        assert_close_rows(model.encode(ids, lens), ref, fmt)
+    for (n, site) in lora:
+        model.set_lora(n, site, None, None, 0.0)
+    assert np.array_equal(model.encode(ids, lens), plain)
+    # from an adapter file: scaling alpha / rank, then alpha / sqrt(rank)
+    alpha = 12.0
+    tensors = {}
+    for (n, site), (a, b, _) in lora.items():
+        tensors[f"layer.{n}.{site}.lora_a"] = a
+        tensors[f"layer.{n}.{site}.lora_b"] = b
+    path = tmp_path / "adapter.safetensors"
+    save_file(tensors, str(path))
+    for rslora in (False, True):
+        scaled = {k: (a, b, alpha / (np.sqrt(a.shape[0]) if rslora else a.shape[0]))
+                  for k, (a, b, _) in lora.items()}
+        ref_f = ob.pool_and_normalize(ob.bert_forward_hidden(w, cfg, ids, mask, lora=scaled), mask)
+        assert model.load_lora(str(path), alpha, use_rslora=rslora) == len(lora)
+        assert_close_rows(model.encode(ids, lens), ref_f, fmt)
+
+
+def test_lora_adapters_distilbert():
+    """DistilBERT's module names (q_lin .. lin2, distilbert.rs:245-296) from an
+    adapter file, against the oracle over the golden fixture's weights."""
+    from safetensors.numpy import save_file
+    import tempfile
+    from jammi_b200 import Bert
+    w, g = load_golden("small_distilbert.npz")
+    d_cfg = json.loads(bytes(g["config_json"]).decode())
+    _, cfg = ob.distilbert_as_bert(w, d_cfg)
+    lora = _lora_set(cfg, 661, ranks=[4, 8], layers=range(cfg.num_hidden_layers),
+                     sites=ob.DISTILBERT_LORA_SITES)
+    ids, mask = g["ids"], g["mask"]
+    lens = mask.sum(1)
+    ref = ob.pool_and_normalize(ob.distilbert_forward_hidden(w, d_cfg, ids, mask, lora=lora), mask)
+    model = Bert.from_weights(w, d_cfg, device=0, fmt="f32", pooling="mean")
+    with tempfile.TemporaryDirectory() as d:
+        path = f"{d}/adapter.safetensors"
+        save_file({f"layer.{n}.{s}.lora_{x}": t for (n, s), (a, b, _) in lora.items()
+                   for x, t in (("a", a), ("b", b))}, path)
+        # scaling 16 / rank, as _lora_set used
+        assert model.load_lora(path, 16.0) == len(lora)
+    assert_close_rows(model.encode(ids, lens), ref, "f32")
+
+
+def test_lora_rejected_in_int8():
+    from jammi_b200._lib import JbError
+    cfg = ob.BertConfig(64, 1, 2, 128, 100, 32)
+    model = _bert(ob.random_bert_weights(cfg, seed=671), cfg.to_dict(), "int8")
+    with pytest.raises(JbError):
+        model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)
