@@ -55,7 +55,9 @@ typedef enum {
   JB_POOL_WEIGHTED_MEAN = 3
 } jb_pooling;
 
-typedef enum { JB_FAMILY_BERT = 0, JB_FAMILY_CLIP_VISION = 1 } jb_family;
+/* JB_FAMILY_CLIP_TEXT: the OpenCLIP text tower (crates/jammi-encoders/src/clip_text.rs),
+ * loaded from the same checkpoint as the vision tower (root-level keys). */
+typedef enum { JB_FAMILY_BERT = 0, JB_FAMILY_CLIP_VISION = 1, JB_FAMILY_CLIP_TEXT = 2 } jb_family;
 /* BERT-family text encoders sharing one forward: BERT (crates/jammi-encoders/src/bert.rs)
  * and DistilBERT (crates/jammi-encoders/src/distilbert.rs: no token-type table,
  * config keys dim / n_layers / n_heads / hidden_dim, weights under "distilbert."). */
@@ -92,6 +94,14 @@ typedef struct {
  * quantised per output channel on load. */
 jb_status jb_model_load(const char* safetensors_path, const char* config_json,
                         int device, int format, jb_model** out);
+/* The same with the tower named: `family` JB_FAMILY_BERT, JB_FAMILY_CLIP_VISION
+ * or JB_FAMILY_CLIP_TEXT (-1: detect, as jb_model_load).  An OpenCLIP
+ * checkpoint holds both towers; CandleBackend::load builds both from it
+ * (candle.rs:1474-1501): load it once per tower.  CLIP text models take
+ * f32 or bf16 weights (ClipTextConfig::from_open_clip_config,
+ * clip_text.rs:53-102: model_cfg.embed_dim, model_cfg.text_cfg). */
+jb_status jb_model_load_family(const char* safetensors_path, const char* config_json,
+                               int device, int format, int family, jb_model** out);
 void jb_model_free(jb_model* model);
 jb_status jb_model_get_info(const jb_model* model, jb_model_info* out);
 const char* jb_last_error(void);
@@ -207,6 +217,10 @@ jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamm
  * dtype F32 or BF16; max_len bounds every row's length. */
 jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
                           int batch, int heads, int head_dim, int max_len, void* stream);
+/* The same under the causal mask of the OpenCLIP text tower: query i of a row
+ * attends to keys j <= i (clip_text.rs:133-162, mask :350-362). */
+jb_status jb_op_attention_causal(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
+                                 int batch, int heads, int head_dim, int max_len, void* stream);
 /* Synchronises `stream` and reads (then clears) the current device's error
  * flag shared by the single-op entry points: JB_ERR_TIMEOUT if a bounded
  * device-side wait gave up in an earlier op. */

@@ -52,13 +52,17 @@ int current_device() {
 
 void check_text_args(const jb_model* m, int batch, int max_seq, int pooling) {
   if (!m) jb::fail(JB_ERR_INVALID, "null model");
-  if (m->family != JB_FAMILY_BERT) jb::fail(JB_ERR_INVALID, "model is not a text encoder");
+  if (m->family != JB_FAMILY_BERT && m->family != JB_FAMILY_CLIP_TEXT)
+    jb::fail(JB_ERR_INVALID, "model is not a text encoder");
   if (batch < 0 || max_seq < 0) jb::fail(JB_ERR_INVALID, "batch and max_seq must be >= 0");
   if (pooling < JB_POOL_MEAN || pooling > JB_POOL_WEIGHTED_MEAN) jb::fail(JB_ERR_INVALID, "unknown pooling");
-  // Bert::forward_hidden's SequenceTooLong check (bert.rs:263-268)
+  // SequenceTooLong: Bert::forward_hidden (bert.rs:263-268), ClipText::forward
+  // (clip_text.rs:302-308, against context_length)
   if (max_seq > m->max_pos)
-    jb::fail(JB_ERR_SEQ_TOO_LONG, "sequence length " + std::to_string(max_seq) +
-                                      " exceeds max_position_embeddings " + std::to_string(m->max_pos));
+    jb::fail(JB_ERR_SEQ_TOO_LONG, "sequence length " + std::to_string(max_seq) + " exceeds " +
+                                      (m->family == JB_FAMILY_CLIP_TEXT ? "context_length "
+                                                                        : "max_position_embeddings ") +
+                                      std::to_string(m->max_pos));
   if (static_cast<int64_t>(batch) * max_seq > (int64_t(1) << 30))
     jb::fail(JB_ERR_INVALID, "batch * max_seq too large");
 }
@@ -80,6 +84,16 @@ jb_status jb_model_load(const char* safetensors_path, const char* config_json, i
   });
 }
 
+jb_status jb_model_load_family(const char* safetensors_path, const char* config_json, int device,
+                               int format, int family, jb_model** out) {
+  return guarded([&] {
+    if (!out) jb::fail(JB_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    if (family < -1 || family > JB_FAMILY_CLIP_TEXT) jb::fail(JB_ERR_INVALID, "unknown model family");
+    *out = jb::model_load(safetensors_path, config_json, device, format, family);
+  });
+}
+
 void jb_model_free(jb_model* model) {
   try {
     jb::model_free(model);
@@ -95,7 +109,7 @@ jb_status jb_model_get_info(const jb_model* m, jb_model_info* out) {
     out->format = m->format;
     out->device = m->device;
     out->hidden = m->hidden;
-    out->output_dim = m->family == JB_FAMILY_BERT ? m->hidden : m->embed_dim;
+    out->output_dim = jb::output_dim(m);
     out->layers = m->layers;
     out->heads = m->heads;
     out->ffn = m->ffn;
@@ -186,8 +200,12 @@ jb_status jb_encode_text(jb_model* m, const uint32_t* ids, const uint32_t* lens,
   return guarded([&] {
     check_text_args(m, batch, max_seq, pooling);
     if (batch == 0) return;
-    if (!ids || !lens || !out) jb::fail(JB_ERR_INVALID, "null buffer");
-    for (int b = 0; b < batch; ++b)
+    // CLIP text ignores lengths and pooling (clip_text.rs:287-295: the rows
+    // end at their EOT token, which is also where they are pooled)
+    const bool clip = m->family == JB_FAMILY_CLIP_TEXT;
+    if (!ids || (!lens && !clip) || !out) jb::fail(JB_ERR_INVALID, "null buffer");
+    if (clip && max_seq == 0) jb::fail(JB_ERR_INVALID, "OpenCLIP text rows need at least one token");
+    for (int b = 0; b < batch && !clip; ++b)
       if (lens[b] > static_cast<uint32_t>(max_seq)) jb::fail(JB_ERR_INVALID, "a row length exceeds max_seq");
     std::lock_guard<std::mutex> lk(m->mu);
     jb::DeviceGuard g(m->device);
@@ -195,11 +213,15 @@ jb_status jb_encode_text(jb_model* m, const uint32_t* ids, const uint32_t* lens,
     jb::ensure_workspace(m, batch, std::max(max_seq, 1));
     jb::Workspace& ws = m->ws;
     jb::check_cuda(cudaMemcpyAsync(ws.ids, ids, size_t(batch) * max_seq * 4, cudaMemcpyHostToDevice, s), "H2D ids");
-    jb::check_cuda(cudaMemcpyAsync(ws.lens, lens, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D lens");
-    jb::run_graphed(m, 0, batch, max_seq, pooling, s, [&](cudaStream_t gs) {
-      jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
+    if (!clip)
+      jb::check_cuda(cudaMemcpyAsync(ws.lens, lens, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D lens");
+    jb::run_graphed(m, 0, batch, max_seq, clip ? 0 : pooling, s, [&](cudaStream_t gs) {
+      if (clip)
+        jb::clip_text_forward_device(m, ws.ids, batch, max_seq, ws.out, gs);
+      else
+        jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
     });
-    jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->hidden * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * jb::output_dim(m) * 4, cudaMemcpyDeviceToHost, s), "D2H");
     jb::check_device_flag(m, s);
   });
 }
@@ -209,7 +231,9 @@ jb_status jb_encode_text_device(jb_model* m, const uint32_t* d_ids, const uint32
   return guarded([&] {
     check_text_args(m, batch, max_seq, pooling);
     if (batch == 0) return;
-    if (!d_ids || !d_lens || !d_out) jb::fail(JB_ERR_INVALID, "null buffer");
+    const bool clip = m->family == JB_FAMILY_CLIP_TEXT;
+    if (!d_ids || (!d_lens && !clip) || !d_out) jb::fail(JB_ERR_INVALID, "null buffer");
+    if (clip && max_seq == 0) jb::fail(JB_ERR_INVALID, "OpenCLIP text rows need at least one token");
     std::lock_guard<std::mutex> lk(m->mu);
     jb::DeviceGuard g(m->device);
     jb::ensure_workspace(m, batch, std::max(max_seq, 1));
@@ -218,11 +242,15 @@ jb_status jb_encode_text_device(jb_model* m, const uint32_t* d_ids, const uint32
     cudaStream_t s = as_stream(stream);
     jb::Workspace& ws = m->ws;
     jb::check_cuda(cudaMemcpyAsync(ws.ids, d_ids, size_t(batch) * max_seq * 4, cudaMemcpyDeviceToDevice, s), "ids");
-    jb::check_cuda(cudaMemcpyAsync(ws.lens, d_lens, size_t(batch) * 4, cudaMemcpyDeviceToDevice, s), "lens");
-    jb::run_graphed(m, 0, batch, max_seq, pooling, s, [&](cudaStream_t gs) {
-      jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
+    if (!clip)
+      jb::check_cuda(cudaMemcpyAsync(ws.lens, d_lens, size_t(batch) * 4, cudaMemcpyDeviceToDevice, s), "lens");
+    jb::run_graphed(m, 0, batch, max_seq, clip ? 0 : pooling, s, [&](cudaStream_t gs) {
+      if (clip)
+        jb::clip_text_forward_device(m, ws.ids, batch, max_seq, ws.out, gs);
+      else
+        jb::bert_forward_device(m, ws.ids, ws.lens, batch, max_seq, pooling, ws.out, nullptr, gs);
     });
-    jb::check_cuda(cudaMemcpyAsync(d_out, ws.out, size_t(batch) * m->hidden * 4, cudaMemcpyDeviceToDevice, s), "out");
+    jb::check_cuda(cudaMemcpyAsync(d_out, ws.out, size_t(batch) * jb::output_dim(m) * 4, cudaMemcpyDeviceToDevice, s), "out");
   });
 }
 
@@ -230,6 +258,9 @@ jb_status jb_forward_hidden_device(jb_model* m, const uint32_t* d_ids, const uin
                                    int batch, int max_seq, float* d_hidden, void* stream) {
   return guarded([&] {
     check_text_args(m, batch, max_seq, JB_POOL_MEAN);
+    // OpenClipTextForward::forward_hidden (open_clip_text.rs:27-44)
+    if (m->family == JB_FAMILY_CLIP_TEXT)
+      jb::fail(JB_ERR_INVALID, "OpenCLIP text encoder does not support forward_hidden");
     if (batch == 0) return;
     if (!d_ids || !d_lens || !d_hidden) jb::fail(JB_ERR_INVALID, "null buffer");
     std::lock_guard<std::mutex> lk(m->mu);
@@ -397,20 +428,32 @@ jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamm
   });
 }
 
-jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype, int batch,
-                          int heads, int head_dim, int max_len, void* stream) {
+namespace {
+jb_status op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype, int batch,
+                       int heads, int head_dim, int max_len, int causal, void* stream) {
   return guarded([&] {
     if (!qkv || !cu_seqlens || !ctx || batch < 0 || heads <= 0 || head_dim <= 0 || max_len < 0)
       jb::fail(JB_ERR_INVALID, "jb_op_attention: bad argument");
     if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
     std::string why;
     cudaError_t e = jb::launch_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len,
-                                         as_stream(stream), &why);
+                                         as_stream(stream), &why, 0, nullptr, causal);
     if (e != cudaSuccess) {
       if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
       jb::check_cuda(e, "jb_op_attention");
     }
   });
+}
+}  // namespace
+
+jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype, int batch,
+                          int heads, int head_dim, int max_len, void* stream) {
+  return op_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len, 0, stream);
+}
+
+jb_status jb_op_attention_causal(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
+                                 int batch, int heads, int head_dim, int max_len, void* stream) {
+  return op_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len, 1, stream);
 }
 
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens, float* out,

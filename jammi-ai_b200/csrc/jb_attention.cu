@@ -89,7 +89,7 @@ template <bool TMA>
 __global__ void __launch_bounds__(kFaThreads, 4)
     flash_attn_bf16_d64(const bf16* __restrict__ qkv, const int* __restrict__ cu,
                         bf16* __restrict__ ctx, int heads, float scale_log2,
-                        const __grid_constant__ CUtensorMap tm, int* err) {
+                        const __grid_constant__ CUtensorMap tm, int* err, int causal) {
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = cu[b], n = cu[b + 1] - start;
   const int q0 = qb * kFaRows;
@@ -126,7 +126,9 @@ __global__ void __launch_bounds__(kFaThreads, 4)
     cp_async_commit();
   }
 
-  const int nkb = (n + kFaKeys - 1) / kFaKeys;
+  // causal: this block's queries see keys up to its own last query, so the
+  // key blocks stop at the diagonal one (kFaKeys == kFaRows)
+  const int nkb = causal ? min(qb + 1, (n + kFaKeys - 1) / kFaKeys) : (n + kFaKeys - 1) / kFaKeys;
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -213,6 +215,14 @@ __global__ void __launch_bounds__(kFaThreads, 4)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) >= n) s[nt][e] = -INFINITY;
+      }
+      if (causal && kb == qb) {  // the diagonal block: key j > query i scores -inf
+        const int qr = q0 + warp * 16 + (lane >> 2);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (kbase + nt * 8 + 2 * (lane & 3) + (e & 1) > qr + 8 * (e >> 1)) s[nt][e] = -INFINITY;
       }
       // row maxima and sums as trees (depth 4, not 8): short dependency chains
       float t0[8], t1[8];
@@ -309,7 +319,8 @@ constexpr int kSimtKeys = 64;
 template <typename T, int D>
 __global__ void __launch_bounds__(kSimtRows) attn_simt(const T* __restrict__ qkv,
                                                       const int* __restrict__ cu,
-                                                      T* __restrict__ ctx, int heads, float scale) {
+                                                      T* __restrict__ ctx, int heads, float scale,
+                                                      int causal) {
   const int b = blockIdx.z, h = blockIdx.y;
   const int start = cu[b], n = cu[b + 1] - start;
   if (blockIdx.x * kSimtRows >= n) return;
@@ -336,7 +347,7 @@ __global__ void __launch_bounds__(kSimtRows) attn_simt(const T* __restrict__ qkv
     }
     __syncthreads();
     if (active) {
-      const int kn = min(kSimtKeys, n - k0);
+      const int kn = causal ? min(min(kSimtKeys, n - k0), q - k0 + 1) : min(kSimtKeys, n - k0);
       for (int j = 0; j < kn; ++j) {
         float s = 0.f;
 #pragma unroll
@@ -362,16 +373,16 @@ __global__ void __launch_bounds__(kSimtRows) attn_simt(const T* __restrict__ qkv
 
 template <typename T>
 cudaError_t launch_simt(const void* qkv, const int* cu, void* ctx, int batch, int heads, int d,
-                        int max_len, cudaStream_t s, std::string* why) {
+                        int max_len, cudaStream_t s, std::string* why, int causal) {
   dim3 grid((max_len + kSimtRows - 1) / kSimtRows, heads, batch);
   const float scale = 1.0f / sqrtf(static_cast<float>(d));
   const T* q = static_cast<const T*>(qkv);
   T* c = static_cast<T*>(ctx);
   switch (d) {
-    case 8: attn_simt<T, 8><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
-    case 16: attn_simt<T, 16><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
-    case 32: attn_simt<T, 32><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
-    case 64: attn_simt<T, 64><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale); break;
+    case 8: attn_simt<T, 8><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale, causal); break;
+    case 16: attn_simt<T, 16><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale, causal); break;
+    case 32: attn_simt<T, 32><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale, causal); break;
+    case 64: attn_simt<T, 64><<<grid, kSimtRows, 0, s>>>(q, cu, c, heads, scale, causal); break;
     default:
       if (why) *why = "attention: head_dim must be 8, 16, 32 or 64";
       return cudaErrorInvalidValue;
@@ -405,7 +416,7 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
 
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
-                             std::string* why, int rows_cap, int* err) {
+                             std::string* why, int rows_cap, int* err, int causal) {
   if (batch == 0 || max_len == 0) return cudaSuccess;
   if (batch > 65535 || heads > 65535) {
     if (why) *why = "attention: batch and heads must be <= 65535";
@@ -421,11 +432,12 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
     kern<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu, static_cast<bf16*>(ctx),
-                                     heads, scale_log2, tm, err);
+                                     heads, scale_log2, tm, err, causal);
     return cudaGetLastError();
   }
-  if (dtype == JB_DT_BF16) return launch_simt<bf16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why);
-  return launch_simt<float>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why);
+  if (dtype == JB_DT_BF16)
+    return launch_simt<bf16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why, causal);
+  return launch_simt<float>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why, causal);
 }
 
 }  // namespace jb

@@ -63,7 +63,8 @@ cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* sca
                                  int activation = JB_EPI_NONE);
 
 // BERT embeddings: word[ids] + type[0] + pos[p] -> LayerNorm, written packed
-// at row cu[b] + p for p < len[b].
+// at row cu[b] + p for p < len[b].  type0 == null: no type row; gamma == null:
+// no LayerNorm (the sum is stored).
 struct EmbedArgs {
   const uint32_t* ids = nullptr;  // [batch, max_seq]
   const int* cu = nullptr;        // [batch + 1]
@@ -82,10 +83,12 @@ struct EmbedArgs {
 };
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
 
+// causal != 0: query i attends to keys j <= i of its row (the OpenCLIP text
+// mask, clip_text.rs:350-362).
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
                              std::string* why,
-                             int rows_cap = 0, int* err = nullptr);
+                             int rows_cap = 0, int* err = nullptr, int causal = 0);
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s);
@@ -107,9 +110,13 @@ cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const vo
                                 const float* gamma, const float* beta, void* y, int dtype,
                                 int batch, int tokens, int W, float eps, cudaStream_t s);
 // ViT pooling before ln_post: CLS token (gap = 0) or mean of tokens 1.. (gap = 1), then LN.
+// cu != null: packed rows, each row's last token (gap must be 0).
 cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* beta, void* y,
                                int dtype, int batch, int tokens, int W, int gap, float eps,
-                               cudaStream_t s);
+                               cudaStream_t s, const int* cu = nullptr);
+// lens[b] = 1 + argmax(ids[b, :S]) (first maximum): OpenCLIP text rows end at
+// their <|endoftext|> token.
+cudaError_t launch_eot_lens(const uint32_t* ids, int batch, int S, uint32_t* lens, cudaStream_t s);
 // cu[b] = b * tokens for b in [0, batch] (fixed-length rows, e.g. ViT tokens).
 cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s);
 // Row-wise x / clamp(||x||, 1e-12) over f32 [rows, cols], in place.

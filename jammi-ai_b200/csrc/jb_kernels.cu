@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
   constexpr int VN = Vec<T>::N;
   __shared__ __align__(16) float sg[kLnMaxCols];
   __shared__ __align__(16) float sb[kLnMaxCols];
-  stage_params(sg, sb, a.gamma, a.beta, a.H);
+  if (a.gamma) stage_params(sg, sb, a.gamma, a.beta, a.H);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = a.H / VN;
   const int slots = a.batch * a.max_seq;
@@ -277,14 +277,28 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
       if (vi < nvec) {
         float t1[VN], t2[VN];
         Vec<T>::load(w + vi * VN, v + i * VN);
-        Vec<T>::load(te + vi * VN, t1);
         Vec<T>::load(pe + vi * VN, t2);
+        if (te) {
+          Vec<T>::load(te + vi * VN, t1);
 #pragma unroll
-        for (int e = 0; e < VN; ++e) v[i * VN + e] = (v[i * VN + e] + t1[e]) + t2[e];
+          for (int e = 0; e < VN; ++e) v[i * VN + e] = (v[i * VN + e] + t1[e]) + t2[e];
+        } else {
+#pragma unroll
+          for (int e = 0; e < VN; ++e) v[i * VN + e] += t2[e];
+        }
       }
     }
     const size_t row = static_cast<size_t>(start + p);
-    ln_finish<T, MAXV>(v, nvec, a.H, lane, sg, sb, a.eps, static_cast<T*>(a.y) + row * a.H,
+    T* yrow = static_cast<T*>(a.y) + row * a.H;
+    if (!a.gamma) {  // token + position only (OpenCLIP text, clip_text.rs:309-312)
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = lane + i * 32;
+        if (vi < nvec) Vec<T>::store(yrow + vi * VN, v + i * VN);
+      }
+      continue;
+    }
+    ln_finish<T, MAXV>(v, nvec, a.H, lane, sg, sb, a.eps, yrow,
                        a.yq ? a.yq + row * a.H : nullptr, a.yscale ? a.yscale + row : nullptr);
   }
 }
@@ -729,7 +743,8 @@ __global__ void __launch_bounds__(256) vit_embed_ln_kernel(const T* patch_out, c
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(32) vit_pool_ln_kernel(const T* x, const float* gamma,
                                                          const float* beta, T* y, int tokens,
-                                                         int W, int gap, float eps) {
+                                                         int W, int gap, float eps,
+                                                         const int* cu) {
   constexpr int VN = Vec<T>::N;
   const int lane = threadIdx.x;
   const int b = blockIdx.x;
@@ -739,7 +754,9 @@ __global__ void __launch_bounds__(32) vit_pool_ln_kernel(const T* x, const float
   for (int k = 0; k < MAXV * VN; ++k) v[k] = 0.f;
   const int t0 = gap ? 1 : 0, t1 = gap ? tokens : 1;
   for (int t = t0; t < t1; ++t) {
-    const T* xr = x + (static_cast<size_t>(b) * tokens + t) * W;
+    // cu: packed rows, the row's last token; else fixed rows of `tokens`
+    const T* xr = cu ? x + static_cast<size_t>(cu[b + 1] - 1) * W
+                     : x + (static_cast<size_t>(b) * tokens + t) * W;
 #pragma unroll
     for (int k = 0; k < MAXV; ++k) {
       const int vi = lane + k * 32;
@@ -758,6 +775,35 @@ __global__ void __launch_bounds__(32) vit_pool_ln_kernel(const T* x, const float
   }
   ln_finish<T, MAXV>(v, nvec, W, lane, gamma, beta, eps, y + static_cast<size_t>(b) * W, nullptr,
                      nullptr);
+}
+
+// One warp per row: len[b] = 1 + the first position of the row's largest id
+// (argmax(input_ids, dim=1), clip_text.rs:322-326; OpenCLIP's <|endoftext|>
+// has the largest id, so the row ends at its EOT token).
+__global__ void __launch_bounds__(256) eot_lens_kernel(const uint32_t* __restrict__ ids, int batch,
+                                                       int S, uint32_t* __restrict__ lens) {
+  const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (b >= batch) return;
+  const uint32_t* r = ids + static_cast<size_t>(b) * S;
+  uint32_t best = 0;
+  int at = S;  // S: none seen yet (every real position compares below)
+  for (int p = lane; p < S; p += 32) {
+    const uint32_t v = r[p];
+    if (at == S || v > best) {  // positions rise per lane: the first maximum wins
+      best = v;
+      at = p;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const uint32_t ob = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oa = __shfl_xor_sync(0xffffffffu, at, off);
+    if (oa < S && (at == S || ob > best || (ob == best && oa < at))) {
+      best = ob;
+      at = oa;
+    }
+  }
+  if (lane == 0) lens[b] = static_cast<uint32_t>(at < S ? at + 1 : 0);
 }
 
 __global__ void fill_cu_uniform_kernel(int* cu, int batch, int tokens) {
@@ -999,17 +1045,24 @@ cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const vo
 
 cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* beta, void* y,
                                int dtype, int batch, int tokens, int W, int gap, float eps,
-                               cudaStream_t s) {
+                               cudaStream_t s, const int* cu) {
   if (batch == 0) return cudaSuccess;
+  if (cu && gap) return cudaErrorInvalidValue;
   if (dtype == JB_DT_BF16) {
     if (W % 8 || W > 1024) return cudaErrorInvalidValue;
     vit_pool_ln_kernel<bf16, 4><<<batch, 32, 0, s>>>(static_cast<const bf16*>(x), gamma, beta,
-                                                     static_cast<bf16*>(y), tokens, W, gap, eps);
+                                                     static_cast<bf16*>(y), tokens, W, gap, eps, cu);
   } else {
     if (W % 4 || W > 1024) return cudaErrorInvalidValue;
     vit_pool_ln_kernel<float, 8><<<batch, 32, 0, s>>>(static_cast<const float*>(x), gamma, beta,
-                                                      static_cast<float*>(y), tokens, W, gap, eps);
+                                                      static_cast<float*>(y), tokens, W, gap, eps, cu);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_eot_lens(const uint32_t* ids, int batch, int S, uint32_t* lens, cudaStream_t s) {
+  if (batch == 0) return cudaSuccess;
+  eot_lens_kernel<<<blocks_for(static_cast<size_t>(batch), 8), 256, 0, s>>>(ids, batch, S, lens);
   return cudaGetLastError();
 }
 

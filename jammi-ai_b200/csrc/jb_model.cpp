@@ -349,6 +349,8 @@ void load_bert(jb_model* m, const SafeTensors& st, const Json& cfg) {
   }
 }
 
+void load_clip_blocks(jb_model* m, const SafeTensors& st, const std::string& p);
+
 void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->family = JB_FAMILY_CLIP_VISION;
   const Json* mc = cfg.get("model_cfg");
@@ -365,7 +367,7 @@ void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->embed_dim = static_cast<int>(mc->num_or("embed_dim", 0));
   m->gap = vc->bool_or("global_average_pool", false);
   m->eps = 1e-5f;
-  const int W = m->hidden, F = m->ffn, P = m->patch, g = m->image_size / m->patch;
+  const int W = m->hidden, P = m->patch, g = m->image_size / m->patch;
   m->tokens = g * g + 1;
   m->max_pos = m->tokens;
   if (W <= 0 || W % m->heads || W % 8 || W > 1024 || m->embed_dim <= 0 || g <= 0)
@@ -378,6 +380,17 @@ void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->vpos = upload_act(m, st.f32(p + "positional_embedding", int64_t(m->tokens) * W));
   m->ln_pre_g = upload_f32(m, st.f32(p + "ln_pre.weight", W));
   m->ln_pre_b = upload_f32(m, st.f32(p + "ln_pre.bias", W));
+  load_clip_blocks(m, st, p);
+  m->ln_post_g = upload_f32(m, st.f32(p + "ln_post.weight", W));
+  m->ln_post_b = upload_f32(m, st.f32(p + "ln_post.bias", W));
+  m->proj = load_linear(m, st, {p + "proj"}, {m->embed_dim}, W, false, ld, /*transpose_src=*/true);
+}
+
+// ResidualAttentionBlock weights under p + "transformer.resblocks.{l}."
+// (open_clip_vit.rs:203-224, clip_text.rs:192-205: the same layout).
+void load_clip_blocks(jb_model* m, const SafeTensors& st, const std::string& p) {
+  const int W = m->hidden, F = m->ffn;
+  const int ld = linear_dtype(m->format);
   for (int l = 0; l < m->layers; ++l) {
     const std::string q = p + "transformer.resblocks." + std::to_string(l) + ".";
     ClipBlockW w;
@@ -407,9 +420,40 @@ void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
     w.ln2_b = upload_f32(m, st.f32(q + "ln_2.bias", W));
     m->clip_blocks.push_back(w);
   }
-  m->ln_post_g = upload_f32(m, st.f32(p + "ln_post.weight", W));
-  m->ln_post_b = upload_f32(m, st.f32(p + "ln_post.bias", W));
-  m->proj = load_linear(m, st, {p + "proj"}, {m->embed_dim}, W, false, ld, /*transpose_src=*/true);
+}
+
+// ClipText::load (clip_text.rs:251-283) with ClipTextConfig::from_open_clip_config
+// (:53-102): width and layers required, heads width/64, context_length 77 and
+// vocab_size 49408 by default; MLP 4 x width (:194-195); LayerNorm eps 1e-5.
+void load_clip_text(jb_model* m, const SafeTensors& st, const Json& cfg) {
+  m->family = JB_FAMILY_CLIP_TEXT;
+  const Json* mc = cfg.get("model_cfg");
+  const Json* tc = mc ? mc->get("text_cfg") : nullptr;
+  if (!mc) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg'");
+  if (!tc) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.text_cfg'");
+  if (!mc->get("embed_dim")) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.embed_dim'");
+  if (!tc->get("width")) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.text_cfg.width'");
+  if (!tc->get("layers")) fail(JB_ERR_INVALID, "OpenCLIP config missing 'model_cfg.text_cfg.layers'");
+  m->hidden = static_cast<int>(tc->num_or("width", 0));
+  m->layers = static_cast<int>(tc->num_or("layers", 0));
+  m->heads = static_cast<int>(tc->num_or("heads", m->hidden / 64));
+  m->max_pos = static_cast<int>(tc->num_or("context_length", 77));
+  m->vocab = static_cast<int>(tc->num_or("vocab_size", 49408));
+  m->embed_dim = static_cast<int>(mc->num_or("embed_dim", 0));
+  m->ffn = 4 * m->hidden;
+  m->eps = 1e-5f;
+  const int W = m->hidden;
+  if (W <= 0 || m->heads <= 0 || W % m->heads || W % 8 || W > 1024 || m->embed_dim <= 0 ||
+      m->max_pos <= 0 || m->vocab <= 0 || m->layers < 0)
+    fail(JB_ERR_INVALID, "OpenCLIP config: unsupported text dimensions");
+  if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are only defined for BERT encoders");
+  const int ld = linear_dtype(m->format);
+  m->word = upload_act(m, st.f32("token_embedding.weight", int64_t(m->vocab) * W));
+  m->pos = upload_act(m, st.f32("positional_embedding", int64_t(m->max_pos) * W));
+  load_clip_blocks(m, st, "");
+  m->ln_post_g = upload_f32(m, st.f32("ln_final.weight", W));
+  m->ln_post_b = upload_f32(m, st.f32("ln_final.bias", W));
+  m->proj = load_linear(m, st, {"text_projection"}, {m->embed_dim}, W, false, ld, /*transpose_src=*/true);
 }
 
 void free_workspace(Workspace& ws) {
@@ -449,6 +493,7 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
     p.aq = round_up(T * std::max(H, F));
     p.as = round_up(T * 4);
   }
+  if (m->family == JB_FAMILY_CLIP_TEXT) p.pooled = round_up(B * H * e);
   if (m->family == JB_FAMILY_CLIP_VISION) {
     const size_t g = m->image_size / m->patch;
     p.pixels = round_up(B * 3 * m->image_size * m->image_size * 4);
@@ -549,7 +594,7 @@ Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq)
   return ws;
 }
 
-jb_model* model_load(const char* path, const char* config_json, int device, int format) {
+jb_model* model_load(const char* path, const char* config_json, int device, int format, int family) {
   if (!path || !config_json) fail(JB_ERR_INVALID, "weights path and config must be non-null");
   if (format < JB_FMT_F32 || format > JB_FMT_INT8) fail(JB_ERR_INVALID, "unknown weight format");
   int ndev = 0;
@@ -576,8 +621,11 @@ jb_model* model_load(const char* path, const char* config_json, int device, int 
   m->act = format == JB_FMT_F32 ? JB_DT_F32 : JB_DT_BF16;
   try {
     SafeTensors st(path);
-    if (cfg.get("model_cfg"))
+    if (family < 0) family = cfg.get("model_cfg") ? JB_FAMILY_CLIP_VISION : JB_FAMILY_BERT;
+    if (family == JB_FAMILY_CLIP_VISION)
       load_clip(m.get(), st, cfg);
+    else if (family == JB_FAMILY_CLIP_TEXT)
+      load_clip_text(m.get(), st, cfg);
     else
       load_bert(m.get(), st, cfg);
     check_cuda(cudaMalloc(&m->d_err, sizeof(int)), "error flag");
@@ -1050,6 +1098,72 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
   }
 }
 
+namespace {
+// The ResidualAttentionBlock stack (open_clip_vit.rs:226-236; clip_text.rs:207-217
+// with the causal mask) over packed rows: the input in ws.x, rows <= rows_cap
+// (*d_rows when given), cu in ws.cu.  Returns the buffer holding the output.
+void* clip_blocks_forward(jb_model* m, int rows_cap, const int* d_rows, int batch, int max_len,
+                          int causal, cudaStream_t s) {
+  Workspace& ws = m->ws;
+  const int W = m->hidden, act = m->act;
+  void* x = ws.x;
+  void* y = ws.y;
+  for (const ClipBlockW& w : m->clip_blocks) {
+    run_ln(m, x, nullptr, w.ln1_g, w.ln1_b, ws.x1, nullptr, nullptr, act, rows_cap, d_rows, W, m->eps, s);
+    run_linear(m, w.qkv, ws.x1, nullptr, rows_cap, d_rows, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+    std::string why;
+    cudaError_t e;
+    {
+      ProfScope ps(m, kProfAttention, s);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, max_len, s, &why,
+                           rows_cap, m->d_err, causal);
+    }
+    if (e != cudaSuccess) {
+      if (!why.empty()) fail(JB_ERR_INVALID, why);
+      check_cuda(e, "attention");
+    }
+    run_linear(m, w.o, ws.ctx, nullptr, rows_cap, d_rows, y, act, JB_EPI_RESIDUAL, x, s);
+    std::swap(x, y);
+    run_ln(m, x, nullptr, w.ln2_g, w.ln2_b, ws.x1, nullptr, nullptr, act, rows_cap, d_rows, W, m->eps, s);
+    run_linear(m, w.fc, ws.x1, nullptr, rows_cap, d_rows, ws.hf, act, JB_EPI_QUICK_GELU, nullptr, s);
+    run_linear(m, w.proj, ws.hf, nullptr, rows_cap, d_rows, y, act, JB_EPI_RESIDUAL, x, s);
+    std::swap(x, y);
+  }
+  return x;
+}
+}  // namespace
+
+void clip_text_forward_device(jb_model* m, const uint32_t* d_ids, int batch, int S, float* d_out,
+                              cudaStream_t s) {
+  Workspace& ws = m->ws;
+  const int W = m->hidden, act = m->act, Mcap = batch * S;
+  // rows end at their EOT token: under the causal mask no later position
+  // reaches the pooled one, so only the prefix up to it is computed
+  PROF_MEM_CALL(launch_eot_lens(d_ids, batch, S, ws.lens, s), "eot");
+  PROF_MEM_CALL(launch_lens_to_cu(ws.lens, batch, S, ws.cu, ws.total, m->d_err, s), "lengths");
+  // token_embedding(ids) + positional_embedding[..S] (clip_text.rs:309-312)
+  EmbedArgs ea;
+  ea.ids = d_ids;
+  ea.cu = ws.cu;
+  ea.word = m->word;
+  ea.pos = m->pos;
+  ea.y = ws.x;
+  ea.dtype = act;
+  ea.batch = batch;
+  ea.max_seq = S;
+  ea.H = W;
+  ea.vocab = m->vocab;
+  ea.err = m->d_err;
+  PROF_MEM_CALL(launch_embed_ln(ea, s), "embeddings");
+  void* x = clip_blocks_forward(m, Mcap, ws.total, batch, S, 1, s);
+  // ln_final at the EOT position, @ text_projection, L2 (clip_text.rs:319-330, 379-389)
+  PROF_MEM_CALL(launch_vit_pool_ln(x, m->ln_post_g, m->ln_post_b, ws.pooled, act, batch, 0, W, 0,
+                                   m->eps, s, ws.cu),
+                "eot pool");
+  run_linear(m, m->proj, ws.pooled, nullptr, batch, nullptr, d_out, JB_DT_F32, JB_EPI_NONE, nullptr, s);
+  PROF_MEM_CALL(launch_l2_rows(d_out, batch, m->embed_dim, s), "l2");
+}
+
 void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s) {
   Workspace& ws = m->ws;
   const int W = m->hidden, T = m->tokens, g = m->image_size / m->patch, act = m->act;
@@ -1062,30 +1176,7 @@ void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out
                                  batch, T, W, m->eps, s),
              "vit embed");
   PROF_MEM_CALL(launch_fill_cu_uniform(ws.cu, batch, T, s), "cu");
-  void* x = ws.x;
-  void* y = ws.y;
-  for (const ClipBlockW& w : m->clip_blocks) {
-    // ResidualAttentionBlock::forward (open_clip_vit.rs:226-236)
-    run_ln(m, x, nullptr, w.ln1_g, w.ln1_b, ws.x1, nullptr, nullptr, act, Mrows, nullptr, W, m->eps, s);
-    run_linear(m, w.qkv, ws.x1, nullptr, Mrows, nullptr, ws.qkv, act, JB_EPI_NONE, nullptr, s);
-    std::string why;
-    cudaError_t e;
-    {
-      ProfScope ps(m, kProfAttention, s);
-      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, T, s, &why,
-                           batch * T, m->d_err);
-    }
-    if (e != cudaSuccess) {
-      if (!why.empty()) fail(JB_ERR_INVALID, why);
-      check_cuda(e, "attention");
-    }
-    run_linear(m, w.o, ws.ctx, nullptr, Mrows, nullptr, y, act, JB_EPI_RESIDUAL, x, s);
-    std::swap(x, y);
-    run_ln(m, x, nullptr, w.ln2_g, w.ln2_b, ws.x1, nullptr, nullptr, act, Mrows, nullptr, W, m->eps, s);
-    run_linear(m, w.fc, ws.x1, nullptr, Mrows, nullptr, ws.hf, act, JB_EPI_QUICK_GELU, nullptr, s);
-    run_linear(m, w.proj, ws.hf, nullptr, Mrows, nullptr, y, act, JB_EPI_RESIDUAL, x, s);
-    std::swap(x, y);
-  }
+  void* x = clip_blocks_forward(m, Mrows, nullptr, batch, T, 0, s);
   // CLS (or GAP) pool -> ln_post -> proj (open_clip_vit.rs:339-352), then l2_normalize (candle.rs:425-438)
   PROF_MEM_CALL(launch_vit_pool_ln(x, m->ln_post_g, m->ln_post_b, ws.pooled, act, batch, T, W,
                                 m->gap ? 1 : 0, m->eps, s),

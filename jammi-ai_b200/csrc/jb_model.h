@@ -118,7 +118,9 @@ struct jb_model {
   void *word = nullptr, *pos = nullptr, *type0 = nullptr;
   float *emb_ln_g = nullptr, *emb_ln_b = nullptr;
   std::vector<jb::BertLayerW> bert_layers;
-  // ViT weights
+  // ViT weights (the text tower reuses word / pos for its token and
+  // positional tables, clip_blocks, ln_post for ln_final, proj for
+  // text_projection)
   jb::Linear conv, proj;
   void *cls = nullptr, *vpos = nullptr;
   float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
@@ -149,13 +151,21 @@ struct jb_model {
 
 namespace jb {
 
-jb_model* model_load(const char* path, const char* config_json, int device, int format);
+// family -1: OpenCLIP vision when the config has "model_cfg", else BERT family.
+jb_model* model_load(const char* path, const char* config_json, int device, int format,
+                     int family = -1);
 void model_free(jb_model* m);
 size_t estimate_batch_bytes(const jb_model* m, int batch, int seq);
 // Forward passes on device buffers (the workspace must already hold them).
 void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens, int batch,
                          int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s);
 void clip_forward_device(jb_model* m, const float* d_px, int batch, float* d_out, cudaStream_t s);
+// OpenCLIP text: ids [batch, S] on device (rows end at their largest id, the
+// EOT token) -> L2-normalised [batch, embed_dim] f32.
+void clip_text_forward_device(jb_model* m, const uint32_t* d_ids, int batch, int S, float* d_out,
+                              cudaStream_t s);
+// Embedding width of the pooled output: H (BERT family) or embed_dim (CLIP).
+inline int output_dim(const jb_model* m);
 void ensure_workspace(jb_model* m, int batch, int seq);
 // A workspace for (batch, seq) laid out over caller-owned device memory at
 // `base` (estimate_batch_bytes(m, batch, seq) bytes, 256-byte aligned); the
@@ -196,3 +206,7 @@ void set_lora(jb_model* m, int layer, int site, const float* a, const float* b, 
 int load_lora(jb_model* m, const char* path, double alpha, bool rslora);
 
 }  // namespace jb
+
+inline int jb::output_dim(const jb_model* m) {
+  return m->family == JB_FAMILY_BERT ? m->hidden : m->embed_dim;
+}

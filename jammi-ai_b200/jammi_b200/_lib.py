@@ -24,7 +24,7 @@ DT_F32, DT_BF16, DT_S8, DT_S32 = 0, 1, 2, 3
 # jb_epilogue
 EPI_NONE, EPI_GELU, EPI_QUICK_GELU, EPI_RESIDUAL = 0, 1, 2, 3
 # jb_family
-FAMILY_BERT, FAMILY_CLIP_VISION = 0, 1
+FAMILY_BERT, FAMILY_CLIP_VISION, FAMILY_CLIP_TEXT = 0, 1, 2
 TEXT_BERT, TEXT_DISTILBERT = 0, 1
 
 
@@ -54,6 +54,7 @@ _I = ctypes.c_int
 _SIGS = [
     ("jb_last_error", ctypes.c_char_p, []),
     ("jb_model_load", _I, [ctypes.c_char_p, ctypes.c_char_p, _I, _I, ctypes.POINTER(_P)]),
+    ("jb_model_load_family", _I, [ctypes.c_char_p, ctypes.c_char_p, _I, _I, _I, ctypes.POINTER(_P)]),
     ("jb_model_free", None, [_P]),
     ("jb_model_get_info", _I, [_P, ctypes.POINTER(ModelInfo)]),
     ("jb_estimate_batch_bytes", ctypes.c_size_t, [_P, _I, _I]),
@@ -77,6 +78,7 @@ _SIGS = [
     ("jb_op_quantize_rows_act", _I, [_P, _I, _I, _P, _P, _I, _I, _P]),
     ("jb_op_layernorm", _I, [_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
     ("jb_op_attention", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    ("jb_op_attention_causal", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_pool_normalize", _I, [_P, _I, _P, _P, _I, _I, _I, _P]),
     ("jb_scheduler_new", _P, [ctypes.c_uint64, ctypes.c_double]),
     ("jb_scheduler_new_unlimited", _P, []),

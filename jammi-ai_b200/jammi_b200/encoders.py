@@ -5,7 +5,9 @@
   ``forward_hidden``, ``hidden_size``, ``max_seq_length``, ``SequenceTooLong``.
 * ``OpenClipVisionTransformer``  -- crates/jammi-ai/src/model/backend/open_clip_vit.rs
   with the caller's ``l2_normalize`` (candle.rs:425-438).
-* ``load_model``                 -- ``CandleBackend::load`` for these two families.
+* ``OpenClipText``               -- crates/jammi-encoders/src/clip_text.rs (the
+  OpenCLIP text tower, ``OpenClipTextForward`` in open_clip_text.rs).
+* ``load_model``                 -- ``CandleBackend::load`` for these families.
 
 All compute runs in libjammi_b200.so on the GPU; numpy/torch only carry
 buffers across the boundary.
@@ -45,12 +47,14 @@ def _stream_ptr(stream) -> int:
 class Model:
     """An owned jb_model handle bound to one device."""
 
+    FAMILY = -1  # detected from the config
+
     def __init__(self, weights_path: str, config: dict | str, device: int = 0,
                  fmt: str = "bf16"):
         cfg = config if isinstance(config, str) else json.dumps(config)
         h = ctypes.c_void_p()
-        check(lib().jb_model_load(weights_path.encode(), cfg.encode(), int(device),
-                                  L.FORMATS[fmt], ctypes.byref(h)))
+        check(lib().jb_model_load_family(weights_path.encode(), cfg.encode(), int(device),
+                                         L.FORMATS[fmt], self.FAMILY, ctypes.byref(h)))
         self._h = h
         self.info = self._info()
         self.device = device
@@ -239,6 +243,7 @@ class Bert(Model):
 
 class OpenClipVisionTransformer(Model):
     """OpenCLIP vision tower + ``l2_normalize`` on the B200 library."""
+    FAMILY = L.FAMILY_CLIP_VISION
 
     def __init__(self, *a, **kw):
         super().__init__(*a, **kw)
@@ -264,15 +269,67 @@ class OpenClipVisionTransformer(Model):
         return out
 
 
+class OpenClipText(Model):
+    """``jammi_encoders::ClipText`` (crates/jammi-encoders/src/clip_text.rs) on
+    the B200 library: token ids -> L2-normalised ``[B, embed_dim]`` in the
+    shared CLIP space, pooled at each row's EOT token (its largest id)."""
+    FAMILY = L.FAMILY_CLIP_TEXT
+
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        if self.info.family != L.FAMILY_CLIP_TEXT:
+            raise JbError(L.ERR_INVALID, "not an OpenCLIP text tower")
+
+    def embed_dim(self) -> int:
+        return self.info.output_dim
+
+    def hidden_size(self) -> int:
+        return self.info.hidden
+
+    def context_length(self) -> int:
+        return self.info.max_seq
+
+    def encode(self, ids, stream=None) -> np.ndarray:
+        """Host ids [B, S] (uint32) -> host f32 [B, embed_dim] (``jb_encode_text``;
+        lengths and pooling do not apply)."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        B, S = ids.shape
+        out = np.zeros((B, self.info.output_dim), dtype=np.float32)
+        try:
+            check(lib().jb_encode_text(self._h, _ptr(ids), None, B, S, L.POOL_MEAN, _ptr(out),
+                                       _stream_ptr(stream)))
+        except JbError as e:
+            _raise_seq(e)
+        return out
+
+    def forward(self, input_ids, attention_mask=None) -> np.ndarray:
+        """``ClipText::forward`` (clip_text.rs:296-331); the mask is accepted and
+        unused, as there."""
+        return self.encode(input_ids)
+
+    def encode_device(self, ids, out, stream=None):
+        """Device ids (torch int32/uint32 [B, S]) -> device f32 out; async."""
+        B, S = ids.shape
+        try:
+            check(lib().jb_encode_text_device(self._h, _ptr(ids), None, B, S, L.POOL_MEAN,
+                                              _ptr(out), _stream_ptr(stream)))
+        except JbError as e:
+            _raise_seq(e)
+        return out
+
+
 def load_model(weights_path: str, config_path_or_dict, device: int = 0, fmt: str = "bf16",
-               pooling: str = "mean"):
-    """``CandleBackend::load`` for the BERT and OpenCLIP-vision arms: the
-    family is detected from the config (``model_cfg`` -> OpenCLIP)."""
+               pooling: str = "mean", tower: str = "vision"):
+    """``CandleBackend::load`` for the BERT and OpenCLIP arms: the family is
+    detected from the config (``model_cfg`` -> OpenCLIP); an OpenCLIP checkpoint
+    holds both towers, ``tower`` ("vision" or "text") picks one."""
     cfg = config_path_or_dict
     if isinstance(cfg, str) and os.path.exists(cfg):
         cfg = json.load(open(cfg))
     if isinstance(cfg, str):
         cfg = json.loads(cfg)
     if "model_cfg" in cfg:
+        if tower == "text":
+            return OpenClipText(weights_path, cfg, device, fmt)
         return OpenClipVisionTransformer(weights_path, cfg, device, fmt)
     return Bert(weights_path, cfg, device, fmt, pooling=pooling)

@@ -83,14 +83,17 @@ def layernorm(x: torch.Tensor, gamma, beta, eps: float, residual=None) -> torch.
     return y
 
 
-def attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, heads: int, max_len: int) -> torch.Tensor:
-    """qkv [T, 3*heads*d] packed rows, cu_seqlens int32 [B+1] -> ctx [T, heads*d]."""
+def attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, heads: int, max_len: int,
+              causal: bool = False) -> torch.Tensor:
+    """qkv [T, 3*heads*d] packed rows, cu_seqlens int32 [B+1] -> ctx [T, heads*d]
+    (``causal``: query i sees keys j <= i of its row)."""
     _contig(qkv, cu_seqlens)
     T, three_h = qkv.shape
     H = three_h // 3
     ctx = torch.empty((T, H), dtype=qkv.dtype, device=qkv.device)
-    check(lib().jb_op_attention(_p(qkv), _p(cu_seqlens), _p(ctx), _DT[qkv.dtype],
-                                cu_seqlens.numel() - 1, heads, H // heads, max_len, _s(qkv)))
+    fn = lib().jb_op_attention_causal if causal else lib().jb_op_attention
+    check(fn(_p(qkv), _p(cu_seqlens), _p(ctx), _DT[qkv.dtype], cu_seqlens.numel() - 1, heads,
+             H // heads, max_len, _s(qkv)))
     return ctx
 
 

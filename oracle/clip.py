@@ -10,6 +10,15 @@ Follows ``crates/jammi-ai/src/model/backend/open_clip_vit.rs``:
   patch, no bias) -> CLS cat -> +pos -> ln_pre -> blocks -> CLS or GAP pool
   (:339-346) -> ln_post -> ``@ proj``
 * the caller's ``l2_normalize``    crates/jammi-ai/src/model/backend/candle.rs:425-438
+
+and the OpenCLIP text tower, ``crates/jammi-encoders/src/clip_text.rs``:
+
+* ``ClipTextConfig::from_open_clip_config`` :53-102  (context 77, vocab 49408,
+  heads width/64 by default; MLP width 4x, :195)
+* ``ClipText::forward``            :296-331  token + positional embedding ->
+  causally masked pre-LN blocks (:133-162, mask :350-362) -> ``ln_final`` ->
+  the hidden state at ``argmax(input_ids)`` (the EOT token, :322-326) ->
+  ``@ text_projection`` -> L2 (:379-389)
 """
 from __future__ import annotations
 
@@ -152,3 +161,113 @@ def random_clip_weights(cfg: ClipVisionConfig, seed: int, std: float = 0.02,
         w[p + "mlp.c_proj.weight"] = r(W, F)
         w[p + "mlp.c_proj.bias"] = r(W)
     return {prefix + k: v for k, v in w.items()}
+
+
+# ── OpenCLIP text tower (clip_text.rs) ───────────────────────────────────────
+
+@dataclass
+class ClipTextConfig:
+    """``ClipTextConfig`` (clip_text.rs:30-45, parsed at :53-102)."""
+    width: int = 512
+    layers: int = 12
+    heads: int = 8
+    context_length: int = 77
+    vocab_size: int = 49408
+    embed_dim: int = 512
+
+    @property
+    def mlp(self) -> int:
+        return 4 * self.width  # fixed 4x MLP ratio (clip_text.rs:194-195)
+
+    @classmethod
+    def from_open_clip_config(cls, d: dict) -> "ClipTextConfig":
+        mc = d["model_cfg"]
+        tc = mc["text_cfg"]
+        width = int(tc["width"])
+        return cls(width=width, layers=int(tc["layers"]), heads=int(tc.get("heads", width // 64)),
+                   context_length=int(tc.get("context_length", 77)),
+                   vocab_size=int(tc.get("vocab_size", 49408)), embed_dim=int(mc["embed_dim"]))
+
+    def to_open_clip_config(self) -> dict:
+        return {"model_cfg": {"embed_dim": self.embed_dim, "text_cfg": {
+            "context_length": self.context_length, "vocab_size": self.vocab_size,
+            "width": self.width, "layers": self.layers, "heads": self.heads}}}
+
+
+def clip_text_forward(weights: dict, cfg: ClipTextConfig, input_ids, dtype=np.float64):
+    """``ClipText::forward`` (clip_text.rs:296-331) -> L2-normalised ``[B, embed_dim]``.
+
+    The causal mask adds ``f32::MIN`` above the diagonal (:350-362), whose
+    exponential is exactly 0: keys after the query are excluded.  Pooling takes
+    the first position of the row's largest id (``argmax``, :322-326)."""
+    g = lambda k: np.asarray(weights[k], dtype=dtype)
+    ids = np.asarray(input_ids, dtype=np.int64)
+    B, S = ids.shape
+    if S > cfg.context_length:
+        raise ValueError(f"sequence length {S} exceeds context length {cfg.context_length}")
+    W, nh = cfg.width, cfg.heads
+    d = W // nh
+    x = g("token_embedding.weight")[ids] + g("positional_embedding")[:S][None]
+    causal = np.triu(np.ones((S, S), dtype=bool), k=1)
+    for i in range(cfg.layers):
+        p = f"transformer.resblocks.{i}."
+        h = layer_norm(x, g(p + "ln_1.weight"), g(p + "ln_1.bias"), CLIP_LN_EPS)
+        qkv = linear(h, g(p + "attn.in_proj_weight"), g(p + "attn.in_proj_bias"))
+        qkv = qkv.reshape(B, S, 3, nh, d).transpose(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        sc = (q @ k.transpose(0, 1, 3, 2)) / math.sqrt(d)
+        sc = np.where(causal[None, None], -np.inf, sc)
+        a = softmax_last(sc) @ v
+        a = a.transpose(0, 2, 1, 3).reshape(B, S, W)
+        x = x + linear(a, g(p + "attn.out_proj.weight"), g(p + "attn.out_proj.bias"))
+        h = layer_norm(x, g(p + "ln_2.weight"), g(p + "ln_2.bias"), CLIP_LN_EPS)
+        h = quick_gelu(linear(h, g(p + "mlp.c_fc.weight"), g(p + "mlp.c_fc.bias")))
+        x = x + linear(h, g(p + "mlp.c_proj.weight"), g(p + "mlp.c_proj.bias"))
+    x = layer_norm(x, g("ln_final.weight"), g("ln_final.bias"), CLIP_LN_EPS)
+    eot = ids.argmax(axis=1)
+    pooled = x[np.arange(B), eot]
+    return l2_normalize_image(pooled @ g("text_projection"))
+
+
+def random_clip_text_weights(cfg: ClipTextConfig, seed: int, std: float = 0.02,
+                             dtype=np.float32) -> dict:
+    """Random-init OpenCLIP text weights (root-level keys) N(0, std), LN gain 1 / bias 0."""
+    rng = np.random.default_rng(seed)
+    W, F = cfg.width, cfg.mlp
+    r = lambda *s: (rng.standard_normal(s, dtype=np.float32) * std).astype(dtype)
+    z = lambda n: np.zeros((n,), dtype=dtype)
+    o = lambda n: np.ones((n,), dtype=dtype)
+    w = {
+        "token_embedding.weight": r(cfg.vocab_size, W),
+        "positional_embedding": r(cfg.context_length, W),
+        "ln_final.weight": o(W), "ln_final.bias": z(W),
+        "text_projection": r(W, cfg.embed_dim),
+    }
+    for i in range(cfg.layers):
+        p = f"transformer.resblocks.{i}."
+        w[p + "ln_1.weight"] = o(W); w[p + "ln_1.bias"] = z(W)
+        w[p + "ln_2.weight"] = o(W); w[p + "ln_2.bias"] = z(W)
+        w[p + "attn.in_proj_weight"] = r(3 * W, W)
+        w[p + "attn.in_proj_bias"] = r(3 * W)
+        w[p + "attn.out_proj.weight"] = r(W, W)
+        w[p + "attn.out_proj.bias"] = r(W)
+        w[p + "mlp.c_fc.weight"] = r(F, W)
+        w[p + "mlp.c_fc.bias"] = r(F)
+        w[p + "mlp.c_proj.weight"] = r(W, F)
+        w[p + "mlp.c_proj.bias"] = r(W)
+    return w
+
+
+def random_clip_text_batch(batch: int, seq: int, lengths, seed: int, vocab: int):
+    """OpenCLIP tokenizer layout: <|startoftext|> (vocab-2) first, text ids in
+    [1, vocab-3], <|endoftext|> (vocab-1, the row's largest id) at position
+    len-1, zeros after (clip_bpe.rs:170-200)."""
+    rng = np.random.default_rng(seed)
+    ids = np.zeros((batch, seq), dtype=np.uint32)
+    for b, n in enumerate(lengths):
+        n = int(n)
+        assert 2 <= n <= seq
+        ids[b, 0] = vocab - 2
+        ids[b, 1:n - 1] = rng.integers(1, vocab - 2, size=n - 2)
+        ids[b, n - 1] = vocab - 1
+    return ids

@@ -20,6 +20,8 @@ Fixtures (``.npz``, weights included so the GPU tests need nothing else):
 * ``tiny_clip_gap.npz`` / ``tiny_clip_cls.npz``  OpenCLIP ViT W 32, 1 layer,
   4 heads, patch 4, image 8, embed 16 (the shape of the reference's
   ``tests/fixtures/tiny_open_clip``), global-average and CLS pooling.
+* ``small_clip_text.npz``  OpenCLIP text tower W 64, 2 layers, context 24 (HF
+  ``CLIPTextModelWithProjection``, float64), ragged EOT positions.
 * ``small_distilbert.npz``  DistilBERT (HF ``DistilBertModel``) H 64, 2 layers, 4 heads,
   FFN 256: the BERT weight recipe under DistilBERT names (``distilbert.`` prefix,
   ``transformer.layer.N.{attention.q_lin, ..., ffn.lin1, output_layer_norm}``) and no
@@ -42,7 +44,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.abspath(os.path.join(HERE, "..", "..")))
 
 from oracle.bert import BertConfig, random_bert_weights  # noqa: E402  (weight recipe only)
-from oracle.clip import ClipVisionConfig, random_clip_weights  # noqa: E402
+from oracle.clip import (ClipTextConfig, ClipVisionConfig, random_clip_text_batch,  # noqa: E402
+                         random_clip_text_weights, random_clip_weights)
 
 REF_TINY_BERT = "/root/reference/cookbook/fixtures/tiny_bert"
 
@@ -248,6 +251,80 @@ def clip_fixture(name, cfg: ClipVisionConfig, seed, batch):
     print("wrote", name, raw.shape)
 
 
+def hf_clip_text_embed(w: dict, cfg: ClipTextConfig, ids) -> np.ndarray:
+    """HF ``CLIPTextModelWithProjection`` in float64 over the OpenCLIP text
+    weights: split ``in_proj``, ``text_projection`` transposed, quick-GELU, eps
+    1e-5, ``eos_token_id`` 2 (pooling at ``argmax(input_ids)``), causal mask."""
+    from transformers import CLIPTextConfig, CLIPTextModelWithProjection
+    hcfg = CLIPTextConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.width,
+                          intermediate_size=cfg.mlp, projection_dim=cfg.embed_dim,
+                          num_hidden_layers=cfg.layers, num_attention_heads=cfg.heads,
+                          max_position_embeddings=cfg.context_length, hidden_act="quick_gelu",
+                          layer_norm_eps=1e-5, eos_token_id=2)
+    hcfg._attn_implementation = "eager"
+    model = CLIPTextModelWithProjection(hcfg).eval().to(torch.float64)
+    t = lambda k: torch.from_numpy(np.asarray(w[k], dtype=np.float64))
+    W = cfg.width
+    sd = {
+        "text_model.embeddings.token_embedding.weight": t("token_embedding.weight"),
+        "text_model.embeddings.position_embedding.weight": t("positional_embedding"),
+        "text_model.final_layer_norm.weight": t("ln_final.weight"),
+        "text_model.final_layer_norm.bias": t("ln_final.bias"),
+        "text_projection.weight": t("text_projection").T.contiguous(),
+    }
+    for i in range(cfg.layers):
+        p = f"transformer.resblocks.{i}."
+        q = f"text_model.encoder.layers.{i}."
+        ipw, ipb = t(p + "attn.in_proj_weight"), t(p + "attn.in_proj_bias")
+        for j, nm in enumerate(("q_proj", "k_proj", "v_proj")):
+            sd[q + f"self_attn.{nm}.weight"] = ipw[j * W:(j + 1) * W]
+            sd[q + f"self_attn.{nm}.bias"] = ipb[j * W:(j + 1) * W]
+        sd[q + "self_attn.out_proj.weight"] = t(p + "attn.out_proj.weight")
+        sd[q + "self_attn.out_proj.bias"] = t(p + "attn.out_proj.bias")
+        sd[q + "layer_norm1.weight"] = t(p + "ln_1.weight")
+        sd[q + "layer_norm1.bias"] = t(p + "ln_1.bias")
+        sd[q + "layer_norm2.weight"] = t(p + "ln_2.weight")
+        sd[q + "layer_norm2.bias"] = t(p + "ln_2.bias")
+        sd[q + "mlp.fc1.weight"] = t(p + "mlp.c_fc.weight")
+        sd[q + "mlp.fc1.bias"] = t(p + "mlp.c_fc.bias")
+        sd[q + "mlp.fc2.weight"] = t(p + "mlp.c_proj.weight")
+        sd[q + "mlp.fc2.bias"] = t(p + "mlp.c_proj.bias")
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    missing = [k for k in missing if "position_ids" not in k]
+    assert not missing and not unexpected, (missing, unexpected)
+    # transformers' eager attention takes the softmax in float32; the fixture
+    # keeps the whole forward in float64 (same math, softmax in the input dtype)
+    import transformers.models.clip.modeling_clip as mc
+    stock = mc.eager_attention_forward
+
+    def attention_f64(module, query, key, value, attention_mask, scaling, dropout=0.0, **kw):
+        w_ = torch.matmul(query, key.transpose(-1, -2)) * scaling
+        if attention_mask is not None:
+            w_ = w_ + attention_mask
+        w_ = torch.softmax(w_, dim=-1)
+        return torch.matmul(w_, value).transpose(1, 2).contiguous(), w_
+
+    mc.eager_attention_forward = attention_f64
+    try:
+        with torch.no_grad():
+            e = model(input_ids=torch.from_numpy(ids.astype(np.int64))).text_embeds.numpy()
+    finally:
+        mc.eager_attention_forward = stock
+    return e / np.maximum(np.linalg.norm(e, axis=-1, keepdims=True), 1e-12)
+
+
+def clip_text_fixture(name, cfg: ClipTextConfig, seed, lens, S):
+    # std 0.1: the blocks move the residual stream well away from the embeddings
+    w = random_clip_text_weights(cfg, seed, std=0.1)
+    ids = random_clip_text_batch(len(lens), S, lens, seed + 1, cfg.vocab_size)
+    embed = hf_clip_text_embed(w, cfg, ids)
+    arrs = {"w::" + k: v for k, v in w.items()}
+    arrs.update({"ids": ids, "embed": embed,
+                 "config_json": np.frombuffer(json.dumps(cfg.to_open_clip_config()).encode(), dtype=np.uint8)})
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, embed.shape)
+
+
 def reference_fixture():
     st = os.path.join(REF_TINY_BERT, "model.safetensors")
     if not os.path.exists(st):
@@ -288,6 +365,9 @@ def main():
     distil = BertConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
                         intermediate_size=256, vocab_size=512, max_position_embeddings=64)
     distilbert_fixture("small_distilbert.npz", distil, seed=321, lens=[64, 17, 1, 0, 40], S=64)
+    ct = ClipTextConfig(width=64, layers=2, heads=4, context_length=24, vocab_size=300,
+                        embed_dim=32)
+    clip_text_fixture("small_clip_text.npz", ct, seed=505, lens=[24, 7, 2, 15, 24, 11], S=24)
     reference_fixture()
 
 

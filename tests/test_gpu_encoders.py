@@ -421,3 +421,60 @@ def test_lora_rejected_in_int8():
     model = _bert(ob.random_bert_weights(cfg, seed=671), cfg.to_dict(), "int8")
     with pytest.raises(JbError):
         model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)
+
+
+# ── OpenCLIP text tower (row (f): sibling encoders) ──────────────────────────
+
+def _clip_text(weights, cfg, fmt):
+    from jammi_b200 import OpenClipText
+    return OpenClipText.from_weights(weights, cfg, device=0, fmt=fmt)
+
+
+@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+def test_clip_text_golden(fmt):
+    """ClipText::forward (clip_text.rs:296-331) against HF
+    CLIPTextModelWithProjection: causal blocks, EOT pooling, text_projection, L2."""
+    w, g = load_golden("small_clip_text.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _clip_text(w, cfg, fmt)
+    assert model.embed_dim() == 32 and model.context_length() == 24
+    for _ in range(3):  # direct, capture, replay
+        assert_close_rows(model.encode(g["ids"]), g["embed"], fmt)
+
+
+def test_clip_text_vit_b32_bf16_config():
+    """The ViT-B/32 text tower (width 512, 12 layers, 8 heads, context 77,
+    vocab 49408, embed 512), bf16, ragged EOT positions."""
+    cfg = oc.ClipTextConfig()
+    w = oc.random_clip_text_weights(cfg, seed=701, std=0.05)
+    rng = np.random.default_rng(702)
+    lens = rng.integers(2, 78, size=24)
+    lens[:3] = [77, 2, 3]
+    ids = oc.random_clip_text_batch(24, 77, lens, seed=703, vocab=cfg.vocab_size)
+    ref = oc.clip_text_forward(w, cfg, ids)
+    model = _clip_text(w, cfg.to_open_clip_config(), "bf16")
+    assert_close_rows(model.encode(ids), ref, "bf16")
+    # ids after the EOT token are never computed: the output does not move
+    noisy = ids.copy()
+    for b, n in enumerate(lens):
+        noisy[b, n:] = rng.integers(1, cfg.vocab_size - 2, size=77 - n)
+    assert np.array_equal(model.encode(noisy), model.encode(ids))
+    # a shorter padded width gives the same rows (positions are absolute)
+    short = ids[3:, :int(lens[3:].max())]
+    np.testing.assert_allclose(model.encode(short), model.encode(ids)[3:], rtol=0, atol=2e-6)
+
+
+def test_clip_text_errors():
+    from jammi_b200 import SequenceTooLong
+    from jammi_b200._lib import JbError
+    w, g = load_golden("small_clip_text.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = _clip_text(w, cfg, "f32")
+    with pytest.raises(SequenceTooLong):  # clip_text.rs:302-308
+        model.encode(np.zeros((1, 25), np.uint32))
+    bad = g["ids"].copy()
+    bad[0, 0] = 300  # vocab 300
+    with pytest.raises(JbError):
+        model.encode(bad)
+    with pytest.raises(JbError):  # text towers carry no projection head or LoRA sites here
+        model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)

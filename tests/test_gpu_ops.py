@@ -244,7 +244,7 @@ def test_layernorm(dev, dtype, cols, with_res):
 
 # ── attention (varlen) ──────────────────────────────────────────────────────
 
-def _attn_ref(qkv, cu, heads):
+def _attn_ref(qkv, cu, heads, causal=False):
     T, three_h = qkv.shape
     H = three_h // 3
     d = H // heads
@@ -257,7 +257,10 @@ def _attn_ref(qkv, cu, heads):
             q = qkv[s:e, h * d:(h + 1) * d]
             k = qkv[s:e, H + h * d:H + (h + 1) * d]
             v = qkv[s:e, 2 * H + h * d:2 * H + (h + 1) * d]
-            out[s:e, h * d:(h + 1) * d] = ob.softmax_last(q @ k.T / math.sqrt(d)) @ v
+            sc = q @ k.T / math.sqrt(d)
+            if causal:  # clip_text.rs:350-362: f32::MIN above the diagonal
+                sc = np.where(np.triu(np.ones(sc.shape, dtype=bool), 1), -np.inf, sc)
+            out[s:e, h * d:(h + 1) * d] = ob.softmax_last(sc) @ v
     return out
 
 
@@ -284,6 +287,35 @@ def test_attention_varlen(dev, dtype, heads, d, lens):
     err = np.abs(ctx.double().cpu().numpy() - ref).max()
     tol = 2e-2 if dtype == "bf16" else 1e-5  # bf16: P and V in bf16, outputs |.| < ~3
     assert err < tol, err
+
+
+@pytest.mark.parametrize("dtype,heads,d,lens", [
+    ("bf16", 8, 64, [77, 1, 2, 63, 64, 65, 128, 129, 30]),
+    ("bf16", 12, 64, [200, 0, 7]),
+    ("f32", 8, 64, [77, 5, 1, 40]),
+    ("f32", 4, 16, [24, 7, 2]),
+])
+def test_attention_causal(dev, dtype, heads, d, lens):
+    """The OpenCLIP text mask: query i attends to keys j <= i of its row."""
+    ops = _ops()
+    rng = np.random.default_rng(sum(lens) + 7 * heads)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = (rng.standard_normal((T, 3 * heads * d)) * 1.5).astype(np.float32)
+    qt = _bf16(qkv, dev) if dtype == "bf16" else torch.from_numpy(qkv).to(dev)
+    ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens), causal=True)
+    ops.sync()
+    ref = _attn_ref(qt.double().cpu().numpy(), cu, heads, causal=True)
+    err = np.abs(ctx.double().cpu().numpy() - ref).max()
+    tol = 2e-2 if dtype == "bf16" else 1e-5
+    assert err < tol, err
+    # a row's first query sees only itself: its context is its own V exactly (f32)
+    if dtype == "f32":
+        H = heads * d
+        for b in range(len(lens)):
+            if lens[b]:
+                r = cu[b]
+                np.testing.assert_allclose(ctx[r].cpu().numpy(), qkv[r, 2 * H:], rtol=0, atol=1e-6)
 
 
 # ── pooling + L2 ────────────────────────────────────────────────────────────

@@ -139,6 +139,32 @@ def test_clip_oracle_matches_golden(name):
     np.testing.assert_allclose(oc.l2_normalize_image(raw), g["embed"], atol=1e-9, rtol=0)
 
 
+def test_clip_text_oracle_matches_golden():
+    """ClipText::forward restated against HF CLIPTextModelWithProjection (f64)."""
+    w, g = load_golden("small_clip_text.npz")
+    cfg = oc.ClipTextConfig.from_open_clip_config(json.loads(bytes(g["config_json"]).decode()))
+    e = oc.clip_text_forward(w, cfg, g["ids"])
+    np.testing.assert_allclose(e, g["embed"], atol=1e-9, rtol=0)
+    np.testing.assert_allclose(np.linalg.norm(e, axis=1), 1.0, atol=1e-12)
+
+
+def test_clip_text_oracle_causal_and_eot():
+    """Under the causal mask, ids after the EOT token (the row's largest id)
+    cannot reach the pooled position (clip_text.rs:287-295, 322-326); a longer
+    context than the config's is SequenceTooLong (:302-308)."""
+    w, g = load_golden("small_clip_text.npz")
+    cfg = oc.ClipTextConfig.from_open_clip_config(json.loads(bytes(g["config_json"]).decode()))
+    ids = g["ids"].copy()
+    eot = ids.argmax(1)
+    rng = np.random.default_rng(1)
+    for b in range(ids.shape[0]):
+        tail = ids.shape[1] - eot[b] - 1
+        ids[b, eot[b] + 1:] = rng.integers(1, cfg.vocab_size - 2, size=tail)
+    np.testing.assert_allclose(oc.clip_text_forward(w, cfg, ids), g["embed"], atol=1e-12, rtol=0)
+    with pytest.raises(ValueError):
+        oc.clip_text_forward(w, cfg, np.zeros((1, cfg.context_length + 1), np.uint32))
+
+
 # ── int8 format: integer-exact properties ───────────────────────────────────
 
 def test_quantize_rows_properties():
