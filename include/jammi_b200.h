@@ -58,10 +58,13 @@ typedef enum {
 /* JB_FAMILY_CLIP_TEXT: the OpenCLIP text tower (crates/jammi-encoders/src/clip_text.rs),
  * loaded from the same checkpoint as the vision tower (root-level keys). */
 typedef enum { JB_FAMILY_BERT = 0, JB_FAMILY_CLIP_VISION = 1, JB_FAMILY_CLIP_TEXT = 2 } jb_family;
-/* BERT-family text encoders sharing one forward: BERT (crates/jammi-encoders/src/bert.rs)
- * and DistilBERT (crates/jammi-encoders/src/distilbert.rs: no token-type table,
- * config keys dim / n_layers / n_heads / hidden_dim, weights under "distilbert."). */
-typedef enum { JB_TEXT_BERT = 0, JB_TEXT_DISTILBERT = 1 } jb_text_variant;
+/* BERT-family text encoders: BERT (crates/jammi-encoders/src/bert.rs) and
+ * DistilBERT (crates/jammi-encoders/src/distilbert.rs: no token-type table,
+ * config keys dim / n_layers / n_heads / hidden_dim, weights under "distilbert.")
+ * share one forward; ModernBERT (crates/jammi-encoders/src/modernbert.rs,
+ * "model_type": "modernbert": RoPE, GeGLU, bias-free pre-norm layers, weights
+ * under "model.") has its own, behind the same text entry points. */
+typedef enum { JB_TEXT_BERT = 0, JB_TEXT_DISTILBERT = 1, JB_TEXT_MODERNBERT = 2 } jb_text_variant;
 
 typedef struct jb_model jb_model;
 

@@ -121,6 +121,13 @@ cudaError_t launch_eot_lens(const uint32_t* ids, int batch, int S, uint32_t* len
 cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s);
 // Row-wise x / clamp(||x||, 1e-12) over f32 [rows, cols], in place.
 cudaError_t launch_l2_rows(float* x, int rows, int cols, cudaStream_t s);
+// ModernBERT: RoPE on the Q and K column blocks of packed qkv [T, 3 * heads * d]
+// in place; cos_t / sin_t f32 [max_pos, d/2], position = index within the row.
+cudaError_t launch_rope_qk(void* qkv, int dtype, const int* cu, int batch, int max_seq, int heads,
+                           int d, const float* cos_t, const float* sin_t, cudaStream_t s);
+// ModernBERT GeGLU: out[r, j] = gelu_erf(ug[r, j]) * ug[r, I + j], rows < *drows.
+cudaError_t launch_geglu(const void* ug, void* out, int dtype, int rows, const int* drows, int I,
+                         cudaStream_t s);
 // x = gelu_erf(x) in place over rows < *drows (drows may be null).
 cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int cols,
                              cudaStream_t s);

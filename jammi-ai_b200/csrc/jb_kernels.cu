@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
       id = 0;
     }
     const T* w = static_cast<const T*>(a.word) + static_cast<size_t>(id) * a.H;
-    const T* pe = static_cast<const T*>(a.pos) + static_cast<size_t>(p) * a.H;
+    const T* pe = a.pos ? static_cast<const T*>(a.pos) + static_cast<size_t>(p) * a.H : nullptr;
     const T* te = static_cast<const T*>(a.type0);
     float v[MAXV * VN];
 #pragma unroll
@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(EmbedArgs a) {
       if (vi < nvec) {
         float t1[VN], t2[VN];
         Vec<T>::load(w + vi * VN, v + i * VN);
+        if (!pe) continue;  // token embedding alone (ModernBERT, modernbert.rs:331-332)
         Vec<T>::load(pe + vi * VN, t2);
         if (te) {
           Vec<T>::load(te + vi * VN, t1);
@@ -507,6 +508,59 @@ __global__ void __launch_bounds__(256) gelu_rows_kernel(T* x, int rows, const in
 #pragma unroll
     for (int e = 0; e < VN; ++e) v[e] = gelu_erf(v[e]);
     Vec<T>::store(x + i * VN, v);
+  }
+}
+
+// RoPE on the Q and K blocks of packed qkv rows [T, 3H], in place
+// (RotaryEmbedding::apply, modernbert.rs:133-163): for head h and i < d/2,
+//   (x_i, x_{i+d/2}) -> (x_i c - x_{i+d/2} s, x_{i+d/2} c + x_i s),
+// c, s = cos / sin[p][i] of the token's position p in its row.  One warp per
+// token, persistent over the (row, position) slots; padding slots skipped.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_qk_kernel(T* qkv, const int* __restrict__ cu, int batch,
+                                                      int max_seq, int heads, int d,
+                                                      const float* __restrict__ cos_t,
+                                                      const float* __restrict__ sin_t) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = d >> 1, H = heads * d, pairs = 2 * heads * half;
+  const int slots = batch * max_seq;
+  for (int slot = blockIdx.x * 8 + warp; slot < slots; slot += gridDim.x * 8) {
+    const int b = slot / max_seq, p = slot % max_seq;
+    const int start = cu[b];
+    if (p >= cu[b + 1] - start) continue;  // warp-uniform
+    T* row = qkv + static_cast<size_t>(start + p) * 3 * H;
+    const float* cr = cos_t + static_cast<size_t>(p) * half;
+    const float* sr = sin_t + static_cast<size_t>(p) * half;
+    for (int j = lane; j < pairs; j += 32) {
+      const int h = j / half, i = j - h * half;  // h < heads: Q, else K (contiguous)
+      T* x = row + h * d + i;
+      const float x1 = to_f(x[0]), x2 = to_f(x[half]);
+      const float c = cr[i], sn = sr[i];
+      x[0] = from_f<T>(x1 * c - x2 * sn);
+      x[half] = from_f<T>(x2 * c + x1 * sn);
+    }
+  }
+}
+
+// GeGLU of ModernBertMlp::forward (modernbert.rs:241-254): up_gate [rows, 2I]
+// -> out[r, j] = gelu_erf(up_gate[r, j]) * up_gate[r, I + j], out [rows, I].
+template <typename T>
+__global__ void __launch_bounds__(256) geglu_kernel(const T* __restrict__ ug, T* __restrict__ out,
+                                                    int rows, const int* drows, int I) {
+  constexpr int VN = Vec<T>::N;
+  const int R = drows ? min(*drows, rows) : rows;
+  const int vpr = I / VN;
+  const size_t nv = static_cast<size_t>(R) * vpr;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / vpr;
+    const int c = static_cast<int>(i - r * vpr) * VN;
+    float g[VN], u[VN];
+    Vec<T>::load(ug + r * 2 * I + c, g);
+    Vec<T>::load(ug + r * 2 * I + I + c, u);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) g[e] = gelu_erf(g[e]) * u[e];
+    Vec<T>::store(out + r * I + c, g);
   }
 }
 
@@ -970,6 +1024,41 @@ cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int
   } else {
     if (cols % 4) return cudaErrorInvalidValue;
     gelu_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(x), rows, drows, cols);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_qk(void* qkv, int dtype, const int* cu, int batch, int max_seq, int heads,
+                           int d, const float* cos_t, const float* sin_t, cudaStream_t s) {
+  const size_t slots = static_cast<size_t>(batch) * max_seq;
+  if (slots == 0) return cudaSuccess;
+  if (d % 2) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned grid = std::min<unsigned>(blocks_for(slots, 8), static_cast<unsigned>(num_sms(dev)) * 8u);
+  if (dtype == JB_DT_BF16)
+    rope_qk_kernel<bf16><<<grid, 256, 0, s>>>(static_cast<bf16*>(qkv), cu, batch, max_seq, heads, d,
+                                              cos_t, sin_t);
+  else
+    rope_qk_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(qkv), cu, batch, max_seq, heads,
+                                               d, cos_t, sin_t);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_geglu(const void* ug, void* out, int dtype, int rows, const int* drows, int I,
+                         cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned grid = static_cast<unsigned>(num_sms(dev)) * 8u;
+  if (dtype == JB_DT_BF16) {
+    if (I % 8) return cudaErrorInvalidValue;
+    geglu_kernel<bf16><<<grid, 256, 0, s>>>(static_cast<const bf16*>(ug), static_cast<bf16*>(out),
+                                            rows, drows, I);
+  } else {
+    if (I % 4) return cudaErrorInvalidValue;
+    geglu_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(ug), static_cast<float*>(out),
+                                             rows, drows, I);
   }
   return cudaGetLastError();
 }

@@ -287,8 +287,68 @@ struct TextNames {
   std::string prefix, type_table, layer, q, k, v, o, ln1, ffn1, ffn2, ln2;
 };
 
+// ModernBert::builder().build (modernbert.rs:495-625) with ModernBertConfig's
+// serde defaults (:72-90): layer_norm_eps 1e-5, global_rope_theta 160000 for
+// every layer; LayerNorms without bias, linears without bias.
+void load_modernbert(jb_model* m, const SafeTensors& st, const Json& cfg) {
+  m->family = JB_FAMILY_BERT;
+  m->variant = JB_TEXT_MODERNBERT;
+  m->hidden = static_cast<int>(cfg.num_or("hidden_size", 0));
+  m->layers = static_cast<int>(cfg.num_or("num_hidden_layers", 0));
+  m->heads = static_cast<int>(cfg.num_or("num_attention_heads", 0));
+  m->ffn = static_cast<int>(cfg.num_or("intermediate_size", 0));
+  m->vocab = static_cast<int>(cfg.num_or("vocab_size", 0));
+  m->max_pos = static_cast<int>(cfg.num_or("max_position_embeddings", 0));
+  m->eps = static_cast<float>(cfg.num_or("layer_norm_eps", 1e-5));
+  m->type_vocab = 0;
+  const double theta = cfg.num_or("global_rope_theta", 160000.0);
+  const int H = m->hidden, I = m->ffn;
+  if (H <= 0 || m->layers <= 0 || m->heads <= 0 || I <= 0 || m->vocab <= 0 || m->max_pos <= 0)
+    fail(JB_ERR_INVALID, "config.json: incomplete ModernBERT dimensions");
+  if (H % m->heads)  // ModernBertBuilder::build (modernbert.rs:502-511)
+    fail(JB_ERR_INVALID, "hidden_size (" + std::to_string(H) + ") must be divisible by num_attention_heads (" +
+                             std::to_string(m->heads) + ")");
+  if (H > 1024 || H % 8 || I % 8) fail(JB_ERR_INVALID, "ModernBERT: hidden_size and intermediate_size must be multiples of 8, hidden_size <= 1024");
+  if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are defined for BERT and DistilBERT encoders");
+  const int d = H / m->heads;
+  if (d % 2) fail(JB_ERR_INVALID, "ModernBERT: head_dim must be even (RoPE pairs)");
+  const std::string p = st.has("model.embeddings.tok_embeddings.weight") ? "model." : "";
+  const int ld = linear_dtype(m->format);
+  const std::vector<float> zeros(H, 0.f);
+  m->word = upload_act(m, st.f32(p + "embeddings.tok_embeddings.weight", int64_t(m->vocab) * H));
+  m->emb_ln_g = upload_f32(m, st.f32(p + "embeddings.norm.weight", H));
+  m->emb_ln_b = upload_f32(m, zeros);
+  for (int l = 0; l < m->layers; ++l) {
+    const std::string q = p + "layers." + std::to_string(l) + ".";
+    BertLayerW w;
+    w.qkv = load_linear(m, st, {q + "attn.Wqkv"}, {3 * H}, H, false, ld);
+    w.o = load_linear(m, st, {q + "attn.Wo"}, {H}, H, false, ld);
+    w.ffn1 = load_linear(m, st, {q + "mlp.Wi"}, {2 * I}, H, false, ld);
+    w.ffn2 = load_linear(m, st, {q + "mlp.Wo"}, {H}, I, false, ld);
+    if (l > 0) w.ln1_g = upload_f32(m, st.f32(q + "attn_norm.weight", H));  // layer 0: identity
+    w.ln1_b = m->emb_ln_b;
+    w.ln2_g = upload_f32(m, st.f32(q + "mlp_norm.weight", H));
+    w.ln2_b = m->emb_ln_b;
+    m->bert_layers.push_back(w);
+  }
+  m->final_ln_g = upload_f32(m, st.f32(p + "final_norm.weight", H));
+  m->final_ln_b = m->emb_ln_b;
+  // RotaryEmbedding::new (modernbert.rs:106-131): theta in f64, tables in f32
+  const int half = d / 2;
+  std::vector<float> c(static_cast<size_t>(m->max_pos) * half), sn(c.size());
+  for (int pos = 0; pos < m->max_pos; ++pos)
+    for (int i = 0; i < half; ++i) {
+      const double t = static_cast<double>(pos) * std::pow(theta, -2.0 * i / static_cast<double>(d));
+      c[static_cast<size_t>(pos) * half + i] = static_cast<float>(std::cos(t));
+      sn[static_cast<size_t>(pos) * half + i] = static_cast<float>(std::sin(t));
+    }
+  m->rope_cos = upload_f32(m, c);
+  m->rope_sin = upload_f32(m, sn);
+}
+
 void load_bert(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->family = JB_FAMILY_BERT;
+  if (cfg.str_or("model_type", "") == "modernbert") return load_modernbert(m, st, cfg);
   const bool distil = cfg.str_or("model_type", "") == "distilbert" ||
                       (cfg.get("dim") && cfg.get("n_layers"));
   m->variant = distil ? JB_TEXT_DISTILBERT : JB_TEXT_BERT;
@@ -485,8 +545,10 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
   p.total = 256;
   p.out = round_up(B * std::max<size_t>(H, m->embed_dim) * 4);
   p.x = round_up(T * H * e);
-  p.qkv = round_up(T * 3 * H * e);
-  p.hf = round_up(T * F * e);
+  const bool modern = m->family == JB_FAMILY_BERT && m->variant == JB_TEXT_MODERNBERT;
+  // ModernBERT: hf holds Wi's [T, 2I]; the GeGLU output [T, I] reuses qkv
+  p.qkv = round_up(T * (modern ? std::max(3 * H, F) : 3 * H) * e);
+  p.hf = round_up(T * (modern ? 2 * F : F) * e);
   p.head_t = m->head_rank > 0 ? round_up(B * m->head_rank * 4) : 0;
   p.lora_t = m->lora_width > 0 ? round_up(T * m->lora_width * e) : 0;
   if (m->format == JB_FMT_INT8) {
@@ -864,6 +926,8 @@ void set_lora(jb_model* m, int layer, int site, const float* a, const float* b, 
   if (m->family != JB_FAMILY_BERT) fail(JB_ERR_INVALID, "LoRA adapters apply to text encoders");
   if (m->format == JB_FMT_INT8)
     fail(JB_ERR_INVALID, "LoRA adapters run in the f32 and bf16 formats");
+  if (m->variant == JB_TEXT_MODERNBERT)
+    fail(JB_ERR_INVALID, "LoRA adapters are wired for the BERT and DistilBERT layer layout");
   if (layer < 0 || layer >= m->layers || site < 0 || site >= kLoraSites || rank < 0 ||
       (rank > 0 && (!a || !b)))
     fail(JB_ERR_INVALID, "LoRA: bad layer, site or rank");
@@ -1002,24 +1066,21 @@ void run_ln(jb_model* m, const void* x, const void* resid, const float* g, const
 }
 }  // namespace
 
-void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens, int batch,
-                         int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s) {
+namespace {
+// ModernBert::forward_hidden (modernbert.rs:318-340) over packed rows, cu in
+// ws.cu: embedding norm; per layer x += Wo(attn(rope(Wqkv(attn_norm(x)))))
+// (layer 0 without attn_norm) and x += mlp.Wo(geglu(Wi(mlp_norm(x))));
+// final_norm.  Returns the buffer holding the final hidden states.
+void* modernbert_forward(jb_model* m, const uint32_t* d_ids, int batch, int max_seq, cudaStream_t s) {
   Workspace& ws = m->ws;
-  const int H = m->hidden, Mcap = batch * max_seq;
-  const bool q8 = m->format == JB_FMT_INT8;
-  const int act = m->act;
-  PROF_MEM_CALL(launch_lens_to_cu(d_lens, batch, max_seq, ws.cu, ws.total, m->d_err, s), "lengths");
+  const int H = m->hidden, I = m->ffn, Mcap = batch * max_seq, act = m->act;
   EmbedArgs ea;
   ea.ids = d_ids;
   ea.cu = ws.cu;
   ea.word = m->word;
-  ea.pos = m->pos;
-  ea.type0 = m->type0;
   ea.gamma = m->emb_ln_g;
   ea.beta = m->emb_ln_b;
   ea.y = ws.x;
-  ea.yq = q8 ? ws.aq : nullptr;
-  ea.yscale = q8 ? ws.as : nullptr;
   ea.dtype = act;
   ea.batch = batch;
   ea.max_seq = max_seq;
@@ -1028,60 +1089,126 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
   ea.eps = m->eps;
   ea.err = m->d_err;
   PROF_MEM_CALL(launch_embed_ln(ea, s), "embeddings");
-  int layer_idx = 0;
   for (const BertLayerW& w : m->bert_layers) {
-    const LoraLayerW* lw = m->lora.empty() ? nullptr : &m->lora[layer_idx];
-    ++layer_idx;
-    // base(x) + scaling (x A^T) B^T: T = x A^T, then C += T B^T in place
-    auto lora = [&](const Linear& A, const Linear& B, const void* x, void* C) {
-      if (!A.w) return;
-      run_linear(m, A, x, nullptr, Mcap, ws.total, ws.lora_t, act, JB_EPI_NONE, nullptr, s);
-      run_linear(m, B, ws.lora_t, nullptr, Mcap, ws.total, C, act, JB_EPI_RESIDUAL, C, s);
-    };
-    // BertSelfAttention (bert.rs:135-155): fused QKV projection
-    run_linear(m, w.qkv, q8 ? ws.aq : ws.x, ws.as, Mcap, ws.total, ws.qkv, act, JB_EPI_NONE, nullptr, s);
-    if (lw) lora(lw->a_qkv, lw->b_qkv, ws.x, ws.qkv);
+    // ModernBertAttention::forward (modernbert.rs:178-227)
+    const void* h = ws.x;
+    if (w.ln1_g) {
+      run_ln(m, ws.x, nullptr, w.ln1_g, w.ln1_b, ws.x1, nullptr, nullptr, act, Mcap, ws.total, H, m->eps, s);
+      h = ws.x1;
+    }
+    run_linear(m, w.qkv, h, nullptr, Mcap, ws.total, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+    PROF_MEM_CALL(launch_rope_qk(ws.qkv, act, ws.cu, batch, max_seq, m->heads, H / m->heads, m->rope_cos,
+                                 m->rope_sin, s),
+                  "rope");
     std::string why;
     cudaError_t e;
     {
       ProfScope ps(m, kProfAttention, s);
-      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s,
-                           &why, Mcap, m->d_err);
+      e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s, &why,
+                           Mcap, m->d_err);
     }
     if (e != cudaSuccess) {
       if (!why.empty()) fail(JB_ERR_INVALID, why);
       check_cuda(e, "attention");
     }
-    if (q8) PROF_MEM_CALL(launch_quantize_rows(ws.ctx, act, ws.aq, ws.as, Mcap, ws.total, H, s), "quantize");
-    // BertSelfOutput (bert.rs:164-167): LN(dense(ctx) + x)
-    run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
-    if (lw) lora(lw->a_o, lw->b_o, ws.ctx, ws.y);
-    run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
-           Mcap, ws.total, H, m->eps, s);
-    // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1)).  int8: the
-    // GELU runs in the quantiser that FFN2's input needs anyway, on the bf16
-    // dense output (the reference's bf16 order: Linear -> bf16 -> gelu).
-    const bool lora1 = lw && lw->a_1.w;  // the adapter adds before the activation
-    run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act,
-               (q8 || lora1) ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
-    if (lora1) {
-      lora(lw->a_1, lw->b_1, ws.x1, ws.hf);
-      PROF_MEM_CALL(launch_gelu_rows(ws.hf, act, Mcap, ws.total, m->ffn, s), "gelu");
+    run_linear(m, w.o, ws.ctx, nullptr, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
+    // ModernBertMlp::forward (modernbert.rs:241-254); the GeGLU output reuses qkv
+    run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x1, nullptr, nullptr, act, Mcap, ws.total, H, m->eps, s);
+    run_linear(m, w.ffn1, ws.x1, nullptr, Mcap, ws.total, ws.hf, act, JB_EPI_NONE, nullptr, s);
+    PROF_MEM_CALL(launch_geglu(ws.hf, ws.qkv, act, Mcap, ws.total, I, s), "geglu");
+    run_linear(m, w.ffn2, ws.qkv, nullptr, Mcap, ws.total, ws.x, act, JB_EPI_RESIDUAL, ws.y, s);
+  }
+  run_ln(m, ws.x, nullptr, m->final_ln_g, m->final_ln_b, ws.x1, nullptr, nullptr, act, Mcap, ws.total, H,
+         m->eps, s);
+  return ws.x1;
+}
+}  // namespace
+
+void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_lens, int batch,
+                         int max_seq, int pooling, float* d_out, float* d_hidden, cudaStream_t s) {
+  Workspace& ws = m->ws;
+  const int H = m->hidden, Mcap = batch * max_seq;
+  const bool q8 = m->format == JB_FMT_INT8;
+  const int act = m->act;
+  PROF_MEM_CALL(launch_lens_to_cu(d_lens, batch, max_seq, ws.cu, ws.total, m->d_err, s), "lengths");
+  void* hid = ws.x;  // the final hidden states
+  if (m->variant == JB_TEXT_MODERNBERT) {
+    hid = modernbert_forward(m, d_ids, batch, max_seq, s);
+  } else {
+    EmbedArgs ea;
+    ea.ids = d_ids;
+    ea.cu = ws.cu;
+    ea.word = m->word;
+    ea.pos = m->pos;
+    ea.type0 = m->type0;
+    ea.gamma = m->emb_ln_g;
+    ea.beta = m->emb_ln_b;
+    ea.y = ws.x;
+    ea.yq = q8 ? ws.aq : nullptr;
+    ea.yscale = q8 ? ws.as : nullptr;
+    ea.dtype = act;
+    ea.batch = batch;
+    ea.max_seq = max_seq;
+    ea.H = H;
+    ea.vocab = m->vocab;
+    ea.eps = m->eps;
+    ea.err = m->d_err;
+    PROF_MEM_CALL(launch_embed_ln(ea, s), "embeddings");
+    int layer_idx = 0;
+    for (const BertLayerW& w : m->bert_layers) {
+      const LoraLayerW* lw = m->lora.empty() ? nullptr : &m->lora[layer_idx];
+      ++layer_idx;
+      // base(x) + scaling (x A^T) B^T: T = x A^T, then C += T B^T in place
+      auto lora = [&](const Linear& A, const Linear& B, const void* x, void* C) {
+        if (!A.w) return;
+        run_linear(m, A, x, nullptr, Mcap, ws.total, ws.lora_t, act, JB_EPI_NONE, nullptr, s);
+        run_linear(m, B, ws.lora_t, nullptr, Mcap, ws.total, C, act, JB_EPI_RESIDUAL, C, s);
+      };
+      // BertSelfAttention (bert.rs:135-155): fused QKV projection
+      run_linear(m, w.qkv, q8 ? ws.aq : ws.x, ws.as, Mcap, ws.total, ws.qkv, act, JB_EPI_NONE, nullptr, s);
+      if (lw) lora(lw->a_qkv, lw->b_qkv, ws.x, ws.qkv);
+      std::string why;
+      cudaError_t e;
+      {
+        ProfScope ps(m, kProfAttention, s);
+        e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s,
+                             &why, Mcap, m->d_err);
+      }
+      if (e != cudaSuccess) {
+        if (!why.empty()) fail(JB_ERR_INVALID, why);
+        check_cuda(e, "attention");
+      }
+      if (q8) PROF_MEM_CALL(launch_quantize_rows(ws.ctx, act, ws.aq, ws.as, Mcap, ws.total, H, s), "quantize");
+      // BertSelfOutput (bert.rs:164-167): LN(dense(ctx) + x)
+      run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
+      if (lw) lora(lw->a_o, lw->b_o, ws.ctx, ws.y);
+      run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
+             Mcap, ws.total, H, m->eps, s);
+      // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1)).  int8: the
+      // GELU runs in the quantiser that FFN2's input needs anyway, on the bf16
+      // dense output (the reference's bf16 order: Linear -> bf16 -> gelu).
+      const bool lora1 = lw && lw->a_1.w;  // the adapter adds before the activation
+      run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act,
+                 (q8 || lora1) ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
+      if (lora1) {
+        lora(lw->a_1, lw->b_1, ws.x1, ws.hf);
+        PROF_MEM_CALL(launch_gelu_rows(ws.hf, act, Mcap, ws.total, m->ffn, s), "gelu");
+      }
+      if (q8)
+        PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s,
+                                           JB_EPI_GELU),
+                      "quantize");
+      // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
+      run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);
+      if (lw) lora(lw->a_2, lw->b_2, ws.hf, ws.y);
+      run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
+             Mcap, ws.total, H, m->eps, s);
     }
-    if (q8)
-      PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s,
-                                         JB_EPI_GELU),
-                    "quantize");
-    // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
-    run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);
-    if (lw) lora(lw->a_2, lw->b_2, ws.hf, ws.y);
-    run_ln(m, ws.y, nullptr, w.ln2_g, w.ln2_b, ws.x, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
-           Mcap, ws.total, H, m->eps, s);
   }
   if (d_hidden)
-    PROF_MEM_CALL(launch_unpack_hidden(ws.x, act, ws.cu, d_hidden, batch, max_seq, H, s), "unpack");
+    PROF_MEM_CALL(launch_unpack_hidden(hid, act, ws.cu, d_hidden, batch, max_seq, H, s), "unpack");
   if (d_out) {
-    PROF_MEM_CALL(launch_pool_normalize(ws.x, act, ws.cu, d_out, batch, H, pooling, s), "pooling");
+    PROF_MEM_CALL(launch_pool_normalize(hid, act, ws.cu, d_out, batch, H, pooling, s), "pooling");
     if (m->head_rank > 0) {  // projection head: d_out += (d_out A^T) (s B)^T, f32
       Linear la, lb;
       la.w = m->head_a;

@@ -117,6 +117,11 @@ struct jb_model {
   // BERT weights
   void *word = nullptr, *pos = nullptr, *type0 = nullptr;
   float *emb_ln_g = nullptr, *emb_ln_b = nullptr;
+  // ModernBERT: final_norm, RoPE tables f32 [max_pos, head_dim / 2] (the layers
+  // reuse BertLayerW: qkv = Wqkv, o = attn.Wo, ffn1 = Wi [2I, H], ffn2 = mlp.Wo,
+  // ln1 = attn_norm (null in layer 0), ln2 = mlp_norm; betas all zero)
+  float *final_ln_g = nullptr, *final_ln_b = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
   std::vector<jb::BertLayerW> bert_layers;
   // ViT weights (the text tower reuses word / pos for its token and
   // positional tables, clip_blocks, ln_post for ln_final, proj for

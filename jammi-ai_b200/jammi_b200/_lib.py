@@ -25,7 +25,7 @@ DT_F32, DT_BF16, DT_S8, DT_S32 = 0, 1, 2, 3
 EPI_NONE, EPI_GELU, EPI_QUICK_GELU, EPI_RESIDUAL = 0, 1, 2, 3
 # jb_family
 FAMILY_BERT, FAMILY_CLIP_VISION, FAMILY_CLIP_TEXT = 0, 1, 2
-TEXT_BERT, TEXT_DISTILBERT = 0, 1
+TEXT_BERT, TEXT_DISTILBERT, TEXT_MODERNBERT = 0, 1, 2
 
 
 class JbError(RuntimeError):

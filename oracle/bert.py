@@ -360,3 +360,100 @@ def distilbert_forward_hidden(weights: dict, d_cfg: dict, input_ids, mask, dtype
         ren = dict(zip(DISTILBERT_LORA_SITES, LORA_SITES))
         lora = {(n, ren.get(s, s)): v for (n, s), v in lora.items()}
     return bert_forward_hidden(w, cfg, input_ids, mask, dtype=dtype, lora=lora)
+
+
+# ── ModernBERT (crates/jammi-encoders/src/modernbert.rs) ─────────────────────
+
+def modernbert_config(cfg: dict) -> dict:
+    """``ModernBertConfig`` (modernbert.rs:72-90): the serde defaults for the
+    optional fields (layer_norm_eps 1e-5, global_rope_theta 160000)."""
+    return {
+        "hidden_size": int(cfg["hidden_size"]), "num_hidden_layers": int(cfg["num_hidden_layers"]),
+        "num_attention_heads": int(cfg["num_attention_heads"]),
+        "intermediate_size": int(cfg["intermediate_size"]), "vocab_size": int(cfg["vocab_size"]),
+        "max_position_embeddings": int(cfg["max_position_embeddings"]),
+        "layer_norm_eps": float(cfg.get("layer_norm_eps", 1e-5)),
+        "global_rope_theta": float(cfg.get("global_rope_theta", 160000.0)),
+    }
+
+
+def modernbert_rope_tables(head_dim: int, max_pos: int, base: float):
+    """``RotaryEmbedding::new`` (modernbert.rs:106-131): theta = pos *
+    base^(-2i/d) in float64, cos / sin stored as float32, ``[max_pos, d/2]``
+    (the reference duplicates the halves to ``[max_pos, d]``)."""
+    i = np.arange(head_dim // 2, dtype=np.float64)
+    inv = np.power(float(base), -2.0 * i / head_dim)
+    theta = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+
+
+def rope_apply(x, cos_half, sin_half):
+    """``RotaryEmbedding::apply`` (modernbert.rs:133-163) on ``[B, h, S, d]``:
+    ``x * cos + rotate_half(x) * sin``, ``rotate_half(x) = cat(-x2, x1)``."""
+    half = x.shape[-1] // 2
+    c = np.concatenate([cos_half, cos_half], axis=-1)[None, None]
+    s = np.concatenate([sin_half, sin_half], axis=-1)[None, None]
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return x * c + rot * s
+
+
+def modernbert_forward_hidden(weights: dict, cfg: dict, input_ids, mask, dtype=np.float64):
+    """``ModernBert::forward_hidden`` (modernbert.rs:318-340) -> ``[B, S, H]``:
+    embedding norm, then per layer the pre-norm attention with RoPE on Q and K
+    (:178-227; layer 0 has no ``attn_norm``) and the GeGLU MLP
+    ``Wo(gelu_erf(gate) * up)`` with gate the first half of ``Wi``'s output
+    (:241-254), each added to its input; ``final_norm`` last.  LayerNorms carry
+    no bias; linears carry none."""
+    c = modernbert_config(cfg)
+    H, L, nh, I = c["hidden_size"], c["num_hidden_layers"], c["num_attention_heads"], c["intermediate_size"]
+    d = H // nh
+    eps = c["layer_norm_eps"]
+    p = "model." if "model.embeddings.tok_embeddings.weight" in weights else ""
+    g = lambda k: np.asarray(weights[p + k], dtype=dtype)
+    ids = np.asarray(input_ids, dtype=np.int64)
+    mask = np.asarray(mask)
+    B, S = ids.shape
+    if S > c["max_position_embeddings"]:
+        raise SequenceTooLong(S, c["max_position_embeddings"])
+    zero = np.zeros((H,), dtype=dtype)
+    x = layer_norm(g("embeddings.tok_embeddings.weight")[ids], g("embeddings.norm.weight"), zero, eps)
+    ext = extended_attention_mask(mask).astype(dtype)
+    cos, sin = modernbert_rope_tables(d, c["max_position_embeddings"], c["global_rope_theta"])
+    cos, sin = cos[:S].astype(dtype), sin[:S].astype(dtype)
+    for n in range(L):
+        q_ = f"layers.{n}."
+        h = x if n == 0 else layer_norm(x, g(q_ + "attn_norm.weight"), zero, eps)
+        qkv = linear(h, g(q_ + "attn.Wqkv.weight"))
+        q = qkv[..., :H].reshape(B, S, nh, d).transpose(0, 2, 1, 3)
+        k = qkv[..., H:2 * H].reshape(B, S, nh, d).transpose(0, 2, 1, 3)
+        v = qkv[..., 2 * H:].reshape(B, S, nh, d).transpose(0, 2, 1, 3)
+        q, k = rope_apply(q, cos, sin), rope_apply(k, cos, sin)
+        probs = softmax_last((q @ k.transpose(0, 1, 3, 2)) / math.sqrt(d) + ext)
+        ctx = (probs @ v).transpose(0, 2, 1, 3).reshape(B, S, H)
+        x = x + linear(ctx, g(q_ + "attn.Wo.weight"))
+        h = layer_norm(x, g(q_ + "mlp_norm.weight"), zero, eps)
+        ug = linear(h, g(q_ + "mlp.Wi.weight"))
+        x = x + linear(gelu_erf(ug[..., :I]) * ug[..., I:], g(q_ + "mlp.Wo.weight"))
+    return layer_norm(x, g("final_norm.weight"), zero, eps)
+
+
+def random_modernbert_weights(cfg: dict, seed: int, std: float = 0.02, dtype=np.float32) -> dict:
+    """Random-init ModernBERT weights under the reference's ``model.`` keys
+    (modernbert.rs:16-27): N(0, std), LayerNorm weights 1 +- 0.1 noise."""
+    c = modernbert_config(cfg)
+    rng = np.random.default_rng(seed)
+    H, I = c["hidden_size"], c["intermediate_size"]
+    r = lambda *s: (rng.standard_normal(s, dtype=np.float32) * std).astype(dtype)
+    ln = lambda: (1.0 + 0.1 * rng.standard_normal(H, dtype=np.float32)).astype(dtype)
+    w = {"model.embeddings.tok_embeddings.weight": r(c["vocab_size"], H),
+         "model.embeddings.norm.weight": ln(), "model.final_norm.weight": ln()}
+    for n in range(c["num_hidden_layers"]):
+        q = f"model.layers.{n}."
+        if n > 0:
+            w[q + "attn_norm.weight"] = ln()
+        w[q + "attn.Wqkv.weight"] = r(3 * H, H)
+        w[q + "attn.Wo.weight"] = r(H, H)
+        w[q + "mlp_norm.weight"] = ln()
+        w[q + "mlp.Wi.weight"] = r(2 * I, H)
+        w[q + "mlp.Wo.weight"] = r(H, I)
+    return w

@@ -22,6 +22,9 @@ Fixtures (``.npz``, weights included so the GPU tests need nothing else):
   ``tests/fixtures/tiny_open_clip``), global-average and CLS pooling.
 * ``small_clip_text.npz``  OpenCLIP text tower W 64, 2 layers, context 24 (HF
   ``CLIPTextModelWithProjection``, float64), ragged EOT positions.
+* ``small_modernbert.npz``  ModernBERT (HF ``ModernBertModel``, every layer global) H 64,
+  3 layers, 4 heads, GeGLU 96, RoPE theta 160000, keys under ``model.``
+  (``crates/jammi-encoders/src/modernbert.rs``).
 * ``small_distilbert.npz``  DistilBERT (HF ``DistilBertModel``) H 64, 2 layers, 4 heads,
   FFN 256: the BERT weight recipe under DistilBERT names (``distilbert.`` prefix,
   ``transformer.layer.N.{attention.q_lin, ..., ffn.lin1, output_layer_norm}``) and no
@@ -325,6 +328,77 @@ def clip_text_fixture(name, cfg: ClipTextConfig, seed, lens, S):
     print("wrote", name, embed.shape)
 
 
+def hf_modernbert_hidden(w: dict, cfg: dict, ids, mask) -> np.ndarray:
+    """HF ``ModernBertModel`` in float64 with every layer global (the reference
+    applies one global RoPE to all layers, modernbert.rs:64-71) and the
+    reference's RoPE table (theta in float64, cos / sin stored as float32,
+    modernbert.rs:106-131); transformers computes that table in float32 and
+    takes RoPE and the softmax in float32, so those three steps are replaced by
+    float64 ones here."""
+    from transformers import ModernBertConfig, ModernBertModel
+    import transformers.models.modernbert.modeling_modernbert as mm
+    from oracle.bert import modernbert_rope_tables
+    L = cfg["num_hidden_layers"]
+    d = cfg["hidden_size"] // cfg["num_attention_heads"]
+    hcfg = ModernBertConfig(vocab_size=cfg["vocab_size"], hidden_size=cfg["hidden_size"],
+                            intermediate_size=cfg["intermediate_size"], num_hidden_layers=L,
+                            num_attention_heads=cfg["num_attention_heads"], hidden_activation="gelu",
+                            max_position_embeddings=cfg["max_position_embeddings"],
+                            norm_eps=cfg.get("layer_norm_eps", 1e-5), norm_bias=False,
+                            attention_bias=False, mlp_bias=False, pad_token_id=0,
+                            global_rope_theta=cfg["global_rope_theta"])
+    hcfg.layer_types = ["full_attention"] * L  # set after validation of the RoPE parameters
+    hcfg._attn_implementation = "eager"
+    model = ModernBertModel(hcfg).eval().to(torch.float64)
+    sd = {k[len("model."):]: torch.from_numpy(np.asarray(v, dtype=np.float64)) for k, v in w.items()}
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not missing and not unexpected, (missing, unexpected)
+    cos_h, sin_h = modernbert_rope_tables(d, cfg["max_position_embeddings"], cfg["global_rope_theta"])
+
+    def rotary_f64(self, x, position_ids, layer_type=None):
+        pos = position_ids[0].numpy()
+        c = np.concatenate([cos_h, cos_h], -1)[pos].astype(np.float64)
+        s_ = np.concatenate([sin_h, sin_h], -1)[pos].astype(np.float64)
+        return torch.from_numpy(c)[None], torch.from_numpy(s_)[None]
+
+    def rope_f64(q, k, cos, sin, unsqueeze_dim=1):
+        cos, sin = cos.unsqueeze(unsqueeze_dim), sin.unsqueeze(unsqueeze_dim)
+        return q * cos + mm.rotate_half(q) * sin, k * cos + mm.rotate_half(k) * sin
+
+    def attention_f64(module, query, key, value, attention_mask, scaling, dropout=0.0, **kw):
+        a = torch.matmul(query, key.transpose(2, 3)) * scaling
+        if attention_mask is not None:
+            a = a + attention_mask
+        a = torch.softmax(a, dim=-1)
+        return torch.matmul(a, value).transpose(1, 2).contiguous(), a
+
+    stock = (mm.ModernBertRotaryEmbedding.forward, mm.apply_rotary_pos_emb, mm.eager_attention_forward)
+    mm.ModernBertRotaryEmbedding.forward = rotary_f64
+    mm.apply_rotary_pos_emb, mm.eager_attention_forward = rope_f64, attention_f64
+    try:
+        with torch.no_grad():
+            out = model(input_ids=torch.from_numpy(ids.astype(np.int64)),
+                        attention_mask=torch.from_numpy(mask.astype(np.int64))).last_hidden_state
+    finally:
+        mm.ModernBertRotaryEmbedding.forward, mm.apply_rotary_pos_emb, mm.eager_attention_forward = stock
+    return (out * torch.from_numpy(mask.astype(np.float64))[:, :, None]).numpy()
+
+
+def modernbert_fixture(name, cfg: dict, seed, lens, S):
+    from oracle.bert import random_modernbert_weights, random_token_batch
+    w = random_modernbert_weights(cfg, seed, std=0.1)
+    ids, mask = random_token_batch(len(lens), S, lens, seed + 1, id_lo=1,
+                                   id_hi=cfg["vocab_size"] - 1, cls_id=1, sep_id=2)
+    hidden = hf_modernbert_hidden(w, cfg, ids, mask)
+    pooled = torch_pool_all(torch.from_numpy(hidden), torch.from_numpy(mask.astype(np.int64)))
+    arrs = {"w::" + k: v for k, v in w.items()}
+    arrs.update({"ids": ids, "mask": mask, "hidden": hidden,
+                 "config_json": np.frombuffer(json.dumps(cfg).encode(), dtype=np.uint8)})
+    arrs.update({"pooled_" + k: v.numpy() for k, v in pooled.items()})
+    np.savez_compressed(os.path.join(HERE, name), **arrs)
+    print("wrote", name, hidden.shape)
+
+
 def reference_fixture():
     st = os.path.join(REF_TINY_BERT, "model.safetensors")
     if not os.path.exists(st):
@@ -368,6 +442,10 @@ def main():
     ct = ClipTextConfig(width=64, layers=2, heads=4, context_length=24, vocab_size=300,
                         embed_dim=32)
     clip_text_fixture("small_clip_text.npz", ct, seed=505, lens=[24, 7, 2, 15, 24, 11], S=24)
+    mb = {"model_type": "modernbert", "hidden_size": 64, "num_hidden_layers": 3,
+          "num_attention_heads": 4, "intermediate_size": 96, "vocab_size": 300,
+          "max_position_embeddings": 80, "layer_norm_eps": 1e-5, "global_rope_theta": 160000.0}
+    modernbert_fixture("small_modernbert.npz", mb, seed=808, lens=[70, 33, 1, 0, 64, 9], S=70)
     reference_fixture()
 
 

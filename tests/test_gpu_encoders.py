@@ -478,3 +478,57 @@ def test_clip_text_errors():
         model.encode(bad)
     with pytest.raises(JbError):  # text towers carry no projection head or LoRA sites here
         model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)
+
+
+# ── ModernBERT (row (f): sibling encoders) ────────────────────────────────────
+
+@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+def test_modernbert_golden(fmt):
+    """ModernBert (modernbert.rs): RoPE on Q/K, GeGLU, bias-free pre-norm layers,
+    against HF ModernBertModel, all poolings and the hidden states."""
+    from jammi_b200 import Bert
+    from jammi_b200._lib import TEXT_MODERNBERT
+    w, g = load_golden("small_modernbert.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = Bert.from_weights(w, cfg, device=0, fmt=fmt)
+    assert model.info.variant == TEXT_MODERNBERT
+    lens = g["mask"].sum(1)
+    for pname in ("mean", "cls", "max", "weighted_mean"):
+        out = model.encode(g["ids"], lens, pooling=pname)
+        rows = lens > 0 if pname == "cls" else None
+        assert_close_rows(out, g["pooled_" + pname], fmt, rows)
+    assert np.all(model.encode(g["ids"], lens)[lens == 0] == 0)
+    h = model.forward_hidden(g["ids"], g["mask"]).cpu().numpy()
+    valid = g["mask"].astype(bool)
+    bar = 1e-4 if fmt == "f32" else 6e-2  # hidden states of magnitude ~1-4
+    assert np.abs(h[valid] - g["hidden"][valid]).max() <= bar
+    assert np.all(h[~valid] == 0)
+
+
+def test_modernbert_base_bf16_config():
+    """ModernBERT-base dimensions (H 768, 22 layers, 12 heads, GeGLU 1152,
+    vocab 50368), bf16, ragged rows, against the oracle."""
+    cfg = {"model_type": "modernbert", "hidden_size": 768, "num_hidden_layers": 22,
+           "num_attention_heads": 12, "intermediate_size": 1152, "vocab_size": 50368,
+           "max_position_embeddings": 8192, "global_rope_theta": 160000.0}
+    w = ob.random_modernbert_weights(cfg, seed=811)
+    rng = np.random.default_rng(812)
+    lens = rng.integers(1, 201, size=10)
+    lens[0] = 200
+    ids, mask = ob.random_token_batch(10, 200, lens, seed=813, id_lo=1, id_hi=50367, cls_id=1, sep_id=2)
+    ref = ob.pool_and_normalize(ob.modernbert_forward_hidden(w, cfg, ids, mask), mask)
+    from jammi_b200 import Bert
+    model = Bert.from_weights(w, cfg, device=0, fmt="bf16")
+    assert_close_rows(model.encode(ids, lens), ref, "bf16")
+
+
+def test_modernbert_refusals():
+    from jammi_b200 import Bert
+    from jammi_b200._lib import JbError
+    w, g = load_golden("small_modernbert.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    with pytest.raises(JbError):  # no int8 ModernBERT weights
+        Bert.from_weights(w, cfg, device=0, fmt="int8")
+    model = Bert.from_weights(w, cfg, device=0, fmt="bf16")
+    with pytest.raises(JbError):
+        model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)

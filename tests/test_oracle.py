@@ -109,6 +109,31 @@ def test_distilbert_oracle_matches_golden():
         np.testing.assert_allclose(out[rows], g["pooled_" + pname][rows], atol=1e-9, rtol=0)
 
 
+def test_modernbert_oracle_matches_golden():
+    """ModernBert::forward_hidden restated against HF ModernBertModel (f64,
+    every layer global, the reference's RoPE table)."""
+    w, g = load_golden("small_modernbert.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    valid = g["mask"].astype(bool)
+    h64 = ob.modernbert_forward_hidden(w, cfg, g["ids"], g["mask"])
+    np.testing.assert_allclose(h64[valid], g["hidden"][valid], atol=1e-9, rtol=0)
+    nonempty = g["mask"].sum(1) > 0
+    for pname, pid in ob.POOLING_NAMES.items():
+        out = ob.pool_and_normalize(h64, g["mask"], pid)
+        rows = nonempty if pid == ob.POOL_CLS else slice(None)
+        np.testing.assert_allclose(out[rows], g["pooled_" + pname][rows], atol=1e-9, rtol=0)
+
+
+def test_modernbert_rope_table():
+    """RotaryEmbedding::new (modernbert.rs:106-131): position 0 is the
+    identity rotation; theta_i = pos * base^(-2i/d)."""
+    c, s = ob.modernbert_rope_tables(8, 4, 10000.0)
+    assert np.all(c[0] == 1) and np.all(s[0] == 0)
+    assert abs(float(c[3, 1]) - math.cos(3 * 10000.0 ** (-2 / 8))) < 1e-7
+    x = np.arange(8, dtype=np.float64)[None, None, None, :]
+    np.testing.assert_array_equal(ob.rope_apply(x, c[:1], s[:1]), x)
+
+
 def test_bert_oracle_on_reference_fixture():
     z = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert.npz"))
     st = os.path.join(REF_FIXTURE, "model.safetensors")
