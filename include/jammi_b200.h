@@ -82,6 +82,8 @@ typedef struct {
   int64_t weight_bytes;    /* device bytes held by the weights */
   int32_t projection_rank; /* rank of the installed projection head, 0 if none */
   int32_t variant;         /* text family: jb_text_variant */
+  float preprocess_mean[3]; /* vision: preprocess_cfg.mean (OpenAI CLIP defaults) */
+  float preprocess_std[3];  /* vision: preprocess_cfg.std */
 } jb_model_info;
 
 /* ── lifecycle ─────────────────────────────────────────────────────────── */
@@ -168,6 +170,23 @@ jb_status jb_forward_hidden_device(jb_model* model, const uint32_t* d_ids, const
  * plus l2_normalize (open_clip_vit.rs:309-353; candle.rs:425-438, 911). */
 jb_status jb_encode_image(jb_model* model, const float* pixels, int batch,
                           float* out, void* stream);
+/* Decoded RGB8 images (HWC bytes, image b at bytes + offsets[b], widths[b] x
+ * heights[b], all inside n_bytes) -> host f32 [batch, embed_dim]: the whole of
+ * CandleModel::forward_image_embedding (candle.rs:858-925) after decoding.
+ * preprocess_image_batch (image_preprocess.rs:15-75: pad to a white square,
+ * Catmull-Rom resize to image_size, (x / 255 - mean) / std with the model's
+ * preprocess_cfg) runs on the device, on raw bytes copied once.  A side above
+ * about 19,000 pixels answers JB_ERR_INVALID. */
+jb_status jb_encode_image_rgb8(jb_model* model, const uint8_t* bytes, size_t n_bytes,
+                               const int64_t* offsets, const int32_t* widths,
+                               const int32_t* heights, int batch, float* out, void* stream);
+/* The preprocessing alone on device buffers: -> f32 [batch, 3, target, target].
+ * max_side = the largest max(width, height) of the batch; mean / std_ are host
+ * float[3]. */
+jb_status jb_op_preprocess_rgb8(const uint8_t* d_bytes, const int64_t* d_offsets,
+                                const int32_t* d_widths, const int32_t* d_heights, int batch,
+                                int max_side, int target, const float* mean, const float* std_,
+                                float* d_out, void* stream);
 jb_status jb_encode_image_device(jb_model* model, const float* d_pixels, int batch,
                                  float* d_out, void* stream);
 

@@ -118,6 +118,10 @@ jb_status jb_model_get_info(const jb_model* m, jb_model_info* out) {
     out->weight_bytes = m->weight_bytes;
     out->projection_rank = m->head_rank;
     out->variant = m->variant;
+    for (int i = 0; i < 3; ++i) {
+      out->preprocess_mean[i] = m->img_mean[i];
+      out->preprocess_std[i] = m->img_std[i];
+    }
   });
 }
 
@@ -289,6 +293,91 @@ jb_status jb_encode_image(jb_model* m, const float* pixels, int batch, float* ou
     });
     jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->embed_dim * 4, cudaMemcpyDeviceToHost, s), "D2H");
     jb::check_device_flag(m, s);
+  });
+}
+
+namespace {
+// Checks one packed RGB8 batch (offsets / sizes inside n_bytes) and returns
+// the largest image side.
+int check_rgb8_batch(const uint8_t* bytes, size_t n_bytes, const int64_t* offsets,
+                     const int32_t* widths, const int32_t* heights, int batch) {
+  if (!bytes || !offsets || !widths || !heights) jb::fail(JB_ERR_INVALID, "null image buffer");
+  int max_side = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int64_t w = widths[b], h = heights[b], off = offsets[b];
+    if (w <= 0 || h <= 0) jb::fail(JB_ERR_INVALID, "image " + std::to_string(b) + " is empty");
+    if (off < 0 || static_cast<uint64_t>(off) + static_cast<uint64_t>(w * h * 3) > n_bytes)
+      jb::fail(JB_ERR_INVALID, "image " + std::to_string(b) + " lies outside the byte buffer");
+    max_side = std::max<int>(max_side, static_cast<int>(std::max(w, h)));
+  }
+  return max_side;
+}
+}  // namespace
+
+jb_status jb_encode_image_rgb8(jb_model* m, const uint8_t* bytes, size_t n_bytes,
+                               const int64_t* offsets, const int32_t* widths,
+                               const int32_t* heights, int batch, float* out, void* stream) {
+  return guarded([&] {
+    if (!m || m->family != JB_FAMILY_CLIP_VISION) jb::fail(JB_ERR_INVALID, "model is not a vision encoder");
+    if (batch < 0) jb::fail(JB_ERR_INVALID, "batch must be >= 0");
+    if (batch == 0) return;
+    if (!out) jb::fail(JB_ERR_INVALID, "null buffer");
+    const int max_side = check_rgb8_batch(bytes, n_bytes, offsets, widths, heights, batch);
+    if (jb::preprocess_smem_bytes(max_side, m->image_size) > jb::kImgMaxSmem)
+      jb::fail(JB_ERR_INVALID, "an image side of " + std::to_string(max_side) + " pixels is too large");
+    std::lock_guard<std::mutex> lk(m->mu);
+    jb::DeviceGuard g(m->device);
+    cudaStream_t s = as_stream(stream);
+    jb::ensure_workspace(m, batch, m->tokens);
+    jb::Workspace& ws = m->ws;
+    // raw bytes, then offsets (8-byte aligned), widths, heights
+    const size_t meta_at = (n_bytes + 15) & ~size_t(15);
+    const size_t need = meta_at + size_t(batch) * 16;
+    if (need > m->img_cap) {
+      jb::check_cuda(cudaStreamSynchronize(s), "image buffer");
+      if (m->img_buf) cudaFree(m->img_buf);
+      m->img_buf = nullptr;
+      m->img_cap = 0;
+      jb::check_cuda(cudaMalloc(&m->img_buf, need), "image buffer");
+      m->img_cap = need;
+    }
+    uint8_t* d_bytes = static_cast<uint8_t*>(m->img_buf);
+    int64_t* d_off = reinterpret_cast<int64_t*>(d_bytes + meta_at);
+    int32_t* d_w = reinterpret_cast<int32_t*>(d_off + batch);
+    int32_t* d_h = d_w + batch;
+    jb::check_cuda(cudaMemcpyAsync(d_bytes, bytes, n_bytes, cudaMemcpyHostToDevice, s), "H2D images");
+    jb::check_cuda(cudaMemcpyAsync(d_off, offsets, size_t(batch) * 8, cudaMemcpyHostToDevice, s), "H2D offsets");
+    jb::check_cuda(cudaMemcpyAsync(d_w, widths, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D widths");
+    jb::check_cuda(cudaMemcpyAsync(d_h, heights, size_t(batch) * 4, cudaMemcpyHostToDevice, s), "H2D heights");
+    std::string why;
+    cudaError_t e = jb::launch_preprocess_rgb8(d_bytes, d_off, d_w, d_h, batch, max_side, m->image_size,
+                                               m->img_mean, m->img_std, ws.pixels, s, &why);
+    if (e != cudaSuccess) {
+      if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
+      jb::check_cuda(e, "image preprocessing");
+    }
+    jb::run_graphed(m, 1, batch, m->tokens, 0, s, [&](cudaStream_t gs) {
+      jb::clip_forward_device(m, ws.pixels, batch, ws.out, gs);
+    });
+    jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->embed_dim * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    jb::check_device_flag(m, s);
+  });
+}
+
+jb_status jb_op_preprocess_rgb8(const uint8_t* d_bytes, const int64_t* d_offsets,
+                                const int32_t* d_widths, const int32_t* d_heights, int batch,
+                                int max_side, int target, const float* mean, const float* stdv,
+                                float* d_out, void* stream) {
+  return guarded([&] {
+    if (!d_bytes || !d_offsets || !d_widths || !d_heights || !mean || !stdv || !d_out || batch < 0)
+      jb::fail(JB_ERR_INVALID, "jb_op_preprocess_rgb8: bad argument");
+    std::string why;
+    cudaError_t e = jb::launch_preprocess_rgb8(d_bytes, d_offsets, d_widths, d_heights, batch, max_side,
+                                               target, mean, stdv, d_out, as_stream(stream), &why);
+    if (e != cudaSuccess) {
+      if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
+      jb::check_cuda(e, "jb_op_preprocess_rgb8");
+    }
   });
 }
 

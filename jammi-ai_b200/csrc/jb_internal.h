@@ -121,6 +121,16 @@ cudaError_t launch_eot_lens(const uint32_t* ids, int batch, int S, uint32_t* len
 cudaError_t launch_fill_cu_uniform(int* cu, int batch, int tokens, cudaStream_t s);
 // Row-wise x / clamp(||x||, 1e-12) over f32 [rows, cols], in place.
 cudaError_t launch_l2_rows(float* x, int rows, int cols, cudaStream_t s);
+// Image preprocessing (image_preprocess.rs:15-75): RGB8 images packed at
+// d_offsets (HWC bytes, widths x heights) -> pad to a white square, Catmull-Rom
+// resize to target x target, (x / 255 - mean) / std -> f32 [batch, 3, target, target].
+// max_side = the largest max(w, h) of the batch (sizes the on-chip row buffer).
+constexpr size_t kImgMaxSmem = 232448;
+size_t preprocess_smem_bytes(int max_side, int target);
+cudaError_t launch_preprocess_rgb8(const uint8_t* d_bytes, const int64_t* d_offsets,
+                                   const int* d_widths, const int* d_heights, int batch,
+                                   int max_side, int target, const float* mean, const float* stdv,
+                                   float* d_out, cudaStream_t s, std::string* why);
 // ModernBERT: RoPE on the Q and K column blocks of packed qkv [T, 3 * heads * d]
 // in place; cos_t / sin_t f32 [max_pos, d/2], position = index within the row.
 cudaError_t launch_rope_qk(void* qkv, int dtype, const int* cu, int batch, int max_seq, int heads,

@@ -427,6 +427,19 @@ void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
   m->embed_dim = static_cast<int>(mc->num_or("embed_dim", 0));
   m->gap = vc->bool_or("global_average_pool", false);
   m->eps = 1e-5f;
+  // preprocess_cfg.mean / .std, three numbers each, else the OpenAI CLIP
+  // defaults (open_clip_vit.rs:98-99, parse_f32_array :105-120)
+  if (const Json* pc = cfg.get("preprocess_cfg")) {
+    for (const char* key : {"mean", "std"}) {
+      const Json* a = pc->get(key);
+      if (!a || a->kind != Json::Arr || a->arr.size() < 3) continue;
+      bool nums = true;
+      for (int i = 0; i < 3; ++i) nums = nums && a->arr[i].kind == Json::Num;
+      if (!nums) continue;
+      float* dst = key[0] == 'm' ? m->img_mean : m->img_std;
+      for (int i = 0; i < 3; ++i) dst[i] = static_cast<float>(a->arr[i].num);
+    }
+  }
   const int W = m->hidden, P = m->patch, g = m->image_size / m->patch;
   m->tokens = g * g + 1;
   m->max_pos = m->tokens;
@@ -713,6 +726,7 @@ void model_free(jb_model* m) {
     if (m->graph_in) cudaEventDestroy(m->graph_in);
     if (m->graph_out) cudaEventDestroy(m->graph_out);
     free_workspace(m->ws);
+    if (m->img_buf) cudaFree(m->img_buf);
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);
     profile_enable(m, false);

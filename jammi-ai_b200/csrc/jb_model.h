@@ -130,6 +130,13 @@ struct jb_model {
   void *cls = nullptr, *vpos = nullptr;
   float *ln_pre_g = nullptr, *ln_pre_b = nullptr, *ln_post_g = nullptr, *ln_post_b = nullptr;
   std::vector<jb::ClipBlockW> clip_blocks;
+  // preprocess_cfg mean / std of the vision tower (open_clip_vit.rs:15-16, 98-99)
+  float img_mean[3] = {0.48145466f, 0.4578275f, 0.40821073f};
+  float img_std[3] = {0.26862954f, 0.26130258f, 0.27577711f};
+  // device copy of the raw RGB8 images of the last jb_encode_image_rgb8 call
+  // (bytes, then offsets / widths / heights), grown on demand
+  void* img_buf = nullptr;
+  size_t img_cap = 0;
   // LoRA adapters (empty: none) and the widest padded rank of a fused site
   std::vector<jb::LoraLayerW> lora;
   int lora_width = 0;

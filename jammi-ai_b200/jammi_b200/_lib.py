@@ -43,7 +43,8 @@ class ModelInfo(ctypes.Structure):
                 ("hidden", ctypes.c_int32), ("output_dim", ctypes.c_int32), ("layers", ctypes.c_int32),
                 ("heads", ctypes.c_int32), ("ffn", ctypes.c_int32), ("max_seq", ctypes.c_int32),
                 ("image_size", ctypes.c_int32), ("weight_bytes", ctypes.c_int64),
-                ("projection_rank", ctypes.c_int32), ("variant", ctypes.c_int32)]
+                ("projection_rank", ctypes.c_int32), ("variant", ctypes.c_int32),
+                ("preprocess_mean", ctypes.c_float * 3), ("preprocess_std", ctypes.c_float * 3)]
 
 
 _lib = None
@@ -70,6 +71,8 @@ _SIGS = [
     ("jb_encode_text_device_noalloc", _I, [_P, _P, _P, _I, _I, _I, _P, _P]),
     ("jb_forward_hidden_device", _I, [_P, _P, _P, _I, _I, _P, _P]),
     ("jb_encode_image", _I, [_P, _P, _I, _P, _P]),
+    ("jb_encode_image_rgb8", _I, [_P, _P, ctypes.c_size_t, _P, _P, _P, _I, _P, _P]),
+    ("jb_op_preprocess_rgb8", _I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     ("jb_encode_image_device", _I, [_P, _P, _I, _P, _P]),
     ("jb_op_sync", _I, [_P]),
     ("jb_op_linear", _I, [_P, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),

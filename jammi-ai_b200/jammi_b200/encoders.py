@@ -263,6 +263,17 @@ class OpenClipVisionTransformer(Model):
         check(lib().jb_encode_image(self._h, _ptr(px), B, _ptr(out), _stream_ptr(stream)))
         return out
 
+    def encode_rgb8(self, images, stream=None) -> np.ndarray:
+        """Decoded RGB8 images (``[h, w, 3]`` uint8 arrays of any sizes) ->
+        host f32 [B, embed_dim]; padding, Catmull-Rom resize and normalisation
+        run on the device (``jb_encode_image_rgb8``)."""
+        buf, offs, ws, hs = pack_rgb8(images)
+        out = np.zeros((len(images), self.info.output_dim), dtype=np.float32)
+        check(lib().jb_encode_image_rgb8(self._h, buf.ctypes.data, buf.nbytes, offs.ctypes.data,
+                                         ws.ctypes.data, hs.ctypes.data, len(images), _ptr(out),
+                                         _stream_ptr(stream)))
+        return out
+
     def forward_image_device(self, pixels, out, stream=None):
         check(lib().jb_encode_image_device(self._h, _ptr(pixels), pixels.shape[0], _ptr(out),
                                            _stream_ptr(stream)))
@@ -316,6 +327,20 @@ class OpenClipText(Model):
         except JbError as e:
             _raise_seq(e)
         return out
+
+
+def pack_rgb8(images):
+    """RGB8 ``[h, w, 3]`` arrays -> (bytes, int64 offsets, int32 widths, int32 heights)."""
+    imgs = [np.ascontiguousarray(im, dtype=np.uint8) for im in images]
+    for im in imgs:
+        if im.ndim != 3 or im.shape[2] != 3:
+            raise ValueError("images must be [h, w, 3] uint8 (RGB8)")
+    sizes = [im.nbytes for im in imgs]
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64) if imgs else np.zeros(0, np.int64)
+    buf = np.concatenate([im.reshape(-1) for im in imgs]) if imgs else np.zeros(1, np.uint8)
+    ws = np.array([im.shape[1] for im in imgs], dtype=np.int32)
+    hs = np.array([im.shape[0] for im in imgs], dtype=np.int32)
+    return buf, offs, ws, hs
 
 
 def load_model(weights_path: str, config_path_or_dict, device: int = 0, fmt: str = "bf16",

@@ -105,3 +105,22 @@ def pool_normalize(hidden: torch.Tensor, cu_seqlens: torch.Tensor, pooling: int 
     check(lib().jb_op_pool_normalize(_p(hidden), _DT[hidden.dtype], _p(cu_seqlens), _p(out), B, H,
                                      pooling, _s(hidden)))
     return out
+
+
+def preprocess_rgb8(images, target: int, mean, std, device="cuda") -> torch.Tensor:
+    """RGB8 ``[h, w, 3]`` arrays -> f32 [B, 3, target, target] on the device
+    (``jb_op_preprocess_rgb8``: white square pad, Catmull-Rom resize, normalise)."""
+    from .encoders import pack_rgb8
+    buf, offs, ws, hs = pack_rgb8(images)
+    dev = torch.device(device)
+    d_buf = torch.from_numpy(buf).to(dev)
+    d_off = torch.from_numpy(offs).to(dev)
+    d_w = torch.from_numpy(ws).to(dev)
+    d_h = torch.from_numpy(hs).to(dev)
+    m = torch.tensor(list(mean), dtype=torch.float32)
+    s = torch.tensor(list(std), dtype=torch.float32)
+    out = torch.empty((len(images), 3, target, target), dtype=torch.float32, device=dev)
+    max_side = int(max(max(int(a), int(b)) for a, b in zip(ws, hs))) if len(images) else 1
+    check(lib().jb_op_preprocess_rgb8(_p(d_buf), _p(d_off), _p(d_w), _p(d_h), len(images), max_side,
+                                      target, m.data_ptr(), s.data_ptr(), _p(out), _s(out)))
+    return out

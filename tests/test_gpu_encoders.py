@@ -532,3 +532,23 @@ def test_modernbert_refusals():
     model = Bert.from_weights(w, cfg, device=0, fmt="bf16")
     with pytest.raises(JbError):
         model.set_lora(0, "query", np.zeros((4, 64), np.float32), np.zeros((64, 4), np.float32), 1.0)
+
+
+# ── device image preprocessing in the image entry point (row (f): host preprocessing) ──
+
+def test_encode_rgb8_matches_preprocessed_pixels():
+    """jb_encode_image_rgb8 (raw RGB8 bytes in, preprocessing on the device)
+    equals jb_encode_image on the oracle's preprocessed pixels, bit for bit."""
+    from oracle import image as oimg
+    from jammi_b200 import OpenClipVisionTransformer
+    w, g = load_golden("tiny_clip_cls.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    cfg["preprocess_cfg"] = {"mean": [0.5, 0.4, 0.3], "std": [0.2, 0.25, 0.3]}
+    model = OpenClipVisionTransformer.from_weights(w, cfg, device=0, fmt="f32")
+    assert np.allclose(list(model.info.preprocess_mean), [0.5, 0.4, 0.3])
+    imgs = oimg.random_images(21, [(40, 20), (8, 8), (3, 11), (100, 100), (9, 64)])
+    px = oimg.preprocess_image_batch(imgs, model.image_size(), (0.5, 0.4, 0.3), (0.2, 0.25, 0.3))
+    for _ in range(3):  # direct, capture, replay
+        assert np.array_equal(model.encode_rgb8(imgs), model.forward_image(px))
+    with pytest.raises(Exception):
+        model.encode_rgb8([np.zeros((0, 4, 3), np.uint8)])

@@ -348,3 +348,22 @@ def test_pool_normalize(dev, pooling, dtype):
     assert np.abs(got - ref).max() < 1e-5
     if pooling in ("mean", "weighted_mean"):
         assert np.all(got[2] == 0)
+
+
+# ── image preprocessing (image_preprocess.rs:15-75) ──────────────────────────
+
+def test_preprocess_rgb8_bit_exact(dev):
+    """White square pad, Catmull-Rom resize and normalisation on the device:
+    bit-equal to the f32 restatement for downscales, upscales, the identity
+    size, extreme aspect ratios and a 1x1 image."""
+    from oracle import image as oimg
+    ops = _ops()
+    sizes = [(100, 200), (300, 150), (224, 224), (50, 30), (640, 480), (1, 1), (3000, 17), (224, 223)]
+    imgs = oimg.random_images(11, sizes)
+    mean, std = oimg.OPENAI_CLIP_MEAN, oimg.OPENAI_CLIP_STD
+    got = ops.preprocess_rgb8(imgs, 224, mean, std, device=dev).cpu().numpy()
+    ref = oimg.preprocess_image_batch(imgs, 224, mean, std)
+    assert np.array_equal(got, ref), np.abs(got - ref).max()
+    # a small target (the tiny fixtures' 8 x 8) with a large downscale ratio
+    got8 = ops.preprocess_rgb8(imgs[:3], 8, (0.5, 0.5, 0.5), (0.25, 0.25, 0.25), device=dev).cpu().numpy()
+    assert np.array_equal(got8, oimg.preprocess_image_batch(imgs[:3], 8, (0.5,) * 3, (0.25,) * 3))

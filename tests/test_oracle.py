@@ -10,6 +10,7 @@ import pytest
 from conftest import load_golden
 from oracle import bert as ob
 from oracle import clip as oc
+from oracle import image as oimg
 from oracle import quant as oq
 
 REF_FIXTURE = "/root/reference/cookbook/fixtures/tiny_bert"
@@ -238,3 +239,45 @@ def test_projection_head_oracle():
     # x A^T = [[0.6, 0.8], [1, 0]]; (x A^T) B^T = [[0.8, 0.6, 0.7], [0, 1, 0.5]]
     assert np.allclose(y, [[0.6 + 1.6, 0.8 + 1.2, 1.4], [1.0, 2.0, 1.0]])
     assert np.array_equal(ob.projection_head(x, a, np.zeros_like(b), 8.0), x)
+
+
+# ── image preprocessing (image_preprocess.rs) ────────────────────────────────
+
+def test_pad_to_square_known_answers():
+    """image_preprocess.rs:95-119: landscape, portrait and square shapes."""
+    assert oimg.pad_to_square(np.zeros((100, 200, 3), np.uint8)).shape == (200, 200, 3)
+    assert oimg.pad_to_square(np.zeros((300, 100, 3), np.uint8)).shape == (300, 300, 3)
+    sq = np.zeros((150, 150, 3), np.uint8)
+    assert oimg.pad_to_square(sq) is sq
+    # centred on white: (size - w) / 2 columns of 255 on the left
+    p = oimg.pad_to_square(np.zeros((2, 5, 3), np.uint8))
+    assert np.all(p[0] == 255) and np.all(p[1:3] == 0) and np.all(p[3:] == 255)
+
+
+def test_preprocess_known_answers():
+    """image_preprocess.rs:121-146: batch shape, and a white image maps to
+    (1 - mean) / std in every pixel of channel 0."""
+    out = oimg.preprocess_image_batch([np.zeros((200, 100, 3), np.uint8),
+                                       np.zeros((150, 300, 3), np.uint8)], 224)
+    assert out.shape == (2, 3, 224, 224)
+    white = np.full((10, 10, 3), 255, np.uint8)
+    v = oimg.preprocess_image_batch([white], 4)
+    exp = (np.float32(1.0) - np.float32(oimg.OPENAI_CLIP_MEAN[0])) / np.float32(oimg.OPENAI_CLIP_STD[0])
+    assert np.all(v[0, 0] == exp)
+    with pytest.raises(ValueError):
+        oimg.preprocess_image_batch([], 224)
+
+
+def test_catmull_rom_resize_properties():
+    """Catmull-Rom interpolates (k(0) = 1, k(+-1) = k(+-2) = 0), so a same-size
+    resize is the identity; weights form a partition of unity; a constant
+    image stays constant."""
+    assert oimg.catmull_rom(0.0) == 1 and oimg.catmull_rom(1.0) == 0 and oimg.catmull_rom(-2.0) == 0
+    img = oimg.random_images(3, [(37, 37)])[0]
+    assert np.array_equal(oimg.resize_catmull_rom(img, 37), img)
+    for o in (0, 17, 223):
+        _, ws = oimg.taps(o, 1000, 224)
+        assert abs(float(sum(ws)) - 1.0) < 1e-5
+    flat = np.full((90, 90, 3), 77, np.uint8)
+    assert np.all(oimg.resize_catmull_rom(flat, 224) == 77)
+    assert np.all(oimg.resize_catmull_rom(flat, 20) == 77)
