@@ -519,14 +519,15 @@ jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamm
 
 namespace {
 jb_status op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype, int batch,
-                       int heads, int head_dim, int max_len, int causal, void* stream) {
+                       int heads, int head_dim, int max_len, int causal, void* stream,
+                       int rows = 0) {
   return guarded([&] {
     if (!qkv || !cu_seqlens || !ctx || batch < 0 || heads <= 0 || head_dim <= 0 || max_len < 0)
       jb::fail(JB_ERR_INVALID, "jb_op_attention: bad argument");
     if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
     std::string why;
     cudaError_t e = jb::launch_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len,
-                                         as_stream(stream), &why, 0, nullptr, causal);
+                                         as_stream(stream), &why, rows, op_flag(current_device()), causal);
     if (e != cudaSuccess) {
       if (!why.empty()) jb::fail(JB_ERR_INVALID, why);
       jb::check_cuda(e, "jb_op_attention");
@@ -543,6 +544,16 @@ jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int
 jb_status jb_op_attention_causal(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
                                  int batch, int heads, int head_dim, int max_len, void* stream) {
   return op_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len, 1, stream);
+}
+
+void jb_set_attention_tcgen05(int on) { jb::set_attention_tcgen05(on != 0); }
+
+jb_status jb_op_attention_rows(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
+                               int batch, int heads, int head_dim, int max_len, int rows,
+                               int causal, void* stream) {
+  if (rows < 0) return jb::record_error(JB_ERR_INVALID, "jb_op_attention_rows: rows must be >= 0");
+  return op_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len, causal ? 1 : 0,
+                      stream, rows);
 }
 
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens, float* out,

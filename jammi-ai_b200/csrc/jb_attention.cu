@@ -13,7 +13,9 @@
 //                        through cp.async into 128-byte-swizzled smem.
 //   attn_simt:           any head_dim in {8,16,32,64}, f32 or bf16 (the f32
 //                        compute precision and the tiny fixtures).
+#include <algorithm>
 #include <cmath>
+#include <atomic>
 #include <cstring>
 
 #include <cudaTypedefs.h>
@@ -89,11 +91,11 @@ template <bool TMA>
 __global__ void __launch_bounds__(kFaThreads, 4)
     flash_attn_bf16_d64(const bf16* __restrict__ qkv, const int* __restrict__ cu,
                         bf16* __restrict__ ctx, int heads, float scale_log2,
-                        const __grid_constant__ CUtensorMap tm, int* err, int causal) {
+                        const __grid_constant__ CUtensorMap tm, int* err, int causal, int skip_le) {
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = cu[b], n = cu[b + 1] - start;
   const int q0 = qb * kFaRows;
-  if (q0 >= n) return;
+  if (q0 >= n || n <= skip_le) return;  // rows of <= skip_le keys: the tcgen05 kernel
   const int H = heads * 64, ld = 3 * H;
   __shared__ __align__(1024) uint8_t sm[5 * kTileBytes];
   __shared__ __align__(8) uint64_t bars[2];
@@ -313,6 +315,324 @@ __global__ void __launch_bounds__(kFaThreads, 4)
   }
 }
 
+// ── tcgen05 attention for rows of at most 192 keys ──────────────────────────
+// A persistent, warp-specialised kernel: one CTA per SM walks the work items
+// (row, head, 128-query block) of rows with at most kTcMaxKeys keys, two
+// items in flight through two shared-memory stages and two 256-column TMEM
+// slots, so that the loads of one item, the MMAs of another and the softmax
+// of a third overlap.  A row's keys all fit one accumulator, so its softmax
+// is exact in one pass (no running rescale).
+//   warp 0  (TMA): Q and K onto one mbarrier, V onto a second, 64-row boxes.
+//   warp 1  (MMA): S = Q K^T, four kind::f16 MMAs (K = 16) into the slot's
+//           columns [0, n_pad), n_pad = the row length rounded up to 16; once
+//           the softmax has written P: O = P V, one MMA per 16-key chunk with
+//           A = P read from TMEM and B = V straight from its TMA tile
+//           (MN-major, 128-byte swizzle), into the slot's columns [192, 256).
+//   warps 2-9 (softmax): warp w reads TMEM lanes 32 (w % 4) .. + 31 (queries
+//           q0 + 32 (w % 4) + lane) and the 16-key chunks j with
+//           j % 2 == (w - 2) / 4: two threads per query row, which exchange
+//           the row max and sum through shared memory.  They zero the V rows
+//           past the row's end (other rows' values: 0 * V must stay 0), load
+//           all their chunks of S at once into registers (max; then
+//           2^(s log2(e) / 8 - m) and the partial sums), write each chunk's
+//           P as bf16 pairs into the
+//           chunk's own first 8 columns, and after O = P V scale their 32
+//           columns of the O row by 1 / sum and store them (64 B).
+// causal != 0 masks keys after the query.  Longer rows are left to the
+// mma.sync kernel; the choice is per row, so a row's result does not depend
+// on its batch.  Every wait is bounded; on a timeout each role stops, the
+// TMA and MMA threads wait (bounded) for their copies and MMAs in flight,
+// the error flag is set and TMEM is freed.
+constexpr int kTcQ = 128;        // queries per item
+constexpr int kTcMaxKeys = 192;  // keys per row this kernel takes
+constexpr int kTcSlotCols = 256; // TMEM columns per slot; two slots
+constexpr int kTcOCol = 192;     // O's first column inside a slot
+constexpr int kTcSoftWarps = 8;
+constexpr int kTcThreads = 64 + 32 * kTcSoftWarps;
+constexpr int kTcSoftBarrier = 1;  // named barrier of the softmax warps
+constexpr int kTcStageBytes = (kTcQ + 2 * kTcMaxKeys) * 128;
+constexpr int kTcSmem = 2 * kTcStageBytes + 1024 + 256 + 2 * 2 * kTcQ * 4;
+
+__device__ __forceinline__ bool soft_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kTcSoftBarrier), "n"(32 * kTcSoftWarps)
+      : "memory");
+  return r != 0;
+}
+
+// Work item idx -> (row, head, query block); false for items with no work here.
+__device__ __forceinline__ bool tc_item(const int* cu, int heads, int idx, int& b, int& h, int& q0,
+                                        int& start, int& n) {
+  const int bh = idx >> 1;
+  b = bh / heads;
+  h = bh - b * heads;
+  q0 = (idx & 1) * kTcQ;
+  start = cu[b];
+  n = cu[b + 1] - start;
+  return q0 < n && n <= kTcMaxKeys;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const int* __restrict__ cu, bf16* __restrict__ ctx, int batch, int heads,
+                   float scale_log2, const __grid_constant__ CUtensorMap tm, int* err, int causal) {
+  const int H = heads * 64;
+  const int items = batch * heads * 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t stage0 = (raw + 1023u) & ~1023u;
+  uint8_t* meta = smem_raw + (stage0 + 2 * kTcStageBytes - raw);
+  const uint32_t bars = smem_u32(meta);
+  // per stage / slot s: ld_qk, ld_v, s_full, p_full, o_full, tmem_free, smem_empty, spare
+  auto bar = [&](int kind, int s) { return bars + 8u * (kind * 2 + s); };
+  enum { kLdQK = 0, kLdV, kSFull, kPFull, kOFull, kTFree, kSEmpty, kSpare };
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(meta + 8 * 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 16 + 4);
+  float* xmax = reinterpret_cast<float*>(meta + 256);  // [2 halves][128 rows]
+  float* xsum = xmax + 2 * kTcQ;
+
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(kLdQK, s), 1);
+      mbar_init(bar(kLdV, s), 1);
+      mbar_init(bar(kSFull, s), 1);
+      mbar_init(bar(kPFull, s), kTcSoftWarps);
+      mbar_init(bar(kOFull, s), 1);
+      mbar_init(bar(kTFree, s), kTcSoftWarps);
+      mbar_init(bar(kSEmpty, s), 1);
+      mbar_init(bar(kSpare, s), 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tslot), 2 * kTcSlotCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ── TMA producer
+      int k = 0;
+      for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
+        int b, h, q0, start, n;
+        if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
+        const int s = k & 1;
+        const uint32_t ph = (k >> 1) & 1;
+        if (!mbar_wait(bar(kSEmpty, s), ph ^ 1u, abort_flag)) break;
+        const uint32_t sQ = stage0 + s * kTcStageBytes, sK = sQ + kTcQ * 128, sV = sK + kTcMaxKeys * 128;
+        const int n_pad = (n + 15) & ~15;
+        const int kboxes = (n_pad + 63) >> 6;
+        const int qboxes = min(2, (n - q0 + 63) >> 6);
+        mbar_arrive_expect_tx(bar(kLdQK, s), static_cast<uint32_t>(qboxes + kboxes) * kTileBytes);
+        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, h * 64, start + q0 + 64 * i, bar(kLdQK, s));
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + h * 64, start + 64 * i, bar(kLdQK, s));
+        mbar_arrive_expect_tx(bar(kLdV, s), static_cast<uint32_t>(kboxes) * kTileBytes);
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + h * 64, start + 64 * i, bar(kLdV, s));
+        ++k;
+      }
+      if (*abort_flag) {
+        // copies in flight land before the CTA leaves (bounded)
+        volatile int no_abort = 0;
+        for (int j = max(0, k - 2); j < k; ++j) {
+          mbar_wait(bar(kLdQK, j & 1), (j >> 1) & 1, &no_abort);
+          mbar_wait(bar(kLdV, j & 1), (j >> 1) & 1, &no_abort);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ── MMA issuer
+      int k = 0;
+      int prev_s = -1, prev_n = 0;  // the item whose O = P V is pending
+      uint32_t prev_ph = 0;
+      bool ok = true;
+      auto issue_s = [&](int s, int n) {
+        tc_fence_after();
+        const uint32_t sQ = stage0 + s * kTcStageBytes, sK = sQ + kTcQ * 128;
+        const uint32_t idesc = idesc_bf16_f32(kTcQ, (n + 15) & ~15);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16(tbase + static_cast<uint32_t>(s * kTcSlotCols), umma_desc_sw128(sQ + 32u * kk),
+                   umma_desc_sw128(sK + 32u * kk), idesc, kk != 0);
+        mma_commit(bar(kSFull, s));
+      };
+      auto issue_pv = [&](int s, int n) {
+        tc_fence_after();
+        const uint32_t sV = stage0 + s * kTcStageBytes + kTcQ * 128 + kTcMaxKeys * 128;
+        const uint32_t slot = tbase + static_cast<uint32_t>(s * kTcSlotCols);
+        const uint32_t idesc = idesc_bf16_f32(kTcQ, 64) | (1u << 16);  // B (V) MN-major
+        const int chunks = ((n + 15) & ~15) >> 4;
+#pragma unroll 1
+        for (int c = 0; c < chunks; ++c)
+          mma_bf16_ta(slot + kTcOCol, slot + 16u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
+        mma_commit(bar(kOFull, s));
+        mma_commit(bar(kSEmpty, s));
+      };
+      for (int idx = blockIdx.x; idx < items && ok; idx += gridDim.x) {
+        int b, h, q0, start, n;
+        if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
+        const int s = k & 1;
+        const uint32_t ph = (k >> 1) & 1;
+        // S of this item (its slot's previous item has left TMEM and Q, K are
+        // in) and O = P V of the previous item (its P is written), each issued
+        // as soon as it is ready; bounded
+        bool s_done = false, pv_done = prev_s < 0;
+        const uint64_t t0 = global_timer_ns();
+        while (!(s_done && pv_done)) {
+          if (!s_done && mbar_try_wait(bar(kTFree, s), ph ^ 1u) && mbar_try_wait(bar(kLdQK, s), ph)) {
+            issue_s(s, n);
+            s_done = true;
+          }
+          if (!pv_done && mbar_try_wait(bar(kPFull, prev_s), prev_ph)) {
+            issue_pv(prev_s, prev_n);
+            pv_done = true;
+          }
+          if (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        prev_s = s;
+        prev_ph = ph;
+        prev_n = n;
+        ++k;
+      }
+      if (ok && prev_s >= 0) {
+        ok = mbar_wait(bar(kPFull, prev_s), prev_ph, abort_flag);
+        if (ok) issue_pv(prev_s, prev_n);
+      }
+      // the last commit's arrival lands before the CTA leaves (bounded)
+      if (ok && prev_s >= 0) ok = mbar_wait(bar(kSEmpty, prev_s), prev_ph, abort_flag);
+      if (!ok) {
+        // every MMA issued completes before TMEM is freed (bounded)
+        volatile int no_abort = 0;
+        mma_commit(bar(kSpare, 0));
+        mbar_wait(bar(kSpare, 0), 0, &no_abort);
+      }
+    }
+  } else {  // ── softmax / epilogue warps
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int stid = tid - 64;  // 0 .. 255
+    const int row = 32 * quarter + lane;
+    int k = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
+      int b, h, q0, start, n;
+      if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
+      const int s = k & 1;
+      const uint32_t ph = (k >> 1) & 1;
+      ++k;
+      const uint32_t sV = stage0 + s * kTcStageBytes + kTcQ * 128 + kTcMaxKeys * 128;
+      const uint32_t trow = tbase + static_cast<uint32_t>(s * kTcSlotCols) +
+                            (static_cast<uint32_t>(32 * quarter) << 16);
+      const int n_pad = (n + 15) & ~15, chunks = n_pad >> 4;
+      // V rows [n, n_pad) -> 0 (whole 128-byte rows, so the swizzle is moot)
+      bool w = mbar_wait(bar(kLdV, s), ph, abort_flag);
+      if (w) {
+        for (int i = stid; i < (n_pad - n) * 8; i += 32 * kTcSoftWarps) {
+          const uint32_t a = sV + static_cast<uint32_t>(n + (i >> 3)) * 128 + (i & 7) * 16;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+        }
+        fence_proxy_async_smem();
+      }
+      w = w && mbar_wait(bar(kSFull, s), ph, abort_flag);
+      tc_fence_after();
+      const int qi = q0 + row;
+      const bool active = q0 + 32 * quarter < n;  // warp-uniform
+      const int kmax = causal ? min(n, qi + 1) : n;
+      const int mine = (chunks - half + 1) >> 1;  // chunks j = half + 2 t, at most 6
+      // all of this thread's S chunks at once (one TMEM round trip), then the
+      // softmax from registers
+      uint32_t r[6][16];
+      float m = -INFINITY;
+      if (w && active) {
+#pragma unroll
+        for (int t = 0; t < 6; ++t)
+          if (t < mine) tmem_ld_32x32b_x16(trow + 16 * (half + 2 * t), r[t]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 6; ++t) {
+          if (t < mine) {
+            const int c = 16 * (half + 2 * t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c + j < kmax) m = fmaxf(m, __uint_as_float(r[t][j]));
+          }
+        }
+      }
+      xmax[half * kTcQ + row] = m;
+      ok = soft_bar_and(w);
+      if (!ok) break;
+      m = fmaxf(m, xmax[(half ^ 1) * kTcQ + row]);
+      float l = 0.f;
+      if (active) {
+        const float mb = m * scale_log2;
+#pragma unroll
+        for (int t = 0; t < 6; ++t) {
+          if (t < mine) {
+            const int c = 16 * (half + 2 * t);
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              const float p0 = c + j < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j]), scale_log2, -mb)) : 0.f;
+              const float p1 = c + j + 1 < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j + 1]), scale_log2, -mb)) : 0.f;
+              l += p0 + p1;
+              pk[j >> 1] = pack_bf16(p0, p1);
+            }
+            tmem_st_32x32b_x8(trow + c, pk);  // the chunk's own, consumed, columns
+          }
+        }
+        tmem_wait_st();
+      }
+      xsum[half * kTcQ + row] = l;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kPFull, s));
+      w = mbar_wait(bar(kOFull, s), ph, abort_flag);
+      ok = soft_bar_and(w);  // also publishes xsum
+      if (!ok) break;
+      tc_fence_after();
+      if (active) {
+        const float inv_l = 1.f / (l + xsum[(half ^ 1) * kTcQ + row]);
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(trow + kTcOCol + 32 * half, o);
+        tmem_wait_ld();
+        if (qi < n) {
+          uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(start + qi) * H + h * 64 + 32 * half);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 wv;
+            wv.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+            wv.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+            wv.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+            wv.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+            dst[v] = wv;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kTFree, s));
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag && err) atomicOr(err, kErrTimeout);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 2 * kTcSlotCols);
+  }
+}
+
 constexpr int kSimtRows = 64;
 constexpr int kSimtKeys = 64;
 
@@ -412,7 +732,12 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+std::atomic<int> g_attn_tc{0};  // jb_set_attention_tcgen05
+bool attn_tc_enabled() { return g_attn_tc.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace
+
+void set_attention_tcgen05(bool on) { g_attn_tc.store(on ? 1 : 0, std::memory_order_relaxed); }
 
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
@@ -428,11 +753,32 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
     CUtensorMap tm;
     memset(&tm, 0, sizeof(tm));
     const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64);
+    int skip_le = 0;  // rows the tcgen05 kernel takes
+    if (tma && attn_tc_enabled()) {
+      // rows of up to kTcMaxKeys keys: S and P V on tcgen05 (one softmax pass)
+      static bool attr = [] {
+        return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kTcSmem) == cudaSuccess;
+      }();
+      if (attr) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int items = batch * heads * 2;
+        const int grid = std::max(1, std::min(items, sms > 0 ? sms : 148));
+        attn_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(cu, static_cast<bf16*>(ctx), batch, heads,
+                                                         scale_log2, tm, err, causal);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess || max_len <= kTcMaxKeys) return e;
+        skip_le = kTcMaxKeys;
+      }
+    }
     auto kern = tma ? flash_attn_bf16_d64<true> : flash_attn_bf16_d64<false>;
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
     kern<<<grid, kFaThreads, 0, s>>>(static_cast<const bf16*>(qkv), cu, static_cast<bf16*>(ctx),
-                                     heads, scale_log2, tm, err, causal);
+                                     heads, scale_log2, tm, err, causal, skip_le);
     return cudaGetLastError();
   }
   if (dtype == JB_DT_BF16)

@@ -83,6 +83,9 @@ struct EmbedArgs {
 };
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
 
+// Rows of <= 192 keys (bf16, head_dim 64, TMA) on the tcgen05 kernel instead
+// of the mma.sync one; process-wide, off by default.
+void set_attention_tcgen05(bool on);
 // causal != 0: query i attends to keys j <= i of its row (the OpenCLIP text
 // mask, clip_text.rs:350-362).
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,

@@ -705,12 +705,15 @@ jb_model* model_load(const char* path, const char* config_json, int device, int 
       load_bert(m.get(), st, cfg);
     check_cuda(cudaMalloc(&m->d_err, sizeof(int)), "error flag");
     check_cuda(cudaMemset(m->d_err, 0, sizeof(int)), "error flag");
+    check_cuda(cudaMallocHost(&m->h_err, sizeof(int)), "error flag");
+    *m->h_err = 0;
     // the int8 FFN2 input quantiser looks the GELU up in a per-device table
     if (m->family == JB_FAMILY_BERT && m->format == JB_FMT_INT8)
       check_cuda(init_gelu_table(nullptr), "GELU table");
   } catch (...) {
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);
+    if (m->h_err) cudaFreeHost(m->h_err);
     throw;
   }
   return m.release();
@@ -729,6 +732,7 @@ void model_free(jb_model* m) {
     if (m->img_buf) cudaFree(m->img_buf);
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);
+    if (m->h_err) cudaFreeHost(m->h_err);
     profile_enable(m, false);
     for (cudaEvent_t e : m->prof_free) cudaEventDestroy(e);
   }
@@ -1016,9 +1020,10 @@ void load_projection_head(jb_model* m, const char* path, double alpha) {
 }
 
 void check_device_flag(jb_model* m, cudaStream_t s) {
+  // the flag rides the stream behind the forward's own copies: one wait
+  check_cuda(cudaMemcpyAsync(m->h_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, s), "error flag read");
   check_cuda(cudaStreamSynchronize(s), "forward");
-  int flag = 0;
-  check_cuda(cudaMemcpy(&flag, m->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error flag read");
+  const int flag = *m->h_err;
   if (!flag) return;
   cudaMemset(m->d_err, 0, sizeof(int));
   if (flag & kErrTimeout) fail(JB_ERR_TIMEOUT, "a device-side wait exceeded its limit");

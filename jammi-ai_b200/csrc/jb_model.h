@@ -147,6 +147,7 @@ struct jb_model {
   std::vector<void*> weight_allocs;
   int64_t weight_bytes = 0;
   int* d_err = nullptr;
+  int* h_err = nullptr;  // pinned host copy of *d_err, read after each synchronous call
   jb::Workspace ws;
   std::mutex mu;
   // CUDA-event timing of every launch (off unless enabled)

@@ -82,6 +82,8 @@ _SIGS = [
     ("jb_op_layernorm", _I, [_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
     ("jb_op_attention", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     ("jb_op_attention_causal", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    ("jb_op_attention_rows", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    ("jb_set_attention_tcgen05", None, [_I]),
     ("jb_op_pool_normalize", _I, [_P, _I, _P, _P, _I, _I, _I, _P]),
     ("jb_scheduler_new", _P, [ctypes.c_uint64, ctypes.c_double]),
     ("jb_scheduler_new_unlimited", _P, []),

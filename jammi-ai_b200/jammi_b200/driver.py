@@ -6,10 +6,16 @@ multi-device embedding driver (all implemented in C++ inside the library).
   (crates/jammi-ai/src/inference/runner.rs:176-256)
 * ``generate_embeddings``  -- the ``generate_embeddings`` driver over one model
   handle per device, row-order output in Arrow FixedSizeList layout.
+* ``embed_texts``          -- the same over text, tokenisation off the critical
+  path: a producer thread tokenises chunk k + 1 while the devices embed chunk k
+  (the embedding pipeline's tokenise -> forward loop, crates/jammi-ai/src/
+  pipeline/embedding.rs:47-282 with tokenizer.rs:45-93, overlapped).
 """
 from __future__ import annotations
 
 import ctypes
+import queue
+import threading
 
 import numpy as np
 
@@ -134,3 +140,63 @@ def generate_embeddings(models, values, offsets, batch_rows: int = 256, pooling:
                                        ctypes.byref(stats)))
     st = {k: getattr(stats, k) for k, _ in GenerateStats._fields_}
     return out, validity, st
+
+
+def generate_embeddings_stream(models, row_chunks, **kw):
+    """``generate_embeddings`` over an iterable of row chunks (lists of token-id
+    sequences), producing chunk k + 1 on a background thread while chunk k is
+    embedded (the C driver releases the GIL).  Yields (out, validity, stats)
+    per chunk, in order."""
+    q: queue.Queue = queue.Queue(maxsize=2)
+    done = object()
+    failure = []
+
+    def produce():
+        try:
+            for rows in row_chunks:
+                q.put(pack_rows(rows))
+        except BaseException as e:  # handed to the consumer
+            failure.append(e)
+        finally:
+            q.put(done)
+
+    t = threading.Thread(target=produce, name="jb-tokenize", daemon=True)
+    t.start()
+    try:
+        while True:
+            item = q.get()
+            if item is done:
+                break
+            values, offsets = item
+            yield generate_embeddings(models, values, offsets, **kw)
+    finally:
+        # let a blocked producer finish, then join it
+        while t.is_alive():
+            try:
+                q.get_nowait()
+            except queue.Empty:
+                t.join(timeout=0.01)
+    if failure:
+        raise failure[0]
+
+
+def embed_texts(models, texts, tokenize, chunk_rows: int = 65536, **kw):
+    """Embeddings of ``texts`` in order: ``tokenize(list_of_texts)`` returns one
+    token-id sequence per text (e.g. a wrapped HF tokenizer's ``input_ids``,
+    [CLS] ... [SEP], truncated to the model's max_seq); it runs on a producer
+    thread one chunk ahead of the devices.  Returns (out f32 [rows, H],
+    validity bitmap, list of per-chunk stats)."""
+    if chunk_rows <= 0:
+        raise ValueError("chunk_rows must be positive")
+    texts = list(texts)
+    H = models[0].info.hidden
+    chunks = (tokenize(texts[i:i + chunk_rows]) for i in range(0, len(texts), chunk_rows))
+    outs, valid, stats = [], [], []
+    for out, validity, st in generate_embeddings_stream(models, chunks, **kw):
+        outs.append(out)
+        valid.append(np.unpackbits(validity, bitorder="little")[: out.shape[0]])
+        stats.append(st)
+    if not outs:
+        return np.zeros((0, H), np.float32), np.zeros(0, np.uint8), stats
+    bits = np.concatenate(valid)
+    return np.concatenate(outs), np.packbits(bits, bitorder="little"), stats

@@ -192,12 +192,17 @@ class Bert(Model):
     def max_seq_length(self) -> int:
         return self.info.max_seq
 
-    def encode(self, ids, lens, pooling: str | None = None, stream=None) -> np.ndarray:
-        """Host buffers in, host f32 [B, H] out (``jb_encode_text``)."""
+    def encode(self, ids, lens, pooling: str | None = None, stream=None, out=None) -> np.ndarray:
+        """Host buffers in, host f32 [B, H] out (``jb_encode_text``); ``out``
+        may be a caller-owned (e.g. pinned) C-contiguous f32 [B, H] array."""
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
         lens = np.ascontiguousarray(lens, dtype=np.uint32)
         B, S = ids.shape
-        out = np.zeros((B, self.info.hidden), dtype=np.float32)
+        if out is None:
+            out = np.empty((B, self.info.hidden), dtype=np.float32)
+        elif (out.dtype != np.float32 or out.shape != (B, self.info.hidden)
+              or not out.flags.c_contiguous):
+            raise ValueError("out must be a C-contiguous float32 [batch, hidden] array")
         try:
             check(lib().jb_encode_text(self._h, _ptr(ids), _ptr(lens), B, S,
                                        POOLING[pooling or self.pooling], _ptr(out),

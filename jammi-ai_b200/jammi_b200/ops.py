@@ -84,13 +84,19 @@ def layernorm(x: torch.Tensor, gamma, beta, eps: float, residual=None) -> torch.
 
 
 def attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, heads: int, max_len: int,
-              causal: bool = False) -> torch.Tensor:
+              causal: bool = False, tma: bool = False) -> torch.Tensor:
     """qkv [T, 3*heads*d] packed rows, cu_seqlens int32 [B+1] -> ctx [T, heads*d]
-    (``causal``: query i sees keys j <= i of its row)."""
+    (``causal``: query i sees keys j <= i of its row; ``tma``: pass the row
+    count, which selects the model forwards' TMA / tcgen05 kernels)."""
     _contig(qkv, cu_seqlens)
     T, three_h = qkv.shape
     H = three_h // 3
     ctx = torch.empty((T, H), dtype=qkv.dtype, device=qkv.device)
+    if tma:
+        check(lib().jb_op_attention_rows(_p(qkv), _p(cu_seqlens), _p(ctx), _DT[qkv.dtype],
+                                         cu_seqlens.numel() - 1, heads, H // heads, max_len, T,
+                                         1 if causal else 0, _s(qkv)))
+        return ctx
     fn = lib().jb_op_attention_causal if causal else lib().jb_op_attention
     check(fn(_p(qkv), _p(cu_seqlens), _p(ctx), _DT[qkv.dtype], cu_seqlens.numel() - 1, heads,
              H // heads, max_len, _s(qkv)))
@@ -124,3 +130,9 @@ def preprocess_rgb8(images, target: int, mean, std, device="cuda") -> torch.Tens
     check(lib().jb_op_preprocess_rgb8(_p(d_buf), _p(d_off), _p(d_w), _p(d_h), len(images), max_side,
                                       target, m.data_ptr(), s.data_ptr(), _p(out), _s(out)))
     return out
+
+
+def set_attention_tcgen05(on: bool):
+    """``jb_set_attention_tcgen05``: rows of <= 192 keys on the tcgen05 attention
+    kernel (process-wide; off by default)."""
+    lib().jb_set_attention_tcgen05(1 if on else 0)

@@ -163,3 +163,41 @@ def test_non_oom_error_propagates_immediately():
         run_chunks(100, 16, forward)
     assert calls == [16], "a systemic error is never retried"
     assert e.value.status == L.ERR_CUDA
+
+
+# ── tokenisation overlapped with the devices (embed_texts) ───────────────────
+
+def test_stream_tokenises_ahead_in_order(monkeypatch):
+    """The producer thread runs one chunk ahead of the embedding calls; chunks
+    come back in order, and a tokenizer failure reaches the caller."""
+    import numpy as np
+    from jammi_b200 import driver as D
+    calls, produced = [], []
+
+    def fake_generate(models, values, offsets, **kw):
+        rows = offsets.size - 1
+        calls.append((len(produced), rows))
+        time.sleep(0.02)
+        out = np.tile(np.arange(rows, dtype=np.float32)[:, None], (1, 4)) + values[:1].sum()
+        return out, np.full((rows + 7) // 8, 0xFF, np.uint8), {"rows": rows}
+
+    def tokenize(texts):
+        produced.append(len(texts))
+        return [[int(t)] * (1 + int(t) % 3) for t in texts]
+
+    monkeypatch.setattr(D, "generate_embeddings", fake_generate)
+
+    class M:
+        class info:
+            hidden = 4
+    out, valid, stats = D.embed_texts([M()], [str(i) for i in range(10)], tokenize, chunk_rows=4)
+    assert [st["rows"] for st in stats] == [4, 4, 2]
+    assert out.shape == (10, 4)
+    assert np.array_equal(np.unpackbits(valid, bitorder="little")[:10], np.ones(10, np.uint8))
+    # by the time chunk k is embedded, chunk k + 1 has usually been tokenised
+    assert calls[0][0] >= 1
+
+    def bad(texts):
+        raise RuntimeError("tokenizer failed")
+    with pytest.raises(RuntimeError):
+        D.embed_texts([M()], ["a", "b"], bad, chunk_rows=1)

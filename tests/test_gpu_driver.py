@@ -66,3 +66,19 @@ def test_generate_embeddings_rejects_long_rows(setup):
     with pytest.raises(JbError):
         generate_embeddings([model], values, offsets)
     model.close()
+
+
+def test_embed_texts_matches_one_job(setup):
+    """embed_texts (tokenisation one chunk ahead of the device) equals one
+    generate_embeddings job over the same rows: row results do not depend on
+    the batch a row lands in."""
+    from jammi_b200 import Bert
+    from jammi_b200.driver import embed_texts, generate_embeddings, pack_rows
+    cfg, w, lens, rows = setup
+    model = Bert.from_weights(w, cfg, device=0, fmt="bf16")
+    texts = list(range(len(rows)))  # "text" i tokenises to row i
+    out, validity, stats = embed_texts([model], texts, lambda ts: [rows[i] for i in ts],
+                                       chunk_rows=96, batch_rows=64)
+    ref, ref_valid, _ = generate_embeddings([model], *pack_rows(rows), batch_rows=64)
+    assert len(stats) == -(-len(rows) // 96)
+    assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)

@@ -145,15 +145,22 @@ def _bert_base(seed):
     return cfg, ob.random_bert_weights(cfg, seed=seed)
 
 
-def test_bert_base_bf16_config():
-    """BERT-base, bf16, seq 256, lengths U[32,256] (batch reduced for the oracle)."""
+@pytest.mark.parametrize("tc_attention", [False, True])
+def test_bert_base_bf16_config(tc_attention):
+    """BERT-base, bf16, seq 256, lengths U[32,256] (batch reduced for the oracle);
+    with tc_attention, rows of <= 192 keys take the tcgen05 attention kernel."""
+    from jammi_b200 import ops
     cfg, w = _bert_base(201)
     rng = np.random.default_rng(202)
     lens = rng.integers(32, 257, size=12)
     lens[0] = 256
     ids, mask = ob.random_token_batch(12, 256, lens, seed=203)
     ref = ob.bert_forward(w, cfg, ids, mask)
-    out = _bert(w, cfg.to_dict(), "bf16").encode(ids, lens)
+    ops.set_attention_tcgen05(tc_attention)
+    try:
+        out = _bert(w, cfg.to_dict(), "bf16").encode(ids, lens)
+    finally:
+        ops.set_attention_tcgen05(False)
     assert_close_rows(out, ref, "bf16")
 
 

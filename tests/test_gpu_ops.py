@@ -289,6 +289,36 @@ def test_attention_varlen(dev, dtype, heads, d, lens):
     assert err < tol, err
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("lens", [
+    [1, 2, 15, 16, 17, 63, 64, 65, 127, 128, 129, 200, 255, 256],
+    [50] * 7,
+    [256, 0, 3, 177],
+])
+@pytest.mark.parametrize("tc", [True, False])
+def test_attention_tma_rows(dev, lens, causal, tc):
+    """The model forwards' TMA kernels: with tc, rows of <= 192 keys on the
+    tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma, P through TMEM) and
+    longer rows on the mma.sync one in the same call; without, mma.sync only."""
+    ops = _ops()
+    ops.set_attention_tcgen05(tc)
+    heads, d = 12, 64
+    rng = np.random.default_rng(sum(lens) + (7 if causal else 0))
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = (rng.standard_normal((T + 5, 3 * heads * d)) * 1.5).astype(np.float32)
+    qt = _bf16(qkv, dev)
+    try:
+        ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens),
+                            causal=causal, tma=True)
+        ops.sync()
+    finally:
+        ops.set_attention_tcgen05(False)
+    ref = _attn_ref(qt.double().cpu().numpy()[:T], cu, heads, causal=causal)
+    err = np.abs(ctx.double().cpu().numpy()[:T] - ref).max()
+    assert err < 2e-2, err
+
+
 @pytest.mark.parametrize("dtype,heads,d,lens", [
     ("bf16", 8, 64, [77, 1, 2, 63, 64, 65, 128, 129, 30]),
     ("bf16", 12, 64, [200, 0, 7]),
