@@ -365,10 +365,15 @@ extern "C" jb_status jb_generate_embeddings(jb_model** models, int n_models, con
     if (!models || n_models < 1 || !offsets || rows < 0 || !opts || !out || (rows > 0 && !ids))
       return err(JB_ERR_INVALID, "jb_generate_embeddings: bad argument");
     if (opts->batch_rows < 1) return err(JB_ERR_INVALID, "batch_rows must be >= 1");
-    const int H = models[0]->hidden;
+    // text encoders: the BERT family, or the OpenCLIP text tower (its rows end
+    // at their EOT token, the zero padding after it is never reached)
+    const int family = models[0] ? models[0]->family : -1;
+    if (family != JB_FAMILY_BERT && family != JB_FAMILY_CLIP_TEXT)
+      return err(JB_ERR_INVALID, "all models must be text encoders of the same width");
+    const int H = jb::output_dim(models[0]);
     int max_seq = 1 << 30;
     for (int i = 0; i < n_models; ++i) {
-      if (!models[i] || models[i]->family != JB_FAMILY_BERT || models[i]->hidden != H)
+      if (!models[i] || models[i]->family != family || jb::output_dim(models[i]) != H)
         return err(JB_ERR_INVALID, "all models must be text encoders of the same width");
       for (int j = 0; j < i; ++j)
         if (models[j]->device == models[i]->device)

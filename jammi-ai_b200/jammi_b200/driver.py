@@ -127,7 +127,7 @@ def generate_embeddings(models, values, offsets, batch_rows: int = 256, pooling:
     values = np.ascontiguousarray(values, dtype=np.uint32)
     offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
     rows = offsets.size - 1
-    H = models[0].info.hidden
+    H = models[0].info.output_dim
     out = np.empty((rows, H), dtype=np.float32)
     validity = np.zeros((rows + 7) // 8, dtype=np.uint8)
     handles = (ctypes.c_void_p * len(models))(*[m.handle.value for m in models])
@@ -189,7 +189,7 @@ def embed_texts(models, texts, tokenize, chunk_rows: int = 65536, **kw):
     if chunk_rows <= 0:
         raise ValueError("chunk_rows must be positive")
     texts = list(texts)
-    H = models[0].info.hidden
+    H = models[0].info.output_dim
     chunks = (tokenize(texts[i:i + chunk_rows]) for i in range(0, len(texts), chunk_rows))
     outs, valid, stats = [], [], []
     for out, validity, st in generate_embeddings_stream(models, chunks, **kw):

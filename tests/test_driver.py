@@ -190,6 +190,7 @@ def test_stream_tokenises_ahead_in_order(monkeypatch):
     class M:
         class info:
             hidden = 4
+            output_dim = 4
     out, valid, stats = D.embed_texts([M()], [str(i) for i in range(10)], tokenize, chunk_rows=4)
     assert [st["rows"] for st in stats] == [4, 4, 2]
     assert out.shape == (10, 4)

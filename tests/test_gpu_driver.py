@@ -82,3 +82,22 @@ def test_embed_texts_matches_one_job(setup):
     ref, ref_valid, _ = generate_embeddings([model], *pack_rows(rows), batch_rows=64)
     assert len(stats) == -(-len(rows) // 96)
     assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)
+
+
+def test_generate_embeddings_clip_text():
+    """The driver over the OpenCLIP text tower: rows padded with zeros after
+    their EOT token, output width embed_dim, same rows as direct calls."""
+    import json
+    from conftest import load_golden
+    from jammi_b200 import OpenClipText
+    from jammi_b200.driver import generate_embeddings, pack_rows
+    w, g = load_golden("small_clip_text.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = OpenClipText.from_weights(w, cfg, device=0, fmt="f32")
+    ids = g["ids"]
+    eot = ids.argmax(1)
+    rows = [ids[b, :eot[b] + 1] for b in range(ids.shape[0])] + [np.zeros(0, np.uint32)]
+    out, validity, stats = generate_embeddings([model], *pack_rows(rows), batch_rows=4)
+    assert out.shape == (len(rows), model.embed_dim())
+    assert np.all(out[-1] == 0) and stats["valid_rows"] == len(rows) - 1
+    assert np.array_equal(out[:-1], model.encode(ids))
