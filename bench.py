@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attention", default="mma", choices=["mma", "tcgen05"],
+                    help="attention kernel for rows of <= 192 keys (jb_set_attention_tcgen05)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed steps only (no clock sampler, e2e loop or CPU leg); "
                          "for profiler captures")
@@ -224,9 +226,10 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    from jammi_b200 import Bert
+    from jammi_b200 import Bert, ops
     from jammi_b200.synthetic import bert_weights
 
+    ops.set_attention_tcgen05(args.attention == "tcgen05")
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -365,6 +368,7 @@ def main():
             "kernel_ms_per_step": {k: v["ms"] / prof_steps for k, v in prof.items()},
             "kernel_ms_source": f"separate {prof_steps}-step pass with per-launch CUDA events",
             "forward": "CUDA graph replay (captured on the second call of a shape)",
+            "attention": args.attention,
             "clocks": clk,
             "cpu_baseline": cpu,
         }

@@ -317,54 +317,42 @@ __global__ void __launch_bounds__(kFaThreads, 4)
 
 // ── tcgen05 attention for rows of at most 192 keys ──────────────────────────
 // A persistent, warp-specialised kernel: one CTA per SM walks the work items
-// (row, head, 128-query block) of rows with at most kTcMaxKeys keys, two
-// items in flight through two shared-memory stages and two 256-column TMEM
-// slots, so that the loads of one item, the MMAs of another and the softmax
-// of a third overlap.  A row's keys all fit one accumulator, so its softmax
-// is exact in one pass (no running rescale).
-//   warp 0  (TMA): Q and K onto one mbarrier, V onto a second, 64-row boxes.
-//   warp 1  (MMA): S = Q K^T, four kind::f16 MMAs (K = 16) into the slot's
-//           columns [0, n_pad), n_pad = the row length rounded up to 16; once
-//           the softmax has written P: O = P V, one MMA per 16-key chunk with
-//           A = P read from TMEM and B = V straight from its TMA tile
-//           (MN-major, 128-byte swizzle), into the slot's columns [192, 256).
-//   warps 2-9 (softmax): warp w reads TMEM lanes 32 (w % 4) .. + 31 (queries
-//           q0 + 32 (w % 4) + lane) and the 16-key chunks j with
-//           j % 2 == (w - 2) / 4: two threads per query row, which exchange
-//           the row max and sum through shared memory.  They zero the V rows
-//           past the row's end (other rows' values: 0 * V must stay 0), load
-//           all their chunks of S at once into registers (max; then
-//           2^(s log2(e) / 8 - m) and the partial sums), write each chunk's
-//           P as bf16 pairs into the
-//           chunk's own first 8 columns, and after O = P V scale their 32
-//           columns of the O row by 1 / sum and store them (64 B).
+// (row, head, 128-query block) of rows with at most kTcMaxKeys keys.  A row's
+// keys all fit one accumulator, so its softmax is exact in one pass (no
+// running rescale).
+//   warp 0  (TMA): Q and K onto one mbarrier, V onto a second, 64-row boxes,
+//           into three shared-memory stages (loads run up to two items ahead).
+//   warp 1  (MMA): S = Q K^T, four kind::f16 MMAs (K = 16) into the item's
+//           TMEM slot, columns [0, n_pad), n_pad = the row length rounded up
+//           to 16; once the softmax has written P: O = P V, one MMA per
+//           16-key chunk with A = P read from TMEM and B = V straight from its
+//           TMA tile (MN-major, 128-byte swizzle), into the slot's columns
+//           [192, 256).  Each is issued as soon as its inputs are ready
+//           (non-blocking probes of the barriers).
+//   warps 2-5 and 6-9 (softmax, two groups ping-ponging on alternate items,
+//           each with its own 256-column TMEM slot): warp w reads TMEM lanes
+//           32 (w % 4) .. + 31, one thread per query row.  The group zeroes
+//           the V rows past the row's end (other rows' values: 0 * V must
+//           stay 0), reads S in register batches (max; then
+//           2^(s log2(e) / 8 - m) and the sum), writes each 16-key chunk's P
+//           as bf16 pairs into the chunk's own first 8 columns and, after
+//           O = P V, scales the O row by 1 / sum and stores it (128 B).  While
+//           one group waits for its O, the other runs its softmax.
 // causal != 0 masks keys after the query.  Longer rows are left to the
 // mma.sync kernel; the choice is per row, so a row's result does not depend
 // on its batch.  Every wait is bounded; on a timeout each role stops, the
 // TMA and MMA threads wait (bounded) for their copies and MMAs in flight,
 // the error flag is set and TMEM is freed.
-constexpr int kTcQ = 128;        // queries per item
-constexpr int kTcMaxKeys = 192;  // keys per row this kernel takes
-constexpr int kTcSlotCols = 256; // TMEM columns per slot; two slots
-constexpr int kTcOCol = 192;     // O's first column inside a slot
-constexpr int kTcSoftWarps = 8;
-constexpr int kTcThreads = 64 + 32 * kTcSoftWarps;
-constexpr int kTcSoftBarrier = 1;  // named barrier of the softmax warps
+constexpr int kTcQ = 128;         // queries per item
+constexpr int kTcMaxKeys = 192;   // keys per row this kernel takes
+constexpr int kTcSlotCols = 256;  // TMEM columns per slot; two slots
+constexpr int kTcOCol = 192;      // O's first column inside a slot
+constexpr int kTcStages = 3;
+constexpr int kTcGroupWarps = 4;
+constexpr int kTcThreads = 64 + 2 * 32 * kTcGroupWarps;
 constexpr int kTcStageBytes = (kTcQ + 2 * kTcMaxKeys) * 128;
-constexpr int kTcSmem = 2 * kTcStageBytes + 1024 + 256 + 2 * 2 * kTcQ * 4;
-
-__device__ __forceinline__ bool soft_bar_and(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "n"(kTcSoftBarrier), "n"(32 * kTcSoftWarps)
-      : "memory");
-  return r != 0;
-}
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256;
+constexpr int kTcBatch = 6;  // 16-column chunks per register batch
 
 // Work item idx -> (row, head, query block); false for items with no work here.
 __device__ __forceinline__ bool tc_item(const int* cu, int heads, int idx, int& b, int& h, int& q0,
@@ -387,27 +375,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t stage0 = (raw + 1023u) & ~1023u;
-  uint8_t* meta = smem_raw + (stage0 + 2 * kTcStageBytes - raw);
+  uint8_t* meta = smem_raw + (stage0 + kTcStages * kTcStageBytes - raw);
   const uint32_t bars = smem_u32(meta);
-  // per stage / slot s: ld_qk, ld_v, s_full, p_full, o_full, tmem_free, smem_empty, spare
-  auto bar = [&](int kind, int s) { return bars + 8u * (kind * 2 + s); };
-  enum { kLdQK = 0, kLdV, kSFull, kPFull, kOFull, kTFree, kSEmpty, kSpare };
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(meta + 8 * 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 16 + 4);
-  float* xmax = reinterpret_cast<float*>(meta + 256);  // [2 halves][128 rows]
-  float* xsum = xmax + 2 * kTcQ;
+  // stage barriers (3 each): ld_qk, ld_v, smem_empty; slot barriers (2 each):
+  // s_full, p_full, o_full, tmem_free; one spare
+  auto sbar = [&](int kind, int st) { return bars + 8u * (kind * kTcStages + st); };
+  auto tbar = [&](int kind, int sl) { return bars + 8u * (3 * kTcStages + kind * 2 + sl); };
+  enum { kLdQK = 0, kLdV = 1, kSEmpty = 2 };
+  enum { kSFull = 0, kPFull = 1, kOFull = 2, kTFree = 3 };
+  const uint32_t spare = bars + 8u * (3 * kTcStages + 8);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(meta + 8 * 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 24 + 4);
 
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(kLdQK, s), 1);
-      mbar_init(bar(kLdV, s), 1);
-      mbar_init(bar(kSFull, s), 1);
-      mbar_init(bar(kPFull, s), kTcSoftWarps);
-      mbar_init(bar(kOFull, s), 1);
-      mbar_init(bar(kTFree, s), kTcSoftWarps);
-      mbar_init(bar(kSEmpty, s), 1);
-      mbar_init(bar(kSpare, s), 1);
+    for (int st = 0; st < kTcStages; ++st) {
+      mbar_init(sbar(kLdQK, st), 1);
+      mbar_init(sbar(kLdV, st), 1);
+      mbar_init(sbar(kSEmpty, st), 1);
     }
+    for (int sl = 0; sl < 2; ++sl) {
+      mbar_init(tbar(kSFull, sl), 1);
+      mbar_init(tbar(kPFull, sl), kTcGroupWarps);
+      mbar_init(tbar(kOFull, sl), 1);
+      mbar_init(tbar(kTFree, sl), kTcGroupWarps);
+    }
+    mbar_init(spare, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -416,6 +408,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  auto stage_of = [&](int k) { return stage0 + static_cast<uint32_t>(k % kTcStages) * kTcStageBytes; };
 
   if (warp == 0) {
     if (lane == 0) {  // ── TMA producer
@@ -423,206 +416,206 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
         int b, h, q0, start, n;
         if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
-        const int s = k & 1;
-        const uint32_t ph = (k >> 1) & 1;
-        if (!mbar_wait(bar(kSEmpty, s), ph ^ 1u, abort_flag)) break;
-        const uint32_t sQ = stage0 + s * kTcStageBytes, sK = sQ + kTcQ * 128, sV = sK + kTcMaxKeys * 128;
+        const int st = k % kTcStages;
+        const uint32_t ph = (k / kTcStages) & 1;
+        if (!mbar_wait(sbar(kSEmpty, st), ph ^ 1u, abort_flag)) break;
+        const uint32_t sQ = stage_of(k), sK = sQ + kTcQ * 128, sV = sK + kTcMaxKeys * 128;
         const int n_pad = (n + 15) & ~15;
         const int kboxes = (n_pad + 63) >> 6;
         const int qboxes = min(2, (n - q0 + 63) >> 6);
-        mbar_arrive_expect_tx(bar(kLdQK, s), static_cast<uint32_t>(qboxes + kboxes) * kTileBytes);
-        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, h * 64, start + q0 + 64 * i, bar(kLdQK, s));
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + h * 64, start + 64 * i, bar(kLdQK, s));
-        mbar_arrive_expect_tx(bar(kLdV, s), static_cast<uint32_t>(kboxes) * kTileBytes);
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + h * 64, start + 64 * i, bar(kLdV, s));
+        mbar_arrive_expect_tx(sbar(kLdQK, st), static_cast<uint32_t>(qboxes + kboxes) * kTileBytes);
+        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, h * 64, start + q0 + 64 * i, sbar(kLdQK, st));
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + h * 64, start + 64 * i, sbar(kLdQK, st));
+        mbar_arrive_expect_tx(sbar(kLdV, st), static_cast<uint32_t>(kboxes) * kTileBytes);
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + h * 64, start + 64 * i, sbar(kLdV, st));
         ++k;
       }
       if (*abort_flag) {
         // copies in flight land before the CTA leaves (bounded)
         volatile int no_abort = 0;
-        for (int j = max(0, k - 2); j < k; ++j) {
-          mbar_wait(bar(kLdQK, j & 1), (j >> 1) & 1, &no_abort);
-          mbar_wait(bar(kLdV, j & 1), (j >> 1) & 1, &no_abort);
+        for (int j = max(0, k - kTcStages); j < k; ++j) {
+          mbar_wait(sbar(kLdQK, j % kTcStages), (j / kTcStages) & 1, &no_abort);
+          mbar_wait(sbar(kLdV, j % kTcStages), (j / kTcStages) & 1, &no_abort);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ── MMA issuer
-      int k = 0;
-      int prev_s = -1, prev_n = 0;  // the item whose O = P V is pending
-      uint32_t prev_ph = 0;
-      bool ok = true;
-      auto issue_s = [&](int s, int n) {
-        tc_fence_after();
-        const uint32_t sQ = stage0 + s * kTcStageBytes, sK = sQ + kTcQ * 128;
-        const uint32_t idesc = idesc_bf16_f32(kTcQ, (n + 15) & ~15);
+      // items k with S issued (< ks) and with O = P V issued (< kp); ns[]
+      // remembers the row lengths of the items in flight
+      int ks = 0, kp = 0;
+      int ns[4] = {0, 0, 0, 0};
+      int idx_s = blockIdx.x;
+      bool more = true, ok = true;
+      const uint64_t t_limit = kWaitLimitNs;
+      uint64_t t0 = global_timer_ns();
+      while (ok) {
+        bool progress = false;
+        // next item whose S can go: its slot free and its Q, K loaded
+        if (more && ks - kp < 2) {
+          int b, h, q0, start, n;
+          bool found = false;
+          int idx = idx_s;
+          for (; idx < items; idx += gridDim.x)
+            if (tc_item(cu, heads, idx, b, h, q0, start, n)) { found = true; break; }
+          if (!found) {
+            more = false;
+          } else {
+            idx_s = idx;
+            const int sl = ks & 1, st = ks % kTcStages;
+            if (mbar_test_wait(tbar(kTFree, sl), ((ks >> 1) & 1) ^ 1u) &&
+                mbar_test_wait(sbar(kLdQK, st), (ks / kTcStages) & 1)) {
+              tc_fence_after();
+              const uint32_t sQ = stage_of(ks), sK = sQ + kTcQ * 128;
+              const uint32_t idesc = idesc_bf16_f32(kTcQ, (n + 15) & ~15);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_bf16(tbase + static_cast<uint32_t>(s * kTcSlotCols), umma_desc_sw128(sQ + 32u * kk),
-                   umma_desc_sw128(sK + 32u * kk), idesc, kk != 0);
-        mma_commit(bar(kSFull, s));
-      };
-      auto issue_pv = [&](int s, int n) {
-        tc_fence_after();
-        const uint32_t sV = stage0 + s * kTcStageBytes + kTcQ * 128 + kTcMaxKeys * 128;
-        const uint32_t slot = tbase + static_cast<uint32_t>(s * kTcSlotCols);
-        const uint32_t idesc = idesc_bf16_f32(kTcQ, 64) | (1u << 16);  // B (V) MN-major
-        const int chunks = ((n + 15) & ~15) >> 4;
-#pragma unroll 1
-        for (int c = 0; c < chunks; ++c)
-          mma_bf16_ta(slot + kTcOCol, slot + 16u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
-        mma_commit(bar(kOFull, s));
-        mma_commit(bar(kSEmpty, s));
-      };
-      for (int idx = blockIdx.x; idx < items && ok; idx += gridDim.x) {
-        int b, h, q0, start, n;
-        if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
-        const int s = k & 1;
-        const uint32_t ph = (k >> 1) & 1;
-        // S of this item (its slot's previous item has left TMEM and Q, K are
-        // in) and O = P V of the previous item (its P is written), each issued
-        // as soon as it is ready; bounded
-        bool s_done = false, pv_done = prev_s < 0;
-        const uint64_t t0 = global_timer_ns();
-        while (!(s_done && pv_done)) {
-          if (!s_done && mbar_try_wait(bar(kTFree, s), ph ^ 1u) && mbar_try_wait(bar(kLdQK, s), ph)) {
-            issue_s(s, n);
-            s_done = true;
-          }
-          if (!pv_done && mbar_try_wait(bar(kPFull, prev_s), prev_ph)) {
-            issue_pv(prev_s, prev_n);
-            pv_done = true;
-          }
-          if (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs) {
-            *abort_flag = 1;
-            ok = false;
-            break;
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16(tbase + static_cast<uint32_t>(sl * kTcSlotCols), umma_desc_sw128(sQ + 32u * kk),
+                         umma_desc_sw128(sK + 32u * kk), idesc, kk != 0);
+              mma_commit(tbar(kSFull, sl));
+              ns[ks & 3] = n;
+              ++ks;
+              idx_s += gridDim.x;
+              progress = true;
+            }
           }
         }
-        if (!ok) break;
-        prev_s = s;
-        prev_ph = ph;
-        prev_n = n;
-        ++k;
-      }
-      if (ok && prev_s >= 0) {
-        ok = mbar_wait(bar(kPFull, prev_s), prev_ph, abort_flag);
-        if (ok) issue_pv(prev_s, prev_n);
+        // O = P V of the oldest item whose P is written
+        if (kp < ks && mbar_test_wait(tbar(kPFull, kp & 1), (kp >> 1) & 1)) {
+          tc_fence_after();
+          const int sl = kp & 1;
+          const uint32_t sV = stage_of(kp) + kTcQ * 128 + kTcMaxKeys * 128;
+          const uint32_t slot = tbase + static_cast<uint32_t>(sl * kTcSlotCols);
+          const uint32_t idesc = idesc_bf16_f32(kTcQ, 64) | (1u << 16);  // B (V) MN-major
+          const int chunks = ((ns[kp & 3] + 15) & ~15) >> 4;
+#pragma unroll 1
+          for (int c = 0; c < chunks; ++c)
+            mma_bf16_ta(slot + kTcOCol, slot + 16u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
+          mma_commit(tbar(kOFull, sl));
+          mma_commit(sbar(kSEmpty, kp % kTcStages));
+          ++kp;
+          progress = true;
+        }
+        if (!more && kp == ks) break;
+        if (progress) {
+          t0 = global_timer_ns();
+        } else if (*abort_flag || global_timer_ns() - t0 > t_limit) {
+          *abort_flag = 1;
+          ok = false;
+        }
       }
       // the last commit's arrival lands before the CTA leaves (bounded)
-      if (ok && prev_s >= 0) ok = mbar_wait(bar(kSEmpty, prev_s), prev_ph, abort_flag);
+      if (ok && kp > 0) ok = mbar_wait(sbar(kSEmpty, (kp - 1) % kTcStages), ((kp - 1) / kTcStages) & 1, abort_flag);
       if (!ok) {
         // every MMA issued completes before TMEM is freed (bounded)
         volatile int no_abort = 0;
-        mma_commit(bar(kSpare, 0));
-        mbar_wait(bar(kSpare, 0), 0, &no_abort);
+        mma_commit(spare);
+        mbar_wait(spare, 0, &no_abort);
       }
     }
-  } else {  // ── softmax / epilogue warps
-    const int quarter = warp & 3, half = (warp - 2) >> 2;
-    const int stid = tid - 64;  // 0 .. 255
+  } else {  // ── softmax / epilogue groups
+    const int group = (warp - 2) / kTcGroupWarps;       // items k with k % 2 == group
+    const int quarter = warp & 3;
+    const int gtid = tid - 64 - group * 32 * kTcGroupWarps;  // 0 .. 127
     const int row = 32 * quarter + lane;
     int k = 0;
-    bool ok = true;
     for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
       int b, h, q0, start, n;
       if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
-      const int s = k & 1;
-      const uint32_t ph = (k >> 1) & 1;
-      ++k;
-      const uint32_t sV = stage0 + s * kTcStageBytes + kTcQ * 128 + kTcMaxKeys * 128;
-      const uint32_t trow = tbase + static_cast<uint32_t>(s * kTcSlotCols) +
+      const int kk = k++;
+      if ((kk & 1) != group) continue;
+      const int st = kk % kTcStages;
+      const uint32_t sph = (kk / kTcStages) & 1, tph = (kk >> 1) & 1;
+      const uint32_t sV = stage_of(kk) + kTcQ * 128 + kTcMaxKeys * 128;
+      const uint32_t trow = tbase + static_cast<uint32_t>(group * kTcSlotCols) +
                             (static_cast<uint32_t>(32 * quarter) << 16);
       const int n_pad = (n + 15) & ~15, chunks = n_pad >> 4;
       // V rows [n, n_pad) -> 0 (whole 128-byte rows, so the swizzle is moot)
-      bool w = mbar_wait(bar(kLdV, s), ph, abort_flag);
-      if (w) {
-        for (int i = stid; i < (n_pad - n) * 8; i += 32 * kTcSoftWarps) {
-          const uint32_t a = sV + static_cast<uint32_t>(n + (i >> 3)) * 128 + (i & 7) * 16;
-          asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
-        }
-        fence_proxy_async_smem();
+      if (!mbar_wait(sbar(kLdV, st), sph, abort_flag)) break;
+      for (int i = gtid; i < (n_pad - n) * 8; i += 32 * kTcGroupWarps) {
+        const uint32_t a = sV + static_cast<uint32_t>(n + (i >> 3)) * 128 + (i & 7) * 16;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
       }
-      w = w && mbar_wait(bar(kSFull, s), ph, abort_flag);
+      fence_proxy_async_smem();
+      if (!mbar_wait(tbar(kSFull, group), tph, abort_flag)) break;
       tc_fence_after();
       const int qi = q0 + row;
       const bool active = q0 + 32 * quarter < n;  // warp-uniform
       const int kmax = causal ? min(n, qi + 1) : n;
-      const int mine = (chunks - half + 1) >> 1;  // chunks j = half + 2 t, at most 6
-      // all of this thread's S chunks at once (one TMEM round trip), then the
-      // softmax from registers
-      uint32_t r[6][16];
-      float m = -INFINITY;
-      if (w && active) {
-#pragma unroll
-        for (int t = 0; t < 6; ++t)
-          if (t < mine) tmem_ld_32x32b_x16(trow + 16 * (half + 2 * t), r[t]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 6; ++t) {
-          if (t < mine) {
-            const int c = 16 * (half + 2 * t);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (c + j < kmax) m = fmaxf(m, __uint_as_float(r[t][j]));
-          }
-        }
-      }
-      xmax[half * kTcQ + row] = m;
-      ok = soft_bar_and(w);
-      if (!ok) break;
-      m = fmaxf(m, xmax[(half ^ 1) * kTcQ + row]);
       float l = 0.f;
       if (active) {
-        const float mb = m * scale_log2;
+        float m = -INFINITY;
+        uint32_t r[kTcBatch][16];
+#pragma unroll 1
+        for (int c0 = 0; c0 < chunks; c0 += kTcBatch) {
 #pragma unroll
-        for (int t = 0; t < 6; ++t) {
-          if (t < mine) {
-            const int c = 16 * (half + 2 * t);
-            uint32_t pk[8];
+          for (int t = 0; t < kTcBatch; ++t)
+            if (c0 + t < chunks) tmem_ld_32x32b_x16(trow + 16 * (c0 + t), r[t]);
+          tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-              const float p0 = c + j < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j]), scale_log2, -mb)) : 0.f;
-              const float p1 = c + j + 1 < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j + 1]), scale_log2, -mb)) : 0.f;
-              l += p0 + p1;
-              pk[j >> 1] = pack_bf16(p0, p1);
+          for (int t = 0; t < kTcBatch; ++t) {
+            if (c0 + t < chunks) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (16 * (c0 + t) + j < kmax) m = fmaxf(m, __uint_as_float(r[t][j]));
             }
-            tmem_st_32x32b_x8(trow + c, pk);  // the chunk's own, consumed, columns
+          }
+        }
+        const float mb = m * scale_log2;
+#pragma unroll 1
+        for (int c0 = 0; c0 < chunks; c0 += kTcBatch) {
+#pragma unroll
+          for (int t = 0; t < kTcBatch; ++t)
+            if (c0 + t < chunks) tmem_ld_32x32b_x16(trow + 16 * (c0 + t), r[t]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < kTcBatch; ++t) {
+            if (c0 + t < chunks) {
+              const int c = 16 * (c0 + t);
+              uint32_t pk[8];
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                const float p0 = c + j < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j]), scale_log2, -mb)) : 0.f;
+                const float p1 = c + j + 1 < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j + 1]), scale_log2, -mb)) : 0.f;
+                l += p0 + p1;
+                pk[j >> 1] = pack_bf16(p0, p1);
+              }
+              tmem_st_32x32b_x8(trow + c, pk);  // the chunk's own, consumed, columns
+            }
           }
         }
         tmem_wait_st();
       }
-      xsum[half * kTcQ + row] = l;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPFull, s));
-      w = mbar_wait(bar(kOFull, s), ph, abort_flag);
-      ok = soft_bar_and(w);  // also publishes xsum
-      if (!ok) break;
+      if (lane == 0) mbar_arrive(tbar(kPFull, group));
+      if (!mbar_wait(tbar(kOFull, group), tph, abort_flag)) break;
       tc_fence_after();
       if (active) {
-        const float inv_l = 1.f / (l + xsum[(half ^ 1) * kTcQ + row]);
+        const float inv_l = 1.f / l;
         uint32_t o[32];
-        tmem_ld_32x32b_x32(trow + kTcOCol + 32 * half, o);
-        tmem_wait_ld();
-        if (qi < n) {
-          uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(start + qi) * H + h * 64 + 32 * half);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 wv;
-            wv.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-            wv.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-            wv.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-            wv.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-            dst[v] = wv;
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld_32x32b_x32(trow + kTcOCol + 32 * half, o);
+          tmem_wait_ld();
+          if (qi < n) {
+            uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(start + qi) * H + h * 64 + 32 * half);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 wv;
+              wv.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+              wv.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+              wv.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+              wv.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+              dst[v] = wv;
+            }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kTFree, s));
+      if (lane == 0) mbar_arrive(tbar(kTFree, group));
     }
-    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
