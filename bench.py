@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attention", default="mma", choices=["mma", "tcgen05"],
-                    help="attention kernel for rows of <= 192 keys (jb_set_attention_tcgen05)")
+                    help="attention kernel for rows of <= 256 keys (jb_set_attention_tcgen05)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed steps only (no clock sampler, e2e loop or CPU leg); "
                          "for profiler captures")

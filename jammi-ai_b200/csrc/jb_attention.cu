@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <cmath>
 #include <atomic>
+#include <mutex>
 #include <cstring>
 
 #include <cudaTypedefs.h>
@@ -315,60 +316,63 @@ __global__ void __launch_bounds__(kFaThreads, 4)
   }
 }
 
-// ── tcgen05 attention for rows of at most 192 keys ──────────────────────────
-// A persistent, warp-specialised kernel: one CTA per SM walks the work items
-// (row, head, 128-query block) of rows with at most kTcMaxKeys keys.  A row's
-// keys all fit one accumulator, so its softmax is exact in one pass (no
-// running rescale).
-//   warp 0  (TMA): Q and K onto one mbarrier, V onto a second, 64-row boxes,
-//           into three shared-memory stages (loads run up to two items ahead).
+// ── tcgen05 attention for rows of at most 256 keys ──────────────────────────
+// A persistent, warp-specialised kernel: one CTA per SM pulls work items
+// (row, head, 128-query block) of rows with at most MAXK keys from a device
+// counter (dynamic schedule: no SM idles while another still has a queue).
+// A row's keys all fit one accumulator, so its softmax is exact in one pass
+// (no running rescale).
+//   warp 0  (TMA): takes the next item from the counter, publishes it to the
+//           other roles in a shared-memory ring beside its stage (an empty
+//           entry, twice, ends the walk), and loads Q and K onto one
+//           mbarrier, V onto a second, 64-row boxes, into STAGES stages.
 //   warp 1  (MMA): S = Q K^T, four kind::f16 MMAs (K = 16) into the item's
 //           TMEM slot, columns [0, n_pad), n_pad = the row length rounded up
 //           to 16; once the softmax has written P: O = P V, one MMA per
 //           16-key chunk with A = P read from TMEM and B = V straight from its
 //           TMA tile (MN-major, 128-byte swizzle), into the slot's columns
-//           [192, 256).  Each is issued as soon as its inputs are ready
+//           [128, 192).  Each is issued as soon as its inputs are ready
 //           (non-blocking probes of the barriers).
 //   warps 2-5 and 6-9 (softmax, two groups ping-ponging on alternate items,
 //           each with its own 256-column TMEM slot): warp w reads TMEM lanes
 //           32 (w % 4) .. + 31, one thread per query row.  The group zeroes
 //           the V rows past the row's end (other rows' values: 0 * V must
 //           stay 0), reads S in register batches (max; then
-//           2^(s log2(e) / 8 - m) and the sum), writes each 16-key chunk's P
-//           as bf16 pairs into the chunk's own first 8 columns and, after
+//           2^(s log2(e) / 8 - m) and the sum), writes chunk c's P as bf16
+//           pairs into columns [8c, 8c + 8) (S columns already consumed: the
+//           chunks are read in ascending batches before their P is written;
+//           P ends below column 128, where O starts) and, after
 //           O = P V, scales the O row by 1 / sum and stores it (128 B).  While
 //           one group waits for its O, the other runs its softmax.
-// causal != 0 masks keys after the query.  Longer rows are left to the
-// mma.sync kernel; the choice is per row, so a row's result does not depend
-// on its batch.  Every wait is bounded; on a timeout each role stops, the
+// causal != 0 masks keys after the query.  MAXK = 192 keeps three 64 KB
+// stages, MAXK = 256 two 80 KB ones.  Longer rows are left to the mma.sync
+// kernel; the choice is per row, so a row's result does not depend on its
+// batch.  Every wait is bounded; on a timeout each role stops, the
 // TMA and MMA threads wait (bounded) for their copies and MMAs in flight,
 // the error flag is set and TMEM is freed.
 constexpr int kTcQ = 128;         // queries per item
-constexpr int kTcMaxKeys = 192;   // keys per row this kernel takes
 constexpr int kTcSlotCols = 256;  // TMEM columns per slot; two slots
-constexpr int kTcOCol = 192;      // O's first column inside a slot
-constexpr int kTcStages = 3;
+constexpr int kTcOCol = 128;      // O's first column inside a slot
 constexpr int kTcGroupWarps = 4;
 constexpr int kTcThreads = 64 + 2 * 32 * kTcGroupWarps;
-constexpr int kTcStageBytes = (kTcQ + 2 * kTcMaxKeys) * 128;
-constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256;
 constexpr int kTcBatch = 6;  // 16-column chunks per register batch
+template <int MAXK>
+constexpr int tc_stage_bytes() { return (kTcQ + 2 * MAXK) * 128; }
+template <int MAXK, int STAGES>
+constexpr int tc_smem() { return STAGES * tc_stage_bytes<MAXK>() + 1024 + 256 + STAGES * 32; }
 
-// Work item idx -> (row, head, query block); false for items with no work here.
-__device__ __forceinline__ bool tc_item(const int* cu, int heads, int idx, int& b, int& h, int& q0,
-                                        int& start, int& n) {
-  const int bh = idx >> 1;
-  b = bh / heads;
-  h = bh - b * heads;
-  q0 = (idx & 1) * kTcQ;
-  start = cu[b];
-  n = cu[b + 1] - start;
-  return q0 < n && n <= kTcMaxKeys;
-}
+// One published work item (or idx < 0: no more).
+struct TcItem {
+  int idx, start, n, h, q0;
+};
 
+template <int MAXK, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attn_tc_kernel(const int* __restrict__ cu, bf16* __restrict__ ctx, int batch, int heads,
-                   float scale_log2, const __grid_constant__ CUtensorMap tm, int* err, int causal) {
+                   float scale_log2, const __grid_constant__ CUtensorMap tm, int* err, int causal,
+                   unsigned int* work) {
+  constexpr int kTcStages = STAGES, kTcMaxKeys = MAXK;
+  constexpr int kTcStageBytes = tc_stage_bytes<MAXK>();
   const int H = heads * 64;
   const int items = batch * heads * 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -386,6 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t spare = bars + 8u * (3 * kTcStages + 8);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(meta + 8 * 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 24 + 4);
+  volatile TcItem* ring = reinterpret_cast<volatile TcItem*>(meta + 256);  // [STAGES]
 
   if (tid == 0) {
     for (int st = 0; st < kTcStages; ++st) {
@@ -412,22 +417,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ── TMA producer
-      int k = 0;
-      for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
-        int b, h, q0, start, n;
-        if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
+      int k = 0, ends = 0;
+      while (ends < 2) {
         const int st = k % kTcStages;
         const uint32_t ph = (k / kTcStages) & 1;
         if (!mbar_wait(sbar(kSEmpty, st), ph ^ 1u, abort_flag)) break;
+        TcItem it{-1, 0, 0, 0, 0};
+        if (ends == 0) {
+          while (true) {
+            const int idx = static_cast<int>(atomicAdd(work, 1u));
+            if (idx >= items) break;
+            const int bh = idx >> 1, b = bh / heads;
+            const int q0 = (idx & 1) * kTcQ, start = cu[b], n = cu[b + 1] - start;
+            if (q0 < n && n <= kTcMaxKeys) {
+              it = TcItem{idx, start, n, bh - b * heads, q0};
+              break;
+            }
+          }
+        }
+        ring[st].idx = it.idx;
+        ring[st].start = it.start;
+        ring[st].n = it.n;
+        ring[st].h = it.h;
+        ring[st].q0 = it.q0;
+        if (it.idx < 0) {  // published by the barriers' release
+          mbar_arrive(sbar(kLdQK, st));
+          mbar_arrive(sbar(kLdV, st));
+          ++ends;
+          ++k;
+          continue;
+        }
         const uint32_t sQ = stage_of(k), sK = sQ + kTcQ * 128, sV = sK + kTcMaxKeys * 128;
-        const int n_pad = (n + 15) & ~15;
+        const int n_pad = (it.n + 15) & ~15;
         const int kboxes = (n_pad + 63) >> 6;
-        const int qboxes = min(2, (n - q0 + 63) >> 6);
+        const int qboxes = min(2, (it.n - it.q0 + 63) >> 6);
         mbar_arrive_expect_tx(sbar(kLdQK, st), static_cast<uint32_t>(qboxes + kboxes) * kTileBytes);
-        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, h * 64, start + q0 + 64 * i, sbar(kLdQK, st));
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + h * 64, start + 64 * i, sbar(kLdQK, st));
+        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, it.h * 64, it.start + it.q0 + 64 * i, sbar(kLdQK, st));
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + it.h * 64, it.start + 64 * i, sbar(kLdQK, st));
         mbar_arrive_expect_tx(sbar(kLdV, st), static_cast<uint32_t>(kboxes) * kTileBytes);
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + h * 64, start + 64 * i, sbar(kLdV, st));
+        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + it.h * 64, it.start + 64 * i, sbar(kLdV, st));
         ++k;
       }
       if (*abort_flag) {
@@ -442,10 +470,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {  // ── MMA issuer
       // items k with S issued (< ks) and with O = P V issued (< kp); ns[]
-      // remembers the row lengths of the items in flight
+      // remembers the row lengths of the items in flight; an empty ring entry
+      // (once its Q/K barrier has completed) ends the walk
       int ks = 0, kp = 0;
       int ns[4] = {0, 0, 0, 0};
-      int idx_s = blockIdx.x;
       bool more = true, ok = true;
       const uint64_t t_limit = kWaitLimitNs;
       uint64_t t0 = global_timer_ns();
@@ -453,18 +481,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool progress = false;
         // next item whose S can go: its slot free and its Q, K loaded
         if (more && ks - kp < 2) {
-          int b, h, q0, start, n;
-          bool found = false;
-          int idx = idx_s;
-          for (; idx < items; idx += gridDim.x)
-            if (tc_item(cu, heads, idx, b, h, q0, start, n)) { found = true; break; }
-          if (!found) {
-            more = false;
-          } else {
-            idx_s = idx;
-            const int sl = ks & 1, st = ks % kTcStages;
-            if (mbar_test_wait(tbar(kTFree, sl), ((ks >> 1) & 1) ^ 1u) &&
-                mbar_test_wait(sbar(kLdQK, st), (ks / kTcStages) & 1)) {
+          const int sl = ks & 1, st = ks % kTcStages;
+          // one probe of the Q/K barrier, then the ring entry decides: an
+          // empty entry (n = 0) must never reach an MMA (N = 0 is invalid)
+          if (mbar_test_wait(sbar(kLdQK, st), (ks / kTcStages) & 1)) {
+            const int n = ring[st].idx < 0 ? 0 : ring[st].n;
+            if (n <= 0) {
+              more = false;
+            } else if (mbar_test_wait(tbar(kTFree, sl), ((ks >> 1) & 1) ^ 1u)) {
               tc_fence_after();
               const uint32_t sQ = stage_of(ks), sK = sQ + kTcQ * 128;
               const uint32_t idesc = idesc_bf16_f32(kTcQ, (n + 15) & ~15);
@@ -475,7 +499,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               mma_commit(tbar(kSFull, sl));
               ns[ks & 3] = n;
               ++ks;
-              idx_s += gridDim.x;
               progress = true;
             }
           }
@@ -490,7 +513,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int chunks = ((ns[kp & 3] + 15) & ~15) >> 4;
 #pragma unroll 1
           for (int c = 0; c < chunks; ++c)
-            mma_bf16_ta(slot + kTcOCol, slot + 16u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
+            mma_bf16_ta(slot + kTcOCol, slot + 8u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
           mma_commit(tbar(kOFull, sl));
           mma_commit(sbar(kSEmpty, kp % kTcStages));
           ++kp;
@@ -518,20 +541,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quarter = warp & 3;
     const int gtid = tid - 64 - group * 32 * kTcGroupWarps;  // 0 .. 127
     const int row = 32 * quarter + lane;
-    int k = 0;
-    for (int idx = blockIdx.x; idx < items; idx += gridDim.x) {
-      int b, h, q0, start, n;
-      if (!tc_item(cu, heads, idx, b, h, q0, start, n)) continue;
-      const int kk = k++;
-      if ((kk & 1) != group) continue;
+    for (int kk = group;; kk += 2) {
       const int st = kk % kTcStages;
       const uint32_t sph = (kk / kTcStages) & 1, tph = (kk >> 1) & 1;
+      if (!mbar_wait(sbar(kLdV, st), sph, abort_flag)) break;
+      const int idx = ring[st].idx;
+      if (idx < 0) break;  // the walk is over
+      const int start = ring[st].start, n = ring[st].n, h = ring[st].h, q0 = ring[st].q0;
       const uint32_t sV = stage_of(kk) + kTcQ * 128 + kTcMaxKeys * 128;
       const uint32_t trow = tbase + static_cast<uint32_t>(group * kTcSlotCols) +
                             (static_cast<uint32_t>(32 * quarter) << 16);
       const int n_pad = (n + 15) & ~15, chunks = n_pad >> 4;
       // V rows [n, n_pad) -> 0 (whole 128-byte rows, so the swizzle is moot)
-      if (!mbar_wait(sbar(kLdV, st), sph, abort_flag)) break;
       for (int i = gtid; i < (n_pad - n) * 8; i += 32 * kTcGroupWarps) {
         const uint32_t a = sV + static_cast<uint32_t>(n + (i >> 3)) * 128 + (i & 7) * 16;
         asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
@@ -580,7 +601,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 l += p0 + p1;
                 pk[j >> 1] = pack_bf16(p0, p1);
               }
-              tmem_st_32x32b_x8(trow + c, pk);  // the chunk's own, consumed, columns
+              tmem_st_32x32b_x8(trow + (c >> 1), pk);  // consumed S columns [8c', 8c' + 8)
             }
           }
         }
@@ -728,13 +749,49 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
 std::atomic<int> g_attn_tc{0};  // jb_set_attention_tcgen05
 bool attn_tc_enabled() { return g_attn_tc.load(std::memory_order_relaxed) != 0; }
 
+template <int MAXK, int STAGES>
+cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int batch, int heads,
+                      float scale_log2, const CUtensorMap& tm, int* err, int causal,
+                      unsigned int* work) {
+  static const bool attr = cudaFuncSetAttribute(attn_tc_kernel<MAXK, STAGES>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                tc_smem<MAXK, STAGES>()) == cudaSuccess;
+  if (!attr) return cudaErrorInvalidConfiguration;
+  attn_tc_kernel<MAXK, STAGES><<<grid, kTcThreads, tc_smem<MAXK, STAGES>(), s>>>(
+      cu, ctx, batch, heads, scale_log2, tm, err, causal, work);
+  return cudaGetLastError();
+}
+
+// Work counters for callers that pass none (the single-op entry points):
+// one slot per call, round robin over kWorkSlots, so calls that overlap on the
+// GPU get distinct counters unless kWorkSlots of them are in flight at once.
+constexpr int kWorkSlots = 64;
+__device__ unsigned int g_attn_work[kWorkSlots];
+unsigned int* shared_work_counter() {
+  static std::mutex mu;
+  static unsigned int* base[64] = {};
+  static unsigned next = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_work) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    base[dev] = static_cast<unsigned int*>(p);
+  }
+  return base[dev] + (next++ % kWorkSlots);
+}
+
 }  // namespace
 
 void set_attention_tcgen05(bool on) { g_attn_tc.store(on ? 1 : 0, std::memory_order_relaxed); }
 
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
-                             std::string* why, int rows_cap, int* err, int causal) {
+                             std::string* why, int rows_cap, int* err, int causal, int* work) {
   if (batch == 0 || max_len == 0) return cudaSuccess;
   if (batch > 65535 || heads > 65535) {
     if (why) *why = "attention: batch and heads must be <= 65535";
@@ -748,23 +805,29 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
     const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64);
     int skip_le = 0;  // rows the tcgen05 kernel takes
     if (tma && attn_tc_enabled()) {
-      // rows of up to kTcMaxKeys keys: S and P V on tcgen05 (one softmax pass)
-      static bool attr = [] {
-        return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kTcSmem) == cudaSuccess;
-      }();
-      if (attr) {
+      // rows of up to 256 keys: S and P V on tcgen05 (one softmax pass)
+      unsigned int* w = work ? reinterpret_cast<unsigned int*>(work) : shared_work_counter();
+      cudaError_t e = w ? cudaMemsetAsync(w, 0, sizeof(unsigned int), s) : cudaErrorInvalidValue;
+      if (e == cudaSuccess) {
         int dev = 0;
         cudaGetDevice(&dev);
         int sms = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int items = batch * heads * 2;
         const int grid = std::max(1, std::min(items, sms > 0 ? sms : 148));
-        attn_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(cu, static_cast<bf16*>(ctx), batch, heads,
-                                                         scale_log2, tm, err, causal);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess || max_len <= kTcMaxKeys) return e;
-        skip_le = kTcMaxKeys;
+        if (max_len <= 192) {
+          e = launch_tc<192, 3>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
+                                err, causal, w);
+          skip_le = 192;
+        } else {
+          e = launch_tc<256, 2>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
+                                err, causal, w);
+          skip_le = 256;
+        }
+        if (e != cudaSuccess) return e;
+        if (max_len <= skip_le) return cudaSuccess;
+      } else {
+        cudaGetLastError();
       }
     }
     auto kern = tma ? flash_attn_bf16_d64<true> : flash_attn_bf16_d64<false>;

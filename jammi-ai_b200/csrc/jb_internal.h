@@ -83,15 +83,19 @@ struct EmbedArgs {
 };
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
 
-// Rows of <= 192 keys (bf16, head_dim 64, TMA) on the tcgen05 kernel instead
-// of the mma.sync one; process-wide, off by default.
+// Rows of <= 256 keys (bf16, head_dim 64, TMA) on the tcgen05 kernel instead
+// of the mma.sync one; process-wide, off by default.  That kernel takes its
+// work items from a device counter: `work` (one int the caller owns, zeroed
+// on the stream before the launch; the model forwards pass one in their
+// workspace), or, when null, a slot of a small static pool.
 void set_attention_tcgen05(bool on);
 // causal != 0: query i attends to keys j <= i of its row (the OpenCLIP text
 // mask, clip_text.rs:350-362).
 cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtype, int batch,
                              int heads, int head_dim, int max_len, cudaStream_t s,
                              std::string* why,
-                             int rows_cap = 0, int* err = nullptr, int causal = 0);
+                             int rows_cap = 0, int* err = nullptr, int causal = 0,
+                             int* work = nullptr);
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s);

@@ -1086,6 +1086,12 @@ void run_ln(jb_model* m, const void* x, const void* resid, const float* g, const
 }  // namespace
 
 namespace {
+// The attention kernels' work counter: 128 bytes into the workspace's 256-byte
+// `total` slot, whose first int is the packed row count.
+int* attn_work(const Workspace& ws) { return ws.total + 32; }
+}  // namespace
+
+namespace {
 // ModernBert::forward_hidden (modernbert.rs:318-340) over packed rows, cu in
 // ws.cu: embedding norm; per layer x += Wo(attn(rope(Wqkv(attn_norm(x)))))
 // (layer 0 without attn_norm) and x += mlp.Wo(geglu(Wi(mlp_norm(x))));
@@ -1124,7 +1130,7 @@ void* modernbert_forward(jb_model* m, const uint32_t* d_ids, int batch, int max_
     {
       ProfScope ps(m, kProfAttention, s);
       e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s, &why,
-                           Mcap, m->d_err);
+                           Mcap, m->d_err, 0, attn_work(ws));
     }
     if (e != cudaSuccess) {
       if (!why.empty()) fail(JB_ERR_INVALID, why);
@@ -1191,7 +1197,7 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
       {
         ProfScope ps(m, kProfAttention, s);
         e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, H / m->heads, max_seq, s,
-                             &why, Mcap, m->d_err);
+                             &why, Mcap, m->d_err, 0, attn_work(ws));
       }
       if (e != cudaSuccess) {
         if (!why.empty()) fail(JB_ERR_INVALID, why);
@@ -1262,7 +1268,7 @@ void* clip_blocks_forward(jb_model* m, int rows_cap, const int* d_rows, int batc
     {
       ProfScope ps(m, kProfAttention, s);
       e = launch_attention(ws.qkv, ws.cu, ws.ctx, act, batch, m->heads, W / m->heads, max_len, s, &why,
-                           rows_cap, m->d_err, causal);
+                           rows_cap, m->d_err, causal, attn_work(ws));
     }
     if (e != cudaSuccess) {
       if (!why.empty()) fail(JB_ERR_INVALID, why);

@@ -133,6 +133,6 @@ def preprocess_rgb8(images, target: int, mean, std, device="cuda") -> torch.Tens
 
 
 def set_attention_tcgen05(on: bool):
-    """``jb_set_attention_tcgen05``: rows of <= 192 keys on the tcgen05 attention
+    """``jb_set_attention_tcgen05``: rows of <= 256 keys on the tcgen05 attention
     kernel (process-wide; off by default)."""
     lib().jb_set_attention_tcgen05(1 if on else 0)

@@ -148,7 +148,7 @@ def _bert_base(seed):
 @pytest.mark.parametrize("tc_attention", [False, True])
 def test_bert_base_bf16_config(tc_attention):
     """BERT-base, bf16, seq 256, lengths U[32,256] (batch reduced for the oracle);
-    with tc_attention, rows of <= 192 keys take the tcgen05 attention kernel."""
+    with tc_attention, rows of <= 256 keys take the tcgen05 attention kernel."""
     from jammi_b200 import ops
     cfg, w = _bert_base(201)
     rng = np.random.default_rng(202)

@@ -294,10 +294,11 @@ def test_attention_varlen(dev, dtype, heads, d, lens):
     [1, 2, 15, 16, 17, 63, 64, 65, 127, 128, 129, 200, 255, 256],
     [50] * 7,
     [256, 0, 3, 177],
+    [300, 17, 257, 256, 1, 512],
 ])
 @pytest.mark.parametrize("tc", [True, False])
 def test_attention_tma_rows(dev, lens, causal, tc):
-    """The model forwards' TMA kernels: with tc, rows of <= 192 keys on the
+    """The model forwards' TMA kernels: with tc, rows of <= 256 keys on the
     tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma, P through TMEM) and
     longer rows on the mma.sync one in the same call; without, mma.sync only."""
     ops = _ops()
