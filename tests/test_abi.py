@@ -59,3 +59,31 @@ def test_mask_to_lengths_rejects_holes():
     assert list(mask_to_lengths(np.array([[1, 1, 0], [0, 0, 0], [1, 1, 1]]))) == [2, 0, 3]
     with pytest.raises(ValueError):
         mask_to_lengths(np.array([[1, 0, 1]]))
+
+
+def test_ctypes_structs_match_the_header(tmp_path):
+    """The Python mirrors of the header's structs have the C compiler's size
+    and field offsets (a layout drift would silently misread fields)."""
+    import shutil
+    import subprocess
+    from jammi_b200 import _lib
+    from jammi_b200.driver import GenerateOpts, GenerateStats
+    if not shutil.which("gcc"):
+        pytest.skip("no C compiler")
+    src = tmp_path / "sizes.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "jammi_b200.h"\n'
+        "int main(void) {\n"
+        '  printf("%zu %zu %zu %zu %zu\\n", sizeof(jb_model_info),\n'
+        "         offsetof(jb_model_info, weight_bytes), offsetof(jb_model_info, preprocess_std),\n"
+        "         sizeof(jb_generate_opts), sizeof(jb_generate_stats));\n"
+        "  return 0;\n}\n")
+    exe = tmp_path / "sizes"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    want = [ctypes.sizeof(_lib.ModelInfo), _lib.ModelInfo.weight_bytes.offset,
+            _lib.ModelInfo.preprocess_std.offset, ctypes.sizeof(GenerateOpts),
+            ctypes.sizeof(GenerateStats)]
+    assert got == want, (got, want)
