@@ -350,6 +350,25 @@ typedef int (*jb_forward_cb)(void* user, int64_t start, int64_t count, char* msg
 jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, void* user);
 int jb_is_oom_message(const char* msg);
 
+/* ── tokenizer (host) ─────────────────────────────────────────────────────
+ * BERT WordPiece from a model's tokenizer.json, the HuggingFace `tokenizers`
+ * pipeline the reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
+ * tokenizer.rs:21-78): added (special) tokens matched in the raw text,
+ * BertNormalizer, BertPreTokenizer, WordPiece, the [CLS] ... [SEP] template,
+ * truncation to max_length (special ids included).  Other tokenizer.json
+ * components answer JB_ERR_INVALID at load.  Output is the ragged layout of
+ * jb_generate_embeddings: ids of text i at ids[offsets[i] .. offsets[i+1]). */
+typedef struct jb_tokenizer jb_tokenizer;
+jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out);
+void jb_tokenizer_free(jb_tokenizer* tokenizer);
+/* texts: n UTF-8 strings of text_bytes[i] bytes (invalid sequences read as
+ * U+FFFD); max_length <= 0 does not truncate.  offsets [n + 1] is always
+ * filled; ids may be NULL (a size query: offsets[n] ids are needed), else it
+ * holds ids_capacity ids.  Long batches are tokenised on all host cores. */
+jb_status jb_tokenize(const jb_tokenizer* tokenizer, const char* const* texts,
+                      const uint64_t* text_bytes, int64_t n, int max_length, uint32_t* ids,
+                      uint64_t ids_capacity, uint64_t* offsets);
+
 /* ── multi-device embedding generation ────────────────────────────────────
  * The generate_embeddings driver (crates/jammi-ai/src/pipeline/embedding.rs:47-282
  * -> runner.rs:176-241 -> candle.rs:764-856) over one model handle per device:

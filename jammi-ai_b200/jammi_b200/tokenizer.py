@@ -1,0 +1,52 @@
+"""``Tokenizer``: the library's host-side BERT WordPiece tokenizer
+(``jb_tokenizer_*``), the counterpart of the reference's ``TokenizerWrapper``
+(crates/jammi-ai/src/model/tokenizer.rs) for the BERT family's tokenizer.json.
+
+Calling it on a list of texts returns one uint32 id array per text, so it can
+be handed to ``driver.embed_texts`` as the ``tokenize`` callable."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import check, lib
+
+
+class Tokenizer:
+    def __init__(self, tokenizer_json: str, max_length: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().jb_tokenizer_load(str(tokenizer_json).encode(), ctypes.byref(h)))
+        self._h = h
+        self.max_length = int(max_length)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().jb_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode_ragged(self, texts, max_length: int | None = None):
+        """texts -> (ids uint32, offsets uint64 [n + 1]), the layout of
+        ``driver.generate_embeddings``."""
+        enc = [t.encode("utf-8") for t in texts]
+        n = len(enc)
+        ptrs = (ctypes.c_char_p * max(n, 1))(*enc)
+        sizes = np.array([len(e) for e in enc], dtype=np.uint64)
+        offsets = np.zeros(n + 1, dtype=np.uint64)
+        ml = self.max_length if max_length is None else int(max_length)
+        check(lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                                None, 0, offsets.ctypes.data))
+        ids = np.zeros(max(int(offsets[-1]), 1), dtype=np.uint32)
+        check(lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                                ids.ctypes.data, ids.size, offsets.ctypes.data))
+        return ids[: int(offsets[-1])], offsets
+
+    def __call__(self, texts, max_length: int | None = None):
+        ids, offsets = self.encode_ragged(list(texts), max_length)
+        return [ids[offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]

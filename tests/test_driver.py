@@ -202,3 +202,31 @@ def test_stream_tokenises_ahead_in_order(monkeypatch):
         raise RuntimeError("tokenizer failed")
     with pytest.raises(RuntimeError):
         D.embed_texts([M()], ["a", "b"], bad, chunk_rows=1)
+
+
+def test_embed_texts_with_the_library_tokenizer(monkeypatch, tmp_path):
+    """The library's Tokenizer is a tokenize callable for embed_texts."""
+    import numpy as np
+    pytest.importorskip("tokenizers")
+    from test_tokenizer import build
+    from jammi_b200 import Tokenizer
+    from jammi_b200 import driver as D
+    hf, path = build(tmp_path, "tok.json")
+    seen = []
+
+    def fake_generate(models, values, offsets, **kw):
+        seen.append((values.copy(), offsets.copy()))
+        rows = offsets.size - 1
+        return np.zeros((rows, 4), np.float32), np.full((rows + 7) // 8, 0xFF, np.uint8), {"rows": rows}
+
+    monkeypatch.setattr(D, "generate_embeddings", fake_generate)
+
+    class M:
+        class info:
+            hidden = 4
+            output_dim = 4
+    texts = ["hello world", "naïve café", "", "東京"]
+    D.embed_texts([M()], texts, Tokenizer(path), chunk_rows=3)
+    ids = np.concatenate([v for v, _ in seen])
+    want = np.concatenate([np.array(e.ids, np.uint32) for e in hf.encode_batch(texts)])
+    assert np.array_equal(ids, want)
