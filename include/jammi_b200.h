@@ -360,6 +360,14 @@ int jb_is_oom_message(const char* msg);
  * jb_generate_embeddings: ids of text i at ids[offsets[i] .. offsets[i+1]). */
 typedef struct jb_tokenizer jb_tokenizer;
 jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out);
+/* The OpenCLIP text tower's BPE from OpenCLIP's merges file (the
+ * bpe_simple_vocab_16e6.txt.gz shipped with OpenCLIP checkpoints; gzip or
+ * plain text): load_open_clip_bpe (crates/jammi-ai/src/model/clip_bpe.rs:
+ * 52-217) -- byte symbols, "</w>" word ends, the CLIP regex pre-tokeniser, no
+ * normaliser, <|startoftext|> ... <|endoftext|> (ids vocab-2 and vocab-1).
+ * The first 48894 merges are read, as OpenCLIP does; a shorter file gives a
+ * smaller vocabulary with the same layout. */
+jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out);
 void jb_tokenizer_free(jb_tokenizer* tokenizer);
 /* texts: n UTF-8 strings of text_bytes[i] bytes (invalid sequences read as
  * U+FFFD); max_length <= 0 does not truncate.  offsets [n + 1] is always

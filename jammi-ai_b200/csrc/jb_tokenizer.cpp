@@ -26,9 +26,24 @@
 //                  cut.
 // Unicode data (categories, lowercase, canonical decompositions and
 // combining classes) comes from jb_unicode_tables.h.
+//
+// The OpenCLIP text tower's tokenizer is the reference's load_open_clip_bpe
+// (crates/jammi-ai/src/model/clip_bpe.rs:52-217), a `tokenizers` BPE built from
+// OpenCLIP's merges file: vocabulary = the 256 byte symbols of the GPT-2 /
+// CLIP byte-to-printable-code-point table, the same with the "</w>"
+// end-of-word suffix, each merge joined, then <|startoftext|> and
+// <|endoftext|>; no normaliser; the CLIP regex as an isolating pre-tokeniser
+// (the special-token literals, the contractions 's 't 're 've 'm 'll 'd,
+// letter runs, single digits, runs of other non-space characters; the spans
+// between matches are pre-tokens too); per pre-token, each character a symbol
+// (the last one with "</w>"), characters outside the vocabulary dropped (the
+// model has no unknown token), then the lowest-ranked adjacent pair merged
+// first (leftmost on ties) until none applies; <|startoftext|> ... <|endoftext|>
+// around the sequence.
 #include <algorithm>
 #include <cstring>
 #include <fstream>
+#include <zlib.h>
 #include <memory>
 #include <sstream>
 #include <string>
@@ -41,6 +56,9 @@
 #include "jb_unicode_tables.h"
 
 struct jb_tokenizer {
+  int kind = 0;  // 0: BERT WordPiece, 1: OpenCLIP BPE
+  // BPE: (left id, right id) -> (rank, merged id)
+  std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;
   bool clean_text = true, handle_chinese = true, strip_accents = true, lowercase = true;
   std::unordered_map<std::string, uint32_t> vocab;
   uint32_t unk_id = 0;
@@ -259,8 +277,84 @@ void wordpiece(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::ve
   ids.insert(ids.end(), pieces.begin(), pieces.end());
 }
 
+bool is_letter(uint32_t c) { return in_table(uni::kLetter, c); }
+bool is_number(uint32_t c) { return in_table(uni::kNumber, c); }
+
+// Length (in code points) of the CLIP pre-tokeniser's match at position i,
+// 0 if no alternative matches there; alternatives are tried in the regex's
+// order, the first that matches wins.
+size_t clip_match(const std::vector<uint32_t>& c, size_t i) {
+  static const char* const kLiterals[] = {"<|startoftext|>", "<|endoftext|>", "'s", "'t", "'re",
+                                          "'ve", "'m", "'ll", "'d"};
+  for (const char* lit : kLiterals) {
+    const size_t len = std::strlen(lit);
+    if (i + len > c.size()) continue;
+    size_t k = 0;
+    while (k < len && c[i + k] == static_cast<unsigned char>(lit[k])) ++k;
+    if (k == len) return len;
+  }
+  if (is_letter(c[i])) {
+    size_t j = i + 1;
+    while (j < c.size() && is_letter(c[j])) ++j;
+    return j - i;
+  }
+  if (is_number(c[i])) return 1;
+  if (is_whitespace(c[i])) return 0;
+  size_t j = i + 1;
+  while (j < c.size() && !is_whitespace(c[j]) && !is_letter(c[j]) && !is_number(c[j])) ++j;
+  return j - i;
+}
+
+void bpe_word(const jb_tokenizer& t, const std::vector<uint32_t>& c, size_t b, size_t e,
+              std::vector<uint32_t>& ids) {
+  std::vector<uint32_t> sym;
+  std::string s;
+  for (size_t k = b; k < e; ++k) {
+    s.clear();
+    append_utf8(c[k], s);
+    if (k + 1 == e) s += "</w>";
+    auto it = t.vocab.find(s);
+    if (it != t.vocab.end()) sym.push_back(it->second);  // unknown characters are dropped
+  }
+  while (sym.size() > 1) {
+    uint32_t best_rank = UINT32_MAX, best_id = 0;
+    size_t best_pos = 0;
+    for (size_t k = 0; k + 1 < sym.size(); ++k) {
+      auto it = t.merges.find((static_cast<uint64_t>(sym[k]) << 32) | sym[k + 1]);
+      if (it != t.merges.end() && it->second.first < best_rank) {
+        best_rank = it->second.first;
+        best_id = it->second.second;
+        best_pos = k;
+      }
+    }
+    if (best_rank == UINT32_MAX) break;
+    sym[best_pos] = best_id;
+    sym.erase(sym.begin() + best_pos + 1);
+  }
+  ids.insert(ids.end(), sym.begin(), sym.end());
+}
+
+void encode_clip(const jb_tokenizer& t, const char* s, size_t n, std::vector<uint32_t>& ids) {
+  std::vector<uint32_t> c;
+  decode_utf8(s, n, c);
+  size_t seg = 0;
+  for (size_t i = 0; i < c.size();) {
+    const size_t len = clip_match(c, i);
+    if (len == 0) {
+      ++i;
+      continue;
+    }
+    if (seg < i) bpe_word(t, c, seg, i, ids);  // the span between matches
+    bpe_word(t, c, i, i + len, ids);
+    i += len;
+    seg = i;
+  }
+  if (seg < c.size()) bpe_word(t, c, seg, c.size(), ids);
+}
+
 // One segment of text between added tokens: normalise, pre-tokenise, WordPiece.
 void encode_segment(const jb_tokenizer& t, const char* s, size_t n, std::vector<uint32_t>& ids) {
+  if (t.kind == 1) return encode_clip(t, s, n, ids);
   std::vector<uint32_t> cps;
   decode_utf8(s, n, cps);
   normalize(t, cps);
@@ -399,10 +493,98 @@ jb_tokenizer* load(const char* path) {
   return t.release();
 }
 
+// The GPT-2 / CLIP byte-to-printable-code-point table: bytes 33-126, 161-172
+// and 174-255 map to themselves, the other 68 bytes, in ascending order, to
+// 256, 257, ...
+std::vector<uint32_t> byte_symbols() {
+  std::vector<uint32_t> out(256);
+  uint32_t extra = 0;
+  for (uint32_t b = 0; b < 256; ++b) {
+    const bool direct = (b >= 33 && b <= 126) || (b >= 161 && b <= 172) || (b >= 174 && b <= 255);
+    out[b] = direct ? b : 256 + extra++;
+  }
+  return out;
+}
+
+std::string read_maybe_gzip(const char* path) {
+  gzFile f = gzopen(path, "rb");  // reads plain files unchanged
+  if (!f) fail(JB_ERR_IO, std::string("cannot open ") + path);
+  std::string data;
+  char buf[1 << 16];
+  int n;
+  while ((n = gzread(f, buf, sizeof(buf))) > 0) data.append(buf, static_cast<size_t>(n));
+  const bool bad = n < 0;
+  gzclose(f);
+  if (bad) fail(JB_ERR_IO, std::string("cannot decompress ") + path);
+  return data;
+}
+
+jb_tokenizer* load_clip(const char* path) {
+  // OpenCLIP's vocabulary: 49408 = 256 + 256 + 48894 merges + 2 specials
+  constexpr size_t kMaxMerges = 49408 - 256 - 2 - 256;
+  const std::string text = read_maybe_gzip(path);
+  std::vector<std::pair<std::string, std::string>> merges;
+  size_t line = 0;
+  for (size_t pos = 0; pos <= text.size() && merges.size() < kMaxMerges;) {
+    size_t nl = text.find('\n', pos);
+    if (nl == std::string::npos) nl = text.size();
+    if (line++ > 0) {  // line 0 is a header
+      std::istringstream ls(text.substr(pos, nl - pos));
+      std::string a, b;
+      if (ls >> a >> b) merges.emplace_back(a, b);
+    }
+    pos = nl + 1;
+  }
+  if (merges.empty()) fail(JB_ERR_IO, std::string("no BPE merges in ") + path);
+  std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
+  t->kind = 1;
+  const std::vector<uint32_t> bytes = byte_symbols();
+  std::vector<std::string> vocab;
+  for (uint32_t c : bytes) {
+    std::string s;
+    append_utf8(c, s);
+    vocab.push_back(s);
+  }
+  for (uint32_t c : bytes) {
+    std::string s;
+    append_utf8(c, s);
+    vocab.push_back(s + "</w>");
+  }
+  for (const auto& m : merges) vocab.push_back(m.first + m.second);
+  vocab.push_back("<|startoftext|>");
+  vocab.push_back("<|endoftext|>");
+  for (size_t i = 0; i < vocab.size(); ++i) t->vocab[vocab[i]] = static_cast<uint32_t>(i);
+  for (size_t r = 0; r < merges.size(); ++r) {
+    auto a = t->vocab.find(merges[r].first), b = t->vocab.find(merges[r].second);
+    auto ab = t->vocab.find(merges[r].first + merges[r].second);
+    if (a == t->vocab.end() || b == t->vocab.end() || ab == t->vocab.end())
+      fail(JB_ERR_IO, "BPE merge " + std::to_string(r + 1) + " names a symbol not in the vocabulary");
+    t->merges[(static_cast<uint64_t>(a->second) << 32) | b->second] =
+        {static_cast<uint32_t>(r), ab->second};
+  }
+  t->before.push_back(static_cast<uint32_t>(vocab.size() - 2));
+  t->after.push_back(static_cast<uint32_t>(vocab.size() - 1));
+  return t.release();
+}
+
 }  // namespace
 }  // namespace jb
 
 extern "C" {
+
+jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out) {
+  if (!out) return jb::record_error(JB_ERR_INVALID, "null output handle");
+  *out = nullptr;
+  try {
+    if (!merges_path) jb::fail(JB_ERR_INVALID, "null path");
+    *out = jb::load_clip(merges_path);
+    return JB_OK;
+  } catch (const jb::Error& e) {
+    return jb::record_error(e.status, e.msg);
+  } catch (const std::exception& e) {
+    return jb::record_error(JB_ERR_INVALID, e.what());
+  }
+}
 
 jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out) {
   if (!out) return jb::record_error(JB_ERR_INVALID, "null output handle");

@@ -1,4 +1,4 @@
-"""``Tokenizer``: the library's host-side BERT WordPiece tokenizer
+"""``Tokenizer``: the library's host-side tokenizers (BERT WordPiece, OpenCLIP BPE)
 (``jb_tokenizer_*``), the counterpart of the reference's ``TokenizerWrapper``
 (crates/jammi-ai/src/model/tokenizer.rs) for the BERT family's tokenizer.json.
 
@@ -14,11 +14,22 @@ from ._lib import check, lib
 
 
 class Tokenizer:
-    def __init__(self, tokenizer_json: str, max_length: int = 0):
-        h = ctypes.c_void_p()
-        check(lib().jb_tokenizer_load(str(tokenizer_json).encode(), ctypes.byref(h)))
-        self._h = h
+    """``Tokenizer(tokenizer_json)``: BERT WordPiece; ``Tokenizer.clip_bpe(path)``:
+    the OpenCLIP text tower's BPE from its merges file."""
+
+    def __init__(self, tokenizer_json: str | None = None, max_length: int = 0, _handle=None):
+        if _handle is None:
+            h = ctypes.c_void_p()
+            check(lib().jb_tokenizer_load(str(tokenizer_json).encode(), ctypes.byref(h)))
+            _handle = h
+        self._h = _handle
         self.max_length = int(max_length)
+
+    @classmethod
+    def clip_bpe(cls, merges_path: str, max_length: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().jb_tokenizer_load_clip_bpe(str(merges_path).encode(), ctypes.byref(h)))
+        return cls(max_length=max_length, _handle=h)
 
     def close(self):
         if getattr(self, "_h", None):
