@@ -351,13 +351,19 @@ jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, vo
 int jb_is_oom_message(const char* msg);
 
 /* ── tokenizer (host) ─────────────────────────────────────────────────────
- * BERT WordPiece from a model's tokenizer.json, the HuggingFace `tokenizers`
- * pipeline the reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
- * tokenizer.rs:21-78): added (special) tokens matched in the raw text,
- * BertNormalizer, BertPreTokenizer, WordPiece, the [CLS] ... [SEP] template,
- * truncation to max_length (special ids included).  Other tokenizer.json
- * components answer JB_ERR_INVALID at load.  Output is the ragged layout of
- * jb_generate_embeddings: ids of text i at ids[offsets[i] .. offsets[i+1]). */
+ * A model's tokenizer.json through the HuggingFace `tokenizers` pipeline the
+ * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
+ * tokenizer.rs:21-78): added tokens (normalized / lstrip / rstrip /
+ * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase (and
+ * Sequences), pre-tokenisers BertPreTokenizer and ByteLevel, models WordPiece
+ * and BPE (byte-level or character-level: unknown token, fuse_unk,
+ * byte_fallback, subword prefix / suffix, ignore_merges), post-processors
+ * TemplateProcessing, BertProcessing, RobertaProcessing, ByteLevel (and
+ * Sequences), truncation to max_length (special ids included) or else the
+ * file's own.  That covers the BERT, DistilBERT and ModernBERT families;
+ * other components (Unigram, Metaspace, NFKC, ...) answer JB_ERR_INVALID at
+ * load.  Output is the ragged layout of jb_generate_embeddings: ids of text i
+ * at ids[offsets[i] .. offsets[i+1]). */
 typedef struct jb_tokenizer jb_tokenizer;
 jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out);
 /* The OpenCLIP text tower's BPE from OpenCLIP's merges file (the
@@ -370,7 +376,8 @@ jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out)
 jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out);
 void jb_tokenizer_free(jb_tokenizer* tokenizer);
 /* texts: n UTF-8 strings of text_bytes[i] bytes (invalid sequences read as
- * U+FFFD); max_length <= 0 does not truncate.  offsets [n + 1] is always
+ * U+FFFD); max_length <= 0 applies the tokenizer.json's own truncation, if
+ * any (with its direction), else none.  offsets [n + 1] is always
  * filled; ids may be NULL (a size query: offsets[n] ids are needed), else it
  * holds ids_capacity ids.  Long batches are tokenised on all host cores. */
 jb_status jb_tokenize(const jb_tokenizer* tokenizer, const char* const* texts,

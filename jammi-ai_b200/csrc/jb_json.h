@@ -72,13 +72,25 @@ struct Json {
             if (i + 4 > s.size()) throw std::runtime_error("json: bad \\u escape");
             unsigned cp = std::stoul(s.substr(i, 4), nullptr, 16);
             i += 4;
+            if (cp >= 0xD800 && cp < 0xDC00 && i + 6 <= s.size() && s[i] == '\\' && s[i + 1] == 'u') {
+              const unsigned lo = std::stoul(s.substr(i + 2, 4), nullptr, 16);
+              if (lo >= 0xDC00 && lo < 0xE000) {  // surrogate pair
+                cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
+                i += 6;
+              }
+            }
             if (cp < 0x80) {
               out += static_cast<char>(cp);
             } else if (cp < 0x800) {
               out += static_cast<char>(0xC0 | (cp >> 6));
               out += static_cast<char>(0x80 | (cp & 0x3F));
-            } else {
+            } else if (cp < 0x10000) {
               out += static_cast<char>(0xE0 | (cp >> 12));
+              out += static_cast<char>(0x80 | ((cp >> 6) & 0x3F));
+              out += static_cast<char>(0x80 | (cp & 0x3F));
+            } else {
+              out += static_cast<char>(0xF0 | (cp >> 18));
+              out += static_cast<char>(0x80 | ((cp >> 12) & 0x3F));
               out += static_cast<char>(0x80 | ((cp >> 6) & 0x3F));
               out += static_cast<char>(0x80 | (cp & 0x3F));
             }

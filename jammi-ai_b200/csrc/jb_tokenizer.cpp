@@ -1,49 +1,65 @@
-// BERT WordPiece tokenizer on the host: texts -> token ids in the ragged
-// layout jb_generate_embeddings takes, so a caller goes from text to
-// embeddings without another runtime.
+// Host tokenizers: texts -> token ids in the ragged layout
+// jb_generate_embeddings takes, so a caller goes from text to embeddings
+// without another runtime.
 //
 // The reference tokenises with the HuggingFace `tokenizers` crate from a
-// model's tokenizer.json (TokenizerWrapper, crates/jammi-ai/src/model/
-// tokenizer.rs:21-78; encode_batch with add_special_tokens and optional
-// truncation).  This restates that crate's pipeline for the BERT family's
-// tokenizer.json layout:
-//   added tokens   special tokens ([CLS], [SEP], [MASK], ...) are matched in
-//                  the raw text first, leftmost, longest at a position, and
-//                  become their own ids;
-//   BertNormalizer clean_text (drop NUL, U+FFFD and category C* except
-//                  \t \n \r; whitespace -> ' '), handle_chinese_chars
-//                  (spaces around CJK ideographs), strip_accents (NFD, then
-//                  drop category Mn; on by default when lowercase is), then
-//                  lowercase (one code point at a time);
-//   BertPreTokenizer split on White_Space, each punctuation character
-//                  (ASCII punctuation or category P*) a word of its own;
-//   WordPiece      greedy longest-match-first per word, continuation pieces
-//                  prefixed ("##"), a word longer than max_input_chars_per_word
-//                  or with no full cover -> the unknown token;
-//   post-processor TemplateProcessing "[CLS] $A [SEP]" or BertProcessing:
-//                  the special ids around the sequence;
-//   truncation     max_length counts the special ids; the sequence's tail is
-//                  cut.
-// Unicode data (categories, lowercase, canonical decompositions and
-// combining classes) comes from jb_unicode_tables.h.
-//
-// The OpenCLIP text tower's tokenizer is the reference's load_open_clip_bpe
-// (crates/jammi-ai/src/model/clip_bpe.rs:52-217), a `tokenizers` BPE built from
-// OpenCLIP's merges file: vocabulary = the 256 byte symbols of the GPT-2 /
-// CLIP byte-to-printable-code-point table, the same with the "</w>"
-// end-of-word suffix, each merge joined, then <|startoftext|> and
-// <|endoftext|>; no normaliser; the CLIP regex as an isolating pre-tokeniser
-// (the special-token literals, the contractions 's 't 're 've 'm 'll 'd,
-// letter runs, single digits, runs of other non-space characters; the spans
-// between matches are pre-tokens too); per pre-token, each character a symbol
-// (the last one with "</w>"), characters outside the vocabulary dropped (the
-// model has no unknown token), then the lowest-ranked adjacent pair merged
-// first (leftmost on ties) until none applies; <|startoftext|> ... <|endoftext|>
-// around the sequence.
+// model's tokenizer.json, any architecture (TokenizerWrapper, crates/jammi-ai/
+// src/model/tokenizer.rs:21-78; encode_batch with add_special_tokens and
+// optional truncation), or from OpenCLIP's merges file (load_open_clip_bpe,
+// crates/jammi-ai/src/model/clip_bpe.rs:52-217).  This restates that crate's
+// pipeline for the tokenizer.json components the encoder families use:
+//   added tokens   matched leftmost-longest, first those flagged
+//                  normalized=false in the raw text, then those flagged
+//                  normalized=true in each normalised piece between them;
+//                  lstrip / rstrip swallow the whitespace beside a match,
+//                  single_word rejects a match inside a word;
+//   normaliser     BertNormalizer: clean_text (drop NUL, U+FFFD and
+//                  category C* except \t \n \r; whitespace -> ' '),
+//                  handle_chinese_chars (spaces around CJK ideographs),
+//                  strip_accents (NFD, then drop category Mn; on by default
+//                  when lowercase is), lowercase (one code point at a time);
+//                  NFC, NFD, Lowercase, and Sequences of these;
+//   pre-tokeniser  BertPreTokenizer: split on White_Space, each punctuation
+//                  character (ASCII punctuation or category P*) a word of its
+//                  own; ByteLevel: an optional leading space (add_prefix_space,
+//                  per piece), the GPT-2 regex ('s 't 're 've 'm 'll 'd,
+//                  ' ?' + letters / numbers / other, whitespace runs that
+//                  leave their last space to the next word), each word's
+//                  UTF-8 bytes mapped to the byte-symbol alphabet below;
+//                  OpenCLIP's regex (the special-token literals, the
+//                  contractions, letter runs, single digits, runs of other
+//                  non-space characters; the spans between matches are words
+//                  too);
+//   model          WordPiece: greedy longest-match-first per word,
+//                  continuation pieces prefixed ("##"), a word longer than
+//                  max_input_chars_per_word or with no full cover -> the
+//                  unknown token.  BPE: each character a symbol (continuing
+//                  prefix on all but the first, end-of-word suffix on the
+//                  last), a character outside the vocabulary -> its
+//                  <0xXX> byte tokens (byte_fallback), else the unknown token
+//                  (consecutive ones fused with fuse_unk), else dropped; then
+//                  the lowest-ranked adjacent pair merged first (leftmost on
+//                  ties) until none applies; ignore_merges takes a word found
+//                  whole in the vocabulary as one token;
+//   post-processor TemplateProcessing, BertProcessing, RobertaProcessing,
+//                  ByteLevel (ids unchanged) and Sequences of these: special
+//                  ids around the sequence;
+//   truncation     max_length counts the special ids and cuts the sequence's
+//                  tail; without one, tokenizer.json's own truncation (with
+//                  its direction) applies.
+// OpenCLIP's merges file becomes the same structure: vocabulary = the 256
+// byte symbols, the same with the "</w>" end-of-word suffix, each merge
+// joined, then <|startoftext|> and <|endoftext|>; no normaliser; the OpenCLIP
+// regex; BPE with "</w>" and no unknown token; <|startoftext|> ...
+// <|endoftext|> around the sequence.
+// Unicode data (categories, lowercase, canonical decompositions, combining
+// classes, NFC composites, word characters) comes from jb_unicode_tables.h.
+
 #include <algorithm>
+#include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <fstream>
-#include <zlib.h>
 #include <memory>
 #include <sstream>
 #include <string>
@@ -51,21 +67,63 @@
 #include <unordered_map>
 #include <vector>
 
+#include <zlib.h>
+
 #include "jb_json.h"
 #include "jb_model.h"
 #include "jb_unicode_tables.h"
 
+namespace jb {
+namespace {
+
+struct AddedToken {
+  std::string content;
+  uint32_t id = 0;
+  bool lstrip = false, rstrip = false, single_word = false;
+};
+
+// Added tokens indexed by first byte, longest first within a byte, so a
+// position's leftmost-longest match is the first candidate that matches.
+struct AddedSet {
+  std::vector<AddedToken> toks;
+  std::vector<std::vector<uint32_t>> by_first = std::vector<std::vector<uint32_t>>(256);
+  void add(const AddedToken& t) {
+    toks.push_back(t);
+    auto& v = by_first[static_cast<unsigned char>(t.content[0])];
+    v.push_back(static_cast<uint32_t>(toks.size() - 1));
+    std::stable_sort(v.begin(), v.end(), [this](uint32_t a, uint32_t b) {
+      return toks[a].content.size() > toks[b].content.size();
+    });
+  }
+};
+
+enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower };
+enum PreTok { kPreNone, kPreBert, kPreByteLevel, kPreClip };
+
+}  // namespace
+}  // namespace jb
+
 struct jb_tokenizer {
-  int kind = 0;  // 0: BERT WordPiece, 1: OpenCLIP BPE
-  // BPE: (left id, right id) -> (rank, merged id)
-  std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;
+  bool wordpiece = true;  // else BPE
+  // normaliser: applied in order
+  std::vector<int> norm;
   bool clean_text = true, handle_chinese = true, strip_accents = true, lowercase = true;
+  int pre = jb::kPreBert;
+  bool add_prefix_space = false, use_regex = true;
   std::unordered_map<std::string, uint32_t> vocab;
+  bool has_unk = false;
   uint32_t unk_id = 0;
+  // WordPiece
   std::string prefix = "##";
   int max_chars = 100;
+  // BPE: (left id, right id) -> (rank, merged id)
+  std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;
+  std::string bpe_prefix, bpe_suffix;
+  bool fuse_unk = false, byte_fallback = false, ignore_merges = false;
   std::vector<uint32_t> before, after;  // special ids around the sequence
-  std::vector<std::pair<std::string, uint32_t>> added;  // matched in the raw text
+  jb::AddedSet raw_added, norm_added;
+  int file_max_length = 0;
+  bool file_trunc_left = false;
 };
 
 namespace jb {
@@ -103,7 +161,7 @@ uint8_t ccc(uint32_t cp) {
   return (it != uni::kCcc + n && it->cp == cp) ? it->ccc : 0;
 }
 
-// The White_Space property.
+// The White_Space property (also the regex \s of both pre-tokenisers).
 bool is_whitespace(uint32_t c) {
   return (c >= 0x9 && c <= 0xD) || c == 0x20 || c == 0x85 || c == 0xA0 || c == 0x1680 ||
          (c >= 0x2000 && c <= 0x200A) || c == 0x2028 || c == 0x2029 || c == 0x202F ||
@@ -124,6 +182,9 @@ bool is_cjk(uint32_t c) {
          (c >= 0x2B740 && c <= 0x2B81F) || (c >= 0x2B920 && c <= 0x2CEAF) ||
          (c >= 0xF900 && c <= 0xFAFF) || (c >= 0x2F800 && c <= 0x2FA1F);
 }
+bool is_letter(uint32_t c) { return in_table(uni::kLetter, c); }
+bool is_number(uint32_t c) { return in_table(uni::kNumber, c); }
+bool is_word_char(uint32_t c) { return in_table(uni::kWord, c); }
 
 // UTF-8 -> code points; an invalid byte sequence decodes to U+FFFD.
 void decode_utf8(const char* s, size_t n, std::vector<uint32_t>& out) {
@@ -170,6 +231,27 @@ void append_utf8(uint32_t c, std::string& s) {
     s.push_back(static_cast<char>(0x80 | (c & 0x3F)));
   }
 }
+std::string to_utf8(const std::vector<uint32_t>& cps) {
+  std::string s;
+  for (uint32_t c : cps) append_utf8(c, s);
+  return s;
+}
+
+// The GPT-2 / CLIP byte-to-printable-code-point table: bytes 33-126, 161-172
+// and 174-255 map to themselves, the other 68 bytes, in ascending order, to
+// 256, 257, ...
+const std::vector<uint32_t>& byte_symbols() {
+  static const std::vector<uint32_t> table = [] {
+    std::vector<uint32_t> out(256);
+    uint32_t extra = 0;
+    for (uint32_t b = 0; b < 256; ++b) {
+      const bool direct = (b >= 33 && b <= 126) || (b >= 161 && b <= 172) || (b >= 174 && b <= 255);
+      out[b] = direct ? b : 256 + extra++;
+    }
+    return out;
+  }();
+  return table;
+}
 
 // Canonical decomposition (NFD): full decompositions from the table, Hangul
 // syllables by the Unicode algorithm, then the canonical ordering of each run
@@ -201,7 +283,59 @@ void nfd(const std::vector<uint32_t>& in, std::vector<uint32_t>& out) {
   }
 }
 
-void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
+// The primary composite of (a, b), 0 if none: Hangul L+V and LV+T by the
+// Unicode algorithm, the rest from the table.
+uint32_t compose_pair(uint32_t a, uint32_t b) {
+  if (a >= 0x1100 && a < 0x1100 + 19 && b >= 0x1161 && b < 0x1161 + 21)
+    return 0xAC00 + ((a - 0x1100) * 21 + (b - 0x1161)) * 28;
+  if (a >= 0xAC00 && a < 0xAC00 + 11172 && (a - 0xAC00) % 28 == 0 && b > 0x11A7 && b < 0x11A7 + 28)
+    return a + (b - 0x11A7);
+  const size_t n = sizeof(uni::kCompose) / sizeof(uni::kCompose[0]);
+  const uni::ComposeEntry* it = std::lower_bound(
+      uni::kCompose, uni::kCompose + n, std::make_pair(a, b),
+      [](const uni::ComposeEntry& e, const std::pair<uint32_t, uint32_t>& k) {
+        return e.first < k.first || (e.first == k.first && e.second < k.second);
+      });
+  return (it != uni::kCompose + n && it->first == a && it->second == b) ? it->composite : 0;
+}
+
+// NFC: NFD, then the canonical composition algorithm -- each character joins
+// the last starter unless a character between them has combining class 0 or
+// a class >= its own (blocked).
+void nfc(const std::vector<uint32_t>& in, std::vector<uint32_t>& out) {
+  std::vector<uint32_t> d;
+  nfd(in, d);
+  out.clear();
+  long starter = -1;
+  for (uint32_t c : d) {
+    const uint8_t cc = ccc(c);
+    if (starter >= 0) {
+      const bool adjacent = static_cast<size_t>(starter) + 1 == out.size();
+      const uint8_t last = adjacent ? 0 : ccc(out.back());
+      if (adjacent || (last != 0 && last < cc)) {
+        if (const uint32_t comp = compose_pair(out[starter], c)) {
+          out[starter] = comp;
+          continue;
+        }
+      }
+    }
+    if (cc == 0) starter = static_cast<long>(out.size());
+    out.push_back(c);
+  }
+}
+
+void lowercase_cps(std::vector<uint32_t>& cps) {
+  std::vector<uint32_t> tmp;
+  for (uint32_t c : cps) {
+    if (const uni::SeqEntry* e = find_seq(uni::kLower, c))
+      tmp.insert(tmp.end(), uni::kLower_seq + e->off, uni::kLower_seq + e->off + e->n);
+    else
+      tmp.push_back(c);
+  }
+  cps.swap(tmp);
+}
+
+void bert_normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
   std::vector<uint32_t> tmp;
   if (t.clean_text) {
     tmp.clear();
@@ -230,17 +364,22 @@ void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
     for (uint32_t c : tmp)
       if (!in_table(uni::kMarkNonspacing, c)) cps.push_back(c);
   }
-  if (t.lowercase) {
-    tmp.clear();
-    for (uint32_t c : cps) {
-      if (const uni::SeqEntry* e = find_seq(uni::kLower, c))
-        tmp.insert(tmp.end(), uni::kLower_seq + e->off, uni::kLower_seq + e->off + e->n);
-      else
-        tmp.push_back(c);
+  if (t.lowercase) lowercase_cps(cps);
+}
+
+void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
+  std::vector<uint32_t> tmp;
+  for (int op : t.norm) {
+    switch (op) {
+      case kNormBert: bert_normalize(t, cps); break;
+      case kNormNfc: nfc(cps, tmp); cps.swap(tmp); break;
+      case kNormNfd: nfd(cps, tmp); cps.swap(tmp); break;
+      case kNormLower: lowercase_cps(cps); break;
     }
-    cps.swap(tmp);
   }
 }
+
+// ---- models -----------------------------------------------------------------
 
 void wordpiece(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
   if (word.empty()) return;
@@ -277,12 +416,81 @@ void wordpiece(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::ve
   ids.insert(ids.end(), pieces.begin(), pieces.end());
 }
 
-bool is_letter(uint32_t c) { return in_table(uni::kLetter, c); }
-bool is_number(uint32_t c) { return in_table(uni::kNumber, c); }
+void bpe(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
+  if (word.empty()) return;
+  if (t.ignore_merges) {
+    auto it = t.vocab.find(to_utf8(word));
+    if (it != t.vocab.end()) {
+      ids.push_back(it->second);
+      return;
+    }
+  }
+  std::vector<uint32_t> sym;
+  bool unk_pending = false;
+  std::string s;
+  for (size_t k = 0; k < word.size(); ++k) {
+    s.clear();
+    if (k > 0) s = t.bpe_prefix;
+    append_utf8(word[k], s);
+    if (k + 1 == word.size()) s += t.bpe_suffix;
+    auto it = t.vocab.find(s);
+    if (it != t.vocab.end()) {
+      if (unk_pending) sym.push_back(t.unk_id);
+      unk_pending = false;
+      sym.push_back(it->second);
+      continue;
+    }
+    if (t.byte_fallback) {
+      std::vector<uint32_t> bytes;
+      char code[8];
+      for (unsigned char b : s) {
+        std::snprintf(code, sizeof(code), "<0x%02X>", b);
+        auto bt = t.vocab.find(code);
+        if (bt == t.vocab.end()) break;
+        bytes.push_back(bt->second);
+      }
+      if (bytes.size() == s.size()) {  // a pending unknown token stays pending
+        sym.insert(sym.end(), bytes.begin(), bytes.end());
+        continue;
+      }
+    }
+    if (t.has_unk) {
+      if (unk_pending && !t.fuse_unk) sym.push_back(t.unk_id);
+      unk_pending = true;
+    }
+    // no unknown token: the character is dropped
+  }
+  if (unk_pending) sym.push_back(t.unk_id);
+  while (sym.size() > 1) {
+    uint32_t best_rank = UINT32_MAX, best_id = 0;
+    size_t best_pos = 0;
+    for (size_t k = 0; k + 1 < sym.size(); ++k) {
+      auto it = t.merges.find((static_cast<uint64_t>(sym[k]) << 32) | sym[k + 1]);
+      if (it != t.merges.end() && it->second.first < best_rank) {
+        best_rank = it->second.first;
+        best_id = it->second.second;
+        best_pos = k;
+      }
+    }
+    if (best_rank == UINT32_MAX) break;
+    sym[best_pos] = best_id;
+    sym.erase(sym.begin() + best_pos + 1);
+  }
+  ids.insert(ids.end(), sym.begin(), sym.end());
+}
 
-// Length (in code points) of the CLIP pre-tokeniser's match at position i,
-// 0 if no alternative matches there; alternatives are tried in the regex's
-// order, the first that matches wins.
+void model(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
+  if (t.wordpiece)
+    wordpiece(t, word, ids);
+  else
+    bpe(t, word, ids);
+}
+
+// ---- pre-tokenisers ---------------------------------------------------------
+
+// Length (in code points) of OpenCLIP's regex match at position i, 0 if no
+// alternative matches there (whitespace); alternatives are tried in the
+// regex's order, the first that matches wins.
 size_t clip_match(const std::vector<uint32_t>& c, size_t i) {
   static const char* const kLiterals[] = {"<|startoftext|>", "<|endoftext|>", "'s", "'t", "'re",
                                           "'ve", "'m", "'ll", "'d"};
@@ -305,102 +513,197 @@ size_t clip_match(const std::vector<uint32_t>& c, size_t i) {
   return j - i;
 }
 
-void bpe_word(const jb_tokenizer& t, const std::vector<uint32_t>& c, size_t b, size_t e,
-              std::vector<uint32_t>& ids) {
-  std::vector<uint32_t> sym;
-  std::string s;
-  for (size_t k = b; k < e; ++k) {
-    s.clear();
-    append_utf8(c[k], s);
-    if (k + 1 == e) s += "</w>";
-    auto it = t.vocab.find(s);
-    if (it != t.vocab.end()) sym.push_back(it->second);  // unknown characters are dropped
+// Length of the GPT-2 regex's match at position i:
+// 's|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+
+size_t gpt2_match(const std::vector<uint32_t>& c, size_t i) {
+  const size_t n = c.size();
+  if (c[i] == '\'' && i + 1 < n) {
+    const uint32_t a = c[i + 1], b = i + 2 < n ? c[i + 2] : 0;
+    if (a == 's' || a == 't' || a == 'm' || a == 'd') return 2;
+    if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l')) return 3;
   }
-  while (sym.size() > 1) {
-    uint32_t best_rank = UINT32_MAX, best_id = 0;
-    size_t best_pos = 0;
-    for (size_t k = 0; k + 1 < sym.size(); ++k) {
-      auto it = t.merges.find((static_cast<uint64_t>(sym[k]) << 32) | sym[k + 1]);
-      if (it != t.merges.end() && it->second.first < best_rank) {
-        best_rank = it->second.first;
-        best_id = it->second.second;
-        best_pos = k;
-      }
+  const size_t j0 = i + (c[i] == ' ' ? 1 : 0);
+  if (j0 < n) {
+    size_t j = j0;
+    if (is_letter(c[j])) {
+      while (j < n && is_letter(c[j])) ++j;
+      return j - i;
     }
-    if (best_rank == UINT32_MAX) break;
-    sym[best_pos] = best_id;
-    sym.erase(sym.begin() + best_pos + 1);
+    if (is_number(c[j])) {
+      while (j < n && is_number(c[j])) ++j;
+      return j - i;
+    }
+    auto other = [](uint32_t x) { return !is_whitespace(x) && !is_letter(x) && !is_number(x); };
+    if (other(c[j])) {
+      while (j < n && other(c[j])) ++j;
+      return j - i;
+    }
   }
-  ids.insert(ids.end(), sym.begin(), sym.end());
+  // c[i] is whitespace here
+  size_t j = i;
+  while (j < n && is_whitespace(c[j])) ++j;
+  if (j == n || j - i == 1) return j - i;
+  return j - 1 - i;  // the last space goes to the next word
 }
 
-void encode_clip(const jb_tokenizer& t, const char* s, size_t n, std::vector<uint32_t>& ids) {
+void pre_tokenize_and_model(const jb_tokenizer& t, const std::string& piece, std::vector<uint32_t>& ids) {
   std::vector<uint32_t> c;
-  decode_utf8(s, n, c);
-  size_t seg = 0;
-  for (size_t i = 0; i < c.size();) {
-    const size_t len = clip_match(c, i);
-    if (len == 0) {
+  decode_utf8(piece.data(), piece.size(), c);
+  if (c.empty()) return;
+  std::vector<uint32_t> word;
+  switch (t.pre) {
+    case kPreNone:
+      model(t, c, ids);
+      return;
+    case kPreBert:
+      for (uint32_t x : c) {
+        if (is_whitespace(x)) {
+          model(t, word, ids);
+          word.clear();
+        } else if (is_punct(x)) {
+          model(t, word, ids);
+          word.assign(1, x);
+          model(t, word, ids);
+          word.clear();
+        } else {
+          word.push_back(x);
+        }
+      }
+      model(t, word, ids);
+      return;
+    case kPreClip: {
+      size_t seg = 0;
+      for (size_t i = 0; i < c.size();) {
+        const size_t len = clip_match(c, i);
+        if (len == 0) {
+          ++i;
+          continue;
+        }
+        if (seg < i) model(t, std::vector<uint32_t>(c.begin() + seg, c.begin() + i), ids);
+        model(t, std::vector<uint32_t>(c.begin() + i, c.begin() + i + len), ids);
+        i += len;
+        seg = i;
+      }
+      if (seg < c.size()) model(t, std::vector<uint32_t>(c.begin() + seg, c.end()), ids);
+      return;
+    }
+    case kPreByteLevel: {
+      if (t.add_prefix_space && c[0] != ' ') c.insert(c.begin(), ' ');
+      const std::vector<uint32_t>& bs = byte_symbols();
+      std::string utf8;
+      for (size_t i = 0; i < c.size();) {
+        const size_t len = t.use_regex ? gpt2_match(c, i) : c.size();
+        utf8.clear();
+        for (size_t k = i; k < i + len; ++k) append_utf8(c[k], utf8);
+        word.clear();
+        for (unsigned char b : utf8) word.push_back(bs[b]);
+        model(t, word, ids);
+        i += len;
+      }
+      return;
+    }
+  }
+}
+
+// ---- added tokens -----------------------------------------------------------
+
+struct Piece {
+  size_t begin, end;
+  long id;  // -1: text
+};
+
+size_t prev_char_start(const std::string& s, size_t i) {  // i > 0
+  do --i;
+  while (i > 0 && (static_cast<unsigned char>(s[i]) & 0xC0) == 0x80);
+  return i;
+}
+uint32_t char_at(const std::string& s, size_t i, size_t* len) {
+  size_t n = 1;
+  while (i + n < s.size() && n < 4 && (static_cast<unsigned char>(s[i + n]) & 0xC0) == 0x80) ++n;
+  std::vector<uint32_t> c;
+  decode_utf8(s.data() + i, n, c);
+  if (len) *len = n;
+  return c.empty() ? 0 : c[0];
+}
+
+// Splits s on the added tokens: leftmost-longest matches in one pass, as the
+// crate's Aho-Corasick scan does (a match dropped by single_word still ends
+// the scan step), lstrip back to the previous piece, rstrip forward.
+std::vector<Piece> split_added(const std::string& s, const AddedSet& added) {
+  std::vector<Piece> out;
+  size_t start_offset = 0;
+  for (size_t i = 0; i < s.size() && !added.toks.empty();) {
+    const AddedToken* best = nullptr;
+    for (uint32_t k : added.by_first[static_cast<unsigned char>(s[i])]) {
+      const AddedToken& a = added.toks[k];
+      if (a.content.size() <= s.size() - i && std::memcmp(s.data() + i, a.content.data(), a.content.size()) == 0) {
+        best = &a;
+        break;
+      }
+    }
+    if (!best) {
       ++i;
       continue;
     }
-    if (seg < i) bpe_word(t, c, seg, i, ids);  // the span between matches
-    bpe_word(t, c, i, i + len, ids);
-    i += len;
-    seg = i;
-  }
-  if (seg < c.size()) bpe_word(t, c, seg, c.size(), ids);
-}
-
-// One segment of text between added tokens: normalise, pre-tokenise, WordPiece.
-void encode_segment(const jb_tokenizer& t, const char* s, size_t n, std::vector<uint32_t>& ids) {
-  if (t.kind == 1) return encode_clip(t, s, n, ids);
-  std::vector<uint32_t> cps;
-  decode_utf8(s, n, cps);
-  normalize(t, cps);
-  std::vector<uint32_t> word;
-  for (uint32_t c : cps) {
-    if (is_whitespace(c)) {
-      wordpiece(t, word, ids);
-      word.clear();
-    } else if (is_punct(c)) {
-      wordpiece(t, word, ids);
-      word.assign(1, c);
-      wordpiece(t, word, ids);
-      word.clear();
-    } else {
-      word.push_back(c);
+    size_t start = i, stop = i + best->content.size();
+    i = stop;
+    if (best->single_word) {
+      const bool word_before = start > 0 && is_word_char(char_at(s, prev_char_start(s, start), nullptr));
+      const bool word_after = stop < s.size() && is_word_char(char_at(s, stop, nullptr));
+      if (word_before || word_after) continue;
     }
-  }
-  wordpiece(t, word, ids);
-}
-
-void encode(const jb_tokenizer& t, const char* s, size_t n, int max_length,
-            std::vector<uint32_t>& out) {
-  std::vector<uint32_t> ids;
-  size_t seg = 0;
-  for (size_t i = 0; i < n;) {
-    size_t best = 0;
-    uint32_t best_id = 0;
-    for (const auto& a : t.added)
-      if (a.first.size() > best && a.first.size() <= n - i && std::memcmp(s + i, a.first.data(), a.first.size()) == 0) {
-        best = a.first.size();
-        best_id = a.second;
+    if (best->lstrip) {
+      size_t ns = start;
+      while (ns > 0) {
+        const size_t p = prev_char_start(s, ns);
+        if (!is_whitespace(char_at(s, p, nullptr))) break;
+        ns = p;
       }
-    if (best) {
-      encode_segment(t, s + seg, i - seg, ids);
-      ids.push_back(best_id);
-      i += best;
-      seg = i;
-    } else {
-      ++i;
+      start = std::max(ns, start_offset);
+    }
+    if (best->rstrip) {
+      size_t len = 0;
+      while (stop < s.size() && is_whitespace(char_at(s, stop, &len))) stop += len;
+      i = std::max(i, stop);
+    }
+    if (start_offset < start) out.push_back({start_offset, start, -1});
+    out.push_back({start, stop, static_cast<long>(best->id)});
+    start_offset = stop;
+  }
+  if (start_offset < s.size()) out.push_back({start_offset, s.size(), -1});
+  return out;
+}
+
+void encode(const jb_tokenizer& t, const char* s, size_t n, int max_length, std::vector<uint32_t>& out) {
+  std::vector<uint32_t> ids;
+  const std::string text(s, n);
+  std::vector<uint32_t> cps;
+  for (const Piece& p : split_added(text, t.raw_added)) {
+    if (p.id >= 0) {
+      ids.push_back(static_cast<uint32_t>(p.id));
+      continue;
+    }
+    cps.clear();
+    decode_utf8(text.data() + p.begin, p.end - p.begin, cps);
+    normalize(t, cps);
+    const std::string normed = to_utf8(cps);
+    for (const Piece& q : split_added(normed, t.norm_added)) {
+      if (q.id >= 0)
+        ids.push_back(static_cast<uint32_t>(q.id));
+      else
+        pre_tokenize_and_model(t, normed.substr(q.begin, q.end - q.begin), ids);
     }
   }
-  encode_segment(t, s + seg, n - seg, ids);
   const size_t specials = t.before.size() + t.after.size();
-  if (max_length > 0) {
-    const size_t keep = static_cast<size_t>(max_length) > specials ? max_length - specials : 0;
-    if (ids.size() > keep) ids.resize(keep);
+  const int limit = max_length > 0 ? max_length : t.file_max_length;
+  if (limit > 0) {
+    const size_t keep = static_cast<size_t>(limit) > specials ? limit - specials : 0;
+    if (ids.size() > keep) {
+      if (max_length <= 0 && t.file_trunc_left)
+        ids.erase(ids.begin(), ids.end() - keep);
+      else
+        ids.resize(keep);
+    }
   }
   out.clear();
   out.insert(out.end(), t.before.begin(), t.before.end());
@@ -408,10 +711,117 @@ void encode(const jb_tokenizer& t, const char* s, size_t n, int max_length,
   out.insert(out.end(), t.after.begin(), t.after.end());
 }
 
+// ---- loading ----------------------------------------------------------------
+
 uint32_t token_id(const jb_tokenizer& t, const std::string& tok) {
   auto it = t.vocab.find(tok);
-  if (it == t.vocab.end()) fail(JB_ERR_IO, "tokenizer.json: special token " + tok + " is not in the vocabulary");
+  if (it == t.vocab.end()) fail(JB_ERR_IO, "tokenizer.json: token " + tok + " is not in the vocabulary");
   return it->second;
+}
+
+void add_merge(jb_tokenizer& t, size_t rank, const std::string& a, const std::string& b) {
+  const std::string joined = a + b.substr(std::min(t.bpe_prefix.size(), b.size()));
+  auto ia = t.vocab.find(a), ib = t.vocab.find(b), iab = t.vocab.find(joined);
+  if (ia == t.vocab.end() || ib == t.vocab.end() || iab == t.vocab.end())
+    fail(JB_ERR_IO, "BPE merge " + std::to_string(rank + 1) + " (" + a + " " + b +
+                        ") names a symbol not in the vocabulary");
+  t.merges[(static_cast<uint64_t>(ia->second) << 32) | ib->second] = {static_cast<uint32_t>(rank),
+                                                                        iab->second};
+}
+
+void parse_normalizer(jb_tokenizer& t, const Json& nz) {
+  const std::string type = nz.str_or("type", "");
+  if (type == "Sequence") {
+    if (const Json* seq = nz.get("normalizers"); seq && seq->kind == Json::Arr)
+      for (const Json& x : seq->arr) parse_normalizer(t, x);
+  } else if (type == "BertNormalizer") {
+    t.clean_text = nz.bool_or("clean_text", true);
+    t.handle_chinese = nz.bool_or("handle_chinese_chars", true);
+    t.lowercase = nz.bool_or("lowercase", true);
+    const Json* sa = nz.get("strip_accents");
+    t.strip_accents = (sa && sa->kind == Json::Bool) ? sa->b : t.lowercase;
+    t.norm.push_back(kNormBert);
+  } else if (type == "NFC") {
+    t.norm.push_back(kNormNfc);
+  } else if (type == "NFD") {
+    t.norm.push_back(kNormNfd);
+  } else if (type == "Lowercase") {
+    t.norm.push_back(kNormLower);
+  } else {
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported normalizer " + type);
+  }
+}
+
+void parse_pre_tokenizer(jb_tokenizer& t, const Json& pt) {
+  std::string type = pt.str_or("type", "");
+  const Json* inner = &pt;
+  if (type == "Sequence") {  // a one-element Sequence is that element
+    const Json* seq = pt.get("pretokenizers");
+    if (!seq || seq->kind != Json::Arr || seq->arr.size() != 1)
+      fail(JB_ERR_INVALID, "tokenizer.json: unsupported pre-tokenizer sequence");
+    inner = &seq->arr[0];
+    type = inner->str_or("type", "");
+  }
+  if (type == "BertPreTokenizer") {
+    t.pre = kPreBert;
+  } else if (type == "ByteLevel") {
+    t.pre = kPreByteLevel;
+    t.add_prefix_space = inner->bool_or("add_prefix_space", true);
+    t.use_regex = inner->bool_or("use_regex", true);
+  } else {
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported pre-tokenizer " + type);
+  }
+}
+
+uint32_t id_of_pair(const Json* p, const char* what) {
+  if (!p || p->kind != Json::Arr || p->arr.size() < 2)
+    fail(JB_ERR_IO, std::string("tokenizer.json: post-processor needs ") + what);
+  return static_cast<uint32_t>(p->arr[1].num);
+}
+
+// One post-processor's special ids around the sequence; a Sequence applies
+// its processors in order, each wrapping the previous result.
+void parse_post(const jb_tokenizer& t, const Json& pp, std::vector<uint32_t>& before,
+                std::vector<uint32_t>& after) {
+  const std::string type = pp.str_or("type", "");
+  std::vector<uint32_t> b, a;
+  if (type == "BertProcessing" || type == "RobertaProcessing") {
+    b.push_back(id_of_pair(pp.get("cls"), "cls"));
+    a.push_back(id_of_pair(pp.get("sep"), "sep"));
+  } else if (type == "TemplateProcessing") {
+    const Json* single = pp.get("single");
+    const Json* specials = pp.get("special_tokens");
+    if (!single || single->kind != Json::Arr) fail(JB_ERR_IO, "tokenizer.json: template without 'single'");
+    bool seen_seq = false;
+    for (const Json& item : single->arr) {
+      if (item.get("Sequence")) {
+        seen_seq = true;
+        continue;
+      }
+      const Json* sp = item.get("SpecialToken");
+      if (!sp) fail(JB_ERR_INVALID, "tokenizer.json: unsupported template item");
+      const std::string name = sp->str_or("id", "");
+      const Json* def = specials ? specials->get(name) : nullptr;
+      const Json* ids = def ? def->get("ids") : nullptr;
+      std::vector<uint32_t> v;
+      if (ids && ids->kind == Json::Arr)
+        for (const Json& x : ids->arr) v.push_back(static_cast<uint32_t>(x.num));
+      else
+        v.push_back(token_id(t, name));
+      auto& dst = seen_seq ? a : b;
+      dst.insert(dst.end(), v.begin(), v.end());
+    }
+  } else if (type == "ByteLevel") {
+    // offsets only
+  } else if (type == "Sequence") {
+    if (const Json* seq = pp.get("processors"); seq && seq->kind == Json::Arr)
+      for (const Json& x : seq->arr) parse_post(t, x, before, after);
+    return;
+  } else {
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported post-processor " + type);
+  }
+  before.insert(before.begin(), b.begin(), b.end());
+  after.insert(after.end(), a.begin(), a.end());
 }
 
 jb_tokenizer* load(const char* path) {
@@ -427,83 +837,68 @@ jb_tokenizer* load(const char* path) {
   }
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
   const Json* model = j.get("model");
-  if (!model || model->str_or("type", "") != "WordPiece")
-    fail(JB_ERR_INVALID, "tokenizer.json: only the WordPiece model (BERT family) is supported");
+  const std::string type = model ? model->str_or("type", "") : "";
+  if (type != "WordPiece" && type != "BPE")
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported model '" + type + "' (WordPiece and BPE are supported)");
+  t->wordpiece = type == "WordPiece";
   const Json* vocab = model->get("vocab");
   if (!vocab || vocab->kind != Json::Obj) fail(JB_ERR_IO, "tokenizer.json: model.vocab missing");
   for (const auto& kv : vocab->obj) t->vocab[kv.first] = static_cast<uint32_t>(kv.second.num);
-  t->prefix = model->str_or("continuing_subword_prefix", "##");
-  t->max_chars = static_cast<int>(model->num_or("max_input_chars_per_word", 100));
-  t->unk_id = token_id(*t, model->str_or("unk_token", "[UNK]"));
-  if (const Json* nz = j.get("normalizer"); nz && nz->kind == Json::Obj) {
-    if (nz->str_or("type", "") != "BertNormalizer")
-      fail(JB_ERR_INVALID, "tokenizer.json: only the BertNormalizer is supported");
-    t->clean_text = nz->bool_or("clean_text", true);
-    t->handle_chinese = nz->bool_or("handle_chinese_chars", true);
-    t->lowercase = nz->bool_or("lowercase", true);
-    const Json* sa = nz->get("strip_accents");
-    t->strip_accents = (sa && sa->kind == Json::Bool) ? sa->b : t->lowercase;
+  if (t->wordpiece) {
+    t->prefix = model->str_or("continuing_subword_prefix", "##");
+    t->max_chars = static_cast<int>(model->num_or("max_input_chars_per_word", 100));
+    t->unk_id = token_id(*t, model->str_or("unk_token", "[UNK]"));
+    t->has_unk = true;
   } else {
-    t->clean_text = t->handle_chinese = t->strip_accents = t->lowercase = false;
-  }
-  if (const Json* pt = j.get("pre_tokenizer"); pt && pt->kind == Json::Obj &&
-                                              pt->str_or("type", "") != "BertPreTokenizer")
-    fail(JB_ERR_INVALID, "tokenizer.json: only the BertPreTokenizer is supported");
-  if (const Json* pp = j.get("post_processor"); pp && pp->kind == Json::Obj) {
-    const std::string type = pp->str_or("type", "");
-    if (type == "BertProcessing") {
-      const Json* cls = pp->get("cls");
-      const Json* sep = pp->get("sep");
-      if (!cls || !sep || cls->arr.size() < 2 || sep->arr.size() < 2)
-        fail(JB_ERR_IO, "tokenizer.json: BertProcessing needs cls and sep");
-      t->before.push_back(static_cast<uint32_t>(cls->arr[1].num));
-      t->after.push_back(static_cast<uint32_t>(sep->arr[1].num));
-    } else if (type == "TemplateProcessing") {
-      const Json* single = pp->get("single");
-      const Json* specials = pp->get("special_tokens");
-      if (!single || single->kind != Json::Arr) fail(JB_ERR_IO, "tokenizer.json: template without 'single'");
-      bool seen_seq = false;
-      for (const Json& item : single->arr) {
-        if (item.get("Sequence")) {
-          seen_seq = true;
-          continue;
-        }
-        const Json* sp = item.get("SpecialToken");
-        if (!sp) fail(JB_ERR_INVALID, "tokenizer.json: unsupported template item");
-        const std::string name = sp->str_or("id", "");
-        const Json* def = specials ? specials->get(name) : nullptr;
-        const Json* ids = def ? def->get("ids") : nullptr;
-        std::vector<uint32_t> v;
-        if (ids && ids->kind == Json::Arr)
-          for (const Json& x : ids->arr) v.push_back(static_cast<uint32_t>(x.num));
-        else
-          v.push_back(token_id(*t, name));
-        auto& dst = seen_seq ? t->after : t->before;
-        dst.insert(dst.end(), v.begin(), v.end());
+    if (const Json* d = model->get("dropout"); d && d->kind == Json::Num && d->num > 0)
+      fail(JB_ERR_INVALID, "tokenizer.json: BPE dropout is not supported");
+    if (const Json* unk = model->get("unk_token"); unk && unk->kind == Json::Str) {
+      t->unk_id = token_id(*t, unk->str);
+      t->has_unk = true;
+    }
+    if (const Json* p = model->get("continuing_subword_prefix"); p && p->kind == Json::Str) t->bpe_prefix = p->str;
+    if (const Json* p = model->get("end_of_word_suffix"); p && p->kind == Json::Str) t->bpe_suffix = p->str;
+    t->fuse_unk = model->bool_or("fuse_unk", false);
+    t->byte_fallback = model->bool_or("byte_fallback", false);
+    t->ignore_merges = model->bool_or("ignore_merges", false);
+    const Json* merges = model->get("merges");
+    if (!merges || merges->kind != Json::Arr) fail(JB_ERR_IO, "tokenizer.json: model.merges missing");
+    for (size_t r = 0; r < merges->arr.size(); ++r) {
+      const Json& m = merges->arr[r];
+      if (m.kind == Json::Arr && m.arr.size() == 2) {  // ["a", "b"]
+        add_merge(*t, r, m.arr[0].str, m.arr[1].str);
+      } else if (m.kind == Json::Str) {  // "a b"
+        const size_t sp = m.str.find(' ', 1);
+        if (sp == std::string::npos) fail(JB_ERR_IO, "tokenizer.json: bad merge " + m.str);
+        add_merge(*t, r, m.str.substr(0, sp), m.str.substr(sp + 1));
+      } else {
+        fail(JB_ERR_IO, "tokenizer.json: bad merge entry");
       }
-    } else {
-      fail(JB_ERR_INVALID, "tokenizer.json: unsupported post-processor " + type);
     }
   }
+  if (const Json* nz = j.get("normalizer"); nz && nz->kind == Json::Obj) parse_normalizer(*t, *nz);
+  if (const Json* pt = j.get("pre_tokenizer"); pt && pt->kind == Json::Obj)
+    parse_pre_tokenizer(*t, *pt);
+  else
+    t->pre = kPreNone;
+  if (const Json* pp = j.get("post_processor"); pp && pp->kind == Json::Obj)
+    parse_post(*t, *pp, t->before, t->after);
   if (const Json* added = j.get("added_tokens"); added && added->kind == Json::Arr)
     for (const Json& a : added->arr) {
-      const std::string content = a.str_or("content", "");
-      if (!content.empty()) t->added.emplace_back(content, static_cast<uint32_t>(a.num_or("id", 0)));
+      AddedToken tok;
+      tok.content = a.str_or("content", "");
+      if (tok.content.empty()) continue;
+      tok.id = static_cast<uint32_t>(a.num_or("id", 0));
+      tok.lstrip = a.bool_or("lstrip", false);
+      tok.rstrip = a.bool_or("rstrip", false);
+      tok.single_word = a.bool_or("single_word", false);
+      (a.bool_or("normalized", false) ? t->norm_added : t->raw_added).add(tok);
     }
-  return t.release();
-}
-
-// The GPT-2 / CLIP byte-to-printable-code-point table: bytes 33-126, 161-172
-// and 174-255 map to themselves, the other 68 bytes, in ascending order, to
-// 256, 257, ...
-std::vector<uint32_t> byte_symbols() {
-  std::vector<uint32_t> out(256);
-  uint32_t extra = 0;
-  for (uint32_t b = 0; b < 256; ++b) {
-    const bool direct = (b >= 33 && b <= 126) || (b >= 161 && b <= 172) || (b >= 174 && b <= 255);
-    out[b] = direct ? b : 256 + extra++;
+  if (const Json* tr = j.get("truncation"); tr && tr->kind == Json::Obj) {
+    t->file_max_length = static_cast<int>(tr->num_or("max_length", 0));
+    t->file_trunc_left = tr->str_or("direction", "Right") == "Left";
   }
-  return out;
+  return t.release();
 }
 
 std::string read_maybe_gzip(const char* path) {
@@ -537,15 +932,16 @@ jb_tokenizer* load_clip(const char* path) {
   }
   if (merges.empty()) fail(JB_ERR_IO, std::string("no BPE merges in ") + path);
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
-  t->kind = 1;
-  const std::vector<uint32_t> bytes = byte_symbols();
+  t->wordpiece = false;
+  t->pre = kPreClip;
+  t->bpe_suffix = "</w>";
   std::vector<std::string> vocab;
-  for (uint32_t c : bytes) {
+  for (uint32_t c : byte_symbols()) {
     std::string s;
     append_utf8(c, s);
     vocab.push_back(s);
   }
-  for (uint32_t c : bytes) {
+  for (uint32_t c : byte_symbols()) {
     std::string s;
     append_utf8(c, s);
     vocab.push_back(s + "</w>");
@@ -554,17 +950,25 @@ jb_tokenizer* load_clip(const char* path) {
   vocab.push_back("<|startoftext|>");
   vocab.push_back("<|endoftext|>");
   for (size_t i = 0; i < vocab.size(); ++i) t->vocab[vocab[i]] = static_cast<uint32_t>(i);
-  for (size_t r = 0; r < merges.size(); ++r) {
-    auto a = t->vocab.find(merges[r].first), b = t->vocab.find(merges[r].second);
-    auto ab = t->vocab.find(merges[r].first + merges[r].second);
-    if (a == t->vocab.end() || b == t->vocab.end() || ab == t->vocab.end())
-      fail(JB_ERR_IO, "BPE merge " + std::to_string(r + 1) + " names a symbol not in the vocabulary");
-    t->merges[(static_cast<uint64_t>(a->second) << 32) | b->second] =
-        {static_cast<uint32_t>(r), ab->second};
-  }
+  for (size_t r = 0; r < merges.size(); ++r) add_merge(*t, r, merges[r].first, merges[r].second);
   t->before.push_back(static_cast<uint32_t>(vocab.size() - 2));
   t->after.push_back(static_cast<uint32_t>(vocab.size() - 1));
   return t.release();
+}
+
+template <typename F>
+jb_status guarded_load(const char* path, jb_tokenizer** out, F&& loader) {
+  if (!out) return record_error(JB_ERR_INVALID, "null output handle");
+  *out = nullptr;
+  try {
+    if (!path) fail(JB_ERR_INVALID, "null path");
+    *out = loader(path);
+    return JB_OK;
+  } catch (const Error& e) {
+    return record_error(e.status, e.msg);
+  } catch (const std::exception& e) {
+    return record_error(JB_ERR_INVALID, e.what());
+  }
 }
 
 }  // namespace
@@ -572,32 +976,12 @@ jb_tokenizer* load_clip(const char* path) {
 
 extern "C" {
 
-jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out) {
-  if (!out) return jb::record_error(JB_ERR_INVALID, "null output handle");
-  *out = nullptr;
-  try {
-    if (!merges_path) jb::fail(JB_ERR_INVALID, "null path");
-    *out = jb::load_clip(merges_path);
-    return JB_OK;
-  } catch (const jb::Error& e) {
-    return jb::record_error(e.status, e.msg);
-  } catch (const std::exception& e) {
-    return jb::record_error(JB_ERR_INVALID, e.what());
-  }
+jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out) {
+  return jb::guarded_load(tokenizer_json_path, out, jb::load);
 }
 
-jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out) {
-  if (!out) return jb::record_error(JB_ERR_INVALID, "null output handle");
-  *out = nullptr;
-  try {
-    if (!tokenizer_json_path) jb::fail(JB_ERR_INVALID, "null path");
-    *out = jb::load(tokenizer_json_path);
-    return JB_OK;
-  } catch (const jb::Error& e) {
-    return jb::record_error(e.status, e.msg);
-  } catch (const std::exception& e) {
-    return jb::record_error(JB_ERR_INVALID, e.what());
-  }
+jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out) {
+  return jb::guarded_load(merges_path, out, jb::load_clip);
 }
 
 void jb_tokenizer_free(jb_tokenizer* t) { delete t; }

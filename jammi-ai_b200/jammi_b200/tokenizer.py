@@ -1,6 +1,7 @@
-"""``Tokenizer``: the library's host-side tokenizers (BERT WordPiece, OpenCLIP BPE)
-(``jb_tokenizer_*``), the counterpart of the reference's ``TokenizerWrapper``
-(crates/jammi-ai/src/model/tokenizer.rs) for the BERT family's tokenizer.json.
+"""``Tokenizer``: the library's host-side tokenizers (``jb_tokenizer_*``), the
+counterpart of the reference's ``TokenizerWrapper`` (crates/jammi-ai/src/model/
+tokenizer.rs): a model's tokenizer.json (WordPiece or BPE, byte-level or
+character-level) or OpenCLIP's merges file (clip_bpe.rs).
 
 Calling it on a list of texts returns one uint32 id array per text, so it can
 be handed to ``driver.embed_texts`` as the ``tokenize`` callable."""
@@ -14,8 +15,9 @@ from ._lib import check, lib
 
 
 class Tokenizer:
-    """``Tokenizer(tokenizer_json)``: BERT WordPiece; ``Tokenizer.clip_bpe(path)``:
-    the OpenCLIP text tower's BPE from its merges file."""
+    """``Tokenizer(tokenizer_json)``: a model's tokenizer.json;
+    ``Tokenizer.clip_bpe(path)``: the OpenCLIP text tower's BPE from its merges
+    file.  ``max_length`` 0 applies the file's own truncation, if any."""
 
     def __init__(self, tokenizer_json: str | None = None, max_length: int = 0, _handle=None):
         if _handle is None:

@@ -102,9 +102,15 @@ def test_many_texts_use_all_cores_in_order(tmp_path):
 def test_unsupported_tokenizer_is_rejected(tmp_path):
     from jammi_b200 import Tokenizer
     from jammi_b200._lib import JbError
-    path = tmp_path / "bpe.json"
-    path.write_text(json.dumps({"model": {"type": "BPE", "vocab": {}, "merges": []}}))
-    with pytest.raises(JbError):
-        Tokenizer(str(path))
+    for doc in ({"model": {"type": "Unigram", "vocab": [["a", 0.0]]}},
+                {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
+                 "pre_tokenizer": {"type": "Metaspace", "replacement": "_"}},
+                {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
+                 "normalizer": {"type": "NFKC"}},
+                {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": ["a b"]}}):
+        path = tmp_path / "bad.json"
+        path.write_text(json.dumps(doc))
+        with pytest.raises(JbError):
+            Tokenizer(str(path))
     with pytest.raises(JbError):
         Tokenizer(str(tmp_path / "missing.json"))
