@@ -350,6 +350,34 @@ typedef int (*jb_forward_cb)(void* user, int64_t start, int64_t count, char* msg
 jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, void* user);
 int jb_is_oom_message(const char* msg);
 
+/* ── ANN sidecar vector formats and exact search (device) ─────────────────
+ * The vector side of the reference's index module on device buffers.
+ * jb_op_fit_binary_threshold: the per-dimension threshold tau a Binary
+ * sidecar sign-packs against (fit_binary_threshold, crates/jammi-db/src/
+ * index/sidecar.rs:162-216) over the first min(rows, 100000) rows of
+ * d_vectors [rows, dim]: JB_THRESHOLD_MEAN (f64 sum in row order / count,
+ * rounded to f32; bit-identical) or JB_THRESHOLD_MEDIAN (f32 total order,
+ * the central pair averaged for an even count); zeros for no rows.
+ * jb_op_pack_threshold_bits: pack_threshold_bits (sidecar.rs:232-241), bit i
+ * = v[i] > tau[i], LSB-first, d_packed [rows, ceil(dim / 8)] bytes.
+ * jb_op_exact_search: exact_vector_search (crates/jammi-db/src/index/
+ * exact.rs:119-175) -- cosine_distance (crates/jammi-numerics/src/
+ * distance.rs:6-21) of every query to every corpus row, bit-identical to the
+ * reference's f32 loop, and the k nearest per query in ascending (distance,
+ * tie rank) order: d_tie_rank [n] is each row's position in ascending
+ * _row_id order (distinct; NULL = row order).  d_scratch holds
+ * n_queries x n floats; d_idx / d_dist are [n_queries, k], entries past the
+ * corpus size -1 / +inf.  k <= 1024.  Repeated tie ranks surface as
+ * JB_ERR_INVALID from jb_op_sync. */
+enum { JB_THRESHOLD_MEAN = 0, JB_THRESHOLD_MEDIAN = 1 };
+jb_status jb_op_fit_binary_threshold(const float* d_vectors, int64_t rows, int dim, int kind,
+                                     float* d_tau, void* stream);
+jb_status jb_op_pack_threshold_bits(const float* d_vectors, int64_t rows, int dim,
+                                    const float* d_tau, uint8_t* d_packed, void* stream);
+jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const uint32_t* d_tie_rank,
+                             const float* d_queries, int n_queries, int k, float* d_scratch,
+                             int64_t* d_idx, float* d_dist, void* stream);
+
 /* ── tokenizer (host) ─────────────────────────────────────────────────────
  * A model's tokenizer.json through the HuggingFace `tokenizers` pipeline the
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/

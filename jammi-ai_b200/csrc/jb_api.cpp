@@ -405,6 +405,7 @@ jb_status jb_op_sync(void* stream) {
     jb::check_cuda(cudaMemcpy(&v, flag, sizeof(int), cudaMemcpyDeviceToHost), "op flag");
     if (v) {
       cudaMemset(flag, 0, sizeof(int));
+      if (v & jb::kErrTieRank) jb::fail(JB_ERR_INVALID, "exact search: tie ranks must be distinct");
       jb::fail(v & jb::kErrTimeout ? JB_ERR_TIMEOUT : JB_ERR_CUDA, "device-side wait exceeded its limit");
     }
   });
@@ -554,6 +555,46 @@ jb_status jb_op_attention_rows(const void* qkv, const int* cu_seqlens, void* ctx
   if (rows < 0) return jb::record_error(JB_ERR_INVALID, "jb_op_attention_rows: rows must be >= 0");
   return op_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len, causal ? 1 : 0,
                       stream, rows);
+}
+
+jb_status jb_op_fit_binary_threshold(const float* d_vectors, int64_t rows, int dim, int kind, float* d_tau,
+                                     void* stream) {
+  return guarded([&] {
+    if (rows < 0 || dim < 0 || (kind != JB_THRESHOLD_MEAN && kind != JB_THRESHOLD_MEDIAN))
+      jb::fail(JB_ERR_INVALID, "jb_op_fit_binary_threshold: bad argument");
+    if (dim > 0 && (!d_tau || (rows > 0 && !d_vectors))) jb::fail(JB_ERR_INVALID, "jb_op_fit_binary_threshold: null buffer");
+    jb::check_cuda(jb::launch_fit_binary_threshold(d_vectors, rows, dim, kind, d_tau, as_stream(stream)),
+                   "jb_op_fit_binary_threshold");
+  });
+}
+
+jb_status jb_op_pack_threshold_bits(const float* d_vectors, int64_t rows, int dim, const float* d_tau,
+                                    uint8_t* d_packed, void* stream) {
+  return guarded([&] {
+    if (rows < 0 || dim < 0) jb::fail(JB_ERR_INVALID, "jb_op_pack_threshold_bits: bad argument");
+    if (rows > 0 && dim > 0 && (!d_vectors || !d_tau || !d_packed))
+      jb::fail(JB_ERR_INVALID, "jb_op_pack_threshold_bits: null buffer");
+    jb::check_cuda(jb::launch_pack_threshold_bits(d_vectors, rows, dim, d_tau, d_packed, as_stream(stream)),
+                   "jb_op_pack_threshold_bits");
+  });
+}
+
+jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const uint32_t* d_tie_rank,
+                             const float* d_queries, int n_queries, int k, float* d_scratch,
+                             int64_t* d_idx, float* d_dist, void* stream) {
+  return guarded([&] {
+    if (n < 0 || dim <= 0 || n_queries < 0 || k < 0)
+      jb::fail(JB_ERR_INVALID, "jb_op_exact_search: bad argument");
+    if (k > jb::kMaxSearchK)
+      jb::fail(JB_ERR_INVALID, "jb_op_exact_search: k above " + std::to_string(jb::kMaxSearchK));
+    if (n > static_cast<int64_t>(UINT32_MAX)) jb::fail(JB_ERR_INVALID, "jb_op_exact_search: corpus above 2^32 rows");
+    if (n_queries > 65535 * 8) jb::fail(JB_ERR_INVALID, "jb_op_exact_search: too many queries in one call");
+    if (n_queries > 0 && k > 0 && (!d_idx || !d_dist || (n > 0 && (!d_corpus || !d_queries || !d_scratch))))
+      jb::fail(JB_ERR_INVALID, "jb_op_exact_search: null buffer");
+    jb::check_cuda(jb::launch_exact_search(d_corpus, n, dim, d_tie_rank, d_queries, n_queries, k, d_scratch,
+                                           d_idx, d_dist, op_flag(current_device()), as_stream(stream)),
+                   "jb_op_exact_search");
+  });
 }
 
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens, float* out,

@@ -1,0 +1,336 @@
+// The vector side of the ANN sidecar and of exact search, on the device:
+// the produced embeddings go from HBM into the index formats without a trip
+// through host loops.
+//
+// * Binary threshold tau (fit_binary_threshold, crates/jammi-db/src/index/
+//   sidecar.rs:162-216): per dimension over the first min(rows, 100000)
+//   rows, either the mean -- an f64 sum taken in row order, divided by the
+//   row count, rounded to f32 -- or the median under f32 total order (the
+//   two central values averaged in f32 for an even count).  The mean runs
+//   one thread per dimension so its additions happen in the reference's
+//   order (bit-identical); the median is a radix select over the total-order
+//   keys, exact by construction.
+// * Threshold sign-packing (pack_threshold_bits, sidecar.rs:232-241): bit i
+//   of a row is v[i] > tau[i], LSB-first in ceil(dim / 8) bytes, padding 0.
+// * Exact search (exact_vector_search, crates/jammi-db/src/index/
+//   exact.rs:119-175, with cosine_distance, crates/jammi-numerics/src/
+//   distance.rs:6-21): distance = 1 - dot / (sqrt(|a|^2) sqrt(|b|^2)), or 1
+//   when that denominator is below f32 epsilon; the three sums accumulate in
+//   f32 in dimension order, each product and sum one IEEE rounding (explicit
+//   _rn intrinsics: no fused multiply-adds), so every distance equals the
+//   reference's bit for bit.  The k best per query under (distance, row-id
+//   rank) -- the reference breaks distance ties by ascending _row_id; the
+//   caller passes each row's rank in that order, or none for row order --
+//   come from a radix select over 64-bit (distance key, rank) keys, then a
+//   rank sort of the k survivors.
+#include <cfloat>
+#include <cstdint>
+
+#include "jb_common.cuh"
+#include "jb_internal.h"
+
+namespace jb {
+namespace {
+
+// f32 total order (Rust's f32::total_cmp) as an unsigned key order.
+__device__ __forceinline__ uint32_t total_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float from_total_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// ---- binary threshold -------------------------------------------------------
+
+__global__ void mean_threshold_kernel(const float* __restrict__ v, int64_t rows, int dim,
+                                      float* __restrict__ tau) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= dim) return;
+  const float* p = v + d;
+  double s = 0.0;
+  int64_t r = 0;
+  for (; r + 8 <= rows; r += 8) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = __ldg(p + (r + u) * dim);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s = __dadd_rn(s, static_cast<double>(x[u]));
+  }
+  for (; r < rows; ++r) s = __dadd_rn(s, static_cast<double>(__ldg(p + r * dim)));
+  const double n = rows > 0 ? static_cast<double>(rows) : 1.0;
+  tau[d] = __double2float_rn(__ddiv_rn(s, n));
+}
+
+constexpr int kMedWarps = 16;
+
+// One CTA per 32 dimensions (lane l owns dimension d0 + l); the warps split
+// the rows.  For each wanted order statistic, four 8-bit passes narrow the
+// key prefix: a shared histogram per lane of the keys that match the prefix
+// so far, then lane l's scan picks the bin holding its remaining rank.
+__global__ void __launch_bounds__(32 * kMedWarps)
+median_threshold_kernel(const float* __restrict__ v, int64_t rows, int dim, float* __restrict__ tau) {
+  __shared__ uint32_t hist[32][257];
+  __shared__ uint32_t s_prefix[32], s_mask[32];
+  __shared__ int64_t s_remaining[32];
+  __shared__ float s_value[2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + lane;
+  const bool live = d < dim;
+  const int64_t mid = rows / 2;
+  const int n_stats = (rows % 2 == 0) ? 2 : 1;
+  for (int st = 0; st < n_stats; ++st) {
+    // 0-based rank: mid - 1 and mid for an even count, mid for an odd one
+    const int64_t rank = (n_stats == 2 && st == 0) ? mid - 1 : mid;
+    if (warp == 0) {
+      s_prefix[lane] = 0;
+      s_mask[lane] = 0;
+      s_remaining[lane] = rank + 1;
+    }
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = threadIdx.x; i < 32 * 257; i += blockDim.x) (&hist[0][0])[i] = 0;
+      __syncthreads();
+      const uint32_t pfx = s_prefix[lane], msk = s_mask[lane];
+      if (live) {
+        int64_t r = warp;
+        for (; r + 3 * kMedWarps < rows; r += 4 * kMedWarps) {  // four loads in flight
+          float x[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) x[u] = __ldg(v + (r + u * kMedWarps) * dim + d);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint32_t key = total_key(x[u]);
+            if ((key & msk) == pfx) atomicAdd(&hist[lane][(key >> shift) & 255u], 1u);
+          }
+        }
+        for (; r < rows; r += kMedWarps) {
+          const uint32_t key = total_key(__ldg(v + r * dim + d));
+          if ((key & msk) == pfx) atomicAdd(&hist[lane][(key >> shift) & 255u], 1u);
+        }
+      }
+      __syncthreads();
+      if (warp == 0 && live) {
+        int64_t cum = 0;
+        for (int b = 0; b < 256; ++b) {
+          const int64_t h = hist[lane][b];
+          if (cum + h >= s_remaining[lane]) {
+            s_prefix[lane] = pfx | (static_cast<uint32_t>(b) << shift);
+            s_mask[lane] = msk | (255u << shift);
+            s_remaining[lane] -= cum;
+            break;
+          }
+          cum += h;
+        }
+      }
+      __syncthreads();
+    }
+    if (warp == 0) s_value[st][lane] = from_total_key(s_prefix[lane]);
+    __syncthreads();
+  }
+  if (warp == 0 && live) {
+    if (rows == 0)
+      tau[d] = 0.0f;
+    else
+      tau[d] = n_stats == 2 ? __fdiv_rn(__fadd_rn(s_value[0][lane], s_value[1][lane]), 2.0f)
+                            : s_value[0][lane];
+  }
+}
+
+__global__ void pack_threshold_bits_kernel(const float* __restrict__ v, int64_t rows, int dim,
+                                           const float* __restrict__ tau, uint8_t* __restrict__ out) {
+  const int nb = (dim + 7) / 8;
+  const int64_t total = rows * nb;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / nb;
+    const int b = static_cast<int>(i - r * nb);
+    uint32_t byte = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int dd = b * 8 + k;
+      if (dd < dim && __ldg(v + r * dim + dd) > __ldg(tau + dd)) byte |= 1u << k;
+    }
+    out[i] = static_cast<uint8_t>(byte);
+  }
+}
+
+// ---- exact search -----------------------------------------------------------
+
+constexpr int kDistRows = 128;  // corpus rows per CTA, one per thread
+constexpr int kDistQ = 8;       // queries per CTA
+constexpr int kDistChunk = 32;  // dimensions staged per step
+
+// dist[q][row] for queries [q0, q0 + kDistQ) x rows [row0, row0 + 128).
+__global__ void __launch_bounds__(kDistRows)
+cosine_distance_kernel(const float* __restrict__ corpus, int64_t n, int dim,
+                       const float* __restrict__ queries, int nq, float* __restrict__ dist) {
+  __shared__ float tile[kDistRows][kDistChunk + 1];
+  __shared__ float qs[kDistQ][kDistChunk];
+  __shared__ float s_qnorm[kDistQ];
+  const int t = threadIdx.x;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kDistRows;
+  const int q0 = blockIdx.y * kDistQ;
+  const int64_t row = row0 + t;
+  float dot[kDistQ];
+#pragma unroll
+  for (int j = 0; j < kDistQ; ++j) dot[j] = 0.0f;
+  float nb = 0.0f, na = 0.0f;  // na: query t's squared norm, threads t < kDistQ
+  for (int d0 = 0; d0 < dim; d0 += kDistChunk) {
+    const int w = min(kDistChunk, dim - d0);
+    for (int e = t; e < kDistRows * kDistChunk; e += kDistRows) {
+      const int r = e / kDistChunk, c = e % kDistChunk;
+      const int64_t gr = row0 + r;
+      tile[r][c] = (gr < n && c < w) ? __ldg(corpus + gr * dim + d0 + c) : 0.0f;
+    }
+    for (int e = t; e < kDistQ * kDistChunk; e += kDistRows) {
+      const int j = e / kDistChunk, c = e % kDistChunk;
+      qs[j][c] = (q0 + j < nq && c < w) ? __ldg(queries + static_cast<int64_t>(q0 + j) * dim + d0 + c) : 0.0f;
+    }
+    __syncthreads();
+    for (int c = 0; c < w; ++c) {
+      const float x = tile[t][c];
+      nb = __fadd_rn(nb, __fmul_rn(x, x));
+#pragma unroll
+      for (int j = 0; j < kDistQ; ++j) dot[j] = __fadd_rn(dot[j], __fmul_rn(qs[j][c], x));
+    }
+    if (t < kDistQ)
+      for (int c = 0; c < w; ++c) na = __fadd_rn(na, __fmul_rn(qs[t][c], qs[t][c]));
+    __syncthreads();
+  }
+  if (t < kDistQ) s_qnorm[t] = na;
+  __syncthreads();
+  if (row >= n) return;
+  const float sb = __fsqrt_rn(nb);
+#pragma unroll
+  for (int j = 0; j < kDistQ; ++j) {
+    if (q0 + j >= nq) break;
+    const float denom = __fmul_rn(__fsqrt_rn(s_qnorm[j]), sb);
+    const float dd = denom < FLT_EPSILON ? 1.0f : __fsub_rn(1.0f, __fdiv_rn(dot[j], denom));
+    dist[static_cast<int64_t>(q0 + j) * n + row] = dd;
+  }
+}
+
+constexpr int kTopkThreads = 1024;
+
+// Total-order key of a distance with ties equal: -0 reads as +0, every NaN
+// as the positive quiet NaN (after all numbers).
+__device__ __forceinline__ uint64_t search_key(float d, uint32_t rank) {
+  if (d == 0.0f) d = 0.0f;
+  if (d != d) d = __uint_as_float(0x7FC00000u);
+  return (static_cast<uint64_t>(total_key(d)) << 32) | rank;
+}
+
+// One CTA per query: the k-th smallest key by radix select (eight 8-bit
+// passes), then the keys at or below it, ordered by counting smaller keys.
+__global__ void __launch_bounds__(kTopkThreads)
+topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restrict__ tie_rank, int k,
+            int64_t* __restrict__ out_idx, float* __restrict__ out_dist, int* err) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint64_t s_prefix, s_mask;
+  __shared__ int64_t s_remaining;
+  __shared__ uint64_t cand_key[kMaxSearchK];
+  __shared__ int64_t cand_idx[kMaxSearchK];
+  __shared__ unsigned s_count;
+  const int q = blockIdx.x, t = threadIdx.x;
+  const float* dq = dist + static_cast<int64_t>(q) * n;
+  const int kk = static_cast<int>(min(static_cast<int64_t>(k), n));
+  auto key_of = [&](int64_t i) {
+    return search_key(dq[i], tie_rank ? tie_rank[i] : static_cast<uint32_t>(i));
+  };
+  for (int s = kk + t; s < k; s += blockDim.x) {
+    out_idx[static_cast<int64_t>(q) * k + s] = -1;
+    out_dist[static_cast<int64_t>(q) * k + s] = __uint_as_float(0x7F800000u);
+  }
+  if (kk == 0) return;
+  if (t == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_remaining = kk;
+    s_count = 0;
+  }
+  for (int pass = 0; pass < 8; ++pass) {
+    const int shift = 56 - 8 * pass;
+    for (int b = t; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    const uint64_t pfx = s_prefix, msk = s_mask;
+    for (int64_t i = t; i < n; i += blockDim.x) {
+      const uint64_t key = key_of(i);
+      if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (t == 0) {
+      int64_t cum = 0;
+      for (int b = 0; b < 256; ++b) {
+        if (cum + hist[b] >= s_remaining) {
+          s_prefix = pfx | (static_cast<uint64_t>(b) << shift);
+          s_mask = msk | (0xFFull << shift);
+          s_remaining -= cum;
+          break;
+        }
+        cum += hist[b];
+      }
+    }
+    __syncthreads();
+  }
+  const uint64_t kth = s_prefix;
+  for (int64_t i = t; i < n; i += blockDim.x) {
+    const uint64_t key = key_of(i);
+    if (key <= kth) {
+      const unsigned slot = atomicAdd(&s_count, 1u);
+      if (slot < static_cast<unsigned>(kMaxSearchK)) {
+        cand_key[slot] = key;
+        cand_idx[slot] = i;
+      }
+    }
+  }
+  __syncthreads();
+  if (s_count != static_cast<unsigned>(kk)) {  // repeated ranks: no total order
+    if (t == 0) atomicOr(err, kErrTieRank);
+    return;
+  }
+  for (int s = t; s < kk; s += blockDim.x) {
+    const uint64_t key = cand_key[s];
+    int pos = 0;
+    for (int j = 0; j < kk; ++j) pos += cand_key[j] < key;
+    out_idx[static_cast<int64_t>(q) * k + pos] = cand_idx[s];
+    out_dist[static_cast<int64_t>(q) * k + pos] = dq[cand_idx[s]];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, int kind, float* tau,
+                                        cudaStream_t s) {
+  if (dim <= 0) return cudaSuccess;
+  rows = rows < kThresholdSampleCap ? rows : kThresholdSampleCap;
+  if (kind == 0)
+    mean_threshold_kernel<<<(dim + 127) / 128, 128, 0, s>>>(v, rows, dim, tau);
+  else
+    median_threshold_kernel<<<(dim + 31) / 32, 32 * kMedWarps, 0, s>>>(v, rows, dim, tau);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_threshold_bits(const float* v, int64_t rows, int dim, const float* tau,
+                                       uint8_t* out, cudaStream_t s) {
+  const int64_t total = rows * ((dim + 7) / 8);
+  if (total <= 0) return cudaSuccess;
+  const int64_t blocks = (total + 255) / 256;
+  pack_threshold_bits_kernel<<<static_cast<unsigned>(blocks < 148 * 64 ? blocks : 148 * 64), 256, 0, s>>>(
+      v, rows, dim, tau, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_exact_search(const float* corpus, int64_t n, int dim, const uint32_t* tie_rank,
+                                const float* queries, int nq, int k, float* scratch, int64_t* out_idx,
+                                float* out_dist, int* err, cudaStream_t s) {
+  if (nq <= 0 || k <= 0) return cudaSuccess;
+  if (n > 0) {
+    const dim3 grid(static_cast<unsigned>((n + kDistRows - 1) / kDistRows), (nq + kDistQ - 1) / kDistQ);
+    cosine_distance_kernel<<<grid, kDistRows, 0, s>>>(corpus, n, dim, queries, nq, scratch);
+  }
+  topk_kernel<<<nq, kTopkThreads, 0, s>>>(scratch, n, tie_rank, k, out_idx, out_dist, err);
+  return cudaGetLastError();
+}
+
+}  // namespace jb

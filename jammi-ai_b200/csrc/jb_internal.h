@@ -11,8 +11,10 @@
 namespace jb {
 
 // Device error flag bits (atomicOr into a caller-owned int): 1 = a bounded
-// wait gave up, 2 = token id out of range, 4 = row length above max_seq.
+// wait gave up, 2 = token id out of range, 4 = row length above max_seq,
+// 8 = exact search given repeated tie ranks.
 constexpr int kErrTimeout = 1;
+constexpr int kErrTieRank = 8;
 
 // y = epi(A[M,K] . W[N,K]^T (+ bias)) with an optional residual; see
 // jb_op_linear / jb_op_linear_s8 for the meaning of every field.
@@ -96,6 +98,19 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
                              std::string* why,
                              int rows_cap = 0, int* err = nullptr, int causal = 0,
                              int* work = nullptr);
+
+// ANN sidecar vector formats and exact search (jb_index.cu).
+constexpr int64_t kThresholdSampleCap = 100000;  // rows a binary threshold is fit over
+constexpr int kMaxSearchK = 1024;
+cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, int kind, float* tau,
+                                        cudaStream_t s);
+cudaError_t launch_pack_threshold_bits(const float* v, int64_t rows, int dim, const float* tau,
+                                       uint8_t* out, cudaStream_t s);
+// scratch: f32 [nq, n]; out_idx / out_dist [nq, k]; repeated tie ranks set
+// kErrTieRank in *err.
+cudaError_t launch_exact_search(const float* corpus, int64_t n, int dim, const uint32_t* tie_rank,
+                                const float* queries, int nq, int k, float* scratch, int64_t* out_idx,
+                                float* out_dist, int* err, cudaStream_t s);
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s);

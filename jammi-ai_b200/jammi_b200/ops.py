@@ -136,3 +136,42 @@ def set_attention_tcgen05(on: bool):
     """``jb_set_attention_tcgen05``: rows of <= 256 keys on the tcgen05 attention
     kernel (process-wide; off by default)."""
     lib().jb_set_attention_tcgen05(1 if on else 0)
+
+
+THRESHOLD_KINDS = {"mean": 0, "median": 1}
+
+
+def fit_binary_threshold(vectors: torch.Tensor, kind: str = "median") -> torch.Tensor:
+    """Per-dimension threshold tau of a Binary sidecar over the first
+    min(rows, 100000) rows of f32 ``vectors`` [rows, dim] ("mean" or "median")."""
+    _contig(vectors)
+    rows, dim = vectors.shape
+    tau = torch.empty(dim, dtype=torch.float32, device=vectors.device)
+    check(lib().jb_op_fit_binary_threshold(_p(vectors), rows, dim, THRESHOLD_KINDS[kind], _p(tau), _s(vectors)))
+    return tau
+
+
+def pack_threshold_bits(vectors: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
+    """uint8 [rows, ceil(dim / 8)]: bit i = vectors[:, i] > tau[i], LSB-first."""
+    _contig(vectors, tau)
+    rows, dim = vectors.shape
+    out = torch.empty((rows, (dim + 7) // 8), dtype=torch.uint8, device=vectors.device)
+    check(lib().jb_op_pack_threshold_bits(_p(vectors), rows, dim, _p(tau), _p(out), _s(vectors)))
+    return out
+
+
+def exact_search(corpus: torch.Tensor, queries: torch.Tensor, k: int, tie_rank=None):
+    """Exact cosine search: (idx int64 [q, min(k, n)], dist f32 [q, min(k, n)])
+    in ascending (distance, tie rank) order; ``tie_rank`` int32/uint32 [n]
+    (distinct) or None for row order.  Synchronises to surface input errors."""
+    _contig(corpus, queries, tie_rank)
+    n, dim = corpus.shape
+    nq = queries.shape[0]
+    scratch = torch.empty((nq, n), dtype=torch.float32, device=corpus.device)
+    idx = torch.empty((nq, k), dtype=torch.int64, device=corpus.device)
+    dist = torch.empty((nq, k), dtype=torch.float32, device=corpus.device)
+    check(lib().jb_op_exact_search(_p(corpus), n, dim, _p(tie_rank), _p(queries), nq, k, _p(scratch),
+                                   _p(idx), _p(dist), _s(corpus)))
+    sync(corpus.device)
+    kk = min(k, n)
+    return idx[:, :kk], dist[:, :kk]
