@@ -194,3 +194,15 @@ def test_many_texts_threads_keep_order(tmp_path):
     got = Tokenizer(path)(texts)
     assert [list(g) for g in got] == [e.ids for e in hf.encode_batch(texts)]
     assert all(isinstance(g, np.ndarray) for g in got[:3])
+
+
+def test_escaped_astral_added_token(tmp_path):
+    """A tokenizer.json written with \\u escapes spells characters outside
+    the BMP as surrogate pairs; they decode to the one character."""
+    from tokenizers import AddedToken
+    from jammi_b200 import Tokenizer
+    hf = build_byte_level(tmp_path)
+    hf.add_tokens([AddedToken("😀🚀", normalized=False, special=True)])
+    hf, path = save(hf, tmp_path / "tok.json", edit=lambda doc: None)
+    assert "\\ud83d" in open(path).read()
+    assert_same(Tokenizer(path), hf, ["a😀🚀b", "😀 🚀", "x 😀🚀😀🚀"])
