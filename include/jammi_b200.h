@@ -350,6 +350,19 @@ typedef int (*jb_forward_cb)(void* user, int64_t start, int64_t count, char* msg
 jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, void* user);
 int jb_is_oom_message(const char* msg);
 
+/* ── pooling declared by a checkpoint (host) ──────────────────────────────
+ * pooling_from_config (crates/jammi-ai/src/model/backend/candle.rs:440-538):
+ * the JB_POOL_* strategy a sentence-transformers 1_Pooling/config.json
+ * declares.  jb_pooling_from_config takes the file's text (NULL: no file ->
+ * JB_POOL_MEAN); jb_pooling_from_model_dir reads <dir>/1_Pooling/config.json
+ * (absent -> JB_POOL_MEAN; read_local_pooling_config, crates/jammi-ai/src/
+ * model/resolver.rs:473-500).  The true pooling_mode_* flags must all name
+ * one representable strategy (mean_sqrt_len_tokens counts as mean);
+ * anything else answers JB_ERR_INVALID (JB_ERR_IO: present but unreadable),
+ * never a silent mean. */
+jb_status jb_pooling_from_config(const char* pooling_config_json, int* pooling);
+jb_status jb_pooling_from_model_dir(const char* model_dir, int* pooling);
+
 /* ── ANN sidecar vector formats and exact search (device) ─────────────────
  * The vector side of the reference's index module on device buffers.
  * jb_op_fit_binary_threshold: the per-dimension threshold tau a Binary

@@ -348,11 +348,34 @@ def pack_rgb8(images):
     return buf, offs, ws, hs
 
 
+POOLING_NAMES = {v: k for k, v in POOLING.items()}
+
+
+def pooling_from_config(cfg=None) -> str:
+    """The pooling a 1_Pooling/config.json declares (``jb_pooling_from_config``):
+    ``cfg`` is the file's JSON text or parsed dict, None when there is no file."""
+    import ctypes
+    out = ctypes.c_int()
+    text = None if cfg is None else (cfg if isinstance(cfg, str) else json.dumps(cfg)).encode()
+    check(lib().jb_pooling_from_config(text, ctypes.byref(out)))
+    return POOLING_NAMES[out.value]
+
+
+def pooling_from_model_dir(model_dir: str) -> str:
+    """``jb_pooling_from_model_dir``: <model_dir>/1_Pooling/config.json, mean if absent."""
+    import ctypes
+    out = ctypes.c_int()
+    check(lib().jb_pooling_from_model_dir(str(model_dir).encode(), ctypes.byref(out)))
+    return POOLING_NAMES[out.value]
+
+
 def load_model(weights_path: str, config_path_or_dict, device: int = 0, fmt: str = "bf16",
-               pooling: str = "mean", tower: str = "vision"):
+               pooling: str | None = None, tower: str = "vision"):
     """``CandleBackend::load`` for the BERT and OpenCLIP arms: the family is
     detected from the config (``model_cfg`` -> OpenCLIP); an OpenCLIP checkpoint
-    holds both towers, ``tower`` ("vision" or "text") picks one."""
+    holds both towers, ``tower`` ("vision" or "text") picks one.  A text
+    encoder's pooling defaults to what the checkpoint directory's
+    1_Pooling/config.json declares (mean without one)."""
     cfg = config_path_or_dict
     if isinstance(cfg, str) and os.path.exists(cfg):
         cfg = json.load(open(cfg))
@@ -362,4 +385,6 @@ def load_model(weights_path: str, config_path_or_dict, device: int = 0, fmt: str
         if tower == "text":
             return OpenClipText(weights_path, cfg, device, fmt)
         return OpenClipVisionTransformer(weights_path, cfg, device, fmt)
+    if pooling is None:
+        pooling = pooling_from_model_dir(os.path.dirname(os.path.abspath(weights_path)))
     return Bert(weights_path, cfg, device, fmt, pooling=pooling)
