@@ -199,4 +199,9 @@ def embed_texts(models, texts, tokenize, chunk_rows: int = 65536, **kw):
     if not outs:
         return np.zeros((0, H), np.float32), np.zeros(0, np.uint8), stats
     bits = np.concatenate(valid)
+    if bits.size and not bits.any():
+        # the all-invalid guard of EmbeddingPipeline::run (embedding.rs:204-230):
+        # a job whose every row is empty produces no table, loudly
+        raise JbError(L.ERR_INVALID, "embedding generation produced no embeddings: every input row "
+                                     "was empty or invalid (no valid content to embed)")
     return np.concatenate(outs), np.packbits(bits, bitorder="little"), stats

@@ -230,3 +230,30 @@ def test_embed_texts_with_the_library_tokenizer(monkeypatch, tmp_path):
     ids = np.concatenate([v for v, _ in seen])
     want = np.concatenate([np.array(e.ids, np.uint32) for e in hf.encode_batch(texts)])
     assert np.array_equal(ids, want)
+
+
+def test_embed_texts_all_invalid_rows_fail_loudly(monkeypatch):
+    """EmbeddingPipeline::run's all-invalid guard (embedding.rs:204-230): every
+    row empty -> an error, not a silently empty result; one valid row is
+    enough to succeed (the empty ones stay null)."""
+    import numpy as np
+    from jammi_b200 import driver as D
+    from jammi_b200._lib import JbError
+
+    def fake_generate(models, values, offsets, **kw):
+        rows = offsets.size - 1
+        lens = np.diff(offsets.astype(np.int64))
+        bits = np.packbits((lens > 0).astype(np.uint8), bitorder="little")
+        return np.zeros((rows, 4), np.float32), bits, {"rows": rows}
+
+    monkeypatch.setattr(D, "generate_embeddings", fake_generate)
+
+    class M:
+        class info:
+            hidden = 4
+            output_dim = 4
+    with pytest.raises(JbError, match="no embeddings"):
+        D.embed_texts([M()], ["", "", ""], lambda ts: [[] for _ in ts], chunk_rows=2)
+    out, valid, _ = D.embed_texts([M()], ["", "x", ""], lambda ts: [[7] if t else [] for t in ts], chunk_rows=2)
+    assert np.unpackbits(valid, bitorder="little")[:3].tolist() == [0, 1, 0]
+    assert D.embed_texts([M()], [], lambda ts: [], chunk_rows=2)[0].shape == (0, 4)
