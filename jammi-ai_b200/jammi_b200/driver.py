@@ -183,14 +183,33 @@ def generate_embeddings_stream(models, row_chunks, **kw):
 def embed_texts(models, texts, tokenize, chunk_rows: int = 65536, **kw):
     """Embeddings of ``texts`` in order: ``tokenize(list_of_texts)`` returns one
     token-id sequence per text (e.g. a wrapped HF tokenizer's ``input_ids``,
-    [CLS] ... [SEP], truncated to the model's max_seq); it runs on a producer
-    thread one chunk ahead of the devices.  Returns (out f32 [rows, H],
-    validity bitmap, list of per-chunk stats)."""
+    [CLS] ... [SEP]); it runs on a producer thread one chunk ahead of the
+    devices.  As ``CandleModel::forward_embedding`` (candle.rs:764-856): an
+    empty or None text is a null row (zero vector, validity 0) and never
+    reaches the tokenizer, and a library ``Tokenizer`` without its own
+    max_length truncates to the model's max sequence length (a caller's own
+    callable must truncate itself).  Returns (out f32 [rows, H], validity
+    bitmap, list of per-chunk stats)."""
     if chunk_rows <= 0:
         raise ValueError("chunk_rows must be positive")
     texts = list(texts)
     H = models[0].info.output_dim
-    chunks = (tokenize(texts[i:i + chunk_rows]) for i in range(0, len(texts), chunk_rows))
+    from .tokenizer import Tokenizer
+    if isinstance(tokenize, Tokenizer) and tokenize.max_length <= 0:
+        max_seq = int(models[0].info.max_seq)
+        base = tokenize
+        tokenize = lambda ts: base(ts, max_length=max_seq)  # noqa: E731
+
+    def tokenize_valid(chunk):
+        keep = [i for i, t in enumerate(chunk)
+                if t is not None and not (isinstance(t, (str, bytes)) and len(t) == 0)]
+        seqs = tokenize([chunk[i] for i in keep]) if keep else []
+        rows = [[] for _ in chunk]
+        for i, seq in zip(keep, seqs):
+            rows[i] = seq
+        return rows
+
+    chunks = (tokenize_valid(texts[i:i + chunk_rows]) for i in range(0, len(texts), chunk_rows))
     outs, valid, stats = [], [], []
     for out, validity, st in generate_embeddings_stream(models, chunks, **kw):
         outs.append(out)

@@ -11,6 +11,7 @@ import ctypes
 
 import numpy as np
 
+from . import _lib as L
 from ._lib import check, lib
 
 
@@ -53,11 +54,18 @@ class Tokenizer:
         sizes = np.array([len(e) for e in enc], dtype=np.uint64)
         offsets = np.zeros(n + 1, dtype=np.uint64)
         ml = self.max_length if max_length is None else int(max_length)
-        check(lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
-                                None, 0, offsets.ctypes.data))
-        ids = np.zeros(max(int(offsets[-1]), 1), dtype=np.uint32)
-        check(lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
-                                ids.ctypes.data, ids.size, offsets.ctypes.data))
+        # One pass in the common case: a token covers at least one byte, so
+        # bytes + a few ids per text (specials, a prefix space) bound the
+        # output; a text dense in added tokens may need the exact-size retry.
+        cap = int(sizes.sum()) + 4 * n + 64
+        ids = np.empty(cap, dtype=np.uint32)
+        st = lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                               ids.ctypes.data, cap, offsets.ctypes.data)
+        if st != L.OK and int(offsets[-1]) > cap:
+            ids = np.empty(int(offsets[-1]), dtype=np.uint32)
+            st = lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                                   ids.ctypes.data, ids.size, offsets.ctypes.data)
+        check(st)
         return ids[: int(offsets[-1])], offsets
 
     def __call__(self, texts, max_length: int | None = None):

@@ -217,7 +217,8 @@ def test_embed_texts_with_the_library_tokenizer(monkeypatch, tmp_path):
     def fake_generate(models, values, offsets, **kw):
         seen.append((values.copy(), offsets.copy()))
         rows = offsets.size - 1
-        return np.zeros((rows, 4), np.float32), np.full((rows + 7) // 8, 0xFF, np.uint8), {"rows": rows}
+        bits = np.packbits((np.diff(offsets.astype(np.int64)) > 0).astype(np.uint8), bitorder="little")
+        return np.zeros((rows, 4), np.float32), bits, {"rows": rows}
 
     monkeypatch.setattr(D, "generate_embeddings", fake_generate)
 
@@ -225,11 +226,16 @@ def test_embed_texts_with_the_library_tokenizer(monkeypatch, tmp_path):
         class info:
             hidden = 4
             output_dim = 4
-    texts = ["hello world", "naïve café", "", "東京"]
-    D.embed_texts([M()], texts, Tokenizer(path), chunk_rows=3)
+            max_seq = 6
+    texts = ["hello world", "naïve café", "", "東京", None, "a b c d e f g h"]
+    _, valid, _ = D.embed_texts([M()], texts, Tokenizer(path), chunk_rows=3)
     ids = np.concatenate([v for v, _ in seen])
-    want = np.concatenate([np.array(e.ids, np.uint32) for e in hf.encode_batch(texts)])
+    # empty / None texts are null rows that never reach the tokenizer; the
+    # rest are truncated to the model's max_seq (candle.rs:779-806)
+    hf.enable_truncation(max_length=6)
+    want = np.concatenate([np.array(e.ids, np.uint32) for e in hf.encode_batch([t for t in texts if t])])
     assert np.array_equal(ids, want)
+    assert np.unpackbits(valid, bitorder="little")[:6].tolist() == [1, 1, 0, 1, 0, 1]
 
 
 def test_embed_texts_all_invalid_rows_fail_loudly(monkeypatch):
