@@ -263,3 +263,27 @@ def test_embed_texts_all_invalid_rows_fail_loudly(monkeypatch):
     out, valid, _ = D.embed_texts([M()], ["", "x", ""], lambda ts: [[7] if t else [] for t in ts], chunk_rows=2)
     assert np.unpackbits(valid, bitorder="little")[:3].tolist() == [0, 1, 0]
     assert D.embed_texts([M()], [], lambda ts: [], chunk_rows=2)[0].shape == (0, 4)
+
+
+def test_embed_images_null_rows():
+    """forward_image_embedding's row rules (candle.rs:880-893): a null image is
+    a null row that never reaches the device; the rest keep their order."""
+    import numpy as np
+    from jammi_b200 import driver as D
+    seen = []
+
+    class M:
+        class info:
+            output_dim = 3
+
+        def encode_rgb8(self, imgs):
+            seen.append(len(imgs))
+            return np.array([[im.shape[0], im.shape[1], 1.0] for im in imgs], np.float32)
+    imgs = [np.zeros((2, 5, 3), np.uint8), None, np.zeros((7, 1, 3), np.uint8), None,
+            np.zeros((4, 4, 3), np.uint8)]
+    out, valid = D.embed_images(M(), imgs, batch_rows=2)
+    assert seen == [2, 1]
+    assert out.tolist() == [[2, 5, 1], [0, 0, 0], [7, 1, 1], [0, 0, 0], [4, 4, 1]]
+    assert np.unpackbits(valid, bitorder="little")[:5].tolist() == [1, 0, 1, 0, 1]
+    out, valid = D.embed_images(M(), [None, None])
+    assert not out.any() and seen == [2, 1]

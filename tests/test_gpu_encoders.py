@@ -559,3 +559,21 @@ def test_encode_rgb8_matches_preprocessed_pixels():
         assert np.array_equal(model.encode_rgb8(imgs), model.forward_image(px))
     with pytest.raises(Exception):
         model.encode_rgb8([np.zeros((0, 4, 3), np.uint8)])
+
+
+def test_embed_images_null_rows_match_direct_calls():
+    """driver.embed_images: null images are zero rows with validity 0, the
+    others equal jb_encode_image_rgb8 on the same images, bit for bit."""
+    from oracle import image as oimg
+    from jammi_b200 import OpenClipVisionTransformer
+    from jammi_b200.driver import embed_images
+    w, g = load_golden("tiny_clip_cls.npz")
+    cfg = json.loads(bytes(g["config_json"]).decode())
+    model = OpenClipVisionTransformer.from_weights(w, cfg, device=0, fmt="f32")
+    imgs = oimg.random_images(5, [(40, 20), (8, 8), (3, 11), (100, 100), (9, 64)])
+    rows = [imgs[0], None, imgs[1], imgs[2], None, imgs[3], imgs[4]]
+    out, valid = embed_images(model, rows, batch_rows=2)
+    want = model.encode_rgb8(imgs)
+    assert np.array_equal(out[[0, 2, 3, 5, 6]], want)
+    assert not out[[1, 4]].any()
+    assert np.unpackbits(valid, bitorder="little")[:7].tolist() == [1, 0, 1, 1, 0, 1, 1]
