@@ -234,9 +234,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                device_id=dev)
+        from jammi_b200.sharding import init_replica_group
+        init_replica_group("nccl", timeout_s=180.0, device_id=dev)
 
     def barrier():
         if world > 1:

@@ -8,6 +8,20 @@ barrier and the max-reduction of each rank's device time.
 from __future__ import annotations
 
 
+def init_replica_group(backend: str, timeout_s: float = 180.0, device_id=None) -> None:
+    """The job's one process group, with a short timeout: a rank that died or
+    never joined ends the others' next collective (or the rendezvous) with an
+    error instead of a hang.  The replicas exchange nothing but a barrier and
+    a max of timings, so no legitimate wait comes near the limit."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    kw = {"timeout": timedelta(seconds=timeout_s)}
+    if device_id is not None:
+        kw["device_id"] = device_id
+    dist.init_process_group(backend, **kw)
+
+
 def shard_batches(n_batches: int, rank: int, world: int) -> list[int]:
     """Round-robin: the batch indices rank `rank` of `world` processes."""
     if not (0 <= rank < world):

@@ -51,3 +51,52 @@ def test_two_rank_sharding_and_max_time():
     assert gathered[0] == [0, 2, 4, 6, 8] and gathered[1] == [1, 3, 5, 7]
     assert t == 2.5, "timing is the max over ranks"
     assert rate == pytest.approx(5 * 2 / 2.5)
+
+
+def _failing_worker(rank, world, port, mode, q):
+    import sys
+    import time
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "jammi-ai_b200"))
+    import torch.distributed as dist
+    from jammi_b200.sharding import init_replica_group, max_over_ranks
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    if rank == 1 and mode == "never_joins":
+        time.sleep(8)
+        return
+    t0 = time.monotonic()
+    try:
+        init_replica_group("gloo", timeout_s=3.0)
+        if rank == 1:  # dies between steps, nothing in flight
+            os._exit(1)
+        max_over_ranks(1.0)
+        dist.barrier()
+        q.put((rank, "no error", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, type(e).__name__, time.monotonic() - t0))
+
+
+@pytest.mark.parametrize("mode", ["dies_after_init", "never_joins"])
+def test_lost_rank_ends_the_others_with_an_error(mode):
+    """Failure detection on the host: a rank that exits between steps, or
+    never joins, makes rank 0's next collective (or the rendezvous) raise
+    within the group's short timeout instead of hanging."""
+    import queue as pyqueue
+
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        rank, outcome, dt = q.get(timeout=60)
+    except pyqueue.Empty:
+        outcome, dt, rank = "hang", None, 0
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and outcome != "no error" and outcome != "hang", outcome
+    assert dt < 30
