@@ -261,6 +261,12 @@ void jb_set_attention_tcgen05(int on);
  * flag shared by the single-op entry points: JB_ERR_TIMEOUT if a bounded
  * device-side wait gave up in an earlier op. */
 jb_status jb_op_sync(void* stream);
+/* A bounded device-side wait (one thread, %globaltimer): until *d_flag ==
+ * expect, at most limit_ms (<= 2000).  On expiry the next jb_op_sync answers
+ * JB_ERR_TIMEOUT and the context stays usable -- the same limit-then-report
+ * rule as every spin inside the library's kernels, as an op that exercises
+ * failure detection without a fault.  No reference counterpart. */
+jb_status jb_op_wait_flag(const int* d_flag, int expect, int limit_ms, void* stream);
 /* pool_and_normalize over packed hidden [T, H] (dtype F32/BF16) with
  * cu_seqlens [batch+1]: out f32 [batch, H] (pooling.rs:31-148). */
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens,

@@ -557,6 +557,14 @@ jb_status jb_op_attention_rows(const void* qkv, const int* cu_seqlens, void* ctx
                       stream, rows);
 }
 
+jb_status jb_op_wait_flag(const int* d_flag, int expect, int limit_ms, void* stream) {
+  return guarded([&] {
+    if (!d_flag || limit_ms < 0 || limit_ms > 2000) jb::fail(JB_ERR_INVALID, "jb_op_wait_flag: bad argument");
+    jb::check_cuda(jb::launch_flag_wait(d_flag, expect, limit_ms, op_flag(current_device()), as_stream(stream)),
+                   "jb_op_wait_flag");
+  });
+}
+
 jb_status jb_op_fit_binary_threshold(const float* d_vectors, int64_t rows, int dim, int kind, float* d_tau,
                                      void* stream) {
   return guarded([&] {

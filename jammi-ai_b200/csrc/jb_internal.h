@@ -99,6 +99,10 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
                              int rows_cap = 0, int* err = nullptr, int causal = 0,
                              int* work = nullptr);
 
+// Bounded wait of one thread until *flag == expect, at most limit_ms; on
+// expiry kErrTimeout in *err (jb_wait.cu).
+cudaError_t launch_flag_wait(const int* flag, int expect, int limit_ms, int* err, cudaStream_t s);
+
 // ANN sidecar vector formats and exact search (jb_index.cu).
 constexpr int64_t kThresholdSampleCap = 100000;  // rows a binary threshold is fit over
 constexpr int kMaxSearchK = 1024;

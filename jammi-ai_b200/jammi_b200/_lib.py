@@ -89,6 +89,7 @@ _SIGS = [
     ("jb_op_attention_rows", _I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     ("jb_set_attention_tcgen05", None, [_I]),
     ("jb_op_pool_normalize", _I, [_P, _I, _P, _P, _I, _I, _I, _P]),
+    ("jb_op_wait_flag", _I, [_P, _I, _I, _P]),
     ("jb_pooling_from_config", _I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]),
     ("jb_pooling_from_model_dir", _I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]),
     ("jb_op_fit_binary_threshold", _I, [_P, ctypes.c_int64, _I, _I, _P, _P]),

@@ -138,6 +138,14 @@ def set_attention_tcgen05(on: bool):
     lib().jb_set_attention_tcgen05(1 if on else 0)
 
 
+def wait_flag(flag: torch.Tensor, expect: int, limit_ms: int):
+    """``jb_op_wait_flag``: a bounded device-side wait until flag[0] == expect;
+    on expiry the next ``sync`` raises JbError (JB_ERR_TIMEOUT)."""
+    if flag.dtype != torch.int32 or flag.numel() < 1:
+        raise ValueError("flag must be an int32 tensor")
+    check(lib().jb_op_wait_flag(_p(flag), int(expect), int(limit_ms), _s(flag)))
+
+
 THRESHOLD_KINDS = {"mean": 0, "median": 1}
 
 

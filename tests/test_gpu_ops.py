@@ -398,3 +398,26 @@ def test_preprocess_rgb8_bit_exact(dev):
     # a small target (the tiny fixtures' 8 x 8) with a large downscale ratio
     got8 = ops.preprocess_rgb8(imgs[:3], 8, (0.5, 0.5, 0.5), (0.25, 0.25, 0.25), device=dev).cpu().numpy()
     assert np.array_equal(got8, oimg.preprocess_image_batch(imgs[:3], 8, (0.5,) * 3, (0.25,) * 3))
+
+
+def test_bounded_wait_runs_out_and_the_context_stays_usable(dev):
+    """Failure detection without a fault: a device-side wait on a flag that
+    nothing sets gives up at its limit and reports JB_ERR_TIMEOUT through
+    jb_op_sync; a satisfied wait reports nothing, and later ops run."""
+    import time
+    from jammi_b200 import _lib as L
+    ops = _ops()
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    t0 = time.monotonic()
+    ops.wait_flag(flag, 1, 200)
+    with pytest.raises(L.JbError) as e:
+        ops.sync(dev)
+    assert e.value.status == L.ERR_TIMEOUT
+    assert time.monotonic() - t0 < 10
+    flag.fill_(1)
+    ops.wait_flag(flag, 1, 200)
+    ops.sync(dev)
+    x = torch.randn(64, 768, device=dev, dtype=torch.bfloat16)
+    q, s = ops.quantize_rows(x)
+    torch.cuda.synchronize()
+    assert q.shape == (64, 768) and bool(torch.isfinite(s).all())
