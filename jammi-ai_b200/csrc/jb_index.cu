@@ -289,13 +289,18 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
     if (t == 0) atomicOr(err, kErrTieRank);
     return;
   }
+  bool dup = false;
   for (int s = t; s < kk; s += blockDim.x) {
     const uint64_t key = cand_key[s];
     int pos = 0;
-    for (int j = 0; j < kk; ++j) pos += cand_key[j] < key;
+    for (int j = 0; j < kk; ++j) {
+      pos += cand_key[j] < key || (cand_key[j] == key && j < s);  // a permutation even with repeats
+      dup |= j != s && cand_key[j] == key;
+    }
     out_idx[static_cast<int64_t>(q) * k + pos] = cand_idx[s];
     out_dist[static_cast<int64_t>(q) * k + pos] = dq[cand_idx[s]];
   }
+  if (dup) atomicOr(err, kErrTieRank);  // repeated ranks inside the k: their order is arbitrary
 }
 
 }  // namespace

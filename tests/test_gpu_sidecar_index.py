@@ -115,3 +115,13 @@ def test_exact_search_rejects_repeated_tie_ranks(dev):
     # the flag is cleared: the next search runs clean
     idx, _ = _ops().exact_search(corpus, corpus[:1].clone(), 5)
     assert idx.cpu().tolist() == [[0, 1, 2, 3, 4]]
+
+
+def test_exact_search_rejects_repeated_tie_ranks_inside_k(dev):
+    """Equal distances with equal ranks inside the k best have no order: an
+    error, and every output slot is still written (no stale values)."""
+    from jammi_b200._lib import JbError
+    corpus = torch.ones((3, 8), device=dev)
+    with pytest.raises(JbError):
+        _ops().exact_search(corpus, corpus[:1].clone(), 3,
+                            tie_rank=torch.zeros(3, dtype=torch.int32, device=dev))
