@@ -230,14 +230,17 @@ def embed_images(model, images, batch_rows: int = 512):
     """``CandleModel::forward_image_embedding`` (candle.rs:858-937) over decoded
     RGB8 images (``[h, w, 3]`` uint8 arrays, preprocessing on the device): a
     None entry (a null image) is a null row -- zero vector, validity 0 -- and
-    never reaches the device.  Returns (out f32 [rows, embed_dim], validity
-    bitmap)."""
+    never reaches the device; a job of only null images is an error.  Returns
+    (out f32 [rows, embed_dim], validity bitmap)."""
     if batch_rows <= 0:
         raise ValueError("batch_rows must be positive")
     images = list(images)
     out = np.zeros((len(images), model.info.output_dim), np.float32)
     valid = np.zeros(len(images), np.uint8)
     keep = [i for i, im in enumerate(images) if im is not None]
+    if images and not keep:  # EmbeddingPipeline::run's all-invalid guard (embedding.rs:204-230)
+        raise JbError(L.ERR_INVALID, "embedding generation produced no embeddings: every input row "
+                                     "was empty or invalid (no valid content to embed)")
     for s in range(0, len(keep), batch_rows):
         idx = keep[s:s + batch_rows]
         out[idx] = model.encode_rgb8([images[i] for i in idx])

@@ -285,5 +285,8 @@ def test_embed_images_null_rows():
     assert seen == [2, 1]
     assert out.tolist() == [[2, 5, 1], [0, 0, 0], [7, 1, 1], [0, 0, 0], [4, 4, 1]]
     assert np.unpackbits(valid, bitorder="little")[:5].tolist() == [1, 0, 1, 0, 1]
-    out, valid = D.embed_images(M(), [None, None])
-    assert not out.any() and seen == [2, 1]
+    from jammi_b200._lib import JbError
+    with pytest.raises(JbError, match="no embeddings"):
+        D.embed_images(M(), [None, None])
+    assert seen == [2, 1]
+    assert D.embed_images(M(), [])[0].shape == (0, 3)
