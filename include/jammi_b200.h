@@ -401,8 +401,10 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
  * A model's tokenizer.json through the HuggingFace `tokenizers` pipeline the
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
  * tokenizer.rs:21-78): added tokens (normalized / lstrip / rstrip /
- * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase (and
- * Sequences), pre-tokenisers BertPreTokenizer and ByteLevel, models WordPiece
+ * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase,
+ * StripAccents, Strip, Prepend, Replace (string patterns) and Sequences,
+ * pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace, WhitespaceSplit,
+ * Punctuation, Digits and Sequences, models WordPiece
  * and BPE (byte-level or character-level: unknown token, fuse_unk,
  * byte_fallback, subword prefix / suffix, ignore_merges), post-processors
  * TemplateProcessing, BertProcessing, RobertaProcessing, ByteLevel (and

@@ -18,14 +18,22 @@
 //                  handle_chinese_chars (spaces around CJK ideographs),
 //                  strip_accents (NFD, then drop category Mn; on by default
 //                  when lowercase is), lowercase (one code point at a time);
-//                  NFC, NFD, Lowercase, and Sequences of these;
-//   pre-tokeniser  BertPreTokenizer: split on White_Space, each punctuation
+//                  NFC, NFD, Lowercase, StripAccents (drop category M*, no
+//                  decomposition of its own), Strip, Prepend (non-empty
+//                  pieces), Replace (string patterns), and Sequences;
+//   pre-tokeniser  (a Sequence applies its steps in order, each to the words
+//                  the previous one produced)
+//                  BertPreTokenizer: split on White_Space, each punctuation
 //                  character (ASCII punctuation or category P*) a word of its
 //                  own; ByteLevel: an optional leading space (add_prefix_space,
 //                  per piece), the GPT-2 regex ('s 't 're 've 'm 'll 'd,
 //                  ' ?' + letters / numbers / other, whitespace runs that
 //                  leave their last space to the next word), each word's
 //                  UTF-8 bytes mapped to the byte-symbol alphabet below;
+//                  Whitespace: the matches of \w+|[^\w\s]+; WhitespaceSplit;
+//                  Punctuation with its split behaviour (isolated, removed,
+//                  merged with the previous / next word, contiguous); Digits
+//                  (each digit, or digit runs);
 //                  OpenCLIP's regex (the special-token literals, the
 //                  contractions, letter runs, single digits, runs of other
 //                  non-space characters; the spans between matches are words
@@ -97,19 +105,30 @@ struct AddedSet {
   }
 };
 
-enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower };
-enum PreTok { kPreNone, kPreBert, kPreByteLevel, kPreClip };
+enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace };
+struct NormStep {
+  int op = kNormBert;
+  bool left = false, right = false;  // Strip
+  std::vector<uint32_t> a, b;        // Prepend: a; Replace: a -> b
+};
+enum PreKind { kPreBert, kPreByteLevel, kPreClip, kPreWhitespace, kPreWhitespaceSplit, kPrePunctuation, kPreDigits };
+enum Behavior { kIsolated, kRemoved, kMergedWithPrevious, kMergedWithNext, kContiguous };
+struct PreStep {
+  int kind = kPreBert;
+  bool add_prefix_space = false, use_regex = true;  // ByteLevel
+  int behavior = kIsolated;                         // Punctuation
+  bool individual_digits = false;                   // Digits
+};
 
 }  // namespace
 }  // namespace jb
 
 struct jb_tokenizer {
   bool wordpiece = true;  // else BPE
-  // normaliser: applied in order
-  std::vector<int> norm;
+  // normaliser and pre-tokeniser steps, applied in order
+  std::vector<jb::NormStep> norm;
   bool clean_text = true, handle_chinese = true, strip_accents = true, lowercase = true;
-  int pre = jb::kPreBert;
-  bool add_prefix_space = false, use_regex = true;
+  std::vector<jb::PreStep> pre;
   std::unordered_map<std::string, uint32_t> vocab;
   bool has_unk = false;
   uint32_t unk_id = 0;
@@ -367,14 +386,48 @@ void bert_normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
   if (t.lowercase) lowercase_cps(cps);
 }
 
+void replace_all(std::vector<uint32_t>& cps, const std::vector<uint32_t>& pat, const std::vector<uint32_t>& with) {
+  if (pat.empty() || cps.size() < pat.size()) return;
+  std::vector<uint32_t> out;
+  size_t i = 0;
+  while (i < cps.size()) {
+    if (i + pat.size() <= cps.size() && std::equal(pat.begin(), pat.end(), cps.begin() + i)) {
+      out.insert(out.end(), with.begin(), with.end());
+      i += pat.size();
+    } else {
+      out.push_back(cps[i++]);
+    }
+  }
+  cps.swap(out);
+}
+
 void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
   std::vector<uint32_t> tmp;
-  for (int op : t.norm) {
-    switch (op) {
+  for (const NormStep& st : t.norm) {
+    switch (st.op) {
       case kNormBert: bert_normalize(t, cps); break;
       case kNormNfc: nfc(cps, tmp); cps.swap(tmp); break;
       case kNormNfd: nfd(cps, tmp); cps.swap(tmp); break;
       case kNormLower: lowercase_cps(cps); break;
+      case kNormStripAccents:  // every combining mark (category M*), no decomposition first
+        tmp.clear();
+        for (uint32_t c : cps)
+          if (!in_table(uni::kMark, c)) tmp.push_back(c);
+        cps.swap(tmp);
+        break;
+      case kNormStrip: {
+        size_t b = 0, e = cps.size();
+        if (st.left)
+          while (b < e && is_whitespace(cps[b])) ++b;
+        if (st.right)
+          while (e > b && is_whitespace(cps[e - 1])) --e;
+        cps = std::vector<uint32_t>(cps.begin() + b, cps.begin() + e);
+        break;
+      }
+      case kNormPrepend:
+        if (!cps.empty()) cps.insert(cps.begin(), st.a.begin(), st.a.end());
+        break;
+      case kNormReplace: replace_all(cps, st.a, st.b); break;
     }
   }
 }
@@ -546,63 +599,139 @@ size_t gpt2_match(const std::vector<uint32_t>& c, size_t i) {
   return j - 1 - i;  // the last space goes to the next word
 }
 
-void pre_tokenize_and_model(const jb_tokenizer& t, const std::string& piece, std::vector<uint32_t>& ids) {
-  std::vector<uint32_t> c;
-  decode_utf8(piece.data(), piece.size(), c);
-  if (c.empty()) return;
-  std::vector<uint32_t> word;
-  switch (t.pre) {
-    case kPreNone:
-      model(t, c, ids);
-      return;
-    case kPreBert:
-      for (uint32_t x : c) {
-        if (is_whitespace(x)) {
-          model(t, word, ids);
-          word.clear();
-        } else if (is_punct(x)) {
-          model(t, word, ids);
-          word.assign(1, x);
-          model(t, word, ids);
-          word.clear();
-        } else {
-          word.push_back(x);
-        }
+using Words = std::vector<std::vector<uint32_t>>;
+
+// The crate's split of one word on a per-character predicate: each matching
+// character is a delimiter, kept, dropped or merged by `behavior`.
+template <typename Pred>
+void split_chars(const std::vector<uint32_t>& w, Pred is_delim, int behavior, Words& out) {
+  struct Seg {
+    size_t b, e;
+    bool delim;
+  };
+  std::vector<Seg> segs;
+  size_t run = 0;
+  for (size_t i = 0; i < w.size(); ++i)
+    if (is_delim(w[i])) {
+      if (run < i) segs.push_back({run, i, false});
+      segs.push_back({i, i + 1, true});
+      run = i + 1;
+    }
+  if (run < w.size()) segs.push_back({run, w.size(), false});
+  std::vector<Seg> merged;
+  bool prev = false;
+  switch (behavior) {
+    case kIsolated:
+    case kRemoved:
+      merged = segs;
+      break;
+    case kContiguous:
+      for (const Seg& g : segs) {
+        if (!merged.empty() && g.delim == prev) merged.back().e = g.e;
+        else merged.push_back({g.b, g.e, false});
+        prev = g.delim;
       }
-      model(t, word, ids);
+      break;
+    case kMergedWithPrevious:
+      for (const Seg& g : segs) {
+        if (g.delim && !prev && !merged.empty()) merged.back().e = g.e;
+        else merged.push_back({g.b, g.e, false});
+        prev = g.delim;
+      }
+      break;
+    case kMergedWithNext:
+      for (size_t k = segs.size(); k-- > 0;) {
+        const Seg& g = segs[k];
+        if (g.delim && !prev && !merged.empty()) merged.back().b = g.b;
+        else merged.push_back({g.b, g.e, false});
+        prev = g.delim;
+      }
+      std::reverse(merged.begin(), merged.end());
+      break;
+  }
+  for (const Seg& g : merged)
+    if (g.e > g.b && !(behavior == kRemoved && g.delim))
+      out.emplace_back(w.begin() + g.b, w.begin() + g.e);
+}
+
+void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32_t>& w, Words& out) {
+  (void)t;
+  switch (st.kind) {
+    case kPreBert: {  // split on White_Space (removed), each punctuation character isolated
+      Words parts;
+      split_chars(w, is_whitespace, kRemoved, parts);
+      for (const auto& p : parts) split_chars(p, is_punct, kIsolated, out);
       return;
+    }
+    case kPreWhitespaceSplit:
+      split_chars(w, is_whitespace, kRemoved, out);
+      return;
+    case kPrePunctuation:
+      split_chars(w, is_punct, st.behavior, out);
+      return;
+    case kPreDigits:
+      split_chars(w, is_number, st.individual_digits ? kIsolated : kContiguous, out);
+      return;
+    case kPreWhitespace: {  // the matches of \w+|[^\w\s]+; the rest dropped
+      auto word = [](uint32_t c) { return is_word_char(c); };
+      for (size_t i = 0; i < w.size();) {
+        if (is_whitespace(w[i])) {
+          ++i;
+          continue;
+        }
+        const bool wd = word(w[i]);
+        size_t j = i + 1;
+        while (j < w.size() && !is_whitespace(w[j]) && word(w[j]) == wd) ++j;
+        out.emplace_back(w.begin() + i, w.begin() + j);
+        i = j;
+      }
+      return;
+    }
     case kPreClip: {
       size_t seg = 0;
-      for (size_t i = 0; i < c.size();) {
-        const size_t len = clip_match(c, i);
+      for (size_t i = 0; i < w.size();) {
+        const size_t len = clip_match(w, i);
         if (len == 0) {
           ++i;
           continue;
         }
-        if (seg < i) model(t, std::vector<uint32_t>(c.begin() + seg, c.begin() + i), ids);
-        model(t, std::vector<uint32_t>(c.begin() + i, c.begin() + i + len), ids);
+        if (seg < i) out.emplace_back(w.begin() + seg, w.begin() + i);
+        out.emplace_back(w.begin() + i, w.begin() + i + len);
         i += len;
         seg = i;
       }
-      if (seg < c.size()) model(t, std::vector<uint32_t>(c.begin() + seg, c.end()), ids);
+      if (seg < w.size()) out.emplace_back(w.begin() + seg, w.end());
       return;
     }
     case kPreByteLevel: {
-      if (t.add_prefix_space && c[0] != ' ') c.insert(c.begin(), ' ');
+      std::vector<uint32_t> c = w;
+      if (st.add_prefix_space && !c.empty() && c[0] != ' ') c.insert(c.begin(), ' ');
       const std::vector<uint32_t>& bs = byte_symbols();
       std::string utf8;
       for (size_t i = 0; i < c.size();) {
-        const size_t len = t.use_regex ? gpt2_match(c, i) : c.size();
+        const size_t len = st.use_regex ? gpt2_match(c, i) : c.size();
         utf8.clear();
         for (size_t k = i; k < i + len; ++k) append_utf8(c[k], utf8);
-        word.clear();
-        for (unsigned char b : utf8) word.push_back(bs[b]);
-        model(t, word, ids);
+        std::vector<uint32_t> sym;
+        for (unsigned char b : utf8) sym.push_back(bs[b]);
+        out.push_back(std::move(sym));
         i += len;
       }
       return;
     }
   }
+}
+
+void pre_tokenize_and_model(const jb_tokenizer& t, const std::string& piece, std::vector<uint32_t>& ids) {
+  Words words(1);
+  decode_utf8(piece.data(), piece.size(), words[0]);
+  if (words[0].empty()) return;
+  for (const PreStep& st : t.pre) {
+    Words next;
+    for (const auto& w : words) pre_step(t, st, w, next);
+    words.swap(next);
+  }
+  for (const auto& w : words) model(t, w, ids);
 }
 
 // ---- added tokens -----------------------------------------------------------
@@ -729,48 +858,88 @@ void add_merge(jb_tokenizer& t, size_t rank, const std::string& a, const std::st
                                                                         iab->second};
 }
 
+std::vector<uint32_t> cps_of(const std::string& u) {
+  std::vector<uint32_t> c;
+  decode_utf8(u.data(), u.size(), c);
+  return c;
+}
+
 void parse_normalizer(jb_tokenizer& t, const Json& nz) {
   const std::string type = nz.str_or("type", "");
+  NormStep st;
   if (type == "Sequence") {
     if (const Json* seq = nz.get("normalizers"); seq && seq->kind == Json::Arr)
       for (const Json& x : seq->arr) parse_normalizer(t, x);
+    return;
   } else if (type == "BertNormalizer") {
     t.clean_text = nz.bool_or("clean_text", true);
     t.handle_chinese = nz.bool_or("handle_chinese_chars", true);
     t.lowercase = nz.bool_or("lowercase", true);
     const Json* sa = nz.get("strip_accents");
     t.strip_accents = (sa && sa->kind == Json::Bool) ? sa->b : t.lowercase;
-    t.norm.push_back(kNormBert);
+    st.op = kNormBert;
   } else if (type == "NFC") {
-    t.norm.push_back(kNormNfc);
+    st.op = kNormNfc;
   } else if (type == "NFD") {
-    t.norm.push_back(kNormNfd);
+    st.op = kNormNfd;
   } else if (type == "Lowercase") {
-    t.norm.push_back(kNormLower);
+    st.op = kNormLower;
+  } else if (type == "StripAccents") {
+    st.op = kNormStripAccents;
+  } else if (type == "Strip") {
+    st.op = kNormStrip;
+    st.left = nz.bool_or("strip_left", true);
+    st.right = nz.bool_or("strip_right", true);
+  } else if (type == "Prepend") {
+    st.op = kNormPrepend;
+    st.a = cps_of(nz.str_or("prepend", ""));
+  } else if (type == "Replace") {
+    const Json* pat = nz.get("pattern");
+    const Json* lit = pat ? pat->get("String") : nullptr;
+    if (!lit || lit->kind != Json::Str)
+      fail(JB_ERR_INVALID, "tokenizer.json: only string patterns are supported in Replace");
+    st.op = kNormReplace;
+    st.a = cps_of(lit->str);
+    st.b = cps_of(nz.str_or("content", ""));
   } else {
     fail(JB_ERR_INVALID, "tokenizer.json: unsupported normalizer " + type);
   }
+  t.norm.push_back(st);
 }
 
 void parse_pre_tokenizer(jb_tokenizer& t, const Json& pt) {
-  std::string type = pt.str_or("type", "");
-  const Json* inner = &pt;
-  if (type == "Sequence") {  // a one-element Sequence is that element
-    const Json* seq = pt.get("pretokenizers");
-    if (!seq || seq->kind != Json::Arr || seq->arr.size() != 1)
-      fail(JB_ERR_INVALID, "tokenizer.json: unsupported pre-tokenizer sequence");
-    inner = &seq->arr[0];
-    type = inner->str_or("type", "");
-  }
-  if (type == "BertPreTokenizer") {
-    t.pre = kPreBert;
+  const std::string type = pt.str_or("type", "");
+  PreStep st;
+  if (type == "Sequence") {
+    if (const Json* seq = pt.get("pretokenizers"); seq && seq->kind == Json::Arr)
+      for (const Json& x : seq->arr) parse_pre_tokenizer(t, x);
+    return;
+  } else if (type == "BertPreTokenizer") {
+    st.kind = kPreBert;
   } else if (type == "ByteLevel") {
-    t.pre = kPreByteLevel;
-    t.add_prefix_space = inner->bool_or("add_prefix_space", true);
-    t.use_regex = inner->bool_or("use_regex", true);
+    st.kind = kPreByteLevel;
+    st.add_prefix_space = pt.bool_or("add_prefix_space", true);
+    st.use_regex = pt.bool_or("use_regex", true);
+  } else if (type == "Whitespace") {
+    st.kind = kPreWhitespace;
+  } else if (type == "WhitespaceSplit") {
+    st.kind = kPreWhitespaceSplit;
+  } else if (type == "Punctuation") {
+    st.kind = kPrePunctuation;
+    const std::string b = pt.str_or("behavior", "Isolated");
+    if (b == "Isolated") st.behavior = kIsolated;
+    else if (b == "Removed") st.behavior = kRemoved;
+    else if (b == "MergedWithPrevious") st.behavior = kMergedWithPrevious;
+    else if (b == "MergedWithNext") st.behavior = kMergedWithNext;
+    else if (b == "Contiguous") st.behavior = kContiguous;
+    else fail(JB_ERR_INVALID, "tokenizer.json: unknown split behavior " + b);
+  } else if (type == "Digits") {
+    st.kind = kPreDigits;
+    st.individual_digits = pt.bool_or("individual_digits", false);
   } else {
     fail(JB_ERR_INVALID, "tokenizer.json: unsupported pre-tokenizer " + type);
   }
+  t.pre.push_back(st);
 }
 
 uint32_t id_of_pair(const Json* p, const char* what) {
@@ -877,10 +1046,7 @@ jb_tokenizer* load(const char* path) {
     }
   }
   if (const Json* nz = j.get("normalizer"); nz && nz->kind == Json::Obj) parse_normalizer(*t, *nz);
-  if (const Json* pt = j.get("pre_tokenizer"); pt && pt->kind == Json::Obj)
-    parse_pre_tokenizer(*t, *pt);
-  else
-    t->pre = kPreNone;
+  if (const Json* pt = j.get("pre_tokenizer"); pt && pt->kind == Json::Obj) parse_pre_tokenizer(*t, *pt);
   if (const Json* pp = j.get("post_processor"); pp && pp->kind == Json::Obj)
     parse_post(*t, *pp, t->before, t->after);
   if (const Json* added = j.get("added_tokens"); added && added->kind == Json::Arr)
@@ -933,7 +1099,7 @@ jb_tokenizer* load_clip(const char* path) {
   if (merges.empty()) fail(JB_ERR_IO, std::string("no BPE merges in ") + path);
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
   t->wordpiece = false;
-  t->pre = kPreClip;
+  t->pre.push_back(PreStep{kPreClip});
   t->bpe_suffix = "</w>";
   std::vector<std::string> vocab;
   for (uint32_t c : byte_symbols()) {

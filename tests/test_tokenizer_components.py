@@ -1,0 +1,126 @@
+"""The remaining tokenizer.json components the native tokenizer reads --
+StripAccents, Strip, Prepend and Replace normalisers; Whitespace,
+WhitespaceSplit, Punctuation (every split behaviour) and Digits
+pre-tokenisers; Sequences of them -- against HuggingFace `tokenizers`, id for
+id, and the reference's own fixture tokenizer (cookbook/fixtures/tiny_bert:
+Lowercase + StripAccents, Whitespace, WordPiece).  CPU only."""
+import json
+import os
+
+import pytest
+
+tokenizers = pytest.importorskip("tokenizers")
+
+from test_tokenizer import CASES, random_texts  # noqa: E402
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert_tokens.json")
+REF_TOKENIZER = "/root/reference/cookbook/fixtures/tiny_bert/tokenizer.json"
+
+EXTRA = CASES + [
+    "Mc: कः  Me: a⃝  Mn: é", "  padded both ends  ", "x__y _z_ a-b-c", "...!!!???", "a1b22c333 4444",
+    "१२३ ٣٤ ½ ²", "don't stop", "[CLS] [SEP]", "ab" * 30,
+]
+
+
+def _train(tok, model_kind, tmp_path, name):
+    from tokenizers import trainers
+    specials = ["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]"]
+    if model_kind == "wordpiece":
+        trainer = trainers.WordPieceTrainer(vocab_size=1200, special_tokens=specials)
+    else:
+        trainer = trainers.BpeTrainer(vocab_size=900, special_tokens=specials, show_progress=False,
+                                      limit_alphabet=120)
+    tok.train_from_iterator(random_texts(1, 2000, 40) + ["reading played 12345 naïve"] * 5, trainer=trainer)
+    from tokenizers import processors
+    cls, sep = tok.token_to_id("[CLS]"), tok.token_to_id("[SEP]")
+    tok.post_processor = processors.TemplateProcessing(single="[CLS] $A [SEP]",
+                                                       special_tokens=[("[CLS]", cls), ("[SEP]", sep)])
+    path = tmp_path / name
+    tok.save(str(path))
+    return tok, str(path)
+
+
+def _same(path, hf, texts):
+    from jammi_b200 import Tokenizer
+    got = Tokenizer(path)(texts)
+    bad = [(t, hf.encode(t).ids, list(g)) for t, g in zip(texts, got) if hf.encode(t).ids != list(g)]
+    assert not bad, bad[:3]
+
+
+def _normalizers():
+    from tokenizers import normalizers as n
+    return {
+        "lower_stripaccents": n.Sequence([n.Lowercase(), n.StripAccents()]),
+        "nfd_stripaccents": n.Sequence([n.NFD(), n.StripAccents()]),
+        "strip_both": n.Strip(),
+        "strip_left": n.Strip(left=True, right=False),
+        "prepend_replace": n.Sequence([n.Replace(" ", "_"), n.Prepend("_")]),
+        "replace_multi": n.Sequence([n.Replace("ab", "X"), n.Replace("  ", " ")]),
+    }
+
+
+def _pre_tokenizers():
+    from tokenizers import pre_tokenizers as p
+    return {
+        "whitespace": p.Whitespace(),
+        "whitespace_split": p.WhitespaceSplit(),
+        "punct_isolated": p.Sequence([p.WhitespaceSplit(), p.Punctuation()]),
+        "punct_removed": p.Sequence([p.WhitespaceSplit(), p.Punctuation("removed")]),
+        "punct_prev": p.Sequence([p.WhitespaceSplit(), p.Punctuation("merged_with_previous")]),
+        "punct_next": p.Sequence([p.WhitespaceSplit(), p.Punctuation("merged_with_next")]),
+        "punct_contiguous": p.Sequence([p.WhitespaceSplit(), p.Punctuation("contiguous")]),
+        "digits_each": p.Sequence([p.Whitespace(), p.Digits(individual_digits=True)]),
+        "digits_runs": p.Sequence([p.WhitespaceSplit(), p.Digits(individual_digits=False)]),
+        "digits_bytelevel": p.Sequence([p.Digits(individual_digits=True), p.ByteLevel(add_prefix_space=False)]),
+    }
+
+
+@pytest.mark.parametrize("norm", sorted(_normalizers()))
+def test_normalizers(tmp_path, norm):
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    tok = Tokenizer(models.WordPiece(unk_token="[UNK]"))
+    tok.normalizer = _normalizers()[norm]
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    hf, path = _train(tok, "wordpiece", tmp_path, "tok.json")
+    _same(path, hf, EXTRA + random_texts(3, 300))
+
+
+@pytest.mark.parametrize("pre", sorted(_pre_tokenizers()))
+def test_pre_tokenizers(tmp_path, pre):
+    from tokenizers import Tokenizer, models
+    kind = "bpe" if "bytelevel" in pre else "wordpiece"
+    tok = Tokenizer(models.BPE(unk_token="[UNK]") if kind == "bpe" else models.WordPiece(unk_token="[UNK]"))
+    tok.pre_tokenizer = _pre_tokenizers()[pre]
+    hf, path = _train(tok, kind, tmp_path, "tok.json")
+    _same(path, hf, EXTRA + random_texts(4, 300))
+
+
+def test_reference_fixture_tokenizer_golden_ids():
+    """The reference's own tiny_bert tokenizer (Lowercase + StripAccents,
+    Whitespace, WordPiece, [CLS]/[SEP]): ids committed from HF `tokenizers`
+    by tests/golden/make_token_golden.py; the file is re-read from the
+    reference checkout when present."""
+    if not os.path.exists(REF_TOKENIZER):
+        pytest.skip("reference checkout not present")
+    from jammi_b200 import Tokenizer
+    g = json.load(open(GOLDEN, encoding="utf-8"))
+    ours = Tokenizer(REF_TOKENIZER)
+    got = [list(map(int, r)) for r in ours(g["texts"])]
+    assert got == g["ids"]
+    for max_len in (4, 9):
+        got = [list(map(int, r)) for r in ours(g["texts"], max_length=max_len)]
+        assert got == g[f"ids_max{max_len}"]
+
+
+def test_unsupported_components_still_fail_loudly(tmp_path):
+    from jammi_b200 import Tokenizer
+    from jammi_b200._lib import JbError
+    base = {"model": {"type": "WordPiece", "vocab": {"[UNK]": 0, "a": 1}, "unk_token": "[UNK]"}}
+    for extra in ({"normalizer": {"type": "NFKC"}},
+                  {"normalizer": {"type": "Replace", "pattern": {"Regex": "a+"}, "content": "b"}},
+                  {"pre_tokenizer": {"type": "Metaspace", "replacement": "_"}},
+                  {"pre_tokenizer": {"type": "Punctuation", "behavior": "Sideways"}}):
+        path = tmp_path / "bad.json"
+        path.write_text(json.dumps({**base, **extra}))
+        with pytest.raises(JbError):
+            Tokenizer(str(path))
