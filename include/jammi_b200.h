@@ -402,9 +402,10 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
  * tokenizer.rs:21-78): added tokens (normalized / lstrip / rstrip /
  * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase,
- * StripAccents, Strip, Prepend, Replace (string patterns) and Sequences,
- * pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace, WhitespaceSplit,
- * Punctuation, Digits and Sequences, models WordPiece
+ * StripAccents, Strip, Prepend, Replace (string patterns, regex \s+) and
+ * Sequences, pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace,
+ * WhitespaceSplit, Punctuation, Digits, Split (string patterns; the CLIP,
+ * GPT-2 and \s+ regexes) and Sequences, models WordLevel, WordPiece
  * and BPE (byte-level or character-level: unknown token, fuse_unk,
  * byte_fallback, subword prefix / suffix, ignore_merges), post-processors
  * TemplateProcessing, BertProcessing, RobertaProcessing, ByteLevel (and

@@ -20,7 +20,8 @@
 //                  when lowercase is), lowercase (one code point at a time);
 //                  NFC, NFD, Lowercase, StripAccents (drop category M*, no
 //                  decomposition of its own), Strip, Prepend (non-empty
-//                  pieces), Replace (string patterns), and Sequences;
+//                  pieces), Replace (string patterns, or the regex \s+),
+//                  and Sequences;
 //   pre-tokeniser  (a Sequence applies its steps in order, each to the words
 //                  the previous one produced)
 //                  BertPreTokenizer: split on White_Space, each punctuation
@@ -33,7 +34,11 @@
 //                  Whitespace: the matches of \w+|[^\w\s]+; WhitespaceSplit;
 //                  Punctuation with its split behaviour (isolated, removed,
 //                  merged with the previous / next word, contiguous); Digits
-//                  (each digit, or digit runs);
+//                  (each digit, or digit runs); Split on a literal string
+//                  (the empty one matches at every character boundary) or on
+//                  the CLIP, GPT-2 or \s+ regular expression, matched by
+//                  hand (any other regex is refused), inverted or not, with
+//                  any split behaviour;
 //                  OpenCLIP's regex (the special-token literals, the
 //                  contractions, letter runs, single digits, runs of other
 //                  non-space characters; the spans between matches are words
@@ -48,7 +53,8 @@
 //                  (consecutive ones fused with fuse_unk), else dropped; then
 //                  the lowest-ranked adjacent pair merged first (leftmost on
 //                  ties) until none applies; ignore_merges takes a word found
-//                  whole in the vocabulary as one token;
+//                  whole in the vocabulary as one token.  WordLevel: the word's
+//                  id, else the unknown token's, else an error;
 //   post-processor TemplateProcessing, BertProcessing, RobertaProcessing,
 //                  ByteLevel (ids unchanged) and Sequences of these: special
 //                  ids around the sequence;
@@ -69,6 +75,7 @@
 #include <cstring>
 #include <fstream>
 #include <memory>
+#include <mutex>
 #include <sstream>
 #include <string>
 #include <thread>
@@ -105,26 +112,35 @@ struct AddedSet {
   }
 };
 
-enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace };
+enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace,
+              kNormReplaceSpaceRuns };
 struct NormStep {
   int op = kNormBert;
   bool left = false, right = false;  // Strip
   std::vector<uint32_t> a, b;        // Prepend: a; Replace: a -> b
 };
-enum PreKind { kPreBert, kPreByteLevel, kPreClip, kPreWhitespace, kPreWhitespaceSplit, kPrePunctuation, kPreDigits };
+enum PreKind { kPreBert, kPreByteLevel, kPreClip, kPreWhitespace, kPreWhitespaceSplit, kPrePunctuation, kPreDigits,
+               kPreSplit };
 enum Behavior { kIsolated, kRemoved, kMergedWithPrevious, kMergedWithNext, kContiguous };
+// Split patterns: a literal string, or one of the regular expressions the
+// encoder families' tokenizer.json files use, matched by hand.
+enum Pattern { kPatLiteral, kPatClip, kPatClipSpecials, kPatGpt2, kPatSpaceRuns };
 struct PreStep {
   int kind = kPreBert;
   bool add_prefix_space = false, use_regex = true;  // ByteLevel
-  int behavior = kIsolated;                         // Punctuation
+  int behavior = kIsolated;                         // Punctuation, Split
   bool individual_digits = false;                   // Digits
+  int pattern = kPatLiteral;                        // Split
+  std::vector<uint32_t> literal;                    // Split, kPatLiteral
+  bool invert = false;                              // Split
 };
+enum ModelKind { kWordPiece, kBpe, kWordLevel };
 
 }  // namespace
 }  // namespace jb
 
 struct jb_tokenizer {
-  bool wordpiece = true;  // else BPE
+  int model = jb::kWordPiece;
   // normaliser and pre-tokeniser steps, applied in order
   std::vector<jb::NormStep> norm;
   bool clean_text = true, handle_chinese = true, strip_accents = true, lowercase = true;
@@ -428,6 +444,19 @@ void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
         if (!cps.empty()) cps.insert(cps.begin(), st.a.begin(), st.a.end());
         break;
       case kNormReplace: replace_all(cps, st.a, st.b); break;
+      case kNormReplaceSpaceRuns: {  // regex \s+ -> content
+        tmp.clear();
+        for (size_t i = 0; i < cps.size();) {
+          if (!is_whitespace(cps[i])) {
+            tmp.push_back(cps[i++]);
+            continue;
+          }
+          while (i < cps.size() && is_whitespace(cps[i])) ++i;
+          tmp.insert(tmp.end(), st.b.begin(), st.b.end());
+        }
+        cps.swap(tmp);
+        break;
+      }
     }
   }
 }
@@ -533,10 +562,16 @@ void bpe(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<u
 }
 
 void model(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
-  if (t.wordpiece)
-    wordpiece(t, word, ids);
-  else
-    bpe(t, word, ids);
+  if (t.model == kWordPiece) return wordpiece(t, word, ids);
+  if (t.model == kBpe) return bpe(t, word, ids);
+  if (word.empty()) return;  // WordLevel: the word itself, else the unknown token
+  auto it = t.vocab.find(to_utf8(word));
+  if (it != t.vocab.end()) {
+    ids.push_back(it->second);
+  } else {
+    if (!t.has_unk) fail(JB_ERR_INVALID, "WordLevel: a word is not in the vocabulary and there is no unknown token");
+    ids.push_back(t.unk_id);
+  }
 }
 
 // ---- pre-tokenisers ---------------------------------------------------------
@@ -544,10 +579,11 @@ void model(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector
 // Length (in code points) of OpenCLIP's regex match at position i, 0 if no
 // alternative matches there (whitespace); alternatives are tried in the
 // regex's order, the first that matches wins.
-size_t clip_match(const std::vector<uint32_t>& c, size_t i) {
+size_t clip_match(const std::vector<uint32_t>& c, size_t i, bool specials = true) {
   static const char* const kLiterals[] = {"<|startoftext|>", "<|endoftext|>", "'s", "'t", "'re",
                                           "'ve", "'m", "'ll", "'d"};
   for (const char* lit : kLiterals) {
+    if (!specials && lit[0] == '<') continue;
     const size_t len = std::strlen(lit);
     if (i + len > c.size()) continue;
     size_t k = 0;
@@ -601,23 +637,14 @@ size_t gpt2_match(const std::vector<uint32_t>& c, size_t i) {
 
 using Words = std::vector<std::vector<uint32_t>>;
 
-// The crate's split of one word on a per-character predicate: each matching
-// character is a delimiter, kept, dropped or merged by `behavior`.
-template <typename Pred>
-void split_chars(const std::vector<uint32_t>& w, Pred is_delim, int behavior, Words& out) {
-  struct Seg {
-    size_t b, e;
-    bool delim;
-  };
-  std::vector<Seg> segs;
-  size_t run = 0;
-  for (size_t i = 0; i < w.size(); ++i)
-    if (is_delim(w[i])) {
-      if (run < i) segs.push_back({run, i, false});
-      segs.push_back({i, i + 1, true});
-      run = i + 1;
-    }
-  if (run < w.size()) segs.push_back({run, w.size(), false});
+// The crate's split of one word: a list of (segment, is-match) covering it,
+// then `behavior` keeps, drops or merges the matches; empty pieces vanish.
+struct Seg {
+  size_t b, e;
+  bool m;
+};
+
+void emit(const std::vector<uint32_t>& w, const std::vector<Seg>& segs, int behavior, Words& out) {
   std::vector<Seg> merged;
   bool prev = false;
   switch (behavior) {
@@ -627,31 +654,98 @@ void split_chars(const std::vector<uint32_t>& w, Pred is_delim, int behavior, Wo
       break;
     case kContiguous:
       for (const Seg& g : segs) {
-        if (!merged.empty() && g.delim == prev) merged.back().e = g.e;
+        if (!merged.empty() && g.m == prev) merged.back().e = g.e;
         else merged.push_back({g.b, g.e, false});
-        prev = g.delim;
+        prev = g.m;
       }
       break;
     case kMergedWithPrevious:
       for (const Seg& g : segs) {
-        if (g.delim && !prev && !merged.empty()) merged.back().e = g.e;
+        if (g.m && !prev && !merged.empty()) merged.back().e = g.e;
         else merged.push_back({g.b, g.e, false});
-        prev = g.delim;
+        prev = g.m;
       }
       break;
     case kMergedWithNext:
       for (size_t k = segs.size(); k-- > 0;) {
         const Seg& g = segs[k];
-        if (g.delim && !prev && !merged.empty()) merged.back().b = g.b;
+        if (g.m && !prev && !merged.empty()) merged.back().b = g.b;
         else merged.push_back({g.b, g.e, false});
-        prev = g.delim;
+        prev = g.m;
       }
       std::reverse(merged.begin(), merged.end());
       break;
   }
   for (const Seg& g : merged)
-    if (g.e > g.b && !(behavior == kRemoved && g.delim))
-      out.emplace_back(w.begin() + g.b, w.begin() + g.e);
+    if (g.e > g.b && !(behavior == kRemoved && g.m)) out.emplace_back(w.begin() + g.b, w.begin() + g.e);
+}
+
+// Each character that satisfies the predicate is a match of its own.
+template <typename Pred>
+std::vector<Seg> char_segments(const std::vector<uint32_t>& w, Pred is_delim) {
+  std::vector<Seg> segs;
+  size_t run = 0;
+  for (size_t i = 0; i < w.size(); ++i)
+    if (is_delim(w[i])) {
+      if (run < i) segs.push_back({run, i, false});
+      segs.push_back({i, i + 1, true});
+      run = i + 1;
+    }
+  if (run < w.size()) segs.push_back({run, w.size(), false});
+  return segs;
+}
+
+template <typename Pred>
+void split_chars(const std::vector<uint32_t>& w, Pred is_delim, int behavior, Words& out) {
+  emit(w, char_segments(w, is_delim), behavior, out);
+}
+
+// Length of the pattern's match starting at i (0: none there).
+size_t pattern_match(const PreStep& st, const std::vector<uint32_t>& c, size_t i) {
+  switch (st.pattern) {
+    case kPatClip: return clip_match(c, i, false);
+    case kPatClipSpecials: return clip_match(c, i, true);
+    case kPatGpt2: return gpt2_match(c, i);
+    case kPatSpaceRuns: {
+      size_t j = i;
+      while (j < c.size() && is_whitespace(c[j])) ++j;
+      return j - i;
+    }
+    default: {
+      const std::vector<uint32_t>& lit = st.literal;
+      return (i + lit.size() <= c.size() && std::equal(lit.begin(), lit.end(), c.begin() + i)) ? lit.size() : 0;
+    }
+  }
+}
+
+// A regex scan's matches in order with the gaps between them; the empty
+// pattern matches the empty string at every boundary, end included.
+std::vector<Seg> pattern_segments(const PreStep& st, const std::vector<uint32_t>& w) {
+  std::vector<Seg> segs;
+  if (w.empty()) return segs;
+  size_t prev = 0;
+  auto add_match = [&](size_t b, size_t e) {
+    if (prev != b) segs.push_back({prev, b, false});
+    segs.push_back({b, e, true});
+    prev = e;
+  };
+  if (st.pattern == kPatLiteral && st.literal.empty()) {
+    for (size_t b = 0; b <= w.size(); ++b) add_match(b, b);
+  } else {
+    for (size_t i = 0; i < w.size();) {
+      const size_t len = pattern_match(st, w, i);
+      if (len == 0) {
+        ++i;
+        continue;
+      }
+      add_match(i, i + len);
+      i += len;
+    }
+  }
+  if (prev != w.size()) segs.push_back({prev, w.size(), false});
+  if (st.invert)
+    for (Seg& g : segs) g.m = !g.m;
+  return segs;
 }
 
 void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32_t>& w, Words& out) {
@@ -671,6 +765,9 @@ void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32
       return;
     case kPreDigits:
       split_chars(w, is_number, st.individual_digits ? kIsolated : kContiguous, out);
+      return;
+    case kPreSplit:
+      emit(w, pattern_segments(st, w), st.behavior, out);
       return;
     case kPreWhitespace: {  // the matches of \w+|[^\w\s]+; the rest dropped
       auto word = [](uint32_t c) { return is_word_char(c); };
@@ -896,15 +993,42 @@ void parse_normalizer(jb_tokenizer& t, const Json& nz) {
   } else if (type == "Replace") {
     const Json* pat = nz.get("pattern");
     const Json* lit = pat ? pat->get("String") : nullptr;
-    if (!lit || lit->kind != Json::Str)
-      fail(JB_ERR_INVALID, "tokenizer.json: only string patterns are supported in Replace");
-    st.op = kNormReplace;
-    st.a = cps_of(lit->str);
+    const Json* re = pat ? pat->get("Regex") : nullptr;
     st.b = cps_of(nz.str_or("content", ""));
+    if (lit && lit->kind == Json::Str) {
+      st.op = kNormReplace;
+      st.a = cps_of(lit->str);
+    } else if (re && re->kind == Json::Str && re->str == "\\s+") {
+      st.op = kNormReplaceSpaceRuns;
+    } else {
+      fail(JB_ERR_INVALID, "tokenizer.json: Replace supports string patterns and the regex \\s+");
+    }
   } else {
     fail(JB_ERR_INVALID, "tokenizer.json: unsupported normalizer " + type);
   }
   t.norm.push_back(st);
+}
+
+int behavior_of(const std::string& b) {
+  if (b == "Isolated") return kIsolated;
+  if (b == "Removed") return kRemoved;
+  if (b == "MergedWithPrevious") return kMergedWithPrevious;
+  if (b == "MergedWithNext") return kMergedWithNext;
+  if (b == "Contiguous") return kContiguous;
+  fail(JB_ERR_INVALID, "tokenizer.json: unknown split behavior " + b);
+}
+
+// The regular expressions this library matches by hand; any other is refused.
+int known_regex(const std::string& re) {
+  static const std::string kClip = "'s|'t|'re|'ve|'m|'ll|'d|[\\p{L}]+|[\\p{N}]|[^\\s\\p{L}\\p{N}]+";
+  static const std::string kClipSpecials = "<\\|startoftext\\|>|<\\|endoftext\\|>|" + kClip;
+  static const std::string kGpt2 =
+      "'s|'t|'re|'ve|'m|'ll|'d| ?\\p{L}+| ?\\p{N}+| ?[^\\s\\p{L}\\p{N}]+|\\s+(?!\\S)|\\s+";
+  if (re == kClip) return kPatClip;
+  if (re == kClipSpecials) return kPatClipSpecials;
+  if (re == kGpt2) return kPatGpt2;
+  if (re == "\\s+") return kPatSpaceRuns;
+  fail(JB_ERR_INVALID, "tokenizer.json: unsupported regex pattern " + re);
 }
 
 void parse_pre_tokenizer(jb_tokenizer& t, const Json& pt) {
@@ -926,13 +1050,22 @@ void parse_pre_tokenizer(jb_tokenizer& t, const Json& pt) {
     st.kind = kPreWhitespaceSplit;
   } else if (type == "Punctuation") {
     st.kind = kPrePunctuation;
-    const std::string b = pt.str_or("behavior", "Isolated");
-    if (b == "Isolated") st.behavior = kIsolated;
-    else if (b == "Removed") st.behavior = kRemoved;
-    else if (b == "MergedWithPrevious") st.behavior = kMergedWithPrevious;
-    else if (b == "MergedWithNext") st.behavior = kMergedWithNext;
-    else if (b == "Contiguous") st.behavior = kContiguous;
-    else fail(JB_ERR_INVALID, "tokenizer.json: unknown split behavior " + b);
+    st.behavior = behavior_of(pt.str_or("behavior", "Isolated"));
+  } else if (type == "Split") {
+    st.kind = kPreSplit;
+    st.behavior = behavior_of(pt.str_or("behavior", "Isolated"));
+    st.invert = pt.bool_or("invert", false);
+    const Json* pat = pt.get("pattern");
+    const Json* lit = pat ? pat->get("String") : nullptr;
+    const Json* re = pat ? pat->get("Regex") : nullptr;
+    if (lit && lit->kind == Json::Str) {
+      st.pattern = kPatLiteral;
+      st.literal = cps_of(lit->str);
+    } else if (re && re->kind == Json::Str) {
+      st.pattern = known_regex(re->str);
+    } else {
+      fail(JB_ERR_INVALID, "tokenizer.json: Split without a pattern");
+    }
   } else if (type == "Digits") {
     st.kind = kPreDigits;
     st.individual_digits = pt.bool_or("individual_digits", false);
@@ -1007,13 +1140,19 @@ jb_tokenizer* load(const char* path) {
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
   const Json* model = j.get("model");
   const std::string type = model ? model->str_or("type", "") : "";
-  if (type != "WordPiece" && type != "BPE")
-    fail(JB_ERR_INVALID, "tokenizer.json: unsupported model '" + type + "' (WordPiece and BPE are supported)");
-  t->wordpiece = type == "WordPiece";
+  if (type != "WordPiece" && type != "BPE" && type != "WordLevel")
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported model '" + type + "' (WordPiece, BPE and WordLevel are supported)");
+  t->model = type == "WordPiece" ? kWordPiece : type == "BPE" ? kBpe : kWordLevel;
   const Json* vocab = model->get("vocab");
   if (!vocab || vocab->kind != Json::Obj) fail(JB_ERR_IO, "tokenizer.json: model.vocab missing");
   for (const auto& kv : vocab->obj) t->vocab[kv.first] = static_cast<uint32_t>(kv.second.num);
-  if (t->wordpiece) {
+  if (t->model == kWordLevel) {
+    if (const Json* unk = model->get("unk_token"); unk && unk->kind == Json::Str) {
+      auto it = t->vocab.find(unk->str);
+      t->has_unk = it != t->vocab.end();
+      if (t->has_unk) t->unk_id = it->second;
+    }
+  } else if (t->model == kWordPiece) {
     t->prefix = model->str_or("continuing_subword_prefix", "##");
     t->max_chars = static_cast<int>(model->num_or("max_input_chars_per_word", 100));
     t->unk_id = token_id(*t, model->str_or("unk_token", "[UNK]"));
@@ -1098,7 +1237,7 @@ jb_tokenizer* load_clip(const char* path) {
   }
   if (merges.empty()) fail(JB_ERR_IO, std::string("no BPE merges in ") + path);
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
-  t->wordpiece = false;
+  t->model = kBpe;
   t->pre.push_back(PreStep{kPreClip});
   t->bpe_suffix = "</w>";
   std::vector<std::string> vocab;
@@ -1161,9 +1300,20 @@ jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uin
     std::vector<std::vector<uint32_t>> rows(static_cast<size_t>(n));
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
     const int64_t workers = n >= 256 ? std::min<int64_t>(hw, (n + 127) / 128) : 1;
+    std::mutex mu;
+    std::string first_error;
+    jb_status first_status = JB_OK;
     auto work = [&](int64_t w) {
-      for (int64_t i = w; i < n; i += workers)
-        jb::encode(*t, texts[i] ? texts[i] : "", texts[i] ? text_bytes[i] : 0, max_length, rows[i]);
+      try {
+        for (int64_t i = w; i < n; i += workers)
+          jb::encode(*t, texts[i] ? texts[i] : "", texts[i] ? text_bytes[i] : 0, max_length, rows[i]);
+      } catch (const jb::Error& e) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (first_status == JB_OK) first_status = e.status, first_error = e.msg;
+      } catch (const std::exception& e) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (first_status == JB_OK) first_status = JB_ERR_INVALID, first_error = e.what();
+      }
     };
     if (workers == 1) {
       work(0);
@@ -1172,6 +1322,7 @@ jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uin
       for (int64_t w = 0; w < workers; ++w) pool.emplace_back(work, w);
       for (auto& th : pool) th.join();
     }
+    if (first_status != JB_OK) jb::fail(first_status, first_error);
     offsets[0] = 0;
     for (int64_t i = 0; i < n; ++i) offsets[i + 1] = offsets[i] + rows[i].size();
     if (!ids) return JB_OK;  // size query

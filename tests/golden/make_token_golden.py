@@ -3,11 +3,13 @@
     python tests/golden/make_token_golden.py
 
 Token ids of seeded synthetic texts under the reference's own fixture
-tokenizer (cookbook/fixtures/tiny_bert/tokenizer.json: Lowercase +
-StripAccents, Whitespace pre-tokeniser, WordPiece, [CLS]/[SEP]), computed by
+tokenizers (cookbook/fixtures/tiny_bert/tokenizer.json: Lowercase +
+StripAccents, Whitespace pre-tokeniser, WordPiece, [CLS]/[SEP]; and
+tests/fixtures/tiny_open_clip/tokenizer.json: WordLevel over single
+characters, '$A <|endoftext|>'), computed by
 HuggingFace `tokenizers` -- the crate the reference tokenises with -- with
-and without truncation.  Only texts and ids are written; the tokenizer file
-stays in the reference checkout.
+and without truncation.  Only texts and ids are written; the tokenizer files
+stay in the reference checkout.
 """
 import json
 import os
@@ -17,6 +19,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_TOKENIZER = "/root/reference/cookbook/fixtures/tiny_bert/tokenizer.json"
+REF_CLIP_TOKENIZER = "/root/reference/tests/fixtures/tiny_open_clip/tokenizer.json"
 
 ALPHABET = ("abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789     .,;:!?'\"()-_/"
             "àáâäãåæçèéêëìíîïñòóôöõøùúûüýÿßÀÉÎÕÜ" "αβγΣσ" "東京数据" "̣́̈" "\t\n　" "😀€…—«»")
@@ -51,6 +54,9 @@ def main():
     for max_len in (4, 9):
         tok.enable_truncation(max_length=max_len)
         doc[f"ids_max{max_len}"] = [e.ids for e in tok.encode_batch(ts)]
+    clip = Tokenizer.from_file(REF_CLIP_TOKENIZER)
+    doc["clip_source"] = "tests/fixtures/tiny_open_clip/tokenizer.json"
+    doc["clip_ids"] = [e.ids for e in clip.encode_batch(ts)]
     with open(os.path.join(HERE, "reference_tiny_bert_tokens.json"), "w", encoding="utf-8") as f:
         json.dump(doc, f, ensure_ascii=False)
 

@@ -124,3 +124,74 @@ def test_unsupported_components_still_fail_loudly(tmp_path):
         path.write_text(json.dumps({**base, **extra}))
         with pytest.raises(JbError):
             Tokenizer(str(path))
+
+
+REF_CLIP_TOKENIZER = "/root/reference/tests/fixtures/tiny_open_clip/tokenizer.json"
+CLIP_PATTERN = r"'s|'t|'re|'ve|'m|'ll|'d|[\p{L}]+|[\p{N}]|[^\s\p{L}\p{N}]+"
+
+
+def test_reference_open_clip_fixture_tokenizer_golden_ids():
+    """The reference's tiny OpenCLIP fixture tokenizer (WordLevel with '<pad>'
+    as the unknown token, Split on the empty string inverted -- one word per
+    character -- and '$A <|endoftext|>'): ids committed from HF `tokenizers`."""
+    if not os.path.exists(REF_CLIP_TOKENIZER):
+        pytest.skip("reference checkout not present")
+    from jammi_b200 import Tokenizer
+    g = json.load(open(GOLDEN, encoding="utf-8"))
+    got = [list(map(int, r)) for r in Tokenizer(REF_CLIP_TOKENIZER)(g["texts"])]
+    assert got == g["clip_ids"]
+
+
+def test_hf_format_clip_tokenizer(tmp_path):
+    """CLIP's tokenizer.json as HF hubs ship it: NFC, whitespace runs -> ' ',
+    Lowercase; Split on the CLIP regex (removed, inverted) then ByteLevel
+    without its regex; BPE with '</w>' word ends; RobertaProcessing."""
+    from tokenizers import Regex, Tokenizer, models, normalizers, pre_tokenizers, processors, trainers
+    tok = Tokenizer(models.BPE(unk_token="<|endoftext|>", end_of_word_suffix="</w>"))
+    tok.normalizer = normalizers.Sequence([normalizers.NFC(), normalizers.Replace(Regex(r"\s+"), " "),
+                                           normalizers.Lowercase()])
+    tok.pre_tokenizer = pre_tokenizers.Sequence([
+        pre_tokenizers.Split(Regex(CLIP_PATTERN), behavior="removed", invert=True),
+        pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)])
+    trainer = trainers.BpeTrainer(vocab_size=1200, special_tokens=["<|startoftext|>", "<|endoftext|>"],
+                                  end_of_word_suffix="</w>", show_progress=False,
+                                  initial_alphabet=pre_tokenizers.ByteLevel.alphabet())
+    tok.train_from_iterator(random_texts(1, 2000, 40) + ["a photo of a cat"] * 5, trainer=trainer)
+    tok.post_processor = processors.RobertaProcessing(("<|endoftext|>", 1), ("<|startoftext|>", 0))
+    path = tmp_path / "clip.json"
+    tok.save(str(path))
+    _same(str(path), tok, EXTRA + random_texts(5, 300))
+
+
+@pytest.mark.parametrize("pattern,behavior,invert", [
+    ("-", "isolated", False), ("-", "removed", False), ("-", "merged_with_previous", False),
+    ("-", "merged_with_next", False), ("-", "contiguous", False), ("ab", "isolated", True),
+    ("", "isolated", True), ("", "removed", False), ("", "contiguous", True),
+    ("regex:\\s+", "removed", False), ("regex:\\s+", "merged_with_next", False),
+    ("regex:gpt2", "isolated", False), ("regex:clip", "removed", True),
+])
+def test_split_pre_tokenizer(tmp_path, pattern, behavior, invert):
+    from tokenizers import Regex, Tokenizer, models, pre_tokenizers
+    if pattern == "regex:gpt2":
+        pat = Regex(r"'s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+")
+    elif pattern == "regex:clip":
+        pat = Regex(CLIP_PATTERN)
+    elif pattern.startswith("regex:"):
+        pat = Regex(pattern[6:])
+    else:
+        pat = pattern
+    tok = Tokenizer(models.WordPiece(unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Split(pat, behavior=behavior, invert=invert)
+    hf, path = _train(tok, "wordpiece", tmp_path, "tok.json")
+    _same(path, hf, EXTRA + ["a-b--c-", "-x-", "abab-ab", "  a  b  "] + random_texts(6, 200))
+
+
+def test_word_level(tmp_path):
+    from tokenizers import Tokenizer, models, pre_tokenizers, trainers
+    tok = Tokenizer(models.WordLevel(unk_token="[UNK]"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.train_from_iterator(random_texts(1, 500, 30),
+                            trainer=trainers.WordLevelTrainer(vocab_size=300, special_tokens=["[UNK]"]))
+    path = tmp_path / "wl.json"
+    tok.save(str(path))
+    _same(str(path), tok, EXTRA + random_texts(7, 200))
