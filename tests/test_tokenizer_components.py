@@ -195,3 +195,19 @@ def test_word_level(tmp_path):
     path = tmp_path / "wl.json"
     tok.save(str(path))
     _same(str(path), tok, EXTRA + random_texts(7, 200))
+
+
+def test_word_level_without_unknown_token_fails_on_every_thread_count(tmp_path):
+    """A word outside a WordLevel vocabulary without an unknown token is an
+    error (the crate's "Missing [UNK] token"), raised from the tokenizing
+    threads as a status, for one text and for a batch split across cores."""
+    from jammi_b200 import Tokenizer
+    from jammi_b200._lib import JbError
+    path = tmp_path / "wl.json"
+    path.write_text(json.dumps({"model": {"type": "WordLevel", "vocab": {"a": 0, "b": 1}, "unk_token": "[UNK]"},
+                                "pre_tokenizer": {"type": "WhitespaceSplit"}}))
+    tok = Tokenizer(str(path))
+    assert [list(map(int, r)) for r in tok(["a b a"])] == [[0, 1, 0]]
+    for texts in (["a c"], ["a b"] * 600 + ["zzz"]):
+        with pytest.raises(JbError, match="WordLevel"):
+            tok(texts)
