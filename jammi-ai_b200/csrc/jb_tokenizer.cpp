@@ -76,6 +76,7 @@
 #include <fstream>
 #include <memory>
 #include <mutex>
+#include <queue>
 #include <sstream>
 #include <string>
 #include <thread>
@@ -498,6 +499,53 @@ void wordpiece(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::ve
   ids.insert(ids.end(), pieces.begin(), pieces.end());
 }
 
+// Applies the merges to a word's symbols, lowest rank first and leftmost on
+// ties, in O(n log n): the symbols form a linked list and the candidate pairs
+// sit in a min-heap keyed (rank, position); a popped pair that no longer
+// exists (a side was merged away or changed) is skipped.
+void merge_symbols(const jb_tokenizer& t, std::vector<uint32_t>& sym) {
+  const int n = static_cast<int>(sym.size());
+  if (n < 2) return;
+  std::vector<int> prev(n), next(n);
+  std::vector<char> live(n, 1);
+  for (int i = 0; i < n; ++i) {
+    prev[i] = i - 1;
+    next[i] = i + 1 < n ? i + 1 : -1;
+  }
+  struct Cand {
+    uint32_t rank;
+    int pos;
+    uint32_t id;
+    bool operator>(const Cand& o) const { return rank != o.rank ? rank > o.rank : pos > o.pos; }
+  };
+  std::priority_queue<Cand, std::vector<Cand>, std::greater<Cand>> heap;
+  auto lookup = [&](int a) {
+    const int b = next[a];
+    if (b < 0) return;
+    auto it = t.merges.find((static_cast<uint64_t>(sym[a]) << 32) | sym[b]);
+    if (it != t.merges.end()) heap.push({it->second.first, a, it->second.second});
+  };
+  for (int i = 0; i + 1 < n; ++i) lookup(i);
+  while (!heap.empty()) {
+    const Cand c = heap.top();
+    heap.pop();
+    const int a = c.pos;
+    if (!live[a] || next[a] < 0) continue;
+    const int b = next[a];
+    auto it = t.merges.find((static_cast<uint64_t>(sym[a]) << 32) | sym[b]);
+    if (it == t.merges.end() || it->second.second != c.id || it->second.first != c.rank) continue;
+    sym[a] = c.id;
+    live[b] = 0;
+    next[a] = next[b];
+    if (next[b] >= 0) prev[next[b]] = a;
+    if (prev[a] >= 0) lookup(prev[a]);
+    lookup(a);
+  }
+  std::vector<uint32_t> out;
+  for (int i = 0; i >= 0; i = next[i]) out.push_back(sym[i]);
+  sym.swap(out);
+}
+
 void bpe(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
   if (word.empty()) return;
   if (t.ignore_merges) {
@@ -543,21 +591,7 @@ void bpe(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<u
     // no unknown token: the character is dropped
   }
   if (unk_pending) sym.push_back(t.unk_id);
-  while (sym.size() > 1) {
-    uint32_t best_rank = UINT32_MAX, best_id = 0;
-    size_t best_pos = 0;
-    for (size_t k = 0; k + 1 < sym.size(); ++k) {
-      auto it = t.merges.find((static_cast<uint64_t>(sym[k]) << 32) | sym[k + 1]);
-      if (it != t.merges.end() && it->second.first < best_rank) {
-        best_rank = it->second.first;
-        best_id = it->second.second;
-        best_pos = k;
-      }
-    }
-    if (best_rank == UINT32_MAX) break;
-    sym[best_pos] = best_id;
-    sym.erase(sym.begin() + best_pos + 1);
-  }
+  merge_symbols(t, sym);
   ids.insert(ids.end(), sym.begin(), sym.end());
 }
 

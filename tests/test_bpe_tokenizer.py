@@ -206,3 +206,19 @@ def test_escaped_astral_added_token(tmp_path):
     hf, path = save(hf, tmp_path / "tok.json", edit=lambda doc: None)
     assert "\\ud83d" in open(path).read()
     assert_same(Tokenizer(path), hf, ["a😀🚀b", "😀 🚀", "x 😀🚀😀🚀"])
+
+
+def test_long_unbroken_words(tmp_path):
+    """Words thousands of symbols long (URLs, base64, repeated letters) merge
+    in the crate's order; the heap-ordered merge keeps this fast."""
+    import time
+    from jammi_b200 import Tokenizer
+    hf, path = save(build_byte_level(tmp_path), tmp_path / "tok.json")
+    rng = np.random.default_rng(3)
+    letters = np.array(list("abcdefghijklmnopqrstuvwxyz"))
+    texts = ["a" * 5000, "ab" * 2500, "".join(rng.choice(letters, 6000)),
+             "https://example.com/" + "x".join(rng.choice(letters, 3000)),
+             "".join(rng.choice(list("ABCDEFGHIJKLMNOPQRSTUVWXYZabcdefghijklmnopqrstuvwxyz0123456789+/"), 8000))]
+    t0 = time.perf_counter()
+    assert_same(Tokenizer(path), hf, texts)
+    assert time.perf_counter() - t0 < 30
