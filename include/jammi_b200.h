@@ -433,6 +433,14 @@ void jb_tokenizer_free(jb_tokenizer* tokenizer);
 jb_status jb_tokenize(const jb_tokenizer* tokenizer, const char* const* texts,
                       const uint64_t* text_bytes, int64_t n, int max_length, uint32_t* ids,
                       uint64_t ids_capacity, uint64_t* offsets);
+/* jb_tokenize with CandleModel::forward_embedding's row rule (crates/jammi-ai/
+ * src/model/backend/candle.rs:779-806): a NULL or empty text is a row with no
+ * tokens -- the null row jb_generate_embeddings emits as a zero vector with a
+ * cleared validity bit -- instead of an encoding of the empty string; pass
+ * the model's max_seq as max_length, as the reference truncates to it. */
+jb_status jb_tokenize_rows(const jb_tokenizer* tokenizer, const char* const* texts,
+                           const uint64_t* text_bytes, int64_t n, int max_length, uint32_t* ids,
+                           uint64_t ids_capacity, uint64_t* offsets);
 
 /* ── multi-device embedding generation ────────────────────────────────────
  * The generate_embeddings driver (crates/jammi-ai/src/pipeline/embedding.rs:47-282

@@ -1313,21 +1313,10 @@ jb_status guarded_load(const char* path, jb_tokenizer** out, F&& loader) {
 }  // namespace
 }  // namespace jb
 
-extern "C" {
-
-jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out) {
-  return jb::guarded_load(tokenizer_json_path, out, jb::load);
-}
-
-jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out) {
-  return jb::guarded_load(merges_path, out, jb::load_clip);
-}
-
-void jb_tokenizer_free(jb_tokenizer* t) { delete t; }
-
-jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uint64_t* text_bytes,
-                      int64_t n, int max_length, uint32_t* ids, uint64_t ids_capacity,
-                      uint64_t* offsets) {
+namespace {
+jb_status tokenize_impl(const jb_tokenizer* t, const char* const* texts, const uint64_t* text_bytes,
+                        int64_t n, int max_length, uint32_t* ids, uint64_t ids_capacity,
+                        uint64_t* offsets, bool empty_rows) {
   try {
     if (!t || n < 0 || !offsets || (n > 0 && (!texts || !text_bytes)))
       jb::fail(JB_ERR_INVALID, "jb_tokenize: bad argument");
@@ -1339,8 +1328,11 @@ jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uin
     jb_status first_status = JB_OK;
     auto work = [&](int64_t w) {
       try {
-        for (int64_t i = w; i < n; i += workers)
+        for (int64_t i = w; i < n; i += workers) {
+          const bool empty = !texts[i] || text_bytes[i] == 0;
+          if (empty && empty_rows) continue;  // a null row: no tokens at all
           jb::encode(*t, texts[i] ? texts[i] : "", texts[i] ? text_bytes[i] : 0, max_length, rows[i]);
+        }
       } catch (const jb::Error& e) {
         std::lock_guard<std::mutex> lk(mu);
         if (first_status == JB_OK) first_status = e.status, first_error = e.msg;
@@ -1370,6 +1362,32 @@ jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uin
   } catch (const std::exception& e) {
     return jb::record_error(JB_ERR_INVALID, e.what());
   }
+}
+
+}  // namespace
+
+extern "C" {
+
+jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out) {
+  return jb::guarded_load(tokenizer_json_path, out, jb::load);
+}
+
+jb_status jb_tokenizer_load_clip_bpe(const char* merges_path, jb_tokenizer** out) {
+  return jb::guarded_load(merges_path, out, jb::load_clip);
+}
+
+void jb_tokenizer_free(jb_tokenizer* t) { delete t; }
+
+jb_status jb_tokenize(const jb_tokenizer* t, const char* const* texts, const uint64_t* text_bytes,
+                      int64_t n, int max_length, uint32_t* ids, uint64_t ids_capacity,
+                      uint64_t* offsets) {
+  return tokenize_impl(t, texts, text_bytes, n, max_length, ids, ids_capacity, offsets, false);
+}
+
+jb_status jb_tokenize_rows(const jb_tokenizer* t, const char* const* texts, const uint64_t* text_bytes,
+                           int64_t n, int max_length, uint32_t* ids, uint64_t ids_capacity,
+                           uint64_t* offsets) {
+  return tokenize_impl(t, texts, text_bytes, n, max_length, ids, ids_capacity, offsets, true);
 }
 
 }  // extern "C"

@@ -58,6 +58,7 @@ _SIGS = [
     ("jb_model_load_family", _I, [ctypes.c_char_p, ctypes.c_char_p, _I, _I, _I, ctypes.POINTER(_P)]),
     ("jb_tokenizer_load", _I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     ("jb_tokenizer_load_clip_bpe", _I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    ("jb_tokenize_rows", _I, [_P, _P, _P, ctypes.c_int64, _I, _P, ctypes.c_uint64, _P]),
     ("jb_tokenizer_free", None, [_P]),
     ("jb_tokenize", _I, [_P, _P, _P, ctypes.c_int64, _I, _P, ctypes.c_uint64, _P]),
     ("jb_model_free", None, [_P]),

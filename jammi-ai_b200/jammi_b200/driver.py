@@ -195,19 +195,22 @@ def embed_texts(models, texts, tokenize, chunk_rows: int = 65536, **kw):
     texts = list(texts)
     H = models[0].info.output_dim
     from .tokenizer import Tokenizer
-    if isinstance(tokenize, Tokenizer) and tokenize.max_length <= 0:
-        max_seq = int(models[0].info.max_seq)
+    if isinstance(tokenize, Tokenizer):
+        max_len = tokenize.max_length if tokenize.max_length > 0 else int(models[0].info.max_seq)
         base = tokenize
-        tokenize = lambda ts: base(ts, max_length=max_seq)  # noqa: E731
 
-    def tokenize_valid(chunk):
-        keep = [i for i, t in enumerate(chunk)
-                if t is not None and not (isinstance(t, (str, bytes)) and len(t) == 0)]
-        seqs = tokenize([chunk[i] for i in keep]) if keep else []
-        rows = [[] for _ in chunk]
-        for i, seq in zip(keep, seqs):
-            rows[i] = seq
-        return rows
+        def tokenize_valid(chunk):  # jb_tokenize_rows: null rows in C, on all host cores
+            ids, offs = base.encode_ragged(chunk, max_length=max_len, null_rows=True)
+            return [ids[offs[i]:offs[i + 1]] for i in range(len(chunk))]
+    else:
+        def tokenize_valid(chunk):
+            keep = [i for i, t in enumerate(chunk)
+                    if t is not None and not (isinstance(t, (str, bytes)) and len(t) == 0)]
+            seqs = tokenize([chunk[i] for i in keep]) if keep else []
+            rows = [[] for _ in chunk]
+            for i, seq in zip(keep, seqs):
+                rows[i] = seq
+            return rows
 
     chunks = (tokenize_valid(texts[i:i + chunk_rows]) for i in range(0, len(texts), chunk_rows))
     outs, valid, stats = [], [], []

@@ -45,10 +45,13 @@ class Tokenizer:
         except Exception:
             pass
 
-    def encode_ragged(self, texts, max_length: int | None = None):
+    def encode_ragged(self, texts, max_length: int | None = None, null_rows: bool = False):
         """texts -> (ids uint32, offsets uint64 [n + 1]), the layout of
-        ``driver.generate_embeddings``."""
-        enc = [t.encode("utf-8") for t in texts]
+        ``driver.generate_embeddings``.  ``null_rows``: a None or empty text is
+        a row without tokens (``jb_tokenize_rows``, the embedding path's row
+        rule) instead of the encoding of the empty string."""
+        enc = [b"" if t is None else t.encode("utf-8") for t in texts]
+        fn = lib().jb_tokenize_rows if null_rows else lib().jb_tokenize
         n = len(enc)
         ptrs = (ctypes.c_char_p * max(n, 1))(*enc)
         sizes = np.array([len(e) for e in enc], dtype=np.uint64)
@@ -59,12 +62,12 @@ class Tokenizer:
         # output; a text dense in added tokens may need the exact-size retry.
         cap = int(sizes.sum()) + 4 * n + 64
         ids = np.empty(cap, dtype=np.uint32)
-        st = lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
-                               ids.ctypes.data, cap, offsets.ctypes.data)
+        st = fn(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                ids.ctypes.data, cap, offsets.ctypes.data)
         if st != L.OK and int(offsets[-1]) > cap:
             ids = np.empty(int(offsets[-1]), dtype=np.uint32)
-            st = lib().jb_tokenize(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
-                                   ids.ctypes.data, ids.size, offsets.ctypes.data)
+            st = fn(self._h, ctypes.cast(ptrs, ctypes.c_void_p), sizes.ctypes.data, n, ml,
+                    ids.ctypes.data, ids.size, offsets.ctypes.data)
         check(st)
         return ids[: int(offsets[-1])], offsets
 

@@ -114,3 +114,18 @@ def test_unsupported_tokenizer_is_rejected(tmp_path):
             Tokenizer(str(path))
     with pytest.raises(JbError):
         Tokenizer(str(tmp_path / "missing.json"))
+
+
+def test_tokenize_rows_null_rows(tmp_path):
+    """jb_tokenize_rows: None / empty texts are rows without tokens (the
+    embedding path's null rows, candle.rs:779-806); the others are
+    jb_tokenize's ids, truncated to max_length."""
+    from jammi_b200 import Tokenizer
+    hf, path = build(tmp_path, "tok.json")
+    texts = ["hello world", "", None, "naïve café " * 20, "x"] + random_texts(12, 300)
+    ours = Tokenizer(path)
+    ids, offsets = ours.encode_ragged(texts, max_length=16, null_rows=True)
+    hf.enable_truncation(max_length=16)
+    for i, t in enumerate(texts):
+        row = list(ids[offsets[i]:offsets[i + 1]])
+        assert row == ([] if not t else hf.encode(t).ids)
