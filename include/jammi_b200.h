@@ -402,17 +402,18 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
  * tokenizer.rs:21-78): added tokens (normalized / lstrip / rstrip /
  * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase,
- * StripAccents, Strip, Prepend, Replace (string patterns, regex \s+) and
- * Sequences, pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace,
- * WhitespaceSplit, Punctuation, Digits, Split (string patterns; the CLIP,
- * GPT-2 and \s+ regexes) and Sequences, models WordLevel, WordPiece
+ * StripAccents, Strip, Prepend, Replace (string patterns, regexes \s+ and
+ * ' {2,}'), Precompiled (sentencepiece character maps) and Sequences,
+ * pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace, WhitespaceSplit,
+ * Punctuation, Digits, Split (string patterns; the CLIP, GPT-2 and \s+
+ * regexes), Metaspace and Sequences, models WordLevel, Unigram, WordPiece
  * and BPE (byte-level or character-level: unknown token, fuse_unk,
  * byte_fallback, subword prefix / suffix, ignore_merges), post-processors
  * TemplateProcessing, BertProcessing, RobertaProcessing, ByteLevel (and
  * Sequences), truncation to max_length (special ids included) or else the
- * file's own.  That covers the BERT, DistilBERT and ModernBERT families;
- * other components (Unigram, Metaspace, NFKC, ...) answer JB_ERR_INVALID at
- * load.  Output is the ragged layout of jb_generate_embeddings: ids of text i
+ * file's own.  That covers the BERT (with RoBERTa, CamemBERT, XLM-RoBERTa),
+ * DistilBERT, ModernBERT and CLIP families; other components (NFKC, other
+ * regexes, ...) answer JB_ERR_INVALID at load.  Output is the ragged layout of jb_generate_embeddings: ids of text i
  * at ids[offsets[i] .. offsets[i+1]). */
 typedef struct jb_tokenizer jb_tokenizer;
 jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out);

@@ -11,6 +11,9 @@ unicodedata:
 * the ranges of general categories C* (other, including unassigned),
   P* (punctuation), Mn (nonspacing marks), L* (letters) and N* (numbers),
 * the ranges of general category M* (marks, for StripAccents),
+* the Grapheme_Cluster_Break classes, Extended_Pictographic and
+  Indic_Conjunct_Break of UAX #29 (the extended grapheme clusters the
+  Precompiled normaliser works on; from the regex module's properties),
 * the ranges of regex word characters (\\w: Alphabetic, marks, decimal
   digits, connector punctuation, joiners; from the `regex` module), the
   \\w of the Whitespace pre-tokeniser and of an added token's single_word
@@ -59,6 +62,40 @@ def main():
     import regex
     word_re = regex.compile(r"\w")
     word = ranges(lambda cp: not 0xD800 <= cp <= 0xDFFF and word_re.match(chr(cp)) is not None)
+
+    # Grapheme_Cluster_Break classes (UAX #29), Extended_Pictographic and
+    # Indic_Conjunct_Break, from the regex module's property support
+    gcb_names = ["CR", "LF", "Control", "Extend", "ZWJ", "Regional_Indicator", "Prepend", "SpacingMark",
+                 "L", "V", "T", "LV", "LVT"]
+    gcb_res = [(k + 1, regex.compile(r"\p{GCB=%s}" % n)) for k, n in enumerate(gcb_names)]
+    incb_res = [(k + 1, regex.compile(r"\p{InCB=%s}" % n)) for k, n in enumerate(["Consonant", "Extend", "Linker"])]
+
+    def classify(res):
+        def f(cp):
+            if 0xD800 <= cp <= 0xDFFF:
+                return 0
+            for k, r in res:
+                if r.match(chr(cp)):
+                    return k
+            return 0
+        return f
+
+    def class_ranges(fn):
+        out, start, cur = [], None, 0
+        for cp in range(MAX_CP):
+            k = fn(cp)
+            if k != cur:
+                if cur:
+                    out.append((start, cp - 1, cur))
+                start, cur = cp, k
+        if cur:
+            out.append((start, MAX_CP - 1, cur))
+        return out
+
+    gcb = class_ranges(classify(gcb_res))
+    incb = class_ranges(classify(incb_res))
+    ext_pict_re = regex.compile(r"\p{Extended_Pictographic}")
+    ext_pict = ranges(lambda cp: not 0xD800 <= cp <= 0xDFFF and ext_pict_re.match(chr(cp)) is not None)
 
     compose = []  # (first, second, composite)
     for cp in range(MAX_CP):
@@ -125,6 +162,10 @@ def main():
         "struct SeqEntry { uint32_t cp, off, n; };",
         "struct CccEntry { uint32_t cp; uint8_t ccc; };",
         "struct ComposeEntry { uint32_t first, second, composite; };",
+        "struct ClassRange { uint32_t lo, hi; uint8_t cls; };",
+        "// Grapheme_Cluster_Break: 1 CR, 2 LF, 3 Control, 4 Extend, 5 ZWJ, 6 Regional_Indicator,",
+        "// 7 Prepend, 8 SpacingMark, 9 L, 10 V, 11 T, 12 LV, 13 LVT (0: Other)",
+        "// Indic_Conjunct_Break: 1 Consonant, 2 Extend, 3 Linker (0: None)",
         f'static const char kUnicodeVersion[] = "{unicodedata.unidata_version}";',
         range_table("kOther", other),
         range_table("kPunct", punct),
@@ -133,6 +174,13 @@ def main():
         range_table("kNumber", number),
         range_table("kWord", word),
         range_table("kMark", mark),
+        range_table("kExtPict", ext_pict),
+        "static const ClassRange kGcb[] = {",
+        *[f"  {{0x{a:X}, 0x{b:X}, {c}}}," for a, b, c in gcb],
+        "};",
+        "static const ClassRange kIncb[] = {",
+        *[f"  {{0x{a:X}, 0x{b:X}, {c}}}," for a, b, c in incb],
+        "};",
         "static const ComposeEntry kCompose[] = {",
         *[f"  {{0x{a:X}, 0x{b:X}, 0x{c:X}}}," for a, b, c in compose],
         "};",

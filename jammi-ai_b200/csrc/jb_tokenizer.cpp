@@ -20,8 +20,11 @@
 //                  when lowercase is), lowercase (one code point at a time);
 //                  NFC, NFD, Lowercase, StripAccents (drop category M*, no
 //                  decomposition of its own), Strip, Prepend (non-empty
-//                  pieces), Replace (string patterns, or the regex \s+),
-//                  and Sequences;
+//                  pieces), Replace (string patterns, or the regexes \s+
+//                  and ' {2,}'), Precompiled (sentencepiece's character map,
+//                  a darts-clone double array, applied per UAX #29 extended
+//                  grapheme cluster of under 6 bytes, else per character,
+//                  shortest matching key first), and Sequences;
 //   pre-tokeniser  (a Sequence applies its steps in order, each to the words
 //                  the previous one produced)
 //                  BertPreTokenizer: split on White_Space, each punctuation
@@ -38,7 +41,9 @@
 //                  (the empty one matches at every character boundary) or on
 //                  the CLIP, GPT-2 or \s+ regular expression, matched by
 //                  hand (any other regex is refused), inverted or not, with
-//                  any split behaviour;
+//                  any split behaviour; Metaspace (' ' -> the replacement,
+//                  prepended always / at the text's start / never, split
+//                  before each replacement);
 //                  OpenCLIP's regex (the special-token literals, the
 //                  contractions, letter runs, single digits, runs of other
 //                  non-space characters; the spans between matches are words
@@ -54,7 +59,8 @@
 //                  the lowest-ranked adjacent pair merged first (leftmost on
 //                  ties) until none applies; ignore_merges takes a word found
 //                  whole in the vocabulary as one token.  WordLevel: the word's
-//                  id, else the unknown token's, else an error;
+//                  id, else the unknown token's, else an error.  Unigram:
+//                  Viterbi over the vocabulary's scores (below);
 //   post-processor TemplateProcessing, BertProcessing, RobertaProcessing,
 //                  ByteLevel (ids unchanged) and Sequences of these: special
 //                  ids around the sequence;
@@ -114,14 +120,15 @@ struct AddedSet {
 };
 
 enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace,
-              kNormReplaceSpaceRuns };
+              kNormReplaceSpaceRuns, kNormReplaceSpaces2, kNormPrecompiled };
 struct NormStep {
   int op = kNormBert;
   bool left = false, right = false;  // Strip
   std::vector<uint32_t> a, b;        // Prepend: a; Replace: a -> b
 };
 enum PreKind { kPreBert, kPreByteLevel, kPreClip, kPreWhitespace, kPreWhitespaceSplit, kPrePunctuation, kPreDigits,
-               kPreSplit };
+               kPreSplit, kPreMetaspace };
+enum PrependScheme { kPrependAlways, kPrependFirst, kPrependNever };
 enum Behavior { kIsolated, kRemoved, kMergedWithPrevious, kMergedWithNext, kContiguous };
 // Split patterns: a literal string, or one of the regular expressions the
 // encoder families' tokenizer.json files use, matched by hand.
@@ -134,8 +141,25 @@ struct PreStep {
   int pattern = kPatLiteral;                        // Split
   std::vector<uint32_t> literal;                    // Split, kPatLiteral
   bool invert = false;                              // Split
+  uint32_t replacement = 0x2581;                    // Metaspace
+  int prepend_scheme = kPrependAlways;              // Metaspace
+  bool split = true;                                // Metaspace
 };
-enum ModelKind { kWordPiece, kBpe, kWordLevel };
+enum ModelKind { kWordPiece, kBpe, kWordLevel, kUnigram };
+
+// sentencepiece's precompiled character map: a darts-clone double array
+// over UTF-8 keys whose values index NUL-terminated replacements.
+struct CharsMap {
+  std::vector<uint32_t> units;
+  std::string normalized;
+};
+
+// The Unigram vocabulary as a byte trie: edges (parent << 8 | byte) ->
+// child, sorted for binary search; piece[node] = vocabulary id or -1.
+struct PieceTrie {
+  std::vector<std::pair<uint64_t, uint32_t>> edges;
+  std::vector<int32_t> piece;
+};
 
 }  // namespace
 }  // namespace jb
@@ -156,6 +180,11 @@ struct jb_tokenizer {
   std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;
   std::string bpe_prefix, bpe_suffix;
   bool fuse_unk = false, byte_fallback = false, ignore_merges = false;
+  // Unigram: scores by id, the piece trie, the lowest score
+  std::vector<double> scores;
+  jb::PieceTrie trie;
+  double min_score = 0.0;
+  jb::CharsMap charsmap;  // Precompiled normaliser
   std::vector<uint32_t> before, after;  // special ids around the sequence
   jb::AddedSet raw_added, norm_added;
   int file_max_length = 0;
@@ -371,6 +400,119 @@ void lowercase_cps(std::vector<uint32_t>& cps) {
   cps.swap(tmp);
 }
 
+template <size_t N>
+uint8_t class_of(const uni::ClassRange (&r)[N], uint32_t cp) {
+  size_t lo = 0, hi = N;
+  while (lo < hi) {
+    const size_t mid = (lo + hi) / 2;
+    if (cp < r[mid].lo) hi = mid;
+    else if (cp > r[mid].hi) lo = mid + 1;
+    else return r[mid].cls;
+  }
+  return 0;
+}
+
+// End of the extended grapheme cluster (UAX #29, GB3-GB13 with GB9c) that
+// starts at i.
+size_t grapheme_end(const std::vector<uint32_t>& c, size_t i) {
+  enum { CR = 1, LF, Control, Extend, ZWJ, RI, Prepend, SpacingMark, L, V, T, LV, LVT };
+  const size_t n = c.size();
+  uint8_t prev = class_of(uni::kGcb, c[i]);
+  int ri = prev == RI;
+  bool pict = in_table(uni::kExtPict, c[i]), pict_zwj = false;
+  const uint8_t ib0 = class_of(uni::kIncb, c[i]);
+  int conj = ib0 == 1 ? 1 : 0;  // 1: consonant [extend|linker]*, 2: ... with a linker
+  size_t j = i + 1;
+  for (; j < n; ++j) {
+    const uint8_t cur = class_of(uni::kGcb, c[j]);
+    const uint8_t ib = class_of(uni::kIncb, c[j]);
+    const bool ext_pict = in_table(uni::kExtPict, c[j]);
+    bool join;
+    if (prev == CR && cur == LF) join = true;
+    else if (prev == Control || prev == CR || prev == LF) join = false;
+    else if (cur == Control || cur == CR || cur == LF) join = false;
+    else if (prev == L && (cur == L || cur == V || cur == LV || cur == LVT)) join = true;
+    else if ((prev == LV || prev == V) && (cur == V || cur == T)) join = true;
+    else if ((prev == LVT || prev == T) && cur == T) join = true;
+    else if (cur == Extend || cur == ZWJ || cur == SpacingMark || prev == Prepend) join = true;
+    else if (conj == 2 && ib == 1) join = true;
+    else if (pict_zwj && ext_pict) join = true;
+    else if (prev == RI && cur == RI && ri % 2 == 1) join = true;
+    else join = false;
+    if (!join) break;
+    ri = cur == RI ? ri + 1 : 0;
+    if (ext_pict) {
+      pict = true;
+      pict_zwj = false;
+    } else if (cur == Extend && pict) {
+      pict_zwj = false;
+    } else if (cur == ZWJ && pict) {
+      pict = false;
+      pict_zwj = true;
+    } else {
+      pict = pict_zwj = false;
+    }
+    if (ib == 1) conj = 1;
+    else if (ib == 3 && conj) conj = 2;
+    else if (ib != 2) conj = 0;
+    prev = cur;
+  }
+  return j;
+}
+
+// darts-clone's common-prefix search, shortest key first; the replacement of
+// the shortest key that prefixes `key`, if any.
+bool charsmap_transform(const CharsMap& m, const std::string& key, std::string& out) {
+  const std::vector<uint32_t>& a = m.units;
+  auto offset = [](uint32_t u) { return (u >> 10) << ((u & (1u << 9)) >> 6); };
+  if (a.empty()) return false;
+  size_t node = offset(a[0]);
+  for (unsigned char ch : key) {
+    if (ch == 0) return false;
+    node ^= ch;
+    if (node >= a.size()) return false;
+    const uint32_t unit = a[node];
+    if ((unit & (0x80000000u | 0xFFu)) != ch) return false;
+    node ^= offset(unit);
+    if ((unit >> 8) & 1u) {
+      if (node >= a.size()) return false;
+      const size_t idx = a[node] & 0x7FFFFFFFu;
+      if (idx > m.normalized.size()) return false;
+      const size_t end = m.normalized.find('\0', idx);
+      out.assign(m.normalized, idx, (end == std::string::npos ? m.normalized.size() : end) - idx);
+      return true;
+    }
+  }
+  return false;
+}
+
+// The Precompiled normaliser: per grapheme cluster shorter than 6 bytes the
+// map's replacement of the whole cluster, else per character.
+void precompiled_normalize(const CharsMap& m, std::vector<uint32_t>& cps) {
+  std::string out, unit, rep;
+  for (size_t i = 0; i < cps.size();) {
+    const size_t e = grapheme_end(cps, i);
+    unit.clear();
+    for (size_t k = i; k < e; ++k) append_utf8(cps[k], unit);
+    if (unit.size() < 6 && charsmap_transform(m, unit, rep)) {
+      out += rep;
+    } else {
+      for (size_t k = i; k < e; ++k) {
+        unit.clear();
+        append_utf8(cps[k], unit);
+        if (charsmap_transform(m, unit, rep)) {
+          out += rep;
+        } else {
+          out += unit;
+        }
+      }
+    }
+    i = e;
+  }
+  cps.clear();
+  decode_utf8(out.data(), out.size(), cps);
+}
+
 void bert_normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
   std::vector<uint32_t> tmp;
   if (t.clean_text) {
@@ -423,6 +565,22 @@ void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
   for (const NormStep& st : t.norm) {
     switch (st.op) {
       case kNormBert: bert_normalize(t, cps); break;
+      case kNormPrecompiled: precompiled_normalize(t.charsmap, cps); break;
+      case kNormReplaceSpaces2: {  // regex " {2,}" -> content
+        tmp.clear();
+        for (size_t i = 0; i < cps.size();) {
+          size_t j = i;
+          while (j < cps.size() && cps[j] == ' ') ++j;
+          if (j - i >= 2) {
+            tmp.insert(tmp.end(), st.b.begin(), st.b.end());
+            i = j;
+          } else {
+            tmp.push_back(cps[i++]);
+          }
+        }
+        cps.swap(tmp);
+        break;
+      }
       case kNormNfc: nfc(cps, tmp); cps.swap(tmp); break;
       case kNormNfd: nfd(cps, tmp); cps.swap(tmp); break;
       case kNormLower: lowercase_cps(cps); break;
@@ -595,8 +753,101 @@ void bpe(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<u
   ids.insert(ids.end(), sym.begin(), sym.end());
 }
 
+// Unigram: the best segmentation by Viterbi over byte positions (the
+// crate's encode_optimized): every vocabulary piece that prefixes the rest
+// of the word from each character boundary, score added to the best path
+// there, the first path found kept on ties; a character with no piece of
+// its own length gets the unknown token at (lowest score - 10); consecutive
+// unknown pieces fuse into one.  Pieces map to ids, the fused unknown runs
+// to <0xXX> byte tokens (byte_fallback) or the unknown id.
+void unigram(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
+  if (word.empty()) return;
+  const std::string s = to_utf8(word);
+  const size_t n = s.size();
+  struct Node {
+    double score = 0.0;
+    long start = -1;
+    int32_t id = 0;
+  };
+  std::vector<Node> best(n + 1);
+  best[0].start = 0;
+  const double unk_score = t.min_score - 10.0;
+  const auto& edges = t.trie.edges;
+  for (size_t at = 0; at < n;) {
+    size_t mblen = 1;
+    while (at + mblen < n && (static_cast<unsigned char>(s[at + mblen]) & 0xC0) == 0x80) ++mblen;
+    const double base = best[at].score;
+    bool single = false;
+    uint32_t node = 0;
+    for (size_t k = at; k < n; ++k) {
+      const uint64_t key = (static_cast<uint64_t>(node) << 8) | static_cast<unsigned char>(s[k]);
+      auto it = std::lower_bound(edges.begin(), edges.end(), std::make_pair(key, 0u),
+                                 [](const std::pair<uint64_t, uint32_t>& a, const std::pair<uint64_t, uint32_t>& b) {
+                                   return a.first < b.first;
+                                 });
+      if (it == edges.end() || it->first != key) break;
+      node = it->second;
+      const int32_t id = t.trie.piece[node];
+      if (id < 0) continue;
+      const size_t end = k + 1;
+      const double cand = base + t.scores[id];
+      if (best[end].start < 0 || cand > best[end].score) best[end] = {cand, static_cast<long>(at), id};
+      if (end - at == mblen) single = true;
+    }
+    if (!single) {
+      if (!t.has_unk) fail(JB_ERR_INVALID, "Unigram: a character has no piece and there is no unknown token");
+      const double cand = base + unk_score;
+      Node& tgt = best[at + mblen];
+      if (tgt.start < 0 || cand > tgt.score) tgt = {cand, static_cast<long>(at), static_cast<int32_t>(t.unk_id)};
+    }
+    at += mblen;
+  }
+  std::vector<std::pair<size_t, size_t>> pieces;  // byte ranges, reversed
+  size_t end = n, unk_end = 0;
+  bool in_unk = false;
+  while (end > 0) {
+    const Node& nd = best[end];
+    const size_t start = static_cast<size_t>(nd.start);
+    if (t.has_unk && static_cast<uint32_t>(nd.id) == t.unk_id) {
+      if (!in_unk) unk_end = end;
+      in_unk = true;
+    } else {
+      if (in_unk) pieces.emplace_back(end, unk_end);
+      in_unk = false;
+      pieces.emplace_back(start, end);
+    }
+    end = start;
+  }
+  if (in_unk) pieces.emplace_back(0, unk_end);
+  for (size_t k = pieces.size(); k-- > 0;) {
+    const std::string piece = s.substr(pieces[k].first, pieces[k].second - pieces[k].first);
+    auto it = t.vocab.find(piece);
+    if (it != t.vocab.end()) {
+      ids.push_back(it->second);
+      continue;
+    }
+    if (t.byte_fallback) {
+      std::vector<uint32_t> bytes;
+      char code[8];
+      for (unsigned char b : piece) {
+        std::snprintf(code, sizeof(code), "<0x%02X>", b);
+        auto bt = t.vocab.find(code);
+        if (bt == t.vocab.end()) break;
+        bytes.push_back(bt->second);
+      }
+      if (bytes.size() == piece.size()) {
+        ids.insert(ids.end(), bytes.begin(), bytes.end());
+        continue;
+      }
+    }
+    if (!t.has_unk) fail(JB_ERR_INVALID, "Unigram: no unknown token");
+    ids.push_back(t.unk_id);
+  }
+}
+
 void model(const jb_tokenizer& t, const std::vector<uint32_t>& word, std::vector<uint32_t>& ids) {
   if (t.model == kWordPiece) return wordpiece(t, word, ids);
+  if (t.model == kUnigram) return unigram(t, word, ids);
   if (t.model == kBpe) return bpe(t, word, ids);
   if (word.empty()) return;  // WordLevel: the word itself, else the unknown token
   auto it = t.vocab.find(to_utf8(word));
@@ -669,7 +920,20 @@ size_t gpt2_match(const std::vector<uint32_t>& c, size_t i) {
   return j - 1 - i;  // the last space goes to the next word
 }
 
-using Words = std::vector<std::vector<uint32_t>>;
+// Words of one piece, each with whether it starts at the text's offset 0
+// (Metaspace's "first" prepend scheme asks).
+struct Words {
+  std::vector<std::vector<uint32_t>> w;
+  std::vector<char> at0;
+  void add(const std::vector<uint32_t>& src, size_t b, size_t e, bool parent_at0) {
+    w.emplace_back(src.begin() + b, src.begin() + e);
+    at0.push_back(parent_at0 && b == 0);
+  }
+  void add(std::vector<uint32_t>&& v, bool flag) {
+    w.push_back(std::move(v));
+    at0.push_back(flag);
+  }
+};
 
 // The crate's split of one word: a list of (segment, is-match) covering it,
 // then `behavior` keeps, drops or merges the matches; empty pieces vanish.
@@ -678,7 +942,7 @@ struct Seg {
   bool m;
 };
 
-void emit(const std::vector<uint32_t>& w, const std::vector<Seg>& segs, int behavior, Words& out) {
+void emit(const std::vector<uint32_t>& w, bool at0, const std::vector<Seg>& segs, int behavior, Words& out) {
   std::vector<Seg> merged;
   bool prev = false;
   switch (behavior) {
@@ -711,7 +975,7 @@ void emit(const std::vector<uint32_t>& w, const std::vector<Seg>& segs, int beha
       break;
   }
   for (const Seg& g : merged)
-    if (g.e > g.b && !(behavior == kRemoved && g.m)) out.emplace_back(w.begin() + g.b, w.begin() + g.e);
+    if (g.e > g.b && !(behavior == kRemoved && g.m)) out.add(w, g.b, g.e, at0);
 }
 
 // Each character that satisfies the predicate is a match of its own.
@@ -730,8 +994,8 @@ std::vector<Seg> char_segments(const std::vector<uint32_t>& w, Pred is_delim) {
 }
 
 template <typename Pred>
-void split_chars(const std::vector<uint32_t>& w, Pred is_delim, int behavior, Words& out) {
-  emit(w, char_segments(w, is_delim), behavior, out);
+void split_chars(const std::vector<uint32_t>& w, bool at0, Pred is_delim, int behavior, Words& out) {
+  emit(w, at0, char_segments(w, is_delim), behavior, out);
 }
 
 // Length of the pattern's match starting at i (0: none there).
@@ -782,27 +1046,40 @@ std::vector<Seg> pattern_segments(const PreStep& st, const std::vector<uint32_t>
   return segs;
 }
 
-void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32_t>& w, Words& out) {
-  (void)t;
+void pre_step(const PreStep& st, const std::vector<uint32_t>& w, bool at0, Words& out) {
   switch (st.kind) {
     case kPreBert: {  // split on White_Space (removed), each punctuation character isolated
       Words parts;
-      split_chars(w, is_whitespace, kRemoved, parts);
-      for (const auto& p : parts) split_chars(p, is_punct, kIsolated, out);
+      split_chars(w, at0, is_whitespace, kRemoved, parts);
+      for (size_t k = 0; k < parts.w.size(); ++k) split_chars(parts.w[k], parts.at0[k], is_punct, kIsolated, out);
       return;
     }
     case kPreWhitespaceSplit:
-      split_chars(w, is_whitespace, kRemoved, out);
+      split_chars(w, at0, is_whitespace, kRemoved, out);
       return;
     case kPrePunctuation:
-      split_chars(w, is_punct, st.behavior, out);
+      split_chars(w, at0, is_punct, st.behavior, out);
       return;
     case kPreDigits:
-      split_chars(w, is_number, st.individual_digits ? kIsolated : kContiguous, out);
+      split_chars(w, at0, is_number, st.individual_digits ? kIsolated : kContiguous, out);
       return;
     case kPreSplit:
-      emit(w, pattern_segments(st, w), st.behavior, out);
+      emit(w, at0, pattern_segments(st, w), st.behavior, out);
       return;
+    case kPreMetaspace: {  // ' ' -> replacement, the prepend scheme, then split before each replacement
+      std::vector<uint32_t> c = w;
+      for (uint32_t& x : c)
+        if (x == ' ') x = st.replacement;
+      const bool prepend = st.prepend_scheme == kPrependAlways || (st.prepend_scheme == kPrependFirst && at0);
+      if (prepend && (c.empty() || c[0] != st.replacement)) c.insert(c.begin(), st.replacement);
+      if (!st.split) {
+        out.add(std::move(c), at0);
+        return;
+      }
+      const uint32_t r = st.replacement;
+      split_chars(c, at0, [r](uint32_t x) { return x == r; }, kMergedWithNext, out);
+      return;
+    }
     case kPreWhitespace: {  // the matches of \w+|[^\w\s]+; the rest dropped
       auto word = [](uint32_t c) { return is_word_char(c); };
       for (size_t i = 0; i < w.size();) {
@@ -813,7 +1090,7 @@ void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32
         const bool wd = word(w[i]);
         size_t j = i + 1;
         while (j < w.size() && !is_whitespace(w[j]) && word(w[j]) == wd) ++j;
-        out.emplace_back(w.begin() + i, w.begin() + j);
+        out.add(w, i, j, at0);
         i = j;
       }
       return;
@@ -826,12 +1103,12 @@ void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32
           ++i;
           continue;
         }
-        if (seg < i) out.emplace_back(w.begin() + seg, w.begin() + i);
-        out.emplace_back(w.begin() + i, w.begin() + i + len);
+        if (seg < i) out.add(w, seg, i, at0);
+        out.add(w, i, i + len, at0);
         i += len;
         seg = i;
       }
-      if (seg < w.size()) out.emplace_back(w.begin() + seg, w.end());
+      if (seg < w.size()) out.add(w, seg, w.size(), at0);
       return;
     }
     case kPreByteLevel: {
@@ -845,7 +1122,7 @@ void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32
         for (size_t k = i; k < i + len; ++k) append_utf8(c[k], utf8);
         std::vector<uint32_t> sym;
         for (unsigned char b : utf8) sym.push_back(bs[b]);
-        out.push_back(std::move(sym));
+        out.add(std::move(sym), at0 && i == 0);
         i += len;
       }
       return;
@@ -853,16 +1130,18 @@ void pre_step(const jb_tokenizer& t, const PreStep& st, const std::vector<uint32
   }
 }
 
-void pre_tokenize_and_model(const jb_tokenizer& t, const std::string& piece, std::vector<uint32_t>& ids) {
-  Words words(1);
-  decode_utf8(piece.data(), piece.size(), words[0]);
-  if (words[0].empty()) return;
+void pre_tokenize_and_model(const jb_tokenizer& t, const std::string& piece, bool at0, std::vector<uint32_t>& ids) {
+  Words words;
+  std::vector<uint32_t> c;
+  decode_utf8(piece.data(), piece.size(), c);
+  if (c.empty()) return;
+  words.add(std::move(c), at0);
   for (const PreStep& st : t.pre) {
     Words next;
-    for (const auto& w : words) pre_step(t, st, w, next);
-    words.swap(next);
+    for (size_t k = 0; k < words.w.size(); ++k) pre_step(st, words.w[k], words.at0[k], next);
+    words = std::move(next);
   }
-  for (const auto& w : words) model(t, w, ids);
+  for (const auto& w : words.w) model(t, w, ids);
 }
 
 // ---- added tokens -----------------------------------------------------------
@@ -950,8 +1229,8 @@ void encode(const jb_tokenizer& t, const char* s, size_t n, int max_length, std:
     for (const Piece& q : split_added(normed, t.norm_added)) {
       if (q.id >= 0)
         ids.push_back(static_cast<uint32_t>(q.id));
-      else
-        pre_tokenize_and_model(t, normed.substr(q.begin, q.end - q.begin), ids);
+      else  // a piece at the text's start stays there whatever the normaliser deleted
+        pre_tokenize_and_model(t, normed.substr(q.begin, q.end - q.begin), p.begin == 0 && q.begin == 0, ids);
     }
   }
   const size_t specials = t.before.size() + t.after.size();
@@ -989,6 +1268,47 @@ void add_merge(jb_tokenizer& t, size_t rank, const std::string& a, const std::st
                                                                         iab->second};
 }
 
+std::string base64_decode(const std::string& in) {
+  auto val = [](char c) -> int {
+    if (c >= 'A' && c <= 'Z') return c - 'A';
+    if (c >= 'a' && c <= 'z') return c - 'a' + 26;
+    if (c >= '0' && c <= '9') return c - '0' + 52;
+    if (c == '+' || c == '-') return 62;
+    if (c == '/' || c == '_') return 63;
+    return -1;
+  };
+  std::string out;
+  uint32_t acc = 0;
+  int bits = 0;
+  for (char c : in) {
+    const int v = val(c);
+    if (v < 0) continue;  // padding, whitespace
+    acc = (acc << 6) | static_cast<uint32_t>(v);
+    bits += 6;
+    if (bits >= 8) {
+      bits -= 8;
+      out.push_back(static_cast<char>((acc >> bits) & 0xFF));
+    }
+  }
+  return out;
+}
+
+// The charsmap blob: u32 little-endian trie size in bytes, the double array,
+// then the NUL-separated replacement strings.
+CharsMap parse_charsmap(const std::string& b64) {
+  const std::string raw = base64_decode(b64);
+  if (raw.size() < 4) fail(JB_ERR_IO, "tokenizer.json: Precompiled charsmap too short");
+  uint32_t trie_bytes = 0;
+  std::memcpy(&trie_bytes, raw.data(), 4);
+  if (trie_bytes % 4 || 4 + static_cast<size_t>(trie_bytes) > raw.size())
+    fail(JB_ERR_IO, "tokenizer.json: Precompiled charsmap is malformed");
+  CharsMap m;
+  m.units.resize(trie_bytes / 4);
+  std::memcpy(m.units.data(), raw.data() + 4, trie_bytes);
+  m.normalized = raw.substr(4 + trie_bytes);
+  return m;
+}
+
 std::vector<uint32_t> cps_of(const std::string& u) {
   std::vector<uint32_t> c;
   decode_utf8(u.data(), u.size(), c);
@@ -1017,6 +1337,9 @@ void parse_normalizer(jb_tokenizer& t, const Json& nz) {
     st.op = kNormLower;
   } else if (type == "StripAccents") {
     st.op = kNormStripAccents;
+  } else if (type == "Precompiled") {
+    st.op = kNormPrecompiled;
+    t.charsmap = parse_charsmap(nz.str_or("precompiled_charsmap", ""));
   } else if (type == "Strip") {
     st.op = kNormStrip;
     st.left = nz.bool_or("strip_left", true);
@@ -1034,8 +1357,10 @@ void parse_normalizer(jb_tokenizer& t, const Json& nz) {
       st.a = cps_of(lit->str);
     } else if (re && re->kind == Json::Str && re->str == "\\s+") {
       st.op = kNormReplaceSpaceRuns;
+    } else if (re && re->kind == Json::Str && re->str == " {2,}") {
+      st.op = kNormReplaceSpaces2;
     } else {
-      fail(JB_ERR_INVALID, "tokenizer.json: Replace supports string patterns and the regex \\s+");
+      fail(JB_ERR_INVALID, "tokenizer.json: Replace supports string patterns and the regexes \\s+ and ' {2,}'");
     }
   } else {
     fail(JB_ERR_INVALID, "tokenizer.json: unsupported normalizer " + type);
@@ -1100,6 +1425,18 @@ void parse_pre_tokenizer(jb_tokenizer& t, const Json& pt) {
     } else {
       fail(JB_ERR_INVALID, "tokenizer.json: Split without a pattern");
     }
+  } else if (type == "Metaspace") {
+    st.kind = kPreMetaspace;
+    const std::vector<uint32_t> rep = cps_of(pt.str_or("replacement", "\xE2\x96\x81"));
+    if (rep.size() != 1) fail(JB_ERR_INVALID, "tokenizer.json: Metaspace replacement must be one character");
+    st.replacement = rep[0];
+    const std::string scheme = pt.str_or("prepend_scheme", "");
+    if (scheme == "always") st.prepend_scheme = kPrependAlways;
+    else if (scheme == "first") st.prepend_scheme = kPrependFirst;
+    else if (scheme == "never") st.prepend_scheme = kPrependNever;
+    else if (scheme.empty()) st.prepend_scheme = pt.bool_or("add_prefix_space", true) ? kPrependAlways : kPrependNever;
+    else fail(JB_ERR_INVALID, "tokenizer.json: unknown Metaspace prepend_scheme " + scheme);
+    st.split = pt.bool_or("split", true);
   } else if (type == "Digits") {
     st.kind = kPreDigits;
     st.individual_digits = pt.bool_or("individual_digits", false);
@@ -1174,13 +1511,52 @@ jb_tokenizer* load(const char* path) {
   std::unique_ptr<jb_tokenizer> t(new jb_tokenizer());
   const Json* model = j.get("model");
   const std::string type = model ? model->str_or("type", "") : "";
-  if (type != "WordPiece" && type != "BPE" && type != "WordLevel")
-    fail(JB_ERR_INVALID, "tokenizer.json: unsupported model '" + type + "' (WordPiece, BPE and WordLevel are supported)");
-  t->model = type == "WordPiece" ? kWordPiece : type == "BPE" ? kBpe : kWordLevel;
+  if (type != "WordPiece" && type != "BPE" && type != "WordLevel" && type != "Unigram")
+    fail(JB_ERR_INVALID, "tokenizer.json: unsupported model '" + type + "' (WordPiece, BPE, WordLevel and Unigram are supported)");
+  t->model = type == "WordPiece" ? kWordPiece : type == "BPE" ? kBpe : type == "WordLevel" ? kWordLevel : kUnigram;
   const Json* vocab = model->get("vocab");
-  if (!vocab || vocab->kind != Json::Obj) fail(JB_ERR_IO, "tokenizer.json: model.vocab missing");
-  for (const auto& kv : vocab->obj) t->vocab[kv.first] = static_cast<uint32_t>(kv.second.num);
-  if (t->model == kWordLevel) {
+  if (t->model == kUnigram) {  // [[piece, score], ...]; ids are positions
+    if (!vocab || vocab->kind != Json::Arr) fail(JB_ERR_IO, "tokenizer.json: Unigram vocab missing");
+    std::unordered_map<uint64_t, uint32_t> edges;
+    t->trie.piece.assign(1, -1);
+    t->min_score = vocab->arr.empty() ? 0.0 : 1e300;
+    for (size_t id = 0; id < vocab->arr.size(); ++id) {
+      const Json& e = vocab->arr[id];
+      if (e.kind != Json::Arr || e.arr.size() < 2 || e.arr[0].kind != Json::Str)
+        fail(JB_ERR_IO, "tokenizer.json: bad Unigram vocabulary entry");
+      const std::string& piece = e.arr[0].str;
+      t->vocab[piece] = static_cast<uint32_t>(id);
+      t->scores.push_back(e.arr[1].num);
+      t->min_score = std::min(t->min_score, e.arr[1].num);
+      uint32_t node = 0;
+      for (unsigned char ch : piece) {
+        const uint64_t key = (static_cast<uint64_t>(node) << 8) | ch;
+        auto it = edges.find(key);
+        if (it == edges.end()) {
+          const uint32_t child = static_cast<uint32_t>(t->trie.piece.size());
+          t->trie.piece.push_back(-1);
+          it = edges.emplace(key, child).first;
+        }
+        node = it->second;
+      }
+      if (node) t->trie.piece[node] = static_cast<int32_t>(id);
+    }
+    t->trie.edges.assign(edges.begin(), edges.end());
+    std::sort(t->trie.edges.begin(), t->trie.edges.end());
+    if (const Json* u = model->get("unk_id"); u && u->kind == Json::Num) {
+      if (u->num < 0 || u->num >= static_cast<double>(vocab->arr.size()))
+        fail(JB_ERR_IO, "tokenizer.json: Unigram unk_id out of range");
+      t->unk_id = static_cast<uint32_t>(u->num);
+      t->has_unk = true;
+    }
+    t->byte_fallback = model->bool_or("byte_fallback", false);
+  } else {
+    if (!vocab || vocab->kind != Json::Obj) fail(JB_ERR_IO, "tokenizer.json: model.vocab missing");
+    for (const auto& kv : vocab->obj) t->vocab[kv.first] = static_cast<uint32_t>(kv.second.num);
+  }
+  if (t->model == kUnigram) {
+    // parsed above
+  } else if (t->model == kWordLevel) {
     if (const Json* unk = model->get("unk_token"); unk && unk->kind == Json::Str) {
       auto it = t->vocab.find(unk->str);
       t->has_unk = it != t->vocab.end();

@@ -102,9 +102,9 @@ def test_many_texts_use_all_cores_in_order(tmp_path):
 def test_unsupported_tokenizer_is_rejected(tmp_path):
     from jammi_b200 import Tokenizer
     from jammi_b200._lib import JbError
-    for doc in ({"model": {"type": "Unigram", "vocab": [["a", 0.0]]}},
+    for doc in ({"model": {"type": "SomethingElse", "vocab": [["a", 0.0]]}},
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
-                 "pre_tokenizer": {"type": "Metaspace", "replacement": "_"}},
+                 "pre_tokenizer": {"type": "UnicodeScripts"}},
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
                  "normalizer": {"type": "NFKC"}},
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": ["a b"]}}):

@@ -118,7 +118,7 @@ def test_unsupported_components_still_fail_loudly(tmp_path):
     base = {"model": {"type": "WordPiece", "vocab": {"[UNK]": 0, "a": 1}, "unk_token": "[UNK]"}}
     for extra in ({"normalizer": {"type": "NFKC"}},
                   {"normalizer": {"type": "Replace", "pattern": {"Regex": "a+"}, "content": "b"}},
-                  {"pre_tokenizer": {"type": "Metaspace", "replacement": "_"}},
+                  {"pre_tokenizer": {"type": "CharDelimiterSplit", "delimiter": "_"}},
                   {"pre_tokenizer": {"type": "Punctuation", "behavior": "Sideways"}}):
         path = tmp_path / "bad.json"
         path.write_text(json.dumps({**base, **extra}))
