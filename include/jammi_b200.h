@@ -401,7 +401,7 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
  * A model's tokenizer.json through the HuggingFace `tokenizers` pipeline the
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/
  * tokenizer.rs:21-78): added tokens (normalized / lstrip / rstrip /
- * single_word), normalisers BertNormalizer, NFC, NFD, Lowercase,
+ * single_word), normalisers BertNormalizer, NFC, NFD, NFKC, NFKD, Lowercase,
  * StripAccents, Strip, Prepend, Replace (string patterns, regexes \s+ and
  * ' {2,}'), Precompiled (sentencepiece character maps) and Sequences,
  * pre-tokenisers BertPreTokenizer, ByteLevel, Whitespace, WhitespaceSplit,
@@ -412,8 +412,8 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
  * TemplateProcessing, BertProcessing, RobertaProcessing, ByteLevel (and
  * Sequences), truncation to max_length (special ids included) or else the
  * file's own.  That covers the BERT (with RoBERTa, CamemBERT, XLM-RoBERTa),
- * DistilBERT, ModernBERT and CLIP families; other components (NFKC, other
- * regexes, ...) answer JB_ERR_INVALID at load.  Output is the ragged layout of jb_generate_embeddings: ids of text i
+ * DistilBERT, ModernBERT and CLIP families; other components (other regexes,
+ * UnicodeScripts, ...) answer JB_ERR_INVALID at load.  Output is the ragged layout of jb_generate_embeddings: ids of text i
  * at ids[offsets[i] .. offsets[i+1]). */
 typedef struct jb_tokenizer jb_tokenizer;
 jb_status jb_tokenizer_load(const char* tokenizer_json_path, jb_tokenizer** out);

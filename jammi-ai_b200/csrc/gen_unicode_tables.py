@@ -5,6 +5,8 @@ unicodedata:
 
 * per-code-point lowercase mappings (one code point at a time, as the HF
   normaliser lowercases, so there is no final-sigma context),
+* compatibility decompositions (full NFKD of each character, where it differs
+  from the canonical one; for NFKC / NFKD),
 * canonical decompositions (full, recursive; Hangul syllables are decomposed
   algorithmically in the C++ code) and canonical combining classes (for the
   canonical reordering of NFD),
@@ -125,6 +127,14 @@ def main():
         if d != chr(cp):
             decomp.append((cp, [ord(c) for c in d]))
 
+    kdecomp = []  # (cp, [decomposed...]) compatibility, full, where it differs from the canonical one
+    for cp in range(MAX_CP):
+        if 0xD800 <= cp <= 0xDFFF or cp in HANGUL:
+            continue
+        k = unicodedata.normalize("NFKD", chr(cp))
+        if k != unicodedata.normalize("NFD", chr(cp)):
+            kdecomp.append((cp, [ord(c) for c in k]))
+
     ccc = [(cp, unicodedata.combining(chr(cp))) for cp in range(MAX_CP)
            if not 0xD800 <= cp <= 0xDFFF and unicodedata.combining(chr(cp))]
 
@@ -186,6 +196,7 @@ def main():
         "};",
         seq_table("kLower", lower),
         seq_table("kDecomp", decomp),
+        seq_table("kCompatDecomp", kdecomp),
         "static const CccEntry kCcc[] = {",
         *[f"  {{0x{cp:X}, {c}}}," for cp, c in ccc],
         "};",

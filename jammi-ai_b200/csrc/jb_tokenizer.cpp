@@ -18,7 +18,7 @@
 //                  handle_chinese_chars (spaces around CJK ideographs),
 //                  strip_accents (NFD, then drop category Mn; on by default
 //                  when lowercase is), lowercase (one code point at a time);
-//                  NFC, NFD, Lowercase, StripAccents (drop category M*, no
+//                  NFC, NFD, NFKC, NFKD, Lowercase, StripAccents (drop category M*, no
 //                  decomposition of its own), Strip, Prepend (non-empty
 //                  pieces), Replace (string patterns, or the regexes \s+
 //                  and ' {2,}'), Precompiled (sentencepiece's character map,
@@ -119,7 +119,7 @@ struct AddedSet {
   }
 };
 
-enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace,
+enum NormOp { kNormBert, kNormNfc, kNormNfd, kNormNfkc, kNormNfkd, kNormLower, kNormStripAccents, kNormStrip, kNormPrepend, kNormReplace,
               kNormReplaceSpaceRuns, kNormReplaceSpaces2, kNormPrecompiled };
 struct NormStep {
   int op = kNormBert;
@@ -321,10 +321,13 @@ const std::vector<uint32_t>& byte_symbols() {
 // Canonical decomposition (NFD): full decompositions from the table, Hangul
 // syllables by the Unicode algorithm, then the canonical ordering of each run
 // of combining marks by combining class (stable).
-void nfd(const std::vector<uint32_t>& in, std::vector<uint32_t>& out) {
+void nfd(const std::vector<uint32_t>& in, std::vector<uint32_t>& out, bool compat = false) {
   out.clear();
   for (uint32_t c : in) {
-    if (c >= 0xAC00 && c < 0xAC00 + 11172) {
+    const uni::SeqEntry* k = compat ? find_seq(uni::kCompatDecomp, c) : nullptr;
+    if (k) {
+      out.insert(out.end(), uni::kCompatDecomp_seq + k->off, uni::kCompatDecomp_seq + k->off + k->n);
+    } else if (c >= 0xAC00 && c < 0xAC00 + 11172) {
       const uint32_t s = c - 0xAC00;
       out.push_back(0x1100 + s / 588);
       out.push_back(0x1161 + (s % 588) / 28);
@@ -367,9 +370,9 @@ uint32_t compose_pair(uint32_t a, uint32_t b) {
 // NFC: NFD, then the canonical composition algorithm -- each character joins
 // the last starter unless a character between them has combining class 0 or
 // a class >= its own (blocked).
-void nfc(const std::vector<uint32_t>& in, std::vector<uint32_t>& out) {
+void nfc(const std::vector<uint32_t>& in, std::vector<uint32_t>& out, bool compat = false) {
   std::vector<uint32_t> d;
-  nfd(in, d);
+  nfd(in, d, compat);
   out.clear();
   long starter = -1;
   for (uint32_t c : d) {
@@ -583,6 +586,8 @@ void normalize(const jb_tokenizer& t, std::vector<uint32_t>& cps) {
       }
       case kNormNfc: nfc(cps, tmp); cps.swap(tmp); break;
       case kNormNfd: nfd(cps, tmp); cps.swap(tmp); break;
+      case kNormNfkc: nfc(cps, tmp, true); cps.swap(tmp); break;
+      case kNormNfkd: nfd(cps, tmp, true); cps.swap(tmp); break;
       case kNormLower: lowercase_cps(cps); break;
       case kNormStripAccents:  // every combining mark (category M*), no decomposition first
         tmp.clear();
@@ -1333,6 +1338,10 @@ void parse_normalizer(jb_tokenizer& t, const Json& nz) {
     st.op = kNormNfc;
   } else if (type == "NFD") {
     st.op = kNormNfd;
+  } else if (type == "NFKC") {
+    st.op = kNormNfkc;
+  } else if (type == "NFKD") {
+    st.op = kNormNfkd;
   } else if (type == "Lowercase") {
     st.op = kNormLower;
   } else if (type == "StripAccents") {

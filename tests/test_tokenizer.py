@@ -106,7 +106,7 @@ def test_unsupported_tokenizer_is_rejected(tmp_path):
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
                  "pre_tokenizer": {"type": "UnicodeScripts"}},
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": []},
-                 "normalizer": {"type": "NFKC"}},
+                 "normalizer": {"type": "ByteLevel"}},
                 {"model": {"type": "BPE", "vocab": {"a": 0}, "merges": ["a b"]}}):
         path = tmp_path / "bad.json"
         path.write_text(json.dumps(doc))

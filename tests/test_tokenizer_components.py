@@ -19,6 +19,7 @@ REF_TOKENIZER = "/root/reference/cookbook/fixtures/tiny_bert/tokenizer.json"
 EXTRA = CASES + [
     "Mc: कः  Me: a⃝  Mn: é", "  padded both ends  ", "x__y _z_ a-b-c", "...!!!???", "a1b22c333 4444",
     "१२३ ٣٤ ½ ²", "don't stop", "[CLS] [SEP]", "ab" * 30,
+    "ｆｕｌｌ ① ㍻ ﬁ ¼ Å Ǆ ᾯ ẛ̣ 가각 ㈜ ⅷ",
 ]
 
 
@@ -56,6 +57,8 @@ def _normalizers():
         "strip_left": n.Strip(left=True, right=False),
         "prepend_replace": n.Sequence([n.Replace(" ", "_"), n.Prepend("_")]),
         "replace_multi": n.Sequence([n.Replace("ab", "X"), n.Replace("  ", " ")]),
+        "nfkc": n.NFKC(),
+        "nfkd_lower": n.Sequence([n.NFKD(), n.Lowercase()]),
     }
 
 
@@ -116,7 +119,7 @@ def test_unsupported_components_still_fail_loudly(tmp_path):
     from jammi_b200 import Tokenizer
     from jammi_b200._lib import JbError
     base = {"model": {"type": "WordPiece", "vocab": {"[UNK]": 0, "a": 1}, "unk_token": "[UNK]"}}
-    for extra in ({"normalizer": {"type": "NFKC"}},
+    for extra in ({"normalizer": {"type": "ByteLevel"}},
                   {"normalizer": {"type": "Replace", "pattern": {"Regex": "a+"}, "content": "b"}},
                   {"pre_tokenizer": {"type": "CharDelimiterSplit", "delimiter": "_"}},
                   {"pre_tokenizer": {"type": "Punctuation", "behavior": "Sideways"}}):
