@@ -1,9 +1,11 @@
 """The remaining tokenizer.json components the native tokenizer reads --
-StripAccents, Strip, Prepend and Replace normalisers; Whitespace,
-WhitespaceSplit, Punctuation (every split behaviour) and Digits
-pre-tokenisers; Sequences of them -- against HuggingFace `tokenizers`, id for
-id, and the reference's own fixture tokenizer (cookbook/fixtures/tiny_bert:
-Lowercase + StripAccents, Whitespace, WordPiece).  CPU only."""
+StripAccents, Strip, Prepend, Replace, NFKC and NFKD normalisers;
+Whitespace, WhitespaceSplit, Punctuation (every split behaviour), Digits and
+Split pre-tokenisers; Sequences of them; the WordLevel model -- against
+HuggingFace `tokenizers`, id for id, and the reference's own fixture
+tokenizers (cookbook/fixtures/tiny_bert: Lowercase + StripAccents,
+Whitespace, WordPiece; tests/fixtures/tiny_open_clip: WordLevel over
+characters).  CPU only."""
 import json
 import os
 
