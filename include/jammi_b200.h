@@ -149,11 +149,17 @@ jb_status jb_encode_text_device(jb_model* model, const uint32_t* d_ids, const ui
  * another runtime's pool has none to allocate.  No counterpart in the
  * reference.  It calls no cudaMalloc, cudaFree or allocating library
  * routine; its scratch is a 64 MiB file-scope device array that every GPU
- * loading this library holds until exit.  Requests whose
- * jb_estimate_batch_bytes exceeds 64 MiB return JB_ERR_INVALID.  All calls on
- * a device share that array (it keeps the previous call's contents): calls
- * that overlap on the GPU race.  The first call on a device looks up the
- * array's device address; make it before any stream capture. */
+ * loading this library holds until exit.  BERT-family handles only (BERT,
+ * DistilBERT, ModernBERT); an OpenCLIP text or vision handle returns
+ * JB_ERR_INVALID.  Requests whose jb_estimate_batch_bytes exceeds 64 MiB
+ * return JB_ERR_INVALID.  All calls on a device share that array (it keeps
+ * the previous call's contents): calls that overlap on the GPU race.  The
+ * first call on a device looks up the array's device address; make it
+ * before any stream capture.  Like jb_encode_text_device it queues work and
+ * returns: an out-of-vocabulary id or a length above max_seq found on the
+ * device is reported by the handle's next synchronising call.  A handle
+ * does not survive cudaDeviceReset (its weights are gone), and neither does
+ * the looked-up address. */
 jb_status jb_encode_text_device_noalloc(jb_model* model, const uint32_t* d_ids,
                                         const uint32_t* d_lens, int batch, int max_seq,
                                         int pooling, float* d_out, void* stream);

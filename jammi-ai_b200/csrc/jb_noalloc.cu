@@ -24,7 +24,13 @@
 //    only discarded tile rows of the GEMMs);
 //  * the first call on a device resolves the array's device address
 //    (cudaGetSymbolAddress, with that device current); make that first call
-//    before any stream capture.
+//    before any stream capture.  Nothing else is set up on a call: the int8
+//    GELU table (also a file-scope device array) is built when an int8 model
+//    loads.  The cached address is not valid after cudaDeviceReset, which
+//    also invalidates every model handle on that device;
+//  * device-side input errors (an id outside the vocabulary, a length above
+//    max_seq) are flagged on the device and reported by the handle's next
+//    synchronising call, as for jb_encode_text_device.
 #include <mutex>
 
 #include "jb_model.h"
@@ -79,7 +85,12 @@ extern "C" jb_status jb_encode_text_device_noalloc(jb_model* m, const uint32_t* 
                                                    int pooling, float* d_out, void* stream) {
   try {
     if (!m) jb::fail(JB_ERR_INVALID, "null model");
-    if (m->family != JB_FAMILY_BERT) jb::fail(JB_ERR_INVALID, "model is not a text encoder");
+    if (m->family != JB_FAMILY_BERT)
+      jb::fail(JB_ERR_INVALID, m->family == JB_FAMILY_CLIP_TEXT
+                                   ? "jb_encode_text_device_noalloc serves BERT-family encoders only, "
+                                     "not the OpenCLIP text tower"
+                                   : "jb_encode_text_device_noalloc serves BERT-family text encoders "
+                                     "only, not an image encoder");
     if (batch < 0 || max_seq < 0) jb::fail(JB_ERR_INVALID, "batch and max_seq must be >= 0");
     if (pooling < JB_POOL_MEAN || pooling > JB_POOL_WEIGHTED_MEAN) jb::fail(JB_ERR_INVALID, "unknown pooling");
     if (max_seq > m->max_pos)

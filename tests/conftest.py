@@ -11,6 +11,16 @@ for p in (ROOT, PKG_DIR):
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
+# A checkout of the reference (f-inverse/jammi-ai), where one exists: the
+# tests that re-read its own fixtures (weights, tokenizer files) run only
+# when JAMMI_REFERENCE names it, and skip otherwise.
+REFERENCE = os.environ.get("JAMMI_REFERENCE", "")
+
+
+def reference_path(*parts):
+    """A file inside the reference checkout, or "" when none is configured."""
+    return os.path.join(REFERENCE, *parts) if REFERENCE else ""
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")

@@ -1,6 +1,9 @@
 """Generate the golden fixtures under tests/golden/ (run once, here, on CPU).
 
-    python tests/golden/make_golden.py
+    JAMMI_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+
+(``reference_tiny_bert.npz`` needs the reference checkout, named by the
+JAMMI_REFERENCE environment variable; the other fixtures need nothing.)
 
 Expected outputs come from HuggingFace ``transformers`` (``BertModel`` and
 ``CLIPVisionModelWithProjection``, eager attention, float64), an independent
@@ -50,7 +53,8 @@ from oracle.bert import BertConfig, random_bert_weights  # noqa: E402  (weight r
 from oracle.clip import (ClipTextConfig, ClipVisionConfig, random_clip_text_batch,  # noqa: E402
                          random_clip_text_weights, random_clip_weights)
 
-REF_TINY_BERT = "/root/reference/cookbook/fixtures/tiny_bert"
+REF_ROOT = os.environ.get("JAMMI_REFERENCE", "")
+REF_TINY_BERT = os.path.join(REF_ROOT, "cookbook", "fixtures", "tiny_bert") if REF_ROOT else ""
 
 
 def torch_pool_all(hidden: torch.Tensor, mask: torch.Tensor) -> dict:
@@ -400,8 +404,8 @@ def modernbert_fixture(name, cfg: dict, seed, lens, S):
 
 
 def reference_fixture():
-    st = os.path.join(REF_TINY_BERT, "model.safetensors")
-    if not os.path.exists(st):
+    st = os.path.join(REF_TINY_BERT, "model.safetensors") if REF_TINY_BERT else ""
+    if not st or not os.path.exists(st):
         print("reference checkout absent: reference_tiny_bert.npz not regenerated")
         return
     from safetensors.numpy import load_file

@@ -1,6 +1,6 @@
 """Generate tests/golden/reference_tiny_bert_tokens.json (run once, here, on CPU).
 
-    python tests/golden/make_token_golden.py
+    JAMMI_REFERENCE=<reference checkout> python tests/golden/make_token_golden.py
 
 Token ids of seeded synthetic texts under the reference's own fixture
 tokenizers (cookbook/fixtures/tiny_bert/tokenizer.json: Lowercase +
@@ -18,8 +18,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_TOKENIZER = "/root/reference/cookbook/fixtures/tiny_bert/tokenizer.json"
-REF_CLIP_TOKENIZER = "/root/reference/tests/fixtures/tiny_open_clip/tokenizer.json"
+REF_ROOT = os.environ.get("JAMMI_REFERENCE", "")
+REF_TOKENIZER = os.path.join(REF_ROOT, "cookbook", "fixtures", "tiny_bert", "tokenizer.json")
+REF_CLIP_TOKENIZER = os.path.join(REF_ROOT, "tests", "fixtures", "tiny_open_clip", "tokenizer.json")
 
 ALPHABET = ("abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789     .,;:!?'\"()-_/"
             "àáâäãåæçèéêëìíîïñòóôöõøùúûüýÿßÀÉÎÕÜ" "αβγΣσ" "東京数据" "̣́̈" "\t\n　" "😀€…—«»")
@@ -45,7 +46,7 @@ def texts(seed=0, n=120):
 
 def main():
     from tokenizers import Tokenizer
-    if not os.path.exists(REF_TOKENIZER):
+    if not REF_ROOT or not os.path.exists(REF_TOKENIZER):
         sys.exit("reference checkout not present")
     tok = Tokenizer.from_file(REF_TOKENIZER)
     ts = texts()

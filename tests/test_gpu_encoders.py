@@ -4,8 +4,10 @@ the golden vectors and the CPU oracle.
 Acceptance (per row, on the L2-normalised embedding):
 * f32 format:  max |gpu - ref| <= 1e-4 and cosine >= 0.9999
 * bf16 format: max |gpu - ref| <= 2e-3 and cosine >= 0.9999
-* int8 format: the same bf16 bar, against the int8 oracle (same quantisation
-  points, integer-exact accumulation); the s32 accumulators themselves are
+* int8 format: the same bf16 bar, against the int8 oracle with bf16 storage
+  between operators (``oracle.quant.bert_int8_bf16_embed``: the same
+  quantisation points and the same bf16 rounding points, integer-exact
+  accumulation), on every row length; the s32 accumulators themselves are
   checked bit-exact in test_gpu_ops.py.
 """
 import json
@@ -90,7 +92,7 @@ def test_distilbert_golden(fmt):
     out = model.encode(ids, lens)
     if fmt == "int8":  # the int8 oracle over the same weights, renamed onto BERT
         bw, cfg = ob.distilbert_as_bert(w, d_cfg)
-        ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(bw, cfg, ids, mask), mask)
+        ref = oq.bert_int8_bf16_embed(bw, cfg, ids, lens)
     else:
         ref = g["pooled_mean"]
     assert_close_rows(out, ref, fmt)
@@ -170,7 +172,7 @@ def test_bert_base_int8_config():
     rng = np.random.default_rng(302)
     lens = rng.integers(32, 257, size=8)
     ids, mask = ob.random_token_batch(8, 256, lens, seed=303)
-    ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    ref = oq.bert_int8_bf16_embed(w, cfg, ids, lens)
     out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
     assert_close_rows(out, ref, "int8")
     # and the quantisation error itself stays small against the float model
@@ -178,10 +180,38 @@ def test_bert_base_int8_config():
     assert (out * fref).sum(1).min() > 0.995
 
 
+def test_bert_base_int8_sharded_job_lengths():
+    """The sharded job's rows: BERT-base int8, 128 rows with lengths
+    lognormal(4.5, 0.8) clipped to [8, 512] (about half of them under 96
+    tokens), plus rows of exactly 8 tokens and one of 512, at the bar on
+    every row."""
+    cfg, w = _bert_base(501)
+    rng = np.random.default_rng(502)
+    lens = np.clip(np.round(rng.lognormal(4.5, 0.8, size=128)), 8, 512).astype(int)
+    lens[:3] = (8, 8, 512)
+    ids, _ = ob.random_token_batch(128, 512, lens, seed=503)
+    ref = oq.bert_int8_bf16_embed(w, cfg, ids, lens)
+    out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
+    assert_close_rows(out, ref, "int8")
+
+
+def test_bert_base_int8_short_rows():
+    """Rows of 1 to 48 tokens (a lone [CLS], [CLS] [SEP], ...): the mean pool
+    averages little of the quantisation noise here, so these rows are the
+    hardest for the int8 bar."""
+    cfg, w = _bert_base(511)
+    lens = np.arange(1, 49)
+    ids, _ = ob.random_token_batch(48, 48, lens, seed=512)
+    ref = oq.bert_int8_bf16_embed(w, cfg, ids, lens)
+    out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
+    assert_close_rows(out, ref, "int8")
+
+
 def test_bert_large_prequantised_int8():
-    """BERT-large layout in the int8 checkpoint format: int8 weights with
-    per-output-channel scales log-uniform in [1e-3, 1e-1]; lengths lognormal."""
-    cfg = ob.BertConfig(1024, 2, 16, 4096, 30522, 512)  # 2 of 24 layers keep the oracle fast
+    """BERT-large in the int8 checkpoint format, full depth (24 layers): int8
+    weights with per-output-channel scales log-uniform in [1e-3, 1e-1];
+    32 rows with lengths lognormal(5.0, 0.6) clipped to [8, 512]."""
+    cfg = ob.BertConfig(1024, 24, 16, 4096, 30522, 512)
     w = ob.random_bert_weights(cfg, seed=401)
     rng = np.random.default_rng(402)
     for n in range(cfg.num_hidden_layers):
@@ -191,9 +221,10 @@ def test_bert_large_prequantised_int8():
             del w[k + ".weight"]
             w[k + ".weight_q"] = q
             w[k + ".weight_scale"] = s
-    lens = np.clip(np.round(rng.lognormal(5.0, 0.6, size=6)), 8, 512).astype(int)
-    ids, mask = ob.random_token_batch(6, int(lens.max()), lens, seed=403)
-    ref = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    lens = np.clip(np.round(rng.lognormal(5.0, 0.6, size=32)), 8, 512).astype(int)
+    lens[0] = 8
+    ids, _ = ob.random_token_batch(32, int(lens.max()), lens, seed=403)
+    ref = oq.bert_int8_bf16_embed(w, cfg, ids, lens)
     out = _bert(w, cfg.to_dict(), "int8").encode(ids, lens)
     assert_close_rows(out, ref, "int8")
 
@@ -203,7 +234,7 @@ def test_clip_vit_b32_bf16_config():
     from jammi_b200 import OpenClipVisionTransformer
     cfg = oc.ClipVisionConfig()
     w = oc.random_clip_weights(cfg, seed=501)
-    px = np.random.default_rng(502).standard_normal((6, 3, 224, 224)).astype(np.float32)
+    px = np.random.default_rng(502).standard_normal((16, 3, 224, 224)).astype(np.float32)
     ref = oc.l2_normalize_image(oc.clip_vision_forward(w, cfg, px))
     model = OpenClipVisionTransformer.from_weights(w, cfg.to_open_clip_config(), device=0, fmt="bf16")
     assert_close_rows(model.forward_image(px), ref, "bf16")

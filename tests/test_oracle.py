@@ -7,13 +7,13 @@ import os
 import numpy as np
 import pytest
 
-from conftest import load_golden
+from conftest import load_golden, reference_path
 from oracle import bert as ob
 from oracle import clip as oc
 from oracle import image as oimg
 from oracle import quant as oq
 
-REF_FIXTURE = "/root/reference/cookbook/fixtures/tiny_bert"
+REF_FIXTURE = reference_path("cookbook", "fixtures", "tiny_bert")
 
 
 # ── crates/jammi-encoders/tests/it/pooling.rs:15-83 (known answers) ─────────
@@ -137,8 +137,8 @@ def test_modernbert_rope_table():
 
 def test_bert_oracle_on_reference_fixture():
     z = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert.npz"))
-    st = os.path.join(REF_FIXTURE, "model.safetensors")
-    if not os.path.exists(st):
+    st = os.path.join(REF_FIXTURE, "model.safetensors") if REF_FIXTURE else ""
+    if not st or not os.path.exists(st):
         pytest.skip("reference checkout not present")
     assert hashlib.sha256(open(st, "rb").read()).hexdigest() == bytes(z["sha256"]).decode()
     from safetensors.numpy import load_file
@@ -227,6 +227,66 @@ def test_int8_bert_close_to_float():
     q = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
     cos = (ref * q).sum(1)
     assert np.all(cos > 0.999), cos
+
+
+# ── int8 format with bf16 storage between operators ─────────────────────────
+
+def test_bf16_round_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(31)
+    x = (rng.standard_normal(200000) * np.exp(rng.uniform(-20, 20, 200000))).astype(np.float32)
+    # ties: values exactly halfway between two bf16 neighbours, both parities
+    x[:4] = np.array([1.0 + 2.0**-8, 1.0 + 3 * 2.0**-8, -(1.0 + 2.0**-8), 0.0], dtype=np.float32)
+    ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    got = oq.bf16_round(x.astype(np.float64))
+    assert got.dtype == np.float32 and np.array_equal(got, ref)
+    assert got[0] == 1.0 and got[1] == 1.0 + 2.0**-6 and got[2] == -1.0
+    assert np.array_equal(oq.bf16_round_f32(x), ref)
+
+
+def test_gemm_s8_exact_at_the_extremes():
+    """Float32 BLAS over 1024-wide K chunks is exact even at |acc| = 4096 * 128^2."""
+    rng = np.random.default_rng(32)
+    a = rng.integers(-128, 128, size=(9, 4096), dtype=np.int64).astype(np.int8)
+    b = rng.integers(-128, 128, size=(7, 4096), dtype=np.int64).astype(np.int8)
+    a[0, :] = -128; b[0, :] = -128; a[1, :] = 127; b[1, :] = -128
+    acc = oq.gemm_s8_exact(a, b)
+    assert acc[0, 0] == 4096 * 128 * 128 and acc[1, 1] == -4096 * 127 * 128
+    assert np.array_equal(acc, a.astype(np.int64) @ b.astype(np.int64).T)
+    assert np.array_equal(oq.gemm_s8_exact(a[:, :1024], b[:, :1024]),
+                          a[:, :1024].astype(np.int64) @ b[:, :1024].astype(np.int64).T)
+
+
+def test_dequant_f32_is_one_fma_then_the_residual():
+    acc = np.array([[16777217, -3]], dtype=np.int64)          # 2^24 + 1 rounds to 2^24 in f32
+    s_tok = np.array([0.5], np.float32)
+    s_ch = np.array([2.0, np.float32(1.0 / 3.0)], np.float32)
+    bias = np.array([4.0, 0.25], np.float32)
+    y = oq.dequant_f32(acc, s_tok, s_ch, bias, resid=np.array([[2.0, 1.0]], np.float32))
+    assert y[0, 0] == 16777216.0 + 4.0 + 2.0                 # not 2^24 + 1 + 4 + 2
+    s1 = np.float32(np.float32(0.5) * np.float32(1.0 / 3.0))
+    want = np.float32(np.float32(-3.0 * np.float64(s1) + 0.25) + np.float32(1.0))
+    assert y[0, 1] == want
+    # a zero bias takes the float32 product, which is the same single rounding
+    y0 = oq.dequant_f32(acc, s_tok, s_ch, np.zeros(2, np.float32))
+    assert y0[0, 1] == np.float32(-3.0 * np.float64(s1))
+
+
+def test_int8_bf16_oracle_agrees_with_float64_int8_oracle():
+    """The two int8 restatements differ only by the bf16 storage of the
+    activations: a few int8 codes at rounding boundaries."""
+    cfg = ob.BertConfig(64, 2, 4, 256, 512, 64)
+    w = ob.random_bert_weights(cfg, 11)
+    lens = np.array([32, 20, 7, 1, 0])
+    ids, mask = ob.random_token_batch(5, 32, lens, seed=5, id_lo=1, id_hi=511, cls_id=1, sep_id=2)
+    f64 = ob.pool_and_normalize(oq.bert_int8_forward_hidden(w, cfg, ids, mask), mask)
+    b16 = oq.bert_int8_bf16_embed(w, cfg, ids, lens)
+    cos = (f64[:4] * b16[:4]).sum(1)
+    assert np.all(cos > 0.999), cos
+    assert np.all(b16[4] == 0)                                # empty row -> zero vector
+    h, cu = oq.bert_int8_bf16_forward(w, cfg, ids, lens)
+    assert h.shape == (int(lens.sum()), 64) and list(cu) == [0, 32, 52, 59, 60, 60]
+    assert h.dtype == np.float32 and np.array_equal(oq.bf16_round_f32(h), h)   # all bf16 values
 
 
 def test_projection_head_oracle():

@@ -13,10 +13,11 @@ import pytest
 
 tokenizers = pytest.importorskip("tokenizers")
 
+from conftest import reference_path  # noqa: E402
 from test_tokenizer import CASES, random_texts  # noqa: E402
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_tiny_bert_tokens.json")
-REF_TOKENIZER = "/root/reference/cookbook/fixtures/tiny_bert/tokenizer.json"
+REF_TOKENIZER = reference_path("cookbook", "fixtures", "tiny_bert", "tokenizer.json")
 
 EXTRA = CASES + [
     "Mc: कः  Me: a⃝  Mn: é", "  padded both ends  ", "x__y _z_ a-b-c", "...!!!???", "a1b22c333 4444",
@@ -105,7 +106,7 @@ def test_reference_fixture_tokenizer_golden_ids():
     Whitespace, WordPiece, [CLS]/[SEP]): ids committed from HF `tokenizers`
     by tests/golden/make_token_golden.py; the file is re-read from the
     reference checkout when present."""
-    if not os.path.exists(REF_TOKENIZER):
+    if not REF_TOKENIZER or not os.path.exists(REF_TOKENIZER):
         pytest.skip("reference checkout not present")
     from jammi_b200 import Tokenizer
     g = json.load(open(GOLDEN, encoding="utf-8"))
@@ -131,7 +132,7 @@ def test_unsupported_components_still_fail_loudly(tmp_path):
             Tokenizer(str(path))
 
 
-REF_CLIP_TOKENIZER = "/root/reference/tests/fixtures/tiny_open_clip/tokenizer.json"
+REF_CLIP_TOKENIZER = reference_path("tests", "fixtures", "tiny_open_clip", "tokenizer.json")
 CLIP_PATTERN = r"'s|'t|'re|'ve|'m|'ll|'d|[\p{L}]+|[\p{N}]|[^\s\p{L}\p{N}]+"
 
 
@@ -139,7 +140,7 @@ def test_reference_open_clip_fixture_tokenizer_golden_ids():
     """The reference's tiny OpenCLIP fixture tokenizer (WordLevel with '<pad>'
     as the unknown token, Split on the empty string inverted -- one word per
     character -- and '$A <|endoftext|>'): ids committed from HF `tokenizers`."""
-    if not os.path.exists(REF_CLIP_TOKENIZER):
+    if not REF_CLIP_TOKENIZER or not os.path.exists(REF_CLIP_TOKENIZER):
         pytest.skip("reference checkout not present")
     from jammi_b200 import Tokenizer
     g = json.load(open(GOLDEN, encoding="utf-8"))
