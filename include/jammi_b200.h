@@ -472,6 +472,15 @@ typedef struct {
 typedef struct {
   int64_t rows, valid_rows, batches, tokens, oom_retries;
   double seconds;
+  /* where the time went (new; the reference records per-batch wall time
+   * only, crates/jammi-ai/src/inference/runner.rs:195-198): */
+  int64_t h2d_bytes, d2h_bytes;  /* host->device ids + lengths, device->host embeddings */
+  double prepare_seconds;        /* validation, length bucketing, null rows (one thread) */
+  double pack_seconds;           /* packing ids into pinned staging, summed over workers */
+  double scatter_seconds;        /* pinned staging -> out in row order, summed over workers */
+  double wait_seconds;           /* workers blocked on their device, summed */
+  double worker_seconds_max;     /* the slowest worker's wall time */
+  double worker_seconds_min;     /* the fastest worker's (max - min: the tail) */
 } jb_generate_stats;
 jb_status jb_generate_embeddings(jb_model** models, int n_models, const uint32_t* ids,
                                  const uint64_t* offsets, int64_t rows,

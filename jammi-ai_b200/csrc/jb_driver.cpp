@@ -213,7 +213,22 @@ struct Shared {
   std::atomic<bool> abort{false};
   std::atomic<int64_t> oom_retries{0};
   std::atomic<int64_t> tokens{0};
+  std::atomic<int64_t> h2d_bytes{0};
+  std::atomic<int64_t> d2h_bytes{0};
   std::mutex mu;
+  // per-phase seconds summed over the workers, and each worker's wall time
+  double pack_s = 0, scatter_s = 0, wait_s = 0;
+  double worker_max = 0, worker_min = 0;
+  int workers_done = 0;
+  void add_times(double pack, double scat, double wait, double wall) {
+    std::lock_guard<std::mutex> lk(mu);
+    pack_s += pack;
+    scatter_s += scat;
+    wait_s += wait;
+    worker_max = workers_done ? std::max(worker_max, wall) : wall;
+    worker_min = workers_done ? std::min(worker_min, wall) : wall;
+    ++workers_done;
+  }
   jb_status first_status = JB_OK;
   std::string first_msg;
   void fail(jb_status st, const std::string& m) {
@@ -236,7 +251,18 @@ void scatter(Shared& sh, Slot& s) {
   s.rows.clear();
 }
 
+using Clock = std::chrono::steady_clock;
+double since(Clock::time_point t) { return std::chrono::duration<double>(Clock::now() - t).count(); }
+
 void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int max_seq) {
+  const auto t_start = Clock::now();
+  double pack_s = 0, scatter_s = 0, wait_s = 0;
+  struct Report {  // the worker's times reach the stats on every exit path
+    Shared& sh;
+    const Clock::time_point& t0;
+    double &pack, &scat, &wait;
+    ~Report() { sh.add_times(pack, scat, wait, since(t0)); }
+  } report{sh, t_start, pack_s, scatter_s, wait_s};
   try {
     jb::DeviceGuard g(m->device);
     cudaStream_t stream;
@@ -301,8 +327,13 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
         while (i < end && !sh.abort) {
           const int64_t len = std::min<int64_t>(bs, end - i);
           Slot& s = slots[k & 1];
+          auto t = Clock::now();
           jb::check_cuda(cudaEventSynchronize(s.done), "slot wait");
+          wait_s += since(t);
+          t = Clock::now();
           scatter(sh, s);
+          scatter_s += since(t);
+          t = Clock::now();
           // pad width: the longest row of the sub-batch (rows are sorted longest first)
           int S = static_cast<int>(row_len(sh, order[i]));
           for (int64_t j = i; j < i + len; ++j) S = std::max<int>(S, static_cast<int>(row_len(sh, order[j])));
@@ -317,6 +348,7 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
             s.h_lens[j] = static_cast<uint32_t>(n);
             toks += n;
           }
+          pack_s += since(t);
           jb::check_cuda(cudaMemcpyAsync(s.d_ids, s.h_ids, size_t(len) * S * 4, cudaMemcpyHostToDevice, stream), "H2D");
           jb::check_cuda(cudaMemcpyAsync(s.d_lens, s.h_lens, size_t(len) * 4, cudaMemcpyHostToDevice, stream), "H2D");
           const jb_status st = jb_encode_text_device(m, s.d_ids, s.d_lens, static_cast<int>(len), S,
@@ -334,13 +366,19 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
           jb::check_cuda(cudaEventRecord(s.done, stream), "event");
           s.rows.assign(order.begin() + i, order.begin() + i + len);
           sh.tokens += toks;
+          sh.h2d_bytes += static_cast<int64_t>(len) * (S + 1) * 4;
+          sh.d2h_bytes += static_cast<int64_t>(len) * sh.H * 4;
           i += len;
           ++k;
         }
       }
       for (Slot& s : slots) {
+        auto t = Clock::now();
         jb::check_cuda(cudaEventSynchronize(s.done), "drain");
+        wait_s += since(t);
+        t = Clock::now();
         scatter(sh, s);
+        scatter_s += since(t);
       }
       jb::check_device_flag(m, stream);
     } catch (...) {
@@ -381,27 +419,45 @@ extern "C" jb_status jb_generate_embeddings(jb_model** models, int n_models, con
       max_seq = std::min(max_seq, models[i]->max_pos);
     }
     const auto t0 = std::chrono::steady_clock::now();
-    std::vector<int64_t> order;
-    order.reserve(static_cast<size_t>(rows));
-    int64_t longest = 0;
+    int64_t longest = 0, valid = 0;
     for (int64_t r = 0; r < rows; ++r) {
       if (offsets[r + 1] < offsets[r]) return err(JB_ERR_INVALID, "offsets must be non-decreasing");
       const int64_t n = static_cast<int64_t>(offsets[r + 1] - offsets[r]);
       longest = std::max(longest, n);
-      if (n > 0) order.push_back(r);  // empty rows: zero vector + null (candle.rs:785-797)
+      valid += n > 0;
     }
     if (longest > max_seq)
       return err(JB_ERR_SEQ_TOO_LONG, "a row of " + std::to_string(longest) +
                                           " tokens exceeds max_position_embeddings " +
                                           std::to_string(max_seq));
-    if (opts->sort_by_length)
-      std::stable_sort(order.begin(), order.end(), [&](int64_t a, int64_t b) {
-        return offsets[a + 1] - offsets[a] > offsets[b + 1] - offsets[b];
-      });
+    // Valid rows, longest first when bucketing: a counting sort over the
+    // lengths (<= max_seq), stable, so equal lengths keep row order.  Empty
+    // rows are left out: they are the zero vector + null (candle.rs:785-797),
+    // and only their output rows are cleared here -- every other row is
+    // written by the workers.
+    std::vector<int64_t> order(static_cast<size_t>(valid));
+    if (opts->sort_by_length) {
+      std::vector<int64_t> start(static_cast<size_t>(longest) + 2, 0);
+      for (int64_t r = 0; r < rows; ++r) {
+        const int64_t n = static_cast<int64_t>(offsets[r + 1] - offsets[r]);
+        if (n > 0) ++start[static_cast<size_t>(longest - n + 1)];
+      }
+      for (size_t i = 1; i < start.size(); ++i) start[i] += start[i - 1];
+      for (int64_t r = 0; r < rows; ++r) {
+        const int64_t n = static_cast<int64_t>(offsets[r + 1] - offsets[r]);
+        if (n > 0) order[static_cast<size_t>(start[static_cast<size_t>(longest - n)]++)] = r;
+      }
+    } else {
+      size_t i = 0;
+      for (int64_t r = 0; r < rows; ++r)
+        if (offsets[r + 1] > offsets[r]) order[i++] = r;
+    }
+    for (int64_t r = 0; r < rows; ++r)
+      if (offsets[r + 1] == offsets[r]) std::memset(out + r * H, 0, sizeof(float) * H);
     std::vector<int64_t> boff;
     for (int64_t i = 0; i < static_cast<int64_t>(order.size()); i += opts->batch_rows) boff.push_back(i);
     boff.push_back(static_cast<int64_t>(order.size()));
-    std::memset(out, 0, sizeof(float) * static_cast<size_t>(rows) * H);
+    const double prepare_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     Shared sh;
     sh.ids = ids;
     sh.offsets = offsets;
@@ -435,6 +491,14 @@ extern "C" jb_status jb_generate_embeddings(jb_model** models, int n_models, con
       stats->tokens = sh.tokens;
       stats->oom_retries = sh.oom_retries;
       stats->seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      stats->h2d_bytes = sh.h2d_bytes;
+      stats->d2h_bytes = sh.d2h_bytes;
+      stats->prepare_seconds = prepare_s;
+      stats->pack_seconds = sh.pack_s;
+      stats->scatter_seconds = sh.scatter_s;
+      stats->wait_seconds = sh.wait_s;
+      stats->worker_seconds_max = sh.worker_max;
+      stats->worker_seconds_min = sh.worker_min;
     }
     return err(JB_OK, "");
   } catch (const jb::Error& e) {

@@ -32,7 +32,11 @@ class GenerateOpts(ctypes.Structure):
 
 class GenerateStats(ctypes.Structure):
     _fields_ = [("rows", ctypes.c_int64), ("valid_rows", ctypes.c_int64), ("batches", ctypes.c_int64),
-                ("tokens", ctypes.c_int64), ("oom_retries", ctypes.c_int64), ("seconds", ctypes.c_double)]
+                ("tokens", ctypes.c_int64), ("oom_retries", ctypes.c_int64), ("seconds", ctypes.c_double),
+                ("h2d_bytes", ctypes.c_int64), ("d2h_bytes", ctypes.c_int64),
+                ("prepare_seconds", ctypes.c_double), ("pack_seconds", ctypes.c_double),
+                ("scatter_seconds", ctypes.c_double), ("wait_seconds", ctypes.c_double),
+                ("worker_seconds_max", ctypes.c_double), ("worker_seconds_min", ctypes.c_double)]
 
 
 FORWARD_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
@@ -121,15 +125,23 @@ def pack_rows(rows) -> tuple[np.ndarray, np.ndarray]:
 
 def generate_embeddings(models, values, offsets, batch_rows: int = 256, pooling: str = "mean",
                         sort_by_length: bool = True, pad_multiple: int = 8,
-                        memory_fraction: float = 0.0):
+                        memory_fraction: float = 0.0, out=None, validity=None):
     """Embeddings for every row, in row order.  ``models``: one Bert per device.
-    Returns (out f32 [rows, H], validity bitmap u8 [(rows+7)//8], stats dict)."""
+    Returns (out f32 [rows, H], validity bitmap u8 [(rows+7)//8], stats dict).
+    ``out`` / ``validity`` may be caller-owned buffers of those shapes (reused
+    across calls, their pages already mapped)."""
     values = np.ascontiguousarray(values, dtype=np.uint32)
     offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
     rows = offsets.size - 1
     H = models[0].info.output_dim
-    out = np.empty((rows, H), dtype=np.float32)
-    validity = np.zeros((rows + 7) // 8, dtype=np.uint8)
+    if out is None:
+        out = np.empty((rows, H), dtype=np.float32)
+    elif out.dtype != np.float32 or out.shape != (rows, H) or not out.flags.c_contiguous:
+        raise ValueError("out must be a C-contiguous float32 [rows, hidden] array")
+    if validity is None:
+        validity = np.zeros((rows + 7) // 8, dtype=np.uint8)
+    elif validity.dtype != np.uint8 or validity.size != (rows + 7) // 8 or not validity.flags.c_contiguous:
+        raise ValueError("validity must be a C-contiguous uint8 [(rows + 7) // 8] array")
     handles = (ctypes.c_void_p * len(models))(*[m.handle.value for m in models])
     opts = GenerateOpts(int(batch_rows), POOLING[pooling], 1 if sort_by_length else 0,
                         int(pad_multiple), float(memory_fraction))

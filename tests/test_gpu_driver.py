@@ -57,6 +57,54 @@ def test_generate_embeddings_row_order_and_nulls(setup, fmt):
         m.close()
 
 
+def test_generate_embeddings_stats_and_caller_buffers(setup):
+    """The stats account for the bytes moved and the time spent, and the
+    caller's own output buffers are written in place (dirty on entry: the
+    driver must clear the null rows itself)."""
+    from jammi_b200 import Bert
+    from jammi_b200.driver import generate_embeddings, pack_rows
+    cfg, w, lens, rows = setup
+    model = Bert.from_weights(w, cfg, device=0, fmt="int8")
+    values, offsets = pack_rows(rows)
+    ref, ref_valid, _ = generate_embeddings([model], values, offsets, batch_rows=64)
+    out = np.full((len(rows), 768), np.nan, dtype=np.float32)
+    validity = np.full((len(rows) + 7) // 8, 0xFF, dtype=np.uint8)
+    got, got_valid, st = generate_embeddings([model], values, offsets, batch_rows=64,
+                                             pad_multiple=32, out=out, validity=validity)
+    assert got is out and got_valid is validity
+    assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)
+    assert st["d2h_bytes"] == st["valid_rows"] * 768 * 4
+    # ids are copied padded to each batch's width (a multiple of 32), plus lengths
+    assert 4 * (st["tokens"] + st["valid_rows"]) <= st["h2d_bytes"]
+    assert st["h2d_bytes"] <= 4 * st["valid_rows"] * (512 + 1)
+    assert 0 < st["worker_seconds_min"] <= st["worker_seconds_max"] <= st["seconds"]
+    assert st["prepare_seconds"] >= 0 and st["pack_seconds"] > 0 and st["scatter_seconds"] > 0
+    model.close()
+
+
+def test_generate_embeddings_two_devices(setup):
+    """One handle on each of two devices: both take batches (the slower
+    worker's wall time bounds the job), and every row equals the one-device
+    job's bit for bit."""
+    from jammi_b200 import Bert
+    from jammi_b200.driver import generate_embeddings, pack_rows
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two devices")
+    cfg, w, lens, rows = setup
+    rows = rows * 8  # 5,600 rows: enough batches for both workers
+    values, offsets = pack_rows(rows)
+    one = Bert.from_weights(w, cfg, device=0, fmt="int8")
+    ref, ref_valid, st1 = generate_embeddings([one], values, offsets, batch_rows=64)
+    two = [one, Bert.from_weights(w, cfg, device=1, fmt="int8")]
+    out, validity, st2 = generate_embeddings(two, values, offsets, batch_rows=64)
+    assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)
+    assert st2["batches"] == st1["batches"] and st2["tokens"] == st1["tokens"]
+    print(f"1 device {st1['seconds']:.3f} s, 2 devices {st2['seconds']:.3f} s "
+          f"(workers {st2['worker_seconds_min']:.3f}-{st2['worker_seconds_max']:.3f} s)")
+    for m in two:
+        m.close()
+
+
 def test_generate_embeddings_rejects_long_rows(setup):
     from jammi_b200 import Bert, JbError
     from jammi_b200.driver import generate_embeddings, pack_rows
