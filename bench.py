@@ -112,7 +112,7 @@ def cpu_model() -> str:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons of the benchmark's GPUs, every 50 ms."""
+    """nvidia-smi clocks / throttle reasons of the benchmark's GPUs, every 100 ms."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -129,7 +129,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -452,6 +452,9 @@ def run_text(args, wl, n, torch):
     clocks.mark()
     ms, ms_dev = device_timed(torch, n, args.steps, args.warmup, step, streams)
     clocks.mark()
+    # the sampler stops before the driver leg: nvidia-smi's queries take the
+    # driver's locks, which stall a host loop that synchronises every batch
+    clk = clocks.stop() if not args.quick else None
     for d in range(n):
         models[d].sync(streams[d])
     value = n * args.steps * B / (ms / 1000.0)
@@ -493,7 +496,6 @@ def run_text(args, wl, n, torch):
                "driver": {k: st[k] for k in ("seconds", "prepare_seconds", "pack_seconds",
                                              "scatter_seconds", "wait_seconds", "worker_seconds_max",
                                              "worker_seconds_min", "batches", "tokens")}}
-    clk = clocks.stop() if not args.quick else None
 
     peaks, src = load_peaks()
     lin_ms, att_ms, mem_ms = (prof[k]["ms"] for k in ("linear", "attention", "memory"))
@@ -579,6 +581,7 @@ def run_image(args, wl, n, torch):
     clocks.mark()
     ms, ms_dev = device_timed(torch, n, args.steps, args.warmup, step, streams)
     clocks.mark()
+    clk = clocks.stop() if not args.quick else None
     value = n * args.steps * B / (ms / 1000.0)
     prof_steps = min(args.steps, 10)
     models[0].profile_enable(True)
@@ -604,7 +607,6 @@ def run_image(args, wl, n, torch):
                "h2d_bytes_per_step": B * 3 * 224 * 224 * 4, "d2h_bytes_per_step": B * E * 4,
                "path": "jb_encode_image: pinned host f32 pixels in, host f32 embeddings out, "
                        f"one host thread per device, {steps_e2e} steps"}
-    clk = clocks.stop() if not args.quick else None
     peaks, src = load_peaks()
     lin, att, extra = vit_flops(cfg)
     lin_ms, att_ms = prof["linear"]["ms"], prof["attention"]["ms"]

@@ -255,13 +255,14 @@ jb_status jb_op_attention_rows(const void* qkv, const int* cu_seqlens, void* ctx
                                int batch, int heads, int head_dim, int max_len, int rows,
                                int causal, void* stream);
 /* Process-wide choice for bf16 head_dim-64 attention with TMA (model forwards
- * and jb_op_attention_rows): on != 0 runs rows of at most 256 keys on the
- * tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma with S and P in TMEM,
- * a persistent TMA / MMA / softmax warp-specialised CTA per SM pulling rows
- * from a device counter), longer rows on the mma.sync kernel; 0 (the
- * default, faster on BERT-base rows of 32-256 tokens) runs every row on the
- * mma.sync kernel.  Single-op calls with it on share a small pool of
- * counters: more than 64 of them in flight at once on one device race. */
+ * and jb_op_attention_rows): on != 0 (the default) runs every row on the
+ * tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma with S, P and O in
+ * TMEM; keys streamed in blocks of 128 with an online softmax; a persistent
+ * TMA / MMA / softmax warp-specialised CTA per SM pulling (row, head,
+ * 128-query) items from a device counter); 0 runs every row on the mma.sync
+ * kernel.  Single-op calls share a small pool of counters: more than 64 of
+ * them in flight at once on one device race.  New (the reference runs
+ * candle's batched matmuls and softmax, crates/jammi-encoders/src/bert.rs:143-152). */
 void jb_set_attention_tcgen05(int on);
 /* Synchronises `stream` and reads (then clears) the current device's error
  * flag shared by the single-op entry points: JB_ERR_TIMEOUT if a bounded

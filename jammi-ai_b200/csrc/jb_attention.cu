@@ -316,219 +316,291 @@ __global__ void __launch_bounds__(kFaThreads, 4)
   }
 }
 
-// ── tcgen05 attention for rows of at most 256 keys ──────────────────────────
+// ── tcgen05 attention, any row length ──────────────────────────────────────
 // A persistent, warp-specialised kernel: one CTA per SM pulls work items
-// (row, head, 128-query block) of rows with at most MAXK keys from a device
-// counter (dynamic schedule: no SM idles while another still has a queue).
-// A row's keys all fit one accumulator, so its softmax is exact in one pass
-// (no running rescale).
-//   warp 0  (TMA): takes the next item from the counter, publishes it to the
-//           other roles in a shared-memory ring beside its stage (an empty
-//           entry, twice, ends the walk), and loads Q and K onto one
-//           mbarrier, V onto a second, 64-row boxes, into STAGES stages.
-//   warp 1  (MMA): S = Q K^T, four kind::f16 MMAs (K = 16) into the item's
-//           TMEM slot, columns [0, n_pad), n_pad = the row length rounded up
-//           to 16; once the softmax has written P: O = P V, one MMA per
-//           16-key chunk with A = P read from TMEM and B = V straight from its
-//           TMA tile (MN-major, 128-byte swizzle), into the slot's columns
-//           [128, 192).  Each is issued as soon as its inputs are ready
-//           (non-blocking probes of the barriers).
-//   warps 2-5 and 6-9 (softmax, two groups ping-ponging on alternate items,
-//           each with its own 256-column TMEM slot): warp w reads TMEM lanes
-//           32 (w % 4) .. + 31, one thread per query row.  The group zeroes
-//           the V rows past the row's end (other rows' values: 0 * V must
-//           stay 0), reads S in register batches (max; then
-//           2^(s log2(e) / 8 - m) and the sum), writes chunk c's P as bf16
-//           pairs into columns [8c, 8c + 8) (S columns already consumed: the
-//           chunks are read in ascending batches before their P is written;
-//           P ends below column 128, where O starts) and, after
-//           O = P V, scales the O row by 1 / sum and stores it (128 B).  While
-//           one group waits for its O, the other runs its softmax.
-// causal != 0 masks keys after the query.  MAXK = 192 keeps three 64 KB
-// stages, MAXK = 256 two 80 KB ones.  Longer rows are left to the mma.sync
-// kernel; the choice is per row, so a row's result does not depend on its
-// batch.  Every wait is bounded; on a timeout each role stops, the
-// TMA and MMA threads wait (bounded) for their copies and MMAs in flight,
-// the error flag is set and TMEM is freed.
-constexpr int kTcQ = 128;         // queries per item
-constexpr int kTcSlotCols = 256;  // TMEM columns per slot; two slots
-constexpr int kTcOCol = 128;      // O's first column inside a slot
-constexpr int kTcGroupWarps = 4;
-constexpr int kTcThreads = 64 + 2 * 32 * kTcGroupWarps;
-constexpr int kTcBatch = 6;  // 16-column chunks per register batch
-template <int MAXK>
-constexpr int tc_stage_bytes() { return (kTcQ + 2 * MAXK) * 128; }
-template <int MAXK, int STAGES>
-constexpr int tc_smem() { return STAGES * tc_stage_bytes<MAXK>() + 1024 + 256 + STAGES * 32; }
+// (row, head, 128-query block) from a device counter and streams the row's
+// keys through it in blocks of 128 with an online softmax.
+//   warp 0  (TMA): takes the next item, publishes it in a 4-entry ring in
+//           shared memory (an end entry per slot finishes the walk), loads
+//           the item's Q (64-row boxes) into its slot's Q buffer, then each
+//           key block's K and V into a 4-stage ring.
+//   warp 1  (MMA): per slot, S = Q K_j^T (kind::f16, M = 128, N = the block's
+//           keys rounded up to 16, four K = 16 steps) into the slot's TMEM
+//           columns [0, 128); once the softmax has written P_j (bf16 pairs,
+//           columns [192, 256)), O (+)= P_j V_j with A = P from TMEM and B =
+//           V_j MN-major straight from its TMA tile, into columns [128, 192),
+//           and S_{j+1} right behind it.  Every step is issued as soon as its
+//           inputs are ready (non-blocking probes of the barriers).
+//   warps 2-9 and 10-17 (softmax, one group per slot; items alternate
+//           slots): warp w reads TMEM lanes 32 (w % 4) .. + 31, and the two
+//           warps of a group on the same lane quarter split each row's key
+//           chunks (even / odd 16-key chunks), so two threads serve a query
+//           row and exchange their partial maxima and sums through shared
+//           memory under a 64-thread named barrier.  Per key block a thread
+//           reads its chunks of S twice, two 16-key chunks at a time (once
+//           for the maximum, once for the exponentials), masks keys past the
+//           row's end (and
+//           past the query when causal) in the block that has them, takes the
+//           block maximum, and computes p = 2^(s log2(e) / 8 - m) against a
+//           reference maximum m: the first block's maximum, raised only when
+//           a later block exceeds it by more than 8 (2^8: p stays far inside
+//           bf16 and f32), the row of O in TMEM and the running sum rescaled
+//           then (lazy rescaling).  P goes to TMEM as bf16 pairs.  After the
+//           last block, O / sum is stored.
+//           The group also zeroes V rows past the row's end in the block's
+//           tile (other rows' values: 0 * V must stay 0).
+// Every wait is bounded; on a timeout each role stops, the TMA and MMA
+// threads wait (bounded) for their copies and MMAs in flight, the error flag
+// is set and TMEM is freed.
+constexpr int kAtQ = 128;            // queries per item
+constexpr int kAtKB = 128;           // keys per block
+constexpr int kAtStages = 4;         // K / V ring
+constexpr int kAtSlotCols = 256;     // TMEM columns per slot; two slots
+constexpr int kAtOCol = 128;         // O's first column inside a slot (S at [0, 128))
+constexpr int kAtPCol = 192;         // P's first column inside a slot (bf16 pairs)
+constexpr int kAtGroupWarps = 8;     // two warps per TMEM lane quarter: two threads per row
+constexpr int kAtThreads = 64 + 2 * 32 * kAtGroupWarps;
+constexpr int kAtQBytes = kAtQ * 128;                  // 16 KB
+constexpr int kAtKBytes = kAtKB * 128;                 // 16 KB (K or V of a block)
+constexpr int kAtMetaBytes = 512 + 2 * 2 * 4 * 2 * 32 * 4 + 2 * 4 * 2 * 32 * 4;  // barriers, ring, exchange
+constexpr int kAtSmem = 1024 + 2 * kAtQBytes + kAtStages * 2 * kAtKBytes + kAtMetaBytes;
+constexpr float kAtRescale = 8.f;    // lazy-rescaling threshold, log2 units
 
-// One published work item (or idx < 0: no more).
-struct TcItem {
-  int idx, start, n, h, q0;
+// One published work item (idx < 0: no more for this slot).  b0 = index of
+// its first key block in the K / V stream, nb = its key blocks.
+struct AtItem {
+  int idx, start, n, h, q0, b0, nb;
 };
 
-template <int MAXK, int STAGES>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// A bounded barrier wait whose outcome is the same for every lane of the
+// warp (false if any lane gave up), so that no warp-collective tcgen05
+// instruction after it is reached by only part of the warp.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x16_at(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__global__ void __launch_bounds__(kAtThreads, 1)
     attn_tc_kernel(const int* __restrict__ cu, bf16* __restrict__ ctx, int batch, int heads,
-                   float scale_log2, const __grid_constant__ CUtensorMap tm, int* err, int causal,
-                   unsigned int* work) {
-  constexpr int kTcStages = STAGES, kTcMaxKeys = MAXK;
-  constexpr int kTcStageBytes = tc_stage_bytes<MAXK>();
+                   int qblocks, float scale_log2, const __grid_constant__ CUtensorMap tm, int* err,
+                   int causal, unsigned int* work) {
   const int H = heads * 64;
-  const int items = batch * heads * 2;
+  const int items = batch * heads * qblocks;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t stage0 = (raw + 1023u) & ~1023u;
-  uint8_t* meta = smem_raw + (stage0 + kTcStages * kTcStageBytes - raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t sQ0 = base;                                   // [2][16 KB]
+  const uint32_t sKV0 = base + 2 * kAtQBytes;                  // [4][K 16 KB | V 16 KB]
+  uint8_t* meta = smem_raw + (sKV0 + kAtStages * 2 * kAtKBytes - raw);
   const uint32_t bars = smem_u32(meta);
-  // stage barriers (3 each): ld_qk, ld_v, smem_empty; slot barriers (2 each):
-  // s_full, p_full, o_full, tmem_free; one spare
-  auto sbar = [&](int kind, int st) { return bars + 8u * (kind * kTcStages + st); };
-  auto tbar = [&](int kind, int sl) { return bars + 8u * (3 * kTcStages + kind * 2 + sl); };
-  enum { kLdQK = 0, kLdV = 1, kSEmpty = 2 };
-  enum { kSFull = 0, kPFull = 1, kOFull = 2, kTFree = 3 };
-  const uint32_t spare = bars + 8u * (3 * kTcStages + 8);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(meta + 8 * 24);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 24 + 4);
-  volatile TcItem* ring = reinterpret_cast<volatile TcItem*>(meta + 256);  // [STAGES]
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] t_free[2]
+  // k_full[4] v_full[4] kv_empty[4] spare
+  auto qfull = [&](int s) { return bars + 8u * (0 + s); };
+  auto qempty = [&](int s) { return bars + 8u * (2 + s); };
+  auto sfull = [&](int s) { return bars + 8u * (4 + s); };
+  auto pfull = [&](int s) { return bars + 8u * (6 + s); };
+  auto ofull = [&](int s) { return bars + 8u * (8 + s); };
+  auto tfree = [&](int s) { return bars + 8u * (10 + s); };
+  auto kfull = [&](int st) { return bars + 8u * (12 + st); };
+  auto vfull = [&](int st) { return bars + 8u * (16 + st); };
+  auto kvempty = [&](int st) { return bars + 8u * (20 + st); };
+  const uint32_t spare = bars + 8u * 24;
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(meta + 8 * 25);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 25 + 4);
+  volatile AtItem* ring = reinterpret_cast<volatile AtItem*>(meta + 256);  // [4]
+  // the two threads of a row exchange their partial maxima (per key block,
+  // double-buffered by block parity) and sums (per item) here
+  volatile float* xmax = reinterpret_cast<volatile float*>(meta + 512);       // [2 g][2 par][4 q][2 half][32]
+  volatile float* xsum = xmax + 2 * 2 * 4 * 2 * 32;                            // [2 g][4 q][2 half][32]
+  auto sK = [&](int st) { return sKV0 + static_cast<uint32_t>(st) * 2 * kAtKBytes; };
+  auto sV = [&](int st) { return sKV0 + static_cast<uint32_t>(st) * 2 * kAtKBytes + kAtKBytes; };
 
   if (tid == 0) {
-    for (int st = 0; st < kTcStages; ++st) {
-      mbar_init(sbar(kLdQK, st), 1);
-      mbar_init(sbar(kLdV, st), 1);
-      mbar_init(sbar(kSEmpty, st), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qfull(s), 1);
+      mbar_init(qempty(s), 1 + kAtGroupWarps);  // the last S MMA's commit + the group's warps
+      mbar_init(sfull(s), 1);
+      mbar_init(pfull(s), kAtGroupWarps);
+      mbar_init(ofull(s), 1);
+      mbar_init(tfree(s), kAtGroupWarps);
     }
-    for (int sl = 0; sl < 2; ++sl) {
-      mbar_init(tbar(kSFull, sl), 1);
-      mbar_init(tbar(kPFull, sl), kTcGroupWarps);
-      mbar_init(tbar(kOFull, sl), 1);
-      mbar_init(tbar(kTFree, sl), kTcGroupWarps);
+    for (int st = 0; st < kAtStages; ++st) {
+      mbar_init(kfull(st), 1);
+      mbar_init(vfull(st), 1);
+      mbar_init(kvempty(st), 1);
     }
     mbar_init(spare, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(smem_u32(tslot), 2 * kTcSlotCols);
+  if (warp == 1) tmem_alloc(smem_u32(tslot_ptr), 2 * kAtSlotCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tbase = *tslot;
-  auto stage_of = [&](int k) { return stage0 + static_cast<uint32_t>(k % kTcStages) * kTcStageBytes; };
+  const uint32_t tbase = *tslot_ptr;
 
   if (warp == 0) {
     if (lane == 0) {  // ── TMA producer
-      int k = 0, ends = 0;
-      while (ends < 2) {
-        const int st = k % kTcStages;
-        const uint32_t ph = (k / kTcStages) & 1;
-        if (!mbar_wait(sbar(kSEmpty, st), ph ^ 1u, abort_flag)) break;
-        TcItem it{-1, 0, 0, 0, 0};
+      int k = 0, bc = 0, ends = 0;
+      bool ok = true;
+      while (ends < 2 && ok) {
+        const int sl = k & 1;
+        if (!mbar_wait(qempty(sl), ((k >> 1) & 1) ^ 1u, abort_flag)) break;
+        AtItem it{-1, 0, 0, 0, 0, 0, 0};
         if (ends == 0) {
           while (true) {
             const int idx = static_cast<int>(atomicAdd(work, 1u));
             if (idx >= items) break;
-            const int bh = idx >> 1, b = bh / heads;
-            const int q0 = (idx & 1) * kTcQ, start = cu[b], n = cu[b + 1] - start;
-            if (q0 < n && n <= kTcMaxKeys) {
-              it = TcItem{idx, start, n, bh - b * heads, q0};
+            const int qb = idx % qblocks, bh = idx / qblocks, b = bh / heads;
+            const int q0 = qb * kAtQ, start = cu[b], n = cu[b + 1] - start;
+            if (q0 < n) {
+              const int nk = (n + kAtKB - 1) / kAtKB;
+              it = AtItem{idx, start, n, bh - b * heads, q0, bc, causal ? min(nk, qb + 1) : nk};
               break;
             }
           }
         }
-        ring[st].idx = it.idx;
-        ring[st].start = it.start;
-        ring[st].n = it.n;
-        ring[st].h = it.h;
-        ring[st].q0 = it.q0;
-        if (it.idx < 0) {  // published by the barriers' release
-          mbar_arrive(sbar(kLdQK, st));
-          mbar_arrive(sbar(kLdV, st));
+        volatile AtItem& e = ring[k & 3];
+        e.idx = it.idx;
+        e.start = it.start;
+        e.n = it.n;
+        e.h = it.h;
+        e.q0 = it.q0;
+        e.b0 = it.b0;
+        e.nb = it.nb;
+        if (it.idx < 0) {  // published by the barrier's release
+          mbar_arrive(qfull(sl));
           ++ends;
           ++k;
           continue;
         }
-        const uint32_t sQ = stage_of(k), sK = sQ + kTcQ * 128, sV = sK + kTcMaxKeys * 128;
-        const int n_pad = (it.n + 15) & ~15;
-        const int kboxes = (n_pad + 63) >> 6;
+        const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
         const int qboxes = min(2, (it.n - it.q0 + 63) >> 6);
-        mbar_arrive_expect_tx(sbar(kLdQK, st), static_cast<uint32_t>(qboxes + kboxes) * kTileBytes);
-        for (int i = 0; i < qboxes; ++i) tma_load_2d(sQ + i * kTileBytes, &tm, it.h * 64, it.start + it.q0 + 64 * i, sbar(kLdQK, st));
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sK + i * kTileBytes, &tm, H + it.h * 64, it.start + 64 * i, sbar(kLdQK, st));
-        mbar_arrive_expect_tx(sbar(kLdV, st), static_cast<uint32_t>(kboxes) * kTileBytes);
-        for (int i = 0; i < kboxes; ++i) tma_load_2d(sV + i * kTileBytes, &tm, 2 * H + it.h * 64, it.start + 64 * i, sbar(kLdV, st));
+        mbar_arrive_expect_tx(qfull(sl), static_cast<uint32_t>(qboxes) * kTileBytes);
+        for (int i = 0; i < qboxes; ++i)
+          tma_load_2d(sQ + i * kTileBytes, &tm, it.h * 64, it.start + it.q0 + 64 * i, qfull(sl));
+        for (int j = 0; j < it.nb; ++j, ++bc) {
+          const int st = bc % kAtStages;
+          if (!mbar_wait(kvempty(st), ((bc / kAtStages) & 1) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int kn = min(kAtKB, it.n - kAtKB * j);
+          const int boxes = (((kn + 15) & ~15) + 63) >> 6;
+          const int row = it.start + kAtKB * j;
+          mbar_arrive_expect_tx(kfull(st), static_cast<uint32_t>(boxes) * kTileBytes);
+          for (int i = 0; i < boxes; ++i)
+            tma_load_2d(sK(st) + i * kTileBytes, &tm, H + it.h * 64, row + 64 * i, kfull(st));
+          mbar_arrive_expect_tx(vfull(st), static_cast<uint32_t>(boxes) * kTileBytes);
+          for (int i = 0; i < boxes; ++i)
+            tma_load_2d(sV(st) + i * kTileBytes, &tm, 2 * H + it.h * 64, row + 64 * i, vfull(st));
+        }
         ++k;
       }
       if (*abort_flag) {
         // copies in flight land before the CTA leaves (bounded)
         volatile int no_abort = 0;
-        for (int j = max(0, k - kTcStages); j < k; ++j) {
-          mbar_wait(sbar(kLdQK, j % kTcStages), (j / kTcStages) & 1, &no_abort);
-          mbar_wait(sbar(kLdV, j % kTcStages), (j / kTcStages) & 1, &no_abort);
+        for (int i = max(0, k - 2); i < k; ++i) mbar_wait(qfull(i & 1), (i >> 1) & 1, &no_abort);
+        for (int b = max(0, bc - kAtStages); b < bc; ++b) {
+          mbar_wait(kfull(b % kAtStages), (b / kAtStages) & 1, &no_abort);
+          mbar_wait(vfull(b % kAtStages), (b / kAtStages) & 1, &no_abort);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ── MMA issuer
-      // items k with S issued (< ks) and with O = P V issued (< kp); ns[]
-      // remembers the row lengths of the items in flight; an empty ring entry
-      // (once its Q/K barrier has completed) ends the walk
-      int ks = 0, kp = 0;
-      int ns[4] = {0, 0, 0, 0};
-      bool more = true, ok = true;
-      const uint64_t t_limit = kWaitLimitNs;
+      // per slot: state 0 = wait for the next item, 1 = issue S_j, 2 = issue
+      // P_j V_j, 3 = finished; ti = items done, bs = key blocks done
+      int state[2] = {0, 0}, ti[2] = {0, 0}, bs[2] = {0, 0}, j[2] = {0, 0};
+      int n_[2] = {0, 0}, b0[2] = {0, 0}, nb[2] = {0, 0};
+      bool ok = true;
+      const uint32_t idesc_pv = idesc_bf16_f32(kAtQ, 64) | (1u << 16);  // B (V) MN-major
       uint64_t t0 = global_timer_ns();
-      while (ok) {
+      while (state[0] != 3 || state[1] != 3) {
         bool progress = false;
-        // next item whose S can go: its slot free and its Q, K loaded
-        if (more && ks - kp < 2) {
-          const int sl = ks & 1, st = ks % kTcStages;
-          // one probe of the Q/K barrier, then the ring entry decides: an
-          // empty entry (n = 0) must never reach an MMA (N = 0 is invalid)
-          if (mbar_test_wait(sbar(kLdQK, st), (ks / kTcStages) & 1)) {
-            const int n = ring[st].idx < 0 ? 0 : ring[st].n;
-            if (n <= 0) {
-              more = false;
-            } else if (mbar_test_wait(tbar(kTFree, sl), ((ks >> 1) & 1) ^ 1u)) {
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          const uint32_t slot = tbase + static_cast<uint32_t>(sl * kAtSlotCols);
+          if (state[sl] == 0 && mbar_test_wait(qfull(sl), ti[sl] & 1)) {
+            const int k = 2 * ti[sl] + sl;
+            if (ring[k & 3].idx < 0) {
+              state[sl] = 3;
+              progress = true;
+            } else if (mbar_test_wait(tfree(sl), (ti[sl] & 1) ^ 1u)) {
+              n_[sl] = ring[k & 3].n;
+              b0[sl] = ring[k & 3].b0;
+              nb[sl] = ring[k & 3].nb;
+              j[sl] = 0;
+              state[sl] = 1;
+              progress = true;
+            }
+          }
+          if (state[sl] == 1) {
+            const int b = b0[sl] + j[sl], st = b % kAtStages;
+            // S_j overwrites S_{j-1}, which the softmax read before it
+            // released P_{j-1}; P_{j-1} V (issued before) is untouched
+            if (mbar_test_wait(kfull(st), (b / kAtStages) & 1)) {
               tc_fence_after();
-              const uint32_t sQ = stage_of(ks), sK = sQ + kTcQ * 128;
-              const uint32_t idesc = idesc_bf16_f32(kTcQ, (n + 15) & ~15);
+              const int kn = min(kAtKB, n_[sl] - kAtKB * j[sl]);
+              const uint32_t idesc = idesc_bf16_f32(kAtQ, (kn + 15) & ~15);
+              const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                mma_bf16(tbase + static_cast<uint32_t>(sl * kTcSlotCols), umma_desc_sw128(sQ + 32u * kk),
-                         umma_desc_sw128(sK + 32u * kk), idesc, kk != 0);
-              mma_commit(tbar(kSFull, sl));
-              ns[ks & 3] = n;
-              ++ks;
+                mma_bf16(slot, umma_desc_sw128(sQ + 32u * kk), umma_desc_sw128(sK(st) + 32u * kk), idesc,
+                         kk != 0);
+              mma_commit(sfull(sl));
+              if (j[sl] == nb[sl] - 1) mma_commit(qempty(sl));  // Q read by the item's last S
+              state[sl] = 2;
+              progress = true;
+            }
+          }
+          if (state[sl] == 2) {
+            const int b = b0[sl] + j[sl], st = b % kAtStages;
+            if (mbar_test_wait(pfull(sl), bs[sl] & 1) && mbar_test_wait(vfull(st), (b / kAtStages) & 1)) {
+              tc_fence_after();
+              const int kn = min(kAtKB, n_[sl] - kAtKB * j[sl]);
+              const int chunks = ((kn + 15) & ~15) >> 4;
+#pragma unroll 1
+              for (int c = 0; c < chunks; ++c)
+                mma_bf16_ta(slot + kAtOCol, slot + kAtPCol + 8u * c, umma_desc_sw128(sV(st) + 2048u * c),
+                            idesc_pv, (j[sl] > 0 || c > 0) ? 1u : 0u);
+              mma_commit(ofull(sl));
+              mma_commit(kvempty(st));
+              ++bs[sl];
+              if (++j[sl] == nb[sl]) {
+                ++ti[sl];
+                state[sl] = 0;
+              } else {
+                state[sl] = 1;
+              }
               progress = true;
             }
           }
         }
-        // O = P V of the oldest item whose P is written
-        if (kp < ks && mbar_test_wait(tbar(kPFull, kp & 1), (kp >> 1) & 1)) {
-          tc_fence_after();
-          const int sl = kp & 1;
-          const uint32_t sV = stage_of(kp) + kTcQ * 128 + kTcMaxKeys * 128;
-          const uint32_t slot = tbase + static_cast<uint32_t>(sl * kTcSlotCols);
-          const uint32_t idesc = idesc_bf16_f32(kTcQ, 64) | (1u << 16);  // B (V) MN-major
-          const int chunks = ((ns[kp & 3] + 15) & ~15) >> 4;
-#pragma unroll 1
-          for (int c = 0; c < chunks; ++c)
-            mma_bf16_ta(slot + kTcOCol, slot + 8u * c, umma_desc_sw128(sV + 2048u * c), idesc, c != 0);
-          mma_commit(tbar(kOFull, sl));
-          mma_commit(sbar(kSEmpty, kp % kTcStages));
-          ++kp;
-          progress = true;
-        }
-        if (!more && kp == ks) break;
         if (progress) {
           t0 = global_timer_ns();
-        } else if (*abort_flag || global_timer_ns() - t0 > t_limit) {
+        } else if (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs) {
           *abort_flag = 1;
           ok = false;
+          break;
         }
       }
-      // the last commit's arrival lands before the CTA leaves (bounded)
-      if (ok && kp > 0) ok = mbar_wait(sbar(kSEmpty, (kp - 1) % kTcStages), ((kp - 1) / kTcStages) & 1, abort_flag);
       if (!ok) {
         // every MMA issued completes before TMEM is freed (bounded)
         volatile int no_abort = 0;
@@ -537,105 +609,172 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else {  // ── softmax / epilogue groups
-    const int group = (warp - 2) / kTcGroupWarps;       // items k with k % 2 == group
-    const int quarter = warp & 3;
-    const int gtid = tid - 64 - group * 32 * kTcGroupWarps;  // 0 .. 127
-    const int row = 32 * quarter + lane;
-    for (int kk = group;; kk += 2) {
-      const int st = kk % kTcStages;
-      const uint32_t sph = (kk / kTcStages) & 1, tph = (kk >> 1) & 1;
-      if (!mbar_wait(sbar(kLdV, st), sph, abort_flag)) break;
-      const int idx = ring[st].idx;
+    const int gw = (warp - 2) % kAtGroupWarps;
+    const int g = (warp - 2) / kAtGroupWarps;          // slot: items k with k % 2 == g
+    const int quarter = warp & 3;                       // TMEM lanes 32 quarter .. + 31
+    const int half = gw >> 2;                           // this thread's key chunks: t % 2 == half
+    const int gtid = tid - 64 - g * 32 * kAtGroupWarps;  // 0 .. 255
+    const int r = 32 * quarter + lane;                  // query row of the item
+    const uint32_t pair_bar = 1 + g * 4 + quarter;     // named barrier of the two warps of a row
+    const uint32_t trow = tbase + static_cast<uint32_t>(g * kAtSlotCols) + (static_cast<uint32_t>(32 * quarter) << 16);
+    auto xm = [&](int par, int hf) { return xmax + (((g * 2 + par) * 4 + quarter) * 2 + hf) * 32 + lane; };
+    auto xs = [&](int hf) { return xsum + ((g * 4 + quarter) * 2 + hf) * 32 + lane; };
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
+    int bs = 0;  // key blocks done in this slot
+    bool ok = true;
+    for (int ti = 0; ok; ++ti) {
+      const int k = 2 * ti + g;
+      if (!warp_wait(qfull(g), ti & 1, abort_flag)) break;
+      const int idx = ring[k & 3].idx;
+      const int start = ring[k & 3].start, n = ring[k & 3].n, h = ring[k & 3].h, q0 = ring[k & 3].q0;
+      const int b0 = ring[k & 3].b0, nb = ring[k & 3].nb;
+      __syncwarp();
       if (idx < 0) break;  // the walk is over
-      const int start = ring[st].start, n = ring[st].n, h = ring[st].h, q0 = ring[st].q0;
-      const uint32_t sV = stage_of(kk) + kTcQ * 128 + kTcMaxKeys * 128;
-      const uint32_t trow = tbase + static_cast<uint32_t>(group * kTcSlotCols) +
-                            (static_cast<uint32_t>(32 * quarter) << 16);
-      const int n_pad = (n + 15) & ~15, chunks = n_pad >> 4;
-      // V rows [n, n_pad) -> 0 (whole 128-byte rows, so the swizzle is moot)
-      for (int i = gtid; i < (n_pad - n) * 8; i += 32 * kTcGroupWarps) {
-        const uint32_t a = sV + static_cast<uint32_t>(n + (i >> 3)) * 128 + (i & 7) * 16;
-        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
-      }
-      fence_proxy_async_smem();
-      if (!mbar_wait(tbar(kSFull, group), tph, abort_flag)) break;
-      tc_fence_after();
-      const int qi = q0 + row;
-      const bool active = q0 + 32 * quarter < n;  // warp-uniform
-      const int kmax = causal ? min(n, qi + 1) : n;
-      float l = 0.f;
-      if (active) {
-        float m = -INFINITY;
-        uint32_t r[kTcBatch][16];
-#pragma unroll 1
-        for (int c0 = 0; c0 < chunks; c0 += kTcBatch) {
-#pragma unroll
-          for (int t = 0; t < kTcBatch; ++t)
-            if (c0 + t < chunks) tmem_ld_32x32b_x16(trow + 16 * (c0 + t), r[t]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int t = 0; t < kTcBatch; ++t) {
-            if (c0 + t < chunks) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                if (16 * (c0 + t) + j < kmax) m = fmaxf(m, __uint_as_float(r[t][j]));
-            }
+      if (lane == 0) mbar_arrive(qempty(g));  // this warp has read the ring entry
+      const int qi = q0 + r;
+      const bool wactive = q0 + 32 * quarter < n;  // uniform over the row's two warps
+      const int kmax = qi < n ? (causal ? min(n, qi + 1) : n) : 0;  // keys this row sees
+      float mref = -INFINITY, l = 0.f;
+      for (int jb = 0; jb < nb; ++jb, ++bs) {
+        const int kbase = kAtKB * jb, kn = min(kAtKB, n - kbase), kpad = (kn + 15) & ~15;
+        if (kpad > kn) {  // the row's last block: V rows [kn, kpad) -> 0
+          const int b = b0 + jb, st = b % kAtStages;
+          if (!warp_wait(vfull(st), (b / kAtStages) & 1, abort_flag)) {
+            ok = false;
+            break;
           }
+          for (int i = gtid; i < (kpad - kn) * 8; i += 32 * kAtGroupWarps) {
+            const uint32_t a = sV(st) + static_cast<uint32_t>(kn + (i >> 3)) * 128 + (i & 7) * 16;
+            asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0) : "memory");
+          }
+          fence_proxy_async_smem();
         }
-        const float mb = m * scale_log2;
-#pragma unroll 1
-        for (int c0 = 0; c0 < chunks; c0 += kTcBatch) {
+        if (!warp_wait(sfull(g), bs & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (wactive) {
+          // this thread's chunks: t = half + 2u, u < mine; read in pairs
+          // (32 values live), once for the maximum and once for the
+          // exponentials
+          const int chunks = kpad >> 4, mine = (chunks - half + 1) >> 1;
+          const int lim = kmax - kbase;  // this row's valid columns in the block
+          float m = -INFINITY;
 #pragma unroll
-          for (int t = 0; t < kTcBatch; ++t)
-            if (c0 + t < chunks) tmem_ld_32x32b_x16(trow + 16 * (c0 + t), r[t]);
-          tmem_wait_ld();
+          for (int u0 = 0; u0 < 4; u0 += 2) {
+            if (u0 < mine) {
+              uint32_t v[2][16];
 #pragma unroll
-          for (int t = 0; t < kTcBatch; ++t) {
-            if (c0 + t < chunks) {
-              const int c = 16 * (c0 + t);
-              uint32_t pk[8];
+              for (int uu = 0; uu < 2; ++uu)
+                if (u0 + uu < mine) tmem_ld_32x32b_x16_at(trow + 16 * (2 * (u0 + uu) + half), v[uu]);
+              tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                const float p0 = c + j < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j]), scale_log2, -mb)) : 0.f;
-                const float p1 = c + j + 1 < kmax ? ex2_approx(fmaf(__uint_as_float(r[t][j + 1]), scale_log2, -mb)) : 0.f;
-                l += p0 + p1;
-                pk[j >> 1] = pack_bf16(p0, p1);
+              for (int uu = 0; uu < 2; ++uu) {
+                if (u0 + uu < mine) {
+                  const int c0 = 16 * (2 * (u0 + uu) + half);
+#pragma unroll
+                  for (int e = 0; e < 16; ++e)
+                    if (c0 + e < lim) m = fmaxf(m, __uint_as_float(v[uu][e]));
+                }
               }
-              tmem_st_32x32b_x8(trow + (c >> 1), pk);  // consumed S columns [8c', 8c' + 8)
             }
           }
+          *xm(bs & 1, half) = m;
+          pair_sync();
+          m = fmaxf(m, *xm(bs & 1, half ^ 1));
+          const float mb = m * scale_log2;
+          if (jb == 0) {
+            mref = mb == -INFINITY ? 0.f : mb;  // a row with no key here keeps p = 0
+          } else {
+            // lazy rescaling: a row whose block maximum exceeds its reference
+            // by more than the threshold moves O (complete through block
+            // jb - 1: a commit tracks every earlier MMA, so S_jb's completion
+            // implies P_{jb-1} V's) and the sum to the new reference (which
+            // also makes P_{jb-1} free to overwrite); each thread of the row rescales its half of
+            // O (columns 32 half .. + 31) and its partial sum.  TMEM loads and
+            // stores are warp-collective: the whole warp runs the loop, with
+            // alpha = 1 on other rows (both warps of a row decide alike).
+            const bool up = mb > mref + kAtRescale;
+            if (__any_sync(0xffffffffu, up)) {
+              const float alpha = up ? ex2_approx(mref - mb) : 1.f;
+              l *= alpha;
+#pragma unroll 1
+              for (int c = 0; c < 32; c += 8) {
+                uint32_t w8[8];
+                tmem_ld_32x32b_x8(trow + kAtOCol + 32 * half + c, w8);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 8; ++e) w8[e] = __float_as_uint(__uint_as_float(w8[e]) * alpha);
+                tmem_st_32x32b_x8(trow + kAtOCol + 32 * half + c, w8);
+              }
+              tmem_wait_st();
+              if (up) mref = mb;
+            }
+          }
+          float lsum0 = 0.f, lsum1 = 0.f;
+#pragma unroll
+          for (int u0 = 0; u0 < 4; u0 += 2) {
+            if (u0 < mine) {
+              uint32_t v[2][16];
+#pragma unroll
+              for (int uu = 0; uu < 2; ++uu)
+                if (u0 + uu < mine) tmem_ld_32x32b_x16_at(trow + 16 * (2 * (u0 + uu) + half), v[uu]);
+              tmem_wait_ld();
+#pragma unroll
+              for (int uu = 0; uu < 2; ++uu) {
+                if (u0 + uu < mine) {
+                  const int t = 2 * (u0 + uu) + half, c0 = 16 * t;
+                  uint32_t pk[8];
+#pragma unroll
+                  for (int e = 0; e < 16; e += 2) {
+                    float2 z = __ffma2_rn(make_float2(__uint_as_float(v[uu][e]), __uint_as_float(v[uu][e + 1])),
+                                          f2(scale_log2), f2(-mref));
+                    if (c0 + e >= lim) z.x = -INFINITY;  // keys past the row's end (or the query)
+                    if (c0 + e + 1 >= lim) z.y = -INFINITY;
+                    const float p0 = ex2_approx(z.x), p1 = ex2_approx(z.y);
+                    lsum0 += p0;
+                    lsum1 += p1;
+                    pk[e >> 1] = pack_bf16(p0, p1);
+                  }
+                  tmem_st_32x32b_x8(trow + kAtPCol + 8 * t, pk);
+                }
+              }
+            }
+          }
+          l += lsum0 + lsum1;
+          tmem_wait_st();
         }
-        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pfull(g));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tbar(kPFull, group));
-      if (!mbar_wait(tbar(kOFull, group), tph, abort_flag)) break;
+      if (!ok) break;
+      if (!warp_wait(ofull(g), (bs - 1) & 1, abort_flag)) break;
       tc_fence_after();
-      if (active) {
-        const float inv_l = 1.f / l;
+      if (wactive) {
+        *xs(half) = l;
+        pair_sync();
+        const float inv_l = 1.f / (l + *xs(half ^ 1));
         uint32_t o[32];
+        tmem_ld_32x32b_x32(trow + kAtOCol + 32 * half, o);
+        tmem_wait_ld();
+        if (qi < n) {
+          uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(start + qi) * H + h * 64 + 32 * half);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld_32x32b_x32(trow + kTcOCol + 32 * half, o);
-          tmem_wait_ld();
-          if (qi < n) {
-            uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(start + qi) * H + h * 64 + 32 * half);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 wv;
-              wv.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-              wv.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-              wv.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-              wv.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-              dst[v] = wv;
-            }
+          for (int q = 0; q < 4; ++q) {
+            uint4 wv;
+            wv.x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+            wv.y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+            wv.z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+            wv.w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
+            dst[q] = wv;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tbar(kTFree, group));
+      if (lane == 0) mbar_arrive(tfree(g));
     }
   }
   tc_fence_before();
@@ -643,7 +782,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0 && *abort_flag && err) atomicOr(err, kErrTimeout);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tbase, 2 * kTcSlotCols);
+    tmem_dealloc(tbase, 2 * kAtSlotCols);
   }
 }
 
@@ -746,19 +885,23 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-std::atomic<int> g_attn_tc{0};  // jb_set_attention_tcgen05
+std::atomic<int> g_attn_tc{1};  // jb_set_attention_tcgen05 (on by default)
 bool attn_tc_enabled() { return g_attn_tc.load(std::memory_order_relaxed) != 0; }
 
-template <int MAXK, int STAGES>
 cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int batch, int heads,
-                      float scale_log2, const CUtensorMap& tm, int* err, int causal,
+                      int qblocks, float scale_log2, const CUtensorMap& tm, int* err, int causal,
                       unsigned int* work) {
-  static const bool attr = cudaFuncSetAttribute(attn_tc_kernel<MAXK, STAGES>,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                tc_smem<MAXK, STAGES>()) == cudaSuccess;
-  if (!attr) return cudaErrorInvalidConfiguration;
-  attn_tc_kernel<MAXK, STAGES><<<grid, kTcThreads, tc_smem<MAXK, STAGES>(), s>>>(
-      cu, ctx, batch, heads, scale_log2, tm, err, causal, work);
+  // the shared-memory opt-in is a property of each device's context
+  static std::atomic<uint8_t> attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
+    const cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev].store(1, std::memory_order_release);
+  }
+  attn_tc_kernel<<<grid, kAtThreads, kAtSmem, s>>>(cu, ctx, batch, heads, qblocks, scale_log2, tm, err,
+                                                    causal, work);
   return cudaGetLastError();
 }
 
@@ -803,33 +946,30 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
     CUtensorMap tm;
     memset(&tm, 0, sizeof(tm));
     const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64);
-    int skip_le = 0;  // rows the tcgen05 kernel takes
     if (tma && attn_tc_enabled()) {
-      // rows of up to 256 keys: S and P V on tcgen05 (one softmax pass)
+      // every row on tcgen05: 128-query items, keys streamed in blocks of 128
       unsigned int* w = work ? reinterpret_cast<unsigned int*>(work) : shared_work_counter();
-      cudaError_t e = w ? cudaMemsetAsync(w, 0, sizeof(unsigned int), s) : cudaErrorInvalidValue;
-      if (e == cudaSuccess) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        int sms = 0;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const int items = batch * heads * 2;
-        const int grid = std::max(1, std::min(items, sms > 0 ? sms : 148));
-        if (max_len <= 192) {
-          e = launch_tc<192, 3>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
-                                err, causal, w);
-          skip_le = 192;
-        } else {
-          e = launch_tc<256, 2>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
-                                err, causal, w);
-          skip_le = 256;
-        }
-        if (e != cudaSuccess) return e;
-        if (max_len <= skip_le) return cudaSuccess;
-      } else {
-        cudaGetLastError();
+      if (!w) {
+        if (why) *why = "attention: no work counter";
+        return cudaErrorInvalidValue;
       }
+      cudaError_t e = cudaMemsetAsync(w, 0, sizeof(unsigned int), s);
+      if (e != cudaSuccess) return e;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int qblocks = (max_len + kAtQ - 1) / kAtQ;
+      const long long items = static_cast<long long>(batch) * heads * qblocks;
+      if (items >= (1ll << 31)) {
+        if (why) *why = "attention: too many work items";
+        return cudaErrorInvalidValue;
+      }
+      const int grid = static_cast<int>(std::max(1ll, std::min<long long>(items, sms > 0 ? sms : 148)));
+      return launch_tc(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, qblocks, scale_log2, tm, err,
+                       causal, w);
     }
+    const int skip_le = 0;
     auto kern = tma ? flash_attn_bf16_d64<true> : flash_attn_bf16_d64<false>;
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);

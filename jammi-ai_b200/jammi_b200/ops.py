@@ -133,8 +133,8 @@ def preprocess_rgb8(images, target: int, mean, std, device="cuda") -> torch.Tens
 
 
 def set_attention_tcgen05(on: bool):
-    """``jb_set_attention_tcgen05``: rows of <= 256 keys on the tcgen05 attention
-    kernel (process-wide; off by default)."""
+    """``jb_set_attention_tcgen05``: every bf16 head-dim-64 row on the tcgen05
+    attention kernel (process-wide; on by default), or off: the mma.sync kernel."""
     lib().jb_set_attention_tcgen05(1 if on else 0)
 
 

@@ -229,6 +229,46 @@ def int8_linear_bf16(x, wq, ws, bias, resid=None, block=512):
     return out
 
 
+LOG2E = 1.4426950408889634
+
+# The attention kernels' block structure: keys in blocks of `block`, p taken
+# against a reference maximum raised only when a block's maximum exceeds it
+# by more than `threshold` (log2 units).  The tcgen05 kernel (the default)
+# uses 128 / 8; the mma.sync kernel 64 / 0 (every rise rescales).
+ATTN_TC = (128, 8.0)
+ATTN_MMA = (64, 0.0)
+
+
+def attention_bf16_p(q, k, v, scale, block=128, threshold=8.0):
+    """softmax(q k^T * scale) v for one row and head, with P stored as bf16 as
+    the device's P V product takes it: per key block, p = 2^(s * scale *
+    log2(e) - m) against the reference maximum m (the first block's maximum,
+    raised -- with O and the sum rescaled -- only when a later block's exceeds
+    it by more than `threshold`); O accumulates bf16(p) V, the sum the
+    unrounded p; the result is O / sum.  float64 otherwise."""
+    t = (np.asarray(q, np.float64) @ np.asarray(k, np.float64).T) * (scale * LOG2E)
+    v = np.asarray(v, np.float64)
+    rows, n = t.shape
+    mref = np.full(rows, -np.inf)
+    lsum = np.zeros(rows)
+    o = np.zeros((rows, v.shape[1]))
+    for b0 in range(0, n, block):
+        tb = t[:, b0:b0 + block]
+        mb = tb.max(axis=1)
+        first = np.isneginf(mref)
+        up = ~first & (mb > mref + threshold)
+        if up.any():
+            alpha = np.exp2(mref[up] - mb[up])
+            o[up] *= alpha[:, None]
+            lsum[up] *= alpha
+            mref[up] = mb[up]
+        mref[first] = mb[first]
+        p = np.exp2(tb - mref[:, None])
+        lsum += p.sum(axis=1)
+        o += bf16_round(p).astype(np.float64) @ v[b0:b0 + block]
+    return o / lsum[:, None]
+
+
 def _row_offsets(lens):
     lens = np.asarray(lens, dtype=np.int64)
     cu = np.zeros(len(lens) + 1, dtype=np.int64)
@@ -236,7 +276,7 @@ def _row_offsets(lens):
     return cu
 
 
-def bert_int8_bf16_forward(weights: dict, cfg: BertConfig, input_ids, lens):
+def bert_int8_bf16_forward(weights: dict, cfg: BertConfig, input_ids, lens, attention=ATTN_TC):
     """The int8 BERT forward with bf16 storage between operators, over the
     valid tokens of each row only (padding never reaches a valid row: the
     -10000 mask of crates/jammi-encoders/src/mask.rs:14-20 underflows to 0).
@@ -244,12 +284,14 @@ def bert_int8_bf16_forward(weights: dict, cfg: BertConfig, input_ids, lens):
     Layer structure as ``Bert::forward_hidden`` (bert.rs:257-276):
     embeddings word + type[0] + position summed in f32 from bf16 tables, LN,
     bf16 (bert.rs:102-111); per layer the Q, K, V int8 linears -> bf16;
-    softmax(QK^T / sqrt(d)) V per row and head in float64 -> bf16 context;
+    softmax(QK^T / sqrt(d)) V per row and head with P stored as bf16 in the
+    block structure of the attention kernel (``attention_bf16_p``; ``attention``
+    = (block, threshold), ``ATTN_TC`` or ``ATTN_MMA``) -> bf16 context;
     attention-out int8 linear + residual -> bf16, LN -> bf16
     (bert.rs:164-167); FFN1 int8 linear -> bf16, exact-erf GELU -> bf16
     (bert.rs:187-190); FFN2 int8 linear + residual -> bf16, LN -> bf16
-    (bert.rs:199-202).  LayerNorm, attention and GELU are evaluated in
-    float64 and rounded once to bf16.
+    (bert.rs:199-202).  LayerNorm, the rest of attention and GELU are
+    evaluated in float64 and rounded once to bf16.
 
     Returns ``(hidden [T, H] float32 of bf16 values, cu [B+1])`` with the
     rows packed: row b is ``hidden[cu[b]:cu[b+1]]``."""
@@ -304,11 +346,11 @@ def bert_int8_bf16_forward(weights: dict, cfg: BertConfig, input_ids, lens):
                     continue
                 m = r1 - r0
                 blk = qkv[r0:r1].astype(np.float64)
-                q = blk[:, 0:H].reshape(m, nh, d).transpose(1, 0, 2)
-                k = blk[:, H:2 * H].reshape(m, nh, d).transpose(1, 0, 2)
-                v = blk[:, 2 * H:].reshape(m, nh, d).transpose(1, 0, 2)
-                probs = softmax_last((q @ k.transpose(0, 2, 1)) * scale)
-                ctx[r0:r1] = bf16_round((probs @ v).transpose(1, 0, 2).reshape(m, H))
+                for hh in range(nh):
+                    c0 = hh * d
+                    ctx[r0:r1, c0:c0 + d] = bf16_round(attention_bf16_p(
+                        blk[:, c0:c0 + d], blk[:, H + c0:H + c0 + d], blk[:, 2 * H + c0:2 * H + c0 + d],
+                        scale, *attention))
 
         _row_blocks(attend, B, 4)
         a = lin(ctx, pre + "attention.output.dense", resid=x)
@@ -339,10 +381,11 @@ def pool_packed(hidden, cu, strategy=0):
     return l2_normalize(out)
 
 
-def bert_int8_bf16_embed(weights: dict, cfg: BertConfig, input_ids, lens, strategy=0):
+def bert_int8_bf16_embed(weights: dict, cfg: BertConfig, input_ids, lens, strategy=0,
+                         attention=ATTN_TC):
     """``Bert::forward`` (bert.rs:279-282) of the int8 format with bf16 storage:
     pooled, L2-normalised ``[B, H]``."""
-    h, cu = bert_int8_bf16_forward(weights, cfg, input_ids, lens)
+    h, cu = bert_int8_bf16_forward(weights, cfg, input_ids, lens, attention)
     return pool_packed(h, cu, strategy)
 
 

@@ -295,12 +295,15 @@ def test_attention_varlen(dev, dtype, heads, d, lens):
     [50] * 7,
     [256, 0, 3, 177],
     [300, 17, 257, 256, 1, 512],
+    [700, 129, 1000],
 ])
 @pytest.mark.parametrize("tc", [True, False])
 def test_attention_tma_rows(dev, lens, causal, tc):
-    """The model forwards' TMA kernels: with tc, rows of <= 256 keys on the
-    tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma, P through TMEM) and
-    longer rows on the mma.sync one in the same call; without, mma.sync only."""
+    """The model forwards' TMA kernels: with tc (the default) every row on the
+    tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma, keys in blocks of 128
+    with an online softmax); without, the mma.sync one.  The rows after the
+    last one hold NaN, as an uninitialised workspace may: keys past a row's end
+    must contribute nothing."""
     ops = _ops()
     ops.set_attention_tcgen05(tc)
     heads, d = 12, 64
@@ -308,16 +311,56 @@ def test_attention_tma_rows(dev, lens, causal, tc):
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])
     qkv = (rng.standard_normal((T + 5, 3 * heads * d)) * 1.5).astype(np.float32)
+    qkv[T:] = np.nan
     qt = _bf16(qkv, dev)
     try:
         ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens),
                             causal=causal, tma=True)
         ops.sync()
     finally:
-        ops.set_attention_tcgen05(False)
+        ops.set_attention_tcgen05(True)
     ref = _attn_ref(qt.double().cpu().numpy()[:T], cu, heads, causal=causal)
-    err = np.abs(ctx.double().cpu().numpy()[:T] - ref).max()
-    assert err < 2e-2, err
+    got = ctx.double().cpu().numpy()[:T]
+    assert np.isfinite(got).all()
+    _assert_bf16_ctx(got, ref)
+
+
+def _assert_bf16_ctx(got, ref):
+    """bf16 context against the exact softmax: P enters the P V product as
+    bf16 (2^-9 relative: at most 2^-9 of max |V| here, ~0.015) and the output
+    is stored as bf16 (half an ulp: 2^-9 |ref|); causal rows' first queries
+    see one or two keys, so |ref| reaches max |V| (~7)."""
+    bound = 1.5e-2 + 4e-3 * np.abs(ref)
+    worst = np.abs(got - ref) / bound
+    assert worst.max() <= 1.0, (np.abs(got - ref).max(), worst.max())
+
+
+def test_attention_tc_rescales_when_a_later_block_dominates(dev):
+    """Online softmax across key blocks: keys 128-135 score ~96 and keys
+    256-263 ~128 against ~N(0, 4^2) elsewhere, so the second block moves the
+    reference maximum by far more than 2^8 (O and the sum rescaled) and the
+    third by less (kept, p up to 2^6): both paths against the exact softmax."""
+    ops = _ops()
+    heads, d = 2, 64
+    lens = [300, 260, 140]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    H = heads * d
+    rng = np.random.default_rng(5)
+    qkv = (rng.standard_normal((T, 3 * H)) * 0.5).astype(np.float32)
+    for b, n in enumerate(lens):
+        s0 = cu[b]
+        qkv[s0:s0 + n, :H] = 1.0                                  # every query = ones
+        qkv[s0 + 128:s0 + 136, H:2 * H] = 1.5                     # block 1: scores 96
+        if n > 256:
+            qkv[s0 + 256:s0 + 264, H:2 * H] = 2.0                 # block 2: scores 128
+    qt = _bf16(qkv, dev)
+    ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens), tma=True)
+    ops.sync()
+    ref = _attn_ref(qt.double().cpu().numpy(), cu, heads)
+    got = ctx.double().cpu().numpy()
+    assert np.isfinite(got).all()
+    _assert_bf16_ctx(got, ref)
 
 
 @pytest.mark.parametrize("dtype,heads,d,lens", [

@@ -289,6 +289,23 @@ def test_int8_bf16_oracle_agrees_with_float64_int8_oracle():
     assert h.dtype == np.float32 and np.array_equal(oq.bf16_round_f32(h), h)   # all bf16 values
 
 
+def test_attention_bf16_p_is_the_softmax_up_to_bf16_p():
+    """The device's P V emulation differs from the exact softmax only by P's
+    bf16 rounding, for every block structure; with one block and no rescale
+    it equals P = bf16(2^(t - max)) / sum(2^(t - max)) exactly."""
+    rng = np.random.default_rng(33)
+    q, k, v = (rng.standard_normal((n, 64)) for n in (40, 300, 300))
+    k[130:140] *= 8.0                                  # a later block dominates
+    exact = ob.softmax_last(q @ k.T / 8.0) @ v
+    for block, thr in (oq.ATTN_TC, oq.ATTN_MMA, (300, 8.0)):
+        got = oq.attention_bf16_p(q, k, v, 1 / 8.0, block, thr)
+        assert np.abs(got - exact).max() < 2e-2 * np.abs(v).max()
+    t = q @ k.T / 8.0 * oq.LOG2E
+    p = np.exp2(t - t.max(1, keepdims=True))
+    want = (oq.bf16_round(p).astype(np.float64) @ v) / p.sum(1, keepdims=True)
+    np.testing.assert_allclose(oq.attention_bf16_p(q, k, v, 1 / 8.0, 300, 8.0), want, rtol=1e-12)
+
+
 def test_projection_head_oracle():
     """LoraLinear over an identity base: x + (alpha/rank) (x A^T) B^T; a zero B
     leaves the embedding unchanged (LoRA's standard init, lora_linear.rs)."""
