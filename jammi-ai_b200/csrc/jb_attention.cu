@@ -317,21 +317,23 @@ __global__ void __launch_bounds__(kFaThreads, 4)
 }
 
 // ── tcgen05 attention, any row length ──────────────────────────────────────
-// A persistent, warp-specialised kernel: one CTA per SM pulls work items
-// (row, head, 128-query block) from a device counter and streams the row's
-// keys through it in blocks of 128 with an online softmax.
-//   warp 0  (TMA): takes the next item, publishes it in a 4-entry ring in
-//           shared memory (an end entry per slot finishes the walk), loads
-//           the item's Q (64-row boxes) into its slot's Q buffer, then each
-//           key block's K and V into a 4-stage ring.
-//   warp 1  (MMA): per slot, S = Q K_j^T (kind::f16, M = 128, N = the block's
+// A persistent, warp-specialised kernel: one CTA per SM pulls (row, head)
+// units from a device counter, splits each into items of 128 queries, and
+// streams the row's keys through each item in blocks of 128 with an online
+// softmax.
+//   warp 0  (TMA): takes the next unit (the counter read two units ahead,
+//           the row offsets one unit ahead), publishes each item in a
+//           4-entry ring in shared memory (an end entry per slot finishes
+//           the walk), loads the item's Q (64-row boxes) into its slot's Q
+//           buffer, then each key block's K and V into a 4-stage ring.
+//   warps 1, 2 (MMA, one per slot): S = Q K_j^T (kind::f16, M = 128, N = the block's
 //           keys rounded up to 16, four K = 16 steps) into the slot's TMEM
 //           columns [0, 128); once the softmax has written P_j (bf16 pairs,
 //           columns [192, 256)), O (+)= P_j V_j with A = P from TMEM and B =
 //           V_j MN-major straight from its TMA tile, into columns [128, 192),
-//           and S_{j+1} right behind it.  Every step is issued as soon as its
-//           inputs are ready (non-blocking probes of the barriers).
-//   warps 2-9 and 10-17 (softmax, one group per slot; items alternate
+//           and S_{j+1} right behind it.  One issuing thread per slot, so
+//           the two slots' MMAs are issued side by side.
+//   warps 3-10 and 11-18 (softmax, one group per slot; items alternate
 //           slots): warp w reads TMEM lanes 32 (w % 4) .. + 31, and the two
 //           warps of a group on the same lane quarter split each row's key
 //           chunks (even / odd 16-key chunks), so two threads serve a query
@@ -359,7 +361,7 @@ constexpr int kAtSlotCols = 256;     // TMEM columns per slot; two slots
 constexpr int kAtOCol = 128;         // O's first column inside a slot (S at [0, 128))
 constexpr int kAtPCol = 192;         // P's first column inside a slot (bf16 pairs)
 constexpr int kAtGroupWarps = 8;     // two warps per TMEM lane quarter: two threads per row
-constexpr int kAtThreads = 64 + 2 * 32 * kAtGroupWarps;
+constexpr int kAtThreads = 96 + 2 * 32 * kAtGroupWarps;  // TMA warp, two MMA warps, softmax
 constexpr int kAtQBytes = kAtQ * 128;                  // 16 KB
 constexpr int kAtKBytes = kAtKB * 128;                 // 16 KB (K or V of a block)
 constexpr int kAtMetaBytes = 512 + 2 * 2 * 4 * 2 * 32 * 4 + 2 * 4 * 2 * 32 * 4;  // barriers, ring, exchange
@@ -397,10 +399,9 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16_at(uint32_t taddr, uint32_t* 
 
 __global__ void __launch_bounds__(kAtThreads, 1)
     attn_tc_kernel(const int* __restrict__ cu, bf16* __restrict__ ctx, int batch, int heads,
-                   int qblocks, float scale_log2, const __grid_constant__ CUtensorMap tm, int* err,
+                   float scale_log2, const __grid_constant__ CUtensorMap tm, int* err,
                    int causal, unsigned int* work) {
   const int H = heads * 64;
-  const int items = batch * heads * qblocks;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -420,9 +421,9 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   auto kfull = [&](int st) { return bars + 8u * (12 + st); };
   auto vfull = [&](int st) { return bars + 8u * (16 + st); };
   auto kvempty = [&](int st) { return bars + 8u * (20 + st); };
-  const uint32_t spare = bars + 8u * 24;
-  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(meta + 8 * 25);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 25 + 4);
+  const uint32_t spare = bars + 8u * 24;  // [2], one per MMA warp
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(meta + 8 * 26);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 26 + 4);
   volatile AtItem* ring = reinterpret_cast<volatile AtItem*>(meta + 256);  // [4]
   // the two threads of a row exchange their partial maxima (per key block,
   // double-buffered by block parity) and sums (per item) here
@@ -446,6 +447,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(kvempty(st), 1);
     }
     mbar_init(spare, 1);
+    mbar_init(spare + 8u, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -457,23 +459,48 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ── TMA producer
+      // Work units are (row, head) pairs from the device counter, expanded
+      // here into their 128-query items.  The counter is read two units
+      // ahead and a unit's row offsets one unit ahead, so neither round trip
+      // sits between two items.
+      const unsigned units = static_cast<unsigned>(batch) * heads;
+      // a_next < a_after < later fetches (one thread's atomics return
+      // increasing values), so a_next >= units means this CTA has no units left
+      unsigned a_next = atomicAdd(work, 1u);
+      unsigned a_after = atomicAdd(work, 1u);  // the unit after the next
+      int next_start = 0, next_n = 0;
+      if (a_next < units) {
+        const int b = static_cast<int>(a_next) / heads;
+        next_start = cu[b];
+        next_n = cu[b + 1] - next_start;
+      }
       int k = 0, bc = 0, ends = 0;
+      int cur_start = 0, cur_n = 0, cur_h = 0, cur_q0 = 0, cur_qend = 0;  // items q0 < cur_qend left
       bool ok = true;
       while (ends < 2 && ok) {
         const int sl = k & 1;
         if (!mbar_wait(qempty(sl), ((k >> 1) & 1) ^ 1u, abort_flag)) break;
         AtItem it{-1, 0, 0, 0, 0, 0, 0};
         if (ends == 0) {
-          while (true) {
-            const int idx = static_cast<int>(atomicAdd(work, 1u));
-            if (idx >= items) break;
-            const int qb = idx % qblocks, bh = idx / qblocks, b = bh / heads;
-            const int q0 = qb * kAtQ, start = cu[b], n = cu[b + 1] - start;
-            if (q0 < n) {
-              const int nk = (n + kAtKB - 1) / kAtKB;
-              it = AtItem{idx, start, n, bh - b * heads, q0, bc, causal ? min(nk, qb + 1) : nk};
-              break;
+          while (cur_q0 >= cur_qend && a_next < units) {  // the next unit with rows
+            cur_start = next_start;
+            cur_n = next_n;
+            cur_h = static_cast<int>(a_next) % heads;
+            cur_q0 = 0;
+            cur_qend = cur_n;
+            a_next = a_after;  // returned long ago: issued a unit earlier
+            if (a_next < units) {
+              const int b = static_cast<int>(a_next) / heads;
+              next_start = cu[b];  // used one unit later
+              next_n = cu[b + 1] - next_start;
+              a_after = atomicAdd(work, 1u);
             }
+          }
+          if (cur_q0 < cur_qend) {
+            const int nk = (cur_n + kAtKB - 1) / kAtKB;
+            const int qb = cur_q0 / kAtQ;
+            it = AtItem{1, cur_start, cur_n, cur_h, cur_q0, bc, causal ? min(nk, qb + 1) : nk};
+            cur_q0 += kAtQ;
           }
         }
         volatile AtItem& e = ring[k & 3];
@@ -523,97 +550,70 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ── MMA issuer
-      // per slot: state 0 = wait for the next item, 1 = issue S_j, 2 = issue
-      // P_j V_j, 3 = finished; ti = items done, bs = key blocks done
-      int state[2] = {0, 0}, ti[2] = {0, 0}, bs[2] = {0, 0}, j[2] = {0, 0};
-      int n_[2] = {0, 0}, b0[2] = {0, 0}, nb[2] = {0, 0};
-      bool ok = true;
+  } else if (warp <= 2) {
+    if (lane == 0) {  // ── MMA issuer of slot warp - 1 (items k with k % 2 == slot)
+      const int sl = warp - 1;
+      const uint32_t slot = tbase + static_cast<uint32_t>(sl * kAtSlotCols);
+      const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
       const uint32_t idesc_pv = idesc_bf16_f32(kAtQ, 64) | (1u << 16);  // B (V) MN-major
-      uint64_t t0 = global_timer_ns();
-      while (state[0] != 3 || state[1] != 3) {
-        bool progress = false;
-#pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          const uint32_t slot = tbase + static_cast<uint32_t>(sl * kAtSlotCols);
-          if (state[sl] == 0 && mbar_test_wait(qfull(sl), ti[sl] & 1)) {
-            const int k = 2 * ti[sl] + sl;
-            if (ring[k & 3].idx < 0) {
-              state[sl] = 3;
-              progress = true;
-            } else if (mbar_test_wait(tfree(sl), (ti[sl] & 1) ^ 1u)) {
-              n_[sl] = ring[k & 3].n;
-              b0[sl] = ring[k & 3].b0;
-              nb[sl] = ring[k & 3].nb;
-              j[sl] = 0;
-              state[sl] = 1;
-              progress = true;
-            }
-          }
-          if (state[sl] == 1) {
-            const int b = b0[sl] + j[sl], st = b % kAtStages;
-            // S_j overwrites S_{j-1}, which the softmax read before it
-            // released P_{j-1}; P_{j-1} V (issued before) is untouched
-            if (mbar_test_wait(kfull(st), (b / kAtStages) & 1)) {
-              tc_fence_after();
-              const int kn = min(kAtKB, n_[sl] - kAtKB * j[sl]);
-              const uint32_t idesc = idesc_bf16_f32(kAtQ, (kn + 15) & ~15);
-              const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_bf16(slot, umma_desc_sw128(sQ + 32u * kk), umma_desc_sw128(sK(st) + 32u * kk), idesc,
-                         kk != 0);
-              mma_commit(sfull(sl));
-              if (j[sl] == nb[sl] - 1) mma_commit(qempty(sl));  // Q read by the item's last S
-              state[sl] = 2;
-              progress = true;
-            }
-          }
-          if (state[sl] == 2) {
-            const int b = b0[sl] + j[sl], st = b % kAtStages;
-            if (mbar_test_wait(pfull(sl), bs[sl] & 1) && mbar_test_wait(vfull(st), (b / kAtStages) & 1)) {
-              tc_fence_after();
-              const int kn = min(kAtKB, n_[sl] - kAtKB * j[sl]);
-              const int chunks = ((kn + 15) & ~15) >> 4;
-#pragma unroll 1
-              for (int c = 0; c < chunks; ++c)
-                mma_bf16_ta(slot + kAtOCol, slot + kAtPCol + 8u * c, umma_desc_sw128(sV(st) + 2048u * c),
-                            idesc_pv, (j[sl] > 0 || c > 0) ? 1u : 0u);
-              mma_commit(ofull(sl));
-              mma_commit(kvempty(st));
-              ++bs[sl];
-              if (++j[sl] == nb[sl]) {
-                ++ti[sl];
-                state[sl] = 0;
-              } else {
-                state[sl] = 1;
-              }
-              progress = true;
-            }
-          }
-        }
-        if (progress) {
-          t0 = global_timer_ns();
-        } else if (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs) {
-          *abort_flag = 1;
+      int bs = 0;  // key blocks done in this slot
+      bool ok = true;
+      for (int ti = 0; ok; ++ti) {
+        const int k = 2 * ti + sl;
+        if (!mbar_wait(qfull(sl), ti & 1, abort_flag)) {
           ok = false;
           break;
+        }
+        if (ring[k & 3].idx < 0) break;  // the walk is over
+        const int n = ring[k & 3].n, b0 = ring[k & 3].b0, nb = ring[k & 3].nb;
+        // the slot's previous item is out of TMEM
+        if (!mbar_wait(tfree(sl), (ti & 1) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        for (int j = 0; j < nb && ok; ++j, ++bs) {
+          const int b = b0 + j, st = b % kAtStages;
+          const int kn = min(kAtKB, n - kAtKB * j), kpad = (kn + 15) & ~15;
+          // S_j overwrites S_{j-1}, which the softmax read before it released
+          // P_{j-1}; P_{j-1} V (issued before) is untouched
+          if (!mbar_wait(kfull(st), (b / kAtStages) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16_f32(kAtQ, kpad);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16(slot, umma_desc_sw128(sQ + 32u * kk), umma_desc_sw128(sK(st) + 32u * kk), idesc, kk != 0);
+          mma_commit(sfull(sl));
+          if (j == nb - 1) mma_commit(qempty(sl));  // Q read by the item's last S
+          if (!mbar_wait(pfull(sl), bs & 1, abort_flag) ||
+              !mbar_wait(vfull(st), (b / kAtStages) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < (kpad >> 4); ++c)
+            mma_bf16_ta(slot + kAtOCol, slot + kAtPCol + 8u * c, umma_desc_sw128(sV(st) + 2048u * c),
+                        idesc_pv, (j > 0 || c > 0) ? 1u : 0u);
+          mma_commit(ofull(sl));
+          mma_commit(kvempty(st));
         }
       }
       if (!ok) {
         // every MMA issued completes before TMEM is freed (bounded)
         volatile int no_abort = 0;
-        mma_commit(spare);
-        mbar_wait(spare, 0, &no_abort);
+        mma_commit(spare + 8u * sl);
+        mbar_wait(spare + 8u * sl, 0, &no_abort);
       }
     }
   } else {  // ── softmax / epilogue groups
-    const int gw = (warp - 2) % kAtGroupWarps;
-    const int g = (warp - 2) / kAtGroupWarps;          // slot: items k with k % 2 == g
+    const int gw = (warp - 3) % kAtGroupWarps;
+    const int g = (warp - 3) / kAtGroupWarps;          // slot: items k with k % 2 == g
     const int quarter = warp & 3;                       // TMEM lanes 32 quarter .. + 31
     const int half = gw >> 2;                           // this thread's key chunks: t % 2 == half
-    const int gtid = tid - 64 - g * 32 * kAtGroupWarps;  // 0 .. 255
+    const int gtid = tid - 96 - g * 32 * kAtGroupWarps;  // 0 .. 255
     const int r = 32 * quarter + lane;                  // query row of the item
     const uint32_t pair_bar = 1 + g * 4 + quarter;     // named barrier of the two warps of a row
     const uint32_t trow = tbase + static_cast<uint32_t>(g * kAtSlotCols) + (static_cast<uint32_t>(32 * quarter) << 16);
@@ -889,7 +889,7 @@ std::atomic<int> g_attn_tc{1};  // jb_set_attention_tcgen05 (on by default)
 bool attn_tc_enabled() { return g_attn_tc.load(std::memory_order_relaxed) != 0; }
 
 cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int batch, int heads,
-                      int qblocks, float scale_log2, const CUtensorMap& tm, int* err, int causal,
+                      float scale_log2, const CUtensorMap& tm, int* err, int causal,
                       unsigned int* work) {
   // the shared-memory opt-in is a property of each device's context
   static std::atomic<uint8_t> attr_set[64];
@@ -900,7 +900,7 @@ cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int ba
     if (e != cudaSuccess) return e;
     attr_set[dev].store(1, std::memory_order_release);
   }
-  attn_tc_kernel<<<grid, kAtThreads, kAtSmem, s>>>(cu, ctx, batch, heads, qblocks, scale_log2, tm, err,
+  attn_tc_kernel<<<grid, kAtThreads, kAtSmem, s>>>(cu, ctx, batch, heads, scale_log2, tm, err,
                                                     causal, work);
   return cudaGetLastError();
 }
@@ -959,14 +959,9 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
       cudaGetDevice(&dev);
       int sms = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int qblocks = (max_len + kAtQ - 1) / kAtQ;
-      const long long items = static_cast<long long>(batch) * heads * qblocks;
-      if (items >= (1ll << 31)) {
-        if (why) *why = "attention: too many work items";
-        return cudaErrorInvalidValue;
-      }
-      const int grid = static_cast<int>(std::max(1ll, std::min<long long>(items, sms > 0 ? sms : 148)));
-      return launch_tc(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, qblocks, scale_log2, tm, err,
+      const long long units = static_cast<long long>(batch) * heads;  // (row, head) pairs
+      const int grid = static_cast<int>(std::max(1ll, std::min<long long>(units, sms > 0 ? sms : 148)));
+      return launch_tc(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm, err,
                        causal, w);
     }
     const int skip_le = 0;
