@@ -410,14 +410,13 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const uint32_t sKV0 = base + 2 * kAtQBytes;                  // [4][K 16 KB | V 16 KB]
   uint8_t* meta = smem_raw + (sKV0 + kAtStages * 2 * kAtKBytes - raw);
   const uint32_t bars = smem_u32(meta);
-  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] t_free[2]
-  // k_full[4] v_full[4] kv_empty[4] spare
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] (unused 2)
+  // k_full[4] v_full[4] kv_empty[4] spare[2]
   auto qfull = [&](int s) { return bars + 8u * (0 + s); };
   auto qempty = [&](int s) { return bars + 8u * (2 + s); };
   auto sfull = [&](int s) { return bars + 8u * (4 + s); };
   auto pfull = [&](int s) { return bars + 8u * (6 + s); };
   auto ofull = [&](int s) { return bars + 8u * (8 + s); };
-  auto tfree = [&](int s) { return bars + 8u * (10 + s); };
   auto kfull = [&](int st) { return bars + 8u * (12 + st); };
   auto vfull = [&](int st) { return bars + 8u * (16 + st); };
   auto kvempty = [&](int st) { return bars + 8u * (20 + st); };
@@ -439,7 +438,6 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(sfull(s), 1);
       mbar_init(pfull(s), kAtGroupWarps);
       mbar_init(ofull(s), 1);
-      mbar_init(tfree(s), kAtGroupWarps);
     }
     for (int st = 0; st < kAtStages; ++st) {
       mbar_init(kfull(st), 1);
@@ -566,11 +564,9 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         if (ring[k & 3].idx < 0) break;  // the walk is over
         const int n = ring[k & 3].n, b0 = ring[k & 3].b0, nb = ring[k & 3].nb;
-        // the slot's previous item is out of TMEM
-        if (!mbar_wait(tfree(sl), (ti & 1) ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
+        // S_0 goes in as soon as the previous item's last P is written (its
+        // S columns are read by then); P_0 V, which overwrites O, waits for
+        // P_0, which the softmax writes only after its epilogue read O
         for (int j = 0; j < nb && ok; ++j, ++bs) {
           const int b = b0 + j, st = b % kAtStages;
           const int kn = min(kAtKB, n - kAtKB * j), kpad = (kn + 15) & ~15;
@@ -673,9 +669,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               for (int uu = 0; uu < 2; ++uu) {
                 if (u0 + uu < mine) {
                   const int c0 = 16 * (2 * (u0 + uu) + half);
+                  if (c0 + 16 <= lim) {  // no masked key in this chunk
+                    float a = fmaxf(__uint_as_float(v[uu][0]), __uint_as_float(v[uu][1]));
 #pragma unroll
-                  for (int e = 0; e < 16; ++e)
-                    if (c0 + e < lim) m = fmaxf(m, __uint_as_float(v[uu][e]));
+                    for (int e = 2; e < 16; e += 2)
+                      a = fmaxf(a, fmaxf(__uint_as_float(v[uu][e]), __uint_as_float(v[uu][e + 1])));
+                    m = fmaxf(m, a);
+                  } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                      if (c0 + e < lim) m = fmaxf(m, __uint_as_float(v[uu][e]));
+                  }
                 }
               }
             }
@@ -725,13 +729,16 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               for (int uu = 0; uu < 2; ++uu) {
                 if (u0 + uu < mine) {
                   const int t = 2 * (u0 + uu) + half, c0 = 16 * t;
+                  const bool full = c0 + 16 <= lim;  // no masked key in this chunk
                   uint32_t pk[8];
 #pragma unroll
                   for (int e = 0; e < 16; e += 2) {
                     float2 z = __ffma2_rn(make_float2(__uint_as_float(v[uu][e]), __uint_as_float(v[uu][e + 1])),
                                           f2(scale_log2), f2(-mref));
-                    if (c0 + e >= lim) z.x = -INFINITY;  // keys past the row's end (or the query)
-                    if (c0 + e + 1 >= lim) z.y = -INFINITY;
+                    if (!full) {  // keys past the row's end (or the query)
+                      if (c0 + e >= lim) z.x = -INFINITY;
+                      if (c0 + e + 1 >= lim) z.y = -INFINITY;
+                    }
                     const float p0 = ex2_approx(z.x), p1 = ex2_approx(z.y);
                     lsum0 += p0;
                     lsum1 += p1;
@@ -772,9 +779,6 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tfree(g));
     }
   }
   tc_fence_before();
