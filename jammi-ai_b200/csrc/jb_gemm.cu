@@ -78,6 +78,7 @@ struct EpiParams {
   int N;
   int K;
   int* err;
+  unsigned int* row_max;
 };
 
 // SIMT path: CUDA's erff / expf.
@@ -207,7 +208,7 @@ template <bool S8>
 __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensorMap* tmC, int row0,
                                               int lane, int col0, const uint32_t (&r)[kUnitCols],
                                               const float* sb, const float* ss, float as,
-                                              uint32_t buf, const uint4 (&rres)[kSlots]) {
+                                              uint32_t buf, const uint4 (&rres)[kSlots], float& vmax) {
   float v[kUnitCols];
   dequant_bias<S8, kUnitCols>(r, sb, ss, as, v);
   activation<kUnitCols>(p.epi, v);
@@ -232,6 +233,10 @@ __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensor
       }
     }
   }
+  if (p.row_max) {  // the largest value before bf16 rounding rounds to the largest stored one
+#pragma unroll
+    for (int j = 0; j < kUnitCols; ++j) vmax = fmaxf(vmax, v[j]);
+  }
 #pragma unroll
   for (int q = 0; q < kSlots; ++q) {
     uint4 out;
@@ -255,7 +260,7 @@ __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensor
 template <bool S8>
 __device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
                                          const uint32_t (&r)[kUnitCols], const float* sb,
-                                         const float* ss, float as) {
+                                         const float* ss, float as, float& vmax) {
   constexpr int W = kUnitCols;
   const int ncols = min(W, p.N - col0);
   const bool full = ncols == W;
@@ -285,6 +290,7 @@ __device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
       if (j < ncols) {
         float x = v[j];
         if (p.epi == JB_EPI_RESIDUAL) x += __bfloat162float(rs[j]);
+        vmax = fmaxf(vmax, x);
         c[j] = __float2bfloat16_rn(x);
       }
     }
@@ -479,6 +485,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      float vmax = 0.f;  // this thread's row: largest output of its columns (row_max)
 #pragma unroll 1
       for (int c = c_begin; c < c_end; c += kUnitCols) {
         const int col0 = nb * BN + c;
@@ -491,12 +498,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           load_resid_unit(p, row0, lane, M, col0 + kUnitCols, rnext);
         tmem_wait_ld();
         if (fast(c))
-          epi_unit_bf16<S8>(p, &tmC, row0, lane, col0, r, pb + c, ps + c, as, my_buf, rres);
+          epi_unit_bf16<S8>(p, &tmC, row0, lane, col0, r, pb + c, ps + c, as, my_buf, rres, vmax);
         else if (row0 + lane < M)
-          epi_unit<S8>(p, row0 + lane, col0, r, pb + c, ps + c, as);
+          epi_unit<S8>(p, row0 + lane, col0, r, pb + c, ps + c, as, vmax);
 #pragma unroll
         for (int i = 0; i < kSlots; ++i) rres[i] = rnext[i];
       }
+      if (p.row_max && vmax > 0.f && row0 + lane < M)
+        atomicMax(p.row_max + row0 + lane, __float_as_uint(__bfloat162float(__float2bfloat16_rn(vmax))));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -687,6 +696,7 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why) {
   p.N = g.N;
   p.K = g.K;
   p.err = g.err;
+  p.row_max = g.row_max;
   if (g.epi == JB_EPI_RESIDUAL && !g.resid) {
     if (why) *why = "linear: residual epilogue without a residual tensor";
     return cudaErrorInvalidValue;

@@ -35,6 +35,10 @@ struct GemmArgs {
   int c_dtype = JB_DT_BF16;
   int epi = JB_EPI_NONE;
   int* err = nullptr;  // device flag set when a bounded wait gives up
+  // optional (tcgen05 path, bf16 output): per output row, atomicMax of the
+  // row's largest stored value as f32 bits when it is positive (the bits of
+  // non-negative floats order as the values do); rows must start at 0
+  unsigned int* row_max = nullptr;
 };
 
 // Returns cudaSuccess or an error; *why receives a message for invalid shapes.
@@ -53,6 +57,7 @@ struct LnArgs {
   const int* drows = nullptr;
   int cols = 0;
   float eps = 1e-12f;
+  unsigned int* zero_rows = nullptr;  // optional: set to 0 for every normalised row
 };
 cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s);
 
@@ -63,6 +68,14 @@ cudaError_t init_gelu_table(cudaStream_t s);
 cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
                                  const int* drows, int cols, cudaStream_t s,
                                  int activation = JB_EPI_NONE);
+// The FFN2 input of the int8 forward: bf16(GELU(x)) per-token int8, with each
+// row's largest x already known (row_max, as a linear's epilogue records it):
+// a row whose largest x is >= 0.5 has amax = GELU(that x) (GELU rises on the
+// positives and stays above -0.17 on the negatives), so the row is quantised
+// in one streaming pass; other rows take two passes.
+cudaError_t launch_gelu_quantize_rowmax(const void* x, const unsigned int* row_max, int8_t* q,
+                                        float* scale, int rows, const int* drows, int cols,
+                                        cudaStream_t s);
 
 // BERT embeddings: word[ids] + type[0] + pos[p] -> LayerNorm, written packed
 // at row cu[b] + p for p < len[b].  type0 == null: no type row; gamma == null:
@@ -85,11 +98,11 @@ struct EmbedArgs {
 };
 cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s);
 
-// Rows of <= 256 keys (bf16, head_dim 64, TMA) on the tcgen05 kernel instead
-// of the mma.sync one; process-wide, off by default.  That kernel takes its
-// work items from a device counter: `work` (one int the caller owns, zeroed
-// on the stream before the launch; the model forwards pass one in their
-// workspace), or, when null, a slot of a small static pool.
+// bf16 head_dim-64 rows with TMA on the tcgen05 kernel (on by default) or the
+// mma.sync one; process-wide.  The tcgen05 kernel takes its work units from
+// a device counter: `work` (one int the caller owns, zeroed on the stream
+// before the launch; the model forwards pass one in their workspace), or,
+// when null, a slot of a small static pool.
 void set_attention_tcgen05(bool on);
 // causal != 0: query i attends to keys j <= i of its row (the OpenCLIP text
 // mask, clip_text.rs:350-362).

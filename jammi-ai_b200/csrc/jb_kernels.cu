@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(LnArgs a) {
                        static_cast<T*>(a.y) + static_cast<size_t>(row) * a.cols,
                        a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
                        a.yscale ? a.yscale + row : nullptr);
+    if (a.zero_rows && lane == 0) a.zero_rows[row] = 0u;
   }
 }
 
@@ -244,6 +245,7 @@ __global__ void __launch_bounds__(256) layernorm_bf16_kernel(LnArgs a) {
                           static_cast<bf16*>(a.y) + static_cast<size_t>(row) * a.cols,
                           a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
                           a.yscale ? a.yscale + row : nullptr);
+    if (a.zero_rows && lane == 0) a.zero_rows[row] = 0u;
   }
 }
 
@@ -403,9 +405,8 @@ __global__ void __launch_bounds__(256, (ACT == JB_EPI_GELU ? JB_GELU_Q_BLOCKS : 
 // Every bf16 input has one correctly rounded bf16 GELU: bf16(x * Phi(x)) with
 // Phi from CUDA's double-precision erf, tabulated once per device (65536
 // entries, 128 KB).  The FFN2-input quantiser stages the table in shared
-// memory and replaces the activation's arithmetic by one lookup for half of
-// the values (the lookups' bank conflicts, not the arithmetic, would bound a
-// table-only kernel); the other half use gelu_tc2.
+// memory and looks every value up: one function for every element, rising
+// on the positives, so a row's largest GELU is the GELU of its largest x.
 __device__ __align__(16) uint16_t g_gelu_bf16[65536];
 
 __global__ void gelu_table_kernel() {
@@ -419,8 +420,11 @@ __global__ void gelu_table_kernel() {
   g_gelu_bf16[u] = static_cast<__nv_bfloat16_raw>(b).x;
 }
 
-constexpr int kGeluQThreads = 512;
+constexpr int kGeluQThreads = 1024;
 constexpr int kGeluTableBytes = 65536 * 2;
+// A row whose largest x reaches this has amax = GELU(largest x): GELU(0.5) =
+// 0.35 exceeds |GELU| anywhere on the negatives (at most 0.17, near -0.75).
+constexpr float kGeluRowMaxFast = 0.5f;
 
 // GELU of the two bf16 halves of w by lookup (table in shared memory).
 __device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* tab, uint32_t w) {
@@ -428,12 +432,16 @@ __device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* tab, uint32_t w
   return lo | (hi << 16);
 }
 
-// One warp per row (up to MAXV 16-byte vectors per lane, held in registers
-// after the lookup); persistent, one block per SM.
-template <int MAXV>
+// Per-token int8 of bf16(GELU(x)), x bf16 [rows, cols] (cols a multiple of
+// 8): one warp per row, persistent (one 1024-thread block per SM with the
+// table in shared memory).  row_max[row] holds the row's largest x (f32
+// bits, 0 when none is positive).  At >= kGeluRowMaxFast the row's amax is a
+// single lookup and the row is read once: 16-byte loads, four per lane in
+// flight, lookup, quantise, 8-byte stores.  Other rows first take the amax
+// over the row (a second read, mostly from L2).
 __global__ void __launch_bounds__(kGeluQThreads, 1)
-    gelu_quantize_bf16_kernel(const bf16* __restrict__ x, int8_t* q, float* scale, int rows,
-                              const int* drows, int cols) {
+    gelu_quantize_kernel(const bf16* __restrict__ x, const unsigned int* row_max, int8_t* q,
+                         float* scale, int rows, const int* drows, int cols) {
   extern __shared__ __align__(16) uint16_t tab[];
   {
     const uint4* src = reinterpret_cast<const uint4*>(g_gelu_bf16);
@@ -447,51 +455,67 @@ __global__ void __launch_bounds__(kGeluQThreads, 1)
   const int nvec = cols / 8;
   for (int row = blockIdx.x * kWarps + warp; row < R; row += gridDim.x * kWarps) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
-    uint4 raw[MAXV];
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i)
-      if (lane + i * 32 < nvec) raw[i] = __ldg(xr + lane + i * 32);
-    // lookup, and the largest |value| as bf16 magnitude bits (integer order
-    // of non-negative bf16 bit patterns is their numeric order)
-    uint32_t mx2 = 0;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      if (lane + i * 32 < nvec) {
-        // half of the values by table (shared-memory pipe), half by the
-        // A&S 7.1.28 arithmetic (FMA pipe): the two pipes share the work
-        raw[i].x = gelu_lookup2(tab, raw[i].x);
-        raw[i].y = gelu_lookup2(tab, raw[i].y);
-        {
-          float v[4];
-          v[0] = __uint_as_float(raw[i].z << 16); v[1] = __uint_as_float(raw[i].z & 0xFFFF0000u);
-          v[2] = __uint_as_float(raw[i].w << 16); v[3] = __uint_as_float(raw[i].w & 0xFFFF0000u);
-          const float2 g0 = gelu_tc2(make_float2(v[0], v[1]));
-          const float2 g1 = gelu_tc2(make_float2(v[2], v[3]));
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(g0.x, g0.y), h1 = __floats2bfloat162_rn(g1.x, g1.y);
-          raw[i].z = *reinterpret_cast<uint32_t*>(&h0);
-          raw[i].w = *reinterpret_cast<uint32_t*>(&h1);
-        }
-        mx2 = __vmaxu2(mx2, raw[i].x & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, raw[i].y & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, raw[i].z & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, raw[i].w & 0x7FFF7FFFu);
+    const float xm = __uint_as_float(row_max[row]);
+    float amax;
+    if (xm >= kGeluRowMaxFast) {
+      amax = __uint_as_float(static_cast<uint32_t>(tab[__float_as_uint(xm) >> 16]) << 16);
+    } else {
+      // the largest |GELU| as bf16 magnitude bits (integer order of
+      // non-negative bf16 bit patterns is their numeric order)
+      uint32_t mx2 = 0;
+      for (int vi = lane; vi < nvec; vi += 32) {
+        const uint4 r = __ldg(xr + vi);
+        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.x) & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.y) & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.z) & 0x7FFF7FFFu);
+        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.w) & 0x7FFF7FFFu);
       }
+      amax = warp_max(fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u)));
     }
-    const float amax = warp_max(fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u)));
     const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-    int8_t* qr = q + static_cast<size_t>(row) * cols;
+    uint2* qr = reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * cols);
+    for (int v0 = lane; v0 < nvec; v0 += 4 * 32) {
+      uint4 r[4];
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = lane + i * 32;
-      if (vi < nvec) {
-        float v[8];
-        Vec<bf16>::unpack(raw[i], v);
-        *reinterpret_cast<uint2*>(qr + vi * 8) =
-            make_uint2(quant4(v[0], v[1], v[2], v[3], inv), quant4(v[4], v[5], v[6], v[7], inv));
+      for (int u = 0; u < 4; ++u)
+        if (v0 + 32 * u < nvec) r[u] = __ldg(xr + v0 + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (v0 + 32 * u < nvec) {
+          uint4 g;
+          g.x = gelu_lookup2(tab, r[u].x);
+          g.y = gelu_lookup2(tab, r[u].y);
+          g.z = gelu_lookup2(tab, r[u].z);
+          g.w = gelu_lookup2(tab, r[u].w);
+          float v[8];
+          Vec<bf16>::unpack(g, v);
+          qr[v0 + 32 * u] = make_uint2(quant4(v[0], v[1], v[2], v[3], inv), quant4(v[4], v[5], v[6], v[7], inv));
+        }
       }
     }
     if (lane == 0) scale[row] = amax / 127.0f;
   }
+}
+
+// Each row's largest bf16 value (f32 bits, 0 when none is positive): the
+// row_max the quantiser above takes, for callers without a linear's epilogue
+// to record it.  One warp per row.
+__global__ void __launch_bounds__(256) row_max_bf16_kernel(const bf16* __restrict__ x, unsigned int* out,
+                                                           int rows, const int* drows, int cols) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerBlock + warp;
+  const int R = drows ? min(*drows, rows) : rows;
+  if (row >= R) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
+  float m = 0.f;
+  for (int vi = lane; vi < cols / 8; vi += 32) {
+    float v[8];
+    Vec<bf16>::unpack(__ldg(xr + vi), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, v[e]);
+  }
+  m = warp_max(m);
+  if (lane == 0) out[row] = __float_as_uint(m);
 }
 
 // ── elementwise exact-erf GELU, in place ──────────────────────────────────
@@ -959,18 +983,16 @@ namespace {
 std::mutex g_gelu_mu;
 bool g_gelu_ready[64] = {};
 
-template <int MAXV>
-cudaError_t launch_gelu_lookup(const bf16* x, int8_t* q, float* scale, int rows, const int* drows,
-                               int cols, cudaStream_t s) {
-  auto kern = gelu_quantize_bf16_kernel<MAXV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+cudaError_t launch_gelu_quantize(const bf16* x, const unsigned int* row_max, int8_t* q, float* scale,
+                                 int rows, const int* drows, int cols, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(gelu_quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kGeluTableBytes);
   if (e != cudaSuccess) return e;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned need = blocks_for(rows, kGeluQThreads / 32);
   const unsigned grid = std::min<unsigned>(need, static_cast<unsigned>(num_sms(dev)));
-  kern<<<grid, kGeluQThreads, kGeluTableBytes, s>>>(x, q, scale, rows, drows, cols);
+  gelu_quantize_kernel<<<grid, kGeluQThreads, kGeluTableBytes, s>>>(x, row_max, q, scale, rows, drows, cols);
   return cudaGetLastError();
 }
 }  // namespace
@@ -996,20 +1018,32 @@ cudaError_t init_gelu_table(cudaStream_t s) {
 cudaError_t launch_quantize_rows(const void* x, int dtype, int8_t* q, float* scale, int rows,
                                  const int* drows, int cols, cudaStream_t s, int activation) {
   if (rows == 0) return cudaSuccess;
-  if (activation == JB_EPI_GELU && dtype == JB_DT_BF16 && cols % 8 == 0 && cols <= 4096) {
+  if (activation == JB_EPI_GELU && dtype == JB_DT_BF16 && cols % 8 == 0) {
     cudaError_t e = init_gelu_table(s);  // no-op after the first call on this device
     if (e != cudaSuccess) return e;
+    // the rows' largest values go to `scale` first (the quantiser reads a
+    // row's entry before it writes the row's scale there)
     const bf16* xb = static_cast<const bf16*>(x);
-    const int per_lane = (cols / 8 + 31) / 32;
-    if (per_lane <= 4) return launch_gelu_lookup<4>(xb, q, scale, rows, drows, cols, s);
-    if (per_lane <= 8) return launch_gelu_lookup<8>(xb, q, scale, rows, drows, cols, s);
-    if (per_lane <= 12) return launch_gelu_lookup<12>(xb, q, scale, rows, drows, cols, s);
-    return launch_gelu_lookup<16>(xb, q, scale, rows, drows, cols, s);
+    unsigned int* rmax = reinterpret_cast<unsigned int*>(scale);
+    row_max_bf16_kernel<<<blocks_for(rows, kRowsPerBlock), 256, 0, s>>>(xb, rmax, rows, drows, cols);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_gelu_quantize(xb, rmax, q, scale, rows, drows, cols, s);
   }
   if (activation == JB_EPI_GELU)
     return launch_quantize_act<JB_EPI_GELU>(x, dtype, q, scale, rows, drows, cols, s);
   if (activation != JB_EPI_NONE) return cudaErrorInvalidValue;
   return launch_quantize_act<JB_EPI_NONE>(x, dtype, q, scale, rows, drows, cols, s);
+}
+
+cudaError_t launch_gelu_quantize_rowmax(const void* x, const unsigned int* row_max, int8_t* q,
+                                        float* scale, int rows, const int* drows, int cols,
+                                        cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (cols % 8) return cudaErrorInvalidValue;
+  cudaError_t e = init_gelu_table(s);  // no-op after the first call on this device
+  if (e != cudaSuccess) return e;
+  return launch_gelu_quantize(static_cast<const bf16*>(x), row_max, q, scale, rows, drows, cols, s);
 }
 
 cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int cols,

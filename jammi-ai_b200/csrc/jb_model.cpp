@@ -539,12 +539,11 @@ size_t esz(int dt) { return dt == JB_DT_F32 ? 4 : 2; }
 // Sizes of every workspace buffer for (batch, seq); shared by the allocator
 // and jb_estimate_batch_bytes.
 struct WsPlan {
-  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, head_t, lora_t, pixels, patches, patch_out,
-      pooled;
+  size_t ids, lens, cu, total, out, x, qkv, hf, aq, as, rowmax, head_t, lora_t, pixels, patches,
+      patch_out, pooled;
   size_t sum() const {
-    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + head_t + lora_t + pixels +
-           patches + patch_out +
-           pooled;
+    return ids + lens + cu + total + out + 4 * x + qkv + hf + aq + as + rowmax + head_t + lora_t +
+           pixels + patches + patch_out + pooled;
   }
 };
 size_t round_up(size_t v) { return (v + 255) & ~size_t(255); }
@@ -567,6 +566,7 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
   if (m->format == JB_FMT_INT8) {
     p.aq = round_up(T * std::max(H, F));
     p.as = round_up(T * 4);
+    p.rowmax = round_up(T * 4);
   }
   if (m->family == JB_FAMILY_CLIP_TEXT) p.pooled = round_up(B * H * e);
   if (m->family == JB_FAMILY_CLIP_VISION) {
@@ -625,6 +625,7 @@ void ensure_workspace(jb_model* m, int batch, int seq) {
   ws.hf = take(p.hf);
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
+  ws.rowmax = static_cast<unsigned int*>(take(p.rowmax));
   ws.head_t = static_cast<float*>(take(p.head_t));
   ws.lora_t = take(p.lora_t);
   ws.pixels = static_cast<float*>(take(p.pixels));
@@ -660,6 +661,7 @@ Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq)
   ws.hf = take(p.hf);
   ws.aq = static_cast<int8_t*>(take(p.aq));
   ws.as = static_cast<float*>(take(p.as));
+  ws.rowmax = static_cast<unsigned int*>(take(p.rowmax));
   ws.head_t = static_cast<float*>(take(p.head_t));
   ws.lora_t = take(p.lora_t);
   ws.pixels = static_cast<float*>(take(p.pixels));
@@ -1040,8 +1042,10 @@ void check_device_flag(jb_model* m, cudaStream_t s) {
 
 namespace {
 void run_linear(jb_model* m, const Linear& L, const void* A, const float* a_scale, int Mcap,
-                const int* dM, void* C, int c_dtype, int epi, const void* resid, cudaStream_t s) {
+                const int* dM, void* C, int c_dtype, int epi, const void* resid, cudaStream_t s,
+                unsigned int* row_max = nullptr) {
   GemmArgs g;
+  g.row_max = row_max;
   g.A = A;
   g.W = L.w;
   g.ab_dtype = L.dtype;
@@ -1066,8 +1070,10 @@ void run_linear(jb_model* m, const Linear& L, const void* A, const float* a_scal
   }
 }
 void run_ln(jb_model* m, const void* x, const void* resid, const float* g, const float* b, void* y, int8_t* yq,
-            float* ys, int dtype, int rows, const int* drows, int cols, float eps, cudaStream_t s) {
+            float* ys, int dtype, int rows, const int* drows, int cols, float eps, cudaStream_t s,
+            unsigned int* zero_rows = nullptr) {
   LnArgs a;
+  a.zero_rows = zero_rows;
   a.x = x;
   a.resid = resid;
   a.gamma = g;
@@ -1208,20 +1214,22 @@ void bert_forward_device(jb_model* m, const uint32_t* d_ids, const uint32_t* d_l
       run_linear(m, w.o, q8 ? ws.aq : ws.ctx, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x, s);
       if (lw) lora(lw->a_o, lw->b_o, ws.ctx, ws.y);
       run_ln(m, ws.y, nullptr, w.ln1_g, w.ln1_b, ws.x1, q8 ? ws.aq : nullptr, q8 ? ws.as : nullptr, act,
-             Mcap, ws.total, H, m->eps, s);
+             Mcap, ws.total, H, m->eps, s, q8 ? ws.rowmax : nullptr);
       // BertIntermediate (bert.rs:187-190): gelu_erf(dense(x1)).  int8: the
       // GELU runs in the quantiser that FFN2's input needs anyway, on the bf16
-      // dense output (the reference's bf16 order: Linear -> bf16 -> gelu).
+      // dense output (the reference's bf16 order: Linear -> bf16 -> gelu);
+      // the dense's epilogue records each row's largest output (rows zeroed
+      // by the LayerNorm above), which fixes the row's scale in advance.
       const bool lora1 = lw && lw->a_1.w;  // the adapter adds before the activation
       run_linear(m, w.ffn1, q8 ? ws.aq : ws.x1, ws.as, Mcap, ws.total, ws.hf, act,
-                 (q8 || lora1) ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s);
+                 (q8 || lora1) ? JB_EPI_NONE : JB_EPI_GELU, nullptr, s, q8 ? ws.rowmax : nullptr);
       if (lora1) {
         lora(lw->a_1, lw->b_1, ws.x1, ws.hf);
         PROF_MEM_CALL(launch_gelu_rows(ws.hf, act, Mcap, ws.total, m->ffn, s), "gelu");
       }
       if (q8)
-        PROF_MEM_CALL(launch_quantize_rows(ws.hf, act, ws.aq, ws.as, Mcap, ws.total, m->ffn, s,
-                                           JB_EPI_GELU),
+        PROF_MEM_CALL(launch_gelu_quantize_rowmax(ws.hf, ws.rowmax, ws.aq, ws.as, Mcap, ws.total,
+                                                  m->ffn, s),
                       "quantize");
       // BertOutput (bert.rs:199-202): LN(dense(h) + x1)
       run_linear(m, w.ffn2, q8 ? ws.aq : ws.hf, ws.as, Mcap, ws.total, ws.y, act, JB_EPI_RESIDUAL, ws.x1, s);

@@ -83,6 +83,7 @@ struct Workspace {
   void *x = nullptr, *x1 = nullptr, *y = nullptr, *qkv = nullptr, *ctx = nullptr, *hf = nullptr;
   int8_t* aq = nullptr;
   float* as = nullptr;
+  unsigned int* rowmax = nullptr;  // int8: each row's largest FFN1 output (f32 bits)
   // vision
   float* head_t = nullptr;  // projection head: x A^T, [batch, rank] f32
   void* lora_t = nullptr;   // LoRA: x A^T, [rows, lora_width] in the activation dtype
