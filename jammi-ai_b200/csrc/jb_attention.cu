@@ -328,17 +328,18 @@ __global__ void __launch_bounds__(kFaThreads, 4)
 //           buffer, then each key block's K and V into a 4-stage ring.
 //   warps 1, 2 (MMA, one per slot): S = Q K_j^T (kind::f16, M = 128, N = the block's
 //           keys rounded up to 16, four K = 16 steps) into the slot's TMEM
-//           columns [0, 128); once the softmax has written P_j (bf16 pairs,
-//           columns [192, 256)), O (+)= P_j V_j with A = P from TMEM and B =
-//           V_j MN-major straight from its TMA tile, into columns [128, 192),
-//           and S_{j+1} right behind it.  One issuing thread per slot, so
-//           the two slots' MMAs are issued side by side.
+//           columns [0, 128), S_{j+1} as soon as the softmax has read S_j
+//           (before it computes P_j, so the next S is ready when it ends);
+//           once P_j is written (bf16 pairs, columns [192, 256)), O (+)=
+//           P_j V_j with A = P from TMEM and B = V_j MN-major straight from
+//           its TMA tile, into columns [128, 192).  One issuing thread per
+//           slot, so the two slots' MMAs are issued side by side.
 //   warps 3-10 and 11-18 (softmax, one group per slot; items alternate
 //           slots): warp w reads TMEM lanes 32 (w % 4) .. + 31, and the two
 //           warps of a group on the same lane quarter split each row's key
 //           chunks (even / odd 16-key chunks), so two threads serve a query
 //           row and exchange their partial maxima and sums through shared
-//           memory under a 64-thread named barrier.  Per key block a thread
+//           memory (an mbarrier of two arrivals per exchange).  Per key block a thread
 //           reads its chunks of S twice, two 16-key chunks at a time (once
 //           for the maximum, once for the exponentials), masks keys past the
 //           row's end (and
@@ -347,8 +348,9 @@ __global__ void __launch_bounds__(kFaThreads, 4)
 //           reference maximum m: the first block's maximum, raised only when
 //           a later block exceeds it by more than 8 (2^8: p stays far inside
 //           bf16 and f32), the row of O in TMEM and the running sum rescaled
-//           then (lazy rescaling).  P goes to TMEM as bf16 pairs.  After the
-//           last block, O / sum is stored.
+//           then (lazy rescaling; P_{j-1} V is waited for before O or P is
+//           touched).  P goes to TMEM as bf16 pairs.  After the last block,
+//           O / sum is stored.
 //           The group also zeroes V rows past the row's end in the block's
 //           tile (other rows' values: 0 * V must stay 0).
 // Every wait is bounded; on a timeout each role stops, the TMA and MMA
@@ -410,24 +412,28 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const uint32_t sKV0 = base + 2 * kAtQBytes;                  // [4][K 16 KB | V 16 KB]
   uint8_t* meta = smem_raw + (sKV0 + kAtStages * 2 * kAtKBytes - raw);
   const uint32_t bars = smem_u32(meta);
-  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] (unused 2)
-  // k_full[4] v_full[4] kv_empty[4] spare[2]
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] s_used[2]
+  // k_full[4] v_full[4] kv_empty[4] spare[2] pair[8][2]
   auto qfull = [&](int s) { return bars + 8u * (0 + s); };
   auto qempty = [&](int s) { return bars + 8u * (2 + s); };
   auto sfull = [&](int s) { return bars + 8u * (4 + s); };
   auto pfull = [&](int s) { return bars + 8u * (6 + s); };
   auto ofull = [&](int s) { return bars + 8u * (8 + s); };
+  auto sused = [&](int s) { return bars + 8u * (10 + s); };  // the softmax has read S_j
   auto kfull = [&](int st) { return bars + 8u * (12 + st); };
   auto vfull = [&](int st) { return bars + 8u * (16 + st); };
   auto kvempty = [&](int st) { return bars + 8u * (20 + st); };
   const uint32_t spare = bars + 8u * 24;  // [2], one per MMA warp
-  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(meta + 8 * 26);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 26 + 4);
-  volatile AtItem* ring = reinterpret_cast<volatile AtItem*>(meta + 256);  // [4]
+  // the two warps of a row meet here to exchange maxima and sums: [2 g][4 q]
+  auto pairbar = [&](int g, int q) { return bars + 8u * (26 + 4 * g + q); };
+  uint32_t* tslot_ptr = reinterpret_cast<uint32_t*>(meta + 8 * 34);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 8 * 34 + 4);
+  volatile AtItem* ring = reinterpret_cast<volatile AtItem*>(meta + 384);  // [4]
   // the two threads of a row exchange their partial maxima (per key block,
   // double-buffered by block parity) and sums (per item) here
   volatile float* xmax = reinterpret_cast<volatile float*>(meta + 512);       // [2 g][2 par][4 q][2 half][32]
   volatile float* xsum = xmax + 2 * 2 * 4 * 2 * 32;                            // [2 g][4 q][2 half][32]
+  static_assert(8 * 34 + 8 <= 384 && 384 + 4 * sizeof(AtItem) <= 512, "meta layout");
   auto sK = [&](int st) { return sKV0 + static_cast<uint32_t>(st) * 2 * kAtKBytes; };
   auto sV = [&](int st) { return sKV0 + static_cast<uint32_t>(st) * 2 * kAtKBytes + kAtKBytes; };
 
@@ -438,6 +444,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(sfull(s), 1);
       mbar_init(pfull(s), kAtGroupWarps);
       mbar_init(ofull(s), 1);
+      mbar_init(sused(s), kAtGroupWarps);
     }
     for (int st = 0; st < kAtStages; ++st) {
       mbar_init(kfull(st), 1);
@@ -446,6 +453,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
     mbar_init(spare, 1);
     mbar_init(spare + 8u, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(pairbar(i >> 2, i & 3), 2);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -554,7 +562,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const uint32_t slot = tbase + static_cast<uint32_t>(sl * kAtSlotCols);
       const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
       const uint32_t idesc_pv = idesc_bf16_f32(kAtQ, 64) | (1u << 16);  // B (V) MN-major
-      int bs = 0;  // key blocks done in this slot
+      int bs = 0;  // key blocks done in this slot (P V issued)
+      int su = 0;  // S issued in this slot (each but the latest released by s_used before the next)
       bool ok = true;
       for (int ti = 0; ok; ++ti) {
         const int k = 2 * ti + sl;
@@ -564,35 +573,48 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
         if (ring[k & 3].idx < 0) break;  // the walk is over
         const int n = ring[k & 3].n, b0 = ring[k & 3].b0, nb = ring[k & 3].nb;
-        // S_0 goes in as soon as the previous item's last P is written (its
-        // S columns are read by then); P_0 V, which overwrites O, waits for
-        // P_0, which the softmax writes only after its epilogue read O
+        // S_j overwrites S_{j-1} as soon as the softmax has read it (s_used),
+        // which is before it computes P_{j-1}: S_j is issued while those
+        // exponentials run, and P_{j-1} V once P_{j-1} is written.  The
+        // softmax waits for P_{j-1} V before it writes P_j or touches O (and
+        // P_0 V, which overwrites O, follows P_0, written after the previous
+        // item's epilogue read O).
+        auto issue_s = [&](int j) -> bool {
+          const int b = b0 + j, st = b % kAtStages;
+          const int kn = min(kAtKB, n - kAtKB * j), kpad = (kn + 15) & ~15;
+          if ((su > 0 && !mbar_wait(sused(sl), (su - 1) & 1, abort_flag)) ||
+              !mbar_wait(kfull(st), (b / kAtStages) & 1, abort_flag))
+            return false;
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16_f32(kAtQ, kpad);
+          // a 32-byte K step advances each descriptor's start address by 2
+          const uint64_t dq = umma_desc_sw128(sQ), dk = umma_desc_sw128(sK(st));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_bf16(slot, dq + 2u * kk, dk + 2u * kk, idesc, kk != 0);
+          mma_commit(sfull(sl));
+          if (j == nb - 1) mma_commit(qempty(sl));  // Q read by the item's last S
+          ++su;
+          return true;
+        };
+        if (!issue_s(0)) {
+          ok = false;
+          break;
+        }
         for (int j = 0; j < nb && ok; ++j, ++bs) {
           const int b = b0 + j, st = b % kAtStages;
           const int kn = min(kAtKB, n - kAtKB * j), kpad = (kn + 15) & ~15;
-          // S_j overwrites S_{j-1}, which the softmax read before it released
-          // P_{j-1}; P_{j-1} V (issued before) is untouched
-          if (!mbar_wait(kfull(st), (b / kAtStages) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t idesc = idesc_bf16_f32(kAtQ, kpad);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16(slot, umma_desc_sw128(sQ + 32u * kk), umma_desc_sw128(sK(st) + 32u * kk), idesc, kk != 0);
-          mma_commit(sfull(sl));
-          if (j == nb - 1) mma_commit(qempty(sl));  // Q read by the item's last S
-          if (!mbar_wait(pfull(sl), bs & 1, abort_flag) ||
+          if ((j + 1 < nb && !issue_s(j + 1)) || !mbar_wait(pfull(sl), bs & 1, abort_flag) ||
               !mbar_wait(vfull(st), (b / kAtStages) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // 16 keys of V (16 rows of 128 bytes) advance the start address by 128
+          const uint64_t dv = umma_desc_sw128(sV(st));
 #pragma unroll 1
           for (int c = 0; c < (kpad >> 4); ++c)
-            mma_bf16_ta(slot + kAtOCol, slot + kAtPCol + 8u * c, umma_desc_sw128(sV(st) + 2048u * c),
-                        idesc_pv, (j > 0 || c > 0) ? 1u : 0u);
+            mma_bf16_ta(slot + kAtOCol, slot + kAtPCol + 8u * c, dv + 128u * c, idesc_pv,
+                        (j > 0 || c > 0) ? 1u : 0u);
           mma_commit(ofull(sl));
           mma_commit(kvempty(st));
         }
@@ -611,11 +633,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     const int half = gw >> 2;                           // this thread's key chunks: t % 2 == half
     const int gtid = tid - 96 - g * 32 * kAtGroupWarps;  // 0 .. 255
     const int r = 32 * quarter + lane;                  // query row of the item
-    const uint32_t pair_bar = 1 + g * 4 + quarter;     // named barrier of the two warps of a row
     const uint32_t trow = tbase + static_cast<uint32_t>(g * kAtSlotCols) + (static_cast<uint32_t>(32 * quarter) << 16);
     auto xm = [&](int par, int hf) { return xmax + (((g * 2 + par) * 4 + quarter) * 2 + hf) * 32 + lane; };
     auto xs = [&](int hf) { return xsum + ((g * 4 + quarter) * 2 + hf) * 32 + lane; };
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
+    // the row's other warp has written its half too (bounded: a partner that
+    // gave up cannot strand this warp)
+    int pairs = 0;
+    auto pair_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pairbar(g, quarter));
+      return warp_wait(pairbar(g, quarter), (pairs++) & 1, abort_flag);
+    };
     int bs = 0;  // key blocks done in this slot
     bool ok = true;
     for (int ti = 0; ok; ++ti) {
@@ -650,13 +678,22 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           break;
         }
         tc_fence_after();
+        // this block's S read (all of it, by this warp): S_{j+1} may go in
+        bool s_released = false;
+        auto release_s = [&]() {
+          if (!s_released) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sused(g));
+            s_released = true;
+          }
+        };
+        // this thread's chunks: t = half + 2u, u < mine; read in pairs (32
+        // values live), once for the maximum and once for the exponentials
+        const int chunks = kpad >> 4, mine = (chunks - half + 1) >> 1;
+        const int lim = kmax - kbase;  // this row's valid columns in the block
+        float m = -INFINITY;
         if (wactive) {
-          // this thread's chunks: t = half + 2u, u < mine; read in pairs
-          // (32 values live), once for the maximum and once for the
-          // exponentials
-          const int chunks = kpad >> 4, mine = (chunks - half + 1) >> 1;
-          const int lim = kmax - kbase;  // this row's valid columns in the block
-          float m = -INFINITY;
 #pragma unroll
           for (int u0 = 0; u0 < 4; u0 += 2) {
             if (u0 < mine) {
@@ -685,18 +722,29 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             }
           }
           *xm(bs & 1, half) = m;
-          pair_sync();
+          if (!pair_sync()) {
+            ok = false;
+            break;
+          }
           m = fmaxf(m, *xm(bs & 1, half ^ 1));
+        }
+        // P_{j-1} V is complete before this block writes P or touches O
+        if (jb > 0) {
+          if (!warp_wait(ofull(g), (bs - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (wactive) {
           const float mb = m * scale_log2;
           if (jb == 0) {
             mref = mb == -INFINITY ? 0.f : mb;  // a row with no key here keeps p = 0
           } else {
             // lazy rescaling: a row whose block maximum exceeds its reference
-            // by more than the threshold moves O (complete through block
-            // jb - 1: a commit tracks every earlier MMA, so S_jb's completion
-            // implies P_{jb-1} V's) and the sum to the new reference (which
-            // also makes P_{jb-1} free to overwrite); each thread of the row rescales its half of
-            // O (columns 32 half .. + 31) and its partial sum.  TMEM loads and
+            // by more than the threshold moves O and the sum to the new
+            // reference; each thread of the row rescales its half of O
+            // (columns 32 half .. + 31) and its partial sum.  TMEM loads and
             // stores are warp-collective: the whole warp runs the loop, with
             // alpha = 1 on other rows (both warps of a row decide alike).
             const bool up = mb > mref + kAtRescale;
@@ -725,6 +773,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               for (int uu = 0; uu < 2; ++uu)
                 if (u0 + uu < mine) tmem_ld_32x32b_x16_at(trow + 16 * (2 * (u0 + uu) + half), v[uu]);
               tmem_wait_ld();
+              if (u0 + 2 >= mine) release_s();  // the last of this thread's S reads
 #pragma unroll
               for (int uu = 0; uu < 2; ++uu) {
                 if (u0 + uu < mine) {
@@ -752,6 +801,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           l += lsum0 + lsum1;
           tmem_wait_st();
         }
+        release_s();  // warps without reads in this pass
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(pfull(g));
@@ -761,7 +811,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       tc_fence_after();
       if (wactive) {
         *xs(half) = l;
-        pair_sync();
+        if (!pair_sync()) break;
         const float inv_l = 1.f / (l + *xs(half ^ 1));
         uint32_t o[32];
         tmem_ld_32x32b_x32(trow + kAtOCol + 32 * half, o);
