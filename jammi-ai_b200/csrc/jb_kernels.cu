@@ -107,6 +107,7 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
   const float var = warp_sum(ss) / static_cast<float>(cols);
   const float rstd = 1.0f / sqrtf(var + eps);
   float amax = 0.f;
+  const float nm = -mean * rstd;  // (x - mean) rstd = x rstd - mean rstd, one packed fma per pair
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int vi = lane + i * 32;
@@ -117,17 +118,19 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
 #pragma unroll
       for (int q = 0; q < VN / 4; ++q) {
         const float4 g = g4[q], b = b4[q];
-        o[4 * q + 0] = (v[i * VN + 4 * q + 0] - mean) * rstd * g.x + b.x;
-        o[4 * q + 1] = (v[i * VN + 4 * q + 1] - mean) * rstd * g.y + b.y;
-        o[4 * q + 2] = (v[i * VN + 4 * q + 2] - mean) * rstd * g.z + b.z;
-        o[4 * q + 3] = (v[i * VN + 4 * q + 3] - mean) * rstd * g.w + b.w;
+        const float2 t01 = __ffma2_rn(make_float2(v[i * VN + 4 * q + 0], v[i * VN + 4 * q + 1]), f2(rstd), f2(nm));
+        const float2 t23 = __ffma2_rn(make_float2(v[i * VN + 4 * q + 2], v[i * VN + 4 * q + 3]), f2(rstd), f2(nm));
+        const float2 o01 = __ffma2_rn(t01, make_float2(g.x, g.y), make_float2(b.x, b.y));
+        const float2 o23 = __ffma2_rn(t23, make_float2(g.z, g.w), make_float2(b.z, b.w));
+        o[4 * q + 0] = o01.x; o[4 * q + 1] = o01.y; o[4 * q + 2] = o23.x; o[4 * q + 3] = o23.y;
       }
+      // stored once; the quantiser reads the stored (rounded) values back
+      // from the packed bits, not through a second conversion
+      const uint4 packed = Vec<T>::pack(o);
+      Vec<T>::unpack(packed, v + i * VN);
+      *reinterpret_cast<uint4*>(yrow + vi * VN) = packed;
 #pragma unroll
-      for (int e = 0; e < VN; ++e) {
-        v[i * VN + e] = Vec<T>::rounded(o[e]);
-        amax = fmaxf(amax, fabsf(v[i * VN + e]));
-      }
-      Vec<T>::store(yrow + vi * VN, o);
+      for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[i * VN + e]));
     }
   }
   if (qrow) {
@@ -420,7 +423,7 @@ __global__ void gelu_table_kernel() {
   g_gelu_bf16[u] = static_cast<__nv_bfloat16_raw>(b).x;
 }
 
-constexpr int kGeluQThreads = 1024;
+constexpr int kGeluQThreads = 512;
 constexpr int kGeluTableBytes = 65536 * 2;
 // A row whose largest x reaches this has amax = GELU(largest x): GELU(0.5) =
 // 0.35 exceeds |GELU| anywhere on the negatives (at most 0.17, near -0.75).
@@ -433,12 +436,15 @@ __device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* tab, uint32_t w
 }
 
 // Per-token int8 of bf16(GELU(x)), x bf16 [rows, cols] (cols a multiple of
-// 8): one warp per row, persistent (one 1024-thread block per SM with the
+// 8): one warp per row, persistent (one 512-thread block per SM with the
 // table in shared memory).  row_max[row] holds the row's largest x (f32
 // bits, 0 when none is positive).  At >= kGeluRowMaxFast the row's amax is a
-// single lookup and the row is read once: 16-byte loads, four per lane in
-// flight, lookup, quantise, 8-byte stores.  Other rows first take the amax
-// over the row (a second read, mostly from L2).
+// single lookup and the row is read once; each lane holds its MAXV 16-byte
+// vectors of the row in registers and loads those of its next row while it
+// quantises the current one (rows of up to 12 vectors per lane), so a whole
+// row's loads are in flight behind the lookups.  Other rows first take the
+// amax over the held values.
+template <int MAXV>
 __global__ void __launch_bounds__(kGeluQThreads, 1)
     gelu_quantize_kernel(const bf16* __restrict__ x, const unsigned int* row_max, int8_t* q,
                          float* scale, int rows, const int* drows, int cols) {
@@ -453,9 +459,35 @@ __global__ void __launch_bounds__(kGeluQThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = drows ? min(*drows, rows) : rows;
   const int nvec = cols / 8;
-  for (int row = blockIdx.x * kWarps + warp; row < R; row += gridDim.x * kWarps) {
+  const int stride = gridDim.x * kWarps;
+  auto fetch = [&](int row, uint4 (&r)[MAXV]) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * cols);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+      if (lane + 32 * i < nvec) r[i] = __ldg(xr + lane + 32 * i);
+  };
+  // the next row's vectors fit beside the current ones up to 12 per lane
+  constexpr bool kPrefetch = MAXV <= 12;
+  uint4 cur[MAXV];
+  int row = blockIdx.x * kWarps + warp;
+  if (kPrefetch && row < R) fetch(row, cur);
+  for (; row < R; row += stride) {
     const float xm = __uint_as_float(row_max[row]);
+    uint4 nxt[kPrefetch ? MAXV : 1];
+    if constexpr (kPrefetch) {
+      if (row + stride < R) fetch(row + stride, nxt);
+    } else {
+      fetch(row, cur);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + 32 * i < nvec) {
+        cur[i].x = gelu_lookup2(tab, cur[i].x);
+        cur[i].y = gelu_lookup2(tab, cur[i].y);
+        cur[i].z = gelu_lookup2(tab, cur[i].z);
+        cur[i].w = gelu_lookup2(tab, cur[i].w);
+      }
+    }
     float amax;
     if (xm >= kGeluRowMaxFast) {
       amax = __uint_as_float(static_cast<uint32_t>(tab[__float_as_uint(xm) >> 16]) << 16);
@@ -463,37 +495,32 @@ __global__ void __launch_bounds__(kGeluQThreads, 1)
       // the largest |GELU| as bf16 magnitude bits (integer order of
       // non-negative bf16 bit patterns is their numeric order)
       uint32_t mx2 = 0;
-      for (int vi = lane; vi < nvec; vi += 32) {
-        const uint4 r = __ldg(xr + vi);
-        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.x) & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.y) & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.z) & 0x7FFF7FFFu);
-        mx2 = __vmaxu2(mx2, gelu_lookup2(tab, r.w) & 0x7FFF7FFFu);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        if (lane + 32 * i < nvec) {
+          mx2 = __vmaxu2(mx2, cur[i].x & 0x7FFF7FFFu);
+          mx2 = __vmaxu2(mx2, cur[i].y & 0x7FFF7FFFu);
+          mx2 = __vmaxu2(mx2, cur[i].z & 0x7FFF7FFFu);
+          mx2 = __vmaxu2(mx2, cur[i].w & 0x7FFF7FFFu);
+        }
       }
       amax = warp_max(fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u)));
     }
     const float inv = amax > 0.f ? 127.0f / amax : 0.f;
     uint2* qr = reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * cols);
-    for (int v0 = lane; v0 < nvec; v0 += 4 * 32) {
-      uint4 r[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (v0 + 32 * u < nvec) r[u] = __ldg(xr + v0 + 32 * u);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (v0 + 32 * u < nvec) {
-          uint4 g;
-          g.x = gelu_lookup2(tab, r[u].x);
-          g.y = gelu_lookup2(tab, r[u].y);
-          g.z = gelu_lookup2(tab, r[u].z);
-          g.w = gelu_lookup2(tab, r[u].w);
-          float v[8];
-          Vec<bf16>::unpack(g, v);
-          qr[v0 + 32 * u] = make_uint2(quant4(v[0], v[1], v[2], v[3], inv), quant4(v[4], v[5], v[6], v[7], inv));
-        }
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + 32 * i < nvec) {
+        float v[8];
+        Vec<bf16>::unpack(cur[i], v);
+        qr[lane + 32 * i] = make_uint2(quant4(v[0], v[1], v[2], v[3], inv), quant4(v[4], v[5], v[6], v[7], inv));
       }
     }
     if (lane == 0) scale[row] = amax / 127.0f;
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) cur[i] = nxt[i];
+    }
   }
 }
 
@@ -983,17 +1010,28 @@ namespace {
 std::mutex g_gelu_mu;
 bool g_gelu_ready[64] = {};
 
-cudaError_t launch_gelu_quantize(const bf16* x, const unsigned int* row_max, int8_t* q, float* scale,
-                                 int rows, const int* drows, int cols, cudaStream_t s) {
-  cudaError_t e = cudaFuncSetAttribute(gelu_quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kGeluTableBytes);
+template <int MAXV>
+cudaError_t launch_gelu_quantize_v(const bf16* x, const unsigned int* row_max, int8_t* q, float* scale,
+                                   int rows, const int* drows, int cols, cudaStream_t s) {
+  auto kern = gelu_quantize_kernel<MAXV>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGeluTableBytes);
   if (e != cudaSuccess) return e;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned need = blocks_for(rows, kGeluQThreads / 32);
   const unsigned grid = std::min<unsigned>(need, static_cast<unsigned>(num_sms(dev)));
-  gelu_quantize_kernel<<<grid, kGeluQThreads, kGeluTableBytes, s>>>(x, row_max, q, scale, rows, drows, cols);
+  kern<<<grid, kGeluQThreads, kGeluTableBytes, s>>>(x, row_max, q, scale, rows, drows, cols);
   return cudaGetLastError();
+}
+// Rows of up to 16 vectors per lane (4096 columns) held in registers.
+cudaError_t launch_gelu_quantize(const bf16* x, const unsigned int* row_max, int8_t* q, float* scale,
+                                 int rows, const int* drows, int cols, cudaStream_t s) {
+  const int per_lane = (cols / 8 + 31) / 32;
+  if (per_lane <= 4) return launch_gelu_quantize_v<4>(x, row_max, q, scale, rows, drows, cols, s);
+  if (per_lane <= 8) return launch_gelu_quantize_v<8>(x, row_max, q, scale, rows, drows, cols, s);
+  if (per_lane <= 12) return launch_gelu_quantize_v<12>(x, row_max, q, scale, rows, drows, cols, s);
+  if (per_lane <= 16) return launch_gelu_quantize_v<16>(x, row_max, q, scale, rows, drows, cols, s);
+  return cudaErrorInvalidValue;
 }
 }  // namespace
 
