@@ -482,6 +482,8 @@ typedef struct {
   double wait_seconds;           /* workers blocked on their device, summed */
   double worker_seconds_max;     /* the slowest worker's wall time */
   double worker_seconds_min;     /* the fastest worker's (max - min: the tail) */
+  double enqueue_seconds;        /* copies + forward enqueued (CUDA graph capture included), summed */
+  double setup_seconds;          /* staging allocation, summed (0 once a handle's staging fits) */
 } jb_generate_stats;
 jb_status jb_generate_embeddings(jb_model** models, int n_models, const uint32_t* ids,
                                  const uint64_t* offsets, int64_t rows,

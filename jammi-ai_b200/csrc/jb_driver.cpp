@@ -190,14 +190,8 @@ jb_status jb_run_chunks(int64_t rows, int* batch_size, jb_forward_cb forward, vo
 namespace {
 
 struct Slot {
-  uint32_t* h_ids = nullptr;
-  uint32_t* h_lens = nullptr;
-  float* h_out = nullptr;
-  uint32_t* d_ids = nullptr;
-  uint32_t* d_lens = nullptr;
-  float* d_out = nullptr;
-  cudaEvent_t done = nullptr;
-  std::vector<int64_t> rows;  // original row index of each output row, pending scatter
+  jb::DriverSlot* buf = nullptr;  // the handle's persistent staging
+  std::vector<int64_t> rows;      // original row index of each output row, pending scatter
 };
 
 struct Shared {
@@ -217,14 +211,16 @@ struct Shared {
   std::atomic<int64_t> d2h_bytes{0};
   std::mutex mu;
   // per-phase seconds summed over the workers, and each worker's wall time
-  double pack_s = 0, scatter_s = 0, wait_s = 0;
+  double pack_s = 0, scatter_s = 0, wait_s = 0, enqueue_s = 0, setup_s = 0;
   double worker_max = 0, worker_min = 0;
   int workers_done = 0;
-  void add_times(double pack, double scat, double wait, double wall) {
+  void add_times(double pack, double scat, double wait, double enq, double setup, double wall) {
     std::lock_guard<std::mutex> lk(mu);
     pack_s += pack;
     scatter_s += scat;
     wait_s += wait;
+    enqueue_s += enq;
+    setup_s += setup;
     worker_max = workers_done ? std::max(worker_max, wall) : wall;
     worker_min = workers_done ? std::min(worker_min, wall) : wall;
     ++workers_done;
@@ -247,52 +243,71 @@ int64_t row_len(const Shared& sh, int64_t r) {
 
 void scatter(Shared& sh, Slot& s) {
   for (size_t i = 0; i < s.rows.size(); ++i)
-    std::memcpy(sh.out + s.rows[i] * sh.H, s.h_out + i * sh.H, sizeof(float) * sh.H);
+    std::memcpy(sh.out + s.rows[i] * sh.H, s.buf->h_out + i * sh.H, sizeof(float) * sh.H);
   s.rows.clear();
 }
 
 using Clock = std::chrono::steady_clock;
 double since(Clock::time_point t) { return std::chrono::duration<double>(Clock::now() - t).count(); }
 
+// Sizes the handle's staging for batches of up to `rows` rows of up to
+// `seq` tokens and an output width of H; reallocates only when it grows.
+void ensure_stage(jb::DriverStage& st, int rows, int seq, int H) {
+  const size_t ids = size_t(rows) * seq, out = size_t(rows) * H;
+  if (!st.stream)
+    jb::check_cuda(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking), "stream");
+  if (ids <= st.ids_cap && size_t(rows) <= st.rows_cap && out <= st.out_cap) return;
+  jb::check_cuda(cudaStreamSynchronize(st.stream), "staging");
+  const size_t ids_cap = std::max(ids, st.ids_cap), rows_cap = std::max(size_t(rows), st.rows_cap),
+               out_cap = std::max(out, st.out_cap);
+  for (jb::DriverSlot& s : st.slot) {
+    for (void* p : {static_cast<void*>(s.h_ids), static_cast<void*>(s.h_lens), static_cast<void*>(s.h_out)})
+      if (p) cudaFreeHost(p);
+    for (void* p : {static_cast<void*>(s.d_ids), static_cast<void*>(s.d_lens), static_cast<void*>(s.d_out)})
+      if (p) cudaFree(p);
+    s.h_ids = s.h_lens = s.d_ids = s.d_lens = nullptr;
+    s.h_out = s.d_out = nullptr;
+  }
+  st.ids_cap = st.rows_cap = st.out_cap = 0;
+  for (jb::DriverSlot& s : st.slot) {
+    jb::check_cuda(cudaHostAlloc(&s.h_ids, ids_cap * 4, cudaHostAllocDefault), "pinned ids");
+    jb::check_cuda(cudaHostAlloc(&s.h_lens, rows_cap * 4, cudaHostAllocDefault), "pinned lens");
+    jb::check_cuda(cudaHostAlloc(&s.h_out, out_cap * 4, cudaHostAllocDefault), "pinned out");
+    jb::check_cuda(cudaMalloc(&s.d_ids, ids_cap * 4), "device ids");
+    jb::check_cuda(cudaMalloc(&s.d_lens, rows_cap * 4), "device lens");
+    jb::check_cuda(cudaMalloc(&s.d_out, out_cap * 4), "device out");
+    if (!s.done) jb::check_cuda(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "event");
+  }
+  st.ids_cap = ids_cap;
+  st.rows_cap = rows_cap;
+  st.out_cap = out_cap;
+}
+
 void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int max_seq) {
   const auto t_start = Clock::now();
-  double pack_s = 0, scatter_s = 0, wait_s = 0;
+  double pack_s = 0, scatter_s = 0, wait_s = 0, enqueue_s = 0, setup_s = 0;
   struct Report {  // the worker's times reach the stats on every exit path
     Shared& sh;
     const Clock::time_point& t0;
-    double &pack, &scat, &wait;
-    ~Report() { sh.add_times(pack, scat, wait, since(t0)); }
-  } report{sh, t_start, pack_s, scatter_s, wait_s};
+    double &pack, &scat, &wait, &enq, &setup;
+    ~Report() { sh.add_times(pack, scat, wait, enq, setup, since(t0)); }
+  } report{sh, t_start, pack_s, scatter_s, wait_s, enqueue_s, setup_s};
   try {
     jb::DeviceGuard g(m->device);
-    cudaStream_t stream;
-    jb::check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    std::lock_guard<std::mutex> job(m->drv_mu);  // one job at a time on a handle's staging
+    jb::DriverStage& stage = m->drv;
+    auto t = Clock::now();
+    ensure_stage(stage, batch_rows, max_seq, sh.H);
+    setup_s += since(t);
+    cudaStream_t stream = stage.stream;
     Slot slots[2];
-    const size_t cap_ids = static_cast<size_t>(batch_rows) * max_seq;
-    auto cleanup = [&]() {
-      cudaStreamSynchronize(stream);
-      for (Slot& s : slots) {
-        if (s.h_ids) cudaFreeHost(s.h_ids);
-        if (s.h_lens) cudaFreeHost(s.h_lens);
-        if (s.h_out) cudaFreeHost(s.h_out);
-        if (s.d_ids) cudaFree(s.d_ids);
-        if (s.d_lens) cudaFree(s.d_lens);
-        if (s.d_out) cudaFree(s.d_out);
-        if (s.done) cudaEventDestroy(s.done);
-      }
-      cudaStreamDestroy(stream);
-    };
-    try {
-      for (Slot& s : slots) {
-        jb::check_cuda(cudaHostAlloc(&s.h_ids, cap_ids * 4, cudaHostAllocDefault), "pinned ids");
-        jb::check_cuda(cudaHostAlloc(&s.h_lens, batch_rows * 4, cudaHostAllocDefault), "pinned lens");
-        jb::check_cuda(cudaHostAlloc(&s.h_out, size_t(batch_rows) * sh.H * 4, cudaHostAllocDefault),
-                       "pinned out");
-        jb::check_cuda(cudaMalloc(&s.d_ids, cap_ids * 4), "device ids");
-        jb::check_cuda(cudaMalloc(&s.d_lens, batch_rows * 4), "device lens");
-        jb::check_cuda(cudaMalloc(&s.d_out, size_t(batch_rows) * sh.H * 4), "device out");
-        jb::check_cuda(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "event");
-      }
+    for (int i = 0; i < 2; ++i) slots[i].buf = &stage.slot[i];
+    // a failed job leaves no copy in flight on the staging it hands back
+    struct Drain {
+      cudaStream_t s;
+      ~Drain() { cudaStreamSynchronize(s); }
+    } drain{stream};
+    {
       int bs = batch_rows;  // halves on OOM, like run_chunks
       // Admission: the handle's workspace for (bs, max_seq) must fit this
       // device's budget; halve until it does, then hold the reservation for
@@ -327,8 +342,9 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
         while (i < end && !sh.abort) {
           const int64_t len = std::min<int64_t>(bs, end - i);
           Slot& s = slots[k & 1];
-          auto t = Clock::now();
-          jb::check_cuda(cudaEventSynchronize(s.done), "slot wait");
+          jb::DriverSlot& sb = *s.buf;
+          t = Clock::now();
+          jb::check_cuda(cudaEventSynchronize(sb.done), "slot wait");
           wait_s += since(t);
           t = Clock::now();
           scatter(sh, s);
@@ -343,16 +359,18 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
           for (int64_t j = 0; j < len; ++j) {
             const int64_t r = order[i + j];
             const int64_t n = row_len(sh, r);
-            std::memcpy(s.h_ids + j * S, sh.ids + sh.offsets[r], n * 4);
-            if (n < S) std::memset(s.h_ids + j * S + n, 0, (S - n) * 4);
-            s.h_lens[j] = static_cast<uint32_t>(n);
+            std::memcpy(sb.h_ids + j * S, sh.ids + sh.offsets[r], n * 4);
+            if (n < S) std::memset(sb.h_ids + j * S + n, 0, (S - n) * 4);
+            sb.h_lens[j] = static_cast<uint32_t>(n);
             toks += n;
           }
           pack_s += since(t);
-          jb::check_cuda(cudaMemcpyAsync(s.d_ids, s.h_ids, size_t(len) * S * 4, cudaMemcpyHostToDevice, stream), "H2D");
-          jb::check_cuda(cudaMemcpyAsync(s.d_lens, s.h_lens, size_t(len) * 4, cudaMemcpyHostToDevice, stream), "H2D");
-          const jb_status st = jb_encode_text_device(m, s.d_ids, s.d_lens, static_cast<int>(len), S,
-                                                     sh.pooling, s.d_out, stream);
+          t = Clock::now();
+          jb::check_cuda(cudaMemcpyAsync(sb.d_ids, sb.h_ids, size_t(len) * S * 4, cudaMemcpyHostToDevice, stream), "H2D");
+          jb::check_cuda(cudaMemcpyAsync(sb.d_lens, sb.h_lens, size_t(len) * 4, cudaMemcpyHostToDevice, stream), "H2D");
+          const jb_status st = jb_encode_text_device(m, sb.d_ids, sb.d_lens, static_cast<int>(len), S,
+                                                     sh.pooling, sb.d_out, stream);
+          enqueue_s += since(t);
           if (st != JB_OK) {
             const std::string msg = jb_last_error();
             if (is_oom_message(msg.c_str()) && bs > 1) {
@@ -362,8 +380,8 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
             }
             jb::fail(st, msg);
           }
-          jb::check_cuda(cudaMemcpyAsync(s.h_out, s.d_out, size_t(len) * sh.H * 4, cudaMemcpyDeviceToHost, stream), "D2H");
-          jb::check_cuda(cudaEventRecord(s.done, stream), "event");
+          jb::check_cuda(cudaMemcpyAsync(sb.h_out, sb.d_out, size_t(len) * sh.H * 4, cudaMemcpyDeviceToHost, stream), "D2H");
+          jb::check_cuda(cudaEventRecord(sb.done, stream), "event");
           s.rows.assign(order.begin() + i, order.begin() + i + len);
           sh.tokens += toks;
           sh.h2d_bytes += static_cast<int64_t>(len) * (S + 1) * 4;
@@ -373,19 +391,15 @@ void worker(Shared& sh, jb_model* m, jb_scheduler* sched, int batch_rows, int ma
         }
       }
       for (Slot& s : slots) {
-        auto t = Clock::now();
-        jb::check_cuda(cudaEventSynchronize(s.done), "drain");
+        t = Clock::now();
+        jb::check_cuda(cudaEventSynchronize(s.buf->done), "drain");
         wait_s += since(t);
         t = Clock::now();
         scatter(sh, s);
         scatter_s += since(t);
       }
       jb::check_device_flag(m, stream);
-    } catch (...) {
-      cleanup();
-      throw;
     }
-    cleanup();
   } catch (const jb::Error& e) {
     sh.fail(e.status, e.msg);
   } catch (const std::exception& e) {
@@ -497,6 +511,8 @@ extern "C" jb_status jb_generate_embeddings(jb_model** models, int n_models, con
       stats->pack_seconds = sh.pack_s;
       stats->scatter_seconds = sh.scatter_s;
       stats->wait_seconds = sh.wait_s;
+      stats->enqueue_seconds = sh.enqueue_s;
+      stats->setup_seconds = sh.setup_s;
       stats->worker_seconds_max = sh.worker_max;
       stats->worker_seconds_min = sh.worker_min;
     }

@@ -581,6 +581,22 @@ WsPlan plan_workspace(const jb_model* m, int batch, int seq) {
 
 }  // namespace
 
+void free_driver_stage(DriverStage& st) {
+  if (st.stream) cudaStreamSynchronize(st.stream);
+  for (DriverSlot& s : st.slot) {
+    if (s.h_ids) cudaFreeHost(s.h_ids);
+    if (s.h_lens) cudaFreeHost(s.h_lens);
+    if (s.h_out) cudaFreeHost(s.h_out);
+    if (s.d_ids) cudaFree(s.d_ids);
+    if (s.d_lens) cudaFree(s.d_lens);
+    if (s.d_out) cudaFree(s.d_out);
+    if (s.done) cudaEventDestroy(s.done);
+    s = DriverSlot{};
+  }
+  if (st.stream) cudaStreamDestroy(st.stream);
+  st = DriverStage{};
+}
+
 size_t estimate_batch_bytes(const jb_model* m, int batch, int seq) {
   if (m->family == JB_FAMILY_CLIP_VISION) seq = m->tokens;
   return plan_workspace(m, batch, seq).sum();
@@ -731,6 +747,7 @@ void model_free(jb_model* m) {
     if (m->graph_in) cudaEventDestroy(m->graph_in);
     if (m->graph_out) cudaEventDestroy(m->graph_out);
     free_workspace(m->ws);
+    free_driver_stage(m->drv);
     if (m->img_buf) cudaFree(m->img_buf);
     for (void* p : m->weight_allocs) cudaFree(p);
     if (m->d_err) cudaFree(m->d_err);

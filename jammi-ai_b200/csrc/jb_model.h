@@ -102,6 +102,21 @@ struct GraphEntry {
   cudaGraphExec_t exec = nullptr;  // captured on the second call
   uint64_t last_use = 0;
 };
+// The multi-device driver's staging on one device, kept by the handle from
+// one jb_generate_embeddings call to the next (pinned allocations and their
+// release are slow and synchronise the device): a stream and two slots of
+// pinned ids / lengths / embeddings with their device copies.
+struct DriverSlot {
+  uint32_t *h_ids = nullptr, *h_lens = nullptr, *d_ids = nullptr, *d_lens = nullptr;
+  float *h_out = nullptr, *d_out = nullptr;
+  cudaEvent_t done = nullptr;
+};
+struct DriverStage {
+  cudaStream_t stream = nullptr;
+  DriverSlot slot[2];
+  size_t ids_cap = 0, rows_cap = 0, out_cap = 0;  // elements per slot
+};
+void free_driver_stage(DriverStage& st);
 }  // namespace jb
 
 struct jb_model {
@@ -151,6 +166,9 @@ struct jb_model {
   int* h_err = nullptr;  // pinned host copy of *d_err, read after each synchronous call
   jb::Workspace ws;
   std::mutex mu;
+  // driver staging (jb_generate_embeddings), held by one job at a time
+  std::mutex drv_mu;
+  jb::DriverStage drv;
   // CUDA-event timing of every launch (off unless enabled)
   bool prof_on = false;
   std::vector<jb::ProfRec> prof_recs;

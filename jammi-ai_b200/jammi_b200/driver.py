@@ -36,7 +36,8 @@ class GenerateStats(ctypes.Structure):
                 ("h2d_bytes", ctypes.c_int64), ("d2h_bytes", ctypes.c_int64),
                 ("prepare_seconds", ctypes.c_double), ("pack_seconds", ctypes.c_double),
                 ("scatter_seconds", ctypes.c_double), ("wait_seconds", ctypes.c_double),
-                ("worker_seconds_max", ctypes.c_double), ("worker_seconds_min", ctypes.c_double)]
+                ("worker_seconds_max", ctypes.c_double), ("worker_seconds_min", ctypes.c_double),
+                ("enqueue_seconds", ctypes.c_double), ("setup_seconds", ctypes.c_double)]
 
 
 FORWARD_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,

@@ -96,11 +96,16 @@ def test_generate_embeddings_two_devices(setup):
     one = Bert.from_weights(w, cfg, device=0, fmt="int8")
     ref, ref_valid, st1 = generate_embeddings([one], values, offsets, batch_rows=64)
     two = [one, Bert.from_weights(w, cfg, device=1, fmt="int8")]
-    out, validity, st2 = generate_embeddings(two, values, offsets, batch_rows=64)
-    assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)
-    assert st2["batches"] == st1["batches"] and st2["tokens"] == st1["tokens"]
-    print(f"1 device {st1['seconds']:.3f} s, 2 devices {st2['seconds']:.3f} s "
-          f"(workers {st2['worker_seconds_min']:.3f}-{st2['worker_seconds_max']:.3f} s)")
+    for call in range(3):  # widths run eagerly, then captured, then replayed
+        out, validity, st2 = generate_embeddings(two, values, offsets, batch_rows=64)
+        assert np.array_equal(out, ref) and np.array_equal(validity, ref_valid)
+        assert st2["batches"] == st1["batches"] and st2["tokens"] == st1["tokens"]
+        print(f"call {call}: 1 device {st1['seconds']:.3f} s, 2 devices {st2['seconds']:.3f} s "
+              f"(workers {st2['worker_seconds_min']:.3f}-{st2['worker_seconds_max']:.3f} s, "
+              f"enqueue {st2['enqueue_seconds']:.3f} s, wait {st2['wait_seconds']:.3f} s, "
+              f"setup {st2['setup_seconds']:.4f} s)")
+    # the handles keep their staging from one call to the next
+    assert st2["setup_seconds"] < 0.05
     for m in two:
         m.close()
 
