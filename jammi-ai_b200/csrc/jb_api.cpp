@@ -275,6 +275,10 @@ jb_status jb_forward_hidden_device(jb_model* m, const uint32_t* d_ids, const uin
   });
 }
 
+// Images per chunk of jb_encode_image's overlapped pixel copy (77 MB of f32
+// pixels at 224 x 224, about as long on the host link as its forward).
+constexpr int kImageChunk = 128;
+
 jb_status jb_encode_image(jb_model* m, const float* pixels, int batch, float* out, void* stream) {
   return guarded([&] {
     if (!m || m->family != JB_FAMILY_CLIP_VISION) jb::fail(JB_ERR_INVALID, "model is not a vision encoder");
@@ -286,11 +290,41 @@ jb_status jb_encode_image(jb_model* m, const float* pixels, int batch, float* ou
     cudaStream_t s = as_stream(stream);
     jb::ensure_workspace(m, batch, m->tokens);
     jb::Workspace& ws = m->ws;
-    const size_t px = size_t(batch) * 3 * m->image_size * m->image_size;
-    jb::check_cuda(cudaMemcpyAsync(ws.pixels, pixels, px * 4, cudaMemcpyHostToDevice, s), "H2D pixels");
-    jb::run_graphed(m, 1, batch, m->tokens, 0, s, [&](cudaStream_t gs) {
-      jb::clip_forward_device(m, ws.pixels, batch, ws.out, gs);
-    });
+    const size_t px = size_t(3) * m->image_size * m->image_size;  // floats per image
+    const int chunks = (batch + kImageChunk - 1) / kImageChunk;
+    if (chunks == 1) {
+      jb::check_cuda(cudaMemcpyAsync(ws.pixels, pixels, batch * px * 4, cudaMemcpyHostToDevice, s), "H2D pixels");
+      jb::run_graphed(m, 1, batch, m->tokens, 0, s, [&](cudaStream_t gs) {
+        jb::clip_forward_device(m, ws.pixels, batch, ws.out, gs);
+      });
+    } else {
+      // Chunk i's pixels go to their own part of the staging buffer on a copy
+      // stream while chunk i - 1's forward runs; images never interact, so
+      // each row's embedding is the one the whole-batch forward gives.  Each
+      // chunk keeps its own CUDA graph (kind 2 + i: its buffers' offsets).
+      if (!m->copy_stream)
+        jb::check_cuda(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking), "copy stream");
+      while (m->copy_ev.size() < static_cast<size_t>(chunks) + 1) {
+        cudaEvent_t e;
+        jb::check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "copy event");
+        m->copy_ev.push_back(e);
+      }
+      // the caller's earlier work on s may still read the staging buffer
+      jb::check_cuda(cudaEventRecord(m->copy_ev[0], s), "copy order");
+      jb::check_cuda(cudaStreamWaitEvent(m->copy_stream, m->copy_ev[0], 0), "copy order");
+      for (int i = 0; i < chunks; ++i) {
+        const int b0 = i * kImageChunk, nb = std::min(kImageChunk, batch - b0);
+        float* d_px = ws.pixels + b0 * px;
+        float* d_out = ws.out + size_t(b0) * m->embed_dim;
+        jb::check_cuda(cudaMemcpyAsync(d_px, pixels + b0 * px, nb * px * 4, cudaMemcpyHostToDevice,
+                                       m->copy_stream), "H2D pixels");
+        jb::check_cuda(cudaEventRecord(m->copy_ev[1 + i], m->copy_stream), "copy order");
+        jb::check_cuda(cudaStreamWaitEvent(s, m->copy_ev[1 + i], 0), "copy order");
+        jb::run_graphed(m, 2 + i, nb, m->tokens, 0, s, [&](cudaStream_t gs) {
+          jb::clip_forward_device(m, d_px, nb, d_out, gs);
+        });
+      }
+    }
     jb::check_cuda(cudaMemcpyAsync(out, ws.out, size_t(batch) * m->embed_dim * 4, cudaMemcpyDeviceToHost, s), "D2H");
     jb::check_device_flag(m, s);
   });

@@ -746,6 +746,8 @@ void model_free(jb_model* m) {
     if (m->graph_stream) cudaStreamDestroy(m->graph_stream);
     if (m->graph_in) cudaEventDestroy(m->graph_in);
     if (m->graph_out) cudaEventDestroy(m->graph_out);
+    if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
+    for (cudaEvent_t e : m->copy_ev) cudaEventDestroy(e);
     free_workspace(m->ws);
     free_driver_stage(m->drv);
     if (m->img_buf) cudaFree(m->img_buf);

@@ -179,6 +179,10 @@ struct jb_model {
   uint64_t graph_clock = 0;
   cudaStream_t graph_stream = nullptr;
   cudaEvent_t graph_in = nullptr, graph_out = nullptr;
+  // jb_encode_image's chunked H2D: a copy stream, an event ordering it after
+  // the caller's stream, and one event per chunk (grown on demand)
+  cudaStream_t copy_stream = nullptr;
+  std::vector<cudaEvent_t> copy_ev;
 };
 
 namespace jb {

@@ -286,6 +286,29 @@ def test_host_and_device_entry_points_agree():
     assert np.array_equal(model.encode(ids, lens), host)  # deterministic
 
 
+def test_image_chunked_copy_matches_device_entry_point():
+    """jb_encode_image copies a batch of more than 128 images in chunks, each
+    chunk's forward overlapping the next chunk's copy: every row equals the
+    whole-batch forward of jb_encode_image_device bit for bit, on the eager
+    first call, the capturing second call and a replaying third call."""
+    from jammi_b200 import OpenClipVisionTransformer
+    cfg = oc.ClipVisionConfig()
+    w = oc.random_clip_weights(cfg, seed=511)
+    model = OpenClipVisionTransformer.from_weights(w, cfg.to_open_clip_config(), device=0, fmt="bf16")
+    px = np.random.default_rng(512).standard_normal((300, 3, 224, 224)).astype(np.float32)
+    d_px = torch.from_numpy(px).cuda()
+    ref = torch.empty((300, model.info.output_dim), device="cuda")
+    model.forward_image_device(d_px, ref, stream=torch.cuda.current_stream())
+    model.sync(torch.cuda.current_stream())
+    ref = ref.cpu().numpy()
+    for _ in range(3):
+        assert np.array_equal(model.forward_image(px), ref)
+    # a batch of one chunk after the chunked ones (and the reverse order of sizes)
+    assert np.array_equal(model.forward_image(px[:100]), ref[:100])
+    assert np.array_equal(model.forward_image(px[:257]), ref[:257])
+    model.close()
+
+
 def test_sequence_too_long():
     from jammi_b200 import SequenceTooLong
     w, g = load_golden("tiny_bert_seeded.npz")
