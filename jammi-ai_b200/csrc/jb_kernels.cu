@@ -88,23 +88,24 @@ __device__ __forceinline__ void ln_finish(float (&v)[MAXV * Vec<T>::N], int nvec
                                           const float* gamma, const float* beta, float eps, T* yrow,
                                           int8_t* qrow, float* scale_out) {
   constexpr int VN = Vec<T>::N;
-  float s = 0.f;
+  // sums over column pairs in packed f32x2 (two partial sums per lane)
+  float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i)
     if (lane + i * 32 < nvec)
 #pragma unroll
-      for (int e = 0; e < VN; ++e) s += v[i * VN + e];
-  const float mean = warp_sum(s) / static_cast<float>(cols);
-  float ss = 0.f;
+      for (int e = 0; e < VN; e += 2) s2 = __fadd2_rn(s2, make_float2(v[i * VN + e], v[i * VN + e + 1]));
+  const float mean = warp_sum(s2.x + s2.y) / static_cast<float>(cols);
+  float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i)
     if (lane + i * 32 < nvec)
 #pragma unroll
-      for (int e = 0; e < VN; ++e) {
-        const float d = v[i * VN + e] - mean;
-        ss += d * d;
+      for (int e = 0; e < VN; e += 2) {
+        const float2 d = __fadd2_rn(make_float2(v[i * VN + e], v[i * VN + e + 1]), f2(-mean));
+        ss2 = __ffma2_rn(d, d, ss2);
       }
-  const float var = warp_sum(ss) / static_cast<float>(cols);
+  const float var = warp_sum(ss2.x + ss2.y) / static_cast<float>(cols);
   const float rstd = 1.0f / sqrtf(var + eps);
   float amax = 0.f;
   const float nm = -mean * rstd;  // (x - mean) rstd = x rstd - mean rstd, one packed fma per pair
