@@ -68,7 +68,7 @@ PAD_MULTIPLE = 32     # the driver pads each batch's width to a multiple of 32 (
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per GEMM launch,
 # averaged over one layer's four linears, from an ncu capture of this
 # workload (the capture's summary, command and date are in profiles/).
-GEMM_TRAFFIC = {"bert-base-int8-s256": (158.9e6, "2026-12-02",
+GEMM_TRAFFIC = {"bert-base-int8-s256": (160.0e6, "2026-12-02",
                                         "profiles/bert_base_int8_b256_s256_launches.md")}
 
 
