@@ -41,11 +41,13 @@ typedef enum {
   JB_ERR_NO_DEVICE = 7        /* require_gpu failed, crates/jammi-ai/src/model/backend/candle.rs:2168-2172 */
 } jb_status;
 
-/* Weight / compute format.  F32 and BF16 mirror ComputePrecision
+/* Weight / compute format.  F32, BF16 and F16 mirror ComputePrecision
  * (crates/jammi-numerics/src/precision.rs:36-51); INT8 is new: int8 weights
  * with per-output-channel scales and per-token int8 activations for the six
- * per-layer linears, bf16 everywhere else. */
-typedef enum { JB_FMT_F32 = 0, JB_FMT_BF16 = 1, JB_FMT_INT8 = 2 } jb_format;
+ * per-layer linears, bf16 everywhere else.  F16 is defined for the BERT and
+ * DistilBERT encoders (no LoRA adapters); other families answer
+ * JB_ERR_INVALID. */
+typedef enum { JB_FMT_F32 = 0, JB_FMT_BF16 = 1, JB_FMT_INT8 = 2, JB_FMT_F16 = 3 } jb_format;
 
 /* Pooling (crates/jammi-encoders/src/pooling.rs:14-30). */
 typedef enum {
@@ -198,7 +200,7 @@ jb_status jb_encode_image_device(jb_model* model, const float* d_pixels, int bat
 
 /* ── single ops (device pointers) ──────────────────────────────────────── */
 /* dtype codes for the op entry points */
-typedef enum { JB_DT_F32 = 0, JB_DT_BF16 = 1, JB_DT_S8 = 2, JB_DT_S32 = 3 } jb_dtype;
+typedef enum { JB_DT_F32 = 0, JB_DT_BF16 = 1, JB_DT_S8 = 2, JB_DT_S32 = 3, JB_DT_F16 = 4 } jb_dtype;
 
 /* Epilogues applied to acc (+ bias) before the store. */
 typedef enum {

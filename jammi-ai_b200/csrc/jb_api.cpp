@@ -449,9 +449,10 @@ jb_status jb_op_linear(const void* A, int a_dtype, const void* W, int w_dtype, c
                        const void* residual, void* C, int c_dtype, int M, int N, int K,
                        int epilogue, void* stream) {
   return guarded([&] {
-    if (a_dtype != w_dtype || (a_dtype != JB_DT_F32 && a_dtype != JB_DT_BF16))
-      jb::fail(JB_ERR_INVALID, "jb_op_linear: A and W must both be f32 or both bf16");
-    if (c_dtype != JB_DT_F32 && c_dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "jb_op_linear: C must be f32 or bf16");
+    if (a_dtype != w_dtype || (a_dtype != JB_DT_F32 && a_dtype != JB_DT_BF16 && a_dtype != JB_DT_F16))
+      jb::fail(JB_ERR_INVALID, "jb_op_linear: A and W must both be f32, both bf16 or both f16");
+    if (c_dtype != JB_DT_F32 && c_dtype != JB_DT_BF16 && c_dtype != JB_DT_F16)
+      jb::fail(JB_ERR_INVALID, "jb_op_linear: C must be f32, bf16 or f16");
     if (epilogue < JB_EPI_NONE || epilogue > JB_EPI_RESIDUAL) jb::fail(JB_ERR_INVALID, "unknown epilogue");
     if (!A || !W || !C || M < 0) jb::fail(JB_ERR_INVALID, "jb_op_linear: null buffer or negative M");
     jb::GemmArgs g;
@@ -537,7 +538,8 @@ jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamm
                           void* stream) {
   return guarded([&] {
     if (!x || !gamma || !beta || !y || rows < 0 || cols <= 0) jb::fail(JB_ERR_INVALID, "jb_op_layernorm: bad argument");
-    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16 && dtype != JB_DT_F16)
+      jb::fail(JB_ERR_INVALID, "dtype must be f32, bf16 or f16");
     jb::LnArgs a;
     a.x = x;
     a.resid = residual;
@@ -559,7 +561,8 @@ jb_status op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dt
   return guarded([&] {
     if (!qkv || !cu_seqlens || !ctx || batch < 0 || heads <= 0 || head_dim <= 0 || max_len < 0)
       jb::fail(JB_ERR_INVALID, "jb_op_attention: bad argument");
-    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16 && dtype != JB_DT_F16)
+      jb::fail(JB_ERR_INVALID, "dtype must be f32, bf16 or f16");
     std::string why;
     cudaError_t e = jb::launch_attention(qkv, cu_seqlens, ctx, dtype, batch, heads, head_dim, max_len,
                                          as_stream(stream), &why, rows, op_flag(current_device()), causal);
@@ -644,7 +647,8 @@ jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seql
   return guarded([&] {
     if (!hidden || !cu_seqlens || !out || batch < 0 || H <= 0) jb::fail(JB_ERR_INVALID, "jb_op_pool_normalize: bad argument");
     if (pooling < JB_POOL_MEAN || pooling > JB_POOL_WEIGHTED_MEAN) jb::fail(JB_ERR_INVALID, "unknown pooling");
-    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16) jb::fail(JB_ERR_INVALID, "dtype must be f32 or bf16");
+    if (dtype != JB_DT_F32 && dtype != JB_DT_BF16 && dtype != JB_DT_F16)
+      jb::fail(JB_ERR_INVALID, "dtype must be f32, bf16 or f16");
     jb::check_cuda(jb::launch_pool_normalize(hidden, dtype, cu_seqlens, out, batch, H, pooling, as_stream(stream)),
                    "jb_op_pool_normalize");
   });

@@ -66,6 +66,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// Two f32 values as an f16 pair (H16) or a bf16 pair.
+template <bool H16>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+  if constexpr (H16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    return pack_bf16(lo, hi);
+  }
+}
 // 64 rows x 8 chunks of 16 B; chunk index XOR (row & 7) avoids bank conflicts.
 __device__ __forceinline__ uint32_t swz(uint32_t tile, int row, int chunk) {
   return tile + row * 128 + ((chunk ^ (row & 7)) << 4);
@@ -399,6 +409,8 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16_at(uint32_t taddr, uint32_t* 
       : "r"(taddr));
 }
 
+// H16: Q, K, V, P and the context are f16 (else bf16).
+template <bool H16>
 __global__ void __launch_bounds__(kAtThreads, 1)
     attn_tc_kernel(const int* __restrict__ cu, bf16* __restrict__ ctx, int batch, int heads,
                    float scale_log2, const __grid_constant__ CUtensorMap tm, int* err,
@@ -561,7 +573,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const int sl = warp - 1;
       const uint32_t slot = tbase + static_cast<uint32_t>(sl * kAtSlotCols);
       const uint32_t sQ = sQ0 + static_cast<uint32_t>(sl) * kAtQBytes;
-      const uint32_t idesc_pv = idesc_bf16_f32(kAtQ, 64) | (1u << 16);  // B (V) MN-major
+      // B (V) MN-major
+      const uint32_t idesc_pv = (H16 ? idesc_f16_f32(kAtQ, 64) : idesc_bf16_f32(kAtQ, 64)) | (1u << 16);
       int bs = 0;  // key blocks done in this slot (P V issued)
       int su = 0;  // S issued in this slot (each but the latest released by s_used before the next)
       bool ok = true;
@@ -586,7 +599,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
               !mbar_wait(kfull(st), (b / kAtStages) & 1, abort_flag))
             return false;
           tc_fence_after();
-          const uint32_t idesc = idesc_bf16_f32(kAtQ, kpad);
+          const uint32_t idesc = H16 ? idesc_f16_f32(kAtQ, kpad) : idesc_bf16_f32(kAtQ, kpad);
           // a 32-byte K step advances each descriptor's start address by 2
           const uint64_t dq = umma_desc_sw128(sQ), dk = umma_desc_sw128(sK(st));
 #pragma unroll
@@ -791,7 +804,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
                     const float p0 = ex2_approx(z.x), p1 = ex2_approx(z.y);
                     lsum0 += p0;
                     lsum1 += p1;
-                    pk[e >> 1] = pack_bf16(p0, p1);
+                    pk[e >> 1] = pack16<H16>(p0, p1);
                   }
                   tmem_st_32x32b_x8(trow + kAtPCol + 8 * t, pk);
                 }
@@ -821,10 +834,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 wv;
-            wv.x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-            wv.y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-            wv.z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-            wv.w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
+            wv.x = pack16<H16>(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+            wv.y = pack16<H16>(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+            wv.z = pack16<H16>(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+            wv.w = pack16<H16>(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
             dst[q] = wv;
           }
         }
@@ -919,7 +932,7 @@ cudaError_t launch_simt(const void* qkv, const int* cu, void* ctx, int batch, in
 
 // 2-D map over qkv [rows, 3 * H] bf16 with one 64 x 64 box (128-byte rows,
 // 128-byte swizzle: the layout swz() reads).
-bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
+bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H, bool h16 = false) {
   static PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -934,7 +947,8 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(3) * H * 2};
   cuuint32_t box[2] = {64, 64};
   cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box,
+  return enc(map, h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+             const_cast<void*>(qkv), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -942,6 +956,7 @@ bool make_qkv_map(CUtensorMap* map, const void* qkv, int rows, int H) {
 std::atomic<int> g_attn_tc{1};  // jb_set_attention_tcgen05 (on by default)
 bool attn_tc_enabled() { return g_attn_tc.load(std::memory_order_relaxed) != 0; }
 
+template <bool H16>
 cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int batch, int heads,
                       float scale_log2, const CUtensorMap& tm, int* err, int causal,
                       unsigned int* work) {
@@ -950,11 +965,12 @@ cudaError_t launch_tc(int grid, cudaStream_t s, const int* cu, bf16* ctx, int ba
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
-    const cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_tc_kernel<H16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev].store(1, std::memory_order_release);
   }
-  attn_tc_kernel<<<grid, kAtThreads, kAtSmem, s>>>(cu, ctx, batch, heads, scale_log2, tm, err,
+  attn_tc_kernel<H16><<<grid, kAtThreads, kAtSmem, s>>>(cu, ctx, batch, heads, scale_log2, tm, err,
                                                     causal, work);
   return cudaGetLastError();
 }
@@ -994,12 +1010,13 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
     if (why) *why = "attention: batch and heads must be <= 65535";
     return cudaErrorInvalidValue;
   }
-  if (dtype == JB_DT_BF16 && head_dim == 64) {
+  const bool h16 = dtype == JB_DT_F16;
+  if ((dtype == JB_DT_BF16 || h16) && head_dim == 64) {
     dim3 grid((max_len + kFaRows - 1) / kFaRows, heads, batch);
     const float scale_log2 = 1.4426950408889634f / sqrtf(64.f);
     CUtensorMap tm;
     memset(&tm, 0, sizeof(tm));
-    const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64);
+    const bool tma = rows_cap > 0 && make_qkv_map(&tm, qkv, rows_cap, heads * 64, h16);
     if (tma && attn_tc_enabled()) {
       // every row on tcgen05: 128-query items, keys streamed in blocks of 128
       unsigned int* w = work ? reinterpret_cast<unsigned int*>(work) : shared_work_counter();
@@ -1015,8 +1032,16 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       const long long units = static_cast<long long>(batch) * heads;  // (row, head) pairs
       const int grid = static_cast<int>(std::max(1ll, std::min<long long>(units, sms > 0 ? sms : 148)));
-      return launch_tc(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm, err,
-                       causal, w);
+      return h16 ? launch_tc<true>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
+                                   err, causal, w)
+                 : launch_tc<false>(grid, s, cu, static_cast<bf16*>(ctx), batch, heads, scale_log2, tm,
+                                    err, causal, w);
+    }
+    if (h16) {
+      if (why)
+        *why = "attention(f16, head_dim 64): runs on the tcgen05 kernel only (a row capacity and "
+               "jb_set_attention_tcgen05(1))";
+      return cudaErrorInvalidValue;
     }
     const int skip_le = 0;
     auto kern = tma ? flash_attn_bf16_d64<true> : flash_attn_bf16_d64<false>;
@@ -1028,6 +1053,11 @@ cudaError_t launch_attention(const void* qkv, const int* cu, void* ctx, int dtyp
   }
   if (dtype == JB_DT_BF16)
     return launch_simt<bf16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why, causal);
+  if (h16) return launch_simt<f16>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why, causal);
+  if (dtype != JB_DT_F32) {
+    if (why) *why = "attention: unsupported dtype";
+    return cudaErrorInvalidValue;
+  }
   return launch_simt<float>(qkv, cu, ctx, batch, heads, head_dim, max_len, s, why, causal);
 }
 

@@ -6,12 +6,14 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace jb {
 
 using bf16 = __nv_bfloat16;
+using f16 = __half;
 
 // Bounded-wait budget for any device-side spin (ns of %globaltimer).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -19,9 +21,11 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
 template <> __device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<f16>(f16 v) { return __half2float(v); }
 template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
 template <> __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ f16 from_f<f16>(float v) { return __float2half_rn(v); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -320,10 +324,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 
 // Instruction descriptor: dense, K-major A and B, M = 128.
 //   bits 4-5 D format (1 = f32, 2 = s32); 7-9 A format; 10-12 B format
-//   (kind::f16: 1 = bf16; kind::i8: 1 = signed); 17-22 N>>3; 24-28 M>>4.
+//   (kind::f16: 0 = f16, 1 = bf16; kind::i8: 1 = signed); 17-22 N>>3; 24-28 M>>4.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {  // A, B f16 (format 0)
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |

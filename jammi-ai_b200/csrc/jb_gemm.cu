@@ -79,6 +79,7 @@ struct EpiParams {
   int K;
   int* err;
   unsigned int* row_max;
+  int h16;  // 16-bit operands, output and residual are f16 (else bf16)
 };
 
 // SIMT path: CUDA's erff / expf.
@@ -118,6 +119,19 @@ constexpr int kSwzShift = kSlots == 4 ? 1 : 2;
 constexpr int kUnitBytes = 32 * kUnitCols * 2;
 __device__ __forceinline__ uint32_t unit_slot(uint32_t buf, int row, int q) {
   return buf + row * (kUnitCols * 2) + ((q ^ ((row >> kSwzShift) & (kSlots - 1))) << 4);
+}
+// Two f32 values as one 16-bit pair (f16 or bf16), and back.
+__device__ __forceinline__ uint32_t pack16(float lo, float hi, bool h16) {
+  if (h16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+__device__ __forceinline__ float2 unpack16(uint32_t w, bool h16) {
+  if (h16) return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 template <int W>
 __device__ __forceinline__ void tmem_ld_unit(uint32_t taddr, uint32_t (&r)[W]) {
@@ -204,7 +218,7 @@ __device__ __forceinline__ void activation(int epi, float (&v)[W]) {
 // are whole row segments; the output is laid out in `buf` in the tensor
 // map's swizzled box layout and written by one TMA store (rows past the
 // map's extent are not written).
-template <bool S8>
+template <bool S8, bool H16>
 __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensorMap* tmC, int row0,
                                               int lane, int col0, const uint32_t (&r)[kUnitCols],
                                               const float* sb, const float* ss, float as,
@@ -224,10 +238,10 @@ __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensor
 #pragma unroll
     for (int q = 0; q < kSlots; ++q) {
       const uint4 raw = lds128(unit_slot(buf, lane, q));
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h[e]);
+        const float2 f = unpack16(w4[e], H16);
         v[8 * q + 2 * e] += f.x;
         v[8 * q + 2 * e + 1] += f.y;
       }
@@ -240,9 +254,10 @@ __device__ __forceinline__ void epi_unit_bf16(const EpiParams& p, const CUtensor
 #pragma unroll
   for (int q = 0; q < kSlots; ++q) {
     uint4 out;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+    out.x = pack16(v[8 * q + 0], v[8 * q + 1], H16);
+    out.y = pack16(v[8 * q + 2], v[8 * q + 3], H16);
+    out.z = pack16(v[8 * q + 4], v[8 * q + 5], H16);
+    out.w = pack16(v[8 * q + 6], v[8 * q + 7], H16);
     sts128(unit_slot(buf, lane, q), out);
   }
   fence_proxy_async_smem();
@@ -294,6 +309,17 @@ __device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
         c[j] = __float2bfloat16_rn(x);
       }
     }
+  } else if (p.c_dtype == JB_DT_F16) {
+    f16* c = static_cast<f16*>(p.C) + off;
+    const f16* rs = static_cast<const f16*>(p.resid) + roff;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      if (j < ncols) {
+        float x = v[j];
+        if (p.epi == JB_EPI_RESIDUAL) x += __half2float(rs[j]);
+        c[j] = __float2half_rn(x);
+      }
+    }
   } else {  // f32 output
     float* c = static_cast<float*>(p.C) + off;
     const float* rs = static_cast<const float*>(p.resid) + roff;
@@ -315,7 +341,9 @@ __device__ __forceinline__ void epi_unit(const EpiParams& p, int row, int col0,
   }
 }
 
-template <bool S8, int BN, int MAXST>
+// H16: 16-bit operands / output / residual are f16 (bf16 otherwise; int8
+// operands always write bf16).
+template <bool S8, int BN, int MAXST, bool H16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const EpiParams p) {
@@ -364,7 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
-    if (p.c_dtype == JB_DT_BF16) prefetch_tensormap(&tmC);
+    if (p.c_dtype == JB_DT_BF16 || p.c_dtype == JB_DT_F16) prefetch_tensormap(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -391,7 +419,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && kb_count > 0) {
-      constexpr uint32_t idesc = S8 ? idesc_s8_s32(kBM, BN) : idesc_bf16_f32(kBM, BN);
+      constexpr uint32_t idesc = S8 ? idesc_s8_s32(kBM, BN)
+                                    : (H16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN));
       int stage = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -432,7 +461,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int part = (warp - 2) >> 2;
     constexpr int kPartCols = BN / (kEpiWarps / 4);
     const uint32_t my_buf = chunks + static_cast<uint32_t>(etid >> 5) * kUnitBytes;
-    const bool fast_out = p.c_dtype == JB_DT_BF16;
+    const bool fast_out = p.c_dtype == JB_DT_BF16 || p.c_dtype == JB_DT_F16;
     const bool res_ahead = fast_out && p.epi == JB_EPI_RESIDUAL;
     // Per-column parameters of a tile: thread etid < BN owns column etid.
     auto load_params = [&](int t, float& b, float& sc) {
@@ -498,7 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           load_resid_unit(p, row0, lane, M, col0 + kUnitCols, rnext);
         tmem_wait_ld();
         if (fast(c))
-          epi_unit_bf16<S8>(p, &tmC, row0, lane, col0, r, pb + c, ps + c, as, my_buf, rres, vmax);
+          epi_unit_bf16<S8, H16>(p, &tmC, row0, lane, col0, r, pb + c, ps + c, as, my_buf, rres, vmax);
         else if (row0 + lane < M)
           epi_unit<S8>(p, row0 + lane, col0, r, pb + c, ps + c, as, vmax);
 #pragma unroll
@@ -608,7 +637,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // 2-D K-major map over [rows, k_elems] with a (128-byte x box_rows) box.
-bool make_map(CUtensorMap* map, const void* ptr, bool s8, int rows, int k_elems, int box_rows) {
+bool make_map(CUtensorMap* map, const void* ptr, bool s8, bool h16, int rows, int k_elems,
+              int box_rows) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   const int esz = s8 ? 1 : 2;
@@ -616,41 +646,46 @@ bool make_map(CUtensorMap* map, const void* ptr, bool s8, int rows, int k_elems,
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(k_elems) * esz};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytes / esz), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+  const CUtensorMapDataType dt = s8    ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : (h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  CUresult r = enc(map, dt, 2,
                    const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-// Store map over a bf16 output [rows, cols] with row stride ld elements: one
+// Store map over a 16-bit output [rows, cols] with row stride ld elements: one
 // epilogue unit (32 rows x kUnitCols columns) per box, swizzled to match
 // unit_slot (64-byte rows: SWIZZLE_64B; 32-byte rows: SWIZZLE_32B).
-bool make_store_map(CUtensorMap* map, void* ptr, int rows, int cols, int ld) {
+bool make_store_map(CUtensorMap* map, void* ptr, bool h16, int rows, int cols, int ld) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(kUnitCols), 32u};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, estr,
+  CUresult r = enc(map, h16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   ptr, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE,
                    kUnitCols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-template <bool S8, int BN, int MAXST = 8>
+template <bool S8, int BN, int MAXST = 8, bool H16 = false>
 cudaError_t launch_tc(const GemmArgs& g, const EpiParams& p, cudaStream_t s, std::string* why) {
   using Cfg = TcCfg<BN, MAXST>;
   CUtensorMap ma, mb, mc;
-  memset(&mc, 0, sizeof(mc));  // unused unless the output is bf16
-  if (!make_map(&ma, g.A, S8, g.M, g.K, kBM) || !make_map(&mb, g.W, S8, g.N, g.K, BN) ||
-      (p.c_dtype == JB_DT_BF16 && !make_store_map(&mc, g.C, g.M, g.N, p.ldc))) {
+  memset(&mc, 0, sizeof(mc));  // unused unless the output is 16-bit
+  constexpr bool h16 = H16;
+  if (!make_map(&ma, g.A, S8, h16, g.M, g.K, kBM) || !make_map(&mb, g.W, S8, h16, g.N, g.K, BN) ||
+      ((p.c_dtype == JB_DT_BF16 || p.c_dtype == JB_DT_F16) &&
+       !make_store_map(&mc, g.C, p.c_dtype == JB_DT_F16, g.M, g.N, p.ldc))) {
     if (why) *why = "cuTensorMapEncodeTiled failed (pointer alignment or shape)";
     return cudaErrorInvalidValue;
   }
-  auto kern = gemm_tc_kernel<S8, BN, MAXST>;
+  auto kern = gemm_tc_kernel<S8, BN, MAXST, H16>;
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
@@ -697,6 +732,7 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why) {
   p.K = g.K;
   p.err = g.err;
   p.row_max = g.row_max;
+  p.h16 = 0;
   if (g.epi == JB_EPI_RESIDUAL && !g.resid) {
     if (why) *why = "linear: residual epilogue without a residual tensor";
     return cudaErrorInvalidValue;
@@ -712,8 +748,15 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why) {
     return cudaGetLastError();
   }
   const bool s8 = g.ab_dtype == JB_DT_S8;
-  if (!s8 && g.ab_dtype != JB_DT_BF16) {
+  if (!s8 && g.ab_dtype != JB_DT_BF16 && g.ab_dtype != JB_DT_F16) {
     if (why) *why = "linear: unsupported operand dtype";
+    return cudaErrorInvalidValue;
+  }
+  // 16-bit outputs and residuals have the operands' 16-bit type (bf16 for int8)
+  p.h16 = g.ab_dtype == JB_DT_F16 ? 1 : 0;
+  if ((g.ab_dtype == JB_DT_F16 && g.c_dtype != JB_DT_F16 && g.c_dtype != JB_DT_F32) ||
+      (g.ab_dtype != JB_DT_F16 && g.c_dtype == JB_DT_F16)) {
+    if (why) *why = "linear: an f16 output needs f16 operands, and f16 operands an f16 or f32 output";
     return cudaErrorInvalidValue;
   }
   // TMA: row strides must be multiples of 16 bytes, bases 16-byte aligned.
@@ -735,6 +778,11 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t s, std::string* why) {
       (g.resid && ((p.ldr % 8) || (reinterpret_cast<uintptr_t>(g.resid) & 15)))) {
     if (why) *why = "linear: C/residual must be 16-byte aligned with row strides multiple of 8";
     return cudaErrorInvalidValue;
+  }
+  if (p.h16) {  // f16 operands
+    if (g.N >= 512 || g.N % 256 == 0) return launch_tc<false, 256, 8, true>(g, p, s, why);
+    if (g.N >= 128) return launch_tc<false, 128, 8, true>(g, p, s, why);
+    return launch_tc<false, 64, 8, true>(g, p, s, why);
   }
   if (g.N >= 512 || g.N % 256 == 0) {
     if (s8 && g.K <= 1024) return launch_tc<true, 256, 3>(g, p, s, why);

@@ -42,6 +42,30 @@ template <> struct Vec<bf16> {
   // value as it will be read back after the store (bf16 rounding)
   __device__ static float rounded(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 };
+template <> struct Vec<f16> {
+  static constexpr int N = 8;
+  __device__ static void load(const f16* p, float* v) {
+    unpack(*reinterpret_cast<const uint4*>(p), v);
+  }
+  __device__ static void unpack(const uint4& raw, float* v) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __half22float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+  __device__ static uint4 pack(const float* v) {
+    uint4 raw;
+    __half2* h = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    return raw;
+  }
+  __device__ static void store(f16* p, const float* v) { *reinterpret_cast<uint4*>(p) = pack(v); }
+  __device__ static float rounded(float x) { return __half2float(__float2half_rn(x)); }
+};
 template <> struct Vec<float> {
   static constexpr int N = 4;
   __device__ static void load(const float* p, float* v) {
@@ -959,9 +983,14 @@ cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
         layernorm_bf16_kernel<4, false>
             <<<persistent_grid<layernorm_bf16_kernel<4, false>>(a.rows), 256, 0, s>>>(a);
     }
-  } else {
+  } else if (a.dtype == JB_DT_F16) {
+    if (a.cols % 8 || a.cols > 1024 || a.yq) return cudaErrorInvalidValue;
+    layernorm_kernel<f16, 4><<<persistent_grid<layernorm_kernel<f16, 4>>(a.rows), 256, 0, s>>>(a);
+  } else if (a.dtype == JB_DT_F32) {
     if (a.cols % 4 || a.cols > 1024) return cudaErrorInvalidValue;
     layernorm_kernel<float, 8><<<persistent_grid<layernorm_kernel<float, 8>>(a.rows), 256, 0, s>>>(a);
+  } else {
+    return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
@@ -972,9 +1001,14 @@ cudaError_t launch_embed_ln(const EmbedArgs& a, cudaStream_t s) {
   if (a.dtype == JB_DT_BF16) {
     if (a.H % 8 || a.H > 1024) return cudaErrorInvalidValue;
     embed_ln_kernel<bf16, 4><<<persistent_grid<embed_ln_kernel<bf16, 4>>(n), 256, 0, s>>>(a);
-  } else {
+  } else if (a.dtype == JB_DT_F16) {
+    if (a.H % 8 || a.H > 1024) return cudaErrorInvalidValue;
+    embed_ln_kernel<f16, 4><<<persistent_grid<embed_ln_kernel<f16, 4>>(n), 256, 0, s>>>(a);
+  } else if (a.dtype == JB_DT_F32) {
     if (a.H % 4 || a.H > 1024) return cudaErrorInvalidValue;
     embed_ln_kernel<float, 8><<<persistent_grid<embed_ln_kernel<float, 8>>(n), 256, 0, s>>>(a);
+  } else {
+    return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
@@ -998,6 +1032,8 @@ cudaError_t launch_quantize_act(const void* x, int dtype, int8_t* q, float* scal
       quantize_rows_kernel<bf16, 16, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
     else
       quantize_rows_kernel<bf16, 0, ACT><<<grid, 256, 0, s>>>(xb, q, scale, rows, drows, cols);
+  } else if (dtype != JB_DT_F32) {
+    return cudaErrorInvalidValue;  // int8 inputs come from bf16 or f32 rows
   } else {
     if (cols % 4) return cudaErrorInvalidValue;
     quantize_rows_kernel<float, 0, ACT><<<grid, 256, 0, s>>>(static_cast<const float*>(x), q,
@@ -1087,6 +1123,7 @@ cudaError_t launch_gelu_quantize_rowmax(const void* x, const unsigned int* row_m
 
 cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int cols,
                              cudaStream_t s) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   if (rows == 0) return cudaSuccess;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1103,6 +1140,7 @@ cudaError_t launch_gelu_rows(void* x, int dtype, int rows, const int* drows, int
 
 cudaError_t launch_rope_qk(void* qkv, int dtype, const int* cu, int batch, int max_seq, int heads,
                            int d, const float* cos_t, const float* sin_t, cudaStream_t s) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   const size_t slots = static_cast<size_t>(batch) * max_seq;
   if (slots == 0) return cudaSuccess;
   if (d % 2) return cudaErrorInvalidValue;
@@ -1120,6 +1158,7 @@ cudaError_t launch_rope_qk(void* qkv, int dtype, const int* cu, int batch, int m
 
 cudaError_t launch_geglu(const void* ug, void* out, int dtype, int rows, const int* drows, int I,
                          cudaStream_t s) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   if (rows == 0) return cudaSuccess;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1144,6 +1183,12 @@ cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, 
     if (H % 8) return cudaErrorInvalidValue;
     pool_normalize_kernel<bf16><<<batch, kPoolWarps * 32, 0, s>>>(static_cast<const bf16*>(hidden),
                                                                   cu, out, H, pooling);
+  } else if (dtype == JB_DT_F16) {
+    if (H % 8) return cudaErrorInvalidValue;
+    pool_normalize_kernel<f16><<<batch, kPoolWarps * 32, 0, s>>>(static_cast<const f16*>(hidden),
+                                                                 cu, out, H, pooling);
+  } else if (dtype != JB_DT_F32) {
+    return cudaErrorInvalidValue;
   } else {
     if (H % 4) return cudaErrorInvalidValue;
     pool_normalize_kernel<float><<<batch, kPoolWarps * 32, 0, s>>>(
@@ -1165,6 +1210,11 @@ cudaError_t launch_unpack_hidden(const void* packed, int dtype, const int* cu, f
   if (dtype == JB_DT_BF16)
     unpack_hidden_kernel<bf16><<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const bf16*>(packed),
                                                                   cu, out, batch, max_seq, H);
+  else if (dtype == JB_DT_F16)
+    unpack_hidden_kernel<f16><<<blocks_for(n, 256), 256, 0, s>>>(static_cast<const f16*>(packed),
+                                                                 cu, out, batch, max_seq, H);
+  else if (dtype != JB_DT_F32)
+    return cudaErrorInvalidValue;
   else
     unpack_hidden_kernel<float><<<blocks_for(n, 256), 256, 0, s>>>(
         static_cast<const float*>(packed), cu, out, batch, max_seq, H);
@@ -1173,6 +1223,7 @@ cudaError_t launch_unpack_hidden(const void* packed, int dtype, const int* cu, f
 
 cudaError_t launch_patchify(const float* px, void* patches, int dtype, int batch, int image,
                             int patch, cudaStream_t s) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   const int g = image / patch;
   const size_t n = static_cast<size_t>(batch) * g * g * 3 * patch * patch;
   if (n == 0) return cudaSuccess;
@@ -1188,6 +1239,7 @@ cudaError_t launch_patchify(const float* px, void* patches, int dtype, int batch
 cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const void* pos,
                                 const float* gamma, const float* beta, void* y, int dtype,
                                 int batch, int tokens, int W, float eps, cudaStream_t s) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   const size_t n = static_cast<size_t>(batch) * tokens;
   if (n == 0) return cudaSuccess;
   const unsigned grid = blocks_for(n, kRowsPerBlock);
@@ -1208,6 +1260,7 @@ cudaError_t launch_vit_embed_ln(const void* patch_out, const void* cls, const vo
 cudaError_t launch_vit_pool_ln(const void* x, const float* gamma, const float* beta, void* y,
                                int dtype, int batch, int tokens, int W, int gap, float eps,
                                cudaStream_t s, const int* cu) {
+  if (dtype != JB_DT_BF16 && dtype != JB_DT_F32) return cudaErrorInvalidValue;  // not an f16 kernel
   if (batch == 0) return cudaSuccess;
   if (cu && gap) return cudaErrorInvalidValue;
   if (dtype == JB_DT_BF16) {

@@ -82,6 +82,30 @@ uint16_t float_to_bf16(float f) {
   return static_cast<uint16_t>(u >> 16);
 }
 
+// IEEE binary16, round to nearest even.  Normal results: the exponent is
+// rebiased (127 -> 15, i.e. minus 112 << 23) and the 13 dropped mantissa bits
+// rounded by adding 0xFFF plus the kept LSB; a carry moves into the exponent.
+// Magnitudes from 65520 up round to infinity; below 2^-14 the result is a
+// subnormal multiple of 2^-24 (the scaling by 2^24 is exact, nearbyint rounds
+// half to even).
+uint16_t float_to_f16(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint16_t sign = static_cast<uint16_t>((x >> 16) & 0x8000u);
+  x &= 0x7FFFFFFFu;
+  if (x > 0x7F800000u) return sign | 0x7E00u;  // NaN
+  if (x >= 0x477FF000u) return sign | 0x7C00u;  // infinity, or rounds to it
+  if (x < 0x38800000u) {
+    float a;
+    std::memcpy(&a, &x, 4);
+    return sign | static_cast<uint16_t>(std::nearbyint(a * 16777216.0f));
+  }
+  return sign | static_cast<uint16_t>((x + 0x0FFFu + ((x >> 13) & 1u) - 0x38000000u) >> 13);
+}
+
+// The model's 16-bit activation / weight encoding of a float.
+uint16_t to_half_bits(int dt, float f) { return dt == JB_DT_F16 ? float_to_f16(f) : float_to_bf16(f); }
+
 struct SafeTensors {
   std::vector<char> file;
   size_t data_start = 0;
@@ -190,11 +214,11 @@ void* upload_bytes(jb_model* m, const void* src, size_t bytes) {
 float* upload_f32(jb_model* m, const std::vector<float>& v) {
   return static_cast<float*>(upload_bytes(m, v.data(), v.size() * 4));
 }
-// Upload in the model's activation dtype (f32 or bf16).
+// Upload in the model's activation dtype (f32, bf16 or f16).
 void* upload_act(jb_model* m, const std::vector<float>& v) {
   if (m->act == JB_DT_F32) return upload_f32(m, v);
   std::vector<uint16_t> h(v.size());
-  for (size_t i = 0; i < v.size(); ++i) h[i] = float_to_bf16(v[i]);
+  for (size_t i = 0; i < v.size(); ++i) h[i] = to_half_bits(m->act, v[i]);
   return upload_bytes(m, h.data(), h.size() * 2);
 }
 
@@ -262,7 +286,7 @@ Linear load_linear(jb_model* m, const SafeTensors& st, const std::vector<std::st
       L.w = upload_f32(m, w);
     } else {
       std::vector<uint16_t> h(w.size());
-      for (size_t i = 0; i < w.size(); ++i) h[i] = float_to_bf16(w[i]);
+      for (size_t i = 0; i < w.size(); ++i) h[i] = to_half_bits(fmt_dtype, w[i]);
       L.w = upload_bytes(m, h.data(), h.size() * 2);
     }
   }
@@ -277,7 +301,9 @@ Linear load_linear(jb_model* m, const SafeTensors& st, const std::vector<std::st
 }
 
 int linear_dtype(int format) {
-  return format == JB_FMT_F32 ? JB_DT_F32 : (format == JB_FMT_INT8 ? JB_DT_S8 : JB_DT_BF16);
+  if (format == JB_FMT_F32) return JB_DT_F32;
+  if (format == JB_FMT_INT8) return JB_DT_S8;
+  return format == JB_FMT_F16 ? JB_DT_F16 : JB_DT_BF16;
 }
 
 // BERT and DistilBERT share the forward (post-LN encoder, exact-erf GELU,
@@ -310,6 +336,7 @@ void load_modernbert(jb_model* m, const SafeTensors& st, const Json& cfg) {
                              std::to_string(m->heads) + ")");
   if (H > 1024 || H % 8 || I % 8) fail(JB_ERR_INVALID, "ModernBERT: hidden_size and intermediate_size must be multiples of 8, hidden_size <= 1024");
   if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are defined for BERT and DistilBERT encoders");
+  if (m->format == JB_FMT_F16) fail(JB_ERR_INVALID, "f16 is defined for BERT and DistilBERT encoders");
   const int d = H / m->heads;
   if (d % 2) fail(JB_ERR_INVALID, "ModernBERT: head_dim must be even (RoPE pairs)");
   const std::string p = st.has("model.embeddings.tok_embeddings.weight") ? "model." : "";
@@ -446,6 +473,7 @@ void load_clip(jb_model* m, const SafeTensors& st, const Json& cfg) {
   if (W <= 0 || W % m->heads || W % 8 || W > 1024 || m->embed_dim <= 0 || g <= 0)
     fail(JB_ERR_INVALID, "OpenCLIP config: unsupported vision dimensions");
   if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are only defined for BERT encoders");
+  if (m->format == JB_FMT_F16) fail(JB_ERR_INVALID, "f16 is defined for BERT and DistilBERT encoders");
   const std::string p = st.has("visual.conv1.weight") ? "visual." : "";
   const int ld = linear_dtype(m->format);
   m->conv = load_linear(m, st, {p + "conv1"}, {W}, 3 * P * P, false, ld);
@@ -520,6 +548,7 @@ void load_clip_text(jb_model* m, const SafeTensors& st, const Json& cfg) {
       m->max_pos <= 0 || m->vocab <= 0 || m->layers < 0)
     fail(JB_ERR_INVALID, "OpenCLIP config: unsupported text dimensions");
   if (m->format == JB_FMT_INT8) fail(JB_ERR_INVALID, "int8 weights are only defined for BERT encoders");
+  if (m->format == JB_FMT_F16) fail(JB_ERR_INVALID, "f16 is defined for BERT and DistilBERT encoders");
   const int ld = linear_dtype(m->format);
   m->word = upload_act(m, st.f32("token_embedding.weight", int64_t(m->vocab) * W));
   m->pos = upload_act(m, st.f32("positional_embedding", int64_t(m->max_pos) * W));
@@ -689,7 +718,7 @@ Workspace carve_workspace(const jb_model* m, void* base_ptr, int batch, int seq)
 
 jb_model* model_load(const char* path, const char* config_json, int device, int format, int family) {
   if (!path || !config_json) fail(JB_ERR_INVALID, "weights path and config must be non-null");
-  if (format < JB_FMT_F32 || format > JB_FMT_INT8) fail(JB_ERR_INVALID, "unknown weight format");
+  if (format < JB_FMT_F32 || format > JB_FMT_F16) fail(JB_ERR_INVALID, "unknown weight format");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
     cudaGetLastError();
@@ -711,7 +740,7 @@ jb_model* model_load(const char* path, const char* config_json, int device, int 
   std::unique_ptr<jb_model> m(new jb_model());
   m->device = device;
   m->format = format;
-  m->act = format == JB_FMT_F32 ? JB_DT_F32 : JB_DT_BF16;
+  m->act = format == JB_FMT_F32 ? JB_DT_F32 : (format == JB_FMT_F16 ? JB_DT_F16 : JB_DT_BF16);
   try {
     SafeTensors st(path);
     if (family < 0) family = cfg.get("model_cfg") ? JB_FAMILY_CLIP_VISION : JB_FAMILY_BERT;
@@ -963,7 +992,7 @@ void build_fused(jb_model* m, const LoraSiteHost* const* sites, const int* outs,
 void set_lora(jb_model* m, int layer, int site, const float* a, const float* b, int rank,
               double scaling) {
   if (m->family != JB_FAMILY_BERT) fail(JB_ERR_INVALID, "LoRA adapters apply to text encoders");
-  if (m->format == JB_FMT_INT8)
+  if (m->format == JB_FMT_INT8 || m->format == JB_FMT_F16)
     fail(JB_ERR_INVALID, "LoRA adapters run in the f32 and bf16 formats");
   if (m->variant == JB_TEXT_MODERNBERT)
     fail(JB_ERR_INVALID, "LoRA adapters are wired for the BERT and DistilBERT layer layout");

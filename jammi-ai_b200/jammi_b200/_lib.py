@@ -15,12 +15,12 @@ OK, ERR_OOM, ERR_INVALID, ERR_CUDA, ERR_TIMEOUT, ERR_SEQ_TOO_LONG, ERR_IO, ERR_N
 STATUS_NAMES = {0: "OK", 1: "OOM", 2: "INVALID", 3: "CUDA", 4: "TIMEOUT", 5: "SEQ_TOO_LONG",
                 6: "IO", 7: "NO_DEVICE"}
 # jb_format
-FMT_F32, FMT_BF16, FMT_INT8 = 0, 1, 2
-FORMATS = {"f32": FMT_F32, "bf16": FMT_BF16, "int8": FMT_INT8}
+FMT_F32, FMT_BF16, FMT_INT8, FMT_F16 = 0, 1, 2, 3
+FORMATS = {"f32": FMT_F32, "bf16": FMT_BF16, "int8": FMT_INT8, "f16": FMT_F16}
 # jb_pooling
 POOL_MEAN, POOL_CLS, POOL_MAX, POOL_WEIGHTED_MEAN = 0, 1, 2, 3
 # jb_dtype
-DT_F32, DT_BF16, DT_S8, DT_S32 = 0, 1, 2, 3
+DT_F32, DT_BF16, DT_S8, DT_S32, DT_F16 = 0, 1, 2, 3, 4
 # jb_epilogue
 EPI_NONE, EPI_GELU, EPI_QUICK_GELU, EPI_RESIDUAL = 0, 1, 2, 3
 # jb_family

@@ -12,7 +12,8 @@ import torch
 from . import _lib as L
 from ._lib import check, lib
 
-_DT = {torch.float32: L.DT_F32, torch.bfloat16: L.DT_BF16, torch.int8: L.DT_S8, torch.int32: L.DT_S32}
+_DT = {torch.float32: L.DT_F32, torch.bfloat16: L.DT_BF16, torch.float16: L.DT_F16, torch.int8: L.DT_S8,
+       torch.int32: L.DT_S32}
 
 
 def _s(t: torch.Tensor) -> int:

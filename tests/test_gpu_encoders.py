@@ -23,7 +23,10 @@ from oracle import quant as oq
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-TOL = {"f32": 1e-4, "bf16": 2e-3, "int8": 2e-3}
+# f16: the reference's own CPU <-> GPU acceptance bar (max |diff| <= 1e-3,
+# crates/jammi-ai/tests/gpu_capability/harness.rs:40); f16 keeps 3 more
+# mantissa bits than bf16.
+TOL = {"f32": 1e-4, "bf16": 2e-3, "int8": 2e-3, "f16": 1e-3}
 COS = 0.9999
 
 
@@ -63,7 +66,7 @@ def _bert(weights, cfg, fmt, pooling="mean"):
 # ── golden fixtures (HF transformers) ───────────────────────────────────────
 
 @pytest.mark.parametrize("name", ["tiny_bert_seeded.npz", "small_bert_prefixed.npz"])
-@pytest.mark.parametrize("fmt", ["f32", "bf16"])
+@pytest.mark.parametrize("fmt", ["f32", "bf16", "f16"])
 def test_bert_golden_all_poolings(name, fmt):
     w, g = load_golden(name)
     cfg = json.loads(bytes(g["config_json"]).decode())
@@ -78,7 +81,7 @@ def test_bert_golden_all_poolings(name, fmt):
     assert np.all(out[lens == 0] == 0)
 
 
-@pytest.mark.parametrize("fmt", ["f32", "bf16", "int8"])
+@pytest.mark.parametrize("fmt", ["f32", "bf16", "int8", "f16"])
 def test_distilbert_golden(fmt):
     """DistilBERT weights and config (distilbert.rs) through the same forward,
     against HF DistilBertModel (f32 / bf16) or the int8 oracle."""
@@ -165,6 +168,40 @@ def test_bert_base_bf16_config(tc_attention):
     finally:
         ops.set_attention_tcgen05(True)
     assert_close_rows(out, ref, "bf16")
+
+
+def test_bert_base_f16_config():
+    """BERT-base in f16 (ComputePrecision::F16, crates/jammi-numerics/src/precision.rs:36-51):
+    f16 weights and activations, f32 accumulation, seq 256, lengths U[32,256]."""
+    cfg, w = _bert_base(211)
+    rng = np.random.default_rng(212)
+    lens = rng.integers(32, 257, size=12)
+    lens[0] = 256
+    ids, mask = ob.random_token_batch(12, 256, lens, seed=213)
+    ref = ob.bert_forward(w, cfg, ids, mask)
+    model = _bert(w, cfg.to_dict(), "f16")
+    assert model.info.format == 3
+    assert_close_rows(model.encode(ids, lens), ref, "f16")
+
+
+def test_f16_is_defined_for_bert_and_distilbert_only(tmp_path):
+    """f16 answers JB_ERR_INVALID for the families without an f16 path
+    (ModernBERT, the OpenCLIP towers) and for LoRA adapters."""
+    from jammi_b200 import JbError, OpenClipVisionTransformer
+    w, g = load_golden("small_modernbert.npz")
+    mcfg = json.loads(bytes(g["config_json"]).decode())
+    with pytest.raises(JbError):
+        _bert(w, mcfg, "f16")
+    ccfg = oc.ClipVisionConfig(image_size=64, patch_size=32, width=64, layers=1, heads=2, embed_dim=32)
+    with pytest.raises(JbError):
+        OpenClipVisionTransformer.from_weights(oc.random_clip_weights(ccfg, seed=1),
+                                               ccfg.to_open_clip_config(), device=0, fmt="f16")
+    bw, bg = load_golden("tiny_bert_seeded.npz")
+    bcfg = json.loads(bytes(bg["config_json"]).decode())
+    model = _bert(bw, bcfg, "f16")
+    H = bcfg["hidden_size"]
+    with pytest.raises(JbError):
+        model.set_lora(0, 0, np.zeros((8, H), np.float32), np.zeros((H, 8), np.float32), 1.0)
 
 
 def test_bert_base_int8_config():

@@ -4,6 +4,7 @@ arithmetic), called through the C ABI on seeded inputs.
 Tolerances (written next to each check):
 * int8 accumulators and int8 quantisation: bit-exact.
 * bf16 outputs: error within a few bf16 ulps of the f32/f64 reference.
+* f16 outputs: error within a few f16 ulps (2^-11 relative) of the reference.
 * f32 outputs: 1e-4 absolute or tighter.
 """
 import math
@@ -106,6 +107,55 @@ def test_tensor_core_activation_accuracy(dev, epi):
         ref = xd / (1 + np.exp(-1.702 * xd))
     err = np.abs(c.double().cpu().numpy() - ref[:, None])
     assert np.all(err <= 1e-6 * np.maximum(1.0, np.abs(xd))[:, None]), err.max()
+
+
+def _f16(x, dev):
+    return torch.from_numpy(np.asarray(x, dtype=np.float32)).to(dev).to(torch.float16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 768, 768), (300, 2304, 768), (777, 3072, 768), (1000, 768, 3072),
+                                   (37, 96, 32), (5, 16, 48)])
+def test_linear_f16_matches_fp32(dev, M, N, K):
+    """f16 operands on the tcgen05 kernel (kind::f16, A and B both f16), f16
+    output: within f16's half ulp (2^-11 of the largest |ref|) plus f32
+    accumulation."""
+    ops = _ops()
+    rng = np.random.default_rng(M * 5 + N + K)
+    a = _f16(rng.standard_normal((M, K)), dev)
+    w = _f16(rng.standard_normal((N, K)) * 0.05, dev)
+    bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+    c = ops.linear(a, w, bias=bias)
+    ops.sync()
+    assert c.dtype == torch.float16
+    ref = a.double() @ w.double().T + bias.double()
+    err = (c.double() - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item() + 1e-4, err
+
+
+@pytest.mark.parametrize("epi", ["gelu", "residual", "f32_out"])
+def test_linear_f16_epilogues(dev, epi):
+    import jammi_b200 as jb
+    ops = _ops()
+    M, N, K = 333, 768, 768
+    rng = np.random.default_rng(15)
+    a = _f16(rng.standard_normal((M, K)), dev)
+    w = _f16(rng.standard_normal((N, K)) * 0.05, dev)
+    bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(dev)
+    res = _f16(rng.standard_normal((M, N)), dev)
+    z = a.double() @ w.double().T + bias.double()
+    if epi == "gelu":
+        c = ops.linear(a, w, bias=bias, epilogue=jb.EPI_GELU)
+        ref = 0.5 * z * (1 + torch.erf(z / math.sqrt(2)))
+    elif epi == "residual":
+        c = ops.linear(a, w, bias=bias, residual=res, epilogue=jb.EPI_RESIDUAL)
+        ref = z + res.double()
+    else:
+        c = ops.linear(a, w, bias=bias, out_dtype=torch.float32)
+        ref = z
+    ops.sync()
+    err = (c.double() - ref).abs().max().item()
+    bar = 1e-4 if epi == "f32_out" else 1e-3 * ref.abs().max().item() + 1e-4
+    assert err <= bar, err
 
 
 def test_linear_bf16_f32_output(dev):
@@ -218,7 +268,8 @@ def test_gelu_quantize_rows(dev):
 
 @pytest.mark.parametrize("dtype,cols,with_res", [
     ("f32", 384, True), ("f32", 32, True), ("bf16", 768, True), ("bf16", 1024, True),
-    ("bf16", 64, True), ("bf16", 768, False), ("bf16", 1024, False), ("bf16", 200, False)])
+    ("bf16", 64, True), ("bf16", 768, False), ("bf16", 1024, False), ("bf16", 200, False),
+    ("f16", 768, True), ("f16", 1024, False), ("f16", 64, False)])
 def test_layernorm(dev, dtype, cols, with_res):
     ops = _ops()
     rng = np.random.default_rng(cols)
@@ -227,7 +278,8 @@ def test_layernorm(dev, dtype, cols, with_res):
     r = rng.standard_normal((R, cols)).astype(np.float32)
     g = rng.uniform(0.5, 1.5, cols).astype(np.float32)
     b = rng.standard_normal(cols).astype(np.float32)
-    mk = (lambda v: _bf16(v, dev)) if dtype == "bf16" else (lambda v: torch.from_numpy(v).to(dev))
+    mk = {"bf16": lambda v: _bf16(v, dev), "f16": lambda v: _f16(v, dev),
+          "f32": lambda v: torch.from_numpy(v).to(dev)}[dtype]
     xt, rt = mk(x), mk(r)
     y = ops.layernorm(xt, torch.from_numpy(g).to(dev), torch.from_numpy(b).to(dev), 1e-12,
                       residual=rt if with_res else None)
@@ -238,6 +290,9 @@ def test_layernorm(dev, dtype, cols, with_res):
     if dtype == "bf16":
         # bf16 output rounding: half an ulp is at most 2^-8 of |y|
         assert np.all(err <= np.abs(ref) * 2.0 ** -8 + 2e-3), err.max()
+    elif dtype == "f16":
+        # f16 output rounding: half an ulp is at most 2^-11 of |y|
+        assert np.all(err <= np.abs(ref) * 2.0 ** -11 + 2e-4), err.max()
     else:
         assert err.max() < 1e-5, err.max()
 
@@ -262,6 +317,48 @@ def _attn_ref(qkv, cu, heads, causal=False):
                 sc = np.where(np.triu(np.ones(sc.shape, dtype=bool), 1), -np.inf, sc)
             out[s:e, h * d:(h + 1) * d] = ob.softmax_last(sc) @ v
     return out
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("lens", [
+    [1, 2, 15, 16, 17, 63, 64, 65, 127, 128, 129, 200, 255, 256],
+    [300, 17, 257, 256, 1, 512],
+])
+def test_attention_tc_f16(dev, lens, causal):
+    """The tcgen05 kernel with f16 Q, K, V, P and context (kind::f16 with
+    both operands f16).  P enters P V as f16 (2^-12 relative, at most ~2e-3
+    here against max |V| ~7) and the output is stored as f16 (2^-12 |ref|)."""
+    ops = _ops()
+    heads, d = 12, 64
+    rng = np.random.default_rng(sum(lens) + 11 + (7 if causal else 0))
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = (rng.standard_normal((T + 5, 3 * heads * d)) * 1.5).astype(np.float32)
+    qkv[T:] = np.nan
+    qt = _f16(qkv, dev)
+    ctx = ops.attention(qt.contiguous(), torch.from_numpy(cu).to(dev), heads, max(lens),
+                        causal=causal, tma=True)
+    ops.sync()
+    assert ctx.dtype == torch.float16
+    ref = _attn_ref(qt.double().cpu().numpy()[:T], cu, heads, causal=causal)
+    got = ctx.double().cpu().numpy()[:T]
+    assert np.isfinite(got).all()
+    bound = 5e-3 + 5e-4 * np.abs(ref)
+    worst = np.abs(got - ref) / bound
+    assert worst.max() <= 1.0, (np.abs(got - ref).max(), worst.max())
+
+
+def test_attention_f16_needs_the_tcgen05_kernel(dev):
+    from jammi_b200 import JbError
+    ops = _ops()
+    qkv = _f16(np.ones((8, 3 * 64)), dev)
+    cu = torch.tensor([0, 8], dtype=torch.int32, device=dev)
+    ops.set_attention_tcgen05(False)
+    try:
+        with pytest.raises(JbError):
+            ops.attention(qkv, cu, 1, 8, tma=True)
+    finally:
+        ops.set_attention_tcgen05(True)
 
 
 @pytest.mark.parametrize("dtype,heads,d,lens", [
@@ -395,7 +492,7 @@ def test_attention_causal(dev, dtype, heads, d, lens):
 # ── pooling + L2 ────────────────────────────────────────────────────────────
 
 @pytest.mark.parametrize("pooling", ["mean", "cls", "max", "weighted_mean"])
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
 def test_pool_normalize(dev, pooling, dtype):
     ops = _ops()
     rng = np.random.default_rng(3)
@@ -406,7 +503,8 @@ def test_pool_normalize(dev, pooling, dtype):
     mask = (np.arange(S)[None, :] < np.array(lens)[:, None]).astype(np.uint32)
     packed = np.concatenate([hidden[b, :n] for b, n in enumerate(lens)], axis=0)
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
-    pt = _bf16(packed, dev) if dtype == "bf16" else torch.from_numpy(packed).to(dev)
+    pt = {"bf16": lambda: _bf16(packed, dev), "f16": lambda: _f16(packed, dev),
+          "f32": lambda: torch.from_numpy(packed).to(dev)}[dtype]()
     out = ops.pool_normalize(pt, torch.from_numpy(cu).to(dev), ob.POOLING_NAMES[pooling])
     ops.sync()
     h_used = np.zeros_like(hidden)
