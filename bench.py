@@ -55,6 +55,8 @@ WORKLOADS = {
                                 dist=("uniform", 32, 256)),
     "bert-base-bf16-s256": dict(kind="text", arch="bert-base", fmt="bf16", batch=256, seq=256,
                                 dist=("uniform", 32, 256)),
+    "bert-base-f16-s256": dict(kind="text", arch="bert-base", fmt="f16", batch=256, seq=256,
+                               dist=("uniform", 32, 256)),
     "bert-large-int8-s512": dict(kind="text", arch="bert-large", fmt="int8", batch=128, seq=512,
                                  dist=("lognormal", 5.0, 0.6, 8, 512), prequantised=True),
     "clip-vit-b32-bf16": dict(kind="image", arch="vit-b32", fmt="bf16", batch=512),
@@ -520,7 +522,8 @@ def run_text(args, wl, n, torch):
                          if traffic else "no capture of this workload"),
         "peak_source": (f"2 x {src} bf16 burst ({peaks['bf16_tflops']} TF/s; B200's dense int8 rate is "
                         "twice bf16): the linears are timed one launch at a time in a short pass"
-                        if int8 else f"{src} bf16 burst ({peaks['bf16_tflops']} TF/s)"),
+                        if int8 else f"{src} bf16 burst ({peaks['bf16_tflops']} TF/s"
+                        + ("; B200's dense f16 rate equals bf16's)" if wl["fmt"] == "f16" else ")")),
         "flops_per_step": lin_f / prof_steps,
         "attention": {"achieved": att_f / (att_ms / 1e3) / 1e12 if att_ms > 0 else None,
                       "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -537,7 +540,7 @@ def run_text(args, wl, n, torch):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "ms_per_step_per_device": [m / args.steps for m in ms_dev],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8/bf16" if int8 else "bf16", "data": "synthetic",
+        "dtype": "int8/bf16" if int8 else wl["fmt"], "data": "synthetic",
         "config": {"workload": args.workload, "arch": wl["arch"], "weights": wl["fmt"],
                    "global_batch": B * n, "batch_per_gpu": B, "seq_len": S, "lengths": dist_name(wl),
                    "valid_tokens_per_step": tokens / prof_steps, "parallelism": f"replicas{n}",
