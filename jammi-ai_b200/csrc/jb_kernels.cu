@@ -223,11 +223,11 @@ __global__ void __launch_bounds__(256) layernorm_kernel(LnArgs a) {
   }
 }
 
-// bf16 rows of up to MAXV x 256 columns, persistent over rows like
-// layernorm_kernel, but each warp loads its next row (and residual row) into
-// registers before it normalises the current one, so the memory latency of
-// one row overlaps the reductions and stores of the other.
-template <int MAXV, bool RES>
+// 16-bit (bf16 or f16) rows of up to MAXV x 256 columns, persistent over
+// rows like layernorm_kernel, but each warp loads its next row (and residual
+// row) into registers before it normalises the current one, so the memory
+// latency of one row overlaps the reductions and stores of the other.
+template <int MAXV, bool RES, typename T = bf16>
 __global__ void __launch_bounds__(256) layernorm_bf16_kernel(LnArgs a) {
   __shared__ __align__(16) float sg[kLnMaxCols];
   __shared__ __align__(16) float sb[kLnMaxCols];
@@ -237,9 +237,9 @@ __global__ void __launch_bounds__(256) layernorm_bf16_kernel(LnArgs a) {
   const int nvec = a.cols / 8;
   const int stride = gridDim.x * kRowsPerBlock;
   auto fetch = [&](int row, uint4 (&xr)[MAXV], uint4 (&rr)[MAXV]) {
-    const uint4* x = reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.x) +
+    const uint4* x = reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) +
                                                     static_cast<size_t>(row) * a.cols);
-    const uint4* r = RES ? reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.resid) +
+    const uint4* r = RES ? reinterpret_cast<const uint4*>(static_cast<const T*>(a.resid) +
                                                          static_cast<size_t>(row) * a.cols)
                          : nullptr;
 #pragma unroll
@@ -259,18 +259,18 @@ __global__ void __launch_bounds__(256) layernorm_bf16_kernel(LnArgs a) {
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       if (lane + i * 32 < nvec) {
-        Vec<bf16>::unpack(nx[i], v + i * 8);
+        Vec<T>::unpack(nx[i], v + i * 8);
         if constexpr (RES) {
           float t[8];
-          Vec<bf16>::unpack(nr[i], t);
+          Vec<T>::unpack(nr[i], t);
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[i * 8 + e] += t[e];
         }
       }
     }
     if (row + stride < R) fetch(row + stride, nx, nr);
-    ln_finish<bf16, MAXV>(v, nvec, a.cols, lane, sg, sb, a.eps,
-                          static_cast<bf16*>(a.y) + static_cast<size_t>(row) * a.cols,
+    ln_finish<T, MAXV>(v, nvec, a.cols, lane, sg, sb, a.eps,
+                       static_cast<T*>(a.y) + static_cast<size_t>(row) * a.cols,
                           a.yq ? a.yq + static_cast<size_t>(row) * a.cols : nullptr,
                           a.yscale ? a.yscale + row : nullptr);
     if (a.zero_rows && lane == 0) a.zero_rows[row] = 0u;
@@ -985,7 +985,21 @@ cudaError_t launch_layernorm(const LnArgs& a, cudaStream_t s) {
     }
   } else if (a.dtype == JB_DT_F16) {
     if (a.cols % 8 || a.cols > 1024 || a.yq) return cudaErrorInvalidValue;
-    layernorm_kernel<f16, 4><<<persistent_grid<layernorm_kernel<f16, 4>>(a.rows), 256, 0, s>>>(a);
+    if (a.cols <= 768) {
+      if (a.resid)
+        layernorm_bf16_kernel<3, true, f16>
+            <<<persistent_grid<layernorm_bf16_kernel<3, true, f16>>(a.rows), 256, 0, s>>>(a);
+      else
+        layernorm_bf16_kernel<3, false, f16>
+            <<<persistent_grid<layernorm_bf16_kernel<3, false, f16>>(a.rows), 256, 0, s>>>(a);
+    } else {
+      if (a.resid)
+        layernorm_bf16_kernel<4, true, f16>
+            <<<persistent_grid<layernorm_bf16_kernel<4, true, f16>>(a.rows), 256, 0, s>>>(a);
+      else
+        layernorm_bf16_kernel<4, false, f16>
+            <<<persistent_grid<layernorm_bf16_kernel<4, false, f16>>(a.rows), 256, 0, s>>>(a);
+    }
   } else if (a.dtype == JB_DT_F32) {
     if (a.cols % 4 || a.cols > 1024) return cudaErrorInvalidValue;
     layernorm_kernel<float, 8><<<persistent_grid<layernorm_kernel<float, 8>>(a.rows), 256, 0, s>>>(a);
