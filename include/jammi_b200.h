@@ -212,8 +212,9 @@ typedef enum {
 
 /* C[M,N] = epi(A[M,K] . W[N,K]^T + bias[N]) -- candle_nn::Linear as called by
  * MaybeLoraLinear::Frozen (crates/jammi-lora/src/wrapper.rs:29-42).
- * a_dtype/w_dtype: F32 (SIMT path) or BF16 (tcgen05 path); c_dtype F32 or
- * BF16; residual has c's dtype and row stride N.  bias may be NULL. */
+ * a_dtype/w_dtype: F32 (SIMT path), or BF16 or F16 (tcgen05 path, both the
+ * same); c_dtype F32, or the operands' 16-bit type; residual has c's dtype
+ * and row stride N.  bias may be NULL. */
 jb_status jb_op_linear(const void* A, int a_dtype, const void* W, int w_dtype,
                        const float* bias, const void* residual, void* C, int c_dtype,
                        int M, int N, int K, int epilogue, void* stream);
@@ -235,7 +236,7 @@ jb_status jb_op_quantize_rows(const void* x, int x_dtype, int8_t* q, float* scal
 jb_status jb_op_quantize_rows_act(const void* x, int x_dtype, int activation, int8_t* q,
                                   float* scale, int rows, int cols, void* stream);
 /* y = LayerNorm(x (+ residual)) over the last dim, in place allowed
- * (crates/jammi-encoders/src/layer_norm.rs:55-84).  x/y dtype F32 or BF16. */
+ * (crates/jammi-encoders/src/layer_norm.rs:55-84).  x/y dtype F32, BF16 or F16. */
 jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamma,
                           const float* beta, void* y, int dtype, int rows, int cols,
                           float eps, void* stream);
@@ -244,7 +245,8 @@ jb_status jb_op_layernorm(const void* x, const void* residual, const float* gamm
  * ctx [T, heads*d].  softmax(Q K^T / sqrt(d)) V per (row, head) over the row's
  * valid tokens -- BertSelfAttention::forward (bert.rs:135-155) with the
  * additive -10000 mask (mask.rs:14-20) realised by excluding padding.
- * dtype F32 or BF16; max_len bounds every row's length. */
+ * dtype F32, BF16 or F16 (F16 with head_dim 64 runs only on the tcgen05
+ * kernel: jb_op_attention_rows); max_len bounds every row's length. */
 jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
                           int batch, int heads, int head_dim, int max_len, void* stream);
 /* The same under the causal mask of the OpenCLIP text tower: query i of a row
@@ -252,11 +254,12 @@ jb_status jb_op_attention(const void* qkv, const int* cu_seqlens, void* ctx, int
 jb_status jb_op_attention_causal(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
                                  int batch, int heads, int head_dim, int max_len, void* stream);
 /* The same with the row count of qkv known (rows >= cu_seqlens[batch]):
- * bf16 head_dim 64 then loads its tiles by TMA (the model forwards' path). */
+ * bf16 / f16 head_dim 64 then loads its tiles by TMA (the model forwards' path). */
 jb_status jb_op_attention_rows(const void* qkv, const int* cu_seqlens, void* ctx, int dtype,
                                int batch, int heads, int head_dim, int max_len, int rows,
                                int causal, void* stream);
-/* Process-wide choice for bf16 head_dim-64 attention with TMA (model forwards
+/* Process-wide choice for bf16 head_dim-64 attention with TMA (model forwards;
+ * f16 always runs on the tcgen05 kernel, and is refused when it is off)
  * and jb_op_attention_rows): on != 0 (the default) runs every row on the
  * tcgen05 kernel (S = QK^T and O = PV as tcgen05.mma with S, P and O in
  * TMEM; keys streamed in blocks of 128 with an online softmax; a persistent
@@ -276,7 +279,7 @@ jb_status jb_op_sync(void* stream);
  * rule as every spin inside the library's kernels, as an op that exercises
  * failure detection without a fault.  No reference counterpart. */
 jb_status jb_op_wait_flag(const int* d_flag, int expect, int limit_ms, void* stream);
-/* pool_and_normalize over packed hidden [T, H] (dtype F32/BF16) with
+/* pool_and_normalize over packed hidden [T, H] (dtype F32/BF16/F16) with
  * cu_seqlens [batch+1]: out f32 [batch, H] (pooling.rs:31-148). */
 jb_status jb_op_pool_normalize(const void* hidden, int dtype, const int* cu_seqlens,
                                float* out, int batch, int H, int pooling, void* stream);
