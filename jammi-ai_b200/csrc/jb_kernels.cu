@@ -841,6 +841,31 @@ __global__ void patchify_kernel(const float* px, T* out, int batch, int image, i
   out[idx] = from_f<T>(v);
 }
 
+// The same gather for patch and image sides that are multiples of 8: one
+// thread per 8 consecutive pixels of one source row of image blockIdx.y
+// (two 16-byte loads, consecutive threads along the row), written as 8
+// consecutive elements of one patch row (one 16-byte store for 16-bit T).
+// 32-bit index arithmetic inside one image.
+template <typename T>
+__global__ void __launch_bounds__(256) patchify8_kernel(const float* __restrict__ px, T* __restrict__ out,
+                                                        int image, int patch) {
+  const int xv = image >> 3, pv = patch >> 3, g = image / patch;
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= 3 * image * xv) return;
+  const int b = blockIdx.y;
+  const int x8 = u % xv, cy = u / xv, y = cy % image, c = cy / image;
+  const float4* src = reinterpret_cast<const float4*>(
+      px + ((static_cast<size_t>(b) * 3 + c) * image + y) * image + x8 * 8);
+  const float4 a0 = __ldg(src), a1 = __ldg(src + 1);
+  const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const int gy = y / patch, ky = y - gy * patch, gx = x8 / pv, kx = (x8 - gx * pv) * 8;
+  const size_t prow = static_cast<size_t>(b) * g * g + gy * g + gx;
+  T* dst = out + prow * (3 * patch * patch) + (c * patch + ky) * patch + kx;
+  constexpr int VN = Vec<T>::N;
+#pragma unroll
+  for (int i = 0; i < 8; i += VN) Vec<T>::store(dst + i, v + i);
+}
+
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) vit_embed_ln_kernel(const T* patch_out, const T* cls,
                                                            const T* pos, const float* gamma,
@@ -1241,6 +1266,22 @@ cudaError_t launch_patchify(const float* px, void* patches, int dtype, int batch
   const int g = image / patch;
   const size_t n = static_cast<size_t>(batch) * g * g * 3 * patch * patch;
   if (n == 0) return cudaSuccess;
+  if (patch % 8 == 0 && image % 8 == 0 && image % patch == 0 && (reinterpret_cast<uintptr_t>(px) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(patches) & 15) == 0) {
+    const unsigned per_image = blocks_for(static_cast<size_t>(3) * image * (image / 8), 256);
+    for (int b0 = 0; b0 < batch; b0 += 65535) {  // grid.y: one image each
+      const int nb = std::min(batch - b0, 65535);
+      const size_t px_off = static_cast<size_t>(b0) * 3 * image * image;
+      const size_t out_off = static_cast<size_t>(b0) * g * g * 3 * patch * patch;
+      if (dtype == JB_DT_BF16)
+        patchify8_kernel<bf16><<<dim3(per_image, nb), 256, 0, s>>>(
+            px + px_off, static_cast<bf16*>(patches) + out_off, image, patch);
+      else
+        patchify8_kernel<float><<<dim3(per_image, nb), 256, 0, s>>>(
+            px + px_off, static_cast<float*>(patches) + out_off, image, patch);
+    }
+    return cudaGetLastError();
+  }
   if (dtype == JB_DT_BF16)
     patchify_kernel<bf16><<<blocks_for(n, 256), 256, 0, s>>>(px, static_cast<bf16*>(patches), batch,
                                                              image, patch);
