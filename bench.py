@@ -31,6 +31,13 @@ clipped to [8, 512], pre-quantised int8 weights with scales log-uniform in
 of 224x224x3, pixels N(0, 1)), and ``sharded-job-int8``: 4,194,304 rows
 (``--rows``) of lengths lognormal(4.5, 0.8) clipped to [8, 512] through the
 driver in one call over N devices (value = e2e = rows/s host to host).
+``sidecar-binary-1m``: the ANN sidecar insert on one device -- 1,048,576
+unit-norm 768-wide f32 embedding rows (1% null in the validity bitmap) into
+a Binary sidecar (jb_sidecar_add, then jb_sidecar_build: median threshold and
+sign-packing), then search_final for 64 queries (k 10, oversample 32);
+value = rows/s of add + build from device-resident rows, e2e = the same from
+pinned host rows.  The sidecar calls return when their work is done, so each
+phase is timed on the host clock around a synchronised call.
 """
 from __future__ import annotations
 
@@ -62,6 +69,8 @@ WORKLOADS = {
     "clip-vit-b32-bf16": dict(kind="image", arch="vit-b32", fmt="bf16", batch=512),
     "sharded-job-int8": dict(kind="job", arch="bert-base", fmt="int8", batch=256, seq=512,
                              dist=("lognormal", 4.5, 0.8, 8, 512), rows=4_194_304),
+    "sidecar-binary-1m": dict(kind="sidecar", rows=1_048_576, dim=768, null_frac=0.01, queries=64,
+                              k=10, oversample=32),
 }
 DEFAULT_WORKLOAD = "bert-base-int8-s256"
 POOL_BATCHES = 8      # distinct resident input batches cycled through the timed steps
@@ -705,6 +714,124 @@ def run_job(args, wl, n, torch):
     return line
 
 
+def _sidecar_phases(L, lib, vectors_ptr, bits_ptr, rows, dim, q_ptr, nq, k, over, keys, dist):
+    """One sidecar step through the C ABI; seconds of (add, build, search)."""
+    import ctypes
+    h = ctypes.c_void_p()
+    L.check(lib.jb_sidecar_create(0, dim, 3, ctypes.byref(h)))
+    try:
+        added = ctypes.c_int64()
+        t0 = time.perf_counter()
+        L.check(lib.jb_sidecar_add(h, vectors_ptr, bits_ptr, rows, None, ctypes.byref(added)))
+        t1 = time.perf_counter()
+        L.check(lib.jb_sidecar_build(h, 1, None))
+        t2 = time.perf_counter()
+        L.check(lib.jb_sidecar_search_final(h, q_ptr, nq, k, over, keys.ctypes.data, dist.ctypes.data))
+        t3 = time.perf_counter()
+    finally:
+        lib.jb_sidecar_free(h)
+    return t1 - t0, t2 - t1, t3 - t2, added.value
+
+
+def run_sidecar(args, wl, n, torch):
+    """The ANN sidecar insert (write_batch -> add -> build) and search_final."""
+    from jammi_b200 import _lib as L
+    if n != 1:
+        raise SystemExit("the sidecar workload runs on one device")
+    lib = L.lib()
+    rows, dim, nq, k, over = wl["rows"], wl["dim"], wl["queries"], wl["k"], wl["oversample"]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    vec = torch.randn((rows, dim), generator=g, device=dev, dtype=torch.float32)
+    vec /= vec.norm(dim=1, keepdim=True)
+    ok = np.random.default_rng(12).random(rows) >= wl["null_frac"]
+    bits = np.packbits(ok, bitorder="little")
+    bits_d = torch.from_numpy(bits).to(dev)
+    q = (vec[:nq] + 0.05 * torch.randn((nq, dim), generator=g, device=dev)).contiguous()
+    keys = np.empty((nq, k), np.int64)
+    dist = np.empty((nq, k), np.float32)
+    torch.cuda.synchronize()
+
+    def leg(vp, bp, qp, steps, warmup):
+        out = []
+        for i in range(warmup + steps):
+            r = _sidecar_phases(L, lib, vp, bp, rows, dim, qp, nq, k, over, keys, dist)
+            if i >= warmup:
+                out.append(r)
+        return out
+
+    clocks = ClockSampler([0])
+    clocks.start()
+    clocks.mark()
+    dev_leg = leg(vec.data_ptr(), bits_d.data_ptr(), q.data_ptr(), args.steps, args.warmup)
+    clocks.mark()
+    clk = clocks.stop()
+    valid = dev_leg[0][3]
+    assert valid == int(ok.sum())
+    h_vec = vec.cpu().pin_memory()
+    h_bits = torch.from_numpy(bits).pin_memory()
+    h_q = q.cpu().pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+    host_leg = leg(h_vec.data_ptr(), h_bits.data_ptr(), h_q.data_ptr(), e2e_steps, 2)
+    med = lambda xs: statistics.median(xs)
+    t_add, t_build, t_search = (med([r[i] for r in dev_leg]) for i in range(3))
+    h_add, h_build, h_search = (med([r[i] for r in host_leg]) for i in range(3))
+    # algorithmic bytes of add + build: read every input row, write the valid
+    # ones to the store, read the store back for the codes, write the codes,
+    # read the threshold sample once
+    nb = (dim + 7) // 8
+    sample = min(valid, 100_000)
+    alg = rows * 4 * dim + valid * (4 * dim + 4 * dim + nb) + sample * 4 * dim
+    peaks, src = load_peaks()
+    ach = alg / (t_add + t_build) / 1e9
+    line = {
+        "metric": "sidecar rows/sec", "value": rows / (t_add + t_build), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * (t_add + t_build),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32/u8",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "rows": rows, "dim": dim, "valid_rows": valid,
+                   "precision": "binary", "threshold": "median", "queries": nq, "k": k, "oversample": over,
+                   "l2": f"{rows * dim * 4 / 1e9:.1f} GB of rows per step, larger than L2",
+                   "timing": "host clock around each synchronised C-ABI call; median over steps"},
+        "phases_ms": {"add": 1e3 * t_add, "build": 1e3 * t_build, "search_final": 1e3 * t_search},
+        "search_final_queries_per_s": nq / t_search,
+        "e2e": {"value": rows / (h_add + h_build), "unit": "rows/s", "h2d_bytes_per_step": rows * dim * 4 +
+                len(bits) + nq * dim * 4, "d2h_bytes_per_step": nq * k * 12,
+                "phases_ms": {"add": 1e3 * h_add, "build": 1e3 * h_build, "search_final": 1e3 * h_search},
+                "path": "jb_sidecar_add from pinned host rows + bitmap, jb_sidecar_build, "
+                        "jb_sidecar_search_final with host queries and results"},
+        # per step: add = one counter reset + (compaction, counter commit) per
+        # staging chunk of min(65536, 64 MiB / row bytes rounded down to 256)
+        # rows; build = threshold + packing; search_final = query packing,
+        # Hamming distances, top-k, rescore, order
+        "gpu_launches": args.steps * (1 + 2 * -(-rows // min(65536, (64 << 20) // (4 * dim) // 256 * 256))
+                                      + 2 + 5),
+        "roofline": {"bound": "hbm", "kernel": "add + build (compaction, threshold, sign-packing)",
+                     "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": f"{src} copy bandwidth",
+                     "bytes_per_step": alg},
+        "clocks": clk,
+    }
+    return line
+
+
+def sidecar_cpu_baseline(wl, sample_rows=65536):
+    """The oracle's insert + build (numpy, one thread for the sort) on a sample."""
+    from oracle import index as oi
+    rng = np.random.default_rng(3)
+    v = rng.standard_normal((sample_rows, wl["dim"])).astype(np.float32)
+    v /= np.linalg.norm(v, axis=1, keepdims=True)
+    bits = np.packbits(rng.random(sample_rows) >= wl["null_frac"], bitorder="little")
+    t0 = time.perf_counter()
+    store = oi.sidecar_add(v, bits)
+    tau = oi.fit_binary_threshold(store, "median")
+    oi.pack_threshold_bits(store, tau)
+    dt = time.perf_counter() - t0
+    return {"value": sample_rows / dt, "unit": "rows/s", "cores": 1, "kind": "port", "cpu": cpu_model(),
+            "sample": f"{sample_rows} rows: oracle sidecar_add + median threshold + sign-packing (numpy)"}
+
+
 def main():
     args = parse()
     wl = WORKLOADS[args.workload]
@@ -713,6 +840,15 @@ def main():
         return  # one process drives every device; the other ranks have no work
     n = max(args.gpus, 1)
     if args.impl == "reference":
+        if wl["kind"] == "sidecar":
+            cb = sidecar_cpu_baseline(wl)
+            print(json.dumps({"impl": "reference", "metric": "sidecar rows/sec", "value": cb["value"],
+                              "unit": "rows/s", "n_gpus": args.gpus, "steps": 1, "warmup": 0,
+                              "higher_is_better": True, "dtype": "f32/u8", "data": "synthetic",
+                              "config": {"workload": args.workload}, "cpu_baseline": cb, "vs_baseline": None,
+                              "e2e": {"value": cb["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
+            return
         run_reference(args, wl)
         return
     import torch
@@ -725,6 +861,11 @@ def main():
         line = run_text(args, wl, n, torch)
     elif wl["kind"] == "image":
         line = run_image(args, wl, n, torch)
+    elif wl["kind"] == "sidecar":
+        line = run_sidecar(args, wl, n, torch)
+        line["cpu_baseline"] = sidecar_cpu_baseline(wl) if not args.no_cpu_baseline else None
+        print(json.dumps(line), flush=True)
+        return
     else:
         line = run_job(args, wl, n, torch)
     if args.quick:

@@ -409,6 +409,68 @@ jb_status jb_op_exact_search(const float* d_corpus, int64_t n, int dim, const ui
                              const float* d_queries, int n_queries, int k, float* d_scratch,
                              int64_t* d_idx, float* d_dist, void* stream);
 
+/* ── ANN sidecar insert and search (device-resident SidecarIndex) ─────────
+ * A sidecar index whose vector store lives on one device, fed straight from
+ * the embedding job's output.  Keys are internal ids 0, 1, 2, ... in add
+ * order (the reference's usearch key = position in row_map); the caller
+ * keeps the key -> _row_id map.  Every pointer argument may be host
+ * (pageable or pinned) or device memory.  Calls on one handle are
+ * serialised by its lock and run on its own stream; each returns when its
+ * work is done.
+ * jb_sidecar_create: SidecarIndex::new (crates/jammi-db/src/index/
+ *   sidecar.rs:407-430) for `dim`-wide vectors at JB_STORAGE_F32 or
+ *   JB_STORAGE_BINARY (StoragePrecision, crates/jammi-db/src/config.rs:
+ *   455-469; F16 and Int8 are quantised inside the graph library and answer
+ *   JB_ERR_INVALID).
+ * jb_sidecar_add: ResultSink::write_batch (crates/jammi-ai/src/pipeline/
+ *   result_sink.rs:61-83) feeding SidecarIndex::add (sidecar.rs:754-790) --
+ *   the rows of vectors [rows, dim] whose bit in `validity` is set
+ *   (LSB-first, the bitmap jb_generate_embeddings writes; NULL = every row)
+ *   are appended in row order; *first_key / *added (either may be NULL)
+ *   receive the first key given and how many rows were taken.  An add after
+ *   a build clears it (and its tie ranks): build again before searching a
+ *   Binary sidecar.
+ * jb_sidecar_build: SidecarIndex::build (sidecar.rs:792-824) -- a Binary
+ *   sidecar fits tau over its first min(len, 100000) vectors
+ *   (JB_THRESHOLD_MEAN / JB_THRESHOLD_MEDIAN; the reference builds with the
+ *   median) and sign-packs every vector against it.  tie_rank [len] (NULL =
+ *   key order) is each key's position in ascending _row_id order, the order
+ *   the reference breaks equal distances in; ranks must be distinct.
+ * jb_sidecar_search: SidecarIndex::search (sidecar.rs:826-864) for
+ *   n_queries queries [n_queries, dim] -> keys int64 / dist f32
+ *   [n_queries, k], nearest first: Binary by Hamming distance (differing
+ *   bits of the codes, as f32), F32 by cosine distance (crates/jammi-
+ *   numerics/src/distance.rs:6-21, bit-identical).  Every key is scanned,
+ *   so the result is the exact k nearest (the reference's usearch HNSW
+ *   graph returns approximate ones).  Slots past len hold -1 / +inf.
+ *   k <= 1024.
+ * jb_sidecar_search_final: SegmentedIndex::search_final (crates/jammi-db/
+ *   src/index/segment.rs:239-264) -- an F32 sidecar answers as
+ *   jb_sidecar_search; a Binary one retrieves k x oversample candidates
+ *   (at least k; oversample below 1 counts as 1, the reference's Binary
+ *   default is 32) by Hamming distance, rescores each with the exact cosine
+ *   distance to its stored f32 vector and keeps the k best under (distance
+ *   in f32 total order, tie rank).  k x oversample <= 1024.
+ * jb_sidecar_export: the bundle's vector files -- exact f32 vectors
+ *   [len, dim] in key order (the .rawf32 rescore companion, sidecar.rs:
+ *   262-281), the codes [len, ceil(dim / 8)] each key would be inserted into
+ *   a usearch b1x8 graph with (sidecar.rs:806-815) and tau [dim] (the
+ *   .threshold companion); NULL skips one.  Codes and tau exist only for a
+ *   built Binary sidecar with at least one vector. */
+enum { JB_STORAGE_F32 = 0, JB_STORAGE_BINARY = 3 };
+typedef struct jb_sidecar jb_sidecar;
+jb_status jb_sidecar_create(int device, int dim, int precision, jb_sidecar** out);
+jb_status jb_sidecar_add(jb_sidecar* sidecar, const float* vectors, const uint8_t* validity, int64_t rows,
+                         int64_t* first_key, int64_t* added);
+jb_status jb_sidecar_build(jb_sidecar* sidecar, int threshold_kind, const uint32_t* tie_rank);
+int64_t jb_sidecar_len(const jb_sidecar* sidecar);
+jb_status jb_sidecar_search(jb_sidecar* sidecar, const float* queries, int n_queries, int k, int64_t* keys,
+                            float* dist);
+jb_status jb_sidecar_search_final(jb_sidecar* sidecar, const float* queries, int n_queries, int k,
+                                  int oversample, int64_t* keys, float* dist);
+jb_status jb_sidecar_export(jb_sidecar* sidecar, float* exact, uint8_t* codes, float* tau);
+void jb_sidecar_free(jb_sidecar* sidecar);
+
 /* ── tokenizer (host) ─────────────────────────────────────────────────────
  * A model's tokenizer.json through the HuggingFace `tokenizers` pipeline the
  * reference runs in TokenizerWrapper (crates/jammi-ai/src/model/

@@ -338,4 +338,11 @@ cudaError_t launch_exact_search(const float* corpus, int64_t n, int dim, const u
   return cudaGetLastError();
 }
 
+cudaError_t launch_topk(const float* dist, int64_t n, const uint32_t* tie_rank, int nq, int k,
+                        int64_t* out_idx, float* out_dist, int* err, cudaStream_t s) {
+  if (nq <= 0 || k <= 0) return cudaSuccess;
+  topk_kernel<<<nq, kTopkThreads, 0, s>>>(dist, n, tie_rank, k, out_idx, out_dist, err);
+  return cudaGetLastError();
+}
+
 }  // namespace jb

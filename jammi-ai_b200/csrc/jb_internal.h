@@ -128,6 +128,10 @@ cudaError_t launch_pack_threshold_bits(const float* v, int64_t rows, int dim, co
 cudaError_t launch_exact_search(const float* corpus, int64_t n, int dim, const uint32_t* tie_rank,
                                 const float* queries, int nq, int k, float* scratch, int64_t* out_idx,
                                 float* out_dist, int* err, cudaStream_t s);
+// The k smallest of each row of dist f32 [nq, n] under (distance, tie rank),
+// the selection stage of launch_exact_search on its own.
+cudaError_t launch_topk(const float* dist, int64_t n, const uint32_t* tie_rank, int nq, int k,
+                        int64_t* out_idx, float* out_dist, int* err, cudaStream_t s);
 
 cudaError_t launch_pool_normalize(const void* hidden, int dtype, const int* cu, float* out,
                                   int batch, int H, int pooling, cudaStream_t s);

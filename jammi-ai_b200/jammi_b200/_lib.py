@@ -96,6 +96,14 @@ _SIGS = [
     ("jb_op_fit_binary_threshold", _I, [_P, ctypes.c_int64, _I, _I, _P, _P]),
     ("jb_op_pack_threshold_bits", _I, [_P, ctypes.c_int64, _I, _P, _P, _P]),
     ("jb_op_exact_search", _I, [_P, ctypes.c_int64, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
+    ("jb_sidecar_create", _I, [_I, _I, _I, ctypes.POINTER(_P)]),
+    ("jb_sidecar_add", _I, [_P, _P, _P, ctypes.c_int64, _P, _P]),
+    ("jb_sidecar_build", _I, [_P, _I, _P]),
+    ("jb_sidecar_len", ctypes.c_int64, [_P]),
+    ("jb_sidecar_search", _I, [_P, _P, _I, _I, _P, _P]),
+    ("jb_sidecar_search_final", _I, [_P, _P, _I, _I, _I, _P, _P]),
+    ("jb_sidecar_export", _I, [_P, _P, _P, _P]),
+    ("jb_sidecar_free", None, [_P]),
     ("jb_scheduler_new", _P, [ctypes.c_uint64, ctypes.c_double]),
     ("jb_scheduler_new_unlimited", _P, []),
     ("jb_scheduler_for_device", _P, [_I, ctypes.c_double]),

@@ -17,6 +17,18 @@ oracle only: tests and the checker import it, the library never does).
 * ``exact_search`` -- exact_vector_search, crates/jammi-db/src/index/
   exact.rs:119-175: the k smallest distances, ties broken by ascending
   _row_id (here: a caller-given rank per row, row order by default).
+* ``sidecar_add`` -- ResultSink::write_batch (crates/jammi-ai/src/pipeline/
+  result_sink.rs:61-83) feeding SidecarIndex::add (sidecar.rs:754-790): the
+  rows whose validity bit is set, in row order, one key each.
+* ``hamming_distances`` / ``sidecar_search`` -- SidecarIndex::search
+  (sidecar.rs:826-864): a Binary sidecar compares the query's threshold code
+  with every key's code by differing bits (usearch's Hamming metric over
+  b1x8); an F32 one by cosine distance.  The k nearest under (distance,
+  rank), scanning every key (the reference's HNSW graph approximates this).
+* ``search_final`` -- SegmentedIndex::search_final (crates/jammi-db/src/
+  index/segment.rs:239-264): k x oversample (at least k) candidates by
+  search, each rescored by cosine distance to its exact vector, ordered by
+  (distance under f32::total_cmp, rank), truncated to k.
 """
 from __future__ import annotations
 
@@ -106,3 +118,71 @@ def cosine_distance_loop(a, b) -> np.float32:
     if denom < F32_EPS:
         return np.float32(1.0)
     return np.float32(np.float32(1.0) - np.float32(dot / denom))
+
+
+def sidecar_add(vectors: np.ndarray, validity=None) -> np.ndarray:
+    """The rows of ``vectors`` [rows, dim] whose bit in the LSB-first
+    ``validity`` bitmap is set (None = all), in row order."""
+    v = np.asarray(vectors, np.float32)
+    if validity is None:
+        return v.copy()
+    bits = np.unpackbits(np.asarray(validity, np.uint8), bitorder="little")[: v.shape[0]].astype(bool)
+    return v[bits]
+
+
+def hamming_distances(qcode: np.ndarray, codes: np.ndarray) -> np.ndarray:
+    """Differing bits of one packed query code and every packed row code."""
+    x = np.bitwise_xor(np.asarray(codes, np.uint8), np.asarray(qcode, np.uint8)[None, :])
+    return np.unpackbits(x, axis=1).sum(axis=1).astype(np.float32)
+
+
+def _order(dist: np.ndarray, rank: np.ndarray, kk: int, total_order: bool) -> np.ndarray:
+    key = total_keys(dist) if total_order else total_keys(dist + np.float32(0.0))
+    return np.lexsort((rank, key))[:kk]
+
+
+def sidecar_search(store: np.ndarray, queries: np.ndarray, k: int, precision: str = "binary",
+                   tau=None, tie_rank=None):
+    """(keys int64 [q, k], dist f32 [q, k]) with -1 / +inf past the store's
+    length.  ``store`` is the exact f32 vectors in key order."""
+    store = np.asarray(store, np.float32)
+    n = store.shape[0]
+    rank = np.arange(n, dtype=np.int64) if tie_rank is None else np.asarray(tie_rank, np.int64)
+    keys = np.full((len(queries), k), -1, np.int64)
+    dist = np.full((len(queries), k), np.inf, np.float32)
+    kk = min(k, n)
+    if kk == 0:
+        return keys, dist
+    codes = pack_threshold_bits(store, tau) if precision == "binary" else None
+    for j, q in enumerate(np.asarray(queries, np.float32)):
+        if precision == "binary":
+            d = hamming_distances(pack_threshold_bits(q[None, :], tau)[0], codes)
+        else:
+            d = cosine_distances(q, store)
+        o = _order(d, rank, kk, total_order=False)
+        keys[j, :kk], dist[j, :kk] = o, d[o]
+    return keys, dist
+
+
+def search_final(store: np.ndarray, queries: np.ndarray, k: int, oversample: int, tau=None,
+                 precision: str = "binary", tie_rank=None):
+    """segment.rs:239-264 over one segment: an exact (F32) store answers as
+    its search; a Binary one retrieves candidate_k = max(k * oversample, k)
+    by Hamming distance, rescores by cosine distance and keeps k."""
+    if precision != "binary":
+        return sidecar_search(store, queries, k, precision, tau, tie_rank)
+    store = np.asarray(store, np.float32)
+    n = store.shape[0]
+    rank = np.arange(n, dtype=np.int64) if tie_rank is None else np.asarray(tie_rank, np.int64)
+    ck = max(k * max(oversample, 1), k)
+    cand, _ = sidecar_search(store, queries, ck, "binary", tau, tie_rank)
+    keys = np.full((len(queries), k), -1, np.int64)
+    dist = np.full((len(queries), k), np.inf, np.float32)
+    for j, q in enumerate(np.asarray(queries, np.float32)):
+        c = cand[j][cand[j] >= 0]
+        if len(c) == 0:
+            continue
+        d = cosine_distances(q, store[c])
+        o = _order(d, rank[c], min(k, len(c)), total_order=True)
+        keys[j, :len(o)], dist[j, :len(o)] = c[o], d[o]
+    return keys, dist

@@ -87,3 +87,22 @@ def test_ctypes_structs_match_the_header(tmp_path):
             _lib.ModelInfo.preprocess_std.offset, ctypes.sizeof(GenerateOpts),
             ctypes.sizeof(GenerateStats)]
     assert got == want, (got, want)
+
+
+def test_sidecar_without_gpu_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from jammi_b200._lib import JbError, ERR_NO_DEVICE, ERR_INVALID, lib
+    from jammi_b200.sidecar import SidecarIndex
+    with pytest.raises(JbError) as e:
+        SidecarIndex(64, "binary")
+    assert e.value.status == ERR_NO_DEVICE
+    with pytest.raises(ValueError):
+        SidecarIndex(64, "int8")  # quantised inside the graph library: not a device sidecar
+    h = ctypes.c_void_p()
+    assert lib().jb_sidecar_create(0, 64, 1, ctypes.byref(h)) == ERR_INVALID  # F16: refused before any device call
+    assert lib().jb_sidecar_create(0, 0, 3, ctypes.byref(h)) == ERR_INVALID
+    assert lib().jb_sidecar_len(None) == -1
+    assert lib().jb_sidecar_add(None, None, None, 0, None, None) == ERR_INVALID
+    lib().jb_sidecar_free(None)
