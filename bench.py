@@ -34,9 +34,9 @@ driver in one call over N devices (value = e2e = rows/s host to host).
 ``sidecar-binary-1m``: the ANN sidecar insert on one device -- 1,048,576
 unit-norm 768-wide f32 embedding rows (1% null in the validity bitmap) into
 a Binary sidecar (jb_sidecar_add, then jb_sidecar_build: median threshold and
-sign-packing), then search_final for 64 queries (k 10, oversample 32);
-value = rows/s of add + build from device-resident rows, e2e = the same from
-pinned host rows.  The sidecar calls return when their work is done, so each
+sign-packing); value = rows/s of create + add + build from device-resident
+rows, e2e = the same from pinned host rows.  search_final for 64 queries
+(k 10, oversample 32) is timed on one built sidecar.  The sidecar calls return when their work is done, so each
 phase is timed on the host clock around a synchronised call.
 """
 from __future__ import annotations
@@ -714,8 +714,9 @@ def run_job(args, wl, n, torch):
     return line
 
 
-def _sidecar_phases(L, lib, vectors_ptr, bits_ptr, rows, dim, q_ptr, nq, k, over, keys, dist):
-    """One sidecar step through the C ABI; seconds of (add, build, search)."""
+def _sidecar_insert(L, lib, vectors_ptr, bits_ptr, rows, dim, keep=False):
+    """One insert step through the C ABI (create, add, build); seconds of
+    (add, build), the valid row count and the handle when kept."""
     import ctypes
     h = ctypes.c_void_p()
     L.check(lib.jb_sidecar_create(0, dim, 3, ctypes.byref(h)))
@@ -726,11 +727,24 @@ def _sidecar_phases(L, lib, vectors_ptr, bits_ptr, rows, dim, q_ptr, nq, k, over
         t1 = time.perf_counter()
         L.check(lib.jb_sidecar_build(h, 1, None))
         t2 = time.perf_counter()
-        L.check(lib.jb_sidecar_search_final(h, q_ptr, nq, k, over, keys.ctypes.data, dist.ctypes.data))
-        t3 = time.perf_counter()
-    finally:
+    except BaseException:
         lib.jb_sidecar_free(h)
-    return t1 - t0, t2 - t1, t3 - t2, added.value
+        raise
+    if not keep:
+        lib.jb_sidecar_free(h)
+        h = None
+    return t1 - t0, t2 - t1, added.value, h
+
+
+def _sidecar_search(L, lib, h, q_ptr, nq, k, over, keys, dist, steps, warmup):
+    """Median seconds of one search_final call of nq queries on a built handle."""
+    ts = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        L.check(lib.jb_sidecar_search_final(h, q_ptr, nq, k, over, keys.ctypes.data, dist.ctypes.data))
+        if i >= warmup:
+            ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
 
 
 def run_sidecar(args, wl, n, torch):
@@ -752,10 +766,10 @@ def run_sidecar(args, wl, n, torch):
     dist = np.empty((nq, k), np.float32)
     torch.cuda.synchronize()
 
-    def leg(vp, bp, qp, steps, warmup):
+    def leg(vp, bp, steps, warmup):
         out = []
         for i in range(warmup + steps):
-            r = _sidecar_phases(L, lib, vp, bp, rows, dim, qp, nq, k, over, keys, dist)
+            r = _sidecar_insert(L, lib, vp, bp, rows, dim)
             if i >= warmup:
                 out.append(r)
         return out
@@ -763,19 +777,27 @@ def run_sidecar(args, wl, n, torch):
     clocks = ClockSampler([0])
     clocks.start()
     clocks.mark()
-    dev_leg = leg(vec.data_ptr(), bits_d.data_ptr(), q.data_ptr(), args.steps, args.warmup)
+    dev_leg = leg(vec.data_ptr(), bits_d.data_ptr(), args.steps, args.warmup)
     clocks.mark()
     clk = clocks.stop()
-    valid = dev_leg[0][3]
+    valid = dev_leg[0][2]
     assert valid == int(ok.sum())
     h_vec = vec.cpu().pin_memory()
     h_bits = torch.from_numpy(bits).pin_memory()
     h_q = q.cpu().pin_memory()
     e2e_steps = max(3, min(args.steps, 10))
-    host_leg = leg(h_vec.data_ptr(), h_bits.data_ptr(), h_q.data_ptr(), e2e_steps, 2)
+    host_leg = leg(h_vec.data_ptr(), h_bits.data_ptr(), e2e_steps, 2)
     med = lambda xs: statistics.median(xs)
-    t_add, t_build, t_search = (med([r[i] for r in dev_leg]) for i in range(3))
-    h_add, h_build, h_search = (med([r[i] for r in host_leg]) for i in range(3))
+    t_add, t_build = (med([r[i] for r in dev_leg]) for i in range(2))
+    h_add, h_build = (med([r[i] for r in host_leg]) for i in range(2))
+    # search_final on one built sidecar (a service's steady state): device
+    # queries and host results, then host queries and host results
+    _, _, _, h = _sidecar_insert(L, lib, vec.data_ptr(), bits_d.data_ptr(), rows, dim, keep=True)
+    try:
+        t_search = _sidecar_search(L, lib, h, q.data_ptr(), nq, k, over, keys, dist, 20, 3)
+        h_search = _sidecar_search(L, lib, h, h_q.data_ptr(), nq, k, over, keys, dist, 20, 3)
+    finally:
+        lib.jb_sidecar_free(h)
     # algorithmic bytes of add + build: read every input row, write the valid
     # ones to the store, read the store back for the codes, write the codes,
     # read the threshold sample once
@@ -800,12 +822,11 @@ def run_sidecar(args, wl, n, torch):
                 "phases_ms": {"add": 1e3 * h_add, "build": 1e3 * h_build, "search_final": 1e3 * h_search},
                 "path": "jb_sidecar_add from pinned host rows + bitmap, jb_sidecar_build, "
                         "jb_sidecar_search_final with host queries and results"},
-        # per step: add = one counter reset + (compaction, counter commit) per
-        # staging chunk of min(65536, 64 MiB / row bytes rounded down to 256)
-        # rows; build = threshold + packing; search_final = query packing,
-        # Hamming distances, top-k, rescore, order
-        "gpu_launches": args.steps * (1 + 2 * -(-rows // min(65536, (64 << 20) // (4 * dim) // 256 * 256))
-                                      + 2 + 5),
+        # per insert step: add = one counter reset + (compaction, counter
+        # commit) per chunk of 131072 rows (device-resident rows are read in
+        # place); build = the median threshold (init, four passes of histogram
+        # + select, final) + packing
+        "gpu_launches": args.steps * (1 + 2 * -(-rows // 131072) + (1 + 4 * 2 + 1) + 1),
         "roofline": {"bound": "hbm", "kernel": "add + build (compaction, threshold, sign-packing)",
                      "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / peaks["hbm_gbs"], "traffic": None,

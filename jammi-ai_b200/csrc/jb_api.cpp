@@ -608,8 +608,16 @@ jb_status jb_op_fit_binary_threshold(const float* d_vectors, int64_t rows, int d
     if (rows < 0 || dim < 0 || (kind != JB_THRESHOLD_MEAN && kind != JB_THRESHOLD_MEDIAN))
       jb::fail(JB_ERR_INVALID, "jb_op_fit_binary_threshold: bad argument");
     if (dim > 0 && (!d_tau || (rows > 0 && !d_vectors))) jb::fail(JB_ERR_INVALID, "jb_op_fit_binary_threshold: null buffer");
-    jb::check_cuda(jb::launch_fit_binary_threshold(d_vectors, rows, dim, kind, d_tau, as_stream(stream)),
-                   "jb_op_fit_binary_threshold");
+    // the median's histograms: stream-ordered scratch, released behind the launches
+    void* scratch = nullptr;
+    const bool median = kind == JB_THRESHOLD_MEDIAN && rows > 0 && dim > 0;
+    if (median)
+      jb::check_cuda(cudaMallocAsync(&scratch, jb::fit_threshold_scratch_bytes(dim), as_stream(stream)),
+                     "jb_op_fit_binary_threshold: scratch");
+    const cudaError_t e = jb::launch_fit_binary_threshold(d_vectors, rows, dim, kind, d_tau, scratch,
+                                                          as_stream(stream));
+    if (scratch) cudaFreeAsync(scratch, as_stream(stream));
+    jb::check_cuda(e, "jb_op_fit_binary_threshold");
   });
 }
 

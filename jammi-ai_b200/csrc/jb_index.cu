@@ -23,6 +23,7 @@
 //   caller passes each row's rank in that order, or none for row order --
 //   come from a radix select over 64-bit (distance key, rank) keys, then a
 //   rank sort of the k survivors.
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 
@@ -62,79 +63,144 @@ __global__ void mean_threshold_kernel(const float* __restrict__ v, int64_t rows,
   tau[d] = __double2float_rn(__ddiv_rn(s, n));
 }
 
-constexpr int kMedWarps = 16;
+// Median: a radix select over f32 total-order keys, four 8-bit passes, the
+// two central order statistics of an even count side by side.  Each pass is
+// two launches: median_hist_kernel spreads the rows over a grid of
+// (32-dimension groups) x (row splits); each CTA histograms the next byte of
+// the keys that match each statistic's prefix so far, in shared memory laid
+// out [statistic][bin][lane] (lane = dimension: no two lanes of a warp share
+// a word), then adds its non-zero bins to the global histograms.
+// median_select_kernel then has one thread per (statistic, dimension) scan
+// its 256 bins for the bin holding its remaining rank, extend the prefix and
+// clear the histogram for the next pass.  Exact by construction.
+constexpr int kMedLanes = 32;
+constexpr int kMedThreads = 256;
+constexpr int kMedBins = 256;
 
-// One CTA per 32 dimensions (lane l owns dimension d0 + l); the warps split
-// the rows.  For each wanted order statistic, four 8-bit passes narrow the
-// key prefix: a shared histogram per lane of the keys that match the prefix
-// so far, then lane l's scan picks the bin holding its remaining rank.
-__global__ void __launch_bounds__(32 * kMedWarps)
-median_threshold_kernel(const float* __restrict__ v, int64_t rows, int dim, float* __restrict__ tau) {
-  __shared__ uint32_t hist[32][257];
-  __shared__ uint32_t s_prefix[32], s_mask[32];
-  __shared__ int64_t s_remaining[32];
-  __shared__ float s_value[2][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int d = blockIdx.x * 32 + lane;
-  const bool live = d < dim;
+struct MedianScratch {
+  uint32_t* hist;       // [2][dim][256]
+  uint32_t* prefix;     // [2][dim]
+  int64_t* remaining;   // [2][dim]
+};
+
+size_t median_scratch_bytes_(int dim) {
+  return size_t(2) * dim * kMedBins * sizeof(uint32_t) + size_t(2) * dim * sizeof(uint32_t) +
+         size_t(2) * dim * sizeof(int64_t) + 64;
+}
+
+MedianScratch carve_median(void* p, int dim) {
+  MedianScratch m;
+  char* c = static_cast<char*>(p);
+  m.remaining = reinterpret_cast<int64_t*>(c);
+  c += size_t(2) * dim * sizeof(int64_t);
+  m.hist = reinterpret_cast<uint32_t*>(c);
+  c += size_t(2) * dim * kMedBins * sizeof(uint32_t);
+  m.prefix = reinterpret_cast<uint32_t*>(c);
+  return m;
+}
+
+__global__ void median_init_kernel(int dim, int64_t rows, int nstats, MedianScratch m) {
+  const int64_t total = int64_t(2) * dim * kMedBins;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
+    m.hist[i] = 0;
   const int64_t mid = rows / 2;
-  const int n_stats = (rows % 2 == 0) ? 2 : 1;
-  for (int st = 0; st < n_stats; ++st) {
-    // 0-based rank: mid - 1 and mid for an even count, mid for an odd one
-    const int64_t rank = (n_stats == 2 && st == 0) ? mid - 1 : mid;
-    if (warp == 0) {
-      s_prefix[lane] = 0;
-      s_mask[lane] = 0;
-      s_remaining[lane] = rank + 1;
-    }
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < 32 * 257; i += blockDim.x) (&hist[0][0])[i] = 0;
-      __syncthreads();
-      const uint32_t pfx = s_prefix[lane], msk = s_mask[lane];
-      if (live) {
-        int64_t r = warp;
-        for (; r + 3 * kMedWarps < rows; r += 4 * kMedWarps) {  // four loads in flight
-          float x[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) x[u] = __ldg(v + (r + u * kMedWarps) * dim + d);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t key = total_key(x[u]);
-            if ((key & msk) == pfx) atomicAdd(&hist[lane][(key >> shift) & 255u], 1u);
-          }
-        }
-        for (; r < rows; r += kMedWarps) {
-          const uint32_t key = total_key(__ldg(v + r * dim + d));
-          if ((key & msk) == pfx) atomicAdd(&hist[lane][(key >> shift) & 255u], 1u);
-        }
-      }
-      __syncthreads();
-      if (warp == 0 && live) {
-        int64_t cum = 0;
-        for (int b = 0; b < 256; ++b) {
-          const int64_t h = hist[lane][b];
-          if (cum + h >= s_remaining[lane]) {
-            s_prefix[lane] = pfx | (static_cast<uint32_t>(b) << shift);
-            s_mask[lane] = msk | (255u << shift);
-            s_remaining[lane] -= cum;
-            break;
-          }
-          cum += h;
-        }
-      }
-      __syncthreads();
-    }
-    if (warp == 0) s_value[st][lane] = from_total_key(s_prefix[lane]);
-    __syncthreads();
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < 2 * int64_t(dim);
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int st = static_cast<int>(i / dim);
+    m.prefix[i] = 0;
+    // 0-based ranks: mid - 1 and mid for an even count, mid for an odd one
+    const int64_t rank = (nstats == 2 && st == 0) ? mid - 1 : mid;
+    m.remaining[i] = rank + 1;
   }
-  if (warp == 0 && live) {
-    if (rows == 0)
-      tau[d] = 0.0f;
-    else
-      tau[d] = n_stats == 2 ? __fdiv_rn(__fadd_rn(s_value[0][lane], s_value[1][lane]), 2.0f)
-                            : s_value[0][lane];
+}
+
+__global__ void __launch_bounds__(kMedThreads)
+median_hist_kernel(const float* __restrict__ v, int64_t rows, int dim, int nstats, int pass,
+                   int64_t rows_per_split, MedianScratch m) {
+  extern __shared__ uint32_t h[];  // [nstats][256][32]
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int entries = nstats * kMedBins * kMedLanes;
+  for (int e = t; e < entries; e += kMedThreads) h[e] = 0;
+  __syncthreads();
+  const int d = blockIdx.x * kMedLanes + lane;
+  const int shift = 24 - 8 * pass;
+  const uint32_t mask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
+  if (d < dim) {
+    const uint32_t p0 = m.prefix[d];
+    // adjacent order statistics mostly share their prefix: one histogram then
+    const uint32_t p1 = (nstats == 2 && m.prefix[dim + d] != p0) ? m.prefix[dim + d] : 0xFFFFFFFFu;
+    const int64_t r_end = min(rows, (blockIdx.y + int64_t(1)) * rows_per_split);
+    int64_t r = blockIdx.y * rows_per_split + warp;
+    constexpr int W = kMedThreads / 32;
+    for (; r + 3 * W < r_end; r += 4 * W) {  // four loads in flight
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = __ldg(v + (r + u * W) * dim + d);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t key = total_key(x[u]);
+        const uint32_t bin = (key >> shift) & 255u;
+        if ((key & mask) == p0) atomicAdd(&h[bin * kMedLanes + lane], 1u);
+        if (p1 != 0xFFFFFFFFu && (key & mask) == p1) atomicAdd(&h[(kMedBins + bin) * kMedLanes + lane], 1u);
+      }
+    }
+    for (; r < r_end; r += W) {
+      const uint32_t key = total_key(__ldg(v + r * dim + d));
+      const uint32_t bin = (key >> shift) & 255u;
+      if ((key & mask) == p0) atomicAdd(&h[bin * kMedLanes + lane], 1u);
+      if (p1 != 0xFFFFFFFFu && (key & mask) == p1) atomicAdd(&h[(kMedBins + bin) * kMedLanes + lane], 1u);
+    }
   }
+  __syncthreads();
+  for (int e = t; e < entries; e += kMedThreads) {
+    const uint32_t c = h[e];
+    if (!c) continue;
+    const int st = e / (kMedBins * kMedLanes);
+    const int bin = (e / kMedLanes) % kMedBins;
+    const int dd = blockIdx.x * kMedLanes + (e % kMedLanes);
+    if (dd < dim) atomicAdd(&m.hist[(size_t(st) * dim + dd) * kMedBins + bin], c);
+  }
+}
+
+// One thread per dimension: each statistic scans its 256 bins (the first
+// statistic's when both shared a prefix this pass) for the bin holding its
+// remaining rank and extends its prefix; the histograms are cleared for the
+// next pass.
+__global__ void median_select_kernel(int dim, int nstats, int pass, MedianScratch m) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= dim) return;
+  const int shift = 24 - 8 * pass;
+  const bool shared = nstats == 2 && m.prefix[dim + d] == m.prefix[d];
+  for (int st = 0; st < nstats; ++st) {
+    const int i = st * dim + d;
+    const uint32_t* hh = m.hist + size_t((st == 1 && shared) ? d : i) * kMedBins;
+    const int64_t rem = m.remaining[i];
+    int64_t cum = 0;
+    for (int b = 0; b < kMedBins; ++b) {
+      const int64_t c = hh[b];
+      if (cum + c >= rem) {
+        m.prefix[i] |= static_cast<uint32_t>(b) << shift;
+        m.remaining[i] = rem - cum;
+        break;
+      }
+      cum += c;
+    }
+  }
+  for (int st = 0; st < nstats; ++st) {
+    uint32_t* hh = m.hist + (size_t(st) * dim + d) * kMedBins;
+    for (int b = 0; b < kMedBins; ++b) hh[b] = 0;
+  }
+}
+
+__global__ void median_final_kernel(int dim, int64_t rows, int nstats, MedianScratch m, float* __restrict__ tau) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= dim) return;
+  if (rows == 0) {
+    tau[d] = 0.0f;
+    return;
+  }
+  const float a = from_total_key(m.prefix[d]);
+  tau[d] = nstats == 2 ? __fdiv_rn(__fadd_rn(a, from_total_key(m.prefix[dim + d])), 2.0f) : a;
 }
 
 __global__ void pack_threshold_bits_kernel(const float* __restrict__ v, int64_t rows, int dim,
@@ -305,14 +371,35 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
 
 }  // namespace
 
+size_t fit_threshold_scratch_bytes(int dim) { return dim > 0 ? median_scratch_bytes_(dim) : 0; }
+
 cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, int kind, float* tau,
-                                        cudaStream_t s) {
+                                        void* scratch, cudaStream_t s) {
   if (dim <= 0) return cudaSuccess;
   rows = rows < kThresholdSampleCap ? rows : kThresholdSampleCap;
-  if (kind == 0)
+  if (kind == 0) {
     mean_threshold_kernel<<<(dim + 127) / 128, 128, 0, s>>>(v, rows, dim, tau);
-  else
-    median_threshold_kernel<<<(dim + 31) / 32, 32 * kMedWarps, 0, s>>>(v, rows, dim, tau);
+    return cudaGetLastError();
+  }
+  const int nstats = (rows > 0 && rows % 2 == 0) ? 2 : 1;
+  const MedianScratch m = carve_median(scratch, dim);
+  const unsigned gx = static_cast<unsigned>((dim + kMedLanes - 1) / kMedLanes);
+  if (rows > 0) {
+    median_init_kernel<<<64, 256, 0, s>>>(dim, rows, nstats, m);
+    // about two CTAs per SM over the (dimension group, row split) grid
+    const int64_t splits_want = std::max<int64_t>(1, (148 * 2 + gx - 1) / gx);
+    int64_t per = (rows + splits_want - 1) / splits_want;
+    per = std::max<int64_t>(per, 256);
+    const unsigned gy = static_cast<unsigned>((rows + per - 1) / per);
+    const int smem = nstats * kMedBins * kMedLanes * static_cast<int>(sizeof(uint32_t));
+    cudaError_t e = cudaFuncSetAttribute(median_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    for (int pass = 0; pass < 4; ++pass) {
+      median_hist_kernel<<<dim3(gx, gy), kMedThreads, smem, s>>>(v, rows, dim, nstats, pass, per, m);
+      median_select_kernel<<<(dim + 127) / 128, 128, 0, s>>>(dim, nstats, pass, m);
+    }
+  }
+  median_final_kernel<<<(dim + 127) / 128, 128, 0, s>>>(dim, rows, nstats, m, tau);
   return cudaGetLastError();
 }
 

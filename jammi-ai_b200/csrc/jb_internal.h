@@ -119,8 +119,11 @@ cudaError_t launch_flag_wait(const int* flag, int expect, int limit_ms, int* err
 // ANN sidecar vector formats and exact search (jb_index.cu).
 constexpr int64_t kThresholdSampleCap = 100000;  // rows a binary threshold is fit over
 constexpr int kMaxSearchK = 1024;
+// scratch: fit_threshold_scratch_bytes(dim) bytes of device memory (the
+// median's histograms; unused by the mean).
+size_t fit_threshold_scratch_bytes(int dim);
 cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, int kind, float* tau,
-                                        cudaStream_t s);
+                                        void* scratch, cudaStream_t s);
 cudaError_t launch_pack_threshold_bits(const float* v, int64_t rows, int dim, const float* tau,
                                        uint8_t* out, cudaStream_t s);
 // scratch: f32 [nq, n]; out_idx / out_dist [nq, k]; repeated tie ranks set

@@ -54,6 +54,8 @@ struct jb_sidecar {
   uint8_t* codes = nullptr;
   size_t codes_cap = 0;
   float* tau = nullptr;
+  unsigned char* fit = nullptr;  // threshold fit scratch
+  size_t fit_cap = 0;
   uint32_t* rank = nullptr;
   size_t rank_cap = 0;
   float* in = nullptr;  // add staging
@@ -87,7 +89,7 @@ constexpr int kHamRows = 256;
 constexpr int kHamQ = 8;
 constexpr int kHamWords = 16;
 constexpr size_t kAddChunkBytes = size_t(64) << 20;    // staging per add chunk
-constexpr int64_t kAddChunkRows = 65536;                // and at most this many rows
+constexpr int64_t kAddChunkRows = 131072;               // and at most this many rows
 constexpr size_t kScratchBytes = size_t(256) << 20;   // distance matrix per query batch
 
 __device__ __forceinline__ uint32_t total_key(float x) {
@@ -149,10 +151,19 @@ compact_rows_kernel(const float* __restrict__ in, int nr, int dim, const uint8_t
     if (p < 0) continue;
     const float* src = in + static_cast<int64_t>(r0 + j) * dim;
     float* dst = store + (base + p) * dim;
-    if (kVec4) {
+    if (kVec4) {  // four 16-byte loads in flight per lane
       const float4* s4 = reinterpret_cast<const float4*>(src);
       float4* d4 = reinterpret_cast<float4*>(dst);
-      for (int c = lane; c < dim / 4; c += 32) d4[c] = __ldg(s4 + c);
+      const int n4 = dim / 4;
+      for (int c0 = lane; c0 < n4; c0 += 32 * 4) {
+        float4 t4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < n4) t4[u] = __ldg(s4 + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < n4) d4[c0 + 32 * u] = t4[u];
+      }
     } else {
       for (int c = lane; c < dim; c += 32) dst[c] = __ldg(src + c);
     }
@@ -340,6 +351,16 @@ void fill_empty(int64_t* keys, float* dist, int64_t count) {
   }
 }
 
+// Memory of `device` itself (or managed memory): kernels there read it in place.
+bool device_resident(const void* p, int device) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return (a.type == cudaMemoryTypeDevice && a.device == device) || a.type == cudaMemoryTypeManaged;
+}
+
 bool host_memory(const void* p) {
   cudaPointerAttributes a{};
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
@@ -448,30 +469,43 @@ jb_status jb_sidecar_add(jb_sidecar* x, const float* vectors, const uint8_t* val
     cudaStream_t s = x->stream;
     const size_t row_bytes = size_t(x->dim) * sizeof(float);
     ensure(&x->exact, &x->exact_cap, size_t(x->len + rows) * row_bytes, true, s);
+    // rows (and bitmap) already in this device's memory are read in place;
+    // others are copied chunk by chunk into the staging buffers
+    const bool direct = device_resident(vectors, x->device);
+    const bool bits_direct = validity && device_resident(validity, x->device);
     // chunk: a multiple of 256 rows (whole bitmap bytes, whole CTAs)
-    int64_t chunk = int64_t(kAddChunkBytes / row_bytes) / kCompactRows * kCompactRows;
+    int64_t chunk = direct ? kAddChunkRows : int64_t(kAddChunkBytes / row_bytes) / kCompactRows * kCompactRows;
     if (chunk < kCompactRows) chunk = kCompactRows;
     if (chunk > kAddChunkRows) chunk = kAddChunkRows;  // each CTA rescans the bitmap before it
     if (chunk > rows) chunk = (rows + kCompactRows - 1) / kCompactRows * kCompactRows;
-    ensure(&x->in, &x->in_cap, size_t(chunk) * row_bytes, false, s);
-    ensure(&x->valid, &x->valid_cap, size_t(chunk / 8), false, s);
+    if (!direct) ensure(&x->in, &x->in_cap, size_t(chunk) * row_bytes, false, s);
+    if (validity && !bits_direct) ensure(&x->valid, &x->valid_cap, size_t(chunk / 8), false, s);
     set_len_kernel<<<1, 1, 0, s>>>(x->d_len, x->len);
     jb::check_cuda(cudaGetLastError(), "jb_sidecar_add");
-    const bool vec4 = x->dim % 4 == 0;
+    // 16-byte row access: a width of whole float4s and a 16-byte aligned base
+    const bool vec4 = x->dim % 4 == 0 && (!direct || reinterpret_cast<uintptr_t>(vectors) % 16 == 0);
     for (int64_t r0 = 0; r0 < rows; r0 += chunk) {
       const int nr = static_cast<int>(rows - r0 < chunk ? rows - r0 : chunk);
-      jb::check_cuda(cudaMemcpyAsync(x->in, vectors + r0 * x->dim, size_t(nr) * row_bytes, cudaMemcpyDefault, s),
-                     "jb_sidecar_add: vectors");
-      if (validity)
-        jb::check_cuda(cudaMemcpyAsync(x->valid, validity + r0 / 8, size_t(nr + 7) / 8, cudaMemcpyDefault, s),
-                       "jb_sidecar_add: validity");
+      const float* src = vectors + r0 * x->dim;
+      if (!direct) {
+        jb::check_cuda(cudaMemcpyAsync(x->in, src, size_t(nr) * row_bytes, cudaMemcpyDefault, s),
+                       "jb_sidecar_add: vectors");
+        src = x->in;
+      }
+      const uint8_t* bits = nullptr;
+      if (validity) {
+        bits = validity + r0 / 8;
+        if (!bits_direct) {
+          jb::check_cuda(cudaMemcpyAsync(x->valid, bits, size_t(nr + 7) / 8, cudaMemcpyDefault, s),
+                         "jb_sidecar_add: validity");
+          bits = x->valid;
+        }
+      }
       const unsigned blocks = static_cast<unsigned>((nr + kCompactRows - 1) / kCompactRows);
       if (vec4)
-        compact_rows_kernel<true><<<blocks, kCompactRows, 0, s>>>(x->in, nr, x->dim, validity ? x->valid : nullptr,
-                                                                  x->exact, x->d_len);
+        compact_rows_kernel<true><<<blocks, kCompactRows, 0, s>>>(src, nr, x->dim, bits, x->exact, x->d_len);
       else
-        compact_rows_kernel<false><<<blocks, kCompactRows, 0, s>>>(x->in, nr, x->dim, validity ? x->valid : nullptr,
-                                                                   x->exact, x->d_len);
+        compact_rows_kernel<false><<<blocks, kCompactRows, 0, s>>>(src, nr, x->dim, bits, x->exact, x->d_len);
       commit_len_kernel<<<1, 1, 0, s>>>(x->d_len);
       jb::check_cuda(cudaGetLastError(), "jb_sidecar_add");
     }
@@ -497,7 +531,8 @@ jb_status jb_sidecar_build(jb_sidecar* x, int threshold_kind, const uint32_t* ti
     cudaStream_t s = x->stream;
     if (x->precision == JB_STORAGE_BINARY && x->len > 0) {
       ensure(&x->codes, &x->codes_cap, size_t(x->len) * x->nb, false, s);
-      jb::check_cuda(jb::launch_fit_binary_threshold(x->exact, x->len, x->dim, threshold_kind, x->tau, s),
+      ensure(&x->fit, &x->fit_cap, jb::fit_threshold_scratch_bytes(x->dim), false, s);
+      jb::check_cuda(jb::launch_fit_binary_threshold(x->exact, x->len, x->dim, threshold_kind, x->tau, x->fit, s),
                      "jb_sidecar_build: threshold");
       jb::check_cuda(jb::launch_pack_threshold_bits(x->exact, x->len, x->dim, x->tau, x->codes, s),
                      "jb_sidecar_build: codes");
@@ -637,7 +672,7 @@ void jb_sidecar_free(jb_sidecar* x) {
   cudaGetDevice(&prev);
   if (cudaSetDevice(x->device) == cudaSuccess) {
     if (x->stream) cudaStreamSynchronize(x->stream);
-    void* bufs[] = {x->exact, x->codes,     x->tau,  x->rank,    x->in,       x->valid,  x->q,   x->qcodes,
+    void* bufs[] = {x->exact, x->codes,     x->tau,  x->fit, x->rank,    x->in,       x->valid,  x->q,   x->qcodes,
                     x->scratch, x->cand, x->cand_dist, x->resc, x->out_idx, x->out_dist, x->d_len, x->err};
     for (void* p : bufs)
       if (p) cudaFree(p);
