@@ -287,17 +287,28 @@ __device__ __forceinline__ uint64_t search_key(float d, uint32_t rank) {
   return (static_cast<uint64_t>(total_key(d)) << 32) | rank;
 }
 
+constexpr int kTopkCompact = 8192;  // keys a CTA narrows down to in shared memory
+constexpr int kTopkDynSmem = kTopkCompact * (8 + 4);
+
 // One CTA per query: the k-th smallest key by radix select (eight 8-bit
 // passes), then the keys at or below it, ordered by counting smaller keys.
+// Once a pass leaves at most kTopkCompact keys on the chosen prefix, one more
+// scan of the row moves them into shared memory (and the keys below the
+// prefix, all among the k best, straight to the candidates); the remaining
+// passes and the final gather then read shared memory only.
 __global__ void __launch_bounds__(kTopkThreads)
 topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restrict__ tie_rank, int k,
             int64_t* __restrict__ out_idx, float* __restrict__ out_dist, int* err) {
   __shared__ uint32_t hist[256];
   __shared__ uint64_t s_prefix, s_mask;
   __shared__ int64_t s_remaining;
+  __shared__ uint32_t s_bin_count;
   __shared__ uint64_t cand_key[kMaxSearchK];
   __shared__ int64_t cand_idx[kMaxSearchK];
-  __shared__ unsigned s_count;
+  __shared__ unsigned s_count, s_m;
+  extern __shared__ __align__(16) unsigned char topk_dyn[];
+  uint64_t* comp_key = reinterpret_cast<uint64_t*>(topk_dyn);             // [kTopkCompact]
+  uint32_t* comp_idx = reinterpret_cast<uint32_t*>(comp_key + kTopkCompact);  // [kTopkCompact]
   const int q = blockIdx.x, t = threadIdx.x;
   const float* dq = dist + static_cast<int64_t>(q) * n;
   const int kk = static_cast<int>(min(static_cast<int64_t>(k), n));
@@ -314,15 +325,25 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
     s_mask = 0;
     s_remaining = kk;
     s_count = 0;
+    s_m = 0;
   }
+  bool compacted = false;  // the same in every thread (decided from shared state)
   for (int pass = 0; pass < 8; ++pass) {
     const int shift = 56 - 8 * pass;
     for (int b = t; b < 256; b += blockDim.x) hist[b] = 0;
     __syncthreads();
     const uint64_t pfx = s_prefix, msk = s_mask;
-    for (int64_t i = t; i < n; i += blockDim.x) {
-      const uint64_t key = key_of(i);
-      if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    if (!compacted) {
+      for (int64_t i = t; i < n; i += blockDim.x) {
+        const uint64_t key = key_of(i);
+        if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+    } else {
+      const unsigned m = s_m;
+      for (unsigned j = t; j < m; j += blockDim.x) {
+        const uint64_t key = comp_key[j];
+        if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
     }
     __syncthreads();
     if (t == 0) {
@@ -332,21 +353,58 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
           s_prefix = pfx | (static_cast<uint64_t>(b) << shift);
           s_mask = msk | (0xFFull << shift);
           s_remaining -= cum;
+          s_bin_count = hist[b];
           break;
         }
         cum += hist[b];
       }
     }
     __syncthreads();
+    if (!compacted && pass < 7 && s_bin_count <= static_cast<uint32_t>(kTopkCompact)) {
+      const uint64_t npfx = s_prefix, nmsk = s_mask;
+      for (int64_t i = t; i < n; i += blockDim.x) {
+        const uint64_t key = key_of(i);
+        const uint64_t top = key & nmsk;
+        if (top == npfx) {
+          const unsigned slot = atomicAdd(&s_m, 1u);
+          if (slot < static_cast<unsigned>(kTopkCompact)) {
+            comp_key[slot] = key;
+            comp_idx[slot] = static_cast<uint32_t>(i);
+          }
+        } else if (top < npfx) {  // below the prefix: among the k best
+          const unsigned slot = atomicAdd(&s_count, 1u);
+          if (slot < static_cast<unsigned>(kMaxSearchK)) {
+            cand_key[slot] = key;
+            cand_idx[slot] = i;
+          }
+        }
+      }
+      compacted = true;
+      __syncthreads();
+    }
   }
   const uint64_t kth = s_prefix;
-  for (int64_t i = t; i < n; i += blockDim.x) {
-    const uint64_t key = key_of(i);
-    if (key <= kth) {
-      const unsigned slot = atomicAdd(&s_count, 1u);
-      if (slot < static_cast<unsigned>(kMaxSearchK)) {
-        cand_key[slot] = key;
-        cand_idx[slot] = i;
+  if (compacted) {
+    const unsigned m = s_m;
+    for (unsigned j = t; j < m; j += blockDim.x) {
+      const uint64_t key = comp_key[j];
+      if (key <= kth) {
+        const unsigned slot = atomicAdd(&s_count, 1u);
+        if (slot < static_cast<unsigned>(kMaxSearchK)) {
+          cand_key[slot] = key;
+          cand_idx[slot] = comp_idx[j];
+        }
+      }
+    }
+  } else {
+    for (int64_t i = t; i < n; i += blockDim.x) {
+      const uint64_t key = key_of(i);
+      if (key <= kth) {
+        const unsigned slot = atomicAdd(&s_count, 1u);
+        if (slot < static_cast<unsigned>(kMaxSearchK)) {
+          cand_key[slot] = key;
+          cand_idx[slot] = i;
+        }
       }
     }
   }
@@ -421,14 +479,18 @@ cudaError_t launch_exact_search(const float* corpus, int64_t n, int dim, const u
     const dim3 grid(static_cast<unsigned>((n + kDistRows - 1) / kDistRows), (nq + kDistQ - 1) / kDistQ);
     cosine_distance_kernel<<<grid, kDistRows, 0, s>>>(corpus, n, dim, queries, nq, scratch);
   }
-  topk_kernel<<<nq, kTopkThreads, 0, s>>>(scratch, n, tie_rank, k, out_idx, out_dist, err);
+  const cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkDynSmem);
+  if (e != cudaSuccess) return e;
+  topk_kernel<<<nq, kTopkThreads, kTopkDynSmem, s>>>(scratch, n, tie_rank, k, out_idx, out_dist, err);
   return cudaGetLastError();
 }
 
 cudaError_t launch_topk(const float* dist, int64_t n, const uint32_t* tie_rank, int nq, int k,
                         int64_t* out_idx, float* out_dist, int* err, cudaStream_t s) {
   if (nq <= 0 || k <= 0) return cudaSuccess;
-  topk_kernel<<<nq, kTopkThreads, 0, s>>>(dist, n, tie_rank, k, out_idx, out_dist, err);
+  const cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkDynSmem);
+  if (e != cudaSuccess) return e;
+  topk_kernel<<<nq, kTopkThreads, kTopkDynSmem, s>>>(dist, n, tie_rank, k, out_idx, out_dist, err);
   return cudaGetLastError();
 }
 
