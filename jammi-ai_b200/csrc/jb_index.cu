@@ -51,12 +51,12 @@ __global__ void mean_threshold_kernel(const float* __restrict__ v, int64_t rows,
   const float* p = v + d;
   double s = 0.0;
   int64_t r = 0;
-  for (; r + 8 <= rows; r += 8) {
-    float x[8];
+  for (; r + 16 <= rows; r += 16) {  // sixteen loads in flight, the additions in row order
+    float x[16];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = __ldg(p + (r + u) * dim);
+    for (int u = 0; u < 16; ++u) x[u] = __ldg(p + (r + u) * dim);
 #pragma unroll
-    for (int u = 0; u < 8; ++u) s = __dadd_rn(s, static_cast<double>(x[u]));
+    for (int u = 0; u < 16; ++u) s = __dadd_rn(s, static_cast<double>(x[u]));
   }
   for (; r < rows; ++r) s = __dadd_rn(s, static_cast<double>(__ldg(p + r * dim)));
   const double n = rows > 0 ? static_cast<double>(rows) : 1.0;
