@@ -315,6 +315,25 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
   auto key_of = [&](int64_t i) {
     return search_key(dq[i], tie_rank ? tie_rank[i] : static_cast<uint32_t>(i));
   };
+  // f(key, index) over the whole row, eight independent loads in flight per
+  // thread (one CTA streams the row alone: latency, not bandwidth, bounds it)
+  auto scan_row = [&](auto&& f) {
+    constexpr int U = 8;
+    const int64_t step = blockDim.x;
+    int64_t i = t;
+    for (; i + (U - 1) * step < n; i += U * step) {
+      float d[U];
+      uint32_t rk[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) d[u] = __ldg(dq + i + u * step);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        rk[u] = tie_rank ? __ldg(tie_rank + i + u * step) : static_cast<uint32_t>(i + u * step);
+#pragma unroll
+      for (int u = 0; u < U; ++u) f(search_key(d[u], rk[u]), i + u * step);
+    }
+    for (; i < n; i += step) f(key_of(i), i);
+  };
   for (int s = kk + t; s < k; s += blockDim.x) {
     out_idx[static_cast<int64_t>(q) * k + s] = -1;
     out_dist[static_cast<int64_t>(q) * k + s] = __uint_as_float(0x7F800000u);
@@ -333,17 +352,14 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
     for (int b = t; b < 256; b += blockDim.x) hist[b] = 0;
     __syncthreads();
     const uint64_t pfx = s_prefix, msk = s_mask;
+    auto count = [&](uint64_t key, int64_t) {
+      if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    };
     if (!compacted) {
-      for (int64_t i = t; i < n; i += blockDim.x) {
-        const uint64_t key = key_of(i);
-        if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-      }
+      scan_row(count);
     } else {
       const unsigned m = s_m;
-      for (unsigned j = t; j < m; j += blockDim.x) {
-        const uint64_t key = comp_key[j];
-        if ((key & msk) == pfx) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-      }
+      for (unsigned j = t; j < m; j += blockDim.x) count(comp_key[j], 0);
     }
     __syncthreads();
     if (t == 0) {
@@ -362,8 +378,7 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
     __syncthreads();
     if (!compacted && pass < 7 && s_bin_count <= static_cast<uint32_t>(kTopkCompact)) {
       const uint64_t npfx = s_prefix, nmsk = s_mask;
-      for (int64_t i = t; i < n; i += blockDim.x) {
-        const uint64_t key = key_of(i);
+      scan_row([&](uint64_t key, int64_t i) {
         const uint64_t top = key & nmsk;
         if (top == npfx) {
           const unsigned slot = atomicAdd(&s_m, 1u);
@@ -378,7 +393,7 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
             cand_idx[slot] = i;
           }
         }
-      }
+      });
       compacted = true;
       __syncthreads();
     }
@@ -397,8 +412,7 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
       }
     }
   } else {
-    for (int64_t i = t; i < n; i += blockDim.x) {
-      const uint64_t key = key_of(i);
+    scan_row([&](uint64_t key, int64_t i) {
       if (key <= kth) {
         const unsigned slot = atomicAdd(&s_count, 1u);
         if (slot < static_cast<unsigned>(kMaxSearchK)) {
@@ -406,7 +420,7 @@ topk_kernel(const float* __restrict__ dist, int64_t n, const uint32_t* __restric
           cand_idx[slot] = i;
         }
       }
-    }
+    });
   }
   __syncthreads();
   if (s_count != static_cast<unsigned>(kk)) {  // repeated ranks: no total order
