@@ -132,12 +132,12 @@ median_hist_kernel(const float* __restrict__ v, int64_t rows, int dim, int nstat
     const int64_t r_end = min(rows, (blockIdx.y + int64_t(1)) * rows_per_split);
     int64_t r = blockIdx.y * rows_per_split + warp;
     constexpr int W = kMedThreads / 32;
-    for (; r + 3 * W < r_end; r += 4 * W) {  // four loads in flight
-      float x[4];
+    for (; r + 7 * W < r_end; r += 8 * W) {  // eight loads in flight
+      float x[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = __ldg(v + (r + u * W) * dim + d);
+      for (int u = 0; u < 8; ++u) x[u] = __ldg(v + (r + u * W) * dim + d);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const uint32_t key = total_key(x[u]);
         const uint32_t bin = (key >> shift) & 255u;
         if ((key & mask) == p0) atomicAdd(&h[bin * kMedLanes + lane], 1u);
@@ -162,33 +162,52 @@ median_hist_kernel(const float* __restrict__ v, int64_t rows, int dim, int nstat
   }
 }
 
-// One thread per dimension: each statistic scans its 256 bins (the first
-// statistic's when both shared a prefix this pass) for the bin holding its
-// remaining rank and extends its prefix; the histograms are cleared for the
-// next pass.
+// One warp per dimension: for each statistic, lane l sums bins [8l, 8l + 8)
+// of its histogram (the first statistic's when both shared a prefix this
+// pass), a warp scan finds the lane whose range holds the remaining rank and
+// that lane walks its eight bins; the histograms are cleared for the next
+// pass.
 __global__ void median_select_kernel(int dim, int nstats, int pass, MedianScratch m) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= dim) return;
+  const int d = static_cast<int>((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (d >= dim) return;  // whole warps
   const int shift = 24 - 8 * pass;
   const bool shared = nstats == 2 && m.prefix[dim + d] == m.prefix[d];
   for (int st = 0; st < nstats; ++st) {
     const int i = st * dim + d;
-    const uint32_t* hh = m.hist + size_t((st == 1 && shared) ? d : i) * kMedBins;
+    const uint4* hh = reinterpret_cast<const uint4*>(m.hist + size_t((st == 1 && shared) ? d : i) * kMedBins);
+    const uint4 a = hh[2 * lane], b = hh[2 * lane + 1];
+    const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    int64_t sum = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) sum += c[u];
+    int64_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int64_t excl = incl - sum;
     const int64_t rem = m.remaining[i];
-    int64_t cum = 0;
-    for (int b = 0; b < kMedBins; ++b) {
-      const int64_t c = hh[b];
-      if (cum + c >= rem) {
-        m.prefix[i] |= static_cast<uint32_t>(b) << shift;
-        m.remaining[i] = rem - cum;
-        break;
+    if (excl < rem && rem <= incl) {  // exactly one lane: its bins hold the rank
+      int64_t cum = excl;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (cum + c[u] >= rem) {
+          m.prefix[i] |= static_cast<uint32_t>(8 * lane + u) << shift;
+          m.remaining[i] = rem - cum;
+          break;
+        }
+        cum += c[u];
       }
-      cum += c;
     }
   }
+  __syncwarp();
+  const uint4 z = make_uint4(0, 0, 0, 0);
   for (int st = 0; st < nstats; ++st) {
-    uint32_t* hh = m.hist + (size_t(st) * dim + d) * kMedBins;
-    for (int b = 0; b < kMedBins; ++b) hh[b] = 0;
+    uint4* hh = reinterpret_cast<uint4*>(m.hist + (size_t(st) * dim + d) * kMedBins);
+    hh[2 * lane] = z;
+    hh[2 * lane + 1] = z;
   }
 }
 
@@ -201,6 +220,26 @@ __global__ void median_final_kernel(int dim, int64_t rows, int nstats, MedianScr
   }
   const float a = from_total_key(m.prefix[d]);
   tau[d] = nstats == 2 ? __fdiv_rn(__fadd_rn(a, from_total_key(m.prefix[dim + d])), 2.0f) : a;
+}
+
+// Widths that are a multiple of 8 on a 16-byte aligned base: each output
+// byte's eight values and thresholds as two 16-byte loads each.
+__global__ void pack_threshold_bits8_kernel(const float* __restrict__ v, int64_t rows, int dim,
+                                            const float* __restrict__ tau, uint8_t* __restrict__ out) {
+  const int nb = dim / 8;
+  const int64_t total = rows * nb;
+  const float4* v4 = reinterpret_cast<const float4*>(v);
+  const float4* t4 = reinterpret_cast<const float4*>(tau);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i % nb);
+    const float4 x0 = __ldg(v4 + 2 * i), x1 = __ldg(v4 + 2 * i + 1);  // row r, byte b: floats 8i .. 8i + 7
+    const float4 a0 = __ldg(t4 + 2 * b), a1 = __ldg(t4 + 2 * b + 1);
+    const uint32_t byte = (x0.x > a0.x ? 1u : 0u) | (x0.y > a0.y ? 2u : 0u) | (x0.z > a0.z ? 4u : 0u) |
+                          (x0.w > a0.w ? 8u : 0u) | (x1.x > a1.x ? 16u : 0u) | (x1.y > a1.y ? 32u : 0u) |
+                          (x1.z > a1.z ? 64u : 0u) | (x1.w > a1.w ? 128u : 0u);
+    out[i] = static_cast<uint8_t>(byte);
+  }
 }
 
 __global__ void pack_threshold_bits_kernel(const float* __restrict__ v, int64_t rows, int dim,
@@ -458,8 +497,8 @@ cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, i
   const unsigned gx = static_cast<unsigned>((dim + kMedLanes - 1) / kMedLanes);
   if (rows > 0) {
     median_init_kernel<<<64, 256, 0, s>>>(dim, rows, nstats, m);
-    // about two CTAs per SM over the (dimension group, row split) grid
-    const int64_t splits_want = std::max<int64_t>(1, (148 * 2 + gx - 1) / gx);
+    // about three CTAs per SM over the (dimension group, row split) grid
+    const int64_t splits_want = std::max<int64_t>(1, (148 * 3 + gx - 1) / gx);
     int64_t per = (rows + splits_want - 1) / splits_want;
     per = std::max<int64_t>(per, 256);
     const unsigned gy = static_cast<unsigned>((rows + per - 1) / per);
@@ -468,7 +507,7 @@ cudaError_t launch_fit_binary_threshold(const float* v, int64_t rows, int dim, i
     if (e != cudaSuccess) return e;
     for (int pass = 0; pass < 4; ++pass) {
       median_hist_kernel<<<dim3(gx, gy), kMedThreads, smem, s>>>(v, rows, dim, nstats, pass, per, m);
-      median_select_kernel<<<(dim + 127) / 128, 128, 0, s>>>(dim, nstats, pass, m);
+      median_select_kernel<<<(dim + 7) / 8, 256, 0, s>>>(dim, nstats, pass, m);
     }
   }
   median_final_kernel<<<(dim + 127) / 128, 128, 0, s>>>(dim, rows, nstats, m, tau);
@@ -480,8 +519,11 @@ cudaError_t launch_pack_threshold_bits(const float* v, int64_t rows, int dim, co
   const int64_t total = rows * ((dim + 7) / 8);
   if (total <= 0) return cudaSuccess;
   const int64_t blocks = (total + 255) / 256;
-  pack_threshold_bits_kernel<<<static_cast<unsigned>(blocks < 148 * 64 ? blocks : 148 * 64), 256, 0, s>>>(
-      v, rows, dim, tau, out);
+  const unsigned grid = static_cast<unsigned>(blocks < 148 * 64 ? blocks : 148 * 64);
+  if (dim % 8 == 0 && reinterpret_cast<uintptr_t>(v) % 16 == 0 && reinterpret_cast<uintptr_t>(tau) % 16 == 0)
+    pack_threshold_bits8_kernel<<<grid, 256, 0, s>>>(v, rows, dim, tau, out);
+  else
+    pack_threshold_bits_kernel<<<grid, 256, 0, s>>>(v, rows, dim, tau, out);
   return cudaGetLastError();
 }
 
